@@ -1,0 +1,283 @@
+"""ctypes binding of libactrain.so (include/actrain.h).
+
+A thin mirror of the C ABI for Python callers (the tests and bench.py).  It mirrors the
+reference trainer classes' vocabulary: `mf_step` is MfTrainGraph::compute plus
+TrainAccumulation::add (src/mf/train.h:148-188), `optimizer` is TrainAccumulation::update
+(src/ac/train_controls.h:89-118).  There is no CPU path: if the library cannot be loaded
+every call raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libactrain.so")
+
+ACT_OK, ACT_ERR_INVALID, ACT_ERR_CUDA, ACT_ERR_NCCL, ACT_ERR_STATE, ACT_ERR_NONFINITE = range(6)
+FAMILY_MELODYFLOW, FAMILY_MUSICGEN = 0, 1
+ADAPTER_LORA, ADAPTER_DORA_ROWS = 0, 1
+TYPE_F32, TYPE_F16, TYPE_Q8_0 = 0, 1, 8
+TARGETS = ("self.qkv", "self.out", "cross.q", "cross.kv", "cross.out", "ff.0", "ff.2")
+
+
+class ModelDesc(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("family", "dim", "layers", "heads", "head_dim", "ff_dim",
+                                        "latent_dim", "cond_dim", "time_dim", "n_skip",
+                                        "add_zero_attn", "n_q", "card", "special_token_id",
+                                        "pos_denominator")] + \
+               [("max_period", C.c_float), ("norm_eps", C.c_float)]
+
+
+class AdapterDesc(C.Structure):
+    _fields_ = [("type", C.c_int), ("rank", C.c_int), ("alpha", C.c_float),
+                ("first_layer", C.c_int), ("targets", C.c_uint), ("seed", C.c_uint32),
+                ("max_batch", C.c_int), ("frames", C.c_int), ("tokens", C.c_int),
+                ("prefix_frames", C.c_int)]
+
+
+class MfBatch(C.Structure):
+    _fields_ = [("n", C.c_int), ("clean", C.c_void_p), ("noise", C.c_void_p),
+                ("hidden", C.c_void_p), ("t", C.c_void_p), ("unconditional", C.c_void_p),
+                ("valid_tokens", C.c_void_p)]
+
+
+class MgBatch(C.Structure):
+    _fields_ = [("n", C.c_int), ("codes", C.c_void_p), ("context", C.c_void_p)]
+
+
+class Opt(C.Structure):
+    _fields_ = [("lr", C.c_float), ("beta1", C.c_float), ("beta2", C.c_float), ("eps", C.c_float),
+                ("weight_decay", C.c_float), ("clip", C.c_float), ("step", C.c_int),
+                ("count", C.c_int)]
+
+
+class ActError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+_lib = None
+
+SIGNATURES = {
+    "act_create": (C.c_int, [C.POINTER(C.c_void_p), C.c_int, C.POINTER(ModelDesc), C.POINTER(AdapterDesc)]),
+    "act_bind_weight": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int, C.c_void_p, C.c_size_t]),
+    "act_finalize": (C.c_int, [C.c_void_p]),
+    "act_param_count": (C.c_int64, [C.c_void_p]),
+    "act_param_tensor_count": (C.c_int, [C.c_void_p]),
+    "act_param_tensor": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t, C.POINTER(C.c_int64),
+                                   C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
+    "act_set_params": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
+    "act_get_params": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]),
+    "act_set_moments": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]),
+    "act_get_grads": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
+    "act_zero_grads": (C.c_int, [C.c_void_p]),
+    "act_mf_step": (C.c_int, [C.c_void_p, C.POINTER(MfBatch), C.c_void_p]),
+    "act_mg_step": (C.c_int, [C.c_void_p, C.POINTER(MgBatch), C.c_void_p]),
+    "act_nccl_get_unique_id": (C.c_int, [C.c_void_p]),
+    "act_nccl_init": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int]),
+    "act_allreduce_grads": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
+    "act_optimizer": (C.c_int, [C.c_void_p, C.POINTER(Opt), C.POINTER(C.c_int)]),
+    "act_last_error": (C.c_char_p, [C.c_void_p]),
+    "act_destroy": (None, [C.c_void_p]),
+    "act_stream": (C.c_void_p, [C.c_void_p]),
+    "act_mf_stage": (C.c_int, [C.c_void_p, C.POINTER(MfBatch)]),
+    "act_mg_stage": (C.c_int, [C.c_void_p, C.POINTER(MgBatch)]),
+    "act_run_staged": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "act_set_profiling": (C.c_int, [C.c_void_p, C.c_int]),
+    "act_kernel_stats": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double),
+                                   C.POINTER(C.c_double), C.POINTER(C.c_int64)]),
+    "act_reset_kernel_stats": (C.c_int, [C.c_void_p]),
+    "act_step_flops": (C.c_double, [C.c_void_p, C.c_int]),
+    "act_graph_kernel_nodes": (C.c_int64, [C.c_void_p, C.c_int]),
+}
+
+
+def lib():
+    """Load libactrain.so; raises if it is missing (there is no fallback path)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ActError(ACT_ERR_STATE, f"{LIB_PATH} is not built: run audiocraft.cpp_b200/build.py")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data
+
+
+class Context:
+    """One device context: MfTrainGraph / MgTrainGraph equivalent for a batch of samples."""
+
+    def __init__(self, model: ModelDesc, adapter: AdapterDesc, device: int = 0):
+        self._L = lib()
+        self.model, self.adapter = model, adapter
+        h = C.c_void_p()
+        rc = self._L.act_create(C.byref(h), device, C.byref(model), C.byref(adapter))
+        if rc != ACT_OK:
+            raise ActError(rc, self._L.act_last_error(None).decode())
+        self.h = h
+        self._keep = []
+
+    def _check(self, rc):
+        if rc != ACT_OK:
+            raise ActError(rc, self._L.act_last_error(self.h).decode())
+
+    def close(self):
+        if getattr(self, "h", None):
+            self._L.act_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ----------------------------------------------------------------- weights
+    def bind(self, name: str, array: np.ndarray, ggml_type: int = TYPE_F32):
+        a = np.ascontiguousarray(array)
+        self._check(self._L.act_bind_weight(self.h, name.encode(), ggml_type, a.ctypes.data, a.nbytes))
+
+    def finalize(self):
+        self._check(self._L.act_finalize(self.h))
+        self.n = int(self._L.act_param_count(self.h))
+
+    # ----------------------------------------------------------------- parameters
+    def param_table(self):
+        out = []
+        buf = C.create_string_buffer(256)
+        for i in range(self._L.act_param_tensor_count(self.h)):
+            off, r, c = C.c_int64(), C.c_int64(), C.c_int64()
+            self._check(self._L.act_param_tensor(self.h, i, buf, 256, C.byref(off), C.byref(r), C.byref(c)))
+            out.append((buf.value.decode(), off.value, (r.value, c.value)))
+        return out
+
+    def get_params(self):
+        v, m, s = (np.zeros(self.n, np.float32) for _ in range(3))
+        self._check(self._L.act_get_params(self.h, v.ctypes.data, m.ctypes.data, s.ctypes.data, self.n))
+        return v, m, s
+
+    def set_params(self, v):
+        v = np.ascontiguousarray(v, np.float32)
+        self._check(self._L.act_set_params(self.h, v.ctypes.data, v.size))
+
+    def set_moments(self, m, v):
+        m = np.ascontiguousarray(m, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        self._check(self._L.act_set_moments(self.h, m.ctypes.data, v.ctypes.data, m.size))
+
+    def get_grads(self):
+        g = np.zeros(self.n, np.float32)
+        self._check(self._L.act_get_grads(self.h, g.ctypes.data, self.n))
+        return g
+
+    def zero_grads(self):
+        self._check(self._L.act_zero_grads(self.h))
+
+    # ----------------------------------------------------------------- steps
+    def _mf_batch(self, clean, noise, hidden, t, unconditional=None, valid_tokens=None):
+        arrs = [np.ascontiguousarray(clean, np.float32), np.ascontiguousarray(noise, np.float32),
+                np.ascontiguousarray(hidden, np.float32), np.ascontiguousarray(t, np.float32),
+                None if unconditional is None else np.ascontiguousarray(unconditional, np.int32),
+                None if valid_tokens is None else np.ascontiguousarray(valid_tokens, np.int32)]
+        self._keep = arrs
+        return MfBatch(arrs[0].shape[0], *[_ptr(a) for a in arrs])
+
+    def mf_step(self, clean, noise, hidden, t, unconditional=None, valid_tokens=None):
+        b = self._mf_batch(clean, noise, hidden, t, unconditional, valid_tokens)
+        loss = np.zeros(b.n, np.float32)
+        self._check(self._L.act_mf_step(self.h, C.byref(b), loss.ctypes.data))
+        return loss
+
+    def mf_stage(self, clean, noise, hidden, t, unconditional=None, valid_tokens=None):
+        b = self._mf_batch(clean, noise, hidden, t, unconditional, valid_tokens)
+        self._check(self._L.act_mf_stage(self.h, C.byref(b)))
+        return b.n
+
+    def mg_step(self, codes, context):
+        arrs = [np.ascontiguousarray(codes, np.int32), np.ascontiguousarray(context, np.float32)]
+        self._keep = arrs
+        b = MgBatch(arrs[0].shape[0], arrs[0].ctypes.data, arrs[1].ctypes.data)
+        loss = np.zeros(b.n, np.float32)
+        self._check(self._L.act_mg_step(self.h, C.byref(b), loss.ctypes.data))
+        return loss
+
+    def mg_stage(self, codes, context):
+        arrs = [np.ascontiguousarray(codes, np.int32), np.ascontiguousarray(context, np.float32)]
+        self._keep = arrs
+        b = MgBatch(arrs[0].shape[0], arrs[0].ctypes.data, arrs[1].ctypes.data)
+        self._check(self._L.act_mg_stage(self.h, C.byref(b)))
+        return b.n
+
+    def run_staged(self, n=None, read_loss=True):
+        if read_loss:
+            loss = np.zeros(n, np.float32)
+            self._check(self._L.act_run_staged(self.h, loss.ctypes.data))
+            return loss
+        self._check(self._L.act_run_staged(self.h, None))
+        return None
+
+    def optimizer(self, lr, step, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.0, clip=1.0, count=0):
+        o = Opt(lr, beta1, beta2, eps, weight_decay, clip, step, count)
+        bad = C.c_int(0)
+        rc = self._L.act_optimizer(self.h, C.byref(o), C.byref(bad))
+        if rc != ACT_OK:
+            raise ActError(rc, self._L.act_last_error(self.h).decode())
+        return bad.value
+
+    # ----------------------------------------------------------------- data parallel
+    @staticmethod
+    def nccl_unique_id() -> bytes:
+        buf = C.create_string_buffer(128)
+        rc = lib().act_nccl_get_unique_id(buf)
+        if rc != ACT_OK:
+            raise ActError(rc, lib().act_last_error(None).decode())
+        return buf.raw
+
+    def nccl_init(self, uid: bytes, nranks: int, rank: int):
+        buf = C.create_string_buffer(uid, 128)
+        self._check(self._L.act_nccl_init(self.h, buf, nranks, rank))
+
+    def allreduce_grads(self, global_count: int):
+        self._check(self._L.act_allreduce_grads(self.h, None, global_count))
+
+    # ----------------------------------------------------------------- measurement
+    def stream(self) -> int:
+        return self._L.act_stream(self.h)
+
+    def set_profiling(self, on: bool):
+        self._check(self._L.act_set_profiling(self.h, int(on)))
+
+    def kernel_stats(self, cls: int):
+        ms, fl, by, n = C.c_double(), C.c_double(), C.c_double(), C.c_int64()
+        self._check(self._L.act_kernel_stats(self.h, cls, C.byref(ms), C.byref(fl), C.byref(by), C.byref(n)))
+        return {"ms": ms.value, "flops": fl.value, "bytes": by.value, "launches": n.value}
+
+    def reset_kernel_stats(self):
+        self._check(self._L.act_reset_kernel_stats(self.h))
+
+    def step_flops(self, n: int) -> float:
+        return float(self._L.act_step_flops(self.h, n))
+
+    def graph_kernel_nodes(self, n: int) -> int:
+        return int(self._L.act_graph_kernel_nodes(self.h, n))
+
+
+def mf_model(dim, layers, heads, ff_dim, latent_dim=128, cond_dim=768, time_dim=256, norm_eps=1e-5):
+    return ModelDesc(FAMILY_MELODYFLOW, dim, layers, heads, dim // heads, ff_dim, latent_dim, cond_dim,
+                     time_dim, (layers - 1) // 2, 1, 0, 0, 0, 0, 10000.0, norm_eps)
+
+
+def mg_model(dim, layers, heads, ff_dim, n_q=4, card=2048, norm_eps=1e-5, max_period=10000.0):
+    return ModelDesc(FAMILY_MUSICGEN, dim, layers, heads, dim // heads, ff_dim, 0, 0, 0, 0, 0, n_q, card,
+                     card, dim // 2 - 1, max_period, norm_eps)

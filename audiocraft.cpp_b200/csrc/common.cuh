@@ -1,0 +1,86 @@
+// common.cuh -- shared device helpers for the adapter-training kernels (sm_100a).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+typedef __nv_bfloat16 bf16;
+
+namespace act {
+
+// A&S 7.1.26 GELU and the derivative of that approximation (the reference trains through
+// the approximation, src/ac/lora.h:97-110, so its gradient is the one autodiff yields).
+__device__ __forceinline__ float gelu_as(float x) {
+    const float z = x * 0.7071067811865475f, a = fabsf(z);
+    const float t = 1.0f / (0.3275911f * a + 1.0f);
+    const float poly =
+        ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
+    const float e = expf(-(z * z));
+    const float sg = z > 0.f ? 1.f : (z < 0.f ? -1.f : 0.f);
+    return x * (0.5f * (sg * (1.0f - poly * e)) + 0.5f);
+}
+
+__device__ __forceinline__ float gelu_as_grad(float x) {
+    const float z = x * 0.7071067811865475f, a = fabsf(z);
+    const float sg = z > 0.f ? 1.f : (z < 0.f ? -1.f : 0.f);
+    const float t = 1.0f / (0.3275911f * a + 1.0f);
+    const float poly =
+        ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
+    const float dpoly =
+        (((5.0f * 1.061405429f * t - 4.0f * 1.453152027f) * t + 3.0f * 1.421413741f) * t - 2.0f * 0.284496736f) * t +
+        0.254829592f;
+    const float e = expf(-(z * z));
+    const float erf_ = sg * (1.0f - poly * e);
+    const float derf = sg * sg * dpoly * 0.3275911f * t * t * e + 2.0f * z * sg * poly * e;
+    return (0.5f * erf_ + 0.5f) + x * 0.5f * derf * 0.7071067811865475f;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
+    const int bytes = pred ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem),
+                 "r"(bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3,
+                                        const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3,
+                                          const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(smem_u32(p)));
+}
+
+// D += A(16x16, row) * B(16x8, col), bf16 inputs, fp32 accumulators.
+__device__ __forceinline__ void mma_bf16(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+}  // namespace act

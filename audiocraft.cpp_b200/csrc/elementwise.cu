@@ -1,0 +1,534 @@
+// elementwise.cu -- row / element kernels of the adapter training step (HBM-bound work).
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace act {
+
+namespace {
+
+constexpr int MAXV = 16;  // float4 per lane: D <= 2048
+
+// ---------------------------------------------------------------------------------------
+// LayerNorm, src/ac/lora.h:86-93: mean, centre, x / sqrt(mean(x^2) + eps), * w + b.
+__global__ void ln_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                              const float* __restrict__ b, const float* __restrict__ add,
+                              int rows_per_clip, bf16* __restrict__ y, float* __restrict__ mean,
+                              float* __restrict__ rstd, int rows, int D, float eps) {
+    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int nv = D / 128;
+    const float4* xr = reinterpret_cast<const float4*>(x + (long)row * D);
+    float4 v[MAXV];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i)
+        if (i < nv) {
+            v[i] = xr[i * 32 + lane];
+            s += v[i].x + v[i].y + v[i].z + v[i].w;
+        }
+    s = warp_sum(s);
+    const float mu = s * (1.0f / (float)D);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i)
+        if (i < nv) {
+            const float a0 = v[i].x - mu, a1 = v[i].y - mu, a2 = v[i].z - mu, a3 = v[i].w - mu;
+            ss += a0 * a0 + a1 * a1 + a2 * a2 + a3 * a3;
+        }
+    ss = warp_sum(ss);
+    const float rs = 1.0f / sqrtf(ss / (float)D + eps);
+    if (lane == 0) {
+        mean[row] = mu;
+        rstd[row] = rs;
+    }
+    const float* ad = add ? add + (long)(row / rows_per_clip) * D : nullptr;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i)
+        if (i < nv) {
+            const int j = (i * 32 + lane) * 4;
+            const float4 ww = *reinterpret_cast<const float4*>(w + j);
+            const float4 bb = *reinterpret_cast<const float4*>(b + j);
+            float o0 = (v[i].x - mu) * rs * ww.x + bb.x, o1 = (v[i].y - mu) * rs * ww.y + bb.y;
+            float o2 = (v[i].z - mu) * rs * ww.z + bb.z, o3 = (v[i].w - mu) * rs * ww.w + bb.w;
+            if (ad) {
+                const float4 aa = *reinterpret_cast<const float4*>(ad + j);
+                o0 += aa.x; o1 += aa.y; o2 += aa.z; o3 += aa.w;
+            }
+            uint2 pk = make_uint2(pack_bf16(o0, o1), pack_bf16(o2, o3));
+            *reinterpret_cast<uint2*>(y + (long)row * D + j) = pk;
+        }
+}
+
+__global__ void ln_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                              const float* __restrict__ w, const float* __restrict__ mean,
+                              const float* __restrict__ rstd, float* __restrict__ dx, int accumulate,
+                              const float* __restrict__ extra, bf16* __restrict__ dx_bf,
+                              const float* __restrict__ colscale, int rows, int D) {
+    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int nv = D / 128;
+    const float mu = mean[row], rs = rstd[row];
+    float4 gv[MAXV], xh[MAXV];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i)
+        if (i < nv) {
+            const int j = (i * 32 + lane) * 4;
+            const float4 d = *reinterpret_cast<const float4*>(dy + (long)row * D + j);
+            const float4 xx = *reinterpret_cast<const float4*>(x + (long)row * D + j);
+            const float4 ww = *reinterpret_cast<const float4*>(w + j);
+            gv[i] = make_float4(d.x * ww.x, d.y * ww.y, d.z * ww.z, d.w * ww.w);
+            xh[i] = make_float4((xx.x - mu) * rs, (xx.y - mu) * rs, (xx.z - mu) * rs, (xx.w - mu) * rs);
+            s1 += gv[i].x + gv[i].y + gv[i].z + gv[i].w;
+            s2 += gv[i].x * xh[i].x + gv[i].y * xh[i].y + gv[i].z * xh[i].z + gv[i].w * xh[i].w;
+        }
+    s1 = warp_sum(s1) / (float)D;
+    s2 = warp_sum(s2) / (float)D;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i)
+        if (i < nv) {
+            const int j = (i * 32 + lane) * 4;
+            float4* dp = reinterpret_cast<float4*>(dx + (long)row * D + j);
+            float4 r = make_float4(rs * (gv[i].x - s1 - xh[i].x * s2), rs * (gv[i].y - s1 - xh[i].y * s2),
+                                   rs * (gv[i].z - s1 - xh[i].z * s2), rs * (gv[i].w - s1 - xh[i].w * s2));
+            if (accumulate) {
+                const float4 o = *dp;
+                r.x += o.x; r.y += o.y; r.z += o.z; r.w += o.w;
+            }
+            if (extra) {
+                const float4 e = *reinterpret_cast<const float4*>(extra + (long)row * D + j);
+                r.x += e.x; r.y += e.y; r.z += e.z; r.w += e.w;
+            }
+            *dp = r;
+            if (dx_bf) {
+                float4 c = make_float4(1.f, 1.f, 1.f, 1.f);
+                if (colscale) c = *reinterpret_cast<const float4*>(colscale + j);
+                *reinterpret_cast<uint2*>(dx_bf + (long)row * D + j) =
+                    make_uint2(pack_bf16(r.x * c.x, r.y * c.y), pack_bf16(r.z * c.z, r.w * c.w));
+            }
+        }
+}
+
+__global__ void resid_bf16_kernel(float* __restrict__ x, const float* __restrict__ extra,
+                                  bf16* __restrict__ dst, const float* __restrict__ colscale, long n4, int D) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n4) return;
+    float4 v = reinterpret_cast<float4*>(x)[i];
+    if (extra) {
+        const float4 e = reinterpret_cast<const float4*>(extra)[i];
+        v.x += e.x; v.y += e.y; v.z += e.z; v.w += e.w;
+        reinterpret_cast<float4*>(x)[i] = v;
+    }
+    float4 c = make_float4(1.f, 1.f, 1.f, 1.f);
+    if (colscale) c = *reinterpret_cast<const float4*>(colscale + (i * 4) % D);
+    reinterpret_cast<uint2*>(dst)[i] = make_uint2(pack_bf16(v.x * c.x, v.y * c.y), pack_bf16(v.z * c.z, v.w * c.w));
+}
+
+__global__ void f32_bf16_kernel(const float* __restrict__ x, bf16* __restrict__ y, long n) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = __float2bfloat16(x[i]);
+}
+
+// ---------------------------------------------------------------------------------------
+// MelodyFlow inputs and loss, src/mf/train.h:154-159 and :107-108, src/mf/dit.h:172-173,208-216.
+__global__ void mf_inputs_kernel(const float* __restrict__ clean, const float* __restrict__ noise,
+                                 const float* __restrict__ tv, int clips, int T, int lat,
+                                 bf16* __restrict__ x0, float* __restrict__ vstar) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long n = (long)clips * lat * T;
+    if (i >= n) return;
+    const int b = (int)(i / ((long)lat * T));
+    const int c = (int)((i / T) % lat), p = (int)(i % T);
+    const float t = tv[b];
+    const float rescale = 1.0f / sqrtf(t * t + (1.0f - t) * (1.0f - t));
+    const float cl = clean[i], nz = noise[i];
+    x0[((long)b * T + p) * lat + c] = __float2bfloat16(((1 - t) * nz + t * cl) * rescale);
+    vstar[i] = cl - nz;
+}
+
+__global__ void mf_loss_kernel(const float* __restrict__ out, const float* __restrict__ vstar, int T,
+                               int lat, float* __restrict__ loss, bf16* __restrict__ dout) {
+    const int b = blockIdx.x;
+    const long n = (long)T * lat;
+    const float inv = 1.0f / (float)n;
+    const float sq2 = sqrtf(2.0f);
+    float acc = 0.f;
+    for (long i = threadIdx.x; i < n; i += blockDim.x) {
+        const int c = (int)(i / T), p = (int)(i % T);
+        const long o = ((long)b * T + p) * lat + c;
+        const float d = out[o] * sq2 - vstar[(long)b * n + i];
+        acc += d * d;
+        dout[o] = __float2bfloat16(2.0f * d * inv * sq2);
+    }
+    __shared__ float red[32];
+    acc = warp_sum(acc);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+        v = warp_sum(v);
+        if (threadIdx.x == 0) loss[b] = v * inv;
+    }
+}
+
+__global__ void linear_f32_kernel(const float* __restrict__ x, const float* __restrict__ W,
+                                  float* __restrict__ y, int rows, int N, int K, int act) {
+    const long w = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (w >= (long)rows * N) return;
+    const int r = (int)(w / N), n = (int)(w % N);
+    float acc = 0.f;
+    for (int k = lane; k < K; k += 32) acc += x[(long)r * K + k] * W[(long)n * K + k];
+    acc = warp_sum(acc);
+    if (lane == 0) y[w] = act == 1 ? acc / (1.0f + expf(-acc)) : acc;
+}
+
+// ---------------------------------------------------------------------------------------
+// DoRA-rows, src/ac/lora.h:62-79 (and the hand-derived backward of that factorisation).
+__global__ void dora_colsum_kernel(const bf16* __restrict__ a, long lda, const bf16* __restrict__ b,
+                                   long ldb, int rows, int N, const float* __restrict__ g,
+                                   float* __restrict__ dg, int rows_per_block) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    const int r0 = blockIdx.y * rows_per_block, r1 = min(rows, r0 + rows_per_block);
+    float acc = 0.f;
+    for (int r = r0; r < r1; ++r)
+        acc += __bfloat162float(a[(long)r * lda + n]) * __bfloat162float(b[(long)r * ldb + n]);
+    const float gg = g[n];
+    atomicAdd(dg + n, acc / (gg * gg));
+}
+
+__global__ void gram_kernel(const float* __restrict__ A, int r, int in, const float* __restrict__ wt,
+                            const float* __restrict__ B, int ldb, float* __restrict__ G) {
+    // G[j][k] = sum_i X[j][i] X[k][i] (A mode, wt == nullptr, X = A [r][in])
+    //        or sum_o wt[o] B[o][j] B[o][k]   (B mode: X^T diag(wt) X with X = B [in=out][r])
+    const int e = blockIdx.x;  // one entry per block
+    const int j = e / r, k = e % r;
+    float acc = 0.f;
+    if (!wt)
+        for (int i = threadIdx.x; i < in; i += blockDim.x) acc += A[(long)j * in + i] * A[(long)k * in + i];
+    else
+        for (int o = threadIdx.x; o < in; o += blockDim.x) acc += wt[o] * B[(long)o * ldb + j] * B[(long)o * ldb + k];
+    __shared__ float red[32];
+    acc = warp_sum(acc);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+        v = warp_sum(v);
+        if (threadIdx.x == 0) G[e] = v;
+    }
+}
+
+__global__ void dora_rows_kernel(const float* __restrict__ B, const float* __restrict__ m,
+                                 const float* __restrict__ P, const float* __restrict__ base,
+                                 const float* __restrict__ G, int r, int RP, int out, float s,
+                                 float* __restrict__ Q, float* __restrict__ nsq, float* __restrict__ g) {
+    const int o = blockIdx.x * blockDim.x + threadIdx.x;
+    if (o >= out) return;
+    float t2 = 0.f, t3 = 0.f;
+    for (int j = 0; j < r; ++j) {
+        float qv = 0.f;
+        for (int k = 0; k < r; ++k) qv += B[(long)o * r + k] * G[k * r + j];
+        Q[(long)o * r + j] = qv;
+        t2 += P[(long)o * RP + j] * B[(long)o * r + j];
+        t3 += B[(long)o * r + j] * qv;
+    }
+    const float n = base[o] + 2.0f * s * t2 + s * s * t3;
+    nsq[o] = n;
+    g[o] = m[o] / sqrtf(n);
+}
+
+__global__ void dora_tail_kernel(const float* __restrict__ dg, const float* __restrict__ nsq,
+                                 const float* __restrict__ g, const float* __restrict__ B,
+                                 const float* __restrict__ P, const float* __restrict__ Q, int r,
+                                 int RP, int out, float s, float* __restrict__ gm, float* __restrict__ gB,
+                                 bf16* __restrict__ BD, float* __restrict__ dt3) {
+    const int o = blockIdx.x * blockDim.x + threadIdx.x;
+    if (o >= out) return;
+    const float sq = sqrtf(nsq[o]);
+    gm[o] += dg[o] / sq;
+    const float dn = -0.5f * dg[o] * g[o] / nsq[o];
+    const float d2 = 2.0f * s * dn, d3 = s * s * dn;
+    dt3[o] = d3;
+    for (int j = 0; j < RP; ++j) {
+        if (j < r) {
+            gB[(long)o * r + j] += d2 * P[(long)o * RP + j] + 2.0f * d3 * Q[(long)o * r + j];
+            BD[(long)o * RP + j] = __float2bfloat16(d2 * B[(long)o * r + j]);
+        } else {
+            BD[(long)o * RP + j] = __float2bfloat16(0.f);
+        }
+    }
+}
+
+__global__ void dora_ga_kernel(const float* __restrict__ dG, const float* __restrict__ A, int r, int in,
+                               float* __restrict__ gA) {
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= (long)r * in) return;
+    const int j = (int)(e / in), i = (int)(e % in);
+    float acc = 0.f;
+    for (int k = 0; k < r; ++k) acc += dG[j * r + k] * A[(long)k * in + i];
+    gA[e] += 2.0f * acc;
+}
+
+// ---------------------------------------------------------------------------------------
+__global__ void refresh_kernel(const CopyJob* jobs) {
+    const CopyJob j = jobs[blockIdx.y];
+    const long n = (long)j.rows * j.cols;
+    for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (long)gridDim.x * blockDim.x) {
+        const int row = (int)(e / j.cols), col = (int)(e % j.cols);
+        j.dst[(long)row * j.ldd + col] = __float2bfloat16(j.src[e]);
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// AdamW, src/ac/train_controls.h:89-118: mean over microbatches, global-norm clip, decoupled
+// decay on lora_A / lora_B only.
+__global__ void grad_norm_kernel(const float* __restrict__ grad, long n, float count,
+                                 double* __restrict__ partials) {
+    double acc = 0.0;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+        const float x = grad[i] / count;
+        acc += (double)x * x;
+    }
+    __shared__ double red[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        double v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (threadIdx.x == 0) partials[blockIdx.x] = v;
+    }
+}
+
+__global__ void adamw_kernel(float* __restrict__ value, float* __restrict__ m, float* __restrict__ v,
+                             float* __restrict__ grad, const uint8_t* __restrict__ decay_mask, long n,
+                             float count, float clip, float lr, float beta1, float beta2, float eps,
+                             float decay, float bc1, float bc2, const double* __restrict__ partials,
+                             int nparts, int* __restrict__ nonfinite) {
+    __shared__ float sscale;
+    if (threadIdx.x < 32) {
+        double acc = 0.0;
+        for (int i = threadIdx.x; i < nparts; i += 32) acc += partials[i];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (threadIdx.x == 0) sscale = (float)fmin(1.0, (double)clip / (sqrt(acc) + 1e-12));
+    }
+    __syncthreads();
+    const float scale = sscale;
+    int bad = 0;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+        const float wd = decay_mask[i] ? decay : 0.0f;
+        const float gr = scale * (grad[i] / count);
+        const float mi = beta1 * m[i] + (1 - beta1) * gr;
+        const float vi = beta2 * v[i] + (1 - beta2) * gr * gr;
+        const float val = value[i] - lr * ((mi / bc1) / (sqrtf(vi / bc2) + eps) + wd * value[i]);
+        m[i] = mi;
+        v[i] = vi;
+        value[i] = val;
+        grad[i] = 0.f;
+        bad += !isfinite(val);
+    }
+    if (bad) atomicAdd(nonfinite, bad);
+}
+
+// ---------------------------------------------------------------------------------------
+// Q8_0: 34-byte blocks {fp16 d; int8 q[32]}; w = d * q exactly in fp32.
+__global__ void q8_bf16_kernel(const uint8_t* __restrict__ blocks, long nblocks, bf16* __restrict__ out) {
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= nblocks * 32) return;
+    const uint8_t* blk = blocks + (e >> 5) * 34;
+    const __half d = __ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8)));
+    out[e] = __float2bfloat16(__half2float(d) * (float)(int8_t)blk[2 + (e & 31)]);
+}
+
+__global__ void q8_f32_kernel(const uint8_t* __restrict__ blocks, long nblocks, float* __restrict__ out) {
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= nblocks * 32) return;
+    const uint8_t* blk = blocks + (e >> 5) * 34;
+    const __half d = __ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8)));
+    out[e] = __half2float(d) * (float)(int8_t)blk[2 + (e & 31)];
+}
+
+__global__ void f16_bf16_kernel(const uint16_t* __restrict__ in, long n, bf16* __restrict__ out) {
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e < n) out[e] = __float2bfloat16(__half2float(__ushort_as_half(in[e])));
+}
+
+// ---------------------------------------------------------------------------------------
+// MusicGen: summed codebook embeddings plus sinusoidal positions (src/mg/train.h:17-22).
+__global__ void mg_embed_kernel(const int32_t* __restrict__ ids, int steps, int nq,
+                                const float* const* __restrict__ emb, const float* __restrict__ pos,
+                                float* __restrict__ x, int D, int seqs) {
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= (long)seqs * steps * D) return;
+    const int j = (int)(e % D);
+    const long row = e / D;
+    const int b = (int)(row / steps), s = (int)(row % steps);
+    float acc = 0.f;
+    for (int q = 0; q < nq; ++q) {
+        const int id = ids[((long)b * nq + q) * steps + s];
+        acc += emb[q][(long)id * D + j];
+    }
+    x[e] = acc + pos[(long)s * D + j];
+}
+
+// ggml_cross_entropy_loss over the selected rows, src/mg/train.h:131.
+__global__ void mg_ce_kernel(const float* __restrict__ logits, int card, const int32_t* __restrict__ targets,
+                             int rows_per_seq, float inv_nsel, float* __restrict__ loss_acc,
+                             bf16* __restrict__ dlogits) {
+    const int row = blockIdx.x;
+    const int tgt = targets[row];
+    const float* lg = logits + (long)row * card;
+    bf16* dl = dlogits + (long)row * card;
+    __shared__ float red[32];
+    __shared__ float sh_max, sh_sum;
+    float mx = -INFINITY;
+    for (int j = threadIdx.x; j < card; j += blockDim.x) mx = fmaxf(mx, lg[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : -INFINITY;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (threadIdx.x == 0) sh_max = v;
+    }
+    __syncthreads();
+    mx = sh_max;
+    float sm = 0.f;
+    for (int j = threadIdx.x; j < card; j += blockDim.x) sm += expf(lg[j] - mx);
+    sm = warp_sum(sm);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sm;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+        v = warp_sum(v);
+        if (threadIdx.x == 0) sh_sum = v;
+    }
+    __syncthreads();
+    sm = sh_sum;
+    if (tgt < 0) {
+        for (int j = threadIdx.x; j < card; j += blockDim.x) dl[j] = __float2bfloat16(0.f);
+        return;
+    }
+    const float inv = 1.0f / sm;
+    for (int j = threadIdx.x; j < card; j += blockDim.x)
+        dl[j] = __float2bfloat16((expf(lg[j] - mx) * inv - (j == tgt ? 1.0f : 0.0f)) * inv_nsel);
+    if (threadIdx.x == 0) atomicAdd(loss_acc + row / rows_per_seq, (mx + logf(sm) - lg[tgt]) * inv_nsel);
+}
+
+inline unsigned blocks_for(long n, int t) { return (unsigned)((n + t - 1) / t); }
+
+}  // namespace
+
+void layernorm_fwd(const float* x, const float* w, const float* b, const float* add, int rows_per_clip,
+                   bf16* y, float* mean, float* rstd, int rows, int D, float eps, cudaStream_t s) {
+    ln_fwd_kernel<<<blocks_for(rows, 8), 256, 0, s>>>(x, w, b, add, rows_per_clip, y, mean, rstd, rows, D, eps);
+}
+
+void layernorm_bwd(const float* dy, const float* x, const float* w, const float* mean, const float* rstd,
+                   float* dx, int accumulate, const float* extra, bf16* dx_bf, const float* colscale,
+                   int rows, int D, cudaStream_t s) {
+    ln_bwd_kernel<<<blocks_for(rows, 8), 256, 0, s>>>(dy, x, w, mean, rstd, dx, accumulate, extra, dx_bf,
+                                                      colscale, rows, D);
+}
+
+void residual_to_bf16(float* x, const float* extra, bf16* dst, const float* colscale, int rows, int D,
+                      cudaStream_t s) {
+    const long n4 = (long)rows * D / 4;
+    resid_bf16_kernel<<<blocks_for(n4, 256), 256, 0, s>>>(x, extra, dst, colscale, n4, D);
+}
+
+void f32_to_bf16(const float* x, bf16* y, long n, cudaStream_t s) {
+    f32_bf16_kernel<<<blocks_for(n, 256), 256, 0, s>>>(x, y, n);
+}
+
+void mf_inputs(const float* clean, const float* noise, const float* t, int clips, int T, int lat, bf16* x0,
+               float* vstar, cudaStream_t s) {
+    const long n = (long)clips * lat * T;
+    mf_inputs_kernel<<<blocks_for(n, 256), 256, 0, s>>>(clean, noise, t, clips, T, lat, x0, vstar);
+}
+
+void mf_loss(const float* out, const float* vstar, int clips, int T, int lat, float* loss, bf16* dout,
+             cudaStream_t s) {
+    mf_loss_kernel<<<clips, 1024, 0, s>>>(out, vstar, T, lat, loss, dout);
+}
+
+void linear_f32(const float* x, const float* W, float* y, int rows, int N, int K, int act, cudaStream_t s) {
+    linear_f32_kernel<<<blocks_for((long)rows * N, 8), 256, 0, s>>>(x, W, y, rows, N, K, act);
+}
+
+void dora_colsum(const bf16* a, long lda, const bf16* b, long ldb, int rows, int N, const float* colscale,
+                 float* dg, cudaStream_t s) {
+    const int rpb = 256;
+    dim3 grid(blocks_for(N, 256), blocks_for(rows, rpb));
+    dora_colsum_kernel<<<grid, 256, 0, s>>>(a, lda, b, ldb, rows, N, colscale, dg, rpb);
+}
+
+void dora_prepare(const float* A, const float* B, const float* m, const float* P, const float* base, int r,
+                  int in, int out, float s, float* G, float* Q, float* nsq, float* g, cudaStream_t st) {
+    gram_kernel<<<r * r, 256, 0, st>>>(A, r, in, nullptr, nullptr, 0, G);
+    const int RP = (r + 31) / 32 * 32;
+    dora_rows_kernel<<<blocks_for(out, 128), 128, 0, st>>>(B, m, P, base, G, r, RP, out, s, Q, nsq, g);
+}
+
+void dora_finish(const float* dg, const float* nsq, const float* g, const float* m, const float* B,
+                 const float* P, const float* Q, const float* A, int r, int RP, int in, int out, float s,
+                 float* gm, float* gB, float* gA, bf16* BD, float* scratch, cudaStream_t st) {
+    float* dt3 = scratch;           // [out]
+    float* dG = scratch + out;      // [r][r]
+    dora_tail_kernel<<<blocks_for(out, 128), 128, 0, st>>>(dg, nsq, g, B, P, Q, r, RP, out, s, gm, gB, BD, dt3);
+    gram_kernel<<<r * r, 256, 0, st>>>(nullptr, r, out, dt3, B, r, dG);
+    dora_ga_kernel<<<blocks_for((long)r * in, 256), 256, 0, st>>>(dG, A, r, in, gA);
+    (void)m;
+}
+
+void refresh_bf16(const CopyJob* jobs_dev, int njobs, int max_elems, cudaStream_t s) {
+    if (njobs <= 0) return;
+    dim3 grid(blocks_for(max_elems, 256) > 256 ? 256 : blocks_for(max_elems, 256), njobs);
+    refresh_kernel<<<grid, 256, 0, s>>>(jobs_dev);
+}
+
+void adamw(float* value, float* m, float* v, float* grad, const uint8_t* decay_mask, long n, float count,
+           float clip, float lr, float beta1, float beta2, float eps, float decay, float bc1, float bc2,
+           double* partials, int* nonfinite, cudaStream_t s) {
+    const int nparts = 592;
+    grad_norm_kernel<<<nparts, 256, 0, s>>>(grad, n, count, partials);
+    adamw_kernel<<<592, 256, 0, s>>>(value, m, v, grad, decay_mask, n, count, clip, lr, beta1, beta2, eps,
+                                     decay, bc1, bc2, partials, nparts, nonfinite);
+}
+
+void q8_0_to_bf16(const uint8_t* blocks, long nblocks, bf16* out, cudaStream_t s) {
+    q8_bf16_kernel<<<blocks_for(nblocks * 32, 256), 256, 0, s>>>(blocks, nblocks, out);
+}
+
+void q8_0_to_f32(const uint8_t* blocks, long nblocks, float* out, cudaStream_t s) {
+    q8_f32_kernel<<<blocks_for(nblocks * 32, 256), 256, 0, s>>>(blocks, nblocks, out);
+}
+
+void f16_to_bf16(const uint16_t* in, long n, bf16* out, cudaStream_t s) {
+    f16_bf16_kernel<<<blocks_for(n, 256), 256, 0, s>>>(in, n, out);
+}
+
+void mg_embed(const int32_t* ids, int steps, int nq, const float* const* emb_dev, const float* pos, float* x,
+              int D, int seqs, cudaStream_t s) {
+    const long n = (long)seqs * steps * D;
+    mg_embed_kernel<<<blocks_for(n, 256), 256, 0, s>>>(ids, steps, nq, emb_dev, pos, x, D, seqs);
+}
+
+void mg_cross_entropy(const float* logits, int rows, int card, const int32_t* targets, int rows_per_seq,
+                      float inv_nsel, float* loss_acc, bf16* dlogits, cudaStream_t s) {
+    mg_ce_kernel<<<rows, 256, 0, s>>>(logits, card, targets, rows_per_seq, inv_nsel, loss_acc, dlogits);
+}
+
+}  // namespace act

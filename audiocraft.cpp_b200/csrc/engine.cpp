@@ -1,0 +1,1488 @@
+// engine.cpp -- host side of libactrain.so: the C ABI of include/actrain.h.
+//
+// One act_ctx owns one device: the frozen base weights (bf16, dequantised once from
+// F32/F16/Q8_0 at bind time), the fp32 adapter master parameters with their Adam moments and
+// gradient accumulator, the activation arena sized for (max_batch, frames, tokens), and one
+// CUDA graph per microbatch size that replays the whole forward + backward.
+//
+// The schedule restates, layer by layer, the reference training graph:
+//   MelodyFlow: dit_forward / dit_block (src/mf/dit.h:105-212) + MSE (src/mf/train.h:107)
+//   MusicGen:   mg_train_forward (src/mg/train.h:12-49) + cross entropy (src/mg/train.h:131)
+// with the backward written out explicitly (ggml autodiff in the reference,
+// src/mf/train.h:118) and the optimizer of TrainAccumulation::update
+// (src/ac/train_controls.h:89-118) run on the device.
+#include "actrain.h"
+
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <random>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "kernels.h"
+
+using namespace act;
+
+namespace {
+
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+#define CK(x)                                                                                 \
+    do {                                                                                      \
+        cudaError_t e_ = (x);                                                                 \
+        if (e_ != cudaSuccess) throw Error(ACT_ERR_CUDA, std::string(#x) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+#define NK(x)                                                                                 \
+    do {                                                                                      \
+        ncclResult_t r_ = (x);                                                                \
+        if (r_ != ncclSuccess) throw Error(ACT_ERR_NCCL, std::string(#x) + ": " + ncclGetErrorString(r_)); \
+    } while (0)
+
+thread_local std::string g_error;
+
+const char* const kTargets[7] = {"self.qkv", "self.out", "cross.q", "cross.kv", "cross.out", "ff.0", "ff.2"};
+
+struct Proj {
+    int in = 0, out = 0;
+    bf16* W = nullptr;
+    bool bound = false;
+    bool adapted = false, dora = false;
+    int r = 0, RP = 0;
+    float s = 0.f;
+    int64_t offA = 0, offB = 0, offM = -1;
+    bf16* A_bf = nullptr;  // [RP][in], rows >= r zero
+    bf16* B_bf = nullptr;  // [out][RP], cols >= r zero
+    float* base = nullptr; // DoRA: frozen ||W_o||^2 + in*1e-12 (double accumulated on the host)
+    float *P = nullptr, *G = nullptr, *Q = nullptr, *nsq = nullptr, *g = nullptr, *dg = nullptr, *scr = nullptr;
+    bf16* BD = nullptr;
+};
+
+struct Layer {
+    Proj p[7];
+    float* norm[6] = {};  // norm1.w, norm1.b, norm_cross.w, norm_cross.b, norm2.w, norm2.b
+    bool consumes = false, produces = false;
+    int proj = 0, src = -1;
+    float *xin = nullptr, *xmid = nullptr, *xmid2 = nullptr, *xout = nullptr;
+    float *mu[3] = {}, *rs[3] = {};
+    bf16 *h1 = nullptr, *hc = nullptr, *f = nullptr, *qkv = nullptr, *o1 = nullptr, *cq = nullptr;
+    bf16 *ckv = nullptr, *o2 = nullptr, *z = nullptr, *gact = nullptr;
+    bf16* U[7] = {};
+    bf16* Yaux[7] = {};
+    float *lse1 = nullptr, *lse2 = nullptr;
+    bf16* xsave_bf = nullptr;
+    float* dsaved = nullptr;
+};
+
+struct PInfo {
+    std::string name;
+    int64_t off, rows, cols;
+};
+
+struct KStat {
+    double ms = 0, flops = 0, bytes = 0;
+    int64_t launches = 0;
+};
+
+}  // namespace
+
+struct act_ctx {
+    int device = 0;
+    act_model_desc md{};
+    act_adapter_desc ad{};
+    bool mf = true;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    bool finalized = false;
+    std::vector<void*> dallocs;
+    std::vector<void*> hallocs;
+
+    int D = 0, F = 0, H = 0, L = 0, T = 0, C = 0, B = 0, RP = 0;
+    long M = 0, MC = 0;  // activation rows, context rows (capacity)
+
+    std::vector<Layer> layers;
+    // MelodyFlow globals
+    bf16 *in_proj = nullptr, *out_proj = nullptr, *cond_w = nullptr;
+    float *cond_b = nullptr, *te0 = nullptr, *te2 = nullptr, *onw = nullptr, *onb = nullptr;
+    std::vector<bf16*> skip;
+    std::vector<float> rope_ff;
+    float* rope = nullptr;
+    // MusicGen globals
+    std::vector<float*> emb;
+    float** emb_dev = nullptr;
+    std::vector<bf16*> head;
+    float* pos = nullptr;
+    std::map<std::string, bool> bound;
+
+    // parameters
+    int64_t nparam = 0;
+    float *value = nullptr, *mom1 = nullptr, *mom2 = nullptr, *grad = nullptr;
+    uint8_t* decay = nullptr;
+    std::vector<PInfo> ptable;
+    CopyJob* jobs_dev = nullptr;
+    int njobs = 0, max_job = 0;
+    double* partials = nullptr;
+    int* nonfinite_dev = nullptr;
+    int accumulated = 0, count_override = 0;
+
+    // staging (host pinned + device)
+    float *h_clean = nullptr, *h_noise = nullptr, *h_hidden = nullptr, *h_t = nullptr, *h_tfeat = nullptr,
+          *h_loss = nullptr, *h_ctx = nullptr;
+    int32_t *h_nvalid = nullptr, *h_ids = nullptr, *h_tgt = nullptr;
+    float *d_clean = nullptr, *d_noise = nullptr, *d_hidden = nullptr, *d_t = nullptr, *d_tfeat = nullptr,
+          *d_loss = nullptr, *d_ctx = nullptr;
+    int32_t *d_nvalid = nullptr, *d_ids = nullptr, *d_tgt = nullptr;
+
+    // global activations / scratch
+    bf16 *x0 = nullptr, *hidden_bf = nullptr, *ctx_bf = nullptr, *xo = nullptr, *dout = nullptr, *xprev_bf = nullptr;
+    float *vstar = nullptr, *te1 = nullptr, *te = nullptr, *x0f = nullptr, *muo = nullptr, *rso = nullptr,
+          *outp = nullptr;
+    float *dx = nullptr, *dtmp = nullptr, *dq_acc = nullptr, *dvec = nullptr;
+    bf16 *dxbf = nullptr, *dz = nullptr, *dU = nullptr, *dob = nullptr, *dqkv = nullptr, *dcq = nullptr,
+         *dckv = nullptr;
+    float* logits = nullptr;
+    bf16* dlogits = nullptr;
+
+    // execution
+    std::map<int, cudaGraphExec_t> graphs;
+    std::map<int, int> eager_runs;
+    std::map<int, int64_t> kernel_nodes;
+    int staged_n = -1;
+    bool profiling = false;
+    KStat stats[3];
+    struct PendingEv {
+        cudaEvent_t a, b;
+        int cls;
+        double flops, bytes;
+    };
+    std::vector<PendingEv> pending;
+    std::vector<cudaEvent_t> evpool;
+    size_t evnext = 0;
+
+    ncclComm_t comm = nullptr;
+
+    // ------------------------------------------------------------------------------------
+    template <class Tp>
+    Tp* dalloc(size_t n) {
+        void* p = nullptr;
+        const size_t bytes = std::max<size_t>(n * sizeof(Tp), 16);
+        CK(cudaMalloc(&p, bytes));
+        CK(cudaMemsetAsync(p, 0, bytes, stream));
+        dallocs.push_back(p);
+        return static_cast<Tp*>(p);
+    }
+    template <class Tp>
+    Tp* halloc(size_t n) {
+        void* p = nullptr;
+        CK(cudaMallocHost(&p, std::max<size_t>(n * sizeof(Tp), 16)));
+        hallocs.push_back(p);
+        return static_cast<Tp*>(p);
+    }
+
+    // ---------------------------------------------------------------- timing helpers
+    cudaEvent_t next_event() {
+        if (evnext >= evpool.size()) {
+            cudaEvent_t e;
+            CK(cudaEventCreate(&e));
+            evpool.push_back(e);
+        }
+        return evpool[evnext++];
+    }
+    template <class Fn>
+    void timed(int cls, double flops, double bytes, Fn&& fn) {
+        if (!profiling) {
+            fn();
+            return;
+        }
+        cudaEvent_t a = next_event(), b = next_event();
+        CK(cudaEventRecord(a, stream));
+        fn();
+        CK(cudaEventRecord(b, stream));
+        pending.push_back({a, b, cls, flops, bytes});
+    }
+    void collect_stats() {
+        if (pending.empty()) return;
+        CK(cudaStreamSynchronize(stream));
+        for (auto& p : pending) {
+            float ms = 0;
+            CK(cudaEventElapsedTime(&ms, p.a, p.b));
+            stats[p.cls].ms += ms;
+            stats[p.cls].flops += p.flops;
+            stats[p.cls].bytes += p.bytes;
+            stats[p.cls].launches += 1;
+        }
+        pending.clear();
+        evnext = 0;
+    }
+
+    void run_gemm(const GemmArgs& g, int cls = 0) {
+        const double fl = 2.0 * g.M * g.N * (double)(g.K1 + g.K2);
+        timed(cls, fl, 0, [&] { gemm(g, stream); });
+    }
+
+    static int splitk_for(long tiles, long ktiles) {
+        long s = std::max<long>(1, 296 / std::max<long>(tiles, 1));
+        s = std::min<long>(s, std::max<long>(1, ktiles / 4));
+        return (int)std::min<long>(s, 64);
+    }
+
+    // ---------------------------------------------------------------- projections
+    // Y = (X W^T + s (X A^T) B^T) * g  with the epilogue given in `e` (mode/out/ldo/resid/aux).
+    void proj_fwd(Proj& p, const bf16* X, long rows, bf16* U, GemmArgs e) {
+        if (p.adapted) {
+            GemmArgs u;
+            u.M = (int)rows; u.N = p.RP; u.K1 = p.in;
+            u.A1 = X; u.lda1 = p.in; u.B1 = p.A_bf; u.ldb1 = p.in;
+            u.mode = EPI_STORE_BF16; u.alpha = p.s; u.out = U; u.ldo = p.RP;
+            run_gemm(u, 2);
+        }
+        e.M = (int)rows; e.N = p.out; e.K1 = p.in;
+        e.A1 = X; e.lda1 = p.in; e.B1 = p.W; e.ldb1 = p.in;
+        if (p.adapted) {
+            e.K2 = p.RP; e.A2 = U; e.lda2 = p.RP; e.B2 = p.B_bf; e.ldb2 = p.RP;
+        }
+        if (p.dora) e.colscale = p.g;
+        run_gemm(e, 0);
+    }
+
+    // Adapter gradients of one projection from dYl (= dY * g, bf16 [rows][out]) and, when
+    // `e` has an output, the input gradient dX = dYl W + dU A.
+    void proj_bwd(Proj& p, const bf16* dYl, long rows, const bf16* X, const bf16* U, const bf16* Y,
+                  bool want_dx, GemmArgs e) {
+        if (p.dora) timed(2, 0, 4.0 * rows * p.out, [&] { dora_colsum(dYl, p.out, Y, p.out, (int)rows, p.out, p.g, p.dg, stream); });
+        if (p.adapted) {
+            GemmArgs u;
+            u.M = (int)rows; u.N = p.RP; u.K1 = p.out;
+            u.A1 = dYl; u.lda1 = p.out; u.B1 = p.B_bf; u.ldb1 = p.RP; u.b_kmajor = false;
+            u.mode = EPI_STORE_BF16; u.alpha = p.s; u.out = dU; u.ldo = p.RP;
+            run_gemm(u, 2);
+            GemmArgs gb;
+            gb.M = p.out; gb.N = p.RP; gb.K1 = (int)rows;
+            gb.A1 = dYl; gb.lda1 = p.out; gb.a_kmajor = false;
+            gb.B1 = U; gb.ldb1 = p.RP; gb.b_kmajor = false;
+            gb.mode = EPI_ATOMIC_F32; gb.out = grad + p.offB; gb.ldo = p.r; gb.nvalid = p.r;
+            gb.splitk = splitk_for((long)((p.out + 127) / 128), (rows + 31) / 32);
+            run_gemm(gb, 2);
+            GemmArgs ga;
+            ga.M = p.RP; ga.N = p.in; ga.K1 = (int)rows;
+            ga.A1 = dU; ga.lda1 = p.RP; ga.a_kmajor = false;
+            ga.B1 = X; ga.ldb1 = p.in; ga.b_kmajor = false;
+            ga.mode = EPI_ATOMIC_F32; ga.out = grad + p.offA; ga.ldo = p.in; ga.mvalid = p.r;
+            ga.splitk = splitk_for((long)((p.in + 127) / 128), (rows + 31) / 32);
+            run_gemm(ga, 2);
+        }
+        if (!want_dx) return;
+        e.M = (int)rows; e.N = p.in; e.K1 = p.out;
+        e.A1 = dYl; e.lda1 = p.out; e.B1 = p.W; e.ldb1 = p.in; e.b_kmajor = false;
+        if (p.adapted) {
+            e.K2 = p.RP; e.A2 = dU; e.lda2 = p.RP; e.B2 = p.A_bf; e.ldb2 = p.in;
+        }
+        run_gemm(e, 0);
+    }
+
+    // ---------------------------------------------------------------- the step
+    void prepare_adapters() {
+        timed(2, 0, 0, [&] { refresh_bf16(jobs_dev, njobs, max_job, stream); });
+        for (auto& lay : layers)
+            for (auto& p : lay.p) {
+                if (!p.dora) continue;
+                GemmArgs a;
+                a.M = p.out; a.N = p.RP; a.K1 = p.in;
+                a.A1 = p.W; a.lda1 = p.in; a.B1 = p.A_bf; a.ldb1 = p.in;
+                a.mode = EPI_STORE_F32; a.out = p.P; a.ldo = p.RP;
+                run_gemm(a, 2);
+                timed(2, 0, 0, [&] {
+                    dora_prepare(value + p.offA, value + p.offB, value + p.offM, p.P, p.base, p.r, p.in, p.out, p.s,
+                                 p.G, p.Q, p.nsq, p.g, stream);
+                    CK(cudaMemsetAsync(p.dg, 0, sizeof(float) * p.out, stream));
+                });
+            }
+    }
+
+    void finish_adapters() {
+        for (auto& lay : layers)
+            for (auto& p : lay.p) {
+                if (!p.dora) continue;
+                timed(2, 0, 0, [&] {
+                    dora_finish(p.dg, p.nsq, p.g, value + p.offM, value + p.offB, p.P, p.Q, value + p.offA, p.r,
+                                p.RP, p.in, p.out, p.s, grad + p.offM, grad + p.offB, grad + p.offA, p.BD, p.scr,
+                                stream);
+                });
+                GemmArgs a;  // gA += BD^T W
+                a.M = p.RP; a.N = p.in; a.K1 = p.out;
+                a.A1 = p.BD; a.lda1 = p.RP; a.a_kmajor = false;
+                a.B1 = p.W; a.ldb1 = p.in; a.b_kmajor = false;
+                a.mode = EPI_ATOMIC_F32; a.out = grad + p.offA; a.ldo = p.in; a.mvalid = p.r;
+                a.splitk = splitk_for((p.in + 127) / 128, (p.out + 31) / 32);
+                run_gemm(a, 2);
+            }
+    }
+
+    // One transformer block forward.  te: per-clip timestep embedding (MelodyFlow) or null.
+    void block_fwd(int l, int n, const int* nvalid_dev) {
+        Layer& y = layers[l];
+        const long rows = (long)n * T, crows = (long)n * C;
+        const float eps = md.norm_eps;
+        const bool dit = mf;
+        // pre-norm self-attention
+        timed(2, 0, 0, [&] { layernorm_fwd(y.xin, y.norm[0], y.norm[1], dit ? te : nullptr, T, y.h1, y.mu[0], y.rs[0], (int)rows, D, eps, stream); });
+        {
+            GemmArgs e; e.mode = EPI_STORE_BF16; e.out = y.qkv; e.ldo = 3 * D;
+            proj_fwd(y.p[0], y.h1, rows, y.U[0], e);
+        }
+        AttnArgs sa;
+        sa.q = y.qkv; sa.k = y.qkv + D; sa.v = y.qkv + 2 * D; sa.ldq = sa.ldk = sa.ldv = 3 * D;
+        sa.T = T; sa.Tk = T; sa.H = H; sa.clips = n; sa.causal = dit ? 0 : 1; sa.zero_key = dit ? md.add_zero_attn : 0;
+        sa.rope = dit ? rope : nullptr; sa.scale = 1.0f / std::sqrt((float)md.head_dim);
+        sa.o = y.o1; sa.ldo = D; sa.lse = y.lse1;
+        timed(1, attn_flops(n, T, true), 0, [&] { attn_fwd(sa, stream); });
+        {
+            GemmArgs e; e.mode = EPI_RESID_F32; e.out = y.xmid; e.ldo = D; e.resid = y.xin; e.ldr = D;
+            if (y.p[1].dora) { e.aux = y.Yaux[1]; e.ldaux = D; }
+            proj_fwd(y.p[1], y.o1, rows, y.U[1], e);
+        }
+        // cross-attention
+        timed(2, 0, 0, [&] { layernorm_fwd(y.xmid, y.norm[2], y.norm[3], dit ? te : nullptr, T, y.hc, y.mu[1], y.rs[1], (int)rows, D, eps, stream); });
+        {
+            GemmArgs e; e.mode = EPI_STORE_BF16; e.out = y.cq; e.ldo = D;
+            proj_fwd(y.p[2], y.hc, rows, y.U[2], e);
+            GemmArgs k; k.mode = EPI_STORE_BF16; k.out = y.ckv; k.ldo = 2 * D;
+            proj_fwd(y.p[3], ctx_bf, crows, y.U[3], k);
+        }
+        AttnArgs ca;
+        ca.q = y.cq; ca.ldq = D; ca.k = y.ckv; ca.v = y.ckv + D; ca.ldk = ca.ldv = 2 * D;
+        ca.T = T; ca.Tk = C; ca.H = H; ca.clips = n; ca.nvalid = dit ? nvalid_dev : nullptr;
+        ca.zero_key = dit ? md.add_zero_attn : 0; ca.scale = sa.scale;
+        ca.o = y.o2; ca.ldo = D; ca.lse = y.lse2;
+        timed(1, attn_flops(n, C, false), 0, [&] { attn_fwd(ca, stream); });
+        {
+            GemmArgs e; e.mode = EPI_RESID_F32; e.out = y.xmid2; e.ldo = D; e.resid = y.xmid; e.ldr = D;
+            if (y.p[4].dora) { e.aux = y.Yaux[4]; e.ldaux = D; }
+            proj_fwd(y.p[4], y.o2, rows, y.U[4], e);
+        }
+        // feed-forward (no timestep)
+        timed(2, 0, 0, [&] { layernorm_fwd(y.xmid2, y.norm[4], y.norm[5], nullptr, T, y.f, y.mu[2], y.rs[2], (int)rows, D, eps, stream); });
+        {
+            GemmArgs e; e.mode = EPI_GELU; e.out = y.gact; e.ldo = F; e.aux = y.z; e.ldaux = F;
+            proj_fwd(y.p[5], y.f, rows, y.U[5], e);
+            GemmArgs o; o.mode = EPI_RESID_F32; o.out = y.xout; o.ldo = D; o.resid = y.xmid2; o.ldr = D;
+            if (y.p[6].dora) { o.aux = y.Yaux[6]; o.ldaux = D; }
+            proj_fwd(y.p[6], y.gact, rows, y.U[6], o);
+        }
+        if (y.produces) timed(2, 0, 0, [&] { residual_to_bf16(y.xout, nullptr, y.xsave_bf, nullptr, (int)rows, D, stream); });
+    }
+
+    // Backward of block l.  On entry dx/dxbf hold d(loss)/d(xout) (dxbf already scaled by
+    // the DoRA factor of ff.2).  On exit dx holds d(loss)/d(xin) and dxbf is NOT prepared.
+    void block_bwd(int l, int n, const int* nvalid_dev, bool need_dx_in) {
+        Layer& y = layers[l];
+        const long rows = (long)n * T, crows = (long)n * C;
+        const bool dit = mf;
+        // ---- feed-forward
+        {
+            GemmArgs e; e.mode = EPI_GELU_BWD; e.out = dz; e.ldo = F; e.auxin = y.z; e.ldauxin = F;
+            e.colscale2 = y.p[5].dora ? y.p[5].g : nullptr;
+            proj_bwd(y.p[6], dxbf, rows, y.gact, y.U[6], y.Yaux[6], true, e);
+            GemmArgs d; d.mode = EPI_STORE_F32; d.out = dtmp; d.ldo = D;
+            proj_bwd(y.p[5], dz, rows, y.f, y.U[5], y.z, true, d);
+        }
+        timed(2, 0, 0, [&] { layernorm_bwd(dtmp, y.xmid2, y.norm[4], y.mu[2], y.rs[2], dx, 1, nullptr, dxbf, y.p[4].dora ? y.p[4].g : nullptr, (int)rows, D, stream); });
+        // ---- cross-attention
+        {
+            GemmArgs e; e.mode = EPI_STORE_BF16; e.out = dob; e.ldo = D;
+            proj_bwd(y.p[4], dxbf, rows, y.o2, y.U[4], y.Yaux[4], true, e);
+        }
+        AttnArgs ca;
+        ca.q = y.cq; ca.ldq = D; ca.k = y.ckv; ca.v = y.ckv + D; ca.ldk = ca.ldv = 2 * D;
+        ca.T = T; ca.Tk = C; ca.H = H; ca.clips = n; ca.nvalid = dit ? nvalid_dev : nullptr;
+        ca.zero_key = dit ? md.add_zero_attn : 0; ca.scale = 1.0f / std::sqrt((float)md.head_dim);
+        ca.o = y.o2; ca.ldo = D; ca.lse = y.lse2;
+        ca.dout = dob; ca.lddo = D; ca.dvec = dvec; ca.dq_acc = dq_acc; ca.ldq_acc = D;
+        ca.dk = dckv; ca.dv = dckv + D; ca.lddk = ca.lddv = 2 * D;
+        ca.kscale = y.p[3].dora ? y.p[3].g : nullptr; ca.vscale = y.p[3].dora ? y.p[3].g + D : nullptr;
+        timed(1, 2 * attn_flops(n, C, false), 0, [&] {
+            CK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * D, stream));
+            attn_bwd(ca, stream);
+            attn_dq_finish(ca, dcq, D, y.p[2].dora ? y.p[2].g : nullptr, stream);
+        });
+        proj_bwd(y.p[3], dckv, crows, ctx_bf, y.U[3], y.ckv, false, GemmArgs());
+        {
+            GemmArgs e; e.mode = EPI_STORE_F32; e.out = dtmp; e.ldo = D;
+            proj_bwd(y.p[2], dcq, rows, y.hc, y.U[2], y.cq, true, e);
+        }
+        timed(2, 0, 0, [&] { layernorm_bwd(dtmp, y.xmid, y.norm[2], y.mu[1], y.rs[1], dx, 1, nullptr, dxbf, y.p[1].dora ? y.p[1].g : nullptr, (int)rows, D, stream); });
+        // ---- self-attention
+        {
+            GemmArgs e; e.mode = EPI_STORE_BF16; e.out = dob; e.ldo = D;
+            proj_bwd(y.p[1], dxbf, rows, y.o1, y.U[1], y.Yaux[1], true, e);
+        }
+        AttnArgs sa;
+        sa.q = y.qkv; sa.k = y.qkv + D; sa.v = y.qkv + 2 * D; sa.ldq = sa.ldk = sa.ldv = 3 * D;
+        sa.T = T; sa.Tk = T; sa.H = H; sa.clips = n; sa.causal = dit ? 0 : 1; sa.zero_key = dit ? md.add_zero_attn : 0;
+        sa.rope = dit ? rope : nullptr; sa.scale = ca.scale;
+        sa.o = y.o1; sa.ldo = D; sa.lse = y.lse1;
+        sa.dout = dob; sa.lddo = D; sa.dvec = dvec; sa.dq_acc = dq_acc; sa.ldq_acc = D;
+        sa.dk = dqkv + D; sa.dv = dqkv + 2 * D; sa.lddk = sa.lddv = 3 * D;
+        sa.kscale = y.p[0].dora ? y.p[0].g + D : nullptr; sa.vscale = y.p[0].dora ? y.p[0].g + 2 * D : nullptr;
+        timed(1, 2 * attn_flops(n, T, true), 0, [&] {
+            CK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * D, stream));
+            attn_bwd(sa, stream);
+            attn_dq_finish(sa, dqkv, 3 * D, y.p[0].dora ? y.p[0].g : nullptr, stream);
+        });
+        {
+            GemmArgs e; e.mode = EPI_STORE_F32; e.out = dtmp; e.ldo = D;
+            proj_bwd(y.p[0], dqkv, rows, y.h1, y.U[0], y.qkv, need_dx_in, e);
+        }
+        if (need_dx_in)
+            timed(2, 0, 0, [&] { layernorm_bwd(dtmp, y.xin, y.norm[0], y.mu[0], y.rs[0], dx, 1, nullptr, nullptr, nullptr, (int)rows, D, stream); });
+    }
+
+    double attn_flops(int n, int keys, bool self) const {
+        const double tk = keys + ((mf && md.add_zero_attn) ? 1 : 0);
+        double f = 4.0 * n * T * tk * D;
+        if (self && !mf) f = 4.0 * n * (T * (T + 1.0) / 2.0) * D;  // causal
+        return f;
+    }
+
+    // dxbf := bf16((dx + dsaved[l]) * g_ff2(l))  -- entering block l's backward
+    void prepare_dxbf(int l, int n) {
+        Layer& y = layers[l];
+        const long rows = (long)n * T;
+        timed(2, 0, 0, [&] { residual_to_bf16(dx, y.produces ? y.dsaved : nullptr, dxbf, y.p[6].dora ? y.p[6].g : nullptr, (int)rows, D, stream); });
+    }
+
+    void mf_graph_body(int n) {
+        const long rows = (long)n * T, crows = (long)n * C;
+        prepare_adapters();
+        timed(2, 0, 0, [&] {
+            mf_inputs(d_clean, d_noise, d_t, n, T, md.latent_dim, x0, vstar, stream);
+            linear_f32(d_tfeat, te0, te1, n, D, md.time_dim, 1, stream);
+            linear_f32(te1, te2, te, n, D, D, 0, stream);
+            f32_to_bf16(d_hidden, hidden_bf, crows * md.cond_dim, stream);
+        });
+        {
+            GemmArgs c;  // context = hidden cond_proj^T + bias
+            c.M = (int)crows; c.N = D; c.K1 = md.cond_dim; c.A1 = hidden_bf; c.lda1 = md.cond_dim;
+            c.B1 = cond_w; c.ldb1 = md.cond_dim; c.mode = EPI_BIAS_BF16; c.bias = cond_b; c.out = ctx_bf; c.ldo = D;
+            run_gemm(c, 0);
+            GemmArgs x;  // in_proj
+            x.M = (int)rows; x.N = D; x.K1 = md.latent_dim; x.A1 = x0; x.lda1 = md.latent_dim;
+            x.B1 = in_proj; x.ldb1 = md.latent_dim; x.mode = EPI_STORE_F32; x.out = x0f; x.ldo = D;
+            run_gemm(x, 0);
+        }
+        for (int l = 0; l < L; ++l) {
+            Layer& y = layers[l];
+            if (y.consumes) {
+                timed(2, 0, 0, [&] { residual_to_bf16(layers[l - 1].xout, nullptr, xprev_bf, nullptr, (int)rows, D, stream); });
+                GemmArgs k;
+                k.M = (int)rows; k.N = D; k.K1 = D; k.K2 = D;
+                k.A1 = xprev_bf; k.lda1 = D; k.A2 = layers[y.src].xsave_bf; k.lda2 = D;
+                k.B1 = skip[y.proj]; k.ldb1 = 2 * D; k.B2 = skip[y.proj] + D; k.ldb2 = 2 * D;
+                k.mode = EPI_STORE_F32; k.out = y.xin; k.ldo = D;
+                run_gemm(k, 0);
+            }
+            block_fwd(l, n, d_nvalid);
+        }
+        Layer& last = layers[L - 1];
+        timed(2, 0, 0, [&] { layernorm_fwd(last.xout, onw, onb, nullptr, T, xo, muo, rso, (int)rows, D, md.norm_eps, stream); });
+        {
+            GemmArgs o;
+            o.M = (int)rows; o.N = md.latent_dim; o.K1 = D; o.A1 = xo; o.lda1 = D; o.B1 = out_proj; o.ldb1 = D;
+            o.mode = EPI_STORE_F32; o.out = outp; o.ldo = md.latent_dim;
+            run_gemm(o, 0);
+        }
+        timed(2, 0, 0, [&] { mf_loss(outp, vstar, n, T, md.latent_dim, d_loss, dout, stream); });
+        // ---------------- backward
+        {
+            GemmArgs d;
+            d.M = (int)rows; d.N = D; d.K1 = md.latent_dim; d.A1 = dout; d.lda1 = md.latent_dim;
+            d.B1 = out_proj; d.ldb1 = D; d.b_kmajor = false; d.mode = EPI_STORE_F32; d.out = dtmp; d.ldo = D;
+            run_gemm(d, 0);
+        }
+        timed(2, 0, 0, [&] {
+            for (auto& y : layers)
+                if (y.produces) CK(cudaMemsetAsync(y.dsaved, 0, sizeof(float) * rows * D, stream));
+            layernorm_bwd(dtmp, last.xout, onw, muo, rso, dx, 0, nullptr, nullptr, nullptr, (int)rows, D, stream);
+        });
+        const int first = ad.first_layer;
+        for (int l = L - 1; l >= first; --l) {
+            Layer& y = layers[l];
+            prepare_dxbf(l, n);
+            const bool need_dx = l > first;
+            block_bwd(l, n, d_nvalid, need_dx);
+            if (need_dx && y.consumes) {
+                timed(2, 0, 0, [&] { residual_to_bf16(dx, nullptr, dxbf, nullptr, (int)rows, D, stream); });
+                GemmArgs a;  // d x_prev = dx Wskip[:, :D]
+                a.M = (int)rows; a.N = D; a.K1 = D; a.A1 = dxbf; a.lda1 = D;
+                a.B1 = skip[y.proj]; a.ldb1 = 2 * D; a.b_kmajor = false; a.mode = EPI_STORE_F32; a.out = dx; a.ldo = D;
+                run_gemm(a, 0);
+                GemmArgs b = a;  // d saved += dx Wskip[:, D:]
+                b.B1 = skip[y.proj] + D; b.mode = EPI_ACCUM_F32; b.out = layers[y.src].dsaved;
+                run_gemm(b, 0);
+            }
+        }
+        finish_adapters();
+    }
+
+    void mg_graph_body(int n) {
+        const long rows = (long)n * T, crows = (long)n * C;
+        const int frames = ad.frames, prefix = ad.prefix_frames, nq = md.n_q, card = md.card;
+        const int sel = frames - prefix;
+        prepare_adapters();
+        timed(2, 0, 0, [&] {
+            mg_embed(d_ids, T, nq, emb_dev, pos, x0f, D, n, stream);
+            f32_to_bf16(d_ctx, ctx_bf, crows * D, stream);
+        });
+        for (int l = 0; l < L; ++l) block_fwd(l, n, nullptr);
+        Layer& last = layers[L - 1];
+        timed(2, 0, 0, [&] {
+            layernorm_fwd(last.xout, onw, onb, nullptr, T, xo, muo, rso, (int)rows, D, md.norm_eps, stream);
+            CK(cudaMemsetAsync(d_loss, 0, sizeof(float) * n, stream));
+            CK(cudaMemsetAsync(dtmp, 0, sizeof(float) * rows * D, stream));
+        });
+        const float inv_nsel = 1.0f / (float)(nq * sel);
+        for (int b = 0; b < n; ++b)
+            for (int q = 0; q < nq; ++q) {
+                const long r0 = (long)b * T + q + prefix;  // rows s = q + prefix .. q + frames - 1
+                float* lg = logits + ((long)(b * nq + q) * sel) * card;
+                bf16* dl = dlogits + ((long)(b * nq + q) * sel) * card;
+                GemmArgs hgm;
+                hgm.M = sel; hgm.N = card; hgm.K1 = D; hgm.A1 = xo + r0 * D; hgm.lda1 = D;
+                hgm.B1 = head[q]; hgm.ldb1 = D; hgm.mode = EPI_STORE_F32; hgm.out = lg; hgm.ldo = card;
+                run_gemm(hgm, 0);
+                timed(2, 0, 0, [&] {
+                    mg_cross_entropy(lg, sel, card, d_tgt + (long)(b * nq + q) * sel, sel * nq, inv_nsel,
+                                     d_loss + b, dl, stream);
+                });
+                GemmArgs dg;
+                dg.M = sel; dg.N = D; dg.K1 = card; dg.A1 = dl; dg.lda1 = card;
+                dg.B1 = head[q]; dg.ldb1 = D; dg.b_kmajor = false;
+                dg.mode = EPI_ACCUM_F32; dg.out = dtmp + r0 * D; dg.ldo = D;
+                run_gemm(dg, 0);
+            }
+        timed(2, 0, 0, [&] { layernorm_bwd(dtmp, last.xout, onw, muo, rso, dx, 0, nullptr, nullptr, nullptr, (int)rows, D, stream); });
+        const int first = ad.first_layer;
+        for (int l = L - 1; l >= first; --l) {
+            prepare_dxbf(l, n);
+            block_bwd(l, n, nullptr, l > first);
+        }
+        finish_adapters();
+    }
+
+    void run_body(int n) {
+        if (mf) mf_graph_body(n);
+        else mg_graph_body(n);
+    }
+
+    void launch_step(int n) {
+        if (profiling) {
+            run_body(n);
+            CK(cudaGetLastError());
+            collect_stats();
+            return;
+        }
+        auto it = graphs.find(n);
+        if (it == graphs.end()) {
+            if (eager_runs[n]++ == 0) {  // first use of this size runs eagerly (sets kernel attributes)
+                run_body(n);
+                CK(cudaGetLastError());
+                return;
+            }
+            cudaGraph_t graph;
+            CK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+            try {
+                run_body(n);
+            } catch (...) {
+                cudaStreamEndCapture(stream, &graph);
+                throw;
+            }
+            CK(cudaStreamEndCapture(stream, &graph));
+            size_t nn = 0;
+            CK(cudaGraphGetNodes(graph, nullptr, &nn));
+            std::vector<cudaGraphNode_t> nodes(nn);
+            CK(cudaGraphGetNodes(graph, nodes.data(), &nn));
+            int64_t kn = 0;
+            for (auto nd : nodes) {
+                cudaGraphNodeType ty;
+                CK(cudaGraphNodeGetType(nd, &ty));
+                kn += ty == cudaGraphNodeTypeKernel;
+            }
+            kernel_nodes[n] = kn;
+            cudaGraphExec_t exec;
+            CK(cudaGraphInstantiate(&exec, graph, 0));
+            CK(cudaGraphDestroy(graph));
+            it = graphs.emplace(n, exec).first;
+        }
+        CK(cudaGraphLaunch(it->second, stream));
+    }
+
+    // ---------------------------------------------------------------- staging
+    void stage_mf(const act_mf_batch* b) {
+        if (!mf) throw Error(ACT_ERR_INVALID, "not a MelodyFlow context");
+        if (!b || b->n <= 0 || b->n > B || !b->clean || !b->noise || !b->hidden || !b->t)
+            throw Error(ACT_ERR_INVALID, "invalid training sample");
+        const int n = b->n, lat = md.latent_dim;
+        const size_t nx = (size_t)n * lat * T, nh = (size_t)n * C * md.cond_dim;
+        for (int i = 0; i < n; ++i) {
+            const float t = b->t[i];
+            if (!std::isfinite(t) || t < 0 || t > 1) throw Error(ACT_ERR_INVALID, "invalid training sample");
+            const int v = b->valid_tokens ? b->valid_tokens[i] : -1;
+            if (v > C) throw Error(ACT_ERR_INVALID, "invalid valid token count");
+            const bool uncond = b->unconditional && b->unconditional[i];
+            h_nvalid[i] = uncond ? 0 : (v >= 0 ? v : C);
+            h_t[i] = t;
+            // timestep features on the host, float arithmetic as src/ac/transformer.h:144-154
+            const int half = md.time_dim / 2;
+            float* tf = h_tfeat + (size_t)i * md.time_dim;
+            for (int k = 0; k < md.time_dim; ++k) tf[k] = 0.f;
+            for (int k = 0; k < half; ++k) {
+                const float freq = std::exp(-std::log(10000.0f) * (float)k / (float)half);
+                const float arg = t * freq;
+                tf[k] = std::cos(arg);
+                tf[half + k] = std::sin(arg);
+            }
+        }
+        std::memcpy(h_clean, b->clean, nx * 4);
+        std::memcpy(h_noise, b->noise, nx * 4);
+        std::memcpy(h_hidden, b->hidden, nh * 4);
+        CK(cudaMemcpyAsync(d_clean, h_clean, nx * 4, cudaMemcpyHostToDevice, stream));
+        CK(cudaMemcpyAsync(d_noise, h_noise, nx * 4, cudaMemcpyHostToDevice, stream));
+        CK(cudaMemcpyAsync(d_hidden, h_hidden, nh * 4, cudaMemcpyHostToDevice, stream));
+        CK(cudaMemcpyAsync(d_t, h_t, n * 4, cudaMemcpyHostToDevice, stream));
+        CK(cudaMemcpyAsync(d_tfeat, h_tfeat, (size_t)n * md.time_dim * 4, cudaMemcpyHostToDevice, stream));
+        CK(cudaMemcpyAsync(d_nvalid, h_nvalid, n * 4, cudaMemcpyHostToDevice, stream));
+        staged_n = n;
+    }
+
+    void stage_mg(const act_mg_batch* b) {
+        if (mf) throw Error(ACT_ERR_INVALID, "not a MusicGen context");
+        if (!b || b->n <= 0 || b->n > B || !b->codes || !b->context)
+            throw Error(ACT_ERR_INVALID, "invalid training sample shape");
+        const int n = b->n, nq = md.n_q, frames = ad.frames, prefix = ad.prefix_frames, sel = frames - prefix;
+        const int S = 1 + frames + (nq - 1);  // src/mg/pattern.h:55
+        for (size_t i = 0; i < (size_t)n * nq * frames; ++i)
+            if (b->codes[i] < 0 || b->codes[i] >= md.card) throw Error(ACT_ERR_INVALID, "invalid codec token");
+        for (size_t i = 0; i < (size_t)n * C * D; ++i)
+            if (!std::isfinite(b->context[i])) throw Error(ACT_ERR_INVALID, "nonfinite condition");
+        for (int s = 0; s < n; ++s) {
+            const int32_t* codes = b->codes + (size_t)s * nq * frames;
+            for (int q = 0; q < nq; ++q) {
+                // build_pattern_sequence (src/mg/pattern.h:64-76), inputs = seq[:, :S-1]
+                for (int st = 0; st < T; ++st) {
+                    const int t = st - 1 - q;  // delays[q] = q
+                    h_ids[((size_t)s * nq + q) * T + st] = (st > 0 && t >= 0 && t < frames) ? codes[(size_t)q * frames + t]
+                                                                                             : md.special_token_id;
+                }
+                for (int k = 0; k < sel; ++k) h_tgt[((size_t)s * nq + q) * sel + k] = codes[(size_t)q * frames + prefix + k];
+            }
+        }
+        (void)S;
+        std::memcpy(h_ctx, b->context, (size_t)n * C * D * 4);
+        CK(cudaMemcpyAsync(d_ids, h_ids, (size_t)n * nq * T * 4, cudaMemcpyHostToDevice, stream));
+        CK(cudaMemcpyAsync(d_tgt, h_tgt, (size_t)n * nq * sel * 4, cudaMemcpyHostToDevice, stream));
+        CK(cudaMemcpyAsync(d_ctx, h_ctx, (size_t)n * C * D * 4, cudaMemcpyHostToDevice, stream));
+        staged_n = n;
+    }
+
+    void run_staged(float* loss) {
+        if (!finalized) throw Error(ACT_ERR_STATE, "act_finalize has not been called");
+        if (staged_n <= 0) throw Error(ACT_ERR_STATE, "no staged batch");
+        const int n = staged_n;
+        launch_step(n);
+        accumulated += n;
+        if (loss) {
+            CK(cudaMemcpyAsync(h_loss, d_loss, n * 4, cudaMemcpyDeviceToHost, stream));
+            CK(cudaStreamSynchronize(stream));
+            for (int i = 0; i < n; ++i) {
+                if (!std::isfinite(h_loss[i])) throw Error(ACT_ERR_NONFINITE, "nonfinite training loss");
+                loss[i] = h_loss[i];
+            }
+        }
+    }
+
+    // ---------------------------------------------------------------- setup
+    void setup(int dev, const act_model_desc* m, const act_adapter_desc* a) {
+        device = dev;
+        md = *m;
+        ad = *a;
+        mf = md.family == ACT_FAMILY_MELODYFLOW;
+        if (md.family != ACT_FAMILY_MELODYFLOW && md.family != ACT_FAMILY_MUSICGEN)
+            throw Error(ACT_ERR_INVALID, "unknown model family");
+        if (md.dim != md.heads * md.head_dim) throw Error(ACT_ERR_INVALID, "dim does not equal heads * head_dim");
+        if (md.head_dim != 64) throw Error(ACT_ERR_INVALID, "the attention kernels need head_dim 64");
+        if (md.dim % 128 || md.dim > 2048 || md.ff_dim % 128) throw Error(ACT_ERR_INVALID, "dim and ff_dim must be multiples of 128 (dim <= 2048)");
+        if (mf && md.n_skip != (md.layers - 1) / 2)
+            throw Error(ACT_ERR_INVALID, "DiT skip count does not match (layers - 1) / 2");
+        if (!mf && md.special_token_id != md.card) throw Error(ACT_ERR_INVALID, "special_token_id should be card");
+        if (ad.frames <= 0 || ad.tokens <= 0 || ad.rank <= 0 || ad.rank > md.dim || !std::isfinite(ad.alpha) ||
+            ad.alpha <= 0 || ad.first_layer < 0 || ad.first_layer >= md.layers ||
+            (ad.type != ACT_ADAPTER_LORA && ad.type != ACT_ADAPTER_DORA_ROWS) || ad.max_batch <= 0 ||
+            (ad.targets & ~0x7Fu) || !ad.targets)
+            throw Error(ACT_ERR_INVALID, "invalid training dimensions or adapter configuration");
+        if (!mf && (ad.prefix_frames < 0 || ad.prefix_frames >= ad.frames))
+            throw Error(ACT_ERR_INVALID, "invalid MusicGen training configuration");
+        if (mf && (md.latent_dim % 8 || md.cond_dim % 8 || md.time_dim % 2))
+            throw Error(ACT_ERR_INVALID, "latent_dim and cond_dim must be multiples of 8");
+        if (ad.tokens % 8) throw Error(ACT_ERR_INVALID, "tokens must be a multiple of 8 (pad the conditioning)");
+        CK(cudaSetDevice(device));
+        CK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+        D = md.dim; F = md.ff_dim; H = md.heads; L = md.layers;
+        C = ad.tokens; B = ad.max_batch;
+        T = mf ? ad.frames : ad.frames + md.n_q - 1;  // MusicGen: pattern steps - 1 (src/mg/train.h:74)
+        RP = (ad.rank + 31) / 32 * 32;
+        M = (long)B * T;
+        MC = (long)B * C;
+        layers.resize(L);
+        int sp = 0;
+        std::vector<int> stack;
+        for (int l = 0; l < L; ++l) {
+            Layer& y = layers[l];
+            if (mf) {  // dit_skip_plan, src/mf/dit.h:87-100
+                const double half = (double)L / 2.0;
+                y.consumes = md.n_skip > 0 && (double)l > half;
+                y.produces = md.n_skip > 0 && (double)l < half - 1.0;
+                if (y.consumes) {
+                    if (stack.empty()) throw Error(ACT_ERR_INVALID, "DiT skip stack underflow");
+                    y.proj = l % md.n_skip;
+                    y.src = stack.back();
+                    stack.pop_back();
+                }
+                if (y.produces) stack.push_back(l);
+            }
+            for (int t = 0; t < 7; ++t) {
+                Proj& p = y.p[t];
+                p.in = t == 6 ? F : D;
+                p.out = t == 0 ? 3 * D : t == 3 ? 2 * D : t == 5 ? F : D;
+            }
+        }
+        (void)sp;
+    }
+
+    // GGUF name -> binding
+    void bind(const char* cname, int type, const void* host, size_t bytes) {
+        if (finalized) throw Error(ACT_ERR_STATE, "weights are bound before act_finalize");
+        if (!cname || !host) throw Error(ACT_ERR_INVALID, "null weight");
+        const std::string name = cname;
+        long rows = 0, cols = 0;
+        enum { DST_BF16, DST_F32, DST_HOST } dst_kind = DST_BF16;
+        void** dst = nullptr;
+        Proj* proj = nullptr;
+        const std::string pre = mf ? "dit." : "lm.";
+        auto layer_of = [&](const std::string& rest, int& l, std::string& tail) {
+            const size_t dot = rest.find('.');
+            if (dot == std::string::npos) return false;
+            for (size_t i = 0; i < dot; ++i)
+                if (!isdigit((unsigned char)rest[i])) return false;
+            l = std::stoi(rest.substr(0, dot));
+            tail = rest.substr(dot + 1);
+            return l >= 0 && l < L;
+        };
+        std::vector<float> f32;  // host fp32 copy when needed
+        if (name.rfind(pre, 0) != 0) throw Error(ACT_ERR_INVALID, "unexpected tensor: " + name);
+        const std::string rest = name.substr(pre.size());
+        int l = -1;
+        std::string tail;
+        if (layer_of(rest, l, tail)) {
+            Layer& y = layers[l];
+            static const char* norms[6] = {"norm1.weight", "norm1.bias", "norm_cross.weight", "norm_cross.bias",
+                                           "norm2.weight", "norm2.bias"};
+            for (int i = 0; i < 6; ++i)
+                if (tail == norms[i]) { dst = (void**)&y.norm[i]; dst_kind = DST_F32; rows = 1; cols = D; }
+            for (int t = 0; t < 7; ++t)
+                if (tail == std::string(kTargets[t]) + ".weight") {
+                    proj = &y.p[t];
+                    dst = (void**)&proj->W;
+                    rows = proj->out;
+                    cols = proj->in;
+                }
+        } else if (mf) {
+            if (rest == "in_proj.weight") { dst = (void**)&in_proj; rows = D; cols = md.latent_dim; }
+            else if (rest == "out_proj.weight") { dst = (void**)&out_proj; rows = md.latent_dim; cols = D; }
+            else if (rest == "time_embed.0.weight") { dst = (void**)&te0; dst_kind = DST_F32; rows = D; cols = md.time_dim; }
+            else if (rest == "time_embed.2.weight") { dst = (void**)&te2; dst_kind = DST_F32; rows = D; cols = D; }
+            else if (rest == "cond_proj.weight") { dst = (void**)&cond_w; rows = D; cols = md.cond_dim; }
+            else if (rest == "cond_proj.bias") { dst = (void**)&cond_b; dst_kind = DST_F32; rows = 1; cols = D; }
+            else if (rest == "out_norm.weight") { dst = (void**)&onw; dst_kind = DST_F32; rows = 1; cols = D; }
+            else if (rest == "out_norm.bias") { dst = (void**)&onb; dst_kind = DST_F32; rows = 1; cols = D; }
+            else if (rest == "rope_freq_factors") { dst_kind = DST_HOST; rows = 1; cols = md.head_dim / 2; }
+            else if (rest.rfind("skip.", 0) == 0) {
+                const int i = std::atoi(rest.c_str() + 5);
+                if (i < 0 || i >= md.n_skip || rest != "skip." + std::to_string(i) + ".weight")
+                    throw Error(ACT_ERR_INVALID, "unexpected tensor: " + name);
+                dst = (void**)&skip[i]; rows = D; cols = 2 * D;
+            } else if (rest == "latent_mean" || rest == "latent_std" || rest == "time_embed.0.bias") {
+                return;  // cache normalisation: not used by the step
+            }
+        } else {
+            if (rest == "out_norm.weight") { dst = (void**)&onw; dst_kind = DST_F32; rows = 1; cols = D; }
+            else if (rest == "out_norm.bias") { dst = (void**)&onb; dst_kind = DST_F32; rows = 1; cols = D; }
+            else if (rest.rfind("emb.", 0) == 0 || rest.rfind("head.", 0) == 0) {
+                const bool isemb = rest[0] == 'e';
+                const int q = std::atoi(rest.c_str() + (isemb ? 4 : 5));
+                if (q < 0 || q >= md.n_q) throw Error(ACT_ERR_INVALID, "unexpected tensor: " + name);
+                if (isemb) { dst = (void**)&emb[q]; dst_kind = DST_F32; rows = md.card + 1; cols = D; }
+                else { dst = (void**)&head[q]; rows = md.card; cols = D; }
+            } else if (rest.rfind("cond_proj", 0) == 0) {
+                return;  // the trainer consumes already projected conditioning
+            }
+        }
+        if (!dst && dst_kind != DST_HOST) throw Error(ACT_ERR_INVALID, "unexpected tensor: " + name);
+        const long n = rows * cols;
+        size_t need = 0;
+        if (type == ACT_TYPE_F32) need = (size_t)n * 4;
+        else if (type == ACT_TYPE_F16) need = (size_t)n * 2;
+        else if (type == ACT_TYPE_Q8_0) {
+            if (cols % 32) throw Error(ACT_ERR_INVALID, "Q8_0 rows must hold whole blocks: " + name);
+            need = (size_t)n / 32 * 34;
+        } else throw Error(ACT_ERR_INVALID, "unsupported weight type for " + name);
+        if (bytes != need) throw Error(ACT_ERR_INVALID, "weight size mismatch: " + name);
+        if (bound.count(name)) throw Error(ACT_ERR_INVALID, "weight bound twice: " + name);
+        // host fp32 view (DoRA norms, fp32 destinations, rope factors)
+        const bool dora_proj = proj && ad.type == ACT_ADAPTER_DORA_ROWS;
+        if (dst_kind != DST_BF16 || dora_proj) {
+            f32.resize(n);
+            if (type == ACT_TYPE_F32) std::memcpy(f32.data(), host, n * 4);
+            else if (type == ACT_TYPE_F16) {
+                const uint16_t* h = static_cast<const uint16_t*>(host);
+                for (long i = 0; i < n; ++i) f32[i] = half_to_float(h[i]);
+            } else {
+                const uint8_t* blk = static_cast<const uint8_t*>(host);
+                for (long bidx = 0; bidx < n / 32; ++bidx) {
+                    const float d = half_to_float((uint16_t)(blk[bidx * 34] | blk[bidx * 34 + 1] << 8));
+                    for (int i = 0; i < 32; ++i) f32[bidx * 32 + i] = d * (float)(int8_t)blk[bidx * 34 + 2 + i];
+                }
+            }
+        }
+        if (dst_kind == DST_HOST) {
+            rope_ff = f32;
+        } else if (dst_kind == DST_F32) {
+            float* d = dalloc<float>(n);
+            CK(cudaMemcpyAsync(d, f32.data(), n * 4, cudaMemcpyHostToDevice, stream));
+            CK(cudaStreamSynchronize(stream));
+            *dst = d;
+        } else {
+            bf16* d = dalloc<bf16>(n);
+            void* tmp = nullptr;
+            CK(cudaMalloc(&tmp, need));
+            CK(cudaMemcpyAsync(tmp, host, need, cudaMemcpyHostToDevice, stream));
+            if (type == ACT_TYPE_F32) f32_to_bf16(static_cast<float*>(tmp), d, n, stream);
+            else if (type == ACT_TYPE_F16) f16_to_bf16(static_cast<uint16_t*>(tmp), n, d, stream);
+            else q8_0_to_bf16(static_cast<uint8_t*>(tmp), n / 32, d, stream);
+            CK(cudaStreamSynchronize(stream));
+            CK(cudaFree(tmp));
+            *dst = d;
+        }
+        if (proj) {
+            proj->bound = true;
+            if (dora_proj) {  // lora_row_norm_sq, src/ac/lora.h:11-32
+                proj->base = dalloc<float>(rows);
+                std::vector<float> nsq(rows);
+                for (long o = 0; o < rows; ++o) {
+                    double s = (double)cols * 1e-12;
+                    for (long i = 0; i < cols; ++i) {
+                        const float v = f32[o * cols + i];
+                        if (!std::isfinite(v)) throw Error(ACT_ERR_INVALID, "nonfinite DoRA base weight");
+                        s += (double)v * v;
+                    }
+                    nsq[o] = (float)s;
+                }
+                CK(cudaMemcpyAsync(proj->base, nsq.data(), rows * 4, cudaMemcpyHostToDevice, stream));
+                CK(cudaStreamSynchronize(stream));
+                host_nsq[proj] = std::move(nsq);
+            }
+        }
+        bound[name] = true;
+    }
+
+    std::map<Proj*, std::vector<float>> host_nsq;
+
+    static float half_to_float(uint16_t h) {
+        const uint32_t sign = (uint32_t)(h >> 15) << 31;
+        uint32_t e = (h >> 10) & 0x1f, man = h & 0x3ff, bits;
+        if (e == 0) {
+            if (man == 0) bits = sign;
+            else {
+                int k = -1;
+                do { ++k; man <<= 1; } while (!(man & 0x400));
+                man &= 0x3ff;
+                bits = sign | (uint32_t)(127 - 15 - k) << 23 | man << 13;
+            }
+        } else if (e == 31) bits = sign | 0x7f800000u | man << 13;
+        else bits = sign | (e + 112) << 23 | man << 13;
+        float f;
+        std::memcpy(&f, &bits, 4);
+        return f;
+    }
+
+    void finalize() {
+        if (finalized) throw Error(ACT_ERR_STATE, "already finalized");
+        // completeness
+        std::vector<std::string> missing;
+        auto need = [&](const std::string& n) { if (!bound.count(n)) missing.push_back(n); };
+        const std::string pre = mf ? "dit." : "lm.";
+        for (int l = 0; l < L; ++l) {
+            for (const char* nn : {"norm1", "norm_cross", "norm2"}) {
+                need(pre + std::to_string(l) + "." + nn + ".weight");
+                need(pre + std::to_string(l) + "." + nn + ".bias");
+            }
+            for (int t = 0; t < 7; ++t) need(pre + std::to_string(l) + "." + kTargets[t] + ".weight");
+        }
+        need(pre + "out_norm.weight");
+        need(pre + "out_norm.bias");
+        if (mf) {
+            for (const char* nn : {"in_proj.weight", "out_proj.weight", "time_embed.0.weight", "time_embed.2.weight",
+                                   "cond_proj.weight", "cond_proj.bias", "rope_freq_factors"})
+                need(pre + nn);
+            for (int i = 0; i < md.n_skip; ++i) need(pre + "skip." + std::to_string(i) + ".weight");
+        } else {
+            for (int q = 0; q < md.n_q; ++q) {
+                need(pre + "emb." + std::to_string(q) + ".weight");
+                need(pre + "head." + std::to_string(q) + ".weight");
+            }
+        }
+        if (!missing.empty()) {
+            std::string m = "missing tensors:";
+            for (size_t i = 0; i < missing.size() && i < 8; ++i) m += " " + missing[i];
+            throw Error(ACT_ERR_INVALID, m);
+        }
+        // parameters, reference order (src/mf/train.h:68-104)
+        const float s = ad.alpha / (float)ad.rank;
+        const bool dora = ad.type == ACT_ADAPTER_DORA_ROWS;
+        int64_t off = 0;
+        std::vector<CopyJob> jobs;
+        for (int l = ad.first_layer; l < L; ++l)
+            for (int t = 0; t < 7; ++t) {
+                if (!(ad.targets >> t & 1)) continue;
+                Proj& p = layers[l].p[t];
+                p.adapted = true;
+                p.dora = dora;
+                p.r = ad.rank;
+                p.RP = RP;
+                p.s = s;
+                const std::string stem = pre + std::to_string(l) + "." + kTargets[t] + ".weight";
+                p.offA = off;
+                ptable.push_back({stem + ".lora_A", off, p.r, p.in});
+                off += (int64_t)p.r * p.in;
+                p.offB = off;
+                ptable.push_back({stem + ".lora_B", off, p.out, p.r});
+                off += (int64_t)p.out * p.r;
+                if (dora) {
+                    p.offM = off;
+                    ptable.push_back({stem + ".magnitude", off, 1, p.out});
+                    off += p.out;
+                }
+            }
+        nparam = off;
+        value = dalloc<float>(nparam);
+        mom1 = dalloc<float>(nparam);
+        mom2 = dalloc<float>(nparam);
+        grad = dalloc<float>(nparam);
+        decay = dalloc<uint8_t>(nparam);
+        partials = dalloc<double>(1024);
+        nonfinite_dev = dalloc<int>(1);
+        {
+            std::vector<uint8_t> dm(nparam, 0);
+            std::vector<float> init(nparam, 0.f);
+            std::mt19937 rng(ad.seed);
+            std::normal_distribution<float> normal(0, 0.02f);
+            for (auto& pi : ptable) {
+                const bool isA = pi.name.size() > 7 && pi.name.compare(pi.name.size() - 7, 7, ".lora_A") == 0;
+                const bool isB = pi.name.size() > 7 && pi.name.compare(pi.name.size() - 7, 7, ".lora_B") == 0;
+                if (isA || isB) std::fill(dm.begin() + pi.off, dm.begin() + pi.off + pi.rows * pi.cols, 1);
+                if (isA)
+                    for (int64_t i = 0; i < pi.rows * pi.cols; ++i) init[pi.off + i] = normal(rng);
+            }
+            for (auto& lay : layers)
+                for (auto& p : lay.p)
+                    if (p.dora) {
+                        const auto& nsq = host_nsq.at(&p);
+                        for (int o = 0; o < p.out; ++o) init[p.offM + o] = std::sqrt(nsq[o]);
+                    }
+            CK(cudaMemcpyAsync(decay, dm.data(), nparam, cudaMemcpyHostToDevice, stream));
+            CK(cudaMemcpyAsync(value, init.data(), nparam * 4, cudaMemcpyHostToDevice, stream));
+            CK(cudaStreamSynchronize(stream));
+        }
+        // adapter working copies and DoRA scratch
+        for (auto& lay : layers)
+            for (auto& p : lay.p) {
+                if (!p.adapted) continue;
+                p.A_bf = dalloc<bf16>((size_t)RP * p.in);
+                p.B_bf = dalloc<bf16>((size_t)p.out * RP);
+                jobs.push_back({value + p.offA, p.A_bf, p.r, p.in, p.in});
+                jobs.push_back({value + p.offB, p.B_bf, p.out, p.r, RP});
+                max_job = std::max(max_job, std::max(p.r * p.in, p.out * p.r));
+                if (p.dora) {
+                    p.P = dalloc<float>((size_t)p.out * RP);
+                    p.G = dalloc<float>((size_t)p.r * p.r);
+                    p.Q = dalloc<float>((size_t)p.out * p.r);
+                    p.nsq = dalloc<float>(p.out);
+                    p.g = dalloc<float>(p.out);
+                    p.dg = dalloc<float>(p.out);
+                    p.scr = dalloc<float>((size_t)p.out + p.r * p.r);
+                    p.BD = dalloc<bf16>((size_t)p.out * RP);
+                }
+            }
+        njobs = (int)jobs.size();
+        jobs_dev = dalloc<CopyJob>(std::max(njobs, 1));
+        if (njobs) CK(cudaMemcpyAsync(jobs_dev, jobs.data(), sizeof(CopyJob) * njobs, cudaMemcpyHostToDevice, stream));
+        // rope table (src/ac/transformer.h:55-61 with freq_base 1): theta = pos / ff[i]
+        if (mf) {
+            if ((int)rope_ff.size() != md.head_dim / 2) throw Error(ACT_ERR_INVALID, "rope_freq_factors size mismatch");
+            std::vector<float> tab((size_t)T * 64);
+            for (int p = 0; p < T; ++p)
+                for (int i = 0; i < 32; ++i) {
+                    const float theta = (float)p / rope_ff[i];
+                    tab[((size_t)p * 32 + i) * 2] = std::cos(theta);
+                    tab[((size_t)p * 32 + i) * 2 + 1] = std::sin(theta);
+                }
+            rope = dalloc<float>(tab.size());
+            CK(cudaMemcpyAsync(rope, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice, stream));
+            CK(cudaStreamSynchronize(stream));
+        } else {
+            // sin_positions (src/mg/lm.h:102-116), double phase
+            std::vector<float> tab((size_t)T * D);
+            const int half = D / 2;
+            for (int t = 0; t < T; ++t)
+                for (int i = 0; i < half; ++i) {
+                    const double ph = (double)t / std::pow((double)md.max_period, (double)i / (double)md.pos_denominator);
+                    tab[(size_t)t * D + i] = (float)std::cos(ph);
+                    tab[(size_t)t * D + half + i] = (float)std::sin(ph);
+                }
+            pos = dalloc<float>(tab.size());
+            CK(cudaMemcpyAsync(pos, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice, stream));
+            emb_dev = dalloc<float*>(md.n_q);
+            CK(cudaMemcpyAsync(emb_dev, emb.data(), sizeof(float*) * md.n_q, cudaMemcpyHostToDevice, stream));
+            CK(cudaStreamSynchronize(stream));
+        }
+        allocate_activations();
+        finalized = true;
+    }
+
+    void allocate_activations() {
+        const long Mr = M, Cr = MC;
+        for (int l = 0; l < L; ++l) {
+            Layer& y = layers[l];
+            if (l == 0) y.xin = x0f = dalloc<float>(Mr * D);
+            else if (y.consumes) y.xin = dalloc<float>(Mr * D);
+            else y.xin = layers[l - 1].xout;
+            y.xmid = dalloc<float>(Mr * D);
+            y.xmid2 = dalloc<float>(Mr * D);
+            y.xout = dalloc<float>(Mr * D);
+            for (int i = 0; i < 3; ++i) {
+                y.mu[i] = dalloc<float>(Mr);
+                y.rs[i] = dalloc<float>(Mr);
+            }
+            y.h1 = dalloc<bf16>(Mr * D);
+            y.hc = dalloc<bf16>(Mr * D);
+            y.f = dalloc<bf16>(Mr * D);
+            y.qkv = dalloc<bf16>(Mr * 3 * D);
+            y.o1 = dalloc<bf16>(Mr * D);
+            y.cq = dalloc<bf16>(Mr * D);
+            y.ckv = dalloc<bf16>(Cr * 2 * D);
+            y.o2 = dalloc<bf16>(Mr * D);
+            y.z = dalloc<bf16>(Mr * F);
+            y.gact = dalloc<bf16>(Mr * F);
+            y.lse1 = dalloc<float>((long)B * H * T);
+            y.lse2 = dalloc<float>((long)B * H * T);
+            for (int t = 0; t < 7; ++t) {
+                if (!y.p[t].adapted) continue;
+                y.U[t] = dalloc<bf16>((t == 3 ? Cr : Mr) * RP);
+                if (y.p[t].dora && (t == 1 || t == 4 || t == 6)) y.Yaux[t] = dalloc<bf16>(Mr * y.p[t].out);
+            }
+            if (y.produces) {
+                y.xsave_bf = dalloc<bf16>(Mr * D);
+                y.dsaved = dalloc<float>(Mr * D);
+            }
+        }
+        if (!x0f) x0f = layers[0].xin;
+        const int lat = mf ? md.latent_dim : 8;
+        x0 = dalloc<bf16>(Mr * lat);
+        vstar = dalloc<float>(Mr * lat);
+        te1 = dalloc<float>((long)B * D);
+        te = dalloc<float>((long)B * D);
+        if (mf) hidden_bf = dalloc<bf16>(Cr * md.cond_dim);
+        ctx_bf = dalloc<bf16>(Cr * D);
+        xo = dalloc<bf16>(Mr * D);
+        muo = dalloc<float>(Mr);
+        rso = dalloc<float>(Mr);
+        outp = dalloc<float>(Mr * lat);
+        dout = dalloc<bf16>(Mr * lat);
+        xprev_bf = dalloc<bf16>(Mr * D);
+        dx = dalloc<float>(Mr * D);
+        dtmp = dalloc<float>(Mr * D);
+        dq_acc = dalloc<float>(Mr * D);
+        dvec = dalloc<float>((long)B * H * T);
+        dxbf = dalloc<bf16>(Mr * D);
+        dz = dalloc<bf16>(Mr * F);
+        dU = dalloc<bf16>(std::max(Mr, Cr) * RP);
+        dob = dalloc<bf16>(Mr * D);
+        dqkv = dalloc<bf16>(Mr * 3 * D);
+        dcq = dalloc<bf16>(Mr * D);
+        dckv = dalloc<bf16>(Cr * 2 * D);
+        d_loss = dalloc<float>(B);
+        h_loss = halloc<float>(B);
+        if (mf) {
+            const size_t nx = (size_t)B * md.latent_dim * T;
+            h_clean = halloc<float>(nx); h_noise = halloc<float>(nx);
+            h_hidden = halloc<float>((size_t)Cr * md.cond_dim);
+            h_t = halloc<float>(B); h_tfeat = halloc<float>((size_t)B * md.time_dim); h_nvalid = halloc<int32_t>(B);
+            d_clean = dalloc<float>(nx); d_noise = dalloc<float>(nx);
+            d_hidden = dalloc<float>((size_t)Cr * md.cond_dim);
+            d_t = dalloc<float>(B); d_tfeat = dalloc<float>((size_t)B * md.time_dim); d_nvalid = dalloc<int32_t>(B);
+        } else {
+            const int sel = ad.frames - ad.prefix_frames;
+            h_ids = halloc<int32_t>((size_t)B * md.n_q * T);
+            h_tgt = halloc<int32_t>((size_t)B * md.n_q * sel);
+            h_ctx = halloc<float>((size_t)Cr * D);
+            d_ids = dalloc<int32_t>((size_t)B * md.n_q * T);
+            d_tgt = dalloc<int32_t>((size_t)B * md.n_q * sel);
+            d_ctx = dalloc<float>((size_t)Cr * D);
+            logits = dalloc<float>((size_t)B * md.n_q * sel * md.card);
+            dlogits = dalloc<bf16>((size_t)B * md.n_q * sel * md.card);
+        }
+        CK(cudaStreamSynchronize(stream));
+    }
+
+    void optimizer(const act_opt* o, int* nonfinite) {
+        if (!finalized) throw Error(ACT_ERR_STATE, "act_finalize has not been called");
+        if (!o || o->step <= 0 || !std::isfinite(o->lr) || o->lr <= 0 || !std::isfinite(o->clip) || o->clip <= 0 ||
+            !(o->beta1 >= 0 && o->beta1 < 1) || !(o->beta2 >= 0 && o->beta2 < 1) || !(o->eps > 0) ||
+            !(o->weight_decay >= 0))
+            throw Error(ACT_ERR_INVALID, "invalid optimizer settings");
+        const int count = o->count > 0 ? o->count : (count_override > 0 ? count_override : accumulated);
+        if (count <= 0) throw Error(ACT_ERR_STATE, "empty gradient accumulation");
+        const float bc1 = 1 - std::pow(o->beta1, (float)o->step), bc2 = 1 - std::pow(o->beta2, (float)o->step);
+        CK(cudaMemsetAsync(nonfinite_dev, 0, sizeof(int), stream));
+        timed(2, 0, 28.0 * nparam, [&] {
+            adamw(value, mom1, mom2, grad, decay, nparam, (float)count, o->clip, o->lr, o->beta1, o->beta2, o->eps,
+                  o->weight_decay, bc1, bc2, partials, nonfinite_dev, stream);
+        });
+        int bad = 0;
+        CK(cudaMemcpyAsync(&bad, nonfinite_dev, sizeof(int), cudaMemcpyDeviceToHost, stream));
+        CK(cudaStreamSynchronize(stream));
+        collect_stats();
+        accumulated = 0;
+        count_override = 0;
+        if (nonfinite) *nonfinite = bad;
+        if (bad) throw Error(ACT_ERR_NONFINITE, "nonfinite optimizer update");
+    }
+
+    double step_flops(int n) const {
+        // algorithmic FLOPs: 2 per multiply-add, no recompute, no padding.
+        const double Td = T, Cd = C;
+        double fwd = 0, bwd = 0;
+        const double proj_tok = 2.0 * (3.0 * D * D + D * (double)D + D * (double)D + D * (double)D + 2.0 * D * F);
+        for (int l = 0; l < L; ++l) {
+            const bool grad_layer = l >= ad.first_layer;
+            fwd += Td * proj_tok + 2.0 * Cd * D * 2.0 * D;
+            fwd += attn_flops(1, T, true) + attn_flops(1, C, false);
+            if (layers[l].consumes) fwd += 2.0 * Td * 2.0 * D * D;
+            if (grad_layer) {
+                bwd += Td * proj_tok;  // dX of every token projection
+                if (l == ad.first_layer) bwd -= Td * 2.0 * 3.0 * D * D;  // no dX below the first adapted layer
+                bwd += 2.0 * (attn_flops(1, T, true) + attn_flops(1, C, false));
+                if (layers[l].consumes && l > ad.first_layer) bwd += 2.0 * Td * 2.0 * D * D;
+                for (int t = 0; t < 7; ++t) {
+                    const Proj& p = layers[l].p[t];
+                    if (!p.adapted) continue;
+                    const double rows = t == 3 ? Cd : Td;
+                    fwd += rows * 2.0 * p.r * (p.in + p.out);
+                    bwd += rows * 4.0 * p.r * (p.in + p.out);
+                }
+            }
+        }
+        if (mf) {
+            fwd += 2.0 * Td * md.latent_dim * D * 2.0 + 2.0 * Cd * md.cond_dim * D;
+            bwd += 2.0 * Td * md.latent_dim * D;
+        } else {
+            const double sel = (double)md.n_q * (ad.frames - ad.prefix_frames);
+            fwd += 2.0 * sel * D * md.card;
+            bwd += 2.0 * sel * D * md.card;
+        }
+        return n * (fwd + bwd);
+    }
+
+    void destroy() {
+        if (stream) cudaStreamSynchronize(stream);
+        for (auto& g : graphs) cudaGraphExecDestroy(g.second);
+        graphs.clear();
+        for (auto e : evpool) cudaEventDestroy(e);
+        if (comm) ncclCommDestroy(comm);
+        for (void* p : dallocs) cudaFree(p);
+        for (void* p : hallocs) cudaFreeHost(p);
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+// ------------------------------------------------------------------------------------------
+// C ABI
+
+namespace {
+
+template <class Fn>
+int guarded(act_ctx* ctx, Fn&& fn) {
+    try {
+        if (ctx) CK(cudaSetDevice(ctx->device));
+        fn();
+        return ACT_OK;
+    } catch (const Error& e) {
+        (ctx ? ctx->err : g_error) = e.what();
+        return e.code;
+    } catch (const std::exception& e) {
+        (ctx ? ctx->err : g_error) = e.what();
+        return ACT_ERR_INVALID;
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int act_create(act_ctx** out, int device, const act_model_desc* model, const act_adapter_desc* adapter) {
+    if (!out || !model || !adapter) {
+        g_error = "null argument";
+        return ACT_ERR_INVALID;
+    }
+    *out = nullptr;
+    auto* ctx = new act_ctx();
+    try {
+        ctx->setup(device, model, adapter);
+        if (ctx->mf) ctx->skip.assign(model->n_skip, nullptr);
+        else {
+            ctx->emb.assign(model->n_q, nullptr);
+            ctx->head.assign(model->n_q, nullptr);
+        }
+    } catch (const Error& e) {
+        g_error = e.what();
+        ctx->destroy();
+        delete ctx;
+        return e.code;
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        ctx->destroy();
+        delete ctx;
+        return ACT_ERR_INVALID;
+    }
+    *out = ctx;
+    return ACT_OK;
+}
+
+int act_bind_weight(act_ctx* ctx, const char* name, int ggml_type, const void* host, size_t bytes) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] { ctx->bind(name, ggml_type, host, bytes); });
+}
+
+int act_finalize(act_ctx* ctx) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] { ctx->finalize(); });
+}
+
+int64_t act_param_count(act_ctx* ctx) { return ctx && ctx->finalized ? ctx->nparam : -1; }
+
+int act_param_tensor_count(act_ctx* ctx) { return ctx && ctx->finalized ? (int)ctx->ptable.size() : -1; }
+
+int act_param_tensor(act_ctx* ctx, int index, char* name, size_t cap, int64_t* offset, int64_t* rows, int64_t* cols) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] {
+        if (!ctx->finalized) throw Error(ACT_ERR_STATE, "act_finalize has not been called");
+        if (index < 0 || index >= (int)ctx->ptable.size()) throw Error(ACT_ERR_INVALID, "parameter index out of range");
+        const auto& p = ctx->ptable[index];
+        if (name && cap) {
+            std::strncpy(name, p.name.c_str(), cap - 1);
+            name[cap - 1] = 0;
+        }
+        if (offset) *offset = p.off;
+        if (rows) *rows = p.rows;
+        if (cols) *cols = p.cols;
+    });
+}
+
+int act_set_params(act_ctx* ctx, const float* v, size_t n) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] {
+        if (!ctx->finalized) throw Error(ACT_ERR_STATE, "act_finalize has not been called");
+        if (!v || (int64_t)n != ctx->nparam) throw Error(ACT_ERR_INVALID, "parameter count mismatch");
+        for (size_t i = 0; i < n; ++i)
+            if (!std::isfinite(v[i])) throw Error(ACT_ERR_INVALID, "nonfinite adapter tensor");
+        CK(cudaMemcpyAsync(ctx->value, v, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+        CK(cudaStreamSynchronize(ctx->stream));
+    });
+}
+
+int act_get_params(act_ctx* ctx, float* v, float* m, float* vv, size_t n) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] {
+        if (!ctx->finalized) throw Error(ACT_ERR_STATE, "act_finalize has not been called");
+        if ((int64_t)n != ctx->nparam) throw Error(ACT_ERR_INVALID, "parameter count mismatch");
+        if (v) CK(cudaMemcpyAsync(v, ctx->value, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        if (m) CK(cudaMemcpyAsync(m, ctx->mom1, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        if (vv) CK(cudaMemcpyAsync(vv, ctx->mom2, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        CK(cudaStreamSynchronize(ctx->stream));
+    });
+}
+
+int act_set_moments(act_ctx* ctx, const float* m, const float* v, size_t n) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] {
+        if (!ctx->finalized) throw Error(ACT_ERR_STATE, "act_finalize has not been called");
+        if ((int64_t)n != ctx->nparam || !m || !v) throw Error(ACT_ERR_INVALID, "parameter count mismatch");
+        CK(cudaMemcpyAsync(ctx->mom1, m, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+        CK(cudaMemcpyAsync(ctx->mom2, v, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+        CK(cudaStreamSynchronize(ctx->stream));
+    });
+}
+
+int act_get_grads(act_ctx* ctx, float* g, size_t n) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] {
+        if (!ctx->finalized) throw Error(ACT_ERR_STATE, "act_finalize has not been called");
+        if (!g || (int64_t)n != ctx->nparam) throw Error(ACT_ERR_INVALID, "parameter count mismatch");
+        CK(cudaMemcpyAsync(g, ctx->grad, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        CK(cudaStreamSynchronize(ctx->stream));
+    });
+}
+
+int act_zero_grads(act_ctx* ctx) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] {
+        if (!ctx->finalized) throw Error(ACT_ERR_STATE, "act_finalize has not been called");
+        CK(cudaMemsetAsync(ctx->grad, 0, ctx->nparam * 4, ctx->stream));
+        CK(cudaStreamSynchronize(ctx->stream));
+        ctx->accumulated = 0;
+        ctx->count_override = 0;
+    });
+}
+
+int act_mf_stage(act_ctx* ctx, const act_mf_batch* b) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] {
+        if (!ctx->finalized) throw Error(ACT_ERR_STATE, "act_finalize has not been called");
+        ctx->stage_mf(b);
+    });
+}
+
+int act_mg_stage(act_ctx* ctx, const act_mg_batch* b) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] {
+        if (!ctx->finalized) throw Error(ACT_ERR_STATE, "act_finalize has not been called");
+        ctx->stage_mg(b);
+    });
+}
+
+int act_run_staged(act_ctx* ctx, float* loss) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] { ctx->run_staged(loss); });
+}
+
+int act_mf_step(act_ctx* ctx, const act_mf_batch* b, float* loss) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] {
+        if (!ctx->finalized) throw Error(ACT_ERR_STATE, "act_finalize has not been called");
+        ctx->stage_mf(b);
+        ctx->run_staged(loss);
+    });
+}
+
+int act_mg_step(act_ctx* ctx, const act_mg_batch* b, float* loss) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] {
+        if (!ctx->finalized) throw Error(ACT_ERR_STATE, "act_finalize has not been called");
+        ctx->stage_mg(b);
+        ctx->run_staged(loss);
+    });
+}
+
+int act_nccl_get_unique_id(void* id) {
+    if (!id) return ACT_ERR_INVALID;
+    try {
+        ncclUniqueId u;
+        NK(ncclGetUniqueId(&u));
+        std::memcpy(id, &u, sizeof(u));
+        return ACT_OK;
+    } catch (const Error& e) {
+        g_error = e.what();
+        return e.code;
+    }
+}
+
+int act_nccl_init(act_ctx* ctx, const void* id, int nranks, int rank) {
+    if (!ctx || !id) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] {
+        if (ctx->comm) throw Error(ACT_ERR_STATE, "communicator already initialised");
+        ncclUniqueId u;
+        std::memcpy(&u, id, sizeof(u));
+        NK(ncclCommInitRank(&ctx->comm, nranks, u, rank));
+    });
+}
+
+int act_allreduce_grads(act_ctx* ctx, void* comm, int global_count) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] {
+        if (!ctx->finalized) throw Error(ACT_ERR_STATE, "act_finalize has not been called");
+        ncclComm_t c = comm ? static_cast<ncclComm_t>(comm) : ctx->comm;
+        if (!c) throw Error(ACT_ERR_STATE, "no NCCL communicator");
+        if (global_count <= 0) throw Error(ACT_ERR_INVALID, "invalid global sample count");
+        ctx->timed(2, 0, 8.0 * ctx->nparam, [&] {
+            NK(ncclAllReduce(ctx->grad, ctx->grad, ctx->nparam, ncclFloat, ncclSum, c, ctx->stream));
+        });
+        ctx->count_override = global_count;
+    });
+}
+
+int act_optimizer(act_ctx* ctx, const act_opt* o, int* nonfinite) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] { ctx->optimizer(o, nonfinite); });
+}
+
+const char* act_last_error(act_ctx* ctx) { return ctx ? ctx->err.c_str() : g_error.c_str(); }
+
+void act_destroy(act_ctx* ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    ctx->destroy();
+    delete ctx;
+}
+
+void* act_stream(act_ctx* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+
+int act_set_profiling(act_ctx* ctx, int enable) {
+    if (!ctx) return ACT_ERR_INVALID;
+    ctx->profiling = enable != 0;
+    return ACT_OK;
+}
+
+int act_kernel_stats(act_ctx* ctx, int cls, double* ms, double* flops, double* bytes, int64_t* launches) {
+    if (!ctx || cls < 0 || cls > 2) return ACT_ERR_INVALID;
+    if (ms) *ms = ctx->stats[cls].ms;
+    if (flops) *flops = ctx->stats[cls].flops;
+    if (bytes) *bytes = ctx->stats[cls].bytes;
+    if (launches) *launches = ctx->stats[cls].launches;
+    return ACT_OK;
+}
+
+int act_reset_kernel_stats(act_ctx* ctx) {
+    if (!ctx) return ACT_ERR_INVALID;
+    for (auto& s : ctx->stats) s = KStat();
+    return ACT_OK;
+}
+
+double act_step_flops(act_ctx* ctx, int n) { return ctx && ctx->finalized ? ctx->step_flops(n) : -1.0; }
+
+int64_t act_graph_kernel_nodes(act_ctx* ctx, int n) {
+    if (!ctx) return -1;
+    auto it = ctx->kernel_nodes.find(n);
+    return it == ctx->kernel_nodes.end() ? -1 : it->second;
+}
+
+}  // extern "C"

@@ -1,0 +1,159 @@
+// kernels.h -- launch interface between the host engine (engine.cpp) and the sm_100a kernels.
+// Every matrix is row-major; activations are token-major [rows][features].
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+typedef __nv_bfloat16 bf16;
+
+namespace act {
+
+// ---------------------------------------------------------------------------------------
+// GEMM:  C[m][n] = epilogue( sum_k A(m,k) B(n,k) ),  K = K1 (+ K2 second segment).
+//   A(m,k): a_kmajor ? A[m*lda + k] : A[k*lda + m]
+//   B(n,k): b_kmajor ? B[n*ldb + k] : B[k*ldb + n]
+// The second segment appends K2 reduction columns from (A2, B2) with the same majors; it
+// carries the LoRA rank block so the adapter path rides in the same tile loop.
+enum EpiMode : int {
+    EPI_STORE_F32 = 0,   // out_f32 = alpha*acc
+    EPI_ACCUM_F32 = 1,   // out_f32 += alpha*acc
+    EPI_ATOMIC_F32 = 2,  // atomicAdd(out_f32, alpha*acc)        (split-K reductions)
+    EPI_RESID_F32 = 3,   // out_f32 = resid + alpha*acc
+    EPI_STORE_BF16 = 4,  // out_bf16 = alpha*acc
+    EPI_GELU = 5,        // aux_bf16 = acc ; out_bf16 = gelu(acc)
+    EPI_GELU_BWD = 6,    // out_bf16 = acc * gelu'(auxin) * colscale2[n]
+    EPI_BIAS_BF16 = 7,   // out_bf16 = acc + bias[n]
+};
+
+struct GemmArgs {
+    int M = 0, N = 0, K1 = 0, K2 = 0;
+    const bf16* A1 = nullptr;
+    const bf16* A2 = nullptr;
+    long lda1 = 0, lda2 = 0;
+    const bf16* B1 = nullptr;
+    const bf16* B2 = nullptr;
+    long ldb1 = 0, ldb2 = 0;
+    bool a_kmajor = true, b_kmajor = true;
+    int splitk = 1;
+    // epilogue
+    int mode = EPI_STORE_F32;
+    float alpha = 1.0f;
+    const float* colscale = nullptr;   // acc *= colscale[n] (DoRA row factor of the output)
+    void* out = nullptr;
+    long ldo = 0;
+    const float* resid = nullptr;      // EPI_RESID_F32
+    long ldr = 0;
+    bf16* aux = nullptr;               // additionally store acc (after colscale) as bf16
+    long ldaux = 0;
+    const bf16* auxin = nullptr;       // EPI_GELU_BWD: pre-activation
+    long ldauxin = 0;
+    const float* colscale2 = nullptr;  // EPI_GELU_BWD: DoRA factor of the producing projection
+    const float* bias = nullptr;       // EPI_BIAS_BF16
+    int nvalid = 1 << 30;              // columns >= nvalid are not written
+    int mvalid = 1 << 30;              // rows >= mvalid are not written
+};
+
+void gemm(const GemmArgs& a, cudaStream_t s);
+
+// ---------------------------------------------------------------------------------------
+// attention over token-major q/k/v (head h at columns h*64 .. h*64+63), head_dim 64.
+struct AttnArgs {
+    const bf16* q = nullptr;
+    const bf16* k = nullptr;
+    const bf16* v = nullptr;
+    long ldq = 0, ldk = 0, ldv = 0;
+    int T = 0;           // queries per clip
+    int Tk = 0;          // stored keys per clip
+    int H = 0;
+    int clips = 0;
+    const int* nvalid = nullptr;  // per clip: keys >= nvalid masked (nullptr: none)
+    int causal = 0;
+    int zero_key = 0;             // add_zero_attn: implicit key with score 0 and value 0
+    const float* rope = nullptr;  // [T][32] (cos, sin) pairs: rotate q and k (self-attention)
+    float scale = 0.125f;
+    bf16* o = nullptr;
+    long ldo = 0;
+    float* lse = nullptr;         // [clips][H][T], log2 units
+    // backward
+    const bf16* dout = nullptr;
+    long lddo = 0;
+    float* dvec = nullptr;        // [clips][H][T]  rowsum(dO * O)
+    float* dq_acc = nullptr;      // [clips*T][ldq_acc] fp32, rotated frame, zeroed by caller
+    long ldq_acc = 0;
+    bf16* dk = nullptr;
+    bf16* dv = nullptr;
+    long lddk = 0, lddv = 0;
+    const float* kscale = nullptr;  // DoRA factor applied to dk columns (nullable)
+    const float* vscale = nullptr;  // DoRA factor applied to dv columns (nullable)
+};
+
+void attn_fwd(const AttnArgs& a, cudaStream_t s);
+void attn_bwd(const AttnArgs& a, cudaStream_t s);  // computes dvec itself
+// dq (bf16) = unrotate(dq_acc) * qscale[col]
+void attn_dq_finish(const AttnArgs& a, bf16* dq, long lddq, const float* qscale, cudaStream_t s);
+
+// ---------------------------------------------------------------------------------------
+// element-wise / row kernels
+// LayerNorm over rows of D (fp32 in), y = xhat*w + b (+ add[row / rows_per_clip]) -> bf16.
+void layernorm_fwd(const float* x, const float* w, const float* b, const float* add, int rows_per_clip,
+                   bf16* y, float* mean, float* rstd, int rows, int D, float eps, cudaStream_t s);
+// dx (=|+=) LN'(dy) (+ extra); also dx_bf = bf16(dx * colscale).  dy fp32.
+void layernorm_bwd(const float* dy, const float* x, const float* w, const float* mean,
+                   const float* rstd, float* dx, int accumulate, const float* extra, bf16* dx_bf,
+                   const float* colscale, int rows, int D, cudaStream_t s);
+// dst_bf = bf16((x (+ extra)) * colscale); x updated with extra when given.
+void residual_to_bf16(float* x, const float* extra, bf16* dst, const float* colscale, int rows, int D,
+                      cudaStream_t s);
+void f32_to_bf16(const float* x, bf16* y, long n, cudaStream_t s);
+
+// MelodyFlow inputs: x0[m][c] = ((1-t)noise + t clean) * rescale(t), vstar = clean - noise.
+void mf_inputs(const float* clean, const float* noise, const float* t, int clips, int T, int lat,
+               bf16* x0, float* vstar, cudaStream_t s);
+// loss[b] = mean((sqrt2*out - vstar)^2) ; dout = d loss / d out (bf16, token-major)
+void mf_loss(const float* out, const float* vstar, int clips, int T, int lat, float* loss, bf16* dout,
+             cudaStream_t s);
+// small fp32 linear for the timestep MLP: y[b][n] = act(sum_k x[b][k] W[n][k]); act 1 = SiLU
+void linear_f32(const float* x, const float* W, float* y, int rows, int N, int K, int act,
+                cudaStream_t s);
+// DoRA: dg[n] += sum_m a[m][n] * b[m][n] / colscale[n]^2  (a already includes colscale)
+void dora_colsum(const bf16* a, long lda, const bf16* b, long ldb, int rows, int N, const float* colscale,
+                 float* dg, cudaStream_t s);
+// DoRA per-step factors: G = A A^T, Q = B G, nsq = base + 2s<P,B> + s^2<B,Q>, g = m / sqrt(nsq)
+void dora_prepare(const float* A, const float* B, const float* m, const float* P, const float* base,
+                  int r, int in, int out, float s, float* G, float* Q, float* nsq, float* g,
+                  cudaStream_t st);
+// DoRA backward tail: gm += dg/sqrt(nsq); dt2 = 2s dnsq, dt3 = s^2 dnsq;
+// gB += dt2 P + 2 dt3 Q; BD = bf16(dt2 * B) [out][RP]; dG = B^T diag(dt3) B -> gA += 2 dG A
+void dora_finish(const float* dg, const float* nsq, const float* g, const float* m, const float* B,
+                 const float* P, const float* Q, const float* A, int r, int RP, int in, int out, float s,
+                 float* gm, float* gB, float* gA, bf16* BD, float* scratch, cudaStream_t st);
+
+// refresh bf16 working copies: dst[row*ldd + col] = src[row*cols + col] for row<rows, col<cols
+struct CopyJob {
+    const float* src;
+    bf16* dst;
+    int rows, cols, ldd;
+};
+void refresh_bf16(const CopyJob* jobs_dev, int njobs, int max_elems, cudaStream_t s);
+
+// AdamW over the flat parameter buffer (TrainAccumulation::update semantics).
+// norm_partials: >= 1024 doubles of scratch.  nonfinite: int counter (accumulates).
+void adamw(float* value, float* m, float* v, float* grad, const uint8_t* decay_mask, long n,
+           float inv_count, float clip, float lr, float beta1, float beta2, float eps, float decay,
+           float bc1, float bc2, double* norm_partials, int* nonfinite, cudaStream_t s);
+
+// Q8_0 blocks -> bf16 (one-time weight binding) and fp32 (parity checks).
+void q8_0_to_bf16(const uint8_t* blocks, long nblocks, bf16* out, cudaStream_t s);
+void q8_0_to_f32(const uint8_t* blocks, long nblocks, float* out, cudaStream_t s);
+void f16_to_bf16(const uint16_t* in, long n, bf16* out, cudaStream_t s);
+
+// MusicGen: x[s][:] = sum_q emb_q[ids[q][s]] + pos[s]   (fp32 out)
+void mg_embed(const int32_t* ids, int steps, int nq, const float* const* emb_dev, const float* pos,
+              float* x, int D, int seqs, cudaStream_t s);
+// Cross entropy over selected rows: logits fp32 [rows][card]; targets per row (-1: skip);
+// loss_acc[seq] += ce / nsel; dlogits bf16 = (softmax - onehot) / nsel.
+void mg_cross_entropy(const float* logits, int rows, int card, const int32_t* targets, int rows_per_seq,
+                      float inv_nsel, float* loss_acc, bf16* dlogits, cudaStream_t s);
+
+}  // namespace act

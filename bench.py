@@ -1,0 +1,387 @@
+"""Benchmark of the adapter training step (BASELINE.json metric: DiT LoRA train steps/s on
+8 x 30 s clips).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload mf|mg]
+
+N > 1 is launched by torchrun (one process per GPU).  Per-GPU work is fixed (8 clips of 750
+frames per rank, weak scaling) and `value` is the whole-job rate in units of 8-clip steps:
+N * K / (max over ranks of the device time of K steps).  Synthetic inputs and N(0, 0.02)
+weights quantised to Q8_0 stand in for the reference's datasets and checkpoints.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "audiocraft.cpp_b200"))
+
+# BASELINE cfg 2: DiT d1024 x24, 16 heads, FFN 4096, 8 x 750 frames, 32 T5 tokens, rank 16
+# LoRA (alpha 32) on self.qkv, self.out, ff.0, ff.2.
+MF = dict(dim=1024, layers=24, heads=16, ff=4096, lat=128, cond=768, tdim=256, T=750, C=32, batch=8,
+          rank=16, alpha=32.0, targets=0x63)
+# BASELINE cfg 4 (per GPU): MusicGen-medium d1536 x48, 24 heads, FFN 6144, 4 codebooks of 2048,
+# 1500 frames, 32 tokens, DoRA-rows rank 16 on all seven projections, 4 sequences per GPU.
+MG = dict(dim=1536, layers=48, heads=24, ff=6144, n_q=4, card=2048, frames=1500, C=32, batch=4,
+          rank=16, alpha=32.0, targets=0x7F)
+
+
+def q8_0(w: np.ndarray) -> np.ndarray:
+    """ggml quantize_row_q8_0 on rows of 32 (d = amax/127 in fp32, q = round half away)."""
+    x = w.reshape(-1, 32).astype(np.float32)
+    d = np.abs(x).max(axis=1, keepdims=True) / np.float32(127)
+    with np.errstate(divide="ignore"):
+        inv = np.where(d == 0, np.float32(0), np.float32(1) / d).astype(np.float32)
+    a = np.abs(x * inv)
+    fl = np.floor(a)
+    q = (np.sign(x) * (fl + np.floor(2 * (a - fl)))).astype(np.int8)
+    out = np.empty((x.shape[0], 34), np.uint8)
+    out[:, :2] = d.astype(np.float16).view(np.uint8).reshape(-1, 2)
+    out[:, 2:] = q.view(np.uint8)
+    return out.ravel()
+
+
+def dit_tensors(c):
+    D, F = c["dim"], c["ff"]
+    t = [("dit.in_proj.weight", (D, c["lat"])), ("dit.out_proj.weight", (c["lat"], D)),
+         ("dit.time_embed.0.weight", (D, c["tdim"])), ("dit.time_embed.2.weight", (D, D)),
+         ("dit.cond_proj.weight", (D, c["cond"])), ("dit.cond_proj.bias", (D,)),
+         ("dit.rope_freq_factors", (32,)), ("dit.out_norm.weight", (D,)), ("dit.out_norm.bias", (D,))]
+    t += [(f"dit.skip.{i}.weight", (D, 2 * D)) for i in range((c["layers"] - 1) // 2)]
+    for l in range(c["layers"]):
+        for n in ("norm1", "norm_cross", "norm2"):
+            t += [(f"dit.{l}.{n}.weight", (D,)), (f"dit.{l}.{n}.bias", (D,))]
+        t += [(f"dit.{l}.self.qkv.weight", (3 * D, D)), (f"dit.{l}.self.out.weight", (D, D)),
+              (f"dit.{l}.cross.q.weight", (D, D)), (f"dit.{l}.cross.kv.weight", (2 * D, D)),
+              (f"dit.{l}.cross.out.weight", (D, D)), (f"dit.{l}.ff.0.weight", (F, D)),
+              (f"dit.{l}.ff.2.weight", (D, F))]
+    return t
+
+
+def lm_tensors(c):
+    D, F = c["dim"], c["ff"]
+    t = [(f"lm.emb.{q}.weight", (c["card"] + 1, D)) for q in range(c["n_q"])]
+    t += [(f"lm.head.{q}.weight", (c["card"], D)) for q in range(c["n_q"])]
+    t += [("lm.out_norm.weight", (D,)), ("lm.out_norm.bias", (D,))]
+    for l in range(c["layers"]):
+        for n in ("norm1", "norm_cross", "norm2"):
+            t += [(f"lm.{l}.{n}.weight", (D,)), (f"lm.{l}.{n}.bias", (D,))]
+        t += [(f"lm.{l}.self.qkv.weight", (3 * D, D)), (f"lm.{l}.self.out.weight", (D, D)),
+              (f"lm.{l}.cross.q.weight", (D, D)), (f"lm.{l}.cross.kv.weight", (2 * D, D)),
+              (f"lm.{l}.cross.out.weight", (D, D)), (f"lm.{l}.ff.0.weight", (F, D)),
+              (f"lm.{l}.ff.2.weight", (D, F))]
+    return t
+
+
+def synth_weight(rng, name, shape):
+    if name.endswith("rope_freq_factors"):
+        return (10000.0 ** (2 * np.arange(32) / 64.0)).astype(np.float32), "f32"
+    if "norm" in name:
+        return (np.ones(shape) if name.endswith("weight") else np.zeros(shape)).astype(np.float32), "f32"
+    if name.endswith(".bias"):
+        return np.zeros(shape, np.float32), "f32"
+    if ".emb." in name:
+        return rng.standard_normal(shape, dtype=np.float32), "f32"
+    return (0.02 * rng.standard_normal(shape, dtype=np.float32)), "q8_0"
+
+
+# ------------------------------------------------------------------------------------------
+# clocks
+
+class Clocks:
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.idx)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------
+# CPU baseline: the C restatement (oracle/), the reference binary being unbuildable here
+
+def cpu_sample(c, seconds_hint=False):
+    """One bounded sample of the step on the host cores: 1 clip, 2 of the 24 layers at full
+    width and length; returns (seconds, scale to one 8-clip 24-layer step, description)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    L = 2
+    cfg = O.DitCfg(c["dim"], L, c["heads"], 64, c["ff"], c["lat"], c["cond"], c["tdim"], (L - 1) // 2, 1e-5, 1)
+    rng = np.random.default_rng(0)
+    shapes = O.dit_tensor_shapes(cfg)
+    W = (0.02 * rng.standard_normal(sum(r * k for r, k in shapes))).astype(np.float32)
+    ad = O.Adapter(c["rank"], c["alpha"], 0, 0, c["targets"])
+    p = (0.02 * rng.standard_normal(O.lib().ora_adapter_numel(c["dim"], c["ff"], L, ad))).astype(np.float32)
+    T = c["T"]
+    args = (rng.standard_normal((1, c["lat"], T)).astype(np.float32), rng.standard_normal((1, c["lat"], T)).astype(np.float32),
+            rng.standard_normal((1, c["C"], c["cond"])).astype(np.float32), np.array([0.5], np.float32),
+            np.zeros(1, np.int32), np.full(1, -1, np.int32))
+    t0 = time.perf_counter()
+    O.dit_step(cfg, W, ad, p, *args)
+    dt = time.perf_counter() - t0
+    scale = (c["layers"] / L) * c["batch"]
+    return dt, scale, f"oracle C restatement, 1 clip x {L} of {c['layers']} layers at d{c['dim']} T{T}, fwd+bwd, scaled x{scale:g}"
+
+
+def run_reference(args, c):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cores = os.cpu_count()
+    for _ in range(args.warmup):
+        cpu_sample(c)
+    times = []
+    for _ in range(args.steps):
+        dt, scale, desc = cpu_sample(c)
+        times.append(dt * scale)
+    step_s = float(np.mean(times))
+    value = 1.0 / step_s
+    unit = "steps/s (8x30s-clip steps)"
+    line = {"metric": "DiT LoRA train steps/s (8x30s clips)", "value": value, "unit": unit, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "mf-cfg2: DiT d1024 L24 H16 F4096, 8x750 frames, 32 tokens, LoRA r16 on qkv/out/ff.0/ff.2",
+                       "global_batch": 8, "seq_len": c["T"], "parallelism": "cpu"},
+            "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port", "sample": desc},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------
+
+def build_context(A, c, workload, device, seed=0):
+    rng = np.random.default_rng(seed)
+    if workload == "mf":
+        md = A.mf_model(c["dim"], c["layers"], c["heads"], c["ff"], c["lat"], c["cond"], c["tdim"])
+        ad = A.AdapterDesc(A.ADAPTER_LORA, c["rank"], c["alpha"], 0, c["targets"], 1234, c["batch"], c["T"], c["C"], 0)
+        tensors = dit_tensors(c)
+    else:
+        md = A.mg_model(c["dim"], c["layers"], c["heads"], c["ff"], c["n_q"], c["card"])
+        ad = A.AdapterDesc(A.ADAPTER_DORA_ROWS, c["rank"], c["alpha"], 0, c["targets"], 1234, c["batch"], c["frames"],
+                           c["C"], 0)
+        tensors = lm_tensors(c)
+    ctx = A.Context(md, ad, device)
+    for name, shape in tensors:
+        w, kind = synth_weight(rng, name, shape)
+        if kind == "q8_0":
+            ctx.bind(name, q8_0(w), A.TYPE_Q8_0)
+        else:
+            ctx.bind(name, w, A.TYPE_F32)
+    ctx.finalize()
+    return ctx
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="mf", choices=["mf", "mg"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    c = MF if args.workload == "mf" else MG
+    if args.impl == "reference":
+        return run_reference(args, c)
+
+    import torch
+    import torch.distributed as dist
+    import actrain as A
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    ctx = build_context(A, c, args.workload, local)
+    if world > 1:
+        uid = [A.Context.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        ctx.nccl_init(uid[0], world, rank)
+
+    rng = np.random.default_rng(1000 + rank)
+    n = c["batch"]
+    if args.workload == "mf":
+        batch = (rng.standard_normal((n, c["lat"], c["T"]), dtype=np.float32),
+                 rng.standard_normal((n, c["lat"], c["T"]), dtype=np.float32),
+                 rng.standard_normal((n, c["C"], c["cond"]), dtype=np.float32),
+                 rng.uniform(0, 1, n).astype(np.float32), np.zeros(n, np.int32), np.full(n, -1, np.int32))
+        stage = lambda: ctx.mf_stage(*batch)
+        e2e_step = lambda: ctx.mf_step(*batch)
+        h2d = sum(a.nbytes for a in batch[:4]) + 4 * n * (1 + c["tdim"])
+    else:
+        batch = (rng.integers(0, c["card"], (n, c["n_q"], c["frames"])).astype(np.int32),
+                 rng.standard_normal((n, c["C"], c["dim"]), dtype=np.float32))
+        stage = lambda: ctx.mg_stage(*batch)
+        e2e_step = lambda: ctx.mg_step(*batch)
+        T = c["frames"] + c["n_q"] - 1
+        h2d = n * c["n_q"] * (T + c["frames"]) * 4 + batch[1].nbytes
+    d2h = 4 * n
+
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    step_counter = [0]
+
+    def one_step(e2e=False):
+        if e2e:
+            e2e_step()
+        else:
+            ctx.run_staged(n, read_loss=False)
+        if world > 1:
+            ctx.allreduce_grads(n * world)
+        step_counter[0] += 1
+        ctx.optimizer(lr=1e-4, step=step_counter[0], weight_decay=0.01, clip=1.0)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- warm-up (first call runs eagerly, second captures the CUDA graph)
+    stage()
+    for _ in range(max(args.warmup, 3)):
+        one_step()
+    barrier()
+
+    # ---- value: device-timed, inputs resident in HBM
+    clocks = Clocks(local)
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        one_step()
+    ev1.record(stream)
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    ms_per_step = ms / args.steps
+    value = world * args.steps / (ms / 1e3)
+
+    # ---- e2e: through the public API with host buffers (H2D inputs + D2H losses inside)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one_step(e2e=True)
+    barrier()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e_value = world * args.steps / e2e_s
+
+    # ---- kernel classes from eagerly launched, event-bracketed steps (profiling mode)
+    ctx.set_profiling(True)
+    ctx.reset_kernel_stats()
+    stage()
+    for _ in range(2):
+        one_step()
+    ctx.set_profiling(False)
+    stats = [ctx.kernel_stats(i) for i in range(3)]
+    kernels_per_step = ctx.graph_kernel_nodes(n) + 2 + (1 if world > 1 else 0)
+    step_flops = ctx.step_flops(n)
+
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    peak_tf = peaks.get("bf16_tflops_sustained", 1400.0)
+    peak_src = "measured (sustained)" if "bf16_tflops_sustained" in peaks else "fallback (sustained)"
+    g = stats[0]
+    achieved = g["flops"] / (g["ms"] / 1e3) / 1e12 if g["ms"] > 0 else 0.0
+    traffic = None
+    try:
+        prof = json.load(open(os.path.join(ROOT, "profiles", "gemm_traffic.json")))
+        traffic = prof.get("bytes_per_launch")
+    except (OSError, ValueError):
+        pass
+
+    line = {
+        "metric": "DiT LoRA train steps/s (8x30s clips)" if args.workload == "mf" else "MusicGen DoRA train steps/s (4x30s seqs per GPU)",
+        "value": value, "unit": "steps/s (8x30s-clip steps, summed over ranks)" if args.workload == "mf" else "steps/s (4-seq steps, summed over ranks)",
+        "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": ("mf-cfg2: DiT d1024 L24 H16 F4096 Q8_0 base, 8x750 frames/rank, 32 tokens, "
+                                "LoRA r16 a32 on qkv/out/ff.0/ff.2 (6,291,456 params), AdamW")
+                   if args.workload == "mf" else
+                   "mg-cfg4: LM d1536 L48 H24 F6144 Q8_0 base, 4x1500 frames/rank, DoRA-rows r16 on 7 projections",
+                   "global_batch": n * world, "seq_len": c.get("T", c.get("frames")),
+                   "parallelism": f"dp{world}", "l2": "no flush: per-step working set (activations ~7 GB, weights 0.9 GB) exceeds the 126 MB L2"},
+        "e2e": {"value": e2e_value, "unit": "steps/s (8x30s-clip steps, summed over ranks)", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": int(kernels_per_step * args.steps),
+        "step_tflops": step_flops / (ms_per_step / 1e3) / 1e12,
+        "step_frac_of_peak": step_flops / (ms_per_step / 1e3) / 1e12 / peak_tf,
+        "roofline": {"kernel": "dense projection GEMMs (class 0)", "bound": "tensor", "achieved": achieved,
+                     "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf if peak_tf else None,
+                     "traffic": traffic, "peak_source": peak_src,
+                     "launches_per_step": g["launches"] / 2, "ms_per_step": g["ms"] / 2},
+        "kernel_classes_ms_per_step": {"gemm": stats[0]["ms"] / 2, "attention": stats[1]["ms"] / 2,
+                                       "other": stats[2]["ms"] / 2},
+    }
+    if clk:
+        line["clocks"] = clk
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "mf":
+        dt, scale, desc = cpu_sample(c)
+        line["cpu_baseline"] = {"value": 1.0 / (dt * scale), "unit": "steps/s (8x30s-clip steps)",
+                                "cores": os.cpu_count(), "kind": "port", "sample": desc}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

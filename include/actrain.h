@@ -1,0 +1,178 @@
+/*
+ * actrain.h -- C ABI of the B200 adapter-training step (libactrain.so).
+ *
+ * This is the seam between the unchanged trainer front ends (mf-train / mg-train argument
+ * parsing, cache sampling, checkpoint files) and the device step.  In the reference the
+ * same seam is the class API of MfTrainGraph / MgTrainGraph plus TrainAccumulation:
+ *   src/mf/train.h:31-256      MfTrainGraph  (ctor, compute, compute_bridge, adam_step, save)
+ *   src/mg/train.h:51-230      MgTrainGraph  (ctor, compute, adam_step, save)
+ *   src/ac/train_controls.h:75-119  TrainAccumulation (add, update)
+ *   src/gguf_model.h:363-436   load_gguf / graph_compute_checked (weights on the device)
+ *
+ * Conventions: every call returns ACT_OK (0) or a nonzero status and never throws; the
+ * message of the last failure is available from act_last_error().  A context is bound to
+ * one CUDA device and is not thread-safe: one host thread per rank.  All pointers in the
+ * batch structs are HOST pointers unless a name says otherwise.
+ */
+#ifndef ACTRAIN_H
+#define ACTRAIN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define ACT_OK 0
+#define ACT_ERR_INVALID 1    /* bad argument, shape or configuration (reference: std::runtime_error) */
+#define ACT_ERR_CUDA 2       /* CUDA runtime failure */
+#define ACT_ERR_NCCL 3       /* NCCL failure */
+#define ACT_ERR_STATE 4      /* call out of order (e.g. step before act_finalize) */
+#define ACT_ERR_NONFINITE 5  /* nonfinite loss or optimizer update (src/mf/train.h:186, train_controls.h:113) */
+
+#define ACT_FAMILY_MELODYFLOW 0
+#define ACT_FAMILY_MUSICGEN 1
+
+#define ACT_ADAPTER_LORA 0
+#define ACT_ADAPTER_DORA_ROWS 1
+
+/* ggml type ids of the base weights accepted by act_bind_weight */
+#define ACT_TYPE_F32 0
+#define ACT_TYPE_F16 1
+#define ACT_TYPE_Q8_0 8
+
+/* adapter target bits, in the reference's order (src/mf/train.h:69, src/mg/train.h:90) */
+#define ACT_TARGET_SELF_QKV (1u << 0)
+#define ACT_TARGET_SELF_OUT (1u << 1)
+#define ACT_TARGET_CROSS_Q (1u << 2)
+#define ACT_TARGET_CROSS_KV (1u << 3)
+#define ACT_TARGET_CROSS_OUT (1u << 4)
+#define ACT_TARGET_FF0 (1u << 5)
+#define ACT_TARGET_FF2 (1u << 6)
+#define ACT_TARGETS_REFERENCE 0x1Fu     /* attention projections (default mf-train / mg-train) */
+#define ACT_TARGETS_REFERENCE_FFN 0x7Fu /* with --train-ffn */
+
+typedef struct act_ctx act_ctx;
+
+/* Model hyper-parameters, read by the caller from GGUF metadata exactly as
+ * DitConfig::from (src/mf/dit.h:44-71) and LmConfig::from (src/mg/lm.h:60-90) do. */
+typedef struct {
+    int family;                                  /* ACT_FAMILY_* */
+    int dim, layers, heads, head_dim, ff_dim;
+    int latent_dim, cond_dim, time_dim, n_skip;  /* MelodyFlow */
+    int add_zero_attn;                           /* MelodyFlow */
+    int n_q, card, special_token_id, pos_denominator; /* MusicGen */
+    float max_period;                            /* MusicGen sin positions */
+    float norm_eps;
+} act_model_desc;
+
+/* Adapter and capacity: MfTrainGraph(W, c, frames, tokens, rank, alpha, first_layer, seed,
+ * type, feedforward) (src/mf/train.h:47-48) / MgTrainGraph(..., prefix, ...) (src/mg/train.h:66-67).
+ * `targets` generalises the reference's feedforward flag (0x1F / 0x7F reproduce it). */
+typedef struct {
+    int type;          /* ACT_ADAPTER_LORA | ACT_ADAPTER_DORA_ROWS */
+    int rank;
+    float alpha;       /* scale = alpha / rank */
+    int first_layer;
+    unsigned targets;  /* ACT_TARGET_* bits */
+    uint32_t seed;     /* lora_A ~ N(0, 0.02) drawn from std::mt19937(seed) in parameter order */
+    int max_batch;     /* clips (MelodyFlow) or sequences (MusicGen) per step on this device */
+    int frames;        /* latent frames (MelodyFlow) / codec timesteps (MusicGen) */
+    int tokens;        /* conditioning tokens */
+    int prefix_frames; /* MusicGen: timesteps before this are not scored (src/mg/train.h:195-196) */
+} act_adapter_desc;
+
+/* One MelodyFlow microbatch (MfTrainGraph::compute, src/mf/train.h:148-188), n <= max_batch. */
+typedef struct {
+    int n;
+    const float* clean;        /* [n][latent_dim][frames] */
+    const float* noise;        /* [n][latent_dim][frames] */
+    const float* hidden;       /* [n][tokens][cond_dim] T5 states (zero padded) */
+    const float* t;            /* [n] flow time in [0, 1] */
+    const int32_t* unconditional; /* [n] or NULL: 1 masks every text token */
+    const int32_t* valid_tokens;  /* [n] or NULL: tokens >= valid are masked; -1 = all */
+} act_mf_batch;
+
+/* One MusicGen microbatch (MgTrainGraph::compute, src/mg/train.h:178-227). */
+typedef struct {
+    int n;
+    const int32_t* codes;      /* [n][n_q][frames] codec tokens in [0, card) */
+    const float* context;      /* [n][tokens][dim] projected conditioning */
+} act_mg_batch;
+
+/* TrainAccumulation::update (src/ac/train_controls.h:89-118). */
+typedef struct {
+    float lr;            /* already scheduled: TrainControls::rate (src/ac/train_controls.h:53-58) */
+    float beta1, beta2, eps;
+    float weight_decay;  /* decoupled; applied to lora_A / lora_B only */
+    float clip;          /* global L2 clip */
+    int step;            /* 1-based optimizer step for bias correction */
+    int count;           /* samples the gradient sum averages over; 0 = accumulated count */
+} act_opt;
+
+/* replaces the MfTrainGraph / MgTrainGraph constructors (graph build + allocation) */
+int act_create(act_ctx** out, int device, const act_model_desc* model, const act_adapter_desc* adapter);
+/* replaces load_gguf's tensor upload (src/gguf_model.h:363-420); name = GGUF tensor name */
+int act_bind_weight(act_ctx* ctx, const char* name, int ggml_type, const void* host, size_t bytes);
+/* after every weight: checks completeness, DoRA row norms (src/ac/lora.h:11-32), parameter init */
+int act_finalize(act_ctx* ctx);
+
+/* parameter table in the reference order (src/mf/train.h:68-104): name, flat offset, shape */
+int64_t act_param_count(act_ctx* ctx);
+int act_param_tensor_count(act_ctx* ctx);
+int act_param_tensor(act_ctx* ctx, int index, char* name, size_t name_cap, int64_t* offset,
+                     int64_t* rows, int64_t* cols);
+int act_set_params(act_ctx* ctx, const float* value, size_t n);
+/* value, m, v (any may be NULL): what save() and the .state sidecar write */
+int act_get_params(act_ctx* ctx, float* value, float* m, float* v, size_t n);
+int act_set_moments(act_ctx* ctx, const float* m, const float* v, size_t n);
+int act_get_grads(act_ctx* ctx, float* grad, size_t n);
+int act_zero_grads(act_ctx* ctx);
+
+/* forward + backward of one microbatch; gradients accumulate on the device (the reference's
+ * compute() followed by TrainAccumulation::add).  loss_per_sample may be NULL. */
+int act_mf_step(act_ctx* ctx, const act_mf_batch* batch, float* loss_per_sample);
+int act_mg_step(act_ctx* ctx, const act_mg_batch* batch, float* loss_per_sample);
+
+/* data parallelism (no counterpart in the reference, which trains on one device) */
+int act_nccl_get_unique_id(void* id_128_bytes);
+int act_nccl_init(act_ctx* ctx, const void* id_128_bytes, int nranks, int rank);
+/* sum gradients over ranks; nccl_comm NULL uses the context's own communicator.
+ * global_count becomes the averaging count of the next act_optimizer. */
+int act_allreduce_grads(act_ctx* ctx, void* nccl_comm, int global_count);
+
+/* mean, clip, AdamW, zero gradients (TrainAccumulation::update).  *nonfinite receives the
+ * number of nonfinite updated values; a nonzero count also returns ACT_ERR_NONFINITE. */
+int act_optimizer(act_ctx* ctx, const act_opt* opt, int* nonfinite);
+
+const char* act_last_error(act_ctx* ctx);
+void act_destroy(act_ctx* ctx);
+
+/* ---- measurement hooks (device-resident inputs, kernel timing) ---- */
+void* act_stream(act_ctx* ctx);   /* the cudaStream_t every kernel of the context runs on */
+/* copy a batch to the device (host->device), then run it from device memory */
+int act_mf_stage(act_ctx* ctx, const act_mf_batch* batch);
+int act_mg_stage(act_ctx* ctx, const act_mg_batch* batch);
+int act_run_staged(act_ctx* ctx, float* loss_per_sample /* may be NULL: no device->host read */);
+/* per-kernel-class timing of eagerly launched steps: 0 disables (steps use the CUDA graph) */
+int act_set_profiling(act_ctx* ctx, int enable);
+/* class 0 = dense projection GEMMs, 1 = attention fwd+bwd, 2 = everything else */
+int act_kernel_stats(act_ctx* ctx, int cls, double* ms, double* flops, double* bytes, int64_t* launches);
+int act_reset_kernel_stats(act_ctx* ctx);
+/* algorithmic FLOPs of one step of n samples (2 per multiply-add) */
+double act_step_flops(act_ctx* ctx, int n);
+/* kernels in the captured step graph for microbatch size n (-1 before the graph exists) */
+int64_t act_graph_kernel_nodes(act_ctx* ctx, int n);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ACTRAIN_H */
