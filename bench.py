@@ -222,8 +222,14 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="mf", choices=["mf", "mg"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="override depth (profiling captures only)")
+    ap.add_argument("--batch", type=int, default=0, help="override clips per rank (profiling captures only)")
     args = ap.parse_args()
-    c = MF if args.workload == "mf" else MG
+    c = dict(MF if args.workload == "mf" else MG)
+    if args.layers:
+        c["layers"] = args.layers
+    if args.batch:
+        c["batch"] = args.batch
     if args.impl == "reference":
         return run_reference(args, c)
 
@@ -357,6 +363,7 @@ def main():
                    if args.workload == "mf" else
                    "mg-cfg4: LM d1536 L48 H24 F6144 Q8_0 base, 4x1500 frames/rank, DoRA-rows r16 on 7 projections",
                    "global_batch": n * world, "seq_len": c.get("T", c.get("frames")),
+                   "layers": c["layers"], "clips_per_rank": n,
                    "parallelism": f"dp{world}", "l2": "no flush: per-step working set (activations ~7 GB, weights 0.9 GB) exceeds the 126 MB L2"},
         "e2e": {"value": e2e_value, "unit": "steps/s (8x30s-clip steps, summed over ranks)", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
