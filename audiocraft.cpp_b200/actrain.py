@@ -93,6 +93,8 @@ SIGNATURES = {
     "act_reset_kernel_stats": (C.c_int, [C.c_void_p]),
     "act_step_flops": (C.c_double, [C.c_void_p, C.c_int]),
     "act_graph_kernel_nodes": (C.c_int64, [C.c_void_p, C.c_int]),
+    "act_gemm_bf16": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                C.c_int]),
 }
 
 
@@ -271,6 +273,18 @@ class Context:
 
     def graph_kernel_nodes(self, n: int) -> int:
         return int(self._L.act_graph_kernel_nodes(self.h, n))
+
+
+def gemm_bf16(A_bits: np.ndarray, B_bits: np.ndarray, M: int, N: int, K: int, b_mn_major: bool, path: int = 0,
+              device: int = 0) -> np.ndarray:
+    """C = A . B(n,k) on the device; A_bits/B_bits are bf16 bit patterns (uint16)."""
+    C_ = np.zeros((M, N), np.float32)
+    a = np.ascontiguousarray(A_bits, np.uint16)
+    b = np.ascontiguousarray(B_bits, np.uint16)
+    rc = lib().act_gemm_bf16(device, a.ctypes.data, b.ctypes.data, C_.ctypes.data, M, N, K, int(b_mn_major), path)
+    if rc != ACT_OK:
+        raise ActError(rc, lib().act_last_error(None).decode())
+    return C_
 
 
 def mf_model(dim, layers, heads, ff_dim, latent_dim=128, cond_dim=768, time_dim=256, norm_eps=1e-5):

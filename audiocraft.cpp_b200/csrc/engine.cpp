@@ -18,6 +18,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cstdlib>
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -171,6 +172,8 @@ struct act_ctx {
     size_t evnext = 0;
 
     ncclComm_t comm = nullptr;
+    int* kerr = nullptr;
+    bool use_tc = true;
 
     // ------------------------------------------------------------------------------------
     template <class Tp>
@@ -228,7 +231,16 @@ struct act_ctx {
 
     void run_gemm(const GemmArgs& g, int cls = 0) {
         const double fl = 2.0 * g.M * g.N * (double)(g.K1 + g.K2);
-        timed(cls, fl, 0, [&] { gemm(g, stream); });
+        if (use_tc && gemm_tc_supported(g)) timed(cls, fl, 0, [&] { gemm_tc(g, kerr, stream); });
+        else timed(cls, fl, 0, [&] { gemm(g, stream); });
+    }
+
+    // kernels record a nonzero code here instead of hanging on a wait that cannot finish
+    void check_kernel_error() {
+        int e = 0;
+        CK(cudaMemcpyAsync(&e, kerr, sizeof(int), cudaMemcpyDeviceToHost, stream));
+        CK(cudaStreamSynchronize(stream));
+        if (e) throw Error(ACT_ERR_CUDA, "device kernel reported a timed-out wait (code " + std::to_string(e) + ")");
     }
 
     static int splitk_for(long tiles, long ktiles) {
@@ -703,7 +715,7 @@ struct act_ctx {
         accumulated += n;
         if (loss) {
             CK(cudaMemcpyAsync(h_loss, d_loss, n * 4, cudaMemcpyDeviceToHost, stream));
-            CK(cudaStreamSynchronize(stream));
+            check_kernel_error();
             for (int i = 0; i < n; ++i) {
                 if (!std::isfinite(h_loss[i])) throw Error(ACT_ERR_NONFINITE, "nonfinite training loss");
                 loss[i] = h_loss[i];
@@ -737,6 +749,9 @@ struct act_ctx {
         if (ad.tokens % 8) throw Error(ACT_ERR_INVALID, "tokens must be a multiple of 8 (pad the conditioning)");
         CK(cudaSetDevice(device));
         CK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+        kerr = dalloc<int>(1);
+        const char* gp = std::getenv("ACTRAIN_GEMM");
+        use_tc = !(gp && std::string(gp) == "mma");
         D = md.dim; F = md.ff_dim; H = md.heads; L = md.layers;
         C = ad.tokens; B = ad.max_batch;
         T = mf ? ad.frames : ad.frames + md.n_q - 1;  // MusicGen: pattern steps - 1 (src/mg/train.h:74)
@@ -1170,7 +1185,7 @@ struct act_ctx {
         });
         int bad = 0;
         CK(cudaMemcpyAsync(&bad, nonfinite_dev, sizeof(int), cudaMemcpyDeviceToHost, stream));
-        CK(cudaStreamSynchronize(stream));
+        check_kernel_error();
         collect_stats();
         accumulated = 0;
         count_override = 0;
@@ -1478,6 +1493,56 @@ int act_reset_kernel_stats(act_ctx* ctx) {
 }
 
 double act_step_flops(act_ctx* ctx, int n) { return ctx && ctx->finalized ? ctx->step_flops(n) : -1.0; }
+
+int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path) {
+    // Stand-alone check of the projection GEMM: C[M][N] (fp32) = A[M][K] . B(n,k), bf16 inputs,
+    // B given as [N][K] (b_mn_major = 0) or [K][N] (1).  path 0 auto, 1 mma.sync, 2 tcgen05.
+    void *dA = nullptr, *dB = nullptr, *dC = nullptr;
+    int* derr = nullptr;
+    cudaStream_t st = nullptr;
+    auto cleanup = [&] {
+        if (st) cudaStreamSynchronize(st);
+        cudaFree(dA); cudaFree(dB); cudaFree(dC); cudaFree(derr);
+        if (st) cudaStreamDestroy(st);
+    };
+    try {
+        if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0) throw Error(ACT_ERR_INVALID, "invalid GEMM arguments");
+        CK(cudaSetDevice(device));
+        CK(cudaStreamCreate(&st));
+        CK(cudaMalloc(&dA, (size_t)M * K * 2));
+        CK(cudaMalloc(&dB, (size_t)N * K * 2));
+        CK(cudaMalloc(&dC, (size_t)M * N * 4));
+        CK(cudaMalloc(&derr, sizeof(int)));
+        CK(cudaMemsetAsync(derr, 0, sizeof(int), st));
+        CK(cudaMemcpyAsync(dA, A, (size_t)M * K * 2, cudaMemcpyHostToDevice, st));
+        CK(cudaMemcpyAsync(dB, B, (size_t)N * K * 2, cudaMemcpyHostToDevice, st));
+        GemmArgs g;
+        g.M = M; g.N = N; g.K1 = K;
+        g.A1 = static_cast<const bf16*>(dA); g.lda1 = K;
+        g.B1 = static_cast<const bf16*>(dB); g.ldb1 = b_mn_major ? N : K; g.b_kmajor = !b_mn_major;
+        g.mode = EPI_STORE_F32; g.out = dC; g.ldo = N;
+        const bool tc = path == 2 || (path == 0 && gemm_tc_supported(g));
+        if (tc && !gemm_tc_supported(g)) throw Error(ACT_ERR_INVALID, "shape not supported by the tcgen05 path");
+        if (tc) gemm_tc(g, derr, st);
+        else gemm(g, st);
+        CK(cudaGetLastError());
+        CK(cudaMemcpyAsync(C, dC, (size_t)M * N * 4, cudaMemcpyDeviceToHost, st));
+        int e = 0;
+        CK(cudaMemcpyAsync(&e, derr, sizeof(int), cudaMemcpyDeviceToHost, st));
+        CK(cudaStreamSynchronize(st));
+        if (e) throw Error(ACT_ERR_CUDA, "GEMM kernel reported a timed-out wait (code " + std::to_string(e) + ")");
+        cleanup();
+        return ACT_OK;
+    } catch (const Error& e) {
+        g_error = e.what();
+        cleanup();
+        return e.code;
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        cleanup();
+        return ACT_ERR_INVALID;
+    }
+}
 
 int64_t act_graph_kernel_nodes(act_ctx* ctx, int n) {
     if (!ctx) return -1;

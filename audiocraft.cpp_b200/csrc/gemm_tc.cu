@@ -1,0 +1,496 @@
+// gemm_tc.cu -- dense projection GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// C[m][n] = epilogue( sum_k A[m][k] B(n,k) ) with A K-major (activations / output gradients,
+// row-major [M][K]) and B either K-major (frozen weight [N][K]: forward Y = X W^T) or MN-major
+// (frozen weight read as [K][N]: input gradient dX = dY W).  A second K segment (A2, B2)
+// carries the LoRA rank block, so  Y = [X | sXA^T] [W | B]^T  and  dX = [dY | dU] [W ; A]
+// are each one pass over the tile.
+//
+// Persistent, warp-specialised CTA (one per SM):
+//   warp 0      TMA producer (one elected thread): A box 128x64, B box 256x64 (or 4 boxes of
+//               64x64 for MN-major B), 128-byte swizzle, into a 4-stage ring
+//   warp 1      MMA issuer (one thread): tcgen05.mma.cta_group::1.kind::f16, 128 x BN x 16,
+//               fp32 accumulators in TMEM, two accumulator buffers so the epilogue of tile i
+//               overlaps the mainloop of tile i+1
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, fused epilogue, 16-byte stores
+// Every mbarrier wait is bounded (globaltimer); on expiry the CTA records an error code,
+// drains what it issued and returns, so a logic error cannot hang the device.
+// No cluster launch and no multicast: every CTA loads its own tiles.
+#include <cuda.h>
+
+#include <stdexcept>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace act {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BKE = 64;  // K elements per stage (one 128-byte swizzle row)
+constexpr int EPI_WARPS = 4;
+constexpr int NTHREADS = (2 + EPI_WARPS) * 32;
+constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s per wait
+
+struct TcParams {
+    int M, N, K1, K2;
+    int num_m, num_n;
+    int mode;
+    float alpha;
+    const float* colscale;
+    void* out;
+    long ldo;
+    const float* resid;
+    long ldr;
+    bf16* aux;
+    long ldaux;
+    const bf16* auxin;
+    long ldauxin;
+    const float* colscale2;
+    const float* bias;
+    int nvalid, mvalid;
+    int* err;
+};
+
+struct TcMaps {
+    CUtensorMap a1, b1, a2, b2;
+};
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: returns false (and records `code`) if the phase does not complete in time.
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
+    if (mbar_try(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer();
+    while (true) {
+        for (int i = 0; i < 256; ++i)
+            if (mbar_try(bar, parity)) return true;
+        if (globaltimer() - t0 > WAIT_NS) {
+            atomicCAS(err, 0, code);
+            return false;
+        }
+        if (*(volatile int*)err) return false;  // another CTA already failed: stop waiting
+    }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+    d |= 1ull << 46;  // descriptor version (sm100)
+    d |= 2ull << 61;  // SWIZZLE_128B
+    return d;
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int BN>
+struct TcCfg {
+    static constexpr int A_BYTES = BM * BKE * 2;
+    static constexpr int B_BYTES = BN * BKE * 2;
+    static constexpr int STAGE = A_BYTES + B_BYTES;
+    static constexpr int STAGES = BN == 256 ? 4 : 6;
+    static constexpr int SMEM = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulator buffers
+};
+
+// Epilogue of 32 consecutive columns n .. n+31 of row m held as fp32 in v[].
+__device__ __forceinline__ void epilogue32(const TcParams& p, int m, int n, float* v) {
+    if (p.alpha != 1.0f)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] *= p.alpha;
+    if (p.colscale) {
+        const float4* cs = reinterpret_cast<const float4*>(p.colscale + n);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 c = cs[i];
+            v[4 * i] *= c.x; v[4 * i + 1] *= c.y; v[4 * i + 2] *= c.z; v[4 * i + 3] *= c.w;
+        }
+    }
+    if (p.aux && p.mode != EPI_GELU) {
+        uint4* a = reinterpret_cast<uint4*>(p.aux + (long)m * p.ldaux + n);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            a[i] = make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
+                              pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
+    }
+    switch (p.mode) {
+        case EPI_STORE_F32:
+        case EPI_ACCUM_F32:
+        case EPI_RESID_F32: {
+            float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) + (long)m * p.ldo + n);
+            if (p.mode == EPI_ACCUM_F32) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float4 r = o[i];
+                    v[4 * i] += r.x; v[4 * i + 1] += r.y; v[4 * i + 2] += r.z; v[4 * i + 3] += r.w;
+                }
+            } else if (p.mode == EPI_RESID_F32) {
+                const float4* rr = reinterpret_cast<const float4*>(p.resid + (long)m * p.ldr + n);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float4 r = rr[i];
+                    v[4 * i] += r.x; v[4 * i + 1] += r.y; v[4 * i + 2] += r.z; v[4 * i + 3] += r.w;
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            break;
+        }
+        case EPI_ATOMIC_F32: {
+            float* o = static_cast<float*>(p.out) + (long)m * p.ldo + n;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) atomicAdd(o + i, v[i]);
+            break;
+        }
+        default: {
+            if (p.mode == EPI_BIAS_BF16) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] += p.bias[n + i];
+            } else if (p.mode == EPI_GELU) {
+                uint4* a = reinterpret_cast<uint4*>(p.aux + (long)m * p.ldaux + n);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const bf16 z0 = __float2bfloat16(v[8 * i + 2 * j]), z1 = __float2bfloat16(v[8 * i + 2 * j + 1]);
+                        w[j] = (uint32_t)__bfloat16_as_ushort(z0) | ((uint32_t)__bfloat16_as_ushort(z1) << 16);
+                        v[8 * i + 2 * j] = gelu_as(__bfloat162float(z0));
+                        v[8 * i + 2 * j + 1] = gelu_as(__bfloat162float(z1));
+                    }
+                    a[i] = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            } else if (p.mode == EPI_GELU_BWD) {
+                const uint4* z = reinterpret_cast<const uint4*>(p.auxin + (long)m * p.ldauxin + n);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint4 zz = z[i];
+                    const uint32_t w[4] = {zz.x, zz.y, zz.z, zz.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        v[8 * i + 2 * j] *= gelu_as_grad(__bfloat162float(__ushort_as_bfloat16((unsigned short)(w[j] & 0xffff))));
+                        v[8 * i + 2 * j + 1] *= gelu_as_grad(__bfloat162float(__ushort_as_bfloat16((unsigned short)(w[j] >> 16))));
+                    }
+                }
+                if (p.colscale2)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] *= p.colscale2[n + i];
+            }
+            uint4* o = reinterpret_cast<uint4*>(static_cast<bf16*>(p.out) + (long)m * p.ldo + n);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                o[i] = make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
+                                  pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
+        }
+    }
+}
+
+template <int BN, bool B_MN>
+__global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(const __grid_constant__ TcMaps maps, const TcParams p) {
+    using Cfg = TcCfg<BN>;
+    constexpr int S = Cfg::STAGES;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023) & ~1023u;
+    unsigned char* smem = smem_raw + (base - raw);
+    const uint32_t bars = base + S * Cfg::STAGE;
+    // barrier layout: full[S], empty[S], tfull[2], tempty[2], drain, then the TMEM address
+    auto full_bar = [&](int s) { return bars + 8 * s; };
+    auto empty_bar = [&](int s) { return bars + 8 * (S + s); };
+    auto tfull_bar = [&](int a) { return bars + 8 * (2 * S + a); };
+    auto tempty_bar = [&](int a) { return bars + 8 * (2 * S + 2 + a); };
+    const uint32_t drain_bar = bars + 8 * (2 * S + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S * Cfg::STAGE + 8 * (2 * S + 5));
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), EPI_WARPS);
+        }
+        mbar_init(drain_bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(Cfg::TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int nk1 = (p.K1 + BKE - 1) / BKE, nk2 = (p.K2 + BKE - 1) / BKE, nk = nk1 + nk2;
+    const int ntiles = p.num_m * p.num_n;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------------------ TMA producer
+        int it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+            const int mb = tile % p.num_m, nb = tile / p.num_m;
+            for (int kb = 0; kb < nk && ok; ++kb, ++it) {
+                const int s = it % S;
+                ok = mbar_wait(empty_bar(s), ((it / S) & 1) ^ 1, p.err, 1);
+                if (!ok) break;
+                const bool seg2 = kb >= nk1;
+                const CUtensorMap* ma = seg2 ? &maps.a2 : &maps.a1;
+                const CUtensorMap* mbm = seg2 ? &maps.b2 : &maps.b1;
+                const int k0 = (seg2 ? kb - nk1 : kb) * BKE;
+                const uint32_t sa = base + s * Cfg::STAGE, sb = sa + Cfg::A_BYTES;
+                mbar_expect_tx(full_bar(s), Cfg::STAGE);
+                tma_load_2d(sa, ma, k0, mb * BM, full_bar(s));
+                if (B_MN) {
+#pragma unroll
+                    for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 8192, mbm, nb * BN + 64 * j, k0, full_bar(s));
+                } else {
+                    tma_load_2d(sb, mbm, k0, nb * BN, full_bar(s));
+                }
+            }
+        }
+        // drain: wait until every stage this thread filled has landed
+        if (!ok)
+            for (int j = 0; j < S && it - 1 - j >= 0; ++j) {
+                const int i2 = it - 1 - j;
+                mbar_wait(full_bar(i2 % S), (i2 / S) & 1, p.err, 5);
+            }
+    } else if (warp == 1 && lane == 0) {
+        // ------------------------------------------------------------ MMA issuer
+        const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((B_MN ? 1u : 0u) << 16) |
+                               ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+        int it = 0, u = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++u) {
+            const int a = u & 1;
+            ok = mbar_wait(tempty_bar(a), ((u >> 1) & 1) ^ 1, p.err, 2);
+            if (!ok) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t tacc = tmem_base + a * BN;
+            for (int kb = 0; kb < nk; ++kb, ++it) {
+                const int s = it % S;
+                ok = mbar_wait(full_bar(s), (it / S) & 1, p.err, 3);
+                if (!ok) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t sa = base + s * Cfg::STAGE, sb = sa + Cfg::A_BYTES;
+                const bool seg2 = kb >= nk1;
+                const int kv = seg2 ? p.K2 - (kb - nk1) * BKE : p.K1 - kb * BKE;
+                const int nk16 = kv >= BKE ? BKE / 16 : (kv + 15) / 16;
+                for (int k16 = 0; k16 < nk16; ++k16) {
+                    const uint64_t ad = smem_desc(sa + k16 * 32, 16, 1024);
+                    const uint64_t bd = B_MN ? smem_desc(sb + k16 * 2048, 8192, 1024) : smem_desc(sb + k16 * 32, 16, 1024);
+                    mma_f16(tacc, ad, bd, idesc, (kb > 0 || k16 > 0) ? 1u : 0u);
+                }
+                mma_commit(empty_bar(s));
+            }
+            if (!ok) break;
+            mma_commit(tfull_bar(a));
+        }
+        // drain: all issued MMAs complete before TMEM is released
+        mma_commit(drain_bar);
+        mbar_wait(drain_bar, 0, p.err, 6);
+    } else if (warp >= 2) {
+        // ------------------------------------------------------------ epilogue
+        const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
+        int u = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++u) {
+            const int a = u & 1;
+            const int mb = tile % p.num_m, nb = tile / p.num_m;
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(tfull_bar(a), (u >> 1) & 1, p.err, 4);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int m = mb * BM + quad * 32 + lane;
+            const bool row_ok = m < p.M && m < p.mvalid;
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + a * BN + c * 32, r);
+                const int n = nb * BN + c * 32;
+                if (row_ok && n < p.nvalid) epilogue32(p, m, n, reinterpret_cast<float*>(r));
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty_bar(a));
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    __syncwarp();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(Cfg::TMEM_COLS));
+}
+
+// ---------------------------------------------------------------------------------------
+// host side: tensor maps through the driver entry point (no libcuda link dependency)
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !p)
+            throw std::runtime_error("cuTensorMapEncodeTiled is unavailable");
+        fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2D bf16 row-major tensor [rows][cols] with row stride ld (elements); box {box_cols, box_rows}.
+void make_map(CUtensorMap* map, const bf16* ptr, long rows, long cols, long ld, int box_cols, int box_rows) {
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * 2) % 16)
+        throw std::runtime_error("gemm_tc: operand not 16-byte aligned");
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<bf16*>(ptr), dims, strides, box,
+                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+}
+
+int g_num_sms = 0;
+
+template <int BN, bool B_MN>
+void launch_tc(const GemmArgs& a, int* err, cudaStream_t s) {
+    using Cfg = TcCfg<BN>;
+    TcMaps maps;
+    // A: [M][K] K-major; box 64 (k) x 128 (m)
+    make_map(&maps.a1, a.A1, a.M, a.K1, a.lda1, BKE, BM);
+    if (B_MN) make_map(&maps.b1, a.B1, a.K1, a.N, a.ldb1, 64, BKE);   // [K][N]: box 64 (n) x 64 (k)
+    else make_map(&maps.b1, a.B1, a.N, a.K1, a.ldb1, BKE, BN);        // [N][K]: box 64 (k) x BN (n)
+    if (a.K2 > 0) {
+        make_map(&maps.a2, a.A2, a.M, a.K2, a.lda2, BKE, BM);
+        if (B_MN) make_map(&maps.b2, a.B2, a.K2, a.N, a.ldb2, 64, BKE);
+        else make_map(&maps.b2, a.B2, a.N, a.K2, a.ldb2, BKE, BN);
+    } else {
+        maps.a2 = maps.a1;
+        maps.b2 = maps.b1;
+    }
+    TcParams p;
+    p.M = a.M; p.N = a.N; p.K1 = a.K1; p.K2 = a.K2;
+    p.num_m = (a.M + BM - 1) / BM; p.num_n = a.N / BN;
+    p.mode = a.mode; p.alpha = a.alpha; p.colscale = a.colscale; p.out = a.out; p.ldo = a.ldo;
+    p.resid = a.resid; p.ldr = a.ldr; p.aux = a.aux; p.ldaux = a.ldaux; p.auxin = a.auxin; p.ldauxin = a.ldauxin;
+    p.colscale2 = a.colscale2; p.bias = a.bias; p.nvalid = a.nvalid; p.mvalid = a.mvalid; p.err = err;
+    auto kern = gemm_tc_kernel<BN, B_MN>;
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+        configured = true;
+    }
+    if (!g_num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    const int tiles = p.num_m * p.num_n;
+    const int grid = tiles < g_num_sms ? tiles : g_num_sms;
+    kern<<<grid, NTHREADS, Cfg::SMEM, s>>>(maps, p);
+}
+
+}  // namespace
+
+bool gemm_tc_supported(const GemmArgs& a) {
+    if (!a.a_kmajor) return false;
+    if (a.M < BM || a.N % 128 || a.K1 % BKE || a.K1 <= 0 || a.splitk != 1) return false;
+    if (a.K2 && (a.K2 % 8 || !a.A2 || !a.B2)) return false;
+    if (a.mode == EPI_ATOMIC_F32 || a.nvalid < a.N || a.mvalid < a.M) return false;
+    if (a.ldo % 8 || (a.aux && a.ldaux % 8) || (a.auxin && a.ldauxin % 8) || (a.resid && a.ldr % 4)) return false;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(a.out) | reinterpret_cast<uintptr_t>(a.aux) |
+                         reinterpret_cast<uintptr_t>(a.auxin) | reinterpret_cast<uintptr_t>(a.resid) |
+                         reinterpret_cast<uintptr_t>(a.colscale) | reinterpret_cast<uintptr_t>(a.A1) |
+                         reinterpret_cast<uintptr_t>(a.B1) | reinterpret_cast<uintptr_t>(a.A2) |
+                         reinterpret_cast<uintptr_t>(a.B2);
+    return (al & 15) == 0;
+}
+
+void gemm_tc(const GemmArgs& a, int* err, cudaStream_t s) {
+    // 256-wide tiles unless that leaves most SMs idle for the last wave
+    const long tiles256 = (long)((a.M + BM - 1) / BM) * (a.N / 256);
+    const bool wide = a.N % 256 == 0 && tiles256 >= 2 * 148;
+    if (a.b_kmajor) {
+        if (wide) launch_tc<256, false>(a, err, s);
+        else launch_tc<128, false>(a, err, s);
+    } else {
+        if (wide) launch_tc<256, true>(a, err, s);
+        else launch_tc<128, true>(a, err, s);
+    }
+}
+
+}  // namespace act

@@ -54,7 +54,9 @@ struct GemmArgs {
     int mvalid = 1 << 30;              // rows >= mvalid are not written
 };
 
-void gemm(const GemmArgs& a, cudaStream_t s);
+void gemm(const GemmArgs& a, cudaStream_t s);                 // mma.sync path, any layout
+bool gemm_tc_supported(const GemmArgs& a);                     // shapes the tcgen05 path takes
+void gemm_tc(const GemmArgs& a, int* err, cudaStream_t s);     // tcgen05 / TMEM / TMA path
 
 // ---------------------------------------------------------------------------------------
 // attention over token-major q/k/v (head h at columns h*64 .. h*64+63), head_dim 64.

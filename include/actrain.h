@@ -165,6 +165,10 @@ int act_kernel_stats(act_ctx* ctx, int cls, double* ms, double* flops, double* b
 int act_reset_kernel_stats(act_ctx* ctx);
 /* algorithmic FLOPs of one step of n samples (2 per multiply-add) */
 double act_step_flops(act_ctx* ctx, int n);
+/* stand-alone projection GEMM on host buffers (tests and the kernel sweep): C[M][N] fp32 =
+ * A[M][K] . B(n,k) with bf16 A and B, B as [N][K] (b_mn_major 0) or [K][N] (1);
+ * path 0 = automatic, 1 = mma.sync kernel, 2 = tcgen05 kernel */
+int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path);
 /* kernels in the captured step graph for microbatch size n (-1 before the graph exists) */
 int64_t act_graph_kernel_nodes(act_ctx* ctx, int n);
 

@@ -56,7 +56,7 @@ def _bind_all(ctx, W, wtype, quantizable):
 
 
 class MfCase:
-    def __init__(self, dim=128, layers=4, heads=2, ff=256, lat=32, cond=32, tdim=16, T=40, C=8, rank=4,
+    def __init__(self, dim=128, layers=4, heads=2, ff=256, lat=32, cond=32, tdim=16, T=48, C=8, rank=4,
                  alpha=8.0, dora=False, targets=0x7F, first=0, seed=0, wstd=0.05, wtype="f32", batch=3,
                  device=0, b_std=0.03):
         rng = np.random.default_rng(seed)
