@@ -93,6 +93,9 @@ SIGNATURES = {
     "act_reset_kernel_stats": (C.c_int, [C.c_void_p]),
     "act_step_flops": (C.c_double, [C.c_void_p, C.c_int]),
     "act_graph_kernel_nodes": (C.c_int64, [C.c_void_p, C.c_int]),
+    "act_attention": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                C.c_void_p, C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_float)]),
     "act_gemm_bf16": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                 C.c_int]),
 }
@@ -285,6 +288,28 @@ def gemm_bf16(A_bits: np.ndarray, B_bits: np.ndarray, M: int, N: int, K: int, b_
     if rc != ACT_OK:
         raise ActError(rc, lib().act_last_error(None).decode())
     return C_
+
+
+def attention(q, k, v, dout, clips, T, Tk, H, nvalid=None, causal=False, zero_key=False, rope=None, device=0):
+    """Kernel-level attention: bf16 bit-pattern inputs (uint16) -> dict of outputs and device times."""
+    D = H * 64
+    o = np.zeros((clips * T, D), np.uint16)
+    lse = np.zeros((clips, H, T), np.float32)
+    dq = np.zeros((clips * T, D), np.uint16)
+    dk = np.zeros((clips * Tk, D), np.uint16)
+    dv = np.zeros((clips * Tk, D), np.uint16)
+    arrs = [np.ascontiguousarray(x, np.uint16) for x in (q, k, v)]
+    d = None if dout is None else np.ascontiguousarray(dout, np.uint16)
+    nv = None if nvalid is None else np.ascontiguousarray(nvalid, np.int32)
+    rp = None if rope is None else np.ascontiguousarray(rope, np.float32)
+    mf, mb = C.c_float(), C.c_float()
+    rc = lib().act_attention(device, arrs[0].ctypes.data, arrs[1].ctypes.data, arrs[2].ctypes.data, _ptr(d), clips, T,
+                             Tk, H, _ptr(nv), int(causal), int(zero_key), _ptr(rp), o.ctypes.data, lse.ctypes.data,
+                             dq.ctypes.data if d is not None else None, dk.ctypes.data if d is not None else None,
+                             dv.ctypes.data if d is not None else None, C.byref(mf), C.byref(mb))
+    if rc != ACT_OK:
+        raise ActError(rc, lib().act_last_error(None).decode())
+    return {"o": o, "lse": lse, "dq": dq, "dk": dk, "dv": dv, "ms_fwd": mf.value, "ms_bwd": mb.value}
 
 
 def mf_model(dim, layers, heads, ff_dim, latent_dim=128, cond_dim=768, time_dim=256, norm_eps=1e-5):

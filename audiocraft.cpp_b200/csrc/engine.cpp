@@ -1544,6 +1544,98 @@ int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int 
     }
 }
 
+int act_attention(int device, const void* q, const void* k, const void* v, const void* dout, int clips, int T,
+                  int Tk, int H, const int32_t* nvalid, int causal, int zero_key, const float* rope, void* o,
+                  float* lse, void* dq, void* dk, void* dv, float* ms_fwd, float* ms_bwd) {
+    // Stand-alone attention forward + backward on host buffers (tests and the kernel sweep).
+    std::vector<void*> bufs;
+    cudaStream_t st = nullptr;
+    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+    auto cleanup = [&] {
+        if (st) cudaStreamSynchronize(st);
+        for (void* b : bufs) cudaFree(b);
+        for (auto e : ev)
+            if (e) cudaEventDestroy(e);
+        if (st) cudaStreamDestroy(st);
+    };
+    try {
+        if (!q || !k || !v || !o || !lse || clips <= 0 || T <= 0 || Tk <= 0 || H <= 0)
+            throw Error(ACT_ERR_INVALID, "invalid attention arguments");
+        if (causal && Tk != T) throw Error(ACT_ERR_INVALID, "causal attention needs Tk == T");
+        CK(cudaSetDevice(device));
+        CK(cudaStreamCreate(&st));
+        for (auto& e : ev) CK(cudaEventCreate(&e));
+        const long D = (long)H * 64, rq = (long)clips * T, rk = (long)clips * Tk;
+        auto up = [&](const void* h, size_t bytes) -> void* {
+            void* d = nullptr;
+            CK(cudaMalloc(&d, std::max<size_t>(bytes, 16)));
+            bufs.push_back(d);
+            if (h) CK(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, st));
+            else CK(cudaMemsetAsync(d, 0, bytes, st));
+            return d;
+        };
+        AttnArgs a;
+        a.q = static_cast<const bf16*>(up(q, rq * D * 2));
+        a.k = static_cast<const bf16*>(up(k, rk * D * 2));
+        a.v = static_cast<const bf16*>(up(v, rk * D * 2));
+        a.ldq = a.ldk = a.ldv = D;
+        a.T = T; a.Tk = Tk; a.H = H; a.clips = clips;
+        a.nvalid = nvalid ? static_cast<const int*>(up(nvalid, clips * 4)) : nullptr;
+        a.causal = causal; a.zero_key = zero_key;
+        a.rope = rope ? static_cast<const float*>(up(rope, (size_t)T * 64 * 4)) : nullptr;
+        if (rope && Tk > T) throw Error(ACT_ERR_INVALID, "RoPE needs Tk <= T");
+        a.scale = 0.125f;
+        a.o = static_cast<bf16*>(up(nullptr, rq * D * 2));
+        a.ldo = D;
+        a.lse = static_cast<float*>(up(nullptr, rq * H * 4));
+        CK(cudaEventRecord(ev[0], st));
+        attn_fwd(a, st);
+        CK(cudaEventRecord(ev[1], st));
+        CK(cudaGetLastError());
+        const bool bwd = dout && dq && dk && dv;
+        bf16* ddq = nullptr;
+        if (bwd) {
+            a.dout = static_cast<const bf16*>(up(dout, rq * D * 2));
+            a.lddo = D;
+            a.dvec = static_cast<float*>(up(nullptr, rq * H * 4));
+            a.dq_acc = static_cast<float*>(up(nullptr, rq * D * 4));
+            a.ldq_acc = D;
+            a.dk = static_cast<bf16*>(up(nullptr, rk * D * 2));
+            a.dv = static_cast<bf16*>(up(nullptr, rk * D * 2));
+            a.lddk = a.lddv = D;
+            ddq = static_cast<bf16*>(up(nullptr, rq * D * 2));
+            CK(cudaEventRecord(ev[2], st));
+            attn_bwd(a, st);
+            attn_dq_finish(a, ddq, D, nullptr, st);
+            CK(cudaEventRecord(ev[3], st));
+            CK(cudaGetLastError());
+        }
+        CK(cudaMemcpyAsync(o, a.o, rq * D * 2, cudaMemcpyDeviceToHost, st));
+        CK(cudaMemcpyAsync(lse, a.lse, rq * H * 4, cudaMemcpyDeviceToHost, st));
+        if (bwd) {
+            CK(cudaMemcpyAsync(dq, ddq, rq * D * 2, cudaMemcpyDeviceToHost, st));
+            CK(cudaMemcpyAsync(dk, a.dk, rk * D * 2, cudaMemcpyDeviceToHost, st));
+            CK(cudaMemcpyAsync(dv, a.dv, rk * D * 2, cudaMemcpyDeviceToHost, st));
+        }
+        CK(cudaStreamSynchronize(st));
+        if (ms_fwd) CK(cudaEventElapsedTime(ms_fwd, ev[0], ev[1]));
+        if (ms_bwd) {
+            *ms_bwd = 0.f;
+            if (bwd) CK(cudaEventElapsedTime(ms_bwd, ev[2], ev[3]));
+        }
+        cleanup();
+        return ACT_OK;
+    } catch (const Error& e) {
+        g_error = e.what();
+        cleanup();
+        return e.code;
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        cleanup();
+        return ACT_ERR_INVALID;
+    }
+}
+
 int64_t act_graph_kernel_nodes(act_ctx* ctx, int n) {
     if (!ctx) return -1;
     auto it = ctx->kernel_nodes.find(n);

@@ -169,6 +169,15 @@ double act_step_flops(act_ctx* ctx, int n);
  * A[M][K] . B(n,k) with bf16 A and B, B as [N][K] (b_mn_major 0) or [K][N] (1);
  * path 0 = automatic, 1 = mma.sync kernel, 2 = tcgen05 kernel */
 int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path);
+/* stand-alone attention forward + backward on host buffers (tests and the kernel sweep):
+ * token-major bf16 q [clips*T][H*64], k/v [clips*Tk][H*64], dout like q; scale 1/8 (head_dim 64);
+ * nvalid: per-clip valid key count or NULL; causal; zero_key = the prepended zero key of
+ * src/ac/transformer.h:74-79; rope: [T][32] (cos, sin) pairs or NULL.  Outputs o (bf16),
+ * lse (fp32 [clips][H][T], base-2 log-sum-exp of the scaled scores), and, when dout is given,
+ * dq (bf16, like q), dk / dv (bf16, like k).  ms_fwd / ms_bwd (nullable) receive device times. */
+int act_attention(int device, const void* q, const void* k, const void* v, const void* dout, int clips, int T,
+                  int Tk, int H, const int32_t* nvalid, int causal, int zero_key, const float* rope, void* o,
+                  float* lse, void* dq, void* dk, void* dv, float* ms_fwd, float* ms_bwd);
 /* kernels in the captured step graph for microbatch size n (-1 before the graph exists) */
 int64_t act_graph_kernel_nodes(act_ctx* ctx, int n);
 
