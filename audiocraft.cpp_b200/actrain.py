@@ -96,6 +96,8 @@ SIGNATURES = {
     "act_attention": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                 C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                 C.c_void_p, C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_float)]),
+    "act_attention_bwd_noalloc": (C.c_int, [C.c_void_p] * 6 + [C.c_void_p] * 3 + [C.c_int] * 4 +
+                                  [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "act_gemm_bf16": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                 C.c_int]),
 }
@@ -310,6 +312,18 @@ def attention(q, k, v, dout, clips, T, Tk, H, nvalid=None, causal=False, zero_ke
     if rc != ACT_OK:
         raise ActError(rc, lib().act_last_error(None).decode())
     return {"o": o, "lse": lse, "dq": dq, "dk": dk, "dv": dv, "ms_fwd": mf.value, "ms_bwd": mb.value}
+
+
+NOALLOC_ATTN_SCRATCH_FLOATS = 8 * 1024 * 1024
+
+
+def attention_bwd_noalloc(q, k, v, o, lse, dout, dq, dk, dv, clips, T, Tk, H, nvalid=0, causal=False,
+                          zero_key=False, rope=0, stream=0):
+    """act_attention_bwd_noalloc: every argument is a device address (int), including the outputs."""
+    rc = lib().act_attention_bwd_noalloc(q, k, v, o, lse, dout, dq, dk, dv, clips, T, Tk, H, nvalid or None,
+                                         int(causal), int(zero_key), rope or None, stream or None)
+    if rc != ACT_OK:
+        raise ActError(rc, lib().act_last_error(None).decode())
 
 
 def mf_model(dim, layers, heads, ff_dim, latent_dim=128, cond_dim=768, time_dim=256, norm_eps=1e-5):

@@ -53,6 +53,12 @@ struct Error : std::runtime_error {
 
 thread_local std::string g_error;
 
+}  // namespace
+
+void act::set_last_error(const std::string& msg) { g_error = msg; }
+
+namespace {
+
 const char* const kTargets[7] = {"self.qkv", "self.out", "cross.q", "cross.kv", "cross.out", "ff.0", "ff.2"};
 
 struct Proj {

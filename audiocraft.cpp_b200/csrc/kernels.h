@@ -5,9 +5,14 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <string>
+
 typedef __nv_bfloat16 bf16;
 
 namespace act {
+
+// message returned by act_last_error(NULL) (defined with the C ABI in engine.cpp)
+void set_last_error(const std::string& msg);
 
 // ---------------------------------------------------------------------------------------
 // GEMM:  C[m][n] = epilogue( sum_k A(m,k) B(n,k) ),  K = K1 (+ K2 second segment).

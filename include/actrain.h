@@ -178,6 +178,26 @@ int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int 
 int act_attention(int device, const void* q, const void* k, const void* v, const void* dout, int clips, int T,
                   int Tk, int H, const int32_t* nvalid, int causal, int zero_key, const float* rope, void* o,
                   float* lse, void* dq, void* dk, void* dv, float* ms_fwd, float* ms_bwd);
+/* ---- attention backward that allocates nothing (no counterpart in the reference) ----
+ * For callers that must not call cudaMalloc / cudaFree: real-time hosts such as an audio
+ * plug-in's processing thread (an allocation can block and synchronise the device), code
+ * recording a CUDA graph under global stream capture (allocation is not permitted there), and
+ * embedders that own all device memory through their own pool.  Same computation and layouts
+ * as the backward half of act_attention, but every pointer is a DEVICE pointer on the calling
+ * thread's current device (nvalid and rope too), o and lse come from a forward pass, and the
+ * work is queued asynchronously on `stream` (NULL = the legacy default stream).
+ * Scratch (the fp32 dQ accumulator and the per-row rowsum(dO*O)) lives in one fixed array of
+ * ACT_NOALLOC_ATTN_SCRATCH_FLOATS floats (32 MiB) compiled into the library; every GPU that
+ * loads the library holds it until the process exits.  A problem needing more than
+ * clips*T*H*64 + clips*H*T <= ACT_NOALLOC_ATTN_SCRATCH_FLOATS floats is rejected with
+ * ACT_ERR_INVALID.  The first call on each device looks up that device's copy of the array
+ * (cudaGetSymbolAddress); make that first call before any stream capture.  Every call uses
+ * the same array and zeroes the accumulator it needs, so calls that overlap on the GPU (on
+ * different streams, or from different threads) race: serialise them. */
+#define ACT_NOALLOC_ATTN_SCRATCH_FLOATS (8L * 1024 * 1024)
+int act_attention_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const float* lse,
+                              const void* dout, void* dq, void* dk, void* dv, int clips, int T, int Tk, int H,
+                              const int32_t* nvalid, int causal, int zero_key, const float* rope, void* stream);
 /* kernels in the captured step graph for microbatch size n (-1 before the graph exists) */
 int64_t act_graph_kernel_nodes(act_ctx* ctx, int n);
 
