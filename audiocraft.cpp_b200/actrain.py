@@ -99,7 +99,7 @@ SIGNATURES = {
     "act_attention_bwd_noalloc": (C.c_int, [C.c_void_p] * 6 + [C.c_void_p] * 3 + [C.c_int] * 4 +
                                   [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "act_gemm_bf16": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
-                                C.c_int]),
+                                C.c_int, C.c_int, C.POINTER(C.c_float)]),
 }
 
 
@@ -281,15 +281,18 @@ class Context:
 
 
 def gemm_bf16(A_bits: np.ndarray, B_bits: np.ndarray, M: int, N: int, K: int, b_mn_major: bool, path: int = 0,
-              device: int = 0) -> np.ndarray:
-    """C = A . B(n,k) on the device; A_bits/B_bits are bf16 bit patterns (uint16)."""
+              device: int = 0, reps: int = 0):
+    """C = A . B(n,k) on the device; A_bits/B_bits are bf16 bit patterns (uint16).  With reps > 0
+    returns (C, mean ms per call)."""
     C_ = np.zeros((M, N), np.float32)
     a = np.ascontiguousarray(A_bits, np.uint16)
     b = np.ascontiguousarray(B_bits, np.uint16)
-    rc = lib().act_gemm_bf16(device, a.ctypes.data, b.ctypes.data, C_.ctypes.data, M, N, K, int(b_mn_major), path)
+    ms = C.c_float(0.0)
+    rc = lib().act_gemm_bf16(device, a.ctypes.data, b.ctypes.data, C_.ctypes.data, M, N, K, int(b_mn_major), path,
+                             reps, C.byref(ms))
     if rc != ACT_OK:
         raise ActError(rc, lib().act_last_error(None).decode())
-    return C_
+    return (C_, ms.value) if reps > 0 else C_
 
 
 def attention(q, k, v, dout, clips, T, Tk, H, nvalid=None, causal=False, zero_key=False, rope=None, device=0):

@@ -8,10 +8,10 @@ namespace act {
 
 namespace {
 
-constexpr int MAXV = 16;  // float4 per lane: D <= 2048
 
 // ---------------------------------------------------------------------------------------
 // LayerNorm, src/ac/lora.h:86-93: mean, centre, x / sqrt(mean(x^2) + eps), * w + b.
+template <int NV>
 __global__ void ln_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
                               const float* __restrict__ b, const float* __restrict__ add,
                               int rows_per_clip, bf16* __restrict__ y, float* __restrict__ mean,
@@ -19,7 +19,8 @@ __global__ void ln_fwd_kernel(const float* __restrict__ x, const float* __restri
     const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
-    const int nv = D / 128;
+    constexpr int MAXV = NV;
+    const int nv = NV;
     const float4* xr = reinterpret_cast<const float4*>(x + (long)row * D);
     float4 v[MAXV];
     float s = 0.f;
@@ -62,6 +63,7 @@ __global__ void ln_fwd_kernel(const float* __restrict__ x, const float* __restri
         }
 }
 
+template <int NV>
 __global__ void ln_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
                               const float* __restrict__ w, const float* __restrict__ mean,
                               const float* __restrict__ rstd, float* __restrict__ dx, int accumulate,
@@ -70,7 +72,8 @@ __global__ void ln_bwd_kernel(const float* __restrict__ dy, const float* __restr
     const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
-    const int nv = D / 128;
+    constexpr int MAXV = NV;
+    const int nv = NV;
     const float mu = mean[row], rs = rstd[row];
     float4 gv[MAXV], xh[MAXV];
     float s1 = 0.f, s2 = 0.f;
@@ -431,16 +434,36 @@ inline unsigned blocks_for(long n, int t) { return (unsigned)((n + t - 1) / t); 
 
 }  // namespace
 
+#define LN_DISPATCH(KERNEL, ...)                                                                  \
+    switch (D / 128) {                                                                            \
+        case 1: KERNEL<1><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
+        case 2: KERNEL<2><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
+        case 3: KERNEL<3><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
+        case 4: KERNEL<4><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
+        case 5: KERNEL<5><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
+        case 6: KERNEL<6><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
+        case 7: KERNEL<7><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
+        case 8: KERNEL<8><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
+        case 9: KERNEL<9><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
+        case 10: KERNEL<10><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
+        case 11: KERNEL<11><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
+        case 12: KERNEL<12><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
+        case 13: KERNEL<13><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
+        case 14: KERNEL<14><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
+        case 15: KERNEL<15><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
+        case 16: KERNEL<16><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
+        default: break; /* rejected at context creation: D must be 128..2048, a multiple of 128 */ \
+    }
+
 void layernorm_fwd(const float* x, const float* w, const float* b, const float* add, int rows_per_clip,
                    bf16* y, float* mean, float* rstd, int rows, int D, float eps, cudaStream_t s) {
-    ln_fwd_kernel<<<blocks_for(rows, 8), 256, 0, s>>>(x, w, b, add, rows_per_clip, y, mean, rstd, rows, D, eps);
+    LN_DISPATCH(ln_fwd_kernel, x, w, b, add, rows_per_clip, y, mean, rstd, rows, D, eps);
 }
 
 void layernorm_bwd(const float* dy, const float* x, const float* w, const float* mean, const float* rstd,
                    float* dx, int accumulate, const float* extra, bf16* dx_bf, const float* colscale,
                    int rows, int D, cudaStream_t s) {
-    ln_bwd_kernel<<<blocks_for(rows, 8), 256, 0, s>>>(dy, x, w, mean, rstd, dx, accumulate, extra, dx_bf,
-                                                      colscale, rows, D);
+    LN_DISPATCH(ln_bwd_kernel, dy, x, w, mean, rstd, dx, accumulate, extra, dx_bf, colscale, rows, D);
 }
 
 void residual_to_bf16(float* x, const float* extra, bf16* dst, const float* colscale, int rows, int D,

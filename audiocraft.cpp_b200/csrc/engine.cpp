@@ -1500,7 +1500,8 @@ int act_reset_kernel_stats(act_ctx* ctx) {
 
 double act_step_flops(act_ctx* ctx, int n) { return ctx && ctx->finalized ? ctx->step_flops(n) : -1.0; }
 
-int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path) {
+int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path,
+                  int reps, float* ms_per_call) {
     // Stand-alone check of the projection GEMM: C[M][N] (fp32) = A[M][K] . B(n,k), bf16 inputs,
     // B given as [N][K] (b_mn_major = 0) or [K][N] (1).  path 0 auto, 1 mma.sync, 2 tcgen05.
     void *dA = nullptr, *dB = nullptr, *dC = nullptr;
@@ -1529,9 +1530,36 @@ int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int 
         g.mode = EPI_STORE_F32; g.out = dC; g.ldo = N;
         const bool tc = path == 2 || (path == 0 && gemm_tc_supported(g));
         if (tc && !gemm_tc_supported(g)) throw Error(ACT_ERR_INVALID, "shape not supported by the tcgen05 path");
-        if (tc) gemm_tc(g, derr, st);
-        else gemm(g, st);
+        auto run = [&] {
+            if (tc) gemm_tc(g, derr, st);
+            else gemm(g, st);
+        };
+        run();
         CK(cudaGetLastError());
+        if (reps > 0 && ms_per_call) {
+            // time `reps` launches replayed from a CUDA graph: device time without host gaps
+            cudaGraph_t graph;
+            cudaGraphExec_t exec;
+            CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+            for (int i = 0; i < reps; ++i) run();
+            CK(cudaStreamEndCapture(st, &graph));
+            CK(cudaGraphInstantiate(&exec, graph, 0));
+            CK(cudaGraphLaunch(exec, st));
+            cudaEvent_t e0, e1;
+            CK(cudaEventCreate(&e0));
+            CK(cudaEventCreate(&e1));
+            CK(cudaEventRecord(e0, st));
+            CK(cudaGraphLaunch(exec, st));
+            CK(cudaEventRecord(e1, st));
+            CK(cudaEventSynchronize(e1));
+            float ms = 0;
+            CK(cudaEventElapsedTime(&ms, e0, e1));
+            *ms_per_call = ms / reps;
+            cudaEventDestroy(e0);
+            cudaEventDestroy(e1);
+            cudaGraphExecDestroy(exec);
+            cudaGraphDestroy(graph);
+        }
         CK(cudaMemcpyAsync(C, dC, (size_t)M * N * 4, cudaMemcpyDeviceToHost, st));
         int e = 0;
         CK(cudaMemcpyAsync(&e, derr, sizeof(int), cudaMemcpyDeviceToHost, st));

@@ -15,10 +15,7 @@ namespace act {
 
 namespace {
 
-constexpr int BK = 32;
-constexpr int STAGES = 4;
-
-template <int BM, int BN, bool AK, bool BKM>
+template <int BM, int BN, bool AK, bool BKM, int BK, int STAGES>
 struct Smem {
     // K-major tile: [rows][BK + 8]; MN-major tile: [BK][cols + 8]
     static constexpr int A_ELEMS = AK ? BM * (BK + 8) : BK * (BM + 8);
@@ -27,14 +24,14 @@ struct Smem {
     static constexpr int BYTES = STAGE * STAGES * 2;
 };
 
-template <int BM, int BN, int WM_, int WN_, bool AK, bool BKM>
+template <int BM, int BN, int WM_, int WN_, bool AK, bool BKM, int BK, int STAGES>
 __global__ void __launch_bounds__(WM_* WN_ * 32)
 gemm_mma_kernel(const GemmArgs p) {
     constexpr int NT = WM_ * WN_ * 32;
     constexpr int WTM = BM / WM_, WTN = BN / WN_;
     constexpr int MI = WTM / 16, NI = WTN / 8;
     static_assert(NI % 2 == 0, "warp tile N must be a multiple of 16");
-    using S = Smem<BM, BN, AK, BKM>;
+    using S = Smem<BM, BN, AK, BKM, BK, STAGES>;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     bf16* smem = reinterpret_cast<bf16*>(smem_raw);
 
@@ -228,10 +225,10 @@ gemm_mma_kernel(const GemmArgs p) {
             }
 }
 
-template <int BM, int BN, int WM_, int WN_, bool AK, bool BKM>
+template <int BM, int BN, int WM_, int WN_, bool AK, bool BKM, int BK = 32, int STAGES = 4>
 void launch(const GemmArgs& a, cudaStream_t s) {
-    using S = Smem<BM, BN, AK, BKM>;
-    auto kern = gemm_mma_kernel<BM, BN, WM_, WN_, AK, BKM>;
+    using S = Smem<BM, BN, AK, BKM, BK, STAGES>;
+    auto kern = gemm_mma_kernel<BM, BN, WM_, WN_, AK, BKM, BK, STAGES>;
     static bool configured = false;  // per instantiation; set before first launch / capture
     if (!configured) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
@@ -243,8 +240,8 @@ void launch(const GemmArgs& a, cudaStream_t s) {
 
 template <bool AK, bool BKM>
 void dispatch(const GemmArgs& a, cudaStream_t s) {
-    if (a.N <= 32)
-        launch<128, 32, 4, 1, AK, BKM>(a, s);
+    if (a.N <= 32)  // rank-block shapes: many short row blocks, deep pipeline (HBM-bound)
+        launch<64, 32, 4, 1, AK, BKM, 64, 6>(a, s);
     else if (a.N <= 64)
         launch<128, 64, 4, 1, AK, BKM>(a, s);
     else if (a.M <= 64)

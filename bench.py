@@ -192,6 +192,50 @@ def run_reference(args, c):
 
 # ------------------------------------------------------------------------------------------
 
+def run_sweep(kind, reps):
+    """Kernel-level sweep (BASELINE cfg 5): one JSON line per shape, device time per call."""
+    import actrain as A
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    peak = peaks.get("bf16_tflops", 1590.0)
+    rng = np.random.default_rng(0)
+    bits = lambda shape: (rng.integers(0x3C00, 0x3F80, size=shape, dtype=np.uint16) ^
+                          (rng.integers(0, 2, size=shape, dtype=np.uint16) << 15))
+    if kind == "gemm":
+        for M in (6000, 2048, 32768):
+            for (N, K) in ((1024, 1024), (3072, 1024), (4096, 1024), (1024, 4096), (1536, 1536), (6144, 1536),
+                           (1536, 6144)):
+                for b_mn in (False, True):
+                    for path in (2, 1):
+                        if M * max(N, K) > 32768 * 6144 // 2 and path == 1:
+                            continue
+                        a, b = bits((M, K)), bits((K, N) if b_mn else (N, K))
+                        _, ms = A.gemm_bf16(a, b, M, N, K, b_mn, path, reps=reps)
+                        tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+                        print(json.dumps({"sweep": "gemm", "M": M, "N": N, "K": K,
+                                          "layout": "NN (dX = dY W)" if b_mn else "NT (Y = X W^T)",
+                                          "kernel": "tcgen05" if path == 2 else "mma.sync", "ms": ms,
+                                          "tflops": tf, "frac_of_peak": tf / peak}), flush=True)
+    else:
+        for H in (16, 24):
+            for T in (750, 1500, 3000):
+                for causal in (False, True):
+                    clips = max(1, 6000 // T)
+                    D = H * 64
+                    q, k, v, do = (bits((clips * T, D)) for _ in range(4))
+                    A.attention(q, k, v, do, clips, T, T, H, None, causal, not causal, None)  # warm
+                    out = A.attention(q, k, v, do, clips, T, T, H, None, causal, not causal, None)
+                    keys = T * (T + 1) / 2 if causal else T * (T + 1)
+                    f_fwd, f_bwd = 4.0 * clips * keys * D, 8.0 * clips * keys * D
+                    print(json.dumps({"sweep": "attention", "heads": H, "seq": T, "clips": clips, "causal": causal,
+                                      "zero_key": not causal, "ms_fwd": out["ms_fwd"], "ms_bwd": out["ms_bwd"],
+                                      "tflops_fwd": f_fwd / (out["ms_fwd"] / 1e3) / 1e12,
+                                      "tflops_bwd": f_bwd / (out["ms_bwd"] / 1e3) / 1e12}), flush=True)
+
+
 def build_context(A, c, workload, device, seed=0):
     rng = np.random.default_rng(seed)
     if workload == "mf":
@@ -224,7 +268,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override depth (profiling captures only)")
     ap.add_argument("--batch", type=int, default=0, help="override clips per rank (profiling captures only)")
+    ap.add_argument("--sweep", choices=["gemm", "attention"], help="kernel-level sweep instead of the step")
     args = ap.parse_args()
+    if args.sweep:
+        return run_sweep(args.sweep, max(args.steps, 3))
     c = dict(MF if args.workload == "mf" else MG)
     if args.layers:
         c["layers"] = args.layers

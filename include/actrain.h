@@ -167,8 +167,10 @@ int act_reset_kernel_stats(act_ctx* ctx);
 double act_step_flops(act_ctx* ctx, int n);
 /* stand-alone projection GEMM on host buffers (tests and the kernel sweep): C[M][N] fp32 =
  * A[M][K] . B(n,k) with bf16 A and B, B as [N][K] (b_mn_major 0) or [K][N] (1);
- * path 0 = automatic, 1 = mma.sync kernel, 2 = tcgen05 kernel */
-int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path);
+ * path 0 = automatic, 1 = mma.sync kernel, 2 = tcgen05 kernel; when reps > 0 the GEMM is
+ * re-run reps times back to back and *ms_per_call receives the mean device time */
+int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path,
+                  int reps, float* ms_per_call);
 /* stand-alone attention forward + backward on host buffers (tests and the kernel sweep):
  * token-major bf16 q [clips*T][H*64], k/v [clips*Tk][H*64], dout like q; scale 1/8 (head_dim 64);
  * nvalid: per-clip valid key count or NULL; causal; zero_key = the prepended zero key of
