@@ -7,10 +7,15 @@
 //     (score 0, value 0), so it only enters through the log-sum-exp;
 //   * masks are per-clip valid-key counts (the reference's -inf columns beyond
 //     valid_tokens, src/mf/train.h:169-175) and an optional causal mask (src/mg/train.h:209-213);
-//   * RoPE with stored frequencies (src/ac/transformer.h:55-61) is applied while Q and K
-//     tiles are staged into shared memory, and undone in the dQ/dK epilogues.
-// Backward follows the standard recompute scheme: P from the saved LSE, D = rowsum(dO*O),
-// dS = P (dP - D); dK and dV are owned by key blocks, dQ accumulates through fp32 atomics.
+//   * RoPE with stored frequencies (src/ac/transformer.h:55-61): the training step rotates q
+//     and k in the projection epilogue, so these kernels read rotated inputs and only undo the
+//     rotation on dQ / dK; with rope_load set (stand-alone entry points) they rotate while
+//     staging tiles instead.
+// Forward: 128 queries per CTA (8 warps x 16 rows), K/V tiles of 64 keys double-buffered with
+// cp.async, online softmax in base 2.  Backward (recompute): one CTA per 64-key block, warps
+// own 16 keys each, so P^T and dS^T stay in registers for dV += P^T dO and dK += dS^T Q; dS^T
+// goes through shared memory once for dQ = dS K, accumulated with fp32 atomics.  Q / dO / LSE / D
+// tiles of the next query block are prefetched while the current one is processed.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -21,15 +26,13 @@ namespace act {
 namespace {
 
 constexpr int HD = 64;
-constexpr int BQ = 64;
 constexpr int BKV = 64;
 constexpr int LDS = HD + 8;
 constexpr float LOG2E = 1.4426950408889634f;
 
-// Stage a [64 rows][64] bf16 tile into smem, rotating pairs when rope != nullptr.
-// Rows >= nrows are zero-filled.  pos0 is the clip position of row 0.
-__device__ __forceinline__ void stage_tile(bf16* sm, const bf16* g, long ld, int nrows, int pos0,
-                                           const float* rope, int tid, int nthreads) {
+// Synchronous staging of a [64 rows][64] bf16 tile, rotating pairs when rope != nullptr.
+__device__ __forceinline__ void stage_tile_sync(bf16* sm, const bf16* g, long ld, int nrows, int pos0,
+                                                const float* rope, int tid, int nthreads) {
     for (int c = tid; c < 64 * 8; c += nthreads) {
         const int r = c >> 3, ch = c & 7;
         uint4 v = make_uint4(0, 0, 0, 0);
@@ -51,26 +54,59 @@ __device__ __forceinline__ void stage_tile(bf16* sm, const bf16* g, long ld, int
     }
 }
 
-__global__ void __launch_bounds__(128) attn_fwd_kernel(const AttnArgs a) {
-    __shared__ __align__(16) bf16 sQ[BQ * LDS];
-    __shared__ __align__(16) bf16 sK[BKV * LDS];
-    __shared__ __align__(16) bf16 sV[BKV * LDS];
+// Asynchronous staging of a [64 rows][64] bf16 tile (rows >= nrows zero-filled).
+__device__ __forceinline__ void stage_tile_async(bf16* sm, const bf16* g, long ld, int nrows, int tid, int nthreads) {
+    for (int c = tid; c < 64 * 8; c += nthreads) {
+        const int r = c >> 3, ch = c & 7;
+        const bool ok = r < nrows;
+        cp_async16(sm + r * LDS + ch * 8, ok ? g + (long)r * ld + ch * 8 : g, ok);
+    }
+}
+
+template <bool ROPE_LOAD>
+__device__ __forceinline__ void stage_tile(bf16* sm, const bf16* g, long ld, int nrows, int pos0, const float* rope,
+                                           int tid, int nthreads) {
+    if (ROPE_LOAD) stage_tile_sync(sm, g, ld, nrows, pos0, rope, tid, nthreads);
+    else stage_tile_async(sm, g, ld, nrows, tid, nthreads);
+}
+
+// ---------------------------------------------------------------------------------------
+// forward
+
+constexpr int FWD_WARPS = 8;
+constexpr int FWD_BQ = FWD_WARPS * 16;
+constexpr int FWD_SMEM = (FWD_BQ + 4 * BKV) * LDS * 2;
+
+template <bool ROPE_LOAD>
+__global__ void __launch_bounds__(FWD_WARPS * 32) attn_fwd_kernel(const AttnArgs a) {
+    extern __shared__ __align__(16) unsigned char smraw[];
+    bf16* sQ = reinterpret_cast<bf16*>(smraw);
+    bf16* sK = sQ + FWD_BQ * LDS;  // [2][64][LDS]
+    bf16* sV = sK + 2 * BKV * LDS;  // [2][64][LDS]
+    constexpr int NT = FWD_WARPS * 32;
     const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, q = lane & 3, lr = lane & 7, lsel = lane >> 3;
-    const int q0 = qb * BQ;
-    const int nq = min(BQ, a.T - q0);
+    const int q0 = qb * FWD_BQ;
+    const int nq = min(FWD_BQ, a.T - q0);
     int kv_end = a.Tk;
     if (a.nvalid) kv_end = min(kv_end, a.nvalid[b]);
-    if (a.causal) kv_end = min(kv_end, q0 + BQ);
+    if (a.causal) kv_end = min(kv_end, q0 + FWD_BQ);
+    const float* rope_load = ROPE_LOAD ? a.rope : nullptr;
 
-    stage_tile(sQ, a.q + ((long)b * a.T + q0) * a.ldq + h * HD, a.ldq, nq, q0, a.rope, tid, 128);
-    __syncthreads();
-    uint32_t qf[4][4];
-#pragma unroll
-    for (int kc = 0; kc < 4; ++kc)
-        ldsm_x4(qf[kc][0], qf[kc][1], qf[kc][2], qf[kc][3],
-                sQ + (warp * 16 + lr + 8 * (lsel & 1)) * LDS + kc * 16 + 8 * (lsel >> 1));
+    const bf16* qg = a.q + ((long)b * a.T + q0) * a.ldq + h * HD;
+    stage_tile<ROPE_LOAD>(sQ, qg, a.ldq, nq, q0, rope_load, tid, NT);
+    stage_tile<ROPE_LOAD>(sQ + 64 * LDS, qg + 64 * a.ldq, a.ldq, nq - 64, q0 + 64, rope_load, tid, NT);
+    const int nkb = (kv_end + BKV - 1) / BKV;
+    auto load_kv = [&](int kb, int buf) {
+        const int k0 = kb * BKV;
+        const int nk = min(BKV, kv_end - k0);
+        stage_tile<ROPE_LOAD>(sK + buf * BKV * LDS, a.k + ((long)b * a.Tk + k0) * a.ldk + h * HD, a.ldk, nk, k0,
+                              rope_load, tid, NT);
+        stage_tile_async(sV + buf * BKV * LDS, a.v + ((long)b * a.Tk + k0) * a.ldv + h * HD, a.ldv, nk, tid, NT);
+    };
+    if (nkb > 0) load_kv(0, 0);
+    cp_async_commit();
 
     const float sl2 = a.scale * LOG2E;
     float mrow[2], lrow[2];
@@ -81,16 +117,23 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const AttnArgs a) {
     for (int i = 0; i < 8; ++i)
 #pragma unroll
         for (int e = 0; e < 4; ++e) o[i][e] = 0.f;
+    uint32_t qf[4][4];
 
-    const int nkb = (kv_end + BKV - 1) / BKV;
     for (int kb = 0; kb < nkb; ++kb) {
+        const int buf = kb & 1;
+        if (kb + 1 < nkb) load_kv(kb + 1, buf ^ 1);
+        cp_async_commit();
+        cp_async_wait<1>();
+        __syncthreads();
+        if (kb == 0) {
+#pragma unroll
+            for (int kc = 0; kc < 4; ++kc)
+                ldsm_x4(qf[kc][0], qf[kc][1], qf[kc][2], qf[kc][3],
+                        sQ + (warp * 16 + lr + 8 * (lsel & 1)) * LDS + kc * 16 + 8 * (lsel >> 1));
+        }
+        const bf16* cK = sK + buf * BKV * LDS;
+        const bf16* cV = sV + buf * BKV * LDS;
         const int k0 = kb * BKV;
-        __syncthreads();
-        stage_tile(sK, a.k + ((long)b * a.Tk + k0) * a.ldk + h * HD, a.ldk, min(BKV, kv_end - k0), k0,
-                   a.rope, tid, 128);
-        stage_tile(sV, a.v + ((long)b * a.Tk + k0) * a.ldv + h * HD, a.ldv, min(BKV, kv_end - k0), k0,
-                   nullptr, tid, 128);
-        __syncthreads();
         float s[8][4];
 #pragma unroll
         for (int i = 0; i < 8; ++i)
@@ -101,18 +144,22 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const AttnArgs a) {
 #pragma unroll
             for (int nj = 0; nj < 4; ++nj) {
                 uint32_t b0, b1, b2, b3;
-                ldsm_x4(b0, b1, b2, b3, sK + (nj * 16 + lr + 8 * (lsel >> 1)) * LDS + kc * 16 + 8 * (lsel & 1));
+                ldsm_x4(b0, b1, b2, b3, cK + (nj * 16 + lr + 8 * (lsel >> 1)) * LDS + kc * 16 + 8 * (lsel & 1));
                 mma_bf16(s[2 * nj], qf[kc], b0, b1);
                 mma_bf16(s[2 * nj + 1], qf[kc], b2, b3);
             }
         float mx[2] = {-INFINITY, -INFINITY};
+        const bool full = (k0 + BKV <= kv_end) && (!a.causal || k0 + BKV - 1 <= q0 + warp * 16);
 #pragma unroll
         for (int ni = 0; ni < 8; ++ni)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const int j = k0 + ni * 8 + 2 * q + (e & 1);
-                const int i = q0 + warp * 16 + g + 8 * (e >> 1);
-                const bool ok = j < kv_end && (!a.causal || j <= i);
+                bool ok = true;
+                if (!full) {
+                    const int j = k0 + ni * 8 + 2 * q + (e & 1);
+                    const int i = q0 + warp * 16 + g + 8 * (e >> 1);
+                    ok = j < kv_end && (!a.causal || j <= i);
+                }
                 s[ni][e] = ok ? s[ni][e] * sl2 : -INFINITY;
                 mx[e >> 1] = fmaxf(mx[e >> 1], s[ni][e]);
             }
@@ -157,13 +204,17 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const AttnArgs a) {
 #pragma unroll
             for (int nj = 0; nj < 4; ++nj) {
                 uint32_t b0, b1, b2, b3;
-                ldsm_x4_t(b0, b1, b2, b3, sV + (kc * 16 + lr + 8 * (lsel & 1)) * LDS + nj * 16 + 8 * (lsel >> 1));
+                ldsm_x4_t(b0, b1, b2, b3, cV + (kc * 16 + lr + 8 * (lsel & 1)) * LDS + nj * 16 + 8 * (lsel >> 1));
                 mma_bf16(o[2 * nj], pa, b0, b1);
                 mma_bf16(o[2 * nj + 1], pa, b2, b3);
             }
         }
+        __syncthreads();  // this buffer is refilled by the prefetch of iteration kb + 2
     }
-    // epilogue
+    if (nkb == 0) {  // no key in range: only the zero key (if any) contributes
+        cp_async_wait<0>();
+        __syncthreads();
+    }
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
         const int i = q0 + warp * 16 + g + 8 * hh;
@@ -181,34 +232,52 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const AttnArgs a) {
     }
 }
 
-// D[b][h][i] = sum_d dO * O   (one warp per (row, head))
+// ---------------------------------------------------------------------------------------
+// D[b][h][i] = sum_d dO * O : 8 threads per (row, head), one 16-byte load each.
 __global__ void attn_dvec_kernel(const AttnArgs a) {
-    const long w = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-    const int lane = threadIdx.x & 31;
+    const long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
     const long rows = (long)a.clips * a.T;
-    if (w >= rows * a.H) return;
-    const long row = w / a.H;
-    const int h = (int)(w % a.H);
-    const bf16* o = a.o + row * a.ldo + h * HD + 2 * lane;
-    const bf16* d = a.dout + row * a.lddo + h * HD + 2 * lane;
-    const __nv_bfloat162 o2 = *reinterpret_cast<const __nv_bfloat162*>(o);
-    const __nv_bfloat162 d2 = *reinterpret_cast<const __nv_bfloat162*>(d);
-    float v = __low2float(o2) * __low2float(d2) + __high2float(o2) * __high2float(d2);
-    v = warp_sum(v);
-    if (lane == 0) {
+    const long per_row = (long)a.H * 8;
+    const bool valid = t < rows * per_row;
+    const long row = valid ? t / per_row : 0;
+    const int rem = (int)(t % per_row), h = rem >> 3, part = rem & 7;
+    float v = 0.f;
+    if (valid) {
+        const uint4 oo = *reinterpret_cast<const uint4*>(a.o + row * a.ldo + h * HD + part * 8);
+        const uint4 dd = *reinterpret_cast<const uint4*>(a.dout + row * a.lddo + h * HD + part * 8);
+        const uint32_t ow[4] = {oo.x, oo.y, oo.z, oo.w}, dw[4] = {dd.x, dd.y, dd.z, dd.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const __nv_bfloat162 o2 = *reinterpret_cast<const __nv_bfloat162*>(&ow[j]);
+            const __nv_bfloat162 d2 = *reinterpret_cast<const __nv_bfloat162*>(&dw[j]);
+            v += __low2float(o2) * __low2float(d2) + __high2float(o2) * __high2float(d2);
+        }
+    }
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    if (valid && part == 0) {
         const int b = (int)(row / a.T), i = (int)(row % a.T);
         a.dvec[((long)b * a.H + h) * a.T + i] = v;
     }
 }
 
+// ---------------------------------------------------------------------------------------
+// backward
+
+constexpr int BWD_BQ = 64;
+constexpr int BWD_SMEM = (2 * BKV + 4 * BWD_BQ + BKV) * LDS * 2 + 4 * BWD_BQ * 4;
+
+template <bool ROPE_LOAD>
 __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
     extern __shared__ __align__(16) unsigned char smraw[];
     bf16* sK = reinterpret_cast<bf16*>(smraw);
     bf16* sV = sK + BKV * LDS;
-    bf16* sQ = sV + BKV * LDS;
-    bf16* sdO = sQ + BQ * LDS;
-    bf16* sP = sdO + BQ * LDS;
-    bf16* sdS = sP + BQ * LDS;
+    bf16* sQ = sV + BKV * LDS;          // [2][64][LDS]
+    bf16* sdO = sQ + 2 * BWD_BQ * LDS;  // [2][64][LDS]
+    bf16* sdS = sdO + 2 * BWD_BQ * LDS; // [64 keys][LDS]  dS^T
+    float* sL = reinterpret_cast<float*>(sdS + BKV * LDS);  // [2][64] lse
+    float* sD = sL + 2 * BWD_BQ;                             // [2][64] rowsum(dO*O)
     const int kb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, q = lane & 3, lr = lane & 7, lsel = lane >> 3;
@@ -216,9 +285,33 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
     int kv_end = a.Tk;
     if (a.nvalid) kv_end = min(kv_end, a.nvalid[b]);
     const int nk = max(0, min(BKV, kv_end - k0));
+    const float* rope_load = ROPE_LOAD ? a.rope : nullptr;
 
-    stage_tile(sK, a.k + ((long)b * a.Tk + k0) * a.ldk + h * HD, a.ldk, nk, k0, a.rope, tid, 128);
-    stage_tile(sV, a.v + ((long)b * a.Tk + k0) * a.ldv + h * HD, a.ldv, nk, k0, nullptr, tid, 128);
+    stage_tile<ROPE_LOAD>(sK, a.k + ((long)b * a.Tk + k0) * a.ldk + h * HD, a.ldk, nk, k0, rope_load, tid, 128);
+    stage_tile_async(sV, a.v + ((long)b * a.Tk + k0) * a.ldv + h * HD, a.ldv, nk, tid, 128);
+
+    const int qb0 = a.causal ? k0 / BWD_BQ : 0;
+    const int nqb = (a.T + BWD_BQ - 1) / BWD_BQ;
+    const int qb_first = nk > 0 ? qb0 : nqb;
+    auto load_q = [&](int qb, int buf) {
+        const int q0 = qb * BWD_BQ;
+        const int nq = min(BWD_BQ, a.T - q0);
+        stage_tile<ROPE_LOAD>(sQ + buf * BWD_BQ * LDS, a.q + ((long)b * a.T + q0) * a.ldq + h * HD, a.ldq, nq, q0,
+                              rope_load, tid, 128);
+        stage_tile_async(sdO + buf * BWD_BQ * LDS, a.dout + ((long)b * a.T + q0) * a.lddo + h * HD, a.lddo, nq, tid, 128);
+        if (tid < 32) {  // 16 x 16 bytes of lse, 16 x 16 bytes of D
+            const int c = tid & 15;
+            const bool ok = c * 4 < nq;
+            const float* src = (tid < 16 ? a.lse : a.dvec) + ((long)b * a.H + h) * a.T + q0 + c * 4;
+            float* dst = (tid < 16 ? sL : sD) + buf * BWD_BQ + c * 4;
+            const bool full = ok && (q0 + c * 4 + 4 <= a.T) && ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
+            if (full) cp_async16(dst, src, true);
+            else
+                for (int j = 0; j < 4; ++j) dst[j] = (q0 + c * 4 + j < a.T) ? src[j] : 0.f;
+        }
+    };
+    if (qb_first < nqb) load_q(qb_first, 0);
+    cp_async_commit();
 
     const float sl2 = a.scale * LOG2E;
     float dk[8][4], dv[8][4];
@@ -227,16 +320,18 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) dk[i][e] = dv[i][e] = 0.f;
 
-    const int qb0 = a.causal ? k0 / BQ : 0;
-    const int nqb = (a.T + BQ - 1) / BQ;
-    for (int qb = (nk > 0 ? qb0 : nqb); qb < nqb; ++qb) {
-        const int q0 = qb * BQ;
-        const int nq = min(BQ, a.T - q0);
+    for (int qb = qb_first, it = 0; qb < nqb; ++qb, ++it) {
+        const int buf = it & 1;
+        if (qb + 1 < nqb) load_q(qb + 1, buf ^ 1);
+        cp_async_commit();
+        cp_async_wait<1>();
         __syncthreads();
-        stage_tile(sQ, a.q + ((long)b * a.T + q0) * a.ldq + h * HD, a.ldq, nq, q0, a.rope, tid, 128);
-        stage_tile(sdO, a.dout + ((long)b * a.T + q0) * a.lddo + h * HD, a.lddo, nq, q0, nullptr, tid, 128);
-        __syncthreads();
-        // S = Q K^T and dP = dO V^T for this warp's 16 query rows
+        const int q0 = qb * BWD_BQ;
+        const bf16* cQ = sQ + buf * BWD_BQ * LDS;
+        const bf16* cdO = sdO + buf * BWD_BQ * LDS;
+        const float* cL = sL + buf * BWD_BQ;
+        const float* cD = sD + buf * BWD_BQ;
+        // S^T = K Q^T and dP^T = V dO^T for this warp's 16 keys x 64 queries
         float s[8][4], dp[8][4];
 #pragma unroll
         for (int i = 0; i < 8; ++i)
@@ -244,49 +339,68 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
             for (int e = 0; e < 4; ++e) s[i][e] = dp[i][e] = 0.f;
 #pragma unroll
         for (int kc = 0; kc < 4; ++kc) {
-            uint32_t qa[4], da[4];
-            ldsm_x4(qa[0], qa[1], qa[2], qa[3], sQ + (warp * 16 + lr + 8 * (lsel & 1)) * LDS + kc * 16 + 8 * (lsel >> 1));
-            ldsm_x4(da[0], da[1], da[2], da[3], sdO + (warp * 16 + lr + 8 * (lsel & 1)) * LDS + kc * 16 + 8 * (lsel >> 1));
+            uint32_t ka[4], va[4];
+            ldsm_x4(ka[0], ka[1], ka[2], ka[3], sK + (warp * 16 + lr + 8 * (lsel & 1)) * LDS + kc * 16 + 8 * (lsel >> 1));
+            ldsm_x4(va[0], va[1], va[2], va[3], sV + (warp * 16 + lr + 8 * (lsel & 1)) * LDS + kc * 16 + 8 * (lsel >> 1));
 #pragma unroll
             for (int nj = 0; nj < 4; ++nj) {
                 uint32_t b0, b1, b2, b3;
-                ldsm_x4(b0, b1, b2, b3, sK + (nj * 16 + lr + 8 * (lsel >> 1)) * LDS + kc * 16 + 8 * (lsel & 1));
-                mma_bf16(s[2 * nj], qa, b0, b1);
-                mma_bf16(s[2 * nj + 1], qa, b2, b3);
-                ldsm_x4(b0, b1, b2, b3, sV + (nj * 16 + lr + 8 * (lsel >> 1)) * LDS + kc * 16 + 8 * (lsel & 1));
-                mma_bf16(dp[2 * nj], da, b0, b1);
-                mma_bf16(dp[2 * nj + 1], da, b2, b3);
+                ldsm_x4(b0, b1, b2, b3, cQ + (nj * 16 + lr + 8 * (lsel >> 1)) * LDS + kc * 16 + 8 * (lsel & 1));
+                mma_bf16(s[2 * nj], ka, b0, b1);
+                mma_bf16(s[2 * nj + 1], ka, b2, b3);
+                ldsm_x4(b0, b1, b2, b3, cdO + (nj * 16 + lr + 8 * (lsel >> 1)) * LDS + kc * 16 + 8 * (lsel & 1));
+                mma_bf16(dp[2 * nj], va, b0, b1);
+                mma_bf16(dp[2 * nj + 1], va, b2, b3);
             }
         }
-        float lse[2], dd[2];
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-            const int i = q0 + warp * 16 + g + 8 * hh;
-            const bool rv = i < a.T;
-            lse[hh] = rv ? a.lse[((long)b * a.H + h) * a.T + i] : 0.f;
-            dd[hh] = rv ? a.dvec[((long)b * a.H + h) * a.T + i] : 0.f;
-        }
+        const bool full = (q0 + BWD_BQ <= a.T) && (k0 + BKV <= kv_end) && (!a.causal || k0 + BKV - 1 <= q0);
 #pragma unroll
         for (int ni = 0; ni < 8; ++ni)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const int j = k0 + ni * 8 + 2 * q + (e & 1);
-                const int i = q0 + warp * 16 + g + 8 * (e >> 1);
-                const bool ok = i < a.T && j < kv_end && (!a.causal || j <= i);
-                const float p = ok ? exp2f(s[ni][e] * sl2 - lse[e >> 1]) : 0.f;
+                const int il = ni * 8 + 2 * q + (e & 1);  // query within the block (column)
+                bool ok = true;
+                if (!full) {
+                    const int i = q0 + il;
+                    const int j = k0 + warp * 16 + g + 8 * (e >> 1);
+                    ok = i < a.T && j < kv_end && (!a.causal || j <= i);
+                }
+                const float p = ok ? exp2f(s[ni][e] * sl2 - cL[il]) : 0.f;
                 s[ni][e] = p;
-                dp[ni][e] = p * (dp[ni][e] - dd[e >> 1]);
+                dp[ni][e] = p * (dp[ni][e] - cD[il]);
             }
-        // P and dS to smem (rows of this warp), as bf16
+        // dV += P^T dO ; dK += dS^T Q  (A operands straight from the accumulators)
 #pragma unroll
-        for (int ni = 0; ni < 8; ++ni)
+        for (int kc = 0; kc < 4; ++kc) {
+            uint32_t pa[4], sa[4];
+            pa[0] = pack_bf16(s[2 * kc][0], s[2 * kc][1]);
+            pa[1] = pack_bf16(s[2 * kc][2], s[2 * kc][3]);
+            pa[2] = pack_bf16(s[2 * kc + 1][0], s[2 * kc + 1][1]);
+            pa[3] = pack_bf16(s[2 * kc + 1][2], s[2 * kc + 1][3]);
+            sa[0] = pack_bf16(dp[2 * kc][0], dp[2 * kc][1]);
+            sa[1] = pack_bf16(dp[2 * kc][2], dp[2 * kc][3]);
+            sa[2] = pack_bf16(dp[2 * kc + 1][0], dp[2 * kc + 1][1]);
+            sa[3] = pack_bf16(dp[2 * kc + 1][2], dp[2 * kc + 1][3]);
+#pragma unroll
+            for (int nj = 0; nj < 4; ++nj) {
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(b0, b1, b2, b3, cdO + (kc * 16 + lr + 8 * (lsel & 1)) * LDS + nj * 16 + 8 * (lsel >> 1));
+                mma_bf16(dv[2 * nj], pa, b0, b1);
+                mma_bf16(dv[2 * nj + 1], pa, b2, b3);
+                ldsm_x4_t(b0, b1, b2, b3, cQ + (kc * 16 + lr + 8 * (lsel & 1)) * LDS + nj * 16 + 8 * (lsel >> 1));
+                mma_bf16(dk[2 * nj], sa, b0, b1);
+                mma_bf16(dk[2 * nj + 1], sa, b2, b3);
+            }
+            // dS^T rows of this warp to shared memory for dQ
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-                const int r = warp * 16 + g + 8 * hh, c = ni * 8 + 2 * q;
-                *reinterpret_cast<uint32_t*>(sP + r * LDS + c) = pack_bf16(s[ni][2 * hh], s[ni][2 * hh + 1]);
-                *reinterpret_cast<uint32_t*>(sdS + r * LDS + c) = pack_bf16(dp[ni][2 * hh], dp[ni][2 * hh + 1]);
+                const int r = warp * 16 + g + 8 * hh;
+                *reinterpret_cast<uint32_t*>(sdS + r * LDS + kc * 16 + 2 * q) = sa[hh];
+                *reinterpret_cast<uint32_t*>(sdS + r * LDS + kc * 16 + 8 + 2 * q) = sa[2 + hh];
             }
-        // dQ(16 rows) = dS(16 x 64 keys) K(64 keys x 64 d)
+        }
+        __syncthreads();
+        // dQ (16 queries of this warp x 64 d) = dS K, summed over this CTA's 64 keys
         {
             float dq[8][4];
 #pragma unroll
@@ -295,17 +409,14 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
                 for (int e = 0; e < 4; ++e) dq[i][e] = 0.f;
 #pragma unroll
             for (int kc = 0; kc < 4; ++kc) {
-                uint32_t pa[4];
-                pa[0] = pack_bf16(dp[2 * kc][0], dp[2 * kc][1]);
-                pa[1] = pack_bf16(dp[2 * kc][2], dp[2 * kc][3]);
-                pa[2] = pack_bf16(dp[2 * kc + 1][0], dp[2 * kc + 1][1]);
-                pa[3] = pack_bf16(dp[2 * kc + 1][2], dp[2 * kc + 1][3]);
+                uint32_t da[4];
+                ldsm_x4_t(da[0], da[1], da[2], da[3], sdS + (kc * 16 + lr + 8 * (lsel >> 1)) * LDS + warp * 16 + 8 * (lsel & 1));
 #pragma unroll
                 for (int nj = 0; nj < 4; ++nj) {
                     uint32_t b0, b1, b2, b3;
                     ldsm_x4_t(b0, b1, b2, b3, sK + (kc * 16 + lr + 8 * (lsel & 1)) * LDS + nj * 16 + 8 * (lsel >> 1));
-                    mma_bf16(dq[2 * nj], pa, b0, b1);
-                    mma_bf16(dq[2 * nj + 1], pa, b2, b3);
+                    mma_bf16(dq[2 * nj], da, b0, b1);
+                    mma_bf16(dq[2 * nj + 1], da, b2, b3);
                 }
             }
 #pragma unroll
@@ -314,31 +425,14 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
                 if (i >= a.T) continue;
                 float* dst = a.dq_acc + ((long)b * a.T + i) * a.ldq_acc + h * HD;
 #pragma unroll
-                for (int ni = 0; ni < 8; ++ni) {
-                    atomicAdd(dst + ni * 8 + 2 * q, dq[ni][2 * hh] * a.scale);
-                    atomicAdd(dst + ni * 8 + 2 * q + 1, dq[ni][2 * hh + 1] * a.scale);
-                }
+                for (int ni = 0; ni < 8; ++ni)
+                    atomicAdd(reinterpret_cast<float2*>(dst + ni * 8 + 2 * q),
+                              make_float2(dq[ni][2 * hh] * a.scale, dq[ni][2 * hh + 1] * a.scale));
             }
         }
-        __syncthreads();
-        // dV(16 keys of this warp) += P^T dO ; dK += dS^T Q
-#pragma unroll
-        for (int kc = 0; kc < 4; ++kc) {  // over query chunks of 16
-            uint32_t pa[4], sa[4];
-            ldsm_x4_t(pa[0], pa[1], pa[2], pa[3], sP + (kc * 16 + lr + 8 * (lsel >> 1)) * LDS + warp * 16 + 8 * (lsel & 1));
-            ldsm_x4_t(sa[0], sa[1], sa[2], sa[3], sdS + (kc * 16 + lr + 8 * (lsel >> 1)) * LDS + warp * 16 + 8 * (lsel & 1));
-#pragma unroll
-            for (int nj = 0; nj < 4; ++nj) {
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4_t(b0, b1, b2, b3, sdO + (kc * 16 + lr + 8 * (lsel & 1)) * LDS + nj * 16 + 8 * (lsel >> 1));
-                mma_bf16(dv[2 * nj], pa, b0, b1);
-                mma_bf16(dv[2 * nj + 1], pa, b2, b3);
-                ldsm_x4_t(b0, b1, b2, b3, sQ + (kc * 16 + lr + 8 * (lsel & 1)) * LDS + nj * 16 + 8 * (lsel >> 1));
-                mma_bf16(dk[2 * nj], sa, b0, b1);
-                mma_bf16(dk[2 * nj + 1], sa, b2, b3);
-            }
-        }
+        __syncthreads();  // sdS and this Q/dO buffer are rewritten next
     }
+    cp_async_wait<0>();
     // epilogue: dK (unrotate), dV, DoRA column factors
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
@@ -372,51 +466,67 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
     }
 }
 
+// dq (bf16) = unrotate(dq_acc) * qscale : 4 floats per thread
 __global__ void attn_dq_finish_kernel(const AttnArgs a, bf16* dq, long lddq, const float* qscale) {
-    const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;  // one pair per thread
+    const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
     const long rows = (long)a.clips * a.T;
-    const int pairs = a.H * HD / 2;
-    if (idx >= rows * pairs) return;
-    const long row = idx / pairs;
-    const int pc = (int)(idx % pairs), c = pc * 2;
-    const float* src = a.dq_acc + row * a.ldq_acc + c;
-    float x0 = src[0], x1 = src[1];
+    const int quads = a.H * HD / 4;
+    if (idx >= rows * quads) return;
+    const long row = idx / quads;
+    const int c = (int)(idx % quads) * 4;
+    const float4 v = *reinterpret_cast<const float4*>(a.dq_acc + row * a.ldq_acc + c);
+    float x[4] = {v.x, v.y, v.z, v.w};
     if (a.rope) {
         const int pos = (int)(row % a.T);
-        const float2 t = reinterpret_cast<const float2*>(a.rope)[(long)pos * 32 + (c % HD) / 2];
-        const float y0 = x0 * t.x + x1 * t.y, y1 = -x0 * t.y + x1 * t.x;
-        x0 = y0;
-        x1 = y1;
+        const float2* t = reinterpret_cast<const float2*>(a.rope) + (long)pos * 32 + (c % HD) / 2;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const float x0 = x[2 * j], x1 = x[2 * j + 1];
+            x[2 * j] = x0 * t[j].x + x1 * t[j].y;
+            x[2 * j + 1] = -x0 * t[j].y + x1 * t[j].x;
+        }
     }
-    if (qscale) {
-        x0 *= qscale[c];
-        x1 *= qscale[c + 1];
-    }
-    *reinterpret_cast<uint32_t*>(dq + row * lddq + c) = pack_bf16(x0, x1);
+    if (qscale)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[j] *= qscale[c + j];
+    *reinterpret_cast<uint2*>(dq + row * lddq + c) = make_uint2(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]));
+}
+
+template <class K>
+void set_smem(K kern, int bytes) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
 }  // namespace
 
 void attn_fwd(const AttnArgs& a, cudaStream_t s) {
-    dim3 grid((a.T + BQ - 1) / BQ, a.H, a.clips);
-    attn_fwd_kernel<<<grid, 128, 0, s>>>(a);
+    static bool configured = false;
+    if (!configured) {
+        set_smem(attn_fwd_kernel<true>, FWD_SMEM);
+        set_smem(attn_fwd_kernel<false>, FWD_SMEM);
+        configured = true;
+    }
+    dim3 grid((a.T + FWD_BQ - 1) / FWD_BQ, a.H, a.clips);
+    if (a.rope && a.rope_load) attn_fwd_kernel<true><<<grid, FWD_WARPS * 32, FWD_SMEM, s>>>(a);
+    else attn_fwd_kernel<false><<<grid, FWD_WARPS * 32, FWD_SMEM, s>>>(a);
 }
 
 void attn_bwd(const AttnArgs& a, cudaStream_t s) {
-    const long warps = (long)a.clips * a.T * a.H;
-    attn_dvec_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(a);
-    const int smem = (2 * BKV + 4 * BQ) * LDS * 2;
+    const long threads = (long)a.clips * a.T * a.H * 8;
+    attn_dvec_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(a);
     static bool configured = false;
     if (!configured) {
-        cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        set_smem(attn_bwd_kernel<true>, BWD_SMEM);
+        set_smem(attn_bwd_kernel<false>, BWD_SMEM);
         configured = true;
     }
     dim3 grid((a.Tk + BKV - 1) / BKV, a.H, a.clips);
-    attn_bwd_kernel<<<grid, 128, smem, s>>>(a);
+    if (a.rope && a.rope_load) attn_bwd_kernel<true><<<grid, 128, BWD_SMEM, s>>>(a);
+    else attn_bwd_kernel<false><<<grid, 128, BWD_SMEM, s>>>(a);
 }
 
 void attn_dq_finish(const AttnArgs& a, bf16* dq, long lddq, const float* qscale, cudaStream_t s) {
-    const long n = (long)a.clips * a.T * a.H * HD / 2;
+    const long n = (long)a.clips * a.T * a.H * HD / 4;
     attn_dq_finish_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(a, dq, lddq, qscale);
 }
 

@@ -81,6 +81,7 @@ extern "C" int act_attention_bwd_noalloc(const void* q, const void* k, const voi
     a.causal = causal;
     a.zero_key = zero_key;
     a.rope = rope;
+    a.rope_load = 1;
     a.scale = 0.125f;
     a.o = const_cast<bf16*>(static_cast<const bf16*>(o));
     a.ldo = D;

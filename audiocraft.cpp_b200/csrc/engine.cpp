@@ -356,13 +356,17 @@ struct act_ctx {
         // pre-norm self-attention
         timed(2, 0, 0, [&] { layernorm_fwd(y.xin, y.norm[0], y.norm[1], dit ? te : nullptr, T, y.h1, y.mu[0], y.rs[0], (int)rows, D, eps, stream); });
         {
+            // q and k leave the projection already rotated (RoPE in the epilogue); DoRA keeps the
+            // unrotated output for its row-norm gradient
             GemmArgs e; e.mode = EPI_STORE_BF16; e.out = y.qkv; e.ldo = 3 * D;
+            if (dit) { e.rope = rope; e.rope_T = T; e.rope_cols = 2 * D; }
+            if (y.p[0].dora) { e.aux = y.Yaux[0]; e.ldaux = 3 * D; }
             proj_fwd(y.p[0], y.h1, rows, y.U[0], e);
         }
         AttnArgs sa;
         sa.q = y.qkv; sa.k = y.qkv + D; sa.v = y.qkv + 2 * D; sa.ldq = sa.ldk = sa.ldv = 3 * D;
         sa.T = T; sa.Tk = T; sa.H = H; sa.clips = n; sa.causal = dit ? 0 : 1; sa.zero_key = dit ? md.add_zero_attn : 0;
-        sa.rope = dit ? rope : nullptr; sa.scale = 1.0f / std::sqrt((float)md.head_dim);
+        sa.rope = dit ? rope : nullptr; sa.rope_load = 0; sa.scale = 1.0f / std::sqrt((float)md.head_dim);
         sa.o = y.o1; sa.ldo = D; sa.lse = y.lse1;
         timed(1, attn_flops(n, T, true), 0, [&] { attn_fwd(sa, stream); });
         {
@@ -448,7 +452,7 @@ struct act_ctx {
         AttnArgs sa;
         sa.q = y.qkv; sa.k = y.qkv + D; sa.v = y.qkv + 2 * D; sa.ldq = sa.ldk = sa.ldv = 3 * D;
         sa.T = T; sa.Tk = T; sa.H = H; sa.clips = n; sa.causal = dit ? 0 : 1; sa.zero_key = dit ? md.add_zero_attn : 0;
-        sa.rope = dit ? rope : nullptr; sa.scale = ca.scale;
+        sa.rope = dit ? rope : nullptr; sa.rope_load = 0; sa.scale = ca.scale;
         sa.o = y.o1; sa.ldo = D; sa.lse = y.lse1;
         sa.dout = dob; sa.lddo = D; sa.dvec = dvec; sa.dq_acc = dq_acc; sa.ldq_acc = D;
         sa.dk = dqkv + D; sa.dv = dqkv + 2 * D; sa.lddk = sa.lddv = 3 * D;
@@ -460,7 +464,7 @@ struct act_ctx {
         });
         {
             GemmArgs e; e.mode = EPI_STORE_F32; e.out = dtmp; e.ldo = D;
-            proj_bwd(y.p[0], dqkv, rows, y.h1, y.U[0], y.qkv, need_dx_in, e);
+            proj_bwd(y.p[0], dqkv, rows, y.h1, y.U[0], y.p[0].dora ? y.Yaux[0] : y.qkv, need_dx_in, e);
         }
         if (need_dx_in)
             timed(2, 0, 0, [&] { layernorm_bwd(dtmp, y.xin, y.norm[0], y.mu[0], y.rs[0], dx, 1, nullptr, nullptr, nullptr, (int)rows, D, stream); });
@@ -1119,7 +1123,7 @@ struct act_ctx {
             for (int t = 0; t < 7; ++t) {
                 if (!y.p[t].adapted) continue;
                 y.U[t] = dalloc<bf16>((t == 3 ? Cr : Mr) * RP);
-                if (y.p[t].dora && (t == 1 || t == 4 || t == 6)) y.Yaux[t] = dalloc<bf16>(Mr * y.p[t].out);
+                if (y.p[t].dora && (t == 0 || t == 1 || t == 4 || t == 6)) y.Yaux[t] = dalloc<bf16>(Mr * y.p[t].out);
             }
             if (y.produces) {
                 y.xsave_bf = dalloc<bf16>(Mr * D);
@@ -1617,6 +1621,7 @@ int act_attention(int device, const void* q, const void* k, const void* v, const
         a.nvalid = nvalid ? static_cast<const int*>(up(nvalid, clips * 4)) : nullptr;
         a.causal = causal; a.zero_key = zero_key;
         a.rope = rope ? static_cast<const float*>(up(rope, (size_t)T * 64 * 4)) : nullptr;
+        a.rope_load = 1;
         if (rope && Tk > T) throw Error(ACT_ERR_INVALID, "RoPE needs Tk <= T");
         a.scale = 0.125f;
         a.o = static_cast<bf16*>(up(nullptr, rq * D * 2));

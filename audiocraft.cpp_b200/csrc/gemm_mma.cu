@@ -165,6 +165,12 @@ gemm_mma_kernel(const GemmArgs p) {
                     if (two) *reinterpret_cast<uint32_t*>(a) = pack_bf16(v0, v1);
                     else a[0] = __float2bfloat16(v0);
                 }
+                if (p.rope && n < p.rope_cols) {  // n is even: (v0, v1) is one rotary pair
+                    const float2 t = reinterpret_cast<const float2*>(p.rope)[(long)(m % p.rope_T) * 32 + (n % 64) / 2];
+                    const float x0 = v0, x1 = v1;
+                    v0 = x0 * t.x - x1 * t.y;
+                    v1 = x0 * t.y + x1 * t.x;
+                }
                 switch (p.mode) {
                     case EPI_STORE_F32:
                     case EPI_ACCUM_F32:

@@ -50,6 +50,8 @@ struct TcParams {
     long ldauxin;
     const float* colscale2;
     const float* bias;
+    const float* rope;
+    int rope_T, rope_cols;
     int nvalid, mvalid;
     int* err;
 };
@@ -175,6 +177,16 @@ __device__ __forceinline__ void epilogue32(const TcParams& p, int m, int n, floa
         for (int i = 0; i < 4; ++i)
             a[i] = make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
                               pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
+    }
+    if (p.rope && n < p.rope_cols) {  // 32 columns inside one 64-wide head: 16 rotary pairs
+        const float2* t = reinterpret_cast<const float2*>(p.rope) + (long)(m % p.rope_T) * 32 + (n % 64) / 2;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const float2 tt = t[j];
+            const float x0 = v[2 * j], x1 = v[2 * j + 1];
+            v[2 * j] = x0 * tt.x - x1 * tt.y;
+            v[2 * j + 1] = x0 * tt.y + x1 * tt.x;
+        }
     }
     switch (p.mode) {
         case EPI_STORE_F32:
@@ -448,6 +460,7 @@ void launch_tc(const GemmArgs& a, int* err, cudaStream_t s) {
     p.mode = a.mode; p.alpha = a.alpha; p.colscale = a.colscale; p.out = a.out; p.ldo = a.ldo;
     p.resid = a.resid; p.ldr = a.ldr; p.aux = a.aux; p.ldaux = a.ldaux; p.auxin = a.auxin; p.ldauxin = a.ldauxin;
     p.colscale2 = a.colscale2; p.bias = a.bias; p.nvalid = a.nvalid; p.mvalid = a.mvalid; p.err = err;
+    p.rope = a.rope; p.rope_T = a.rope_T; p.rope_cols = a.rope_cols;
     auto kern = gemm_tc_kernel<BN, B_MN>;
     static bool configured = false;
     if (!configured) {

@@ -55,6 +55,8 @@ struct GemmArgs {
     long ldauxin = 0;
     const float* colscale2 = nullptr;  // EPI_GELU_BWD: DoRA factor of the producing projection
     const float* bias = nullptr;       // EPI_BIAS_BF16
+    const float* rope = nullptr;       // rotate column pairs n < rope_cols by position m % rope_T
+    int rope_T = 1, rope_cols = 0;     //   ([rope_T][32] (cos, sin) table, 64-column heads; after aux)
     int nvalid = 1 << 30;              // columns >= nvalid are not written
     int mvalid = 1 << 30;              // rows >= mvalid are not written
 };
@@ -77,7 +79,9 @@ struct AttnArgs {
     const int* nvalid = nullptr;  // per clip: keys >= nvalid masked (nullptr: none)
     int causal = 0;
     int zero_key = 0;             // add_zero_attn: implicit key with score 0 and value 0
-    const float* rope = nullptr;  // [T][32] (cos, sin) pairs: rotate q and k (self-attention)
+    const float* rope = nullptr;  // [T][32] (cos, sin) pairs of the self-attention RoPE
+    int rope_load = 0;            // 1: q/k arrive unrotated (rotate while staging); 0: pre-rotated
+                                  // (either way dq / dk come back unrotated)
     float scale = 0.125f;
     bf16* o = nullptr;
     long ldo = 0;
