@@ -15,7 +15,7 @@
 //   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, fused epilogue, 16-byte stores
 // Every mbarrier wait is bounded (globaltimer); on expiry the CTA records an error code,
 // drains what it issued and returns, so a logic error cannot hang the device.
-// No cluster launch and no multicast: every CTA loads its own tiles.
+// No cluster launch: every CTA issues its own TMA loads for its own tiles.
 #include <cuda.h>
 
 #include <stdexcept>
