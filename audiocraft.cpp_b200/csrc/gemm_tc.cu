@@ -18,6 +18,7 @@
 // No cluster launch: every CTA issues its own TMA loads for its own tiles.
 #include <cuda.h>
 
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -494,9 +495,15 @@ bool gemm_tc_supported(const GemmArgs& a) {
 }
 
 void gemm_tc(const GemmArgs& a, int* err, cudaStream_t s) {
-    // 256-wide tiles unless that leaves most SMs idle for the last wave
     const long tiles256 = (long)((a.M + BM - 1) / BM) * (a.N / 256);
-    const bool wide = a.N % 256 == 0 && tiles256 >= 2 * 148;
+    static const int force_bn = [] {
+        const char* e = std::getenv("ACTRAIN_TC_BN");  // tuning experiments only
+        return e ? std::atoi(e) : 0;
+    }();
+    // 256-wide tiles whenever N allows: measured faster than 128-wide at every cfg-2 shape,
+    // even when they leave part of the last wave idle (higher FLOP per byte staged from L2)
+    (void)tiles256;
+    const bool wide = a.N % 256 == 0 && force_bn != 128;
     if (a.b_kmajor) {
         if (wide) launch_tc<256, false>(a, err, s);
         else launch_tc<128, false>(a, err, s);
