@@ -249,9 +249,11 @@ struct act_ctx {
         if (e) throw Error(ACT_ERR_CUDA, "device kernel reported a timed-out wait (code " + std::to_string(e) + ")");
     }
 
+    // split-K count for the token reductions: about two CTAs per SM, each with a long enough
+    // run of 64-deep k-tiles to keep its pipeline full and its final atomics rare
     static int splitk_for(long tiles, long ktiles) {
         long s = std::max<long>(1, 296 / std::max<long>(tiles, 1));
-        s = std::min<long>(s, std::max<long>(1, ktiles / 4));
+        s = std::min<long>(s, std::max<long>(1, ktiles / 8));
         return (int)std::min<long>(s, 64);
     }
 
@@ -290,14 +292,14 @@ struct act_ctx {
             gb.A1 = dYl; gb.lda1 = p.out; gb.a_kmajor = false;
             gb.B1 = U; gb.ldb1 = p.RP; gb.b_kmajor = false;
             gb.mode = EPI_ATOMIC_F32; gb.out = grad + p.offB; gb.ldo = p.r; gb.nvalid = p.r;
-            gb.splitk = splitk_for((long)((p.out + 127) / 128), (rows + 31) / 32);
+            gb.splitk = splitk_for((long)((p.out + 63) / 64), (rows + 63) / 64);
             run_gemm(gb, 2);
             GemmArgs ga;
             ga.M = p.RP; ga.N = p.in; ga.K1 = (int)rows;
             ga.A1 = dU; ga.lda1 = p.RP; ga.a_kmajor = false;
             ga.B1 = X; ga.ldb1 = p.in; ga.b_kmajor = false;
             ga.mode = EPI_ATOMIC_F32; ga.out = grad + p.offA; ga.ldo = p.in; ga.mvalid = p.r;
-            ga.splitk = splitk_for((long)((p.in + 127) / 128), (rows + 31) / 32);
+            ga.splitk = splitk_for((long)((p.in + 127) / 128), (rows + 63) / 64);
             run_gemm(ga, 2);
         }
         if (!want_dx) return;
@@ -342,7 +344,7 @@ struct act_ctx {
                 a.A1 = p.BD; a.lda1 = p.RP; a.a_kmajor = false;
                 a.B1 = p.W; a.ldb1 = p.in; a.b_kmajor = false;
                 a.mode = EPI_ATOMIC_F32; a.out = grad + p.offA; a.ldo = p.in; a.mvalid = p.r;
-                a.splitk = splitk_for((p.in + 127) / 128, (p.out + 31) / 32);
+                a.splitk = splitk_for((p.in + 127) / 128, (p.out + 63) / 64);
                 run_gemm(a, 2);
             }
     }
@@ -1534,8 +1536,10 @@ int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int 
         g.mode = EPI_STORE_F32; g.out = dC; g.ldo = N;
         const bool tc = path == 2 || (path == 0 && gemm_tc_supported(g));
         if (tc && !gemm_tc_supported(g)) throw Error(ACT_ERR_INVALID, "shape not supported by the tcgen05 path");
+        if (path == 3 && !gemm_tc2_supported(g)) throw Error(ACT_ERR_INVALID, "shape not supported by the 2-CTA path");
         auto run = [&] {
-            if (tc) gemm_tc(g, derr, st);
+            if (path == 3) gemm_tc2(g, derr, st);
+            else if (tc) gemm_tc(g, derr, st);
             else gemm(g, st);
         };
         run();

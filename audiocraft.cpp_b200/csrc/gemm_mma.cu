@@ -246,8 +246,11 @@ void launch(const GemmArgs& a, cudaStream_t s) {
 
 template <bool AK, bool BKM>
 void dispatch(const GemmArgs& a, cudaStream_t s) {
-    if (a.N <= 32)  // rank-block shapes: many short row blocks, deep pipeline (HBM-bound)
+    // rank-block shapes are HBM-bound: small tiles (enough CTAs for every SM), deep pipelines
+    if (a.N <= 32)                  // u = s X A^T, dU = s dY B (rows x 32); dB += dY^T U
         launch<64, 32, 4, 1, AK, BKM, 64, 6>(a, s);
+    else if (a.M <= 32 && !AK)      // dA += dU^T X: 32 x in, split over rows
+        launch<32, 128, 2, 4, AK, BKM, 64, 6>(a, s);
     else if (a.N <= 64)
         launch<128, 64, 4, 1, AK, BKM>(a, s);
     else if (a.M <= 64)

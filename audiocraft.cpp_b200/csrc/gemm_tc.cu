@@ -149,18 +149,103 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+constexpr int EPI_F_LD = 36;  // fp32 staging row stride (floats): 16-byte rows, conflict-free
+constexpr int EPI_B_LD = 40;  // bf16 staging row stride (elements)
+constexpr int EPI_WARP_BYTES = 32 * EPI_F_LD * 4 + 32 * EPI_B_LD * 2;
+constexpr int EPI_SMEM = EPI_WARPS * EPI_WARP_BYTES;
+
 template <int BN>
 struct TcCfg {
     static constexpr int A_BYTES = BM * BKE * 2;
     static constexpr int B_BYTES = BN * BKE * 2;
     static constexpr int STAGE = A_BYTES + B_BYTES;
     static constexpr int STAGES = BN == 256 ? 4 : 6;
-    static constexpr int SMEM = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int SMEM = STAGES * STAGE + EPI_SMEM + 1024 /*align*/ + 256 /*barriers*/;
     static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulator buffers
 };
 
-// Epilogue of 32 consecutive columns n .. n+31 of row m held as fp32 in v[].
-__device__ __forceinline__ void epilogue32(const TcParams& p, int m, int n, float* v) {
+// ---------------------------------------------------------------------------------------
+// Epilogue.  After tcgen05.ld each thread holds 32 consecutive columns of ONE row, so direct
+// stores would touch 32 cache lines per warp instruction.  Each epilogue warp therefore stages
+// its 32 x 32 chunk through a padded shared-memory tile and moves whole 128-byte row segments
+// (fp32: 4 rows per instruction, bf16: 8 rows) to and from global memory.
+
+__device__ __forceinline__ void tile_f32_load(float* tf, const float* g, long ld, int rows, int lane) {
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+        const int r = it * 4 + (lane >> 3), c = (lane & 7) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < rows) v = *reinterpret_cast<const float4*>(g + (long)r * ld + c);
+        *reinterpret_cast<float4*>(tf + r * EPI_F_LD + c) = v;
+    }
+}
+
+__device__ __forceinline__ void tile_f32_store(const float* tf, float* g, long ld, int rows, int lane) {
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+        const int r = it * 4 + (lane >> 3), c = (lane & 7) * 4;
+        if (r < rows) *reinterpret_cast<float4*>(g + (long)r * ld + c) = *reinterpret_cast<const float4*>(tf + r * EPI_F_LD + c);
+    }
+}
+
+__device__ __forceinline__ void tile_b16_load(bf16* tb, const bf16* g, long ld, int rows, int lane) {
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+        const int r = it * 8 + (lane >> 2), c = (lane & 3) * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < rows) v = *reinterpret_cast<const uint4*>(g + (long)r * ld + c);
+        *reinterpret_cast<uint4*>(tb + r * EPI_B_LD + c) = v;
+    }
+}
+
+__device__ __forceinline__ void tile_b16_store(const bf16* tb, bf16* g, long ld, int rows, int lane) {
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+        const int r = it * 8 + (lane >> 2), c = (lane & 3) * 8;
+        if (r < rows) *reinterpret_cast<uint4*>(g + (long)r * ld + c) = *reinterpret_cast<const uint4*>(tb + r * EPI_B_LD + c);
+    }
+}
+
+__device__ __forceinline__ void row_f32_put(float* tf, int lane, const float* v) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        *reinterpret_cast<float4*>(tf + lane * EPI_F_LD + 4 * i) = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
+__device__ __forceinline__ void row_f32_add(const float* tf, int lane, float* v) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 r = *reinterpret_cast<const float4*>(tf + lane * EPI_F_LD + 4 * i);
+        v[4 * i] += r.x; v[4 * i + 1] += r.y; v[4 * i + 2] += r.z; v[4 * i + 3] += r.w;
+    }
+}
+
+__device__ __forceinline__ void row_b16_put(bf16* tb, int lane, const float* v) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        *reinterpret_cast<uint4*>(tb + lane * EPI_B_LD + 8 * i) =
+            make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
+                       pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
+}
+
+__device__ __forceinline__ void row_b16_get(const bf16* tb, int lane, float* v) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 q = *reinterpret_cast<const uint4*>(tb + lane * EPI_B_LD + 8 * i);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            v[8 * i + 2 * j] = __bfloat162float(__ushort_as_bfloat16((unsigned short)(w[j] & 0xffff)));
+            v[8 * i + 2 * j + 1] = __bfloat162float(__ushort_as_bfloat16((unsigned short)(w[j] >> 16)));
+        }
+    }
+}
+
+// Warp-collective epilogue of the 32 x 32 chunk rows m_base .. m_base+31 (the first `rows`
+// valid), columns n .. n+31; lane l holds row m_base + l in v[].
+__device__ __forceinline__ void epilogue_warp32(const TcParams& p, int m_base, int rows, int n, float* v, float* tf,
+                                                bf16* tb, int lane) {
+    const int m = m_base + lane;
     if (p.alpha != 1.0f)
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] *= p.alpha;
@@ -173,11 +258,10 @@ __device__ __forceinline__ void epilogue32(const TcParams& p, int m, int n, floa
         }
     }
     if (p.aux && p.mode != EPI_GELU) {
-        uint4* a = reinterpret_cast<uint4*>(p.aux + (long)m * p.ldaux + n);
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            a[i] = make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
-                              pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
+        row_b16_put(tb, lane, v);
+        __syncwarp();
+        tile_b16_store(tb, p.aux + (long)m_base * p.ldaux + n, p.ldaux, rows, lane);
+        __syncwarp();
     }
     if (p.rope && n < p.rope_cols) {  // 32 columns inside one 64-wide head: 16 rotary pairs
         const float2* t = reinterpret_cast<const float2*>(p.rope) + (long)(m % p.rope_T) * 32 + (n % 64) / 2;
@@ -193,29 +277,26 @@ __device__ __forceinline__ void epilogue32(const TcParams& p, int m, int n, floa
         case EPI_STORE_F32:
         case EPI_ACCUM_F32:
         case EPI_RESID_F32: {
-            float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) + (long)m * p.ldo + n);
-            if (p.mode == EPI_ACCUM_F32) {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const float4 r = o[i];
-                    v[4 * i] += r.x; v[4 * i + 1] += r.y; v[4 * i + 2] += r.z; v[4 * i + 3] += r.w;
-                }
-            } else if (p.mode == EPI_RESID_F32) {
-                const float4* rr = reinterpret_cast<const float4*>(p.resid + (long)m * p.ldr + n);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const float4 r = rr[i];
-                    v[4 * i] += r.x; v[4 * i + 1] += r.y; v[4 * i + 2] += r.z; v[4 * i + 3] += r.w;
-                }
+            float* o = static_cast<float*>(p.out) + (long)m_base * p.ldo + n;
+            if (p.mode != EPI_STORE_F32) {
+                if (p.mode == EPI_ACCUM_F32) tile_f32_load(tf, o, p.ldo, rows, lane);
+                else tile_f32_load(tf, p.resid + (long)m_base * p.ldr + n, p.ldr, rows, lane);
+                __syncwarp();
+                row_f32_add(tf, lane, v);
+                __syncwarp();
             }
-#pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            row_f32_put(tf, lane, v);
+            __syncwarp();
+            tile_f32_store(tf, o, p.ldo, rows, lane);
+            __syncwarp();
             break;
         }
-        case EPI_ATOMIC_F32: {
-            float* o = static_cast<float*>(p.out) + (long)m * p.ldo + n;
+        case EPI_ATOMIC_F32: {  // not taken by the tcgen05 paths (kept for completeness)
+            if (lane < rows) {
+                float* o = static_cast<float*>(p.out) + (long)m * p.ldo + n;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) atomicAdd(o + i, v[i]);
+                for (int i = 0; i < 32; ++i) atomicAdd(o + i, v[i]);
+            }
             break;
         }
         default: {
@@ -223,40 +304,30 @@ __device__ __forceinline__ void epilogue32(const TcParams& p, int m, int n, floa
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] += p.bias[n + i];
             } else if (p.mode == EPI_GELU) {
-                uint4* a = reinterpret_cast<uint4*>(p.aux + (long)m * p.ldaux + n);
+                // the stored pre-activation is bf16; the activation and its backward use that value
+                row_b16_put(tb, lane, v);
+                __syncwarp();
+                tile_b16_store(tb, p.aux + (long)m_base * p.ldaux + n, p.ldaux, rows, lane);
+                row_b16_get(tb, lane, v);
+                __syncwarp();
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    uint32_t w[4];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const bf16 z0 = __float2bfloat16(v[8 * i + 2 * j]), z1 = __float2bfloat16(v[8 * i + 2 * j + 1]);
-                        w[j] = (uint32_t)__bfloat16_as_ushort(z0) | ((uint32_t)__bfloat16_as_ushort(z1) << 16);
-                        v[8 * i + 2 * j] = gelu_as(__bfloat162float(z0));
-                        v[8 * i + 2 * j + 1] = gelu_as(__bfloat162float(z1));
-                    }
-                    a[i] = make_uint4(w[0], w[1], w[2], w[3]);
-                }
+                for (int i = 0; i < 32; ++i) v[i] = gelu_as(v[i]);
             } else if (p.mode == EPI_GELU_BWD) {
-                const uint4* z = reinterpret_cast<const uint4*>(p.auxin + (long)m * p.ldauxin + n);
+                float z[32];
+                tile_b16_load(tb, p.auxin + (long)m_base * p.ldauxin + n, p.ldauxin, rows, lane);
+                __syncwarp();
+                row_b16_get(tb, lane, z);
+                __syncwarp();
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const uint4 zz = z[i];
-                    const uint32_t w[4] = {zz.x, zz.y, zz.z, zz.w};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        v[8 * i + 2 * j] *= gelu_as_grad(__bfloat162float(__ushort_as_bfloat16((unsigned short)(w[j] & 0xffff))));
-                        v[8 * i + 2 * j + 1] *= gelu_as_grad(__bfloat162float(__ushort_as_bfloat16((unsigned short)(w[j] >> 16))));
-                    }
-                }
+                for (int i = 0; i < 32; ++i) v[i] *= gelu_as_grad(z[i]);
                 if (p.colscale2)
 #pragma unroll
                     for (int i = 0; i < 32; ++i) v[i] *= p.colscale2[n + i];
             }
-            uint4* o = reinterpret_cast<uint4*>(static_cast<bf16*>(p.out) + (long)m * p.ldo + n);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-                o[i] = make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
-                                  pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
+            row_b16_put(tb, lane, v);
+            __syncwarp();
+            tile_b16_store(tb, static_cast<bf16*>(p.out) + (long)m_base * p.ldo + n, p.ldo, rows, lane);
+            __syncwarp();
         }
     }
 }
@@ -269,14 +340,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(const __grid_const
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023) & ~1023u;
     unsigned char* smem = smem_raw + (base - raw);
-    const uint32_t bars = base + S * Cfg::STAGE;
+    const uint32_t bars = base + S * Cfg::STAGE + EPI_SMEM;
     // barrier layout: full[S], empty[S], tfull[2], tempty[2], drain, then the TMEM address
     auto full_bar = [&](int s) { return bars + 8 * s; };
     auto empty_bar = [&](int s) { return bars + 8 * (S + s); };
     auto tfull_bar = [&](int a) { return bars + 8 * (2 * S + a); };
     auto tempty_bar = [&](int a) { return bars + 8 * (2 * S + 2 + a); };
     const uint32_t drain_bar = bars + 8 * (2 * S + 4);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S * Cfg::STAGE + 8 * (2 * S + 5));
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S * Cfg::STAGE + EPI_SMEM + 8 * (2 * S + 5));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -382,13 +453,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(const __grid_const
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const int m = mb * BM + quad * 32 + lane;
-            const bool row_ok = m < p.M && m < p.mvalid;
+            const int m_base = mb * BM + quad * 32;
+            const int rows = max(0, min(32, min(p.M, p.mvalid) - m_base));
+            float* tf = reinterpret_cast<float*>(smem + S * Cfg::STAGE + (warp - 2) * EPI_WARP_BYTES);
+            bf16* tb = reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(tf) + 32 * EPI_F_LD * 4);
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t r[32];
                 tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + a * BN + c * 32, r);
                 const int n = nb * BN + c * 32;
-                if (row_ok && n < p.nvalid) epilogue32(p, m, n, reinterpret_cast<float*>(r));
+                if (n < p.nvalid) epilogue_warp32(p, m_base, rows, n, reinterpret_cast<float*>(r), tf, tb, lane);
             }
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
@@ -401,6 +474,217 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(const __grid_const
     __syncwarp();
     if (warp == 0)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(Cfg::TMEM_COLS));
+}
+
+// ---------------------------------------------------------------------------------------
+// 2-CTA variant: a cluster of two CTAs computes a 256 x 256 output tile with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256).  Each CTA stages its own 128 rows of A and its
+// own 128 rows of B (half of the tile's columns); the leader CTA (cluster rank 0) issues the
+// MMAs, which read both CTAs' shared memory and write both CTAs' TMEM (rows 0..127 in the
+// leader, 128..255 in the peer).  Twice the FLOPs per byte staged from L2 of the 1-CTA
+// 128 x 256 tile, which is what bounds that kernel.  Loads are plain per-CTA TMA loads whose
+// completion bytes are posted to the leader's barrier; the leader signals the peer's barriers
+// with ordinary commits addressed through mapa.
+
+constexpr int BN2 = 256;
+constexpr int BH2 = BN2 / 2;
+
+struct Tc2Cfg {
+    static constexpr int A_BYTES = BM * BKE * 2;
+    static constexpr int B_BYTES = BH2 * BKE * 2;
+    static constexpr int STAGE = A_BYTES + B_BYTES;
+    static constexpr int STAGES = 6;
+    static constexpr int SMEM = STAGES * STAGE + EPI_SMEM + 1024 + 256;
+    static constexpr uint32_t TMEM_COLS = 2 * BN2;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// shared::cluster address of the same shared-memory offset in cluster CTA `rank`
+__device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                                 uint32_t leader_bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(leader_bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_f16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
+                 : "memory");
+}
+
+template <bool B_MN>
+__global__ void __launch_bounds__(NTHREADS, 1) gemm_tc2_kernel(const __grid_constant__ TcMaps maps, const TcParams p) {
+    using Cfg = Tc2Cfg;
+    constexpr int S = Cfg::STAGES;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023) & ~1023u;
+    unsigned char* smem = smem_raw + (base - raw);
+    const uint32_t bars = base + S * Cfg::STAGE + EPI_SMEM;
+    auto full_bar = [&](int s) { return bars + 8 * s; };
+    auto empty_bar = [&](int s) { return bars + 8 * (S + s); };
+    auto tfull_bar = [&](int a) { return bars + 8 * (2 * S + a); };
+    auto tempty_bar = [&](int a) { return bars + 8 * (2 * S + 2 + a); };
+    const uint32_t drain_bar = bars + 8 * (2 * S + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S * Cfg::STAGE + EPI_SMEM + 8 * (2 * S + 5));
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(full_bar(s), 1);   // leader: one arrive_expect_tx for both CTAs' bytes
+            mbar_init(empty_bar(s), 1);  // each CTA: one commit from the leader
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), 2 * EPI_WARPS);  // leader: both CTAs' epilogue warps
+        }
+        mbar_init(drain_bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(Cfg::TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int nk1 = (p.K1 + BKE - 1) / BKE, nk2 = (p.K2 + BKE - 1) / BKE, nk = nk1 + nk2;
+    const int num_m2 = (p.M + 2 * BM - 1) / (2 * BM);
+    const int ntiles = num_m2 * p.num_n;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------------------ TMA producer (both CTAs)
+        int it = 0;
+        bool ok = true;
+        for (int tile = pair; tile < ntiles && ok; tile += npairs) {
+            const int mb = tile % num_m2, nb = tile / num_m2;
+            for (int kb = 0; kb < nk && ok; ++kb, ++it) {
+                const int s = it % S;
+                ok = mbar_wait(empty_bar(s), ((it / S) & 1) ^ 1, p.err, 11);
+                if (!ok) break;
+                const bool seg2 = kb >= nk1;
+                const CUtensorMap* ma = seg2 ? &maps.a2 : &maps.a1;
+                const CUtensorMap* mbm = seg2 ? &maps.b2 : &maps.b1;
+                const int k0 = (seg2 ? kb - nk1 : kb) * BKE;
+                const uint32_t sa = base + s * Cfg::STAGE, sb = sa + Cfg::A_BYTES;
+                const uint32_t lbar = map_rank(full_bar(s), 0);
+                if (rank == 0) mbar_expect_tx(full_bar(s), 2 * Cfg::STAGE);
+                tma_load_2d_pair(sa, ma, k0, mb * 2 * BM + rank * BM, lbar);
+                const int n0 = nb * BN2 + rank * BH2;
+                if (B_MN) {
+#pragma unroll
+                    for (int j = 0; j < BH2 / 64; ++j) tma_load_2d_pair(sb + j * 8192, mbm, n0 + 64 * j, k0, lbar);
+                } else {
+                    tma_load_2d_pair(sb, mbm, k0, n0, lbar);
+                }
+            }
+        }
+    } else if (warp == 1 && lane == 0 && rank == 0) {
+        // ------------------------------------------------------------ MMA issuer (leader)
+        const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((B_MN ? 1u : 0u) << 16) |
+                               ((uint32_t)(BN2 >> 3) << 17) | ((uint32_t)((2 * BM) >> 4) << 24);
+        int it = 0, u = 0;
+        bool ok = true;
+        for (int tile = pair; tile < ntiles && ok; tile += npairs, ++u) {
+            const int a = u & 1;
+            ok = mbar_wait(tempty_bar(a), ((u >> 1) & 1) ^ 1, p.err, 12);
+            if (!ok) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t tacc = tmem_base + a * BN2;
+            for (int kb = 0; kb < nk; ++kb, ++it) {
+                const int s = it % S;
+                ok = mbar_wait(full_bar(s), (it / S) & 1, p.err, 13);
+                if (!ok) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t sa = base + s * Cfg::STAGE, sb = sa + Cfg::A_BYTES;
+                const bool seg2 = kb >= nk1;
+                const int kv = seg2 ? p.K2 - (kb - nk1) * BKE : p.K1 - kb * BKE;
+                const int nk16 = kv >= BKE ? BKE / 16 : (kv + 15) / 16;
+                for (int k16 = 0; k16 < nk16; ++k16) {
+                    const uint64_t ad = smem_desc(sa + k16 * 32, 16, 1024);
+                    const uint64_t bd = B_MN ? smem_desc(sb + k16 * 2048, 8192, 1024) : smem_desc(sb + k16 * 32, 16, 1024);
+                    mma_f16_pair(tacc, ad, bd, idesc, (kb > 0 || k16 > 0) ? 1u : 0u);
+                }
+                mma_commit_pair(map_rank(empty_bar(s), 0));
+                mma_commit_pair(map_rank(empty_bar(s), 1));
+            }
+            if (!ok) break;
+            mma_commit_pair(map_rank(tfull_bar(a), 0));
+            mma_commit_pair(map_rank(tfull_bar(a), 1));
+        }
+        mma_commit_pair(map_rank(drain_bar, 0));
+        mbar_wait(drain_bar, 0, p.err, 16);
+    } else if (warp >= 2) {
+        // ------------------------------------------------------------ epilogue (both CTAs)
+        const int quad = warp & 3;
+        const uint32_t leader_tempty0 = map_rank(tempty_bar(0), 0), leader_tempty1 = map_rank(tempty_bar(1), 0);
+        int u = 0;
+        for (int tile = pair; tile < ntiles; tile += npairs, ++u) {
+            const int a = u & 1;
+            const int mb = tile % num_m2, nb = tile / num_m2;
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(tfull_bar(a), (u >> 1) & 1, p.err, 14);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int m_base = mb * 2 * BM + (int)rank * BM + quad * 32;
+            const int rows = max(0, min(32, min(p.M, p.mvalid) - m_base));
+            float* tf = reinterpret_cast<float*>(smem + S * Cfg::STAGE + (warp - 2) * EPI_WARP_BYTES);
+            bf16* tb = reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(tf) + 32 * EPI_F_LD * 4);
+            for (int c = 0; c < BN2 / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + a * BN2 + c * 32, r);
+                const int n = nb * BN2 + c * 32;
+                if (n < p.nvalid) epilogue_warp32(p, m_base, rows, n, reinterpret_cast<float*>(r), tf, tb, lane);
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(a ? leader_tempty1 : leader_tempty0);
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    cluster_sync();  // no CTA leaves while its partner may still signal it or read its smem
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    __syncwarp();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(Cfg::TMEM_COLS));
 }
 
 // ---------------------------------------------------------------------------------------
@@ -478,6 +762,57 @@ void launch_tc(const GemmArgs& a, int* err, cudaStream_t s) {
     kern<<<grid, NTHREADS, Cfg::SMEM, s>>>(maps, p);
 }
 
+template <bool B_MN>
+void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
+    using Cfg = Tc2Cfg;
+    TcMaps maps;
+    make_map(&maps.a1, a.A1, a.M, a.K1, a.lda1, BKE, BM);
+    if (B_MN) make_map(&maps.b1, a.B1, a.K1, a.N, a.ldb1, 64, BKE);
+    else make_map(&maps.b1, a.B1, a.N, a.K1, a.ldb1, BKE, BH2);
+    if (a.K2 > 0) {
+        make_map(&maps.a2, a.A2, a.M, a.K2, a.lda2, BKE, BM);
+        if (B_MN) make_map(&maps.b2, a.B2, a.K2, a.N, a.ldb2, 64, BKE);
+        else make_map(&maps.b2, a.B2, a.N, a.K2, a.ldb2, BKE, BH2);
+    } else {
+        maps.a2 = maps.a1;
+        maps.b2 = maps.b1;
+    }
+    TcParams p;
+    p.M = a.M; p.N = a.N; p.K1 = a.K1; p.K2 = a.K2;
+    p.num_m = (a.M + BM - 1) / BM; p.num_n = a.N / BN2;
+    p.mode = a.mode; p.alpha = a.alpha; p.colscale = a.colscale; p.out = a.out; p.ldo = a.ldo;
+    p.resid = a.resid; p.ldr = a.ldr; p.aux = a.aux; p.ldaux = a.ldaux; p.auxin = a.auxin; p.ldauxin = a.ldauxin;
+    p.colscale2 = a.colscale2; p.bias = a.bias; p.nvalid = a.nvalid; p.mvalid = a.mvalid; p.err = err;
+    p.rope = a.rope; p.rope_T = a.rope_T; p.rope_cols = a.rope_cols;
+    auto kern = gemm_tc2_kernel<B_MN>;
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+        configured = true;
+    }
+    if (!g_num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    const int tiles = ((a.M + 2 * BM - 1) / (2 * BM)) * (a.N / BN2);
+    const int pairs = tiles < g_num_sms / 2 ? tiles : g_num_sms / 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(NTHREADS, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, maps, p);
+}
+
 }  // namespace
 
 bool gemm_tc_supported(const GemmArgs& a) {
@@ -492,6 +827,13 @@ bool gemm_tc_supported(const GemmArgs& a) {
                          reinterpret_cast<uintptr_t>(a.B1) | reinterpret_cast<uintptr_t>(a.A2) |
                          reinterpret_cast<uintptr_t>(a.B2);
     return (al & 15) == 0;
+}
+
+bool gemm_tc2_supported(const GemmArgs& a) { return gemm_tc_supported(a) && a.N % BN2 == 0 && a.M > BM; }
+
+void gemm_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
+    if (a.b_kmajor) launch_tc2<false>(a, err, s);
+    else launch_tc2<true>(a, err, s);
 }
 
 void gemm_tc(const GemmArgs& a, int* err, cudaStream_t s) {

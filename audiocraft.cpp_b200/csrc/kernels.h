@@ -64,6 +64,8 @@ struct GemmArgs {
 void gemm(const GemmArgs& a, cudaStream_t s);                 // mma.sync path, any layout
 bool gemm_tc_supported(const GemmArgs& a);                     // shapes the tcgen05 path takes
 void gemm_tc(const GemmArgs& a, int* err, cudaStream_t s);     // tcgen05 / TMEM / TMA path
+bool gemm_tc2_supported(const GemmArgs& a);                    // 2-CTA (cta_group::2) 256 x 256 tiles
+void gemm_tc2(const GemmArgs& a, int* err, cudaStream_t s);
 
 // ---------------------------------------------------------------------------------------
 // attention over token-major q/k/v (head h at columns h*64 .. h*64+63), head_dim 64.

@@ -205,19 +205,23 @@ def run_sweep(kind, reps):
     bits = lambda shape: (rng.integers(0x3C00, 0x3F80, size=shape, dtype=np.uint16) ^
                           (rng.integers(0, 2, size=shape, dtype=np.uint16) << 15))
     if kind == "gemm":
-        for M in ((6000,) if os.environ.get("SWEEP_QUICK") else (6000, 2048, 32768)):
-            for (N, K) in ((1024, 1024), (3072, 1024), (4096, 1024), (1024, 4096), (1536, 1536), (6144, 1536),
-                           (1536, 6144)):
-                for b_mn in (False, True):
-                    for path in (2, 1):
+        one = os.environ.get("SWEEP_SHAPE")  # "M,N,K": a single shape (profiling captures)
+        for M in ((int(one.split(",")[0]),) if one else (6000,) if os.environ.get("SWEEP_QUICK") else (6000, 2048, 32768)):
+            for (N, K) in (((int(one.split(",")[1]), int(one.split(",")[2])),) if one else
+                           ((1024, 1024), (3072, 1024), (4096, 1024), (1024, 4096), (1536, 1536), (6144, 1536),
+                            (1536, 6144))):
+                for b_mn in ((False,) if one else (False, True)):
+                    for path in ((3, 2) if one else (3, 2, 1)):
                         if M * max(N, K) > 32768 * 6144 // 2 and path == 1:
+                            continue
+                        if path == 3 and N % 256:
                             continue
                         a, b = bits((M, K)), bits((K, N) if b_mn else (N, K))
                         _, ms = A.gemm_bf16(a, b, M, N, K, b_mn, path, reps=reps)
                         tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
                         print(json.dumps({"sweep": "gemm", "M": M, "N": N, "K": K,
                                           "layout": "NN (dX = dY W)" if b_mn else "NT (Y = X W^T)",
-                                          "kernel": "tcgen05" if path == 2 else "mma.sync", "ms": ms,
+                                          "kernel": {1: "mma.sync", 2: "tcgen05", 3: "tcgen05_pair"}[path], "ms": ms,
                                           "tflops": tf, "frac_of_peak": tf / peak}), flush=True)
     else:
         for H in (16, 24):

@@ -167,7 +167,8 @@ int act_reset_kernel_stats(act_ctx* ctx);
 double act_step_flops(act_ctx* ctx, int n);
 /* stand-alone projection GEMM on host buffers (tests and the kernel sweep): C[M][N] fp32 =
  * A[M][K] . B(n,k) with bf16 A and B, B as [N][K] (b_mn_major 0) or [K][N] (1);
- * path 0 = automatic, 1 = mma.sync kernel, 2 = tcgen05 kernel; when reps > 0 the GEMM is
+ * path 0 = automatic, 1 = mma.sync kernel, 2 = tcgen05 kernel, 3 = tcgen05 2-CTA (cta_group::2)
+ * kernel; when reps > 0 the GEMM is
  * re-run reps times back to back and *ms_per_call receives the mean device time */
 int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path,
                   int reps, float* ms_per_call);

@@ -16,11 +16,13 @@ def bits_to_f32(b):
     return (b.astype(np.uint32) << 16).view(np.float32)
 
 
-@pytest.mark.parametrize("path", [1, 2], ids=["mma", "tcgen05"])
+@pytest.mark.parametrize("path", [1, 2, 3], ids=["mma", "tcgen05", "tcgen05_pair"])
 @pytest.mark.parametrize("b_mn", [False, True], ids=["NT", "NN"])
 @pytest.mark.parametrize("M,N,K", [(128, 128, 64), (300, 256, 128), (6000, 1024, 1024), (1000, 4096, 256),
                                    (130, 512, 4096)])
 def test_gemm_matches_numpy(path, b_mn, M, N, K):
+    if path == 3 and (N % 256 or M <= 128):
+        pytest.skip("the 2-CTA kernel needs N % 256 == 0 and M > 128")
     rng = np.random.default_rng(M + N + K)
     a = bf16_bits(rng.standard_normal((M, K)))
     b = bf16_bits(rng.standard_normal((K, N) if b_mn else (N, K)))
