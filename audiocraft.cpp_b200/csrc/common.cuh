@@ -10,12 +10,15 @@ namespace act {
 
 // A&S 7.1.26 GELU and the derivative of that approximation (the reference trains through
 // the approximation, src/ac/lora.h:97-110, so its gradient is the one autodiff yields).
+// The reciprocal and exponential use the fast hardware approximations (relative error ~1e-6):
+// every caller rounds the result to bf16 (relative step 2^-8), and these run once per element
+// of the widest GEMM epilogues.
 __device__ __forceinline__ float gelu_as(float x) {
     const float z = x * 0.7071067811865475f, a = fabsf(z);
-    const float t = 1.0f / (0.3275911f * a + 1.0f);
+    const float t = __fdividef(1.0f, 0.3275911f * a + 1.0f);
     const float poly =
         ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
-    const float e = expf(-(z * z));
+    const float e = __expf(-(z * z));
     const float sg = z > 0.f ? 1.f : (z < 0.f ? -1.f : 0.f);
     return x * (0.5f * (sg * (1.0f - poly * e)) + 0.5f);
 }
@@ -23,16 +26,34 @@ __device__ __forceinline__ float gelu_as(float x) {
 __device__ __forceinline__ float gelu_as_grad(float x) {
     const float z = x * 0.7071067811865475f, a = fabsf(z);
     const float sg = z > 0.f ? 1.f : (z < 0.f ? -1.f : 0.f);
-    const float t = 1.0f / (0.3275911f * a + 1.0f);
+    const float t = __fdividef(1.0f, 0.3275911f * a + 1.0f);
     const float poly =
         ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
     const float dpoly =
         (((5.0f * 1.061405429f * t - 4.0f * 1.453152027f) * t + 3.0f * 1.421413741f) * t - 2.0f * 0.284496736f) * t +
         0.254829592f;
-    const float e = expf(-(z * z));
+    const float e = __expf(-(z * z));
     const float erf_ = sg * (1.0f - poly * e);
     const float derf = sg * sg * dpoly * 0.3275911f * t * t * e + 2.0f * z * sg * poly * e;
     return (0.5f * erf_ + 0.5f) + x * 0.5f * derf * 0.7071067811865475f;
+}
+
+// gelu_as(x) and gelu_as_grad(x) from one evaluation of the shared terms.  sg(z)^2 = 1 is used
+// in the derivative: it differs only at z = 0, where that term is multiplied by x = 0.
+__device__ __forceinline__ void gelu_as_pair(float x, float& g, float& dg) {
+    const float z = x * 0.7071067811865475f, a = fabsf(z);
+    const float t = __fdividef(1.0f, 0.3275911f * a + 1.0f);
+    const float poly =
+        ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
+    const float dpoly =
+        (((5.0f * 1.061405429f * t - 4.0f * 1.453152027f) * t + 3.0f * 1.421413741f) * t - 2.0f * 0.284496736f) * t +
+        0.254829592f;
+    const float e = __expf(-(z * z));
+    const float pe = poly * e;
+    const float half_cdf = 0.5f * copysignf(1.0f - pe, z) + 0.5f;
+    g = x * half_cdf;
+    const float derf = dpoly * 0.3275911f * t * t * e + 2.0f * a * pe;
+    dg = half_cdf + x * 0.5f * derf * 0.7071067811865475f;
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -237,7 +237,7 @@ struct act_ctx {
 
     void run_gemm(const GemmArgs& g, int cls = 0) {
         const double fl = 2.0 * g.M * g.N * (double)(g.K1 + g.K2);
-        if (use_tc && gemm_tc_supported(g)) timed(cls, fl, 0, [&] { gemm_tc(g, kerr, stream); });
+        if (use_tc && gemm_tc_supported(g)) timed(cls, fl, 0, [&] { gemm_tc_auto(g, kerr, stream); });
         else timed(cls, fl, 0, [&] { gemm(g, stream); });
     }
 
@@ -398,7 +398,8 @@ struct act_ctx {
         // feed-forward (no timestep)
         timed(2, 0, 0, [&] { layernorm_fwd(y.xmid2, y.norm[4], y.norm[5], nullptr, T, y.f, y.mu[2], y.rs[2], (int)rows, D, eps, stream); });
         {
-            GemmArgs e; e.mode = EPI_GELU; e.out = y.gact; e.ldo = F; e.aux = y.z; e.ldaux = F;
+            // without DoRA on ff.0 the backward needs only gelu'(z): store that instead of z
+            GemmArgs e; e.mode = y.p[5].dora ? EPI_GELU : EPI_GELU_D; e.out = y.gact; e.ldo = F; e.aux = y.z; e.ldaux = F;
             proj_fwd(y.p[5], y.f, rows, y.U[5], e);
             GemmArgs o; o.mode = EPI_RESID_F32; o.out = y.xout; o.ldo = D; o.resid = y.xmid2; o.ldr = D;
             if (y.p[6].dora) { o.aux = y.Yaux[6]; o.ldaux = D; }
@@ -415,7 +416,7 @@ struct act_ctx {
         const bool dit = mf;
         // ---- feed-forward
         {
-            GemmArgs e; e.mode = EPI_GELU_BWD; e.out = dz; e.ldo = F; e.auxin = y.z; e.ldauxin = F;
+            GemmArgs e; e.mode = y.p[5].dora ? EPI_GELU_BWD : EPI_GELU_BWD_D; e.out = dz; e.ldo = F; e.auxin = y.z; e.ldauxin = F;
             e.colscale2 = y.p[5].dora ? y.p[5].g : nullptr;
             proj_bwd(y.p[6], dxbf, rows, y.gact, y.U[6], y.Yaux[6], true, e);
             GemmArgs d; d.mode = EPI_STORE_F32; d.out = dtmp; d.ldo = D;
@@ -1539,6 +1540,7 @@ int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int 
         if (path == 3 && !gemm_tc2_supported(g)) throw Error(ACT_ERR_INVALID, "shape not supported by the 2-CTA path");
         auto run = [&] {
             if (path == 3) gemm_tc2(g, derr, st);
+            else if (path == 0 && tc) gemm_tc_auto(g, derr, st);
             else if (tc) gemm_tc(g, derr, st);
             else gemm(g, st);
         };

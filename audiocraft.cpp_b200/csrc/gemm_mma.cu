@@ -197,7 +197,9 @@ gemm_mma_kernel(const GemmArgs p) {
                     case EPI_STORE_BF16:
                     case EPI_BIAS_BF16:
                     case EPI_GELU:
-                    case EPI_GELU_BWD: {
+                    case EPI_GELU_D:
+                    case EPI_GELU_BWD:
+                    case EPI_GELU_BWD_D: {
                         if (p.mode == EPI_BIAS_BF16) {
                             v0 += p.bias[n];
                             if (two) v1 += p.bias[n + 1];
@@ -209,10 +211,24 @@ gemm_mma_kernel(const GemmArgs p) {
                             if (two) a[1] = z1;
                             v0 = gelu_as(__bfloat162float(z0));
                             v1 = gelu_as(__bfloat162float(z1));
-                        } else if (p.mode == EPI_GELU_BWD) {
+                        } else if (p.mode == EPI_GELU_D) {
+                            bf16* a = p.aux + (long)m * p.ldaux + n;
+                            float g0, d0, g1, d1;
+                            gelu_as_pair(__bfloat162float(__float2bfloat16(v0)), g0, d0);
+                            gelu_as_pair(__bfloat162float(__float2bfloat16(v1)), g1, d1);
+                            a[0] = __float2bfloat16(d0);
+                            if (two) a[1] = __float2bfloat16(d1);
+                            v0 = g0;
+                            v1 = g1;
+                        } else if (p.mode == EPI_GELU_BWD || p.mode == EPI_GELU_BWD_D) {
                             const bf16* z = p.auxin + (long)m * p.ldauxin + n;
-                            v0 *= gelu_as_grad(__bfloat162float(z[0]));
-                            if (two) v1 *= gelu_as_grad(__bfloat162float(z[1]));
+                            if (p.mode == EPI_GELU_BWD) {
+                                v0 *= gelu_as_grad(__bfloat162float(z[0]));
+                                if (two) v1 *= gelu_as_grad(__bfloat162float(z[1]));
+                            } else {
+                                v0 *= __bfloat162float(z[0]);
+                                if (two) v1 *= __bfloat162float(z[1]);
+                            }
                             if (p.colscale2) {
                                 v0 *= p.colscale2[n];
                                 if (two) v1 *= p.colscale2[n + 1];

@@ -59,6 +59,7 @@ struct TcParams {
 
 struct TcMaps {
     CUtensorMap a1, b1, a2, b2;
+    CUtensorMap out, aux;  // epilogue stores: box 32 x 32, swizzle 128 B (fp32) / 64 B (bf16)
 };
 
 __device__ __forceinline__ unsigned long long globaltimer() {
@@ -84,8 +85,8 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait: returns false (and records `code`) if the phase does not complete in time.
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
-    if (mbar_try(bar, parity)) return true;
+// The first probe is inline (the common case on the issue paths); the polling loop is not.
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, int* err, int code) {
     const unsigned long long t0 = globaltimer();
     while (true) {
         for (int i = 0; i < 256; ++i)
@@ -96,6 +97,10 @@ __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, 
         }
         if (*(volatile int*)err) return false;  // another CTA already failed: stop waiting
     }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
+    return mbar_try(bar, parity) || mbar_wait_slow(bar, parity, err, code);
 }
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
@@ -149,10 +154,12 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-constexpr int EPI_F_LD = 36;  // fp32 staging row stride (floats): 16-byte rows, conflict-free
-constexpr int EPI_B_LD = 40;  // bf16 staging row stride (elements)
-constexpr int EPI_WARP_BYTES = 32 * EPI_F_LD * 4 + 32 * EPI_B_LD * 2;
-constexpr int EPI_SMEM = EPI_WARPS * EPI_WARP_BYTES;
+// Epilogue staging, per epilogue warp: a 32-row x 128-byte tile for the output chunk (32 fp32
+// or 32 bf16 columns; 128-byte swizzle) and a 32 x 64-byte tile for bf16 side outputs/inputs
+// (64-byte swizzle).  Both leave shared memory through TMA bulk tensor stores.
+constexpr int EPI_OUT_BYTES = 32 * 128;
+constexpr int EPI_AUX_BYTES = 32 * 64;
+constexpr int EPI_SMEM = EPI_WARPS * (EPI_OUT_BYTES + EPI_AUX_BYTES);
 
 template <int BN>
 struct TcCfg {
@@ -165,86 +172,124 @@ struct TcCfg {
 };
 
 // ---------------------------------------------------------------------------------------
-// Epilogue.  After tcgen05.ld each thread holds 32 consecutive columns of ONE row, so direct
-// stores would touch 32 cache lines per warp instruction.  Each epilogue warp therefore stages
-// its 32 x 32 chunk through a padded shared-memory tile and moves whole 128-byte row segments
-// (fp32: 4 rows per instruction, bf16: 8 rows) to and from global memory.
+// Epilogue.  After tcgen05.ld each lane holds 32 consecutive columns of ONE row.  The warp
+// writes the chunk into its swizzled staging tile (conflict-free: the 16-byte unit u of row r
+// sits at unit u ^ f(r)) and one lane issues a TMA bulk tensor store, which clips rows past the
+// tensor's extent.  Residual / accumulator / GELU inputs come in through the same tiles with
+// coalesced loads (one 128-byte row segment per 8 or 4 lanes).
 
-__device__ __forceinline__ void tile_f32_load(float* tf, const float* g, long ld, int rows, int lane) {
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-        const int r = it * 4 + (lane >> 3), c = (lane & 7) * 4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (r < rows) v = *reinterpret_cast<const float4*>(g + (long)r * ld + c);
-        *reinterpret_cast<float4*>(tf + r * EPI_F_LD + c) = v;
+// byte offset of 16-byte unit u of row r: 128-byte swizzle (rows of 128 B, tile 1024-aligned)
+__device__ __forceinline__ uint32_t sw128(int r, int u) { return r * 128 + ((u ^ (r & 7)) << 4); }
+// 64-byte swizzle (rows of 64 B, tile 512-aligned)
+__device__ __forceinline__ uint32_t sw64(int r, int u) { return r * 64 + ((u ^ ((r >> 1) & 3)) << 4); }
+
+struct EpiTiles {
+    unsigned char* o;  // output chunk tile (EPI_OUT_BYTES)
+    unsigned char* x;  // bf16 side tile (EPI_AUX_BYTES)
+    uint32_t o_s, x_s; // their shared-state-space addresses
+};
+
+// previous bulk stores of this warp have finished reading the staging tiles
+__device__ __forceinline__ void tiles_free(int lane) {
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    __syncwarp();
+}
+
+__device__ __forceinline__ void tile_store(const CUtensorMap* map, uint32_t src, int x, int y, int lane) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) {
+        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+                     ::"l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(src)
+                     : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
     }
 }
 
-__device__ __forceinline__ void tile_f32_store(const float* tf, float* g, long ld, int rows, int lane) {
+__device__ __forceinline__ void put_row_f32(unsigned char* t, int lane, const float* v) {
 #pragma unroll
-    for (int it = 0; it < 8; ++it) {
-        const int r = it * 4 + (lane >> 3), c = (lane & 7) * 4;
-        if (r < rows) *reinterpret_cast<float4*>(g + (long)r * ld + c) = *reinterpret_cast<const float4*>(tf + r * EPI_F_LD + c);
+    for (int u = 0; u < 8; ++u)
+        *reinterpret_cast<float4*>(t + sw128(lane, u)) = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+}
+
+__device__ __forceinline__ void add_row_f32(const unsigned char* t, int lane, float* v) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        const float4 r = *reinterpret_cast<const float4*>(t + sw128(lane, u));
+        v[4 * u] += r.x; v[4 * u + 1] += r.y; v[4 * u + 2] += r.z; v[4 * u + 3] += r.w;
     }
 }
 
-__device__ __forceinline__ void tile_b16_load(bf16* tb, const bf16* g, long ld, int rows, int lane) {
+// 32 bf16 of this lane's row into a 64-byte-swizzled tile
+__device__ __forceinline__ void put_row_b16(unsigned char* t, int lane, const float* v) {
 #pragma unroll
-    for (int it = 0; it < 4; ++it) {
-        const int r = it * 8 + (lane >> 2), c = (lane & 3) * 8;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (r < rows) v = *reinterpret_cast<const uint4*>(g + (long)r * ld + c);
-        *reinterpret_cast<uint4*>(tb + r * EPI_B_LD + c) = v;
-    }
+    for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<uint4*>(t + sw64(lane, u)) =
+            make_uint4(pack_bf16(v[8 * u], v[8 * u + 1]), pack_bf16(v[8 * u + 2], v[8 * u + 3]),
+                       pack_bf16(v[8 * u + 4], v[8 * u + 5]), pack_bf16(v[8 * u + 6], v[8 * u + 7]));
 }
 
-__device__ __forceinline__ void tile_b16_store(const bf16* tb, bf16* g, long ld, int rows, int lane) {
+__device__ __forceinline__ void get_row_b16(const unsigned char* t, int lane, float* v) {
 #pragma unroll
-    for (int it = 0; it < 4; ++it) {
-        const int r = it * 8 + (lane >> 2), c = (lane & 3) * 8;
-        if (r < rows) *reinterpret_cast<uint4*>(g + (long)r * ld + c) = *reinterpret_cast<const uint4*>(tb + r * EPI_B_LD + c);
-    }
-}
-
-__device__ __forceinline__ void row_f32_put(float* tf, int lane, const float* v) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-        *reinterpret_cast<float4*>(tf + lane * EPI_F_LD + 4 * i) = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-}
-
-__device__ __forceinline__ void row_f32_add(const float* tf, int lane, float* v) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const float4 r = *reinterpret_cast<const float4*>(tf + lane * EPI_F_LD + 4 * i);
-        v[4 * i] += r.x; v[4 * i + 1] += r.y; v[4 * i + 2] += r.z; v[4 * i + 3] += r.w;
-    }
-}
-
-__device__ __forceinline__ void row_b16_put(bf16* tb, int lane, const float* v) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-        *reinterpret_cast<uint4*>(tb + lane * EPI_B_LD + 8 * i) =
-            make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
-                       pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
-}
-
-__device__ __forceinline__ void row_b16_get(const bf16* tb, int lane, float* v) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint4 q = *reinterpret_cast<const uint4*>(tb + lane * EPI_B_LD + 8 * i);
+    for (int u = 0; u < 4; ++u) {
+        const uint4 q = *reinterpret_cast<const uint4*>(t + sw64(lane, u));
         const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            v[8 * i + 2 * j] = __bfloat162float(__ushort_as_bfloat16((unsigned short)(w[j] & 0xffff)));
-            v[8 * i + 2 * j + 1] = __bfloat162float(__ushort_as_bfloat16((unsigned short)(w[j] >> 16)));
+            v[8 * u + 2 * j] = __uint_as_float(w[j] << 16);
+            v[8 * u + 2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
         }
+    }
+}
+
+// Epilogue inputs read per chunk: fp32 residual / accumulator rows (RESID, ACCUM) or bf16 GELU
+// pre-activations (GELU_BWD).  They are fetched one chunk ahead into registers as coalesced
+// 128-byte row segments, so their latency overlaps the previous chunk, then staged in the tile.
+__device__ __forceinline__ int epi_input_kind(int mode) {
+    return (mode == EPI_RESID_F32 || mode == EPI_ACCUM_F32) ? 1
+           : (mode == EPI_GELU_BWD || mode == EPI_GELU_BWD_D) ? 2 : 0;
+}
+
+// chunk rows m_base .. m_base+rows-1 (rows <= 0: nothing), columns n .. n+31
+__device__ __forceinline__ void fetch_input(const TcParams& p, int kind, int m_base, int rows, int n, int lane,
+                                            float4* pre) {
+    if (kind == 1) {
+        const bool acc = p.mode == EPI_ACCUM_F32;
+        const float* g = acc ? static_cast<const float*>(p.out) : p.resid;
+        const long ld = acc ? p.ldo : p.ldr;
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+            const int r = it * 4 + (lane >> 3), u = lane & 7;
+            pre[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (r < rows) pre[it] = *reinterpret_cast<const float4*>(g + (long)(m_base + r) * ld + n + 4 * u);
+        }
+    } else if (kind == 2) {
+#pragma unroll
+        for (int it = 0; it < 4; ++it) {
+            const int r = it * 8 + (lane >> 2), u = lane & 3;
+            pre[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (r < rows)
+                pre[it] = *reinterpret_cast<const float4*>(p.auxin + (long)(m_base + r) * p.ldauxin + n + 8 * u);
+        }
+    }
+}
+
+__device__ __forceinline__ void stage_input(int kind, const float4* pre, const EpiTiles& t, int lane) {
+    if (kind == 1) {
+#pragma unroll
+        for (int it = 0; it < 8; ++it)
+            *reinterpret_cast<float4*>(t.o + sw128(it * 4 + (lane >> 3), lane & 7)) = pre[it];
+    } else if (kind == 2) {
+#pragma unroll
+        for (int it = 0; it < 4; ++it)
+            *reinterpret_cast<float4*>(t.x + sw64(it * 8 + (lane >> 2), lane & 3)) = pre[it];
     }
 }
 
 // Warp-collective epilogue of the 32 x 32 chunk rows m_base .. m_base+31 (the first `rows`
 // valid), columns n .. n+31; lane l holds row m_base + l in v[].
-__device__ __forceinline__ void epilogue_warp32(const TcParams& p, int m_base, int rows, int n, float* v, float* tf,
-                                                bf16* tb, int lane) {
+__device__ __forceinline__ void epilogue_warp32(const TcParams& p, const TcMaps& maps, int m_base, int rows, int n,
+                                                float* v, const EpiTiles& t, int lane) {
     const int m = m_base + lane;
     if (p.alpha != 1.0f)
 #pragma unroll
@@ -257,78 +302,97 @@ __device__ __forceinline__ void epilogue_warp32(const TcParams& p, int m_base, i
             v[4 * i] *= c.x; v[4 * i + 1] *= c.y; v[4 * i + 2] *= c.z; v[4 * i + 3] *= c.w;
         }
     }
-    if (p.aux && p.mode != EPI_GELU) {
-        row_b16_put(tb, lane, v);
-        __syncwarp();
-        tile_b16_store(tb, p.aux + (long)m_base * p.ldaux + n, p.ldaux, rows, lane);
-        __syncwarp();
+    if (p.aux && p.mode != EPI_GELU && p.mode != EPI_GELU_D) {
+        tiles_free(lane);
+        put_row_b16(t.x, lane, v);
+        tile_store(&maps.aux, t.x_s, n, m_base, lane);
     }
     if (p.rope && n < p.rope_cols) {  // 32 columns inside one 64-wide head: 16 rotary pairs
-        const float2* t = reinterpret_cast<const float2*>(p.rope) + (long)(m % p.rope_T) * 32 + (n % 64) / 2;
+        const float2* tt = reinterpret_cast<const float2*>(p.rope) + (long)(m % p.rope_T) * 32 + (n % 64) / 2;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-            const float2 tt = t[j];
+            const float2 c = tt[j];
             const float x0 = v[2 * j], x1 = v[2 * j + 1];
-            v[2 * j] = x0 * tt.x - x1 * tt.y;
-            v[2 * j + 1] = x0 * tt.y + x1 * tt.x;
+            v[2 * j] = x0 * c.x - x1 * c.y;
+            v[2 * j + 1] = x0 * c.y + x1 * c.x;
         }
     }
-    switch (p.mode) {
-        case EPI_STORE_F32:
-        case EPI_ACCUM_F32:
-        case EPI_RESID_F32: {
-            float* o = static_cast<float*>(p.out) + (long)m_base * p.ldo + n;
-            if (p.mode != EPI_STORE_F32) {
-                if (p.mode == EPI_ACCUM_F32) tile_f32_load(tf, o, p.ldo, rows, lane);
-                else tile_f32_load(tf, p.resid + (long)m_base * p.ldr + n, p.ldr, rows, lane);
-                __syncwarp();
-                row_f32_add(tf, lane, v);
-                __syncwarp();
+    if (p.mode == EPI_STORE_F32 || p.mode == EPI_ACCUM_F32 || p.mode == EPI_RESID_F32) {
+        if (p.mode == EPI_STORE_F32) tiles_free(lane);
+        else add_row_f32(t.o, lane, v);  // residual / accumulator already staged in the tile
+        put_row_f32(t.o, lane, v);
+        tile_store(&maps.out, t.o_s, n, m_base, lane);
+        return;
+    }
+    if (p.mode == EPI_BIAS_BF16) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] += p.bias[n + i];
+    } else if (p.mode == EPI_GELU) {
+        // the stored pre-activation is bf16; the activation and its backward use that value
+        tiles_free(lane);
+        put_row_b16(t.x, lane, v);
+        get_row_b16(t.x, lane, v);
+        tile_store(&maps.aux, t.x_s, n, m_base, lane);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = gelu_as(v[i]);
+    } else if (p.mode == EPI_GELU_D) {
+        // gelu' of the bf16-rounded pre-activation goes to aux, gelu of it to the output
+        tiles_free(lane);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            float d8[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float g;
+                gelu_as_pair(__bfloat162float(__float2bfloat16(v[8 * u + j])), g, d8[j]);
+                v[8 * u + j] = g;
             }
-            row_f32_put(tf, lane, v);
-            __syncwarp();
-            tile_f32_store(tf, o, p.ldo, rows, lane);
-            __syncwarp();
-            break;
+            *reinterpret_cast<uint4*>(t.x + sw64(lane, u)) =
+                make_uint4(pack_bf16(d8[0], d8[1]), pack_bf16(d8[2], d8[3]), pack_bf16(d8[4], d8[5]),
+                           pack_bf16(d8[6], d8[7]));
         }
-        case EPI_ATOMIC_F32: {  // not taken by the tcgen05 paths (kept for completeness)
-            if (lane < rows) {
-                float* o = static_cast<float*>(p.out) + (long)m * p.ldo + n;
+        tile_store(&maps.aux, t.x_s, n, m_base, lane);
+    } else if (p.mode == EPI_GELU_BWD || p.mode == EPI_GELU_BWD_D) {
+        float z[32];
+        get_row_b16(t.x, lane, z);  // pre-activation (or its gelu') already staged in the side tile
+        if (p.mode == EPI_GELU_BWD) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) atomicAdd(o + i, v[i]);
+            for (int i = 0; i < 32; ++i) v[i] *= gelu_as_grad(z[i]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= z[i];
+        }
+        if (p.colscale2)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= p.colscale2[n + i];
+    }
+    tiles_free(lane);
+    put_row_b16(t.o, lane, v);
+    tile_store(&maps.out, t.o_s, n, m_base, lane);
+}
+
+// All chunks of one accumulator tile (NCH x 32 columns from TMEM row address `trow`).  The
+// next chunk's inputs (this tile's, or chunk 0 of the warp's next tile) are fetched while the
+// current one is finished.
+template <int NCH>
+__device__ __forceinline__ void epilogue_tile(const TcParams& p, const TcMaps& maps, uint32_t trow, int m_base,
+                                              int rows, int n0, int next_m_base, int next_rows, int next_n0,
+                                              const EpiTiles& t, int lane, float4* pre) {
+    const int kind = epi_input_kind(p.mode);
+    for (int c = 0; c < NCH; ++c) {
+        uint32_t r[32];
+        tmem_ld32(trow + c * 32, r);
+        const int n = n0 + c * 32;
+        if (kind) {
+            if (rows > 0) {
+                tiles_free(lane);
+                stage_input(kind, pre, t, lane);
             }
-            break;
-        }
-        default: {
-            if (p.mode == EPI_BIAS_BF16) {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] += p.bias[n + i];
-            } else if (p.mode == EPI_GELU) {
-                // the stored pre-activation is bf16; the activation and its backward use that value
-                row_b16_put(tb, lane, v);
-                __syncwarp();
-                tile_b16_store(tb, p.aux + (long)m_base * p.ldaux + n, p.ldaux, rows, lane);
-                row_b16_get(tb, lane, v);
-                __syncwarp();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = gelu_as(v[i]);
-            } else if (p.mode == EPI_GELU_BWD) {
-                float z[32];
-                tile_b16_load(tb, p.auxin + (long)m_base * p.ldauxin + n, p.ldauxin, rows, lane);
-                __syncwarp();
-                row_b16_get(tb, lane, z);
-                __syncwarp();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] *= gelu_as_grad(z[i]);
-                if (p.colscale2)
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] *= p.colscale2[n + i];
-            }
-            row_b16_put(tb, lane, v);
-            __syncwarp();
-            tile_b16_store(tb, static_cast<bf16*>(p.out) + (long)m_base * p.ldo + n, p.ldo, rows, lane);
+            if (c + 1 < NCH) fetch_input(p, kind, m_base, rows, n + 32, lane, pre);
+            else fetch_input(p, kind, next_m_base, next_rows, next_n0, lane, pre);
             __syncwarp();
         }
+        if (rows > 0) epilogue_warp32(p, maps, m_base, rows, n, reinterpret_cast<float*>(r), t, lane);
     }
 }
 
@@ -378,14 +442,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(const __grid_const
 
     if (warp == 0 && lane == 0) {
         // ------------------------------------------------------------ TMA producer
-        int it = 0;
+        int it = 0, s = 0;
+        uint32_t ph = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
             const int mb = tile % p.num_m, nb = tile / p.num_m;
-            for (int kb = 0; kb < nk && ok; ++kb, ++it) {
-                const int s = it % S;
-                ok = mbar_wait(empty_bar(s), ((it / S) & 1) ^ 1, p.err, 1);
-                if (!ok) break;
+            for (int kb = 0; kb < nk; ++kb, ++it) {
+                if (!mbar_wait(empty_bar(s), ph ^ 1, p.err, 1)) { ok = false; break; }
                 const bool seg2 = kb >= nk1;
                 const CUtensorMap* ma = seg2 ? &maps.a2 : &maps.a1;
                 const CUtensorMap* mbm = seg2 ? &maps.b2 : &maps.b1;
@@ -399,6 +462,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(const __grid_const
                 } else {
                     tma_load_2d(sb, mbm, k0, nb * BN, full_bar(s));
                 }
+                if (++s == S) { s = 0; ph ^= 1; }
             }
         }
         // drain: wait until every stage this thread filled has landed
@@ -411,7 +475,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(const __grid_const
         // ------------------------------------------------------------ MMA issuer
         const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((B_MN ? 1u : 0u) << 16) |
                                ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-        int it = 0, u = 0;
+        // Stage-0 descriptors; a stage offset or a k16 step is added to the 14-bit start-address
+        // field (shared-memory addresses stay below 256 KB, so the field cannot carry over).
+        const uint64_t a_desc0 = smem_desc(base, 16, 1024);
+        const uint64_t b_desc0 = B_MN ? smem_desc(base + Cfg::A_BYTES, 8192, 1024)
+                                      : smem_desc(base + Cfg::A_BYTES, 16, 1024);
+        constexpr uint32_t A_STEP = 32 >> 4, B_STEP = (B_MN ? 2048 : 32) >> 4;
+        int s = 0, u = 0;
+        uint32_t ph = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++u) {
             const int a = u & 1;
@@ -419,21 +490,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(const __grid_const
             if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t tacc = tmem_base + a * BN;
-            for (int kb = 0; kb < nk; ++kb, ++it) {
-                const int s = it % S;
-                ok = mbar_wait(full_bar(s), (it / S) & 1, p.err, 3);
-                if (!ok) break;
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t sa = base + s * Cfg::STAGE, sb = sa + Cfg::A_BYTES;
-                const bool seg2 = kb >= nk1;
-                const int kv = seg2 ? p.K2 - (kb - nk1) * BKE : p.K1 - kb * BKE;
-                const int nk16 = kv >= BKE ? BKE / 16 : (kv + 15) / 16;
-                for (int k16 = 0; k16 < nk16; ++k16) {
-                    const uint64_t ad = smem_desc(sa + k16 * 32, 16, 1024);
-                    const uint64_t bd = B_MN ? smem_desc(sb + k16 * 2048, 8192, 1024) : smem_desc(sb + k16 * 32, 16, 1024);
-                    mma_f16(tacc, ad, bd, idesc, (kb > 0 || k16 > 0) ? 1u : 0u);
+            for (int kb = 0; kb < nk; ++kb) {
+                if (!mbar_wait(full_bar(s), ph, p.err, 3)) { ok = false; break; }
+                const uint64_t soff = (uint64_t)((s * Cfg::STAGE) >> 4);
+                const uint64_t ad = a_desc0 + soff, bd = b_desc0 + soff;
+                const int kv = kb >= nk1 ? p.K2 - (kb - nk1) * BKE : BKE;
+                if (kv >= BKE) {
+#pragma unroll
+                    for (int k16 = 0; k16 < BKE / 16; ++k16)
+                        mma_f16(tacc, ad + A_STEP * k16, bd + B_STEP * k16, idesc, (kb | k16) ? 1u : 0u);
+                } else {
+                    for (int k16 = 0; k16 < (kv + 15) / 16; ++k16)
+                        mma_f16(tacc, ad + A_STEP * k16, bd + B_STEP * k16, idesc, (kb | k16) ? 1u : 0u);
                 }
                 mma_commit(empty_bar(s));
+                if (++s == S) { s = 0; ph ^= 1; }
             }
             if (!ok) break;
             mma_commit(tfull_bar(a));
@@ -444,29 +515,41 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(const __grid_const
     } else if (warp >= 2) {
         // ------------------------------------------------------------ epilogue
         const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
+        EpiTiles tiles;
+        tiles.o = smem + S * Cfg::STAGE + (warp - 2) * EPI_OUT_BYTES;
+        tiles.x = smem + S * Cfg::STAGE + EPI_WARPS * EPI_OUT_BYTES + (warp - 2) * EPI_AUX_BYTES;
+        tiles.o_s = smem_u32(tiles.o);
+        tiles.x_s = smem_u32(tiles.x);
+        const int mlim = min(p.M, p.mvalid);
+        auto tile_rows = [&](int tl, int& m_base, int& rows, int& n0) {
+            m_base = (tl % p.num_m) * BM + quad * 32;
+            rows = tl < ntiles ? max(0, min(32, mlim - m_base)) : 0;
+            n0 = (tl / p.num_m) * BN;
+        };
+        float4 pre[8];
+        {
+            int mb0, r0, n00;
+            tile_rows(blockIdx.x, mb0, r0, n00);
+            fetch_input(p, epi_input_kind(p.mode), mb0, r0, n00, lane, pre);
+        }
         int u = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++u) {
             const int a = u & 1;
-            const int mb = tile % p.num_m, nb = tile / p.num_m;
             bool ok = true;
             if (lane == 0) ok = mbar_wait(tfull_bar(a), (u >> 1) & 1, p.err, 4);
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const int m_base = mb * BM + quad * 32;
-            const int rows = max(0, min(32, min(p.M, p.mvalid) - m_base));
-            float* tf = reinterpret_cast<float*>(smem + S * Cfg::STAGE + (warp - 2) * EPI_WARP_BYTES);
-            bf16* tb = reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(tf) + 32 * EPI_F_LD * 4);
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + a * BN + c * 32, r);
-                const int n = nb * BN + c * 32;
-                if (n < p.nvalid) epilogue_warp32(p, m_base, rows, n, reinterpret_cast<float*>(r), tf, tb, lane);
-            }
+            int m_base, rows, n0, nm, nr, nn;
+            tile_rows(tile, m_base, rows, n0);
+            tile_rows(tile + gridDim.x, nm, nr, nn);
+            epilogue_tile<BN / 32>(p, maps, tmem_base + ((uint32_t)(quad * 32) << 16) + a * BN, m_base, rows, n0, nm,
+                                   nr, nn, tiles, lane, pre);
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty_bar(a));
         }
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // stores complete
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -590,14 +673,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc2_kernel(const __grid_cons
 
     if (warp == 0 && lane == 0) {
         // ------------------------------------------------------------ TMA producer (both CTAs)
-        int it = 0;
+        int s = 0;
+        uint32_t ph = 0;
         bool ok = true;
         for (int tile = pair; tile < ntiles && ok; tile += npairs) {
             const int mb = tile % num_m2, nb = tile / num_m2;
-            for (int kb = 0; kb < nk && ok; ++kb, ++it) {
-                const int s = it % S;
-                ok = mbar_wait(empty_bar(s), ((it / S) & 1) ^ 1, p.err, 11);
-                if (!ok) break;
+            for (int kb = 0; kb < nk; ++kb) {
+                if (!mbar_wait(empty_bar(s), ph ^ 1, p.err, 11)) { ok = false; break; }
                 const bool seg2 = kb >= nk1;
                 const CUtensorMap* ma = seg2 ? &maps.a2 : &maps.a1;
                 const CUtensorMap* mbm = seg2 ? &maps.b2 : &maps.b1;
@@ -613,13 +695,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc2_kernel(const __grid_cons
                 } else {
                     tma_load_2d_pair(sb, mbm, k0, n0, lbar);
                 }
+                if (++s == S) { s = 0; ph ^= 1; }
             }
         }
     } else if (warp == 1 && lane == 0 && rank == 0) {
         // ------------------------------------------------------------ MMA issuer (leader)
         const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((B_MN ? 1u : 0u) << 16) |
                                ((uint32_t)(BN2 >> 3) << 17) | ((uint32_t)((2 * BM) >> 4) << 24);
-        int it = 0, u = 0;
+        const uint64_t a_desc0 = smem_desc(base, 16, 1024);
+        const uint64_t b_desc0 = B_MN ? smem_desc(base + Cfg::A_BYTES, 8192, 1024)
+                                      : smem_desc(base + Cfg::A_BYTES, 16, 1024);
+        constexpr uint32_t A_STEP = 32 >> 4, B_STEP = (B_MN ? 2048 : 32) >> 4;
+        const uint32_t empty0 = map_rank(empty_bar(0), 0), empty1 = map_rank(empty_bar(0), 1);
+        int s = 0, u = 0;
+        uint32_t ph = 0;
         bool ok = true;
         for (int tile = pair; tile < ntiles && ok; tile += npairs, ++u) {
             const int a = u & 1;
@@ -627,22 +716,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc2_kernel(const __grid_cons
             if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t tacc = tmem_base + a * BN2;
-            for (int kb = 0; kb < nk; ++kb, ++it) {
-                const int s = it % S;
-                ok = mbar_wait(full_bar(s), (it / S) & 1, p.err, 13);
-                if (!ok) break;
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t sa = base + s * Cfg::STAGE, sb = sa + Cfg::A_BYTES;
-                const bool seg2 = kb >= nk1;
-                const int kv = seg2 ? p.K2 - (kb - nk1) * BKE : p.K1 - kb * BKE;
-                const int nk16 = kv >= BKE ? BKE / 16 : (kv + 15) / 16;
-                for (int k16 = 0; k16 < nk16; ++k16) {
-                    const uint64_t ad = smem_desc(sa + k16 * 32, 16, 1024);
-                    const uint64_t bd = B_MN ? smem_desc(sb + k16 * 2048, 8192, 1024) : smem_desc(sb + k16 * 32, 16, 1024);
-                    mma_f16_pair(tacc, ad, bd, idesc, (kb > 0 || k16 > 0) ? 1u : 0u);
+            for (int kb = 0; kb < nk; ++kb) {
+                if (!mbar_wait(full_bar(s), ph, p.err, 13)) { ok = false; break; }
+                const uint64_t soff = (uint64_t)((s * Cfg::STAGE) >> 4);
+                const uint64_t ad = a_desc0 + soff, bd = b_desc0 + soff;
+                const int kv = kb >= nk1 ? p.K2 - (kb - nk1) * BKE : BKE;
+                if (kv >= BKE) {
+#pragma unroll
+                    for (int k16 = 0; k16 < BKE / 16; ++k16)
+                        mma_f16_pair(tacc, ad + A_STEP * k16, bd + B_STEP * k16, idesc, (kb | k16) ? 1u : 0u);
+                } else {
+                    for (int k16 = 0; k16 < (kv + 15) / 16; ++k16)
+                        mma_f16_pair(tacc, ad + A_STEP * k16, bd + B_STEP * k16, idesc, (kb | k16) ? 1u : 0u);
                 }
-                mma_commit_pair(map_rank(empty_bar(s), 0));
-                mma_commit_pair(map_rank(empty_bar(s), 1));
+                mma_commit_pair(empty0 + 8 * s);
+                mma_commit_pair(empty1 + 8 * s);
+                if (++s == S) { s = 0; ph ^= 1; }
             }
             if (!ok) break;
             mma_commit_pair(map_rank(tfull_bar(a), 0));
@@ -653,30 +742,42 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc2_kernel(const __grid_cons
     } else if (warp >= 2) {
         // ------------------------------------------------------------ epilogue (both CTAs)
         const int quad = warp & 3;
+        EpiTiles tiles;
+        tiles.o = smem + S * Cfg::STAGE + (warp - 2) * EPI_OUT_BYTES;
+        tiles.x = smem + S * Cfg::STAGE + EPI_WARPS * EPI_OUT_BYTES + (warp - 2) * EPI_AUX_BYTES;
+        tiles.o_s = smem_u32(tiles.o);
+        tiles.x_s = smem_u32(tiles.x);
         const uint32_t leader_tempty0 = map_rank(tempty_bar(0), 0), leader_tempty1 = map_rank(tempty_bar(1), 0);
+        const int mlim = min(p.M, p.mvalid);
+        auto tile_rows = [&](int tl, int& m_base, int& rows, int& n0) {
+            m_base = (tl % num_m2) * 2 * BM + (int)rank * BM + quad * 32;
+            rows = tl < ntiles ? max(0, min(32, mlim - m_base)) : 0;
+            n0 = (tl / num_m2) * BN2;
+        };
+        float4 pre[8];
+        {
+            int mb0, r0, n00;
+            tile_rows(pair, mb0, r0, n00);
+            fetch_input(p, epi_input_kind(p.mode), mb0, r0, n00, lane, pre);
+        }
         int u = 0;
         for (int tile = pair; tile < ntiles; tile += npairs, ++u) {
             const int a = u & 1;
-            const int mb = tile % num_m2, nb = tile / num_m2;
             bool ok = true;
             if (lane == 0) ok = mbar_wait(tfull_bar(a), (u >> 1) & 1, p.err, 14);
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const int m_base = mb * 2 * BM + (int)rank * BM + quad * 32;
-            const int rows = max(0, min(32, min(p.M, p.mvalid) - m_base));
-            float* tf = reinterpret_cast<float*>(smem + S * Cfg::STAGE + (warp - 2) * EPI_WARP_BYTES);
-            bf16* tb = reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(tf) + 32 * EPI_F_LD * 4);
-            for (int c = 0; c < BN2 / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + a * BN2 + c * 32, r);
-                const int n = nb * BN2 + c * 32;
-                if (n < p.nvalid) epilogue_warp32(p, m_base, rows, n, reinterpret_cast<float*>(r), tf, tb, lane);
-            }
+            int m_base, rows, n0, nm, nr, nn;
+            tile_rows(tile, m_base, rows, n0);
+            tile_rows(tile + npairs, nm, nr, nn);
+            epilogue_tile<BN2 / 32>(p, maps, tmem_base + ((uint32_t)(quad * 32) << 16) + a * BN2, m_base, rows, n0, nm,
+                                    nr, nn, tiles, lane, pre);
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(a ? leader_tempty1 : leader_tempty0);
         }
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -721,6 +822,31 @@ void make_map(CUtensorMap* map, const bf16* ptr, long rows, long cols, long ld, 
     if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
 }
 
+// Epilogue store maps: the output as fp32 (box 32 x 32, 128-byte swizzle) or bf16 (box 32 x 32,
+// 64-byte swizzle) over rows min(M, mvalid); the bf16 side output (aux) the same way.
+void make_store_map(CUtensorMap* map, const void* ptr, bool f32, long rows, long cols, long ld) {
+    const int esz = f32 ? 4 : 2;
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * esz) % 16)
+        throw std::runtime_error("gemm_tc: epilogue output not 16-byte aligned");
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * esz)};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                             const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled (store) failed: " + std::to_string((int)r));
+}
+
+void make_epilogue_maps(TcMaps& maps, const GemmArgs& a) {
+    const long rows = a.M < a.mvalid ? a.M : a.mvalid;
+    const bool f32 = a.mode == EPI_STORE_F32 || a.mode == EPI_ACCUM_F32 || a.mode == EPI_RESID_F32;
+    make_store_map(&maps.out, a.out, f32, rows, a.N, a.ldo);
+    if (a.aux) make_store_map(&maps.aux, a.aux, false, rows, a.N, a.ldaux);
+    else maps.aux = maps.out;
+}
+
 int g_num_sms = 0;
 
 template <int BN, bool B_MN>
@@ -739,6 +865,7 @@ void launch_tc(const GemmArgs& a, int* err, cudaStream_t s) {
         maps.a2 = maps.a1;
         maps.b2 = maps.b1;
     }
+    make_epilogue_maps(maps, a);
     TcParams p;
     p.M = a.M; p.N = a.N; p.K1 = a.K1; p.K2 = a.K2;
     p.num_m = (a.M + BM - 1) / BM; p.num_n = a.N / BN;
@@ -777,6 +904,7 @@ void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
         maps.a2 = maps.a1;
         maps.b2 = maps.b1;
     }
+    make_epilogue_maps(maps, a);
     TcParams p;
     p.M = a.M; p.N = a.N; p.K1 = a.K1; p.K2 = a.K2;
     p.num_m = (a.M + BM - 1) / BM; p.num_n = a.N / BN2;
@@ -820,6 +948,8 @@ bool gemm_tc_supported(const GemmArgs& a) {
     if (a.M < BM || a.N % 128 || a.K1 % BKE || a.K1 <= 0 || a.splitk != 1) return false;
     if (a.K2 && (a.K2 % 8 || !a.A2 || !a.B2)) return false;
     if (a.mode == EPI_ATOMIC_F32 || a.nvalid < a.N || a.mvalid < a.M) return false;
+    if ((a.mode == EPI_GELU_BWD || a.mode == EPI_GELU_BWD_D) && a.aux)
+        return false;  // its pre-activation input occupies the side tile
     if (a.ldo % 8 || (a.aux && a.ldaux % 8) || (a.auxin && a.ldauxin % 8) || (a.resid && a.ldr % 4)) return false;
     const uintptr_t al = reinterpret_cast<uintptr_t>(a.out) | reinterpret_cast<uintptr_t>(a.aux) |
                          reinterpret_cast<uintptr_t>(a.auxin) | reinterpret_cast<uintptr_t>(a.resid) |
@@ -834,6 +964,23 @@ bool gemm_tc2_supported(const GemmArgs& a) { return gemm_tc_supported(a) && a.N 
 void gemm_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
     if (a.b_kmajor) launch_tc2<false>(a, err, s);
     else launch_tc2<true>(a, err, s);
+}
+
+void gemm_tc_auto(const GemmArgs& a, int* err, cudaStream_t s) {
+    if (gemm_tc2_supported(a)) {
+        if (!g_num_sms) {
+            int dev = 0;
+            cudaGetDevice(&dev);
+            cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+        }
+        const long t1 = (long)((a.M + BM - 1) / BM) * (a.N / BN2), t2 = (long)((a.M + 2 * BM - 1) / (2 * BM)) * (a.N / BN2);
+        const long r1 = (t1 + g_num_sms - 1) / g_num_sms, r2 = (t2 + g_num_sms / 2 - 1) / (g_num_sms / 2);
+        if (r2 <= r1) {
+            gemm_tc2(a, err, s);
+            return;
+        }
+    }
+    gemm_tc(a, err, s);
 }
 
 void gemm_tc(const GemmArgs& a, int* err, cudaStream_t s) {

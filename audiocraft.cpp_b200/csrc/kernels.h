@@ -29,6 +29,8 @@ enum EpiMode : int {
     EPI_GELU = 5,        // aux_bf16 = acc ; out_bf16 = gelu(acc)
     EPI_GELU_BWD = 6,    // out_bf16 = acc * gelu'(auxin) * colscale2[n]
     EPI_BIAS_BF16 = 7,   // out_bf16 = acc + bias[n]
+    EPI_GELU_D = 8,      // z = bf16(acc): aux_bf16 = gelu'(z) ; out_bf16 = gelu(z)   (z itself not kept)
+    EPI_GELU_BWD_D = 9,  // out_bf16 = acc * auxin(= gelu') * colscale2[n]
 };
 
 struct GemmArgs {
@@ -51,7 +53,7 @@ struct GemmArgs {
     long ldr = 0;
     bf16* aux = nullptr;               // additionally store acc (after colscale) as bf16
     long ldaux = 0;
-    const bf16* auxin = nullptr;       // EPI_GELU_BWD: pre-activation
+    const bf16* auxin = nullptr;       // EPI_GELU_BWD: pre-activation; EPI_GELU_BWD_D: gelu' of it
     long ldauxin = 0;
     const float* colscale2 = nullptr;  // EPI_GELU_BWD: DoRA factor of the producing projection
     const float* bias = nullptr;       // EPI_BIAS_BF16
@@ -66,6 +68,9 @@ bool gemm_tc_supported(const GemmArgs& a);                     // shapes the tcg
 void gemm_tc(const GemmArgs& a, int* err, cudaStream_t s);     // tcgen05 / TMEM / TMA path
 bool gemm_tc2_supported(const GemmArgs& a);                    // 2-CTA (cta_group::2) 256 x 256 tiles
 void gemm_tc2(const GemmArgs& a, int* err, cudaStream_t s);
+// tcgen05 path with the tile shape chosen per problem: 2-CTA 256 x 256 tiles unless they need
+// more waves over the SMs than 1-CTA 128 x 256 tiles
+void gemm_tc_auto(const GemmArgs& a, int* err, cudaStream_t s);
 
 // ---------------------------------------------------------------------------------------
 // attention over token-major q/k/v (head h at columns h*64 .. h*64+63), head_dim 64.
