@@ -100,6 +100,8 @@ SIGNATURES = {
                                   [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "act_gemm_bf16": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                 C.c_int, C.c_int, C.POINTER(C.c_float)]),
+    "act_rank_gemm_bf16": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                     C.c_int, C.c_int, C.c_float, C.c_int, C.c_int, C.POINTER(C.c_float)]),
 }
 
 
@@ -290,6 +292,28 @@ def gemm_bf16(A_bits: np.ndarray, B_bits: np.ndarray, M: int, N: int, K: int, b_
     ms = C.c_float(0.0)
     rc = lib().act_gemm_bf16(device, a.ctypes.data, b.ctypes.data, C_.ctypes.data, M, N, K, int(b_mn_major), path,
                              reps, C.byref(ms))
+    if rc != ACT_OK:
+        raise ActError(rc, lib().act_last_error(None).decode())
+    return (C_, ms.value) if reps > 0 else C_
+
+
+RANK_ACC, RANK_ACC_T, RANK_STORE = 0, 1, 2
+
+
+def rank_gemm_bf16(A_bits: np.ndarray, B_bits: np.ndarray, M: int, K: int, nb: int, a_mn: bool, b_mn: bool,
+                   kind: int, alpha: float = 1.0, C_init: np.ndarray | None = None, splits: int = 0, device: int = 0,
+                   reps: int = 0):
+    """Rank-block product C = alpha A(M x K) B(K x nb) (act_rank_gemm_bf16).  A_bits is [M][K]
+    (a_mn False) or [K][M]; B_bits is [nb][K] (b_mn False) or [K][nb].  kind RANK_ACC returns
+    C_init + C ([M][nb]), RANK_ACC_T returns C_init + C^T ([nb][M]), RANK_STORE returns bf16(C).
+    With reps > 0 returns (C, mean ms per call)."""
+    shape = (nb, M) if kind == RANK_ACC_T else (M, nb)
+    C_ = np.zeros(shape, np.float32) if C_init is None else np.ascontiguousarray(C_init, np.float32).copy()
+    a = np.ascontiguousarray(A_bits, np.uint16)
+    b = np.ascontiguousarray(B_bits, np.uint16)
+    ms = C.c_float(0.0)
+    rc = lib().act_rank_gemm_bf16(device, kind, a.ctypes.data, b.ctypes.data, C_.ctypes.data, M, K, nb, int(a_mn),
+                                  int(b_mn), float(alpha), splits, reps, C.byref(ms))
     if rc != ACT_OK:
         raise ActError(rc, lib().act_last_error(None).decode())
     return (C_, ms.value) if reps > 0 else C_

@@ -241,6 +241,14 @@ struct act_ctx {
         else timed(cls, fl, 0, [&] { gemm(g, stream); });
     }
 
+    // rank-block products: the tcgen05 skinny kernel, or the generic GEMM `fallback` when the
+    // tcgen05 paths are disabled or the operands do not qualify
+    void run_rank(const SkinnyArgs& k, const GemmArgs& fallback) {
+        const double fl = 2.0 * k.M * k.nb * (double)k.K;
+        if (use_tc && skinny_supported(k)) timed(2, fl, 0, [&] { skinny_gemm(k, kerr, stream); });
+        else run_gemm(fallback, 2);
+    }
+
     // kernels record a nonzero code here instead of hanging on a wait that cannot finish
     void check_kernel_error() {
         int e = 0;
@@ -265,7 +273,11 @@ struct act_ctx {
             u.M = (int)rows; u.N = p.RP; u.K1 = p.in;
             u.A1 = X; u.lda1 = p.in; u.B1 = p.A_bf; u.ldb1 = p.in;
             u.mode = EPI_STORE_BF16; u.alpha = p.s; u.out = U; u.ldo = p.RP;
-            run_gemm(u, 2);
+            SkinnyArgs k;  // U = s X A^T
+            k.M = (int)rows; k.K = p.in; k.nb = p.RP;
+            k.A = X; k.lda = p.in; k.B = p.A_bf; k.ldb = p.in;
+            k.kind = SKINNY_STORE; k.alpha = p.s; k.out = U; k.ldo = p.RP;
+            run_rank(k, u);
         }
         e.M = (int)rows; e.N = p.out; e.K1 = p.in;
         e.A1 = X; e.lda1 = p.in; e.B1 = p.W; e.ldb1 = p.in;
@@ -286,21 +298,33 @@ struct act_ctx {
             u.M = (int)rows; u.N = p.RP; u.K1 = p.out;
             u.A1 = dYl; u.lda1 = p.out; u.B1 = p.B_bf; u.ldb1 = p.RP; u.b_kmajor = false;
             u.mode = EPI_STORE_BF16; u.alpha = p.s; u.out = dU; u.ldo = p.RP;
-            run_gemm(u, 2);
+            SkinnyArgs ku;  // dU = s dYl B
+            ku.M = (int)rows; ku.K = p.out; ku.nb = p.RP;
+            ku.A = dYl; ku.lda = p.out; ku.B = p.B_bf; ku.ldb = p.RP; ku.b_mn = true;
+            ku.kind = SKINNY_STORE; ku.alpha = p.s; ku.out = dU; ku.ldo = p.RP;
+            run_rank(ku, u);
             GemmArgs gb;
             gb.M = p.out; gb.N = p.RP; gb.K1 = (int)rows;
             gb.A1 = dYl; gb.lda1 = p.out; gb.a_kmajor = false;
             gb.B1 = U; gb.ldb1 = p.RP; gb.b_kmajor = false;
             gb.mode = EPI_ATOMIC_F32; gb.out = grad + p.offB; gb.ldo = p.r; gb.nvalid = p.r;
             gb.splitk = splitk_for((long)((p.out + 63) / 64), (rows + 63) / 64);
-            run_gemm(gb, 2);
+            SkinnyArgs kb;  // dB += dYl^T U   ([out][r])
+            kb.M = p.out; kb.K = (int)rows; kb.nb = p.r;
+            kb.A = dYl; kb.lda = p.out; kb.a_mn = true; kb.B = U; kb.ldb = p.RP; kb.b_mn = true;
+            kb.kind = SKINNY_ACC; kb.out = grad + p.offB; kb.ldo = p.r;
+            run_rank(kb, gb);
             GemmArgs ga;
             ga.M = p.RP; ga.N = p.in; ga.K1 = (int)rows;
             ga.A1 = dU; ga.lda1 = p.RP; ga.a_kmajor = false;
             ga.B1 = X; ga.ldb1 = p.in; ga.b_kmajor = false;
             ga.mode = EPI_ATOMIC_F32; ga.out = grad + p.offA; ga.ldo = p.in; ga.mvalid = p.r;
             ga.splitk = splitk_for((long)((p.in + 127) / 128), (rows + 63) / 64);
-            run_gemm(ga, 2);
+            SkinnyArgs ka;  // dA += dU^T X   ([r][in], computed as its transpose)
+            ka.M = p.in; ka.K = (int)rows; ka.nb = p.r;
+            ka.A = X; ka.lda = p.in; ka.a_mn = true; ka.B = dU; ka.ldb = p.RP; ka.b_mn = true;
+            ka.kind = SKINNY_ACC_T; ka.out = grad + p.offA; ka.ldo = p.in;
+            run_rank(ka, ga);
         }
         if (!want_dx) return;
         e.M = (int)rows; e.N = p.in; e.K1 = p.out;
@@ -345,7 +369,11 @@ struct act_ctx {
                 a.B1 = p.W; a.ldb1 = p.in; a.b_kmajor = false;
                 a.mode = EPI_ATOMIC_F32; a.out = grad + p.offA; a.ldo = p.in; a.mvalid = p.r;
                 a.splitk = splitk_for((p.in + 127) / 128, (p.out + 63) / 64);
-                run_gemm(a, 2);
+                SkinnyArgs k;  // the same as (W^T BD)^T over the out dimension
+                k.M = p.in; k.K = p.out; k.nb = p.r;
+                k.A = p.W; k.lda = p.in; k.a_mn = true; k.B = p.BD; k.ldb = p.RP; k.b_mn = true;
+                k.kind = SKINNY_ACC_T; k.out = grad + p.offA; k.ldo = p.in;
+                run_rank(k, a);
             }
     }
 
@@ -1506,6 +1534,95 @@ int act_reset_kernel_stats(act_ctx* ctx) {
 }
 
 double act_step_flops(act_ctx* ctx, int n) { return ctx && ctx->finalized ? ctx->step_flops(n) : -1.0; }
+
+int act_rank_gemm_bf16(int device, int kind, const void* A, const void* B, float* C, int M, int K, int nb, int a_mn,
+                       int b_mn, float alpha, int splits, int reps, float* ms_per_call) {
+    void *dA = nullptr, *dB = nullptr, *dC = nullptr;
+    int* derr = nullptr;
+    cudaStream_t st = nullptr;
+    auto cleanup = [&] {
+        if (st) cudaStreamSynchronize(st);
+        cudaFree(dA); cudaFree(dB); cudaFree(dC); cudaFree(derr);
+        if (st) cudaStreamDestroy(st);
+    };
+    try {
+        if (!A || !B || !C || M <= 0 || K <= 0 || nb <= 0 || kind < 0 || kind > 2)
+            throw Error(ACT_ERR_INVALID, "invalid rank-GEMM arguments");
+        CK(cudaSetDevice(device));
+        CK(cudaStreamCreate(&st));
+        const size_t cn = (size_t)M * nb;
+        CK(cudaMalloc(&dA, (size_t)M * K * 2));
+        CK(cudaMalloc(&dB, (size_t)nb * K * 2));
+        CK(cudaMalloc(&dC, cn * 4));
+        CK(cudaMalloc(&derr, sizeof(int)));
+        CK(cudaMemsetAsync(derr, 0, sizeof(int), st));
+        CK(cudaMemcpyAsync(dA, A, (size_t)M * K * 2, cudaMemcpyHostToDevice, st));
+        CK(cudaMemcpyAsync(dB, B, (size_t)nb * K * 2, cudaMemcpyHostToDevice, st));
+        SkinnyArgs g;
+        g.M = M; g.K = K; g.nb = nb;
+        g.A = static_cast<const bf16*>(dA); g.lda = a_mn ? M : K; g.a_mn = a_mn != 0;
+        g.B = static_cast<const bf16*>(dB); g.ldb = b_mn ? nb : K; g.b_mn = b_mn != 0;
+        g.kind = kind; g.alpha = alpha; g.out = dC; g.ldo = kind == SKINNY_ACC_T ? M : nb;
+        g.splits = splits;
+        if (kind == SKINNY_STORE) {
+            CK(cudaMemsetAsync(dC, 0, cn * 4, st));
+        } else {
+            CK(cudaMemcpyAsync(dC, C, cn * 4, cudaMemcpyHostToDevice, st));
+        }
+        if (!skinny_supported(g)) throw Error(ACT_ERR_INVALID, "operands not supported by the rank-GEMM kernel");
+        skinny_gemm(g, derr, st);
+        CK(cudaGetLastError());
+        if (reps > 0 && ms_per_call) {
+            cudaGraph_t graph;
+            cudaGraphExec_t exec;
+            CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+            for (int i = 0; i < reps; ++i) skinny_gemm(g, derr, st);
+            CK(cudaStreamEndCapture(st, &graph));
+            CK(cudaGraphInstantiate(&exec, graph, 0));
+            CK(cudaGraphLaunch(exec, st));
+            cudaEvent_t e0, e1;
+            CK(cudaEventCreate(&e0));
+            CK(cudaEventCreate(&e1));
+            CK(cudaEventRecord(e0, st));
+            CK(cudaGraphLaunch(exec, st));
+            CK(cudaEventRecord(e1, st));
+            CK(cudaEventSynchronize(e1));
+            float ms = 0;
+            CK(cudaEventElapsedTime(&ms, e0, e1));
+            *ms_per_call = ms / reps;
+            cudaEventDestroy(e0);
+            cudaEventDestroy(e1);
+            cudaGraphExecDestroy(exec);
+            cudaGraphDestroy(graph);
+        }
+        if (kind == SKINNY_STORE) {
+            std::vector<uint16_t> hb(cn);
+            // the bf16 result occupies the first cn * 2 bytes of dC (row stride nb)
+            CK(cudaMemcpyAsync(hb.data(), dC, cn * 2, cudaMemcpyDeviceToHost, st));
+            CK(cudaStreamSynchronize(st));
+            for (size_t i = 0; i < cn; ++i) {
+                const uint32_t w = (uint32_t)hb[i] << 16;
+                std::memcpy(&C[i], &w, 4);
+            }
+        } else {
+            CK(cudaMemcpyAsync(C, dC, cn * 4, cudaMemcpyDeviceToHost, st));
+        }
+        int e = 0;
+        CK(cudaMemcpyAsync(&e, derr, sizeof(int), cudaMemcpyDeviceToHost, st));
+        CK(cudaStreamSynchronize(st));
+        if (e) throw Error(ACT_ERR_CUDA, "rank-GEMM kernel reported a timed-out wait (code " + std::to_string(e) + ")");
+        cleanup();
+        return ACT_OK;
+    } catch (const Error& e) {
+        g_error = e.what();
+        cleanup();
+        return e.code;
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        cleanup();
+        return ACT_ERR_CUDA;
+    }
+}
 
 int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path,
                   int reps, float* ms_per_call) {

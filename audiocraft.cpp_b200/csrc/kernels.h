@@ -68,6 +68,27 @@ bool gemm_tc_supported(const GemmArgs& a);                     // shapes the tcg
 void gemm_tc(const GemmArgs& a, int* err, cudaStream_t s);     // tcgen05 / TMEM / TMA path
 bool gemm_tc2_supported(const GemmArgs& a);                    // 2-CTA (cta_group::2) 256 x 256 tiles
 void gemm_tc2(const GemmArgs& a, int* err, cudaStream_t s);
+// Rank-block products on tcgen05 (gemm_skinny.cu): C = alpha * A(M x K) B(K x nb), nb <= 64,
+// split over K across CTAs.  ACC / ACC_T add C (or C^T) into an fp32 gradient with atomics;
+// STORE writes bf16 C, reducing the split-K partials of a tile inside a thread-block cluster.
+enum { SKINNY_ACC = 0, SKINNY_ACC_T = 1, SKINNY_STORE = 2 };
+struct SkinnyArgs {
+    int M = 0, K = 0, nb = 0;
+    const bf16* A = nullptr;  // A(m, k): a_mn ? A[k * lda + m] : A[m * lda + k]
+    long lda = 0;
+    bool a_mn = false;
+    const bf16* B = nullptr;  // B(k, n): b_mn ? B[k * ldb + n] : B[n * ldb + k]
+    long ldb = 0;
+    bool b_mn = false;
+    int kind = SKINNY_ACC;
+    float alpha = 1.0f;
+    void* out = nullptr;      // ACC: out[m * ldo + n]; ACC_T: out[n * ldo + m]; STORE: bf16 out[m * ldo + n]
+    long ldo = 0;
+    int splits = 0;           // 0: about two CTAs per SM (STORE: a power of two <= 8)
+};
+bool skinny_supported(const SkinnyArgs& a);
+void skinny_gemm(const SkinnyArgs& a, int* err, cudaStream_t s);
+
 // tcgen05 path with the tile shape chosen per problem: 2-CTA 256 x 256 tiles unless they need
 // more waves over the SMs than 1-CTA 128 x 256 tiles
 void gemm_tc_auto(const GemmArgs& a, int* err, cudaStream_t s);

@@ -172,6 +172,15 @@ double act_step_flops(act_ctx* ctx, int n);
  * re-run reps times back to back and *ms_per_call receives the mean device time */
 int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path,
                   int reps, float* ms_per_call);
+/* stand-alone rank-block product (tests and the kernel sweep): C = alpha * A(M x K) B(K x nb),
+ * nb <= 64, bf16 A stored [M][K] (a_mn 0) or [K][M] (1), bf16 B stored [nb][K] (b_mn 0) or
+ * [K][nb] (1).  kind 0: C [M][nb] fp32 += result; kind 1: C [nb][M] fp32 += result transposed;
+ * kind 2: C [M][nb] = the result rounded to bf16 (returned as fp32).  splits 0 = automatic.
+ * No reference counterpart: the reference evaluates these products as separate ggml mul_mat
+ * nodes (src/ac/lora.h:34-95).  When reps > 0 the call is re-run reps times (kind 0/1 keep
+ * accumulating) and *ms_per_call receives the mean device time. */
+int act_rank_gemm_bf16(int device, int kind, const void* A, const void* B, float* C, int M, int K, int nb, int a_mn,
+                       int b_mn, float alpha, int splits, int reps, float* ms_per_call);
 /* stand-alone attention forward + backward on host buffers (tests and the kernel sweep):
  * token-major bf16 q [clips*T][H*64], k/v [clips*Tk][H*64], dout like q; scale 1/8 (head_dim 64);
  * nvalid: per-clip valid key count or NULL; causal; zero_key = the prepended zero key of
