@@ -511,9 +511,13 @@ void attn_fwd(const AttnArgs& a, cudaStream_t s) {
     else attn_fwd_kernel<false><<<grid, FWD_WARPS * 32, FWD_SMEM, s>>>(a);
 }
 
-void attn_bwd(const AttnArgs& a, cudaStream_t s) {
+void attn_dvec(const AttnArgs& a, cudaStream_t s) {
     const long threads = (long)a.clips * a.T * a.H * 8;
     attn_dvec_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(a);
+}
+
+void attn_bwd(const AttnArgs& a, cudaStream_t s) {
+    attn_dvec(a, s);
     static bool configured = false;
     if (!configured) {
         set_smem(attn_bwd_kernel<true>, BWD_SMEM);

@@ -398,7 +398,10 @@ struct act_ctx {
         sa.T = T; sa.Tk = T; sa.H = H; sa.clips = n; sa.causal = dit ? 0 : 1; sa.zero_key = dit ? md.add_zero_attn : 0;
         sa.rope = dit ? rope : nullptr; sa.rope_load = 0; sa.scale = 1.0f / std::sqrt((float)md.head_dim);
         sa.o = y.o1; sa.ldo = D; sa.lse = y.lse1;
-        timed(1, attn_flops(n, T, true), 0, [&] { attn_fwd(sa, stream); });
+        timed(1, attn_flops(n, T, true), 0, [&] {
+            if (use_tc && attn_fwd_tc_supported(sa)) attn_fwd_tc(sa, kerr, stream);
+            else attn_fwd(sa, stream);
+        });
         {
             GemmArgs e; e.mode = EPI_RESID_F32; e.out = y.xmid; e.ldo = D; e.resid = y.xin; e.ldr = D;
             if (y.p[1].dora) { e.aux = y.Yaux[1]; e.ldaux = D; }
@@ -490,7 +493,8 @@ struct act_ctx {
         sa.kscale = y.p[0].dora ? y.p[0].g + D : nullptr; sa.vscale = y.p[0].dora ? y.p[0].g + 2 * D : nullptr;
         timed(1, 2 * attn_flops(n, T, true), 0, [&] {
             CK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * D, stream));
-            attn_bwd(sa, stream);
+            if (use_tc && attn_bwd_tc_supported(sa)) attn_bwd_tc(sa, kerr, stream);
+            else attn_bwd(sa, stream);
             attn_dq_finish(sa, dqkv, 3 * D, y.p[0].dora ? y.p[0].g : nullptr, stream);
         });
         {
@@ -1744,14 +1748,17 @@ int act_attention(int device, const void* q, const void* k, const void* v, const
         a.nvalid = nvalid ? static_cast<const int*>(up(nvalid, clips * 4)) : nullptr;
         a.causal = causal; a.zero_key = zero_key;
         a.rope = rope ? static_cast<const float*>(up(rope, (size_t)T * 64 * 4)) : nullptr;
-        a.rope_load = 1;
+        a.rope_load = rope ? 1 : 0;  // unrotated inputs: rotate while staging
         if (rope && Tk > T) throw Error(ACT_ERR_INVALID, "RoPE needs Tk <= T");
         a.scale = 0.125f;
         a.o = static_cast<bf16*>(up(nullptr, rq * D * 2));
         a.ldo = D;
         a.lse = static_cast<float*>(up(nullptr, rq * H * 4));
+        int* derr = static_cast<int*>(up(nullptr, sizeof(int)));
+        const bool tc_fwd = attn_fwd_tc_supported(a) && !std::getenv("ACTRAIN_ATTN_MMA");
         CK(cudaEventRecord(ev[0], st));
-        attn_fwd(a, st);
+        if (tc_fwd) attn_fwd_tc(a, derr, st);
+        else attn_fwd(a, st);
         CK(cudaEventRecord(ev[1], st));
         CK(cudaGetLastError());
         const bool bwd = dout && dq && dk && dv;
@@ -1767,7 +1774,8 @@ int act_attention(int device, const void* q, const void* k, const void* v, const
             a.lddk = a.lddv = D;
             ddq = static_cast<bf16*>(up(nullptr, rq * D * 2));
             CK(cudaEventRecord(ev[2], st));
-            attn_bwd(a, st);
+            if (attn_bwd_tc_supported(a) && !std::getenv("ACTRAIN_ATTN_MMA")) attn_bwd_tc(a, derr, st);
+            else attn_bwd(a, st);
             attn_dq_finish(a, ddq, D, nullptr, st);
             CK(cudaEventRecord(ev[3], st));
             CK(cudaGetLastError());
@@ -1779,7 +1787,10 @@ int act_attention(int device, const void* q, const void* k, const void* v, const
             CK(cudaMemcpyAsync(dk, a.dk, rk * D * 2, cudaMemcpyDeviceToHost, st));
             CK(cudaMemcpyAsync(dv, a.dv, rk * D * 2, cudaMemcpyDeviceToHost, st));
         }
+        int e = 0;
+        CK(cudaMemcpyAsync(&e, derr, sizeof(int), cudaMemcpyDeviceToHost, st));
         CK(cudaStreamSynchronize(st));
+        if (e) throw Error(ACT_ERR_CUDA, "attention kernel reported a timed-out wait (code " + std::to_string(e) + ")");
         if (ms_fwd) CK(cudaEventElapsedTime(ms_fwd, ev[0], ev[1]));
         if (ms_bwd) {
             *ms_bwd = 0.f;

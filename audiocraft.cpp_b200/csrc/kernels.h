@@ -128,7 +128,15 @@ struct AttnArgs {
 };
 
 void attn_fwd(const AttnArgs& a, cudaStream_t s);
+// the same forward on tcgen05 (attention_tc.cu): pre-rotated q/k (rope_load 0), Tk >= 64
+bool attn_fwd_tc_supported(const AttnArgs& a);
+void attn_fwd_tc(const AttnArgs& a, int* err, cudaStream_t s);
 void attn_bwd(const AttnArgs& a, cudaStream_t s);  // computes dvec itself
+void attn_dvec(const AttnArgs& a, cudaStream_t s);  // dvec = rowsum(dO * O)
+// the same backward on tcgen05 (attention_tc.cu): pre-rotated q/k, Tk >= 128; computes dvec itself
+// and adds into dq_acc (zeroed by the caller) like attn_bwd
+bool attn_bwd_tc_supported(const AttnArgs& a);
+void attn_bwd_tc(const AttnArgs& a, int* err, cudaStream_t s);
 // dq (bf16) = unrotate(dq_acc) * qscale[col]
 void attn_dq_finish(const AttnArgs& a, bf16* dq, long lddq, const float* qscale, cudaStream_t s);
 

@@ -78,6 +78,9 @@ CASES = {
     "self_zero_key_rope": dict(clips=2, T=150, Tk=150, H=2, nvalid=None, causal=False, zero_key=True, rope=True),
     "cross_masked": dict(clips=3, T=90, Tk=16, H=2, nvalid=[16, 5, 0], causal=False, zero_key=True, rope=False),
     "causal": dict(clips=2, T=130, Tk=130, H=3, nvalid=None, causal=True, zero_key=False, rope=False),
+    # pre-rotated inputs at the benchmark's clip length: the tcgen05 forward
+    "self_zero_key_750": dict(clips=2, T=750, Tk=750, H=2, nvalid=None, causal=False, zero_key=True, rope=False),
+    "causal_333": dict(clips=1, T=333, Tk=333, H=2, nvalid=None, causal=True, zero_key=False, rope=False),
 }
 
 
