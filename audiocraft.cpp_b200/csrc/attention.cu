@@ -79,6 +79,8 @@ constexpr int FWD_SMEM = (FWD_BQ + 4 * BKV) * LDS * 2;
 
 template <bool ROPE_LOAD>
 __global__ void __launch_bounds__(FWD_WARPS * 32) attn_fwd_kernel(const AttnArgs a) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ __align__(16) unsigned char smraw[];
     bf16* sQ = reinterpret_cast<bf16*>(smraw);
     bf16* sK = sQ + FWD_BQ * LDS;  // [2][64][LDS]
@@ -235,6 +237,8 @@ __global__ void __launch_bounds__(FWD_WARPS * 32) attn_fwd_kernel(const AttnArgs
 // ---------------------------------------------------------------------------------------
 // D[b][h][i] = sum_d dO * O : 8 threads per (row, head), one 16-byte load each.
 __global__ void attn_dvec_kernel(const AttnArgs a) {
+    pdl_wait();
+    pdl_trigger();
     const long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
     const long rows = (long)a.clips * a.T;
     const long per_row = (long)a.H * 8;
@@ -270,6 +274,8 @@ constexpr int BWD_SMEM = (2 * BKV + 4 * BWD_BQ + BKV) * LDS * 2 + 4 * BWD_BQ * 4
 
 template <bool ROPE_LOAD>
 __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ __align__(16) unsigned char smraw[];
     bf16* sK = reinterpret_cast<bf16*>(smraw);
     bf16* sV = sK + BKV * LDS;
@@ -468,6 +474,8 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
 
 // dq (bf16) = unrotate(dq_acc) * qscale : 4 floats per thread
 __global__ void attn_dq_finish_kernel(const AttnArgs a, bf16* dq, long lddq, const float* qscale) {
+    pdl_wait();
+    pdl_trigger();
     const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
     const long rows = (long)a.clips * a.T;
     const int quads = a.H * HD / 4;
@@ -507,13 +515,13 @@ void attn_fwd(const AttnArgs& a, cudaStream_t s) {
         configured = true;
     }
     dim3 grid((a.T + FWD_BQ - 1) / FWD_BQ, a.H, a.clips);
-    if (a.rope && a.rope_load) attn_fwd_kernel<true><<<grid, FWD_WARPS * 32, FWD_SMEM, s>>>(a);
-    else attn_fwd_kernel<false><<<grid, FWD_WARPS * 32, FWD_SMEM, s>>>(a);
+    if (a.rope && a.rope_load) launch_pdl(attn_fwd_kernel<true>, grid, dim3(FWD_WARPS * 32), FWD_SMEM, s, a);
+    else launch_pdl(attn_fwd_kernel<false>, grid, dim3(FWD_WARPS * 32), FWD_SMEM, s, a);
 }
 
 void attn_dvec(const AttnArgs& a, cudaStream_t s) {
     const long threads = (long)a.clips * a.T * a.H * 8;
-    attn_dvec_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(a);
+    launch_pdl(attn_dvec_kernel, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, s, a);
 }
 
 void attn_bwd(const AttnArgs& a, cudaStream_t s) {
@@ -525,13 +533,13 @@ void attn_bwd(const AttnArgs& a, cudaStream_t s) {
         configured = true;
     }
     dim3 grid((a.Tk + BKV - 1) / BKV, a.H, a.clips);
-    if (a.rope && a.rope_load) attn_bwd_kernel<true><<<grid, 128, BWD_SMEM, s>>>(a);
-    else attn_bwd_kernel<false><<<grid, 128, BWD_SMEM, s>>>(a);
+    if (a.rope && a.rope_load) launch_pdl(attn_bwd_kernel<true>, grid, dim3(128), BWD_SMEM, s, a);
+    else launch_pdl(attn_bwd_kernel<false>, grid, dim3(128), BWD_SMEM, s, a);
 }
 
 void attn_dq_finish(const AttnArgs& a, bf16* dq, long lddq, const float* qscale, cudaStream_t s) {
     const long n = (long)a.clips * a.T * a.H * HD / 4;
-    attn_dq_finish_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(a, dq, lddq, qscale);
+    launch_pdl(attn_dq_finish_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, a, dq, lddq, qscale);
 }
 
 }  // namespace act

@@ -147,6 +147,8 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_fwd_tc_kernel(const __grid
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
     const uint32_t tS = tmem, tO = tmem + 2 * AT_BK;  // S buffer t at tS + t * AT_BK
+    pdl_wait();
+    pdl_trigger();
 
     if (warp == 0 && lane == 0) {
         // ------------------------------------------------------------ TMA producer
@@ -384,6 +386,8 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
     const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 320, tdQ = tmem + 384;
+    pdl_wait();
+    pdl_trigger();
 
     if (warp == 0 && lane == 0) {
         // ------------------------------------------------------------ TMA producer
@@ -676,8 +680,18 @@ void attn_fwd_tc(const AttnArgs& a, int* err, cudaStream_t s) {
         cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
         configured = true;
     }
-    dim3 grid((a.T + AT_BQ - 1) / AT_BQ, a.H, a.clips);
-    attn_fwd_tc_kernel<<<grid, AT_THREADS, AT_SMEM, s>>>(maps, a, err);
+    {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((a.T + AT_BQ - 1) / AT_BQ, a.H, a.clips);
+        cfg.blockDim = dim3(AT_THREADS, 1, 1);
+        cfg.dynamicSmemBytes = AT_SMEM;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        pdl_attr(attr[0]);
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaLaunchKernelEx(&cfg, attn_fwd_tc_kernel, maps, a, err);
+    }
 }
 
 }  // namespace act
@@ -706,8 +720,18 @@ void attn_bwd_tc(const AttnArgs& a, int* err, cudaStream_t s) {
         cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AB_SMEM);
         configured = true;
     }
-    dim3 grid((a.Tk + AB_BK - 1) / AB_BK, a.H, a.clips);
-    attn_bwd_tc_kernel<<<grid, AB_THREADS, AB_SMEM, s>>>(maps, a, err);
+    {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((a.Tk + AB_BK - 1) / AB_BK, a.H, a.clips);
+        cfg.blockDim = dim3(AB_THREADS, 1, 1);
+        cfg.dynamicSmemBytes = AB_SMEM;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        pdl_attr(attr[0]);
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaLaunchKernelEx(&cfg, attn_bwd_tc_kernel, maps, a, err);
+    }
 }
 
 }  // namespace act

@@ -104,4 +104,33 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+
+// ---------------------------------------------------------------------------------------
+// Programmatic dependent launch: a kernel launched with the programmatic-serialization attribute
+// may start while its predecessor drains; it runs its prologue (barriers, TMEM, descriptors),
+// then waits here before touching memory the predecessor writes.  Every kernel lets its
+// successor start early (the successor still waits for this grid's completion).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+inline void pdl_attr(cudaLaunchAttribute& at) {
+    at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at.val.programmaticStreamSerializationAllowed = 1;
+}
+
+// Launch a kernel that starts with pdl_wait() with the programmatic-serialization attribute.
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    pdl_attr(attr[0]);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 }  // namespace act

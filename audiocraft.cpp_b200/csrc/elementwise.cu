@@ -16,6 +16,8 @@ __global__ void ln_fwd_kernel(const float* __restrict__ x, const float* __restri
                               const float* __restrict__ b, const float* __restrict__ add,
                               int rows_per_clip, bf16* __restrict__ y, float* __restrict__ mean,
                               float* __restrict__ rstd, int rows, int D, float eps) {
+    pdl_wait();
+    pdl_trigger();
     const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -69,6 +71,8 @@ __global__ void ln_bwd_kernel(const float* __restrict__ dy, const float* __restr
                               const float* __restrict__ rstd, float* __restrict__ dx, int accumulate,
                               const float* __restrict__ extra, bf16* __restrict__ dx_bf,
                               const float* __restrict__ colscale, int rows, int D) {
+    pdl_wait();
+    pdl_trigger();
     const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -118,6 +122,8 @@ __global__ void ln_bwd_kernel(const float* __restrict__ dy, const float* __restr
 
 __global__ void resid_bf16_kernel(float* __restrict__ x, const float* __restrict__ extra,
                                   bf16* __restrict__ dst, const float* __restrict__ colscale, long n4, int D) {
+    pdl_wait();
+    pdl_trigger();
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n4) return;
     float4 v = reinterpret_cast<float4*>(x)[i];
@@ -436,22 +442,22 @@ inline unsigned blocks_for(long n, int t) { return (unsigned)((n + t - 1) / t); 
 
 #define LN_DISPATCH(KERNEL, ...)                                                                  \
     switch (D / 128) {                                                                            \
-        case 1: KERNEL<1><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
-        case 2: KERNEL<2><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
-        case 3: KERNEL<3><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
-        case 4: KERNEL<4><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
-        case 5: KERNEL<5><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
-        case 6: KERNEL<6><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
-        case 7: KERNEL<7><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
-        case 8: KERNEL<8><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
-        case 9: KERNEL<9><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
-        case 10: KERNEL<10><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
-        case 11: KERNEL<11><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
-        case 12: KERNEL<12><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
-        case 13: KERNEL<13><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
-        case 14: KERNEL<14><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
-        case 15: KERNEL<15><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
-        case 16: KERNEL<16><<<blocks_for(rows, 8), 256, 0, s>>>(__VA_ARGS__); break;                 \
+        case 1: launch_pdl(KERNEL<1>, dim3(blocks_for(rows, 8)), dim3(256), 0, s, __VA_ARGS__); break; \
+        case 2: launch_pdl(KERNEL<2>, dim3(blocks_for(rows, 8)), dim3(256), 0, s, __VA_ARGS__); break; \
+        case 3: launch_pdl(KERNEL<3>, dim3(blocks_for(rows, 8)), dim3(256), 0, s, __VA_ARGS__); break; \
+        case 4: launch_pdl(KERNEL<4>, dim3(blocks_for(rows, 8)), dim3(256), 0, s, __VA_ARGS__); break; \
+        case 5: launch_pdl(KERNEL<5>, dim3(blocks_for(rows, 8)), dim3(256), 0, s, __VA_ARGS__); break; \
+        case 6: launch_pdl(KERNEL<6>, dim3(blocks_for(rows, 8)), dim3(256), 0, s, __VA_ARGS__); break; \
+        case 7: launch_pdl(KERNEL<7>, dim3(blocks_for(rows, 8)), dim3(256), 0, s, __VA_ARGS__); break; \
+        case 8: launch_pdl(KERNEL<8>, dim3(blocks_for(rows, 8)), dim3(256), 0, s, __VA_ARGS__); break; \
+        case 9: launch_pdl(KERNEL<9>, dim3(blocks_for(rows, 8)), dim3(256), 0, s, __VA_ARGS__); break; \
+        case 10: launch_pdl(KERNEL<10>, dim3(blocks_for(rows, 8)), dim3(256), 0, s, __VA_ARGS__); break; \
+        case 11: launch_pdl(KERNEL<11>, dim3(blocks_for(rows, 8)), dim3(256), 0, s, __VA_ARGS__); break; \
+        case 12: launch_pdl(KERNEL<12>, dim3(blocks_for(rows, 8)), dim3(256), 0, s, __VA_ARGS__); break; \
+        case 13: launch_pdl(KERNEL<13>, dim3(blocks_for(rows, 8)), dim3(256), 0, s, __VA_ARGS__); break; \
+        case 14: launch_pdl(KERNEL<14>, dim3(blocks_for(rows, 8)), dim3(256), 0, s, __VA_ARGS__); break; \
+        case 15: launch_pdl(KERNEL<15>, dim3(blocks_for(rows, 8)), dim3(256), 0, s, __VA_ARGS__); break; \
+        case 16: launch_pdl(KERNEL<16>, dim3(blocks_for(rows, 8)), dim3(256), 0, s, __VA_ARGS__); break; \
         default: break; /* rejected at context creation: D must be 128..2048, a multiple of 128 */ \
     }
 
@@ -469,7 +475,7 @@ void layernorm_bwd(const float* dy, const float* x, const float* w, const float*
 void residual_to_bf16(float* x, const float* extra, bf16* dst, const float* colscale, int rows, int D,
                       cudaStream_t s) {
     const long n4 = (long)rows * D / 4;
-    resid_bf16_kernel<<<blocks_for(n4, 256), 256, 0, s>>>(x, extra, dst, colscale, n4, D);
+    launch_pdl(resid_bf16_kernel, dim3(blocks_for(n4, 256)), dim3(256), 0, s, x, extra, dst, colscale, n4, D);
 }
 
 void f32_to_bf16(const float* x, bf16* y, long n, cudaStream_t s) {

@@ -27,6 +27,8 @@ struct Smem {
 template <int BM, int BN, int WM_, int WN_, bool AK, bool BKM, int BK, int STAGES>
 __global__ void __launch_bounds__(WM_* WN_ * 32)
 gemm_mma_kernel(const GemmArgs p) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int NT = WM_ * WN_ * 32;
     constexpr int WTM = BM / WM_, WTN = BN / WN_;
     constexpr int MI = WTM / 16, NI = WTN / 8;
@@ -257,7 +259,7 @@ void launch(const GemmArgs& a, cudaStream_t s) {
         configured = true;
     }
     dim3 grid((a.N + BN - 1) / BN, (a.M + BM - 1) / BM, a.splitk);
-    kern<<<grid, WM_ * WN_ * 32, S::BYTES, s>>>(a);
+    launch_pdl(kern, grid, dim3(WM_ * WN_ * 32), S::BYTES, s, a);
 }
 
 template <bool AK, bool BKM>

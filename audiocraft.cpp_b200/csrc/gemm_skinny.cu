@@ -122,6 +122,8 @@ __global__ void __launch_bounds__(SK_THREADS, 2) skinny_kernel(const __grid_cons
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();
+    pdl_trigger();
 
     if (warp == 0 && lane == 0) {
         // ------------------------------------------------------------ TMA producer
@@ -299,13 +301,14 @@ void skinny_gemm(const SkinnyArgs& a, int* err, cudaStream_t s) {
     cfg.blockDim = dim3(SK_THREADS, 1, 1);
     cfg.dynamicSmemBytes = SK_SMEM;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
     attr[0].val.clusterDim.y = a.kind == SKINNY_STORE ? splits : 1;
     attr[0].val.clusterDim.z = 1;
+    pdl_attr(attr[1]);
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     cudaLaunchKernelEx(&cfg, skinny_kernel, maps, p);
 }
 

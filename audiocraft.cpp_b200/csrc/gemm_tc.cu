@@ -346,6 +346,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(const __grid_const
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();
+    pdl_trigger();
 
     const int nk1 = (p.K1 + BKE - 1) / BKE, nk2 = (p.K2 + BKE - 1) / BKE, nk = nk1 + nk2;
     const int ntiles = p.num_m * p.num_n;
@@ -575,6 +577,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc2_kernel(const __grid_cons
     cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();
+    pdl_trigger();
 
     const int nk1 = (p.K1 + BKE - 1) / BKE, nk2 = (p.K2 + BKE - 1) / BKE, nk = nk1 + nk2;
     const int num_m2 = (p.M + 2 * BM - 1) / (2 * BM);
@@ -796,7 +800,16 @@ void launch_tc(const GemmArgs& a, int* err, cudaStream_t s) {
     }
     const int tiles = p.num_m * p.num_n;
     const int grid = tiles < g_num_sms ? tiles : g_num_sms;
-    kern<<<grid, NTHREADS, Cfg::SMEM, s>>>(maps, p);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(NTHREADS, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    pdl_attr(attr[0]);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, maps, p);
 }
 
 template <bool B_MN>
@@ -841,13 +854,14 @@ void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
     cfg.blockDim = dim3(NTHREADS, 1, 1);
     cfg.dynamicSmemBytes = Cfg::SMEM;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    pdl_attr(attr[1]);
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     cudaLaunchKernelEx(&cfg, kern, maps, p);
 }
 

@@ -105,6 +105,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
 
 }  // namespace tc
 
+
 // Host: cuTensorMapEncodeTiled through the driver entry point (no libcuda link dependency).
 // 2D bf16 row-major tensor [rows][cols] with row stride ld (elements); box {box_cols, box_rows},
 // 128-byte swizzle.
