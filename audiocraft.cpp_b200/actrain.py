@@ -100,6 +100,7 @@ SIGNATURES = {
                                   [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "act_gemm_bf16": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                 C.c_int, C.c_int, C.POINTER(C.c_float)]),
+    "act_gelu_bf16": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int]),
     "act_rank_gemm_bf16": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                      C.c_int, C.c_int, C.c_float, C.c_int, C.c_int, C.POINTER(C.c_float)]),
 }
@@ -295,6 +296,17 @@ def gemm_bf16(A_bits: np.ndarray, B_bits: np.ndarray, M: int, N: int, K: int, b_
     if rc != ACT_OK:
         raise ActError(rc, lib().act_last_error(None).decode())
     return (C_, ms.value) if reps > 0 else C_
+
+
+def gelu_bf16(z_bits: np.ndarray, direct: bool, device: int = 0):
+    """act_gelu_bf16: (gelu bits, gelu' bits) of bf16 inputs, by the A&S evaluation or the table."""
+    z = np.ascontiguousarray(z_bits, np.uint16)
+    g = np.zeros_like(z)
+    dg = np.zeros_like(z)
+    rc = lib().act_gelu_bf16(device, z.ctypes.data, g.ctypes.data, dg.ctypes.data, z.size, int(direct))
+    if rc != ACT_OK:
+        raise ActError(rc, lib().act_last_error(None).decode())
+    return g, dg
 
 
 RANK_ACC, RANK_ACC_T, RANK_STORE = 0, 1, 2

@@ -56,6 +56,40 @@ __device__ __forceinline__ void gelu_as_pair(float x, float& g, float& dg) {
     dg = half_cdf + x * 0.5f * derf * 0.7071067811865475f;
 }
 
+// GELU of a bf16 pre-activation by table.  z takes finitely many values: for |z| in
+// [2^-16, 16) the table holds bf16(gelu_as(z)) | bf16(gelu_as_grad(z)) << 16 for every bf16 z
+// (20 exponents x 128 mantissas x 2 signs), computed with gelu_as_pair; below 2^-16 both round
+// to z / 2 and 0.5 exactly, and from 16 up the A&S exponential underflows, giving z and 1 (or
+// -0 and -0 for negative z).  Results equal the direct evaluation bit for bit.
+constexpr int GELU_TAB_E0 = 111;  // biased exponent of 2^-16
+constexpr int GELU_TAB_NE = 20;
+constexpr int GELU_TAB_ENTRIES = 2 * GELU_TAB_NE * 128;
+
+__device__ __forceinline__ uint32_t gelu_tab_entry(int i) {
+    const uint32_t neg = i / (GELU_TAB_NE * 128), r = i % (GELU_TAB_NE * 128);
+    const uint32_t bits = (neg << 15) | ((GELU_TAB_E0 + (r >> 7)) << 7) | (r & 127);
+    float g, dg;
+    gelu_as_pair(__uint_as_float(bits << 16), g, dg);
+    const __nv_bfloat162 v = __floats2bfloat162_rn(g, dg);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// u: bf16 bits of z -> bf16 bits of gelu(z) | bf16 bits of gelu'(z) << 16
+__device__ __forceinline__ uint32_t gelu_tab_lookup(const uint32_t* tab, uint32_t u) {
+    const int e = (int)((u >> 7) & 0xFF);
+    const uint32_t neg = u >> 15;
+    const int idx = min(max(((e - GELU_TAB_E0) << 7) | (int)(u & 127), 0), GELU_TAB_NE * 128 - 1) +
+                    (int)neg * (GELU_TAB_NE * 128);
+    uint32_t t = tab[idx];
+    if (e < GELU_TAB_E0) {
+        const __nv_bfloat16 h = __float2bfloat16(__uint_as_float(u << 16) * 0.5f);
+        t = (uint32_t)(*reinterpret_cast<const unsigned short*>(&h)) | (0x3F00u << 16);
+    } else if (e >= GELU_TAB_E0 + GELU_TAB_NE) {
+        t = neg ? 0x80008000u : (u | (0x3F80u << 16));
+    }
+    return t;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -1,6 +1,8 @@
 // elementwise.cu -- row / element kernels of the adapter training step (HBM-bound work).
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -436,6 +438,54 @@ __global__ void mg_ce_kernel(const float* __restrict__ logits, int card, const i
     if (threadIdx.x == 0) atomicAdd(loss_acc + row / rows_per_seq, (mx + logf(sm) - lg[tgt]) * inv_nsel);
 }
 
+// the GELU table (built once per context)
+__global__ void gelu_table_kernel(uint32_t* tab) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < GELU_TAB_ENTRIES) tab[i] = gelu_tab_entry(i);
+}
+
+// gact = gelu(z); with store_grad, z is overwritten by gelu'(z).  8 bf16 per thread and step.
+__global__ void __launch_bounds__(256) gelu_fwd_kernel(const uint32_t* __restrict__ tab_g, bf16* __restrict__ z,
+                                                       bf16* __restrict__ gact, long n8, int store_grad) {
+    __shared__ __align__(16) uint32_t tab[GELU_TAB_ENTRIES];
+    pdl_wait();
+    pdl_trigger();
+    for (int i = threadIdx.x; i < GELU_TAB_ENTRIES / 4; i += blockDim.x)
+        reinterpret_cast<uint4*>(tab)[i] = reinterpret_cast<const uint4*>(tab_g)[i];
+    __syncthreads();
+    for (long c = (long)blockIdx.x * blockDim.x + threadIdx.x; c < n8; c += (long)gridDim.x * blockDim.x) {
+        const uint4 zz = reinterpret_cast<const uint4*>(z)[c];
+        const uint32_t w[4] = {zz.x, zz.y, zz.z, zz.w};
+        uint32_t g[4], d[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t lo = gelu_tab_lookup(tab, w[j] & 0xFFFFu), hi = gelu_tab_lookup(tab, w[j] >> 16);
+            g[j] = (lo & 0xFFFFu) | (hi << 16);
+            d[j] = (lo >> 16) | (hi & 0xFFFF0000u);
+        }
+        reinterpret_cast<uint4*>(gact)[c] = make_uint4(g[0], g[1], g[2], g[3]);
+        if (store_grad) reinterpret_cast<uint4*>(z)[c] = make_uint4(d[0], d[1], d[2], d[3]);
+    }
+}
+
+// stand-alone check: gelu / gelu' of bf16 inputs, directly (A&S evaluation) or by table
+__global__ void gelu_check_kernel(const uint32_t* tab, const uint16_t* z, uint16_t* g, uint16_t* dg, long n,
+                                  int direct) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    uint32_t t;
+    if (direct) {
+        float gv, dv;
+        gelu_as_pair(__uint_as_float((uint32_t)z[i] << 16), gv, dv);
+        const __nv_bfloat162 v = __floats2bfloat162_rn(gv, dv);
+        t = *reinterpret_cast<const uint32_t*>(&v);
+    } else {
+        t = gelu_tab_lookup(tab, z[i]);
+    }
+    g[i] = (uint16_t)(t & 0xFFFFu);
+    dg[i] = (uint16_t)(t >> 16);
+}
+
 inline unsigned blocks_for(long n, int t) { return (unsigned)((n + t - 1) / t); }
 
 }  // namespace
@@ -476,6 +526,20 @@ void residual_to_bf16(float* x, const float* extra, bf16* dst, const float* cols
                       cudaStream_t s) {
     const long n4 = (long)rows * D / 4;
     launch_pdl(resid_bf16_kernel, dim3(blocks_for(n4, 256)), dim3(256), 0, s, x, extra, dst, colscale, n4, D);
+}
+
+void gelu_table_init(uint32_t* tab, cudaStream_t s) {
+    gelu_table_kernel<<<blocks_for(GELU_TAB_ENTRIES, 256), 256, 0, s>>>(tab);
+}
+
+void gelu_check(const uint32_t* tab, const uint16_t* z, uint16_t* g, uint16_t* dg, long n, int direct, cudaStream_t s) {
+    gelu_check_kernel<<<blocks_for(n, 256), 256, 0, s>>>(tab, z, g, dg, n, direct);
+}
+
+void gelu_fwd(const uint32_t* tab, bf16* z, bf16* gact, long n, int store_grad, cudaStream_t s) {
+    const long n8 = n / 8;
+    long blocks = std::min<long>(blocks_for(n8, 256), 148L * 8);
+    launch_pdl(gelu_fwd_kernel, dim3((unsigned)blocks), dim3(256), 0, s, tab, z, gact, n8, store_grad);
 }
 
 void f32_to_bf16(const float* x, bf16* y, long n, cudaStream_t s) {

@@ -125,6 +125,7 @@ struct act_ctx {
     std::vector<bf16*> skip;
     std::vector<float> rope_ff;
     float* rope = nullptr;
+    uint32_t* gelu_tab = nullptr;  // bf16 GELU / GELU' table for the feed-forward activation
     // MusicGen globals
     std::vector<float*> emb;
     float** emb_dev = nullptr;
@@ -429,9 +430,17 @@ struct act_ctx {
         // feed-forward (no timestep)
         timed(2, 0, 0, [&] { layernorm_fwd(y.xmid2, y.norm[4], y.norm[5], nullptr, T, y.f, y.mu[2], y.rs[2], (int)rows, D, eps, stream); });
         {
-            // without DoRA on ff.0 the backward needs only gelu'(z): store that instead of z
-            GemmArgs e; e.mode = y.p[5].dora ? EPI_GELU : EPI_GELU_D; e.out = y.gact; e.ldo = F; e.aux = y.z; e.ldaux = F;
-            proj_fwd(y.p[5], y.f, rows, y.U[5], e);
+            // ff.0 stores its pre-activation z; the activation runs by table as its own pass
+            // (the GEMM epilogue is then a plain store).  Without DoRA on ff.0 the backward needs
+            // only gelu'(z), which replaces z in place.
+            if (y.p[5].dora) {
+                GemmArgs e; e.mode = EPI_GELU; e.out = y.gact; e.ldo = F; e.aux = y.z; e.ldaux = F;
+                proj_fwd(y.p[5], y.f, rows, y.U[5], e);
+            } else {
+                GemmArgs e; e.mode = EPI_STORE_BF16; e.out = y.z; e.ldo = F;
+                proj_fwd(y.p[5], y.f, rows, y.U[5], e);
+                timed(2, 0, 6.0 * rows * F, [&] { gelu_fwd(gelu_tab, y.z, y.gact, rows * F, 1, stream); });
+            }
             GemmArgs o; o.mode = EPI_RESID_F32; o.out = y.xout; o.ldo = D; o.resid = y.xmid2; o.ldr = D;
             if (y.p[6].dora) { o.aux = y.Yaux[6]; o.ldaux = D; }
             proj_fwd(y.p[6], y.gact, rows, y.U[6], o);
@@ -1097,6 +1106,8 @@ struct act_ctx {
         jobs_dev = dalloc<CopyJob>(std::max(njobs, 1));
         if (njobs) CK(cudaMemcpyAsync(jobs_dev, jobs.data(), sizeof(CopyJob) * njobs, cudaMemcpyHostToDevice, stream));
         // rope table (src/ac/transformer.h:55-61 with freq_base 1): theta = pos / ff[i]
+        gelu_tab = dalloc<uint32_t>(GELU_TABLE_WORDS);
+        gelu_table_init(gelu_tab, stream);
         if (mf) {
             if ((int)rope_ff.size() != md.head_dim / 2) throw Error(ACT_ERR_INVALID, "rope_freq_factors size mismatch");
             std::vector<float> tab((size_t)T * 64);
@@ -1539,6 +1550,43 @@ int act_reset_kernel_stats(act_ctx* ctx) {
 
 double act_step_flops(act_ctx* ctx, int n) { return ctx && ctx->finalized ? ctx->step_flops(n) : -1.0; }
 
+int act_gelu_bf16(int device, const uint16_t* z, uint16_t* g, uint16_t* dg, int64_t n, int direct) {
+    void *dz = nullptr, *dgo = nullptr, *ddg = nullptr, *tab = nullptr;
+    cudaStream_t st = nullptr;
+    auto cleanup = [&] {
+        if (st) cudaStreamSynchronize(st);
+        cudaFree(dz); cudaFree(dgo); cudaFree(ddg); cudaFree(tab);
+        if (st) cudaStreamDestroy(st);
+    };
+    try {
+        if (!z || !g || !dg || n <= 0) throw Error(ACT_ERR_INVALID, "invalid GELU arguments");
+        CK(cudaSetDevice(device));
+        CK(cudaStreamCreate(&st));
+        CK(cudaMalloc(&dz, n * 2));
+        CK(cudaMalloc(&dgo, n * 2));
+        CK(cudaMalloc(&ddg, n * 2));
+        CK(cudaMalloc(&tab, GELU_TABLE_WORDS * 4));
+        gelu_table_init(static_cast<uint32_t*>(tab), st);
+        CK(cudaMemcpyAsync(dz, z, n * 2, cudaMemcpyHostToDevice, st));
+        gelu_check(static_cast<const uint32_t*>(tab), static_cast<const uint16_t*>(dz), static_cast<uint16_t*>(dgo),
+                   static_cast<uint16_t*>(ddg), n, direct, st);
+        CK(cudaGetLastError());
+        CK(cudaMemcpyAsync(g, dgo, n * 2, cudaMemcpyDeviceToHost, st));
+        CK(cudaMemcpyAsync(dg, ddg, n * 2, cudaMemcpyDeviceToHost, st));
+        CK(cudaStreamSynchronize(st));
+        cleanup();
+        return ACT_OK;
+    } catch (const Error& e) {
+        g_error = e.what();
+        cleanup();
+        return e.code;
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        cleanup();
+        return ACT_ERR_CUDA;
+    }
+}
+
 int act_rank_gemm_bf16(int device, int kind, const void* A, const void* B, float* C, int M, int K, int nb, int a_mn,
                        int b_mn, float alpha, int splits, int reps, float* ms_per_call) {
     void *dA = nullptr, *dB = nullptr, *dC = nullptr;
@@ -1656,11 +1704,14 @@ int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int 
         g.A1 = static_cast<const bf16*>(dA); g.lda1 = K;
         g.B1 = static_cast<const bf16*>(dB); g.ldb1 = b_mn_major ? N : K; g.b_kmajor = !b_mn_major;
         g.mode = EPI_STORE_F32; g.out = dC; g.ldo = N;
-        const bool tc = path == 2 || (path == 0 && gemm_tc_supported(g));
+        const bool tc = path >= 2 || (path == 0 && gemm_tc_supported(g));
         if (tc && !gemm_tc_supported(g)) throw Error(ACT_ERR_INVALID, "shape not supported by the tcgen05 path");
-        if (path == 3 && !gemm_tc2_supported(g)) throw Error(ACT_ERR_INVALID, "shape not supported by the 2-CTA path");
+        if ((path == 3 || path == 4) && !gemm_tc2_supported(g))
+            throw Error(ACT_ERR_INVALID, "shape not supported by the 2-CTA path");
+        if (path < 0 || path > 4) throw Error(ACT_ERR_INVALID, "unknown GEMM path");
         auto run = [&] {
             if (path == 3) gemm_tc2(g, derr, st);
+            else if (path == 4) gemm_tc2_width(g, derr, st, 128);
             else if (path == 0 && tc) gemm_tc_auto(g, derr, st);
             else if (tc) gemm_tc(g, derr, st);
             else gemm(g, st);

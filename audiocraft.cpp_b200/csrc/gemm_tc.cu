@@ -481,16 +481,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(const __grid_const
 // completion bytes are posted to the leader's barrier; the leader signals the peer's barriers
 // with ordinary commits addressed through mapa.
 
-constexpr int BN2 = 256;
-constexpr int BH2 = BN2 / 2;
-
+// BNP: output columns of a pair tile (256 or 128); each CTA stages BNP / 2 rows of B
+template <int BNP>
 struct Tc2Cfg {
+    static constexpr int BH = BNP / 2;
     static constexpr int A_BYTES = BM * BKE * 2;
-    static constexpr int B_BYTES = BH2 * BKE * 2;
+    static constexpr int B_BYTES = BH * BKE * 2;
     static constexpr int STAGE = A_BYTES + B_BYTES;
-    static constexpr int STAGES = 6;
+    static constexpr int STAGES = BNP == 256 ? 6 : 8;
     static constexpr int SMEM = STAGES * STAGE + EPI_SMEM + 1024 + 256;
-    static constexpr uint32_t TMEM_COLS = 2 * BN2;
+    static constexpr uint32_t TMEM_COLS = 2 * BNP;
 };
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -536,9 +536,10 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
                  : "memory");
 }
 
-template <bool B_MN>
+template <int BN2, bool B_MN>
 __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc2_kernel(const __grid_constant__ TcMaps maps, const TcParams p) {
-    using Cfg = Tc2Cfg;
+    using Cfg = Tc2Cfg<BN2>;
+    constexpr int BH2 = Cfg::BH;
     constexpr int S = Cfg::STAGES;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -812,9 +813,10 @@ void launch_tc(const GemmArgs& a, int* err, cudaStream_t s) {
     cudaLaunchKernelEx(&cfg, kern, maps, p);
 }
 
-template <bool B_MN>
+template <int BN2, bool B_MN>
 void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
-    using Cfg = Tc2Cfg;
+    using Cfg = Tc2Cfg<BN2>;
+    constexpr int BH2 = Cfg::BH;
     TcMaps maps;
     make_map(&maps.a1, a.A1, a.M, a.K1, a.lda1, BKE, BM);
     if (B_MN) make_map(&maps.b1, a.B1, a.K1, a.N, a.ldb1, 64, BKE);
@@ -835,7 +837,7 @@ void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
     p.resid = a.resid; p.ldr = a.ldr; p.aux = a.aux; p.ldaux = a.ldaux; p.auxin = a.auxin; p.ldauxin = a.ldauxin;
     p.colscale2 = a.colscale2; p.bias = a.bias; p.nvalid = a.nvalid; p.mvalid = a.mvalid; p.err = err;
     p.rope = a.rope; p.rope_T = a.rope_T; p.rope_cols = a.rope_cols;
-    auto kern = gemm_tc2_kernel<B_MN>;
+    auto kern = gemm_tc2_kernel<BN2, B_MN>;
     static bool configured = false;
     if (!configured) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
@@ -883,28 +885,46 @@ bool gemm_tc_supported(const GemmArgs& a) {
     return (al & 15) == 0;
 }
 
-bool gemm_tc2_supported(const GemmArgs& a) { return gemm_tc_supported(a) && a.N % BN2 == 0 && a.M > BM; }
+bool gemm_tc2_supported(const GemmArgs& a) { return gemm_tc_supported(a) && a.M > BM; }
 
-void gemm_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
-    if (a.b_kmajor) launch_tc2<false>(a, err, s);
-    else launch_tc2<true>(a, err, s);
+void gemm_tc2_width(const GemmArgs& a, int* err, cudaStream_t s, int width) {
+    if (width == 256) {
+        if (a.b_kmajor) launch_tc2<256, false>(a, err, s);
+        else launch_tc2<256, true>(a, err, s);
+    } else {
+        if (a.b_kmajor) launch_tc2<128, false>(a, err, s);
+        else launch_tc2<128, true>(a, err, s);
+    }
 }
 
+void gemm_tc2(const GemmArgs& a, int* err, cudaStream_t s) { gemm_tc2_width(a, err, s, a.N % 256 == 0 ? 256 : 128); }
+
 void gemm_tc_auto(const GemmArgs& a, int* err, cudaStream_t s) {
-    if (gemm_tc2_supported(a)) {
-        if (!g_num_sms) {
-            int dev = 0;
-            cudaGetDevice(&dev);
-            cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-        }
-        const long t1 = (long)((a.M + BM - 1) / BM) * (a.N / BN2), t2 = (long)((a.M + 2 * BM - 1) / (2 * BM)) * (a.N / BN2);
-        const long r1 = (t1 + g_num_sms - 1) / g_num_sms, r2 = (t2 + g_num_sms / 2 - 1) / (g_num_sms / 2);
-        if (r2 <= r1) {
-            gemm_tc2(a, err, s);
-            return;
-        }
+    if (!g_num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
     }
-    gemm_tc(a, err, s);
+    // Each SM computes 128-row tiles in every variant; the cost of a launch is its number of
+    // rounds over the SMs times the tile width, scaled by per-column efficiencies measured on
+    // the cfg-2 shapes (256-wide 2-CTA tiles fastest; 128-wide pair tiles 1.6x slower per
+    // column, so they only win where they save whole rounds).
+    static const double eff[3] = {1.05, 1.0, 1.62};  // 1-CTA 256 (or 128), 2-CTA 256, 2-CTA 128
+    auto rounds = [&](long tiles, long slots) { return (tiles + slots - 1) / slots; };
+    const long m1 = (a.M + BM - 1) / BM, m2 = (a.M + 2 * BM - 1) / (2 * BM), pairs = g_num_sms / 2;
+    const int w1 = a.N % 256 == 0 ? 256 : 128;
+    double best = rounds(m1 * (a.N / w1), g_num_sms) * (double)w1 * eff[0];
+    int choice = 0;
+    if (gemm_tc2_supported(a)) {
+        if (a.N % 256 == 0) {
+            const double c = rounds(m2 * (a.N / 256), pairs) * 256.0 * eff[1];
+            if (c < best) { best = c; choice = 1; }
+        }
+        const double c = rounds(m2 * (a.N / 128), pairs) * 128.0 * eff[2];
+        if (c < best) { best = c; choice = 2; }
+    }
+    if (choice == 0) gemm_tc(a, err, s);
+    else gemm_tc2_width(a, err, s, choice == 1 ? 256 : 128);
 }
 
 void gemm_tc(const GemmArgs& a, int* err, cudaStream_t s) {

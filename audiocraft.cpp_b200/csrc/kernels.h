@@ -66,8 +66,9 @@ struct GemmArgs {
 void gemm(const GemmArgs& a, cudaStream_t s);                 // mma.sync path, any layout
 bool gemm_tc_supported(const GemmArgs& a);                     // shapes the tcgen05 path takes
 void gemm_tc(const GemmArgs& a, int* err, cudaStream_t s);     // tcgen05 / TMEM / TMA path
-bool gemm_tc2_supported(const GemmArgs& a);                    // 2-CTA (cta_group::2) 256 x 256 tiles
-void gemm_tc2(const GemmArgs& a, int* err, cudaStream_t s);
+bool gemm_tc2_supported(const GemmArgs& a);                    // 2-CTA (cta_group::2) 256-row pair tiles
+void gemm_tc2(const GemmArgs& a, int* err, cudaStream_t s);     // 256 columns when N allows, else 128
+void gemm_tc2_width(const GemmArgs& a, int* err, cudaStream_t s, int width);  // width 256 or 128
 // Rank-block products on tcgen05 (gemm_skinny.cu): C = alpha * A(M x K) B(K x nb), nb <= 64,
 // split over K across CTAs.  ACC / ACC_T add C (or C^T) into an fp32 gradient with atomics;
 // STORE writes bf16 C, reducing the split-K partials of a tile inside a thread-block cluster.
@@ -153,6 +154,13 @@ void layernorm_bwd(const float* dy, const float* x, const float* w, const float*
 void residual_to_bf16(float* x, const float* extra, bf16* dst, const float* colscale, int rows, int D,
                       cudaStream_t s);
 void f32_to_bf16(const float* x, bf16* y, long n, cudaStream_t s);
+// GELU by table (bit-identical to the A&S evaluation on bf16 inputs): tab holds
+// GELU_TAB_ENTRIES words filled by gelu_table_init; gact = gelu(z) and, with store_grad,
+// z <- gelu'(z) in place (n a multiple of 8)
+constexpr int GELU_TABLE_WORDS = 5120;
+void gelu_table_init(uint32_t* tab, cudaStream_t s);
+void gelu_fwd(const uint32_t* tab, bf16* z, bf16* gact, long n, int store_grad, cudaStream_t s);
+void gelu_check(const uint32_t* tab, const uint16_t* z, uint16_t* g, uint16_t* dg, long n, int direct, cudaStream_t s);
 
 // MelodyFlow inputs: x0[m][c] = ((1-t)noise + t clean) * rescale(t), vstar = clean - noise.
 void mf_inputs(const float* clean, const float* noise, const float* t, int clips, int T, int lat,

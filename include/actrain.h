@@ -168,7 +168,7 @@ double act_step_flops(act_ctx* ctx, int n);
 /* stand-alone projection GEMM on host buffers (tests and the kernel sweep): C[M][N] fp32 =
  * A[M][K] . B(n,k) with bf16 A and B, B as [N][K] (b_mn_major 0) or [K][N] (1);
  * path 0 = automatic, 1 = mma.sync kernel, 2 = tcgen05 kernel, 3 = tcgen05 2-CTA (cta_group::2)
- * kernel; when reps > 0 the GEMM is
+ * kernel, 4 = the 2-CTA kernel with 128-column pair tiles; when reps > 0 the GEMM is
  * re-run reps times back to back and *ms_per_call receives the mean device time */
 int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path,
                   int reps, float* ms_per_call);
@@ -179,6 +179,10 @@ int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int 
  * No reference counterpart: the reference evaluates these products as separate ggml mul_mat
  * nodes (src/ac/lora.h:34-95).  When reps > 0 the call is re-run reps times (kind 0/1 keep
  * accumulating) and *ms_per_call receives the mean device time. */
+/* stand-alone check of the feed-forward activation: g = bf16(gelu(z)), dg = bf16(gelu'(z)) for
+ * bf16 z (A&S 7.1.26 GELU of src/ac/lora.h:97-110 and the derivative of that approximation),
+ * evaluated directly (direct = 1) or by the lookup table the training step uses (0). */
+int act_gelu_bf16(int device, const uint16_t* z, uint16_t* g, uint16_t* dg, int64_t n, int direct);
 int act_rank_gemm_bf16(int device, int kind, const void* A, const void* B, float* C, int M, int K, int nb, int a_mn,
                        int b_mn, float alpha, int splits, int reps, float* ms_per_call);
 /* stand-alone attention forward + backward on host buffers (tests and the kernel sweep):

@@ -16,13 +16,14 @@ def bits_to_f32(b):
     return (b.astype(np.uint32) << 16).view(np.float32)
 
 
-@pytest.mark.parametrize("path", [1, 2, 3], ids=["mma", "tcgen05", "tcgen05_pair"])
+@pytest.mark.parametrize("path", [0, 1, 2, 3, 4], ids=["auto", "mma", "tcgen05", "tcgen05_pair", "tcgen05_pair128"])
 @pytest.mark.parametrize("b_mn", [False, True], ids=["NT", "NN"])
 @pytest.mark.parametrize("M,N,K", [(128, 128, 64), (300, 256, 128), (6000, 1024, 1024), (1000, 4096, 256),
-                                   (130, 512, 4096)])
+                                   (130, 512, 4096), (1000, 384, 256)])
 def test_gemm_matches_numpy(path, b_mn, M, N, K):
-    if path == 3 and (N % 256 or M <= 128):
-        pytest.skip("the 2-CTA kernel needs N % 256 == 0 and M > 128")
+    # path 3 takes 256-wide pair tiles when N % 256 == 0, else 128-wide ones (N = 384)
+    if path in (3, 4) and M <= 128:
+        pytest.skip("the 2-CTA kernel needs M > 128")
     rng = np.random.default_rng(M + N + K)
     a = bf16_bits(rng.standard_normal((M, K)))
     b = bf16_bits(rng.standard_normal((K, N) if b_mn else (N, K)))
