@@ -33,13 +33,27 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase completes or the hint
+// (nanoseconds) expires, instead of polling and taking issue slots from the warps that work
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait: returns false (and records `code`) if the phase does not complete in time.
-// The first probe is inline (the common case on the issue paths); the polling loop is not.
+// The first probe is inline (the common case on the issue paths); the sleeping loop is not.
 static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, int* err, int code) {
     const unsigned long long t0 = globaltimer();
     while (true) {
-        for (int i = 0; i < 256; ++i)
-            if (mbar_try(bar, parity)) return true;
+        for (int i = 0; i < 16; ++i)
+            if (mbar_try_sleep(bar, parity, 100000u)) return true;
         if (globaltimer() - t0 > WAIT_NS) {
             atomicCAS(err, 0, code);
             return false;

@@ -166,6 +166,22 @@ def cpu_sample(c, seconds_hint=False):
     return dt, scale, f"oracle C restatement, 1 clip x {L} of {c['layers']} layers at d{c['dim']} T{T}, fwd+bwd, scaled x{scale:g}"
 
 
+def line_header(args, c, n, world):
+    """metric, unit and config shared by both arms (the driver compares their values)."""
+    mf = args.workload == "mf"
+    unit = "steps/s (8x30s-clip steps, summed over ranks)" if mf else "steps/s (4-seq steps, summed over ranks)"
+    metric = "DiT LoRA train steps/s (8x30s clips)" if mf else "MusicGen DoRA train steps/s (4x30s seqs per GPU)"
+    config = {"workload": ("mf-cfg2: DiT d1024 L24 H16 F4096 Q8_0 base, 8x750 frames/rank, 32 tokens, "
+                           "LoRA r16 a32 on qkv/out/ff.0/ff.2 (6,291,456 params), AdamW")
+              if mf else
+              "mg-cfg4: LM d1536 L48 H24 F6144 Q8_0 base, 4x1500 frames/rank, DoRA-rows r16 on 7 projections",
+              "global_batch": n * world, "seq_len": c.get("T", c.get("frames")),
+              "layers": c["layers"], "clips_per_rank": n,
+              "parallelism": f"dp{world}",
+              "l2": "no flush: the per-step working set (activations and frozen weights, GBs) exceeds the 126 MB L2"}
+    return metric, unit, config
+
+
 def run_reference(args, c):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -179,12 +195,11 @@ def run_reference(args, c):
         times.append(dt * scale)
     step_s = float(np.mean(times))
     value = 1.0 / step_s
-    unit = "steps/s (8x30s-clip steps)"
-    line = {"metric": "DiT LoRA train steps/s (8x30s clips)", "value": value, "unit": unit, "n_gpus": args.gpus,
+    metric, unit, config = line_header(args, c, c["batch"], max(args.gpus, 1))
+    line = {"metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": "mf-cfg2: DiT d1024 L24 H16 F4096, 8x750 frames, 32 tokens, LoRA r16 on qkv/out/ff.0/ff.2",
-                       "global_batch": 8, "seq_len": c["T"], "parallelism": "cpu"},
+            "config": config,
             "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port", "sample": desc},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -404,20 +419,13 @@ def main():
     except (OSError, ValueError):
         pass
 
-    line_unit = "steps/s (8x30s-clip steps, summed over ranks)" if args.workload == "mf" else \
-        "steps/s (4-seq steps, summed over ranks)"
+    metric, line_unit, config = line_header(args, c, n, world)
     line = {
-        "metric": "DiT LoRA train steps/s (8x30s clips)" if args.workload == "mf" else "MusicGen DoRA train steps/s (4x30s seqs per GPU)",
+        "metric": metric,
         "value": value, "unit": line_unit,
         "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": ("mf-cfg2: DiT d1024 L24 H16 F4096 Q8_0 base, 8x750 frames/rank, 32 tokens, "
-                                "LoRA r16 a32 on qkv/out/ff.0/ff.2 (6,291,456 params), AdamW")
-                   if args.workload == "mf" else
-                   "mg-cfg4: LM d1536 L48 H24 F6144 Q8_0 base, 4x1500 frames/rank, DoRA-rows r16 on 7 projections",
-                   "global_batch": n * world, "seq_len": c.get("T", c.get("frames")),
-                   "layers": c["layers"], "clips_per_rank": n,
-                   "parallelism": f"dp{world}", "l2": "no flush: the per-step working set (activations and frozen weights, GBs) exceeds the 126 MB L2"},
+        "config": config,
         "e2e": {"value": e2e_value, "unit": line_unit, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": int(kernels_per_step * args.steps),
@@ -434,7 +442,7 @@ def main():
         line["clocks"] = clk
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "mf":
         dt, scale, desc = cpu_sample(c)
-        line["cpu_baseline"] = {"value": 1.0 / (dt * scale), "unit": "steps/s (8x30s-clip steps)",
+        line["cpu_baseline"] = {"value": 1.0 / (dt * scale), "unit": line_unit,
                                 "cores": os.cpu_count(), "kind": "port", "sample": desc}
     if rank == 0:
         print(json.dumps(line), flush=True)
