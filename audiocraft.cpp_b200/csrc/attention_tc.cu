@@ -27,8 +27,9 @@
 //   dV += P^T dO, dK += dS^T Q             (fp32 accumulators stay in TMEM across the loop)
 //   dQ  = dS K  (dS read back from the dS^T tile as an MN-major operand), added into the fp32
 //         dQ accumulator with TMA bulk reduce-add tiles (out-of-range rows add exact zeros)
-// Warp roles: 0 TMA (K, V once; Q, dO per block into 2 stages), 1 MMA issue, 2..5 P / dS and
-// the final dK / dV epilogue (RoPE undone on dK, DoRA column factors), 6..9 the dQ epilogue.
+// Warp roles: 0 TMA (K, V once; Q, dO per block into 2 stages), 1 MMA issue, 2..9 P / dS in two
+// groups of query columns and the final dK / dV epilogue (RoPE undone on dK, DoRA column
+// factors), 10..13 the dQ epilogue.
 // Every mbarrier wait is bounded (globaltimer) and reports into the shared error word.
 #include <cuda.h>
 
@@ -331,7 +332,7 @@ constexpr int AB_DQ_OFF = 10 * AB_T16;       // dQ staging: two [128 queries][32
 constexpr int AB_LSE_OFF = 12 * AB_T16;      // [2] x { lse[128], D[128] } fp32
 constexpr int AB_BAR_OFF = AB_LSE_OFF + 2 * 256 * 4;
 constexpr int AB_SMEM = AB_BAR_OFF + 256 + 1024;
-constexpr int AB_THREADS = 10 * 32;
+constexpr int AB_THREADS = 14 * 32;
 constexpr uint32_t AB_TMEM_COLS = 512;  // S^T 0..127, dP^T 128..255, dV 256..319, dK 320..383, dQ 384..447
 
 struct AbMaps {
@@ -363,8 +364,8 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
     if (threadIdx.x == 0) {
         mbar_init(kv_full, 1);
         mbar_init(s_full, 1);
-        mbar_init(s_free, 4);
-        mbar_init(ds_full, 4);
+        mbar_init(s_free, 8);   // one arrive per elementwise warp
+        mbar_init(ds_full, 8);
         mbar_init(ds_free, 1);
         mbar_init(dq_full, 1);
         mbar_init(dq_free, 4);
@@ -444,8 +445,11 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
             mma_commit(dq_full);
         }
         if (ok && nq > 0) mma_commit(acc_done);
-    } else if (warp >= 2 && warp < 6) {
+    } else if (warp >= 2 && warp < 10) {
         // ------------------------------------------------------------ P / dS, then dK / dV
+        // two groups of four warps: group g takes query columns 64g .. 64g+63 of every block
+        // (both groups read the same TMEM lanes), then group 0 writes dK and group 1 dV
+        const int grp = (warp - 2) >> 2;
         const int quad = warp & 3;
         const int kr = quad * 32 + lane, key = k0 + kr;
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
@@ -459,11 +463,12 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
             // this block's lse / D into shared memory (one element per thread)
             {
                 float* L = lsd + (u & 1) * 256;
-                const int t = threadIdx.x - 64, qi = q0 + t;
+                const int t = threadIdx.x - 64 - grp * 128, c = grp * 64 + (t & 63), qi = q0 + c;
                 const long off = ((long)b * a.H + h) * a.T + qi;
-                L[t] = qi < a.T ? a.lse[off] : 0.f;
-                L[128 + t] = qi < a.T ? a.dvec[off] : 0.f;
-                asm volatile("bar.sync 1, 128;" ::: "memory");
+                if (t < 64) L[c] = qi < a.T ? a.lse[off] : 0.f;
+                else L[128 + c] = qi < a.T ? a.dvec[off] : 0.f;
+                if (grp == 0) asm volatile("bar.sync 1, 128;" ::: "memory");
+                else asm volatile("bar.sync 3, 128;" ::: "memory");
             }
             const float* L = lsd + (u & 1) * 256;
             // after a failed wait the loop keeps running (without work) so that every warp still
@@ -474,38 +479,45 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
             }
             if (!ok) continue;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            for (int half = 0; half < 2; ++half) {
-                float sv[64], dp[64];
-                tmem_ld32_nw(tS + lb + half * 64, sv);
-                tmem_ld32_nw(tS + lb + half * 64 + 32, sv + 32);
-                tmem_ld32_nw(tdP + lb + half * 64, dp);
-                tmem_ld32_nw(tdP + lb + half * 64 + 32, dp + 32);
+            for (int qt = 2 * grp; qt < 2 * grp + 2; ++qt) {  // 32 query columns at a time
+                float sv[32], dp[32];
+                tmem_ld32_nw(tS + lb + qt * 32, sv);
+                tmem_ld32_nw(tdP + lb + qt * 32, dp);
                 tmem_wait_ld();
-                if (half == 1) {  // S^T and dP^T are in registers: the next block's may be computed
+                if (qt == 2 * grp + 1) {  // this warp's S^T / dP^T consumed: the next block's may start
                     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                     __syncwarp();
                     if (lane == 0) mbar_arrive(s_free);
                 }
-                const int qbase = q0 + half * 64;
-                // valid queries of this half for this key: q in [qlo, qhi)
-                int qlo = 0, qhi = min(64, a.T - qbase);
+                const int qbase = q0 + qt * 32;
+                // valid queries of this quarter for this key: q in [qlo, qhi)
+                int qlo = 0, qhi = min(32, a.T - qbase);
                 if (key >= kv_end) qhi = 0;
                 if (a.causal) qlo = max(0, key - qbase);
+                const float4* L4 = reinterpret_cast<const float4*>(L + qt * 32);         // lse
+                const float4* D4 = reinterpret_cast<const float4*>(L + 128 + qt * 32);   // D
+                const bool full = qlo == 0 && qhi == 32;  // all but the edge blocks
 #pragma unroll
-                for (int c = 0; c < 64; ++c) {
-                    const bool v = c >= qlo && c < qhi;
-                    const float pv = v ? fast_ex2(fmaf(sv[c], sl2, -L[half * 64 + c])) : 0.f;
-                    sv[c] = pv;
-                    dp[c] = pv * (dp[c] - L[128 + half * 64 + c]);
+                for (int c4 = 0; c4 < 8; ++c4) {
+                    const float4 l = L4[c4], dv = D4[c4];
+                    const float lv[4] = {l.x, l.y, l.z, l.w}, dd[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int c = 4 * c4 + e;
+                        float pv = fast_ex2(fmaf(sv[c], sl2, -lv[e]));
+                        if (!full && (c < qlo || c >= qhi)) pv = 0.f;
+                        sv[c] = pv;
+                        dp[c] = pv * (dp[c] - dd[e]);
+                    }
                 }
-                if (half == 0 && u > 0) {  // the previous block's MMAs have read P^T / dS^T
+                if (qt == 2 * grp && u > 0) {  // the previous block's MMAs have read P^T / dS^T
                     if (lane == 0) ok = mbar_wait(ds_free, (u - 1) & 1, err, 48);
                     ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
                     if (!ok) break;
                 }
 #pragma unroll
-                for (int un = 0; un < 8; ++un) {
-                    const uint32_t off = half * AB_T16 + at_sw128(kr, un);
+                for (int un = 0; un < 4; ++un) {
+                    const uint32_t off = (qt >> 1) * AB_T16 + at_sw128(kr, (qt & 1) * 4 + un);
                     *reinterpret_cast<uint4*>(Pt + off) =
                         make_uint4(pack_bf16(sv[8 * un], sv[8 * un + 1]), pack_bf16(sv[8 * un + 2], sv[8 * un + 3]),
                                    pack_bf16(sv[8 * un + 4], sv[8 * un + 5]), pack_bf16(sv[8 * un + 6], sv[8 * un + 7]));
@@ -531,55 +543,52 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
         bf16* dvr = a.dv + ((long)b * a.Tk + krow) * a.lddv + h * 64;
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
-            float vk[32], vv[32];
+            float x[32];
             if (have) {
-                tmem_ld32_nw(tdK + lb + c * 32, vk);
-                tmem_ld32_nw(tdV + lb + c * 32, vv);
+                tmem_ld32_nw((grp == 0 ? tdK : tdV) + lb + c * 32, x);
                 tmem_wait_ld();
             } else {
 #pragma unroll
-                for (int e = 0; e < 32; ++e) vk[e] = vv[e] = 0.f;
+                for (int e = 0; e < 32; ++e) x[e] = 0.f;
             }
             if (key < a.Tk) {
+                if (grp == 0) {  // dK: scale, back to the unrotated frame, DoRA column factor
 #pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    const int col = c * 32 + e;
-                    float x0 = vk[e] * a.scale, x1 = vk[e + 1] * a.scale;
-                    if (a.rope) {  // back to the unrotated frame of the projection
-                        const float2 t = reinterpret_cast<const float2*>(a.rope)[(long)key * 32 + col / 2];
-                        const float y0 = x0 * t.x + x1 * t.y, y1 = -x0 * t.y + x1 * t.x;
-                        x0 = y0;
-                        x1 = y1;
+                    for (int e = 0; e < 32; e += 2) {
+                        const int col = c * 32 + e;
+                        float x0 = x[e] * a.scale, x1 = x[e + 1] * a.scale;
+                        if (a.rope) {
+                            const float2 t = reinterpret_cast<const float2*>(a.rope)[(long)key * 32 + col / 2];
+                            const float y0 = x0 * t.x + x1 * t.y, y1 = -x0 * t.y + x1 * t.x;
+                            x0 = y0;
+                            x1 = y1;
+                        }
+                        if (a.kscale) {
+                            x0 *= a.kscale[h * 64 + col];
+                            x1 *= a.kscale[h * 64 + col + 1];
+                        }
+                        x[e] = x0;
+                        x[e + 1] = x1;
                     }
-                    float v0 = vv[e], v1 = vv[e + 1];
-                    if (a.kscale) {
-                        x0 *= a.kscale[h * 64 + col];
-                        x1 *= a.kscale[h * 64 + col + 1];
-                    }
-                    if (a.vscale) {
-                        v0 *= a.vscale[h * 64 + col];
-                        v1 *= a.vscale[h * 64 + col + 1];
-                    }
-                    vk[e] = x0; vk[e + 1] = x1; vv[e] = v0; vv[e + 1] = v1;
-                }
+                } else if (a.vscale) {  // dV: DoRA column factor
 #pragma unroll
-                for (int un = 0; un < 4; ++un) {
-                    *reinterpret_cast<uint4*>(dkr + c * 32 + 8 * un) =
-                        make_uint4(pack_bf16(vk[8 * un], vk[8 * un + 1]), pack_bf16(vk[8 * un + 2], vk[8 * un + 3]),
-                                   pack_bf16(vk[8 * un + 4], vk[8 * un + 5]), pack_bf16(vk[8 * un + 6], vk[8 * un + 7]));
-                    *reinterpret_cast<uint4*>(dvr + c * 32 + 8 * un) =
-                        make_uint4(pack_bf16(vv[8 * un], vv[8 * un + 1]), pack_bf16(vv[8 * un + 2], vv[8 * un + 3]),
-                                   pack_bf16(vv[8 * un + 4], vv[8 * un + 5]), pack_bf16(vv[8 * un + 6], vv[8 * un + 7]));
+                    for (int e = 0; e < 32; ++e) x[e] *= a.vscale[h * 64 + c * 32 + e];
                 }
+                bf16* dst = (grp == 0 ? dkr : dvr) + c * 32;
+#pragma unroll
+                for (int un = 0; un < 4; ++un)
+                    *reinterpret_cast<uint4*>(dst + 8 * un) =
+                        make_uint4(pack_bf16(x[8 * un], x[8 * un + 1]), pack_bf16(x[8 * un + 2], x[8 * un + 3]),
+                                   pack_bf16(x[8 * un + 4], x[8 * un + 5]), pack_bf16(x[8 * un + 6], x[8 * un + 7]));
             }
         }
-    } else if (warp >= 6) {
+    } else if (warp >= 10) {
         // ------------------------------------------------------------ dQ epilogue (reduce-add)
         const int quad = warp & 3;
         const int qr = quad * 32 + lane;
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
         unsigned char* stg = smem + AB_DQ_OFF;
-        const bool leader = threadIdx.x == 192;
+        const bool leader = threadIdx.x == 320;
         bool ok = true;
         for (int u = 0; u < nq; ++u) {
             const int q0 = (qb_first + u) * AB_BQ;
