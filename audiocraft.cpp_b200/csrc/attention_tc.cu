@@ -416,19 +416,28 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
         const uint64_t dP_k = smem_desc(base + AB_P_OFF, 16, 1024), dS_k = smem_desc(base + AB_DS_OFF, 16, 1024);
         const uint64_t dS_mn = smem_desc(base + AB_DS_OFF, 16384, 1024);
         bool ok = nq > 0 && mbar_wait(kv_full, 0, err, 42);
-        for (int u = 0; ok && u < nq; ++u) {
-            const int st = u & 1;
-            const uint32_t qs = base + AB_QD_OFF + st * 2 * AB_T16;
-            if (!mbar_wait(qd_full(st), (u >> 1) & 1, err, 43)) { ok = false; break; }
-            if (u > 0 && !mbar_wait(s_free, (u - 1) & 1, err, 44)) { ok = false; break; }
+        // S^T / dP^T of block u (reduction over d).  Block u + 1's are issued as soon as the
+        // elementwise warps have read block u's out of TMEM, ahead of block u's dV / dK / dQ, so
+        // the tensor core computes them while the P / dS pass of block u still runs.
+        auto issue_s = [&](int u) {
+            const uint32_t qs = base + AB_QD_OFF + (u & 1) * 2 * AB_T16;
+            if (!mbar_wait(qd_full(u & 1), (u >> 1) & 1, err, 43)) return false;
+            if (u > 0 && !mbar_wait(s_free, (u - 1) & 1, err, 44)) return false;
             const uint64_t dQ_k = smem_desc(qs, 16, 1024), dO_k = smem_desc(qs + AB_T16, 16, 1024);
-            const uint64_t dQ_mn = smem_desc(qs, 8192, 1024), dO_mn = smem_desc(qs + AB_T16, 8192, 1024);
 #pragma unroll
-            for (int k16 = 0; k16 < 4; ++k16) {  // S^T = K Q^T ; dP^T = V dO^T   (reduction over d)
+            for (int k16 = 0; k16 < 4; ++k16) {
                 mma_f16(tS, dK_k + 2 * k16, dQ_k + 2 * k16, ID_S, k16 > 0 ? 1u : 0u);
                 mma_f16(tdP, dV_k + 2 * k16, dO_k + 2 * k16, ID_S, k16 > 0 ? 1u : 0u);
             }
             mma_commit(s_full);
+            return true;
+        };
+        if (ok) ok = issue_s(0);
+        for (int u = 0; ok && u < nq; ++u) {
+            const int st = u & 1;
+            const uint32_t qs = base + AB_QD_OFF + st * 2 * AB_T16;
+            if (u + 1 < nq && !issue_s(u + 1)) { ok = false; break; }
+            const uint64_t dQ_mn = smem_desc(qs, 8192, 1024), dO_mn = smem_desc(qs + AB_T16, 8192, 1024);
             if (!mbar_wait(ds_full, u & 1, err, 45)) { ok = false; break; }
 #pragma unroll
             for (int k16 = 0; k16 < 8; ++k16) {  // dV += P^T dO ; dK += dS^T Q   (reduction over queries)
