@@ -284,7 +284,7 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
     bf16* sdS = sdO + 2 * BWD_BQ * LDS; // [64 keys][LDS]  dS^T
     float* sL = reinterpret_cast<float*>(sdS + BKV * LDS);  // [2][64] lse
     float* sD = sL + 2 * BWD_BQ;                             // [2][64] rowsum(dO*O)
-    const int kb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int kb = blockIdx.x / a.qsplit, part = blockIdx.x % a.qsplit, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, q = lane & 3, lr = lane & 7, lsel = lane >> 3;
     const int k0 = kb * BKV;
@@ -298,7 +298,10 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
 
     const int qb0 = a.causal ? k0 / BWD_BQ : 0;
     const int nqb = (a.T + BWD_BQ - 1) / BWD_BQ;
-    const int qb_first = nk > 0 ? qb0 : nqb;
+    const int qb_all = nk > 0 ? qb0 : nqb;
+    // this CTA's share of the key block's query blocks
+    const int qb_first = qb_all + (int)((long)(nqb - qb_all) * part / a.qsplit);
+    const int qb_end = qb_all + (int)((long)(nqb - qb_all) * (part + 1) / a.qsplit);
     auto load_q = [&](int qb, int buf) {
         const int q0 = qb * BWD_BQ;
         const int nq = min(BWD_BQ, a.T - q0);
@@ -316,7 +319,7 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
                 for (int j = 0; j < 4; ++j) dst[j] = (q0 + c * 4 + j < a.T) ? src[j] : 0.f;
         }
     };
-    if (qb_first < nqb) load_q(qb_first, 0);
+    if (qb_first < qb_end) load_q(qb_first, 0);
     cp_async_commit();
 
     const float sl2 = a.scale * LOG2E;
@@ -326,9 +329,9 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) dk[i][e] = dv[i][e] = 0.f;
 
-    for (int qb = qb_first, it = 0; qb < nqb; ++qb, ++it) {
+    for (int qb = qb_first, it = 0; qb < qb_end; ++qb, ++it) {
         const int buf = it & 1;
-        if (qb + 1 < nqb) load_q(qb + 1, buf ^ 1);
+        if (qb + 1 < qb_end) load_q(qb + 1, buf ^ 1);
         cp_async_commit();
         cp_async_wait<1>();
         __syncthreads();
@@ -466,10 +469,33 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
                 v0 *= a.vscale[h * HD + c];
                 v1 *= a.vscale[h * HD + c + 1];
             }
-            *reinterpret_cast<uint32_t*>(dkr + c) = pack_bf16(x0, x1);
-            *reinterpret_cast<uint32_t*>(dvr + c) = pack_bf16(v0, v1);
+            if (a.dk_acc) {  // partial over this CTA's query blocks
+                if (qb_first < qb_end) {
+                    const long r = ((long)b * a.Tk + j) * a.H * HD + h * HD + c;
+                    atomicAdd(reinterpret_cast<float2*>(a.dk_acc + r), make_float2(x0, x1));
+                    atomicAdd(reinterpret_cast<float2*>(a.dv_acc + r), make_float2(v0, v1));
+                }
+            } else {
+                *reinterpret_cast<uint32_t*>(dkr + c) = pack_bf16(x0, x1);
+                *reinterpret_cast<uint32_t*>(dvr + c) = pack_bf16(v0, v1);
+            }
         }
     }
+}
+
+// dk / dv (bf16) from the fp32 accumulators of a query-split backward: 4 floats per thread
+__global__ void attn_dkv_finish_kernel(const AttnArgs a) {
+    pdl_wait();
+    pdl_trigger();
+    const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int quads = a.H * HD / 4;
+    if (idx >= (long)a.clips * a.Tk * quads) return;
+    const long row = idx / quads;
+    const int c = (int)(idx % quads) * 4;
+    const float4 k = *reinterpret_cast<const float4*>(a.dk_acc + row * a.H * HD + c);
+    const float4 v = *reinterpret_cast<const float4*>(a.dv_acc + row * a.H * HD + c);
+    *reinterpret_cast<uint2*>(a.dk + row * a.lddk + c) = make_uint2(pack_bf16(k.x, k.y), pack_bf16(k.z, k.w));
+    *reinterpret_cast<uint2*>(a.dv + row * a.lddv + c) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
 }
 
 // dq (bf16) = unrotate(dq_acc) * qscale : 4 floats per thread
@@ -532,9 +558,16 @@ void attn_bwd(const AttnArgs& a, cudaStream_t s) {
         set_smem(attn_bwd_kernel<false>, BWD_SMEM);
         configured = true;
     }
-    dim3 grid((a.Tk + BKV - 1) / BKV, a.H, a.clips);
+    if (a.qsplit < 1 || (a.qsplit > 1 && (!a.dk_acc || !a.dv_acc)))
+        throw std::runtime_error("attn_bwd: query split needs dk_acc / dv_acc");
+    dim3 grid((unsigned)(((a.Tk + BKV - 1) / BKV) * a.qsplit), a.H, a.clips);
     if (a.rope && a.rope_load) launch_pdl(attn_bwd_kernel<true>, grid, dim3(128), BWD_SMEM, s, a);
     else launch_pdl(attn_bwd_kernel<false>, grid, dim3(128), BWD_SMEM, s, a);
+}
+
+void attn_dkv_finish(const AttnArgs& a, cudaStream_t s) {
+    const long n = (long)a.clips * a.Tk * a.H * HD / 4;
+    launch_pdl(attn_dkv_finish_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, a);
 }
 
 void attn_dq_finish(const AttnArgs& a, bf16* dq, long lddq, const float* qscale, cudaStream_t s) {

@@ -157,6 +157,7 @@ struct act_ctx {
     float *vstar = nullptr, *te1 = nullptr, *te = nullptr, *x0f = nullptr, *muo = nullptr, *rso = nullptr,
           *outp = nullptr;
     float *dx = nullptr, *dtmp = nullptr, *dq_acc = nullptr, *dvec = nullptr;
+    float* dkv_acc = nullptr;  // cross-attention dK | dV partial sums (fp32, [2][clips * C][D])
     bf16 *dxbf = nullptr, *dz = nullptr, *dU = nullptr, *dob = nullptr, *dqkv = nullptr, *dcq = nullptr,
          *dckv = nullptr;
     float* logits = nullptr;
@@ -476,9 +477,18 @@ struct act_ctx {
         ca.dout = dob; ca.lddo = D; ca.dvec = dvec; ca.dq_acc = dq_acc; ca.ldq_acc = D;
         ca.dk = dckv; ca.dv = dckv + D; ca.lddk = ca.lddv = 2 * D;
         ca.kscale = y.p[3].dora ? y.p[3].g : nullptr; ca.vscale = y.p[3].dora ? y.p[3].g + D : nullptr;
+        // few keys: split every (head, clip)'s query blocks over CTAs, dK / dV through fp32 partials
+        const bool split = C <= 64;
+        if (split) {
+            ca.qsplit = (T + 63) / 64;
+            ca.dk_acc = dkv_acc;
+            ca.dv_acc = dkv_acc + crows * D;
+        }
         timed(1, 2 * attn_flops(n, C, false), 0, [&] {
             CK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * D, stream));
+            if (split) CK(cudaMemsetAsync(dkv_acc, 0, sizeof(float) * crows * 2 * D, stream));
             attn_bwd(ca, stream);
+            if (split) attn_dkv_finish(ca, stream);
             attn_dq_finish(ca, dcq, D, y.p[2].dora ? y.p[2].g : nullptr, stream);
         });
         proj_bwd(y.p[3], dckv, crows, ctx_bf, y.U[3], y.ckv, false, GemmArgs());
@@ -1201,6 +1211,7 @@ struct act_ctx {
         dqkv = dalloc<bf16>(Mr * 3 * D);
         dcq = dalloc<bf16>(Mr * D);
         dckv = dalloc<bf16>(Cr * 2 * D);
+        dkv_acc = dalloc<float>(Cr * 2 * D);
         d_loss = dalloc<float>(B);
         h_loss = halloc<float>(B);
         if (mf) {
@@ -1825,8 +1836,17 @@ int act_attention(int device, const void* q, const void* k, const void* v, const
             a.lddk = a.lddv = D;
             ddq = static_cast<bf16*>(up(nullptr, rq * D * 2));
             CK(cudaEventRecord(ev[2], st));
-            if (attn_bwd_tc_supported(a) && !std::getenv("ACTRAIN_ATTN_MMA")) attn_bwd_tc(a, derr, st);
-            else attn_bwd(a, st);
+            if (attn_bwd_tc_supported(a) && !std::getenv("ACTRAIN_ATTN_MMA")) {
+                attn_bwd_tc(a, derr, st);
+            } else if (Tk <= 64) {  // few keys: query-split backward, as the training step runs it
+                a.qsplit = (T + 63) / 64;
+                a.dk_acc = static_cast<float*>(up(nullptr, rk * D * 4));
+                a.dv_acc = static_cast<float*>(up(nullptr, rk * D * 4));
+                attn_bwd(a, st);
+                attn_dkv_finish(a, st);
+            } else {
+                attn_bwd(a, st);
+            }
             attn_dq_finish(a, ddq, D, nullptr, st);
             CK(cudaEventRecord(ev[3], st));
             CK(cudaGetLastError());

@@ -126,6 +126,13 @@ struct AttnArgs {
     long lddk = 0, lddv = 0;
     const float* kscale = nullptr;  // DoRA factor applied to dk columns (nullable)
     const float* vscale = nullptr;  // DoRA factor applied to dv columns (nullable)
+    // mma.sync backward only: split each key block's query blocks over qsplit CTAs; the partial
+    // dK / dV then go by fp32 atomics into dk_acc / dv_acc ([clips*Tk][H*64], zeroed by the
+    // caller) and attn_dkv_finish writes dk / dv.  For few keys (cross-attention) this spreads the
+    // query loop over the GPU instead of one CTA per (key block, head, clip).
+    int qsplit = 1;
+    float* dk_acc = nullptr;
+    float* dv_acc = nullptr;
 };
 
 void attn_fwd(const AttnArgs& a, cudaStream_t s);
@@ -134,6 +141,7 @@ bool attn_fwd_tc_supported(const AttnArgs& a);
 void attn_fwd_tc(const AttnArgs& a, int* err, cudaStream_t s);
 void attn_bwd(const AttnArgs& a, cudaStream_t s);  // computes dvec itself
 void attn_dvec(const AttnArgs& a, cudaStream_t s);  // dvec = rowsum(dO * O)
+void attn_dkv_finish(const AttnArgs& a, cudaStream_t s);  // dk / dv (bf16) from dk_acc / dv_acc
 // the same backward on tcgen05 (attention_tc.cu): pre-rotated q/k, Tk >= 128; computes dvec itself
 // and adds into dq_acc (zeroed by the caller) like attn_bwd
 bool attn_bwd_tc_supported(const AttnArgs& a);
