@@ -110,6 +110,10 @@ struct act_ctx {
     act_adapter_desc ad{};
     bool mf = true;
     cudaStream_t stream = nullptr;
+    // second stream for work that may overlap the main stream's (captured as graph branches)
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    bool side_pending = false;
     std::string err;
     bool finalized = false;
     std::vector<void*> dallocs;
@@ -243,6 +247,29 @@ struct act_ctx {
         else timed(cls, fl, 0, [&] { gemm(g, stream); });
     }
 
+    // Issue fn's kernels on the side stream, after everything the main stream has issued so far
+    // and concurrently with what it issues until join_side().  The profiling pass keeps one
+    // stream so that every launch is bracketed by its own events.
+    template <class Fn>
+    void on_side(Fn&& fn) {
+        if (profiling) {
+            fn();
+            return;
+        }
+        CK(cudaEventRecord(ev_fork, stream));
+        CK(cudaStreamWaitEvent(side, ev_fork, 0));
+        std::swap(stream, side);
+        fn();
+        std::swap(stream, side);
+        side_pending = true;
+    }
+    void join_side() {
+        if (!side_pending) return;
+        CK(cudaEventRecord(ev_join, side));
+        CK(cudaStreamWaitEvent(stream, ev_join, 0));
+        side_pending = false;
+    }
+
     // rank-block products: the tcgen05 skinny kernel, or the generic GEMM `fallback` when the
     // tcgen05 paths are disabled or the operands do not qualify
     void run_rank(const SkinnyArgs& k, const GemmArgs& fallback) {
@@ -315,7 +342,6 @@ struct act_ctx {
             kb.M = p.out; kb.K = (int)rows; kb.nb = p.r;
             kb.A = dYl; kb.lda = p.out; kb.a_mn = true; kb.B = U; kb.ldb = p.RP; kb.b_mn = true;
             kb.kind = SKINNY_ACC; kb.out = grad + p.offB; kb.ldo = p.r;
-            run_rank(kb, gb);
             GemmArgs ga;
             ga.M = p.RP; ga.N = p.in; ga.K1 = (int)rows;
             ga.A1 = dU; ga.lda1 = p.RP; ga.a_kmajor = false;
@@ -326,15 +352,24 @@ struct act_ctx {
             ka.M = p.in; ka.K = (int)rows; ka.nb = p.r;
             ka.A = X; ka.lda = p.in; ka.a_mn = true; ka.B = dU; ka.ldb = p.RP; ka.b_mn = true;
             ka.kind = SKINNY_ACC_T; ka.out = grad + p.offA; ka.ldo = p.in;
-            run_rank(ka, ga);
+            // the adapter gradients only read dYl, U, X and dU: they overlap the input-gradient
+            // GEMM below (which fills its last wave with idle SMs) and join before returning
+            on_side([&] {
+                run_rank(kb, gb);
+                run_rank(ka, ga);
+            });
         }
-        if (!want_dx) return;
+        if (!want_dx) {
+            join_side();
+            return;
+        }
         e.M = (int)rows; e.N = p.in; e.K1 = p.out;
         e.A1 = dYl; e.lda1 = p.out; e.B1 = p.W; e.ldb1 = p.in; e.b_kmajor = false;
         if (p.adapted) {
             e.K2 = p.RP; e.A2 = dU; e.lda2 = p.RP; e.B2 = p.A_bf; e.ldb2 = p.in;
         }
         run_gemm(e, 0);
+        join_side();
     }
 
     // ---------------------------------------------------------------- the step
@@ -813,6 +848,9 @@ struct act_ctx {
         if (ad.tokens % 8) throw Error(ACT_ERR_INVALID, "tokens must be a multiple of 8 (pad the conditioning)");
         CK(cudaSetDevice(device));
         CK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+        CK(cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking));
+        CK(cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming));
+        CK(cudaEventCreateWithFlags(&ev_join, cudaEventDisableTiming));
         kerr = dalloc<int>(1);
         const char* gp = std::getenv("ACTRAIN_GEMM");
         use_tc = !(gp && std::string(gp) == "mma");
@@ -1303,6 +1341,10 @@ struct act_ctx {
         if (comm) ncclCommDestroy(comm);
         for (void* p : dallocs) cudaFree(p);
         for (void* p : hallocs) cudaFreeHost(p);
+        if (side) cudaStreamSynchronize(side);
+        if (ev_fork) cudaEventDestroy(ev_fork);
+        if (ev_join) cudaEventDestroy(ev_join);
+        if (side) cudaStreamDestroy(side);
         if (stream) cudaStreamDestroy(stream);
     }
 };
