@@ -433,10 +433,18 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
                 const int i = q0 + warp * 16 + g + 8 * hh;
                 if (i >= a.T) continue;
                 float* dst = a.dq_acc + ((long)b * a.T + i) * a.ldq_acc + h * HD;
+                // with a single key block this CTA is the only contributor to these rows
+                if (a.Tk <= BKV) {
 #pragma unroll
-                for (int ni = 0; ni < 8; ++ni)
-                    atomicAdd(reinterpret_cast<float2*>(dst + ni * 8 + 2 * q),
-                              make_float2(dq[ni][2 * hh] * a.scale, dq[ni][2 * hh + 1] * a.scale));
+                    for (int ni = 0; ni < 8; ++ni)
+                        *reinterpret_cast<float2*>(dst + ni * 8 + 2 * q) =
+                            make_float2(dq[ni][2 * hh] * a.scale, dq[ni][2 * hh + 1] * a.scale);
+                } else {
+#pragma unroll
+                    for (int ni = 0; ni < 8; ++ni)
+                        atomicAdd(reinterpret_cast<float2*>(dst + ni * 8 + 2 * q),
+                                  make_float2(dq[ni][2 * hh] * a.scale, dq[ni][2 * hh + 1] * a.scale));
+                }
             }
         }
         __syncthreads();  // sdS and this Q/dO buffer are rewritten next

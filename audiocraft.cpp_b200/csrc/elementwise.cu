@@ -161,17 +161,21 @@ __global__ void mf_inputs_kernel(const float* __restrict__ clean, const float* _
     vstar[i] = cl - nz;
 }
 
-__global__ void mf_loss_kernel(const float* __restrict__ out, const float* __restrict__ vstar, int T,
-                               int lat, float* __restrict__ loss, bf16* __restrict__ dout) {
-    const int b = blockIdx.x;
+// MSE of the rescaled output against v* (flow target) and its seed gradient.  out / dout are
+// [clips][T][lat] (token-major), vstar [clips][lat][T]; block (b, j) takes a strided share of
+// clip b in out's order (coalesced out / dout) and leaves its partial sum in part[b][j].
+constexpr int LOSS_PARTS = 32;
+__global__ void mf_loss_part_kernel(const float* __restrict__ out, const float* __restrict__ vstar, int T,
+                                    int lat, float* __restrict__ part, bf16* __restrict__ dout) {
+    const int b = blockIdx.x, j = blockIdx.y;
     const long n = (long)T * lat;
     const float inv = 1.0f / (float)n;
     const float sq2 = sqrtf(2.0f);
     float acc = 0.f;
-    for (long i = threadIdx.x; i < n; i += blockDim.x) {
-        const int c = (int)(i / T), p = (int)(i % T);
-        const long o = ((long)b * T + p) * lat + c;
-        const float d = out[o] * sq2 - vstar[(long)b * n + i];
+    for (long i = (long)j * blockDim.x + threadIdx.x; i < n; i += (long)LOSS_PARTS * blockDim.x) {
+        const int p = (int)(i / lat), c = (int)(i % lat);
+        const long o = (long)b * n + i;
+        const float d = out[o] * sq2 - vstar[(long)b * n + (long)c * T + p];
         acc += d * d;
         dout[o] = __float2bfloat16(2.0f * d * inv * sq2);
     }
@@ -182,8 +186,17 @@ __global__ void mf_loss_kernel(const float* __restrict__ out, const float* __res
     if (threadIdx.x < 32) {
         float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
         v = warp_sum(v);
-        if (threadIdx.x == 0) loss[b] = v * inv;
+        if (threadIdx.x == 0) part[b * LOSS_PARTS + j] = v;
     }
+}
+
+// loss[b] = sum of clip b's partials / (T * lat), in a fixed order
+__global__ void mf_loss_sum_kernel(const float* __restrict__ part, int clips, float inv, float* __restrict__ loss) {
+    const int b = threadIdx.x;
+    if (b >= clips) return;
+    float v = 0.f;
+    for (int j = 0; j < LOSS_PARTS; ++j) v += part[b * LOSS_PARTS + j];
+    loss[b] = v * inv;
 }
 
 __global__ void linear_f32_kernel(const float* __restrict__ x, const float* __restrict__ W,
@@ -553,8 +566,9 @@ void mf_inputs(const float* clean, const float* noise, const float* t, int clips
 }
 
 void mf_loss(const float* out, const float* vstar, int clips, int T, int lat, float* loss, bf16* dout,
-             cudaStream_t s) {
-    mf_loss_kernel<<<clips, 1024, 0, s>>>(out, vstar, T, lat, loss, dout);
+             float* part, cudaStream_t s) {
+    mf_loss_part_kernel<<<dim3(clips, LOSS_PARTS), 256, 0, s>>>(out, vstar, T, lat, part, dout);
+    mf_loss_sum_kernel<<<1, 32 * ((clips + 31) / 32), 0, s>>>(part, clips, 1.0f / ((float)T * lat), loss);
 }
 
 void linear_f32(const float* x, const float* W, float* y, int rows, int N, int K, int act, cudaStream_t s) {

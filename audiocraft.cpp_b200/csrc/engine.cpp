@@ -154,6 +154,7 @@ struct act_ctx {
     int32_t *h_nvalid = nullptr, *h_ids = nullptr, *h_tgt = nullptr;
     float *d_clean = nullptr, *d_noise = nullptr, *d_hidden = nullptr, *d_t = nullptr, *d_tfeat = nullptr,
           *d_loss = nullptr, *d_ctx = nullptr;
+    float* loss_part = nullptr;  // per-clip partial sums of the MSE ([max_batch][32])
     int32_t *d_nvalid = nullptr, *d_ids = nullptr, *d_tgt = nullptr;
 
     // global activations / scratch
@@ -515,7 +516,7 @@ struct act_ctx {
         // few keys: split every (head, clip)'s query blocks over CTAs, dK / dV through fp32 partials
         const bool split = C <= 64;
         if (split) {
-            ca.qsplit = (T + 63) / 64;
+            ca.qsplit = ((T + 63) / 64 + 1) / 2;  // two query blocks per CTA
             ca.dk_acc = dkv_acc;
             ca.dv_acc = dkv_acc + crows * D;
         }
@@ -613,7 +614,7 @@ struct act_ctx {
             o.mode = EPI_STORE_F32; o.out = outp; o.ldo = md.latent_dim;
             run_gemm(o, 0);
         }
-        timed(2, 0, 0, [&] { mf_loss(outp, vstar, n, T, md.latent_dim, d_loss, dout, stream); });
+        timed(2, 0, 0, [&] { mf_loss(outp, vstar, n, T, md.latent_dim, d_loss, dout, loss_part, stream); });
         // ---------------- backward
         {
             GemmArgs d;
@@ -1251,6 +1252,7 @@ struct act_ctx {
         dckv = dalloc<bf16>(Cr * 2 * D);
         dkv_acc = dalloc<float>(Cr * 2 * D);
         d_loss = dalloc<float>(B);
+        loss_part = dalloc<float>((long)B * 32);
         h_loss = halloc<float>(B);
         if (mf) {
             const size_t nx = (size_t)B * md.latent_dim * T;

@@ -174,8 +174,9 @@ void gelu_check(const uint32_t* tab, const uint16_t* z, uint16_t* g, uint16_t* d
 void mf_inputs(const float* clean, const float* noise, const float* t, int clips, int T, int lat,
                bf16* x0, float* vstar, cudaStream_t s);
 // loss[b] = mean((sqrt2*out - vstar)^2) ; dout = d loss / d out (bf16, token-major)
+// part: clips * 32 floats of scratch (partial sums)
 void mf_loss(const float* out, const float* vstar, int clips, int T, int lat, float* loss, bf16* dout,
-             cudaStream_t s);
+             float* part, cudaStream_t s);
 // small fp32 linear for the timestep MLP: y[b][n] = act(sum_k x[b][k] W[n][k]); act 1 = SiLU
 void linear_f32(const float* x, const float* W, float* y, int rows, int N, int K, int act,
                 cudaStream_t s);
