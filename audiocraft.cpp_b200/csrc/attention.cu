@@ -450,6 +450,7 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
         __syncthreads();  // sdS and this Q/dO buffer are rewritten next
     }
     cp_async_wait<0>();
+    if (!a.dk && !a.dk_acc) return;  // dQ only (nothing consumes dK / dV)
     // epilogue: dK (unrotate), dV, DoRA column factors
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
@@ -566,8 +567,8 @@ void attn_bwd(const AttnArgs& a, cudaStream_t s) {
         set_smem(attn_bwd_kernel<false>, BWD_SMEM);
         configured = true;
     }
-    if (a.qsplit < 1 || (a.qsplit > 1 && (!a.dk_acc || !a.dv_acc)))
-        throw std::runtime_error("attn_bwd: query split needs dk_acc / dv_acc");
+    if (a.qsplit < 1 || (a.qsplit > 1 && a.dk && (!a.dk_acc || !a.dv_acc)))
+        throw std::runtime_error("attn_bwd: query split with dK / dV needs dk_acc / dv_acc");
     dim3 grid((unsigned)(((a.Tk + BKV - 1) / BKV) * a.qsplit), a.H, a.clips);
     if (a.rope && a.rope_load) launch_pdl(attn_bwd_kernel<true>, grid, dim3(128), BWD_SMEM, s, a);
     else launch_pdl(attn_bwd_kernel<false>, grid, dim3(128), BWD_SMEM, s, a);

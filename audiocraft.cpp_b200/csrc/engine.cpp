@@ -421,6 +421,12 @@ struct act_ctx {
         const long rows = (long)n * T, crows = (long)n * C;
         const float eps = md.norm_eps;
         const bool dit = mf;
+        // the cross-attention K/V projection reads only the conditioning: it runs on the side
+        // stream, overlapping the self-attention half of the block
+        on_side([&] {
+            GemmArgs k; k.mode = EPI_STORE_BF16; k.out = y.ckv; k.ldo = 2 * D;
+            proj_fwd(y.p[3], ctx_bf, crows, y.U[3], k);
+        });
         // pre-norm self-attention
         timed(2, 0, 0, [&] { layernorm_fwd(y.xin, y.norm[0], y.norm[1], dit ? te : nullptr, T, y.h1, y.mu[0], y.rs[0], (int)rows, D, eps, stream); });
         {
@@ -450,9 +456,8 @@ struct act_ctx {
         {
             GemmArgs e; e.mode = EPI_STORE_BF16; e.out = y.cq; e.ldo = D;
             proj_fwd(y.p[2], y.hc, rows, y.U[2], e);
-            GemmArgs k; k.mode = EPI_STORE_BF16; k.out = y.ckv; k.ldo = 2 * D;
-            proj_fwd(y.p[3], ctx_bf, crows, y.U[3], k);
         }
+        join_side();
         AttnArgs ca;
         ca.q = y.cq; ca.ldq = D; ca.k = y.ckv; ca.v = y.ckv + D; ca.ldk = ca.ldv = 2 * D;
         ca.T = T; ca.Tk = C; ca.H = H; ca.clips = n; ca.nvalid = dit ? nvalid_dev : nullptr;
@@ -511,23 +516,30 @@ struct act_ctx {
         ca.zero_key = dit ? md.add_zero_attn : 0; ca.scale = 1.0f / std::sqrt((float)md.head_dim);
         ca.o = y.o2; ca.ldo = D; ca.lse = y.lse2;
         ca.dout = dob; ca.lddo = D; ca.dvec = dvec; ca.dq_acc = dq_acc; ca.ldq_acc = D;
-        ca.dk = dckv; ca.dv = dckv + D; ca.lddk = ca.lddv = 2 * D;
+        // dK / dV of the conditioning only feed an adapter on cross.kv (the conditioning itself
+        // takes no gradient): without one they are not computed
+        const bool need_dkv = y.p[3].adapted;
+        if (need_dkv) {
+            ca.dk = dckv; ca.dv = dckv + D; ca.lddk = ca.lddv = 2 * D;
+        }
         ca.kscale = y.p[3].dora ? y.p[3].g : nullptr; ca.vscale = y.p[3].dora ? y.p[3].g + D : nullptr;
         // few keys: split every (head, clip)'s query blocks over CTAs, dK / dV through fp32 partials
         const bool split = C <= 64;
         if (split) {
             ca.qsplit = ((T + 63) / 64 + 1) / 2;  // two query blocks per CTA
-            ca.dk_acc = dkv_acc;
-            ca.dv_acc = dkv_acc + crows * D;
+            if (need_dkv) {
+                ca.dk_acc = dkv_acc;
+                ca.dv_acc = dkv_acc + crows * D;
+            }
         }
         timed(1, 2 * attn_flops(n, C, false), 0, [&] {
             CK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * D, stream));
-            if (split) CK(cudaMemsetAsync(dkv_acc, 0, sizeof(float) * crows * 2 * D, stream));
+            if (split && need_dkv) CK(cudaMemsetAsync(dkv_acc, 0, sizeof(float) * crows * 2 * D, stream));
             attn_bwd(ca, stream);
-            if (split) attn_dkv_finish(ca, stream);
+            if (split && need_dkv) attn_dkv_finish(ca, stream);
             attn_dq_finish(ca, dcq, D, y.p[2].dora ? y.p[2].g : nullptr, stream);
         });
-        proj_bwd(y.p[3], dckv, crows, ctx_bf, y.U[3], y.ckv, false, GemmArgs());
+        if (need_dkv) proj_bwd(y.p[3], dckv, crows, ctx_bf, y.U[3], y.ckv, false, GemmArgs());
         {
             GemmArgs e; e.mode = EPI_STORE_F32; e.out = dtmp; e.ldo = D;
             proj_bwd(y.p[2], dcq, rows, y.hc, y.U[2], y.cq, true, e);
