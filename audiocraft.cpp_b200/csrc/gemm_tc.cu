@@ -36,6 +36,11 @@ constexpr int BM = 128;
 constexpr int BKE = 64;  // K elements per stage (one 128-byte swizzle row)
 constexpr int EPI_WARPS = 4;
 constexpr int NTHREADS = (2 + EPI_WARPS) * 32;
+// The 2-CTA kernel drains each accumulator with two warps per TMEM lane quarter (one per half
+// of the tile's columns): the epilogue of a tile is latency-bound per warp, so twice the warps
+// finish it in about half the time.
+constexpr int EPI_WARPS2 = 8;
+constexpr int NTHREADS2 = (2 + EPI_WARPS2) * 32;
 
 struct TcParams {
     int M, N, K1, K2;
@@ -99,7 +104,7 @@ struct EpiTiles {
     uint32_t o_s, x_s; // their shared-state-space addresses
 };
 
-// previous bulk stores of this warp have finished reading the staging tiles
+// previous bulk stores of this warp (all issued by lane 0) have finished reading the tiles
 __device__ __forceinline__ void tiles_free(int lane) {
     if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
     __syncwarp();
@@ -197,7 +202,8 @@ __device__ __forceinline__ void stage_input(int kind, const float4* pre, const E
 }
 
 // Warp-collective epilogue of the 32 x 32 chunk rows m_base .. m_base+31 (the first `rows`
-// valid), columns n .. n+31; lane l holds row m_base + l in v[].
+// valid), columns n .. n+31; lane l holds row m_base + l in v[].  The caller has made the
+// tiles `t` free.
 __device__ __forceinline__ void epilogue_warp32(const TcParams& p, const TcMaps& maps, int m_base, int rows, int n,
                                                 float* v, const EpiTiles& t, int lane) {
     const int m = m_base + lane;
@@ -213,7 +219,6 @@ __device__ __forceinline__ void epilogue_warp32(const TcParams& p, const TcMaps&
         }
     }
     if (p.aux && p.mode != EPI_GELU && p.mode != EPI_GELU_D) {
-        tiles_free(lane);
         put_row_b16(t.x, lane, v);
         tile_store(&maps.aux, t.x_s, n, m_base, lane);
     }
@@ -228,8 +233,7 @@ __device__ __forceinline__ void epilogue_warp32(const TcParams& p, const TcMaps&
         }
     }
     if (p.mode == EPI_STORE_F32 || p.mode == EPI_ACCUM_F32 || p.mode == EPI_RESID_F32) {
-        if (p.mode == EPI_STORE_F32) tiles_free(lane);
-        else add_row_f32(t.o, lane, v);  // residual / accumulator already staged in the tile
+        if (p.mode != EPI_STORE_F32) add_row_f32(t.o, lane, v);  // residual / accumulator already staged in the tile
         put_row_f32(t.o, lane, v);
         tile_store(&maps.out, t.o_s, n, m_base, lane);
         return;
@@ -239,7 +243,6 @@ __device__ __forceinline__ void epilogue_warp32(const TcParams& p, const TcMaps&
         for (int i = 0; i < 32; ++i) v[i] += p.bias[n + i];
     } else if (p.mode == EPI_GELU) {
         // the stored pre-activation is bf16; the activation and its backward use that value
-        tiles_free(lane);
         put_row_b16(t.x, lane, v);
         get_row_b16(t.x, lane, v);
         tile_store(&maps.aux, t.x_s, n, m_base, lane);
@@ -247,7 +250,6 @@ __device__ __forceinline__ void epilogue_warp32(const TcParams& p, const TcMaps&
         for (int i = 0; i < 32; ++i) v[i] = gelu_as(v[i]);
     } else if (p.mode == EPI_GELU_D) {
         // gelu' of the bf16-rounded pre-activation goes to aux, gelu of it to the output
-        tiles_free(lane);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             float d8[8];
@@ -276,7 +278,6 @@ __device__ __forceinline__ void epilogue_warp32(const TcParams& p, const TcMaps&
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] *= p.colscale2[n + i];
     }
-    tiles_free(lane);
     put_row_b16(t.o, lane, v);
     tile_store(&maps.out, t.o_s, n, m_base, lane);
 }
@@ -293,11 +294,9 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, const TcMaps& m
         uint32_t r[32];
         tmem_ld32(trow + c * 32, r);
         const int n = n0 + c * 32;
+        if (rows > 0) tiles_free(lane);
         if (kind) {
-            if (rows > 0) {
-                tiles_free(lane);
-                stage_input(kind, pre, t, lane);
-            }
+            if (rows > 0) stage_input(kind, pre, t, lane);
             if (c + 1 < NCH) fetch_input(p, kind, m_base, rows, n + 32, lane, pre);
             else fetch_input(p, kind, next_m_base, next_rows, next_n0, lane, pre);
             __syncwarp();
@@ -480,6 +479,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(const __grid_const
 // 128 x 256 tile, which is what bounds that kernel.  Loads are plain per-CTA TMA loads whose
 // completion bytes are posted to the leader's barrier; the leader signals the peer's barriers
 // with ordinary commits addressed through mapa.
+// Each CTA drains its 128 accumulator rows with 8 epilogue warps (warps 2..9): two per TMEM
+// lane quarter, each taking half of the tile's columns.
 
 // BNP: output columns of a pair tile (256 or 128); each CTA stages BNP / 2 rows of B
 template <int BNP>
@@ -488,8 +489,9 @@ struct Tc2Cfg {
     static constexpr int A_BYTES = BM * BKE * 2;
     static constexpr int B_BYTES = BH * BKE * 2;
     static constexpr int STAGE = A_BYTES + B_BYTES;
-    static constexpr int STAGES = BNP == 256 ? 6 : 8;
-    static constexpr int SMEM = STAGES * STAGE + EPI_SMEM + 1024 + 256;
+    static constexpr int STAGES = BNP == 256 ? 5 : 7;
+    static constexpr int EPI = EPI_WARPS2 * (EPI_OUT_BYTES + EPI_AUX_BYTES);
+    static constexpr int SMEM = STAGES * STAGE + EPI + 1024 + 256;
     static constexpr uint32_t TMEM_COLS = 2 * BNP;
 };
 
@@ -537,7 +539,7 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
 }
 
 template <int BN2, bool B_MN>
-__global__ void __launch_bounds__(NTHREADS, 1) gemm_tc2_kernel(const __grid_constant__ TcMaps maps, const TcParams p) {
+__global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_constant__ TcMaps maps, const TcParams p) {
     using Cfg = Tc2Cfg<BN2>;
     constexpr int BH2 = Cfg::BH;
     constexpr int S = Cfg::STAGES;
@@ -545,13 +547,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc2_kernel(const __grid_cons
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023) & ~1023u;
     unsigned char* smem = smem_raw + (base - raw);
-    const uint32_t bars = base + S * Cfg::STAGE + EPI_SMEM;
+    const uint32_t bars = base + S * Cfg::STAGE + Cfg::EPI;
     auto full_bar = [&](int s) { return bars + 8 * s; };
     auto empty_bar = [&](int s) { return bars + 8 * (S + s); };
     auto tfull_bar = [&](int a) { return bars + 8 * (2 * S + a); };
     auto tempty_bar = [&](int a) { return bars + 8 * (2 * S + 2 + a); };
     const uint32_t drain_bar = bars + 8 * (2 * S + 4);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S * Cfg::STAGE + EPI_SMEM + 8 * (2 * S + 5));
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S * Cfg::STAGE + Cfg::EPI + 8 * (2 * S + 5));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_rank();
@@ -562,7 +564,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc2_kernel(const __grid_cons
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(tfull_bar(a), 1);
-            mbar_init(tempty_bar(a), 2 * EPI_WARPS);  // leader: both CTAs' epilogue warps
+            mbar_init(tempty_bar(a), 2 * EPI_WARPS2);  // leader: both CTAs' epilogue warps
         }
         mbar_init(drain_bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -656,10 +658,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc2_kernel(const __grid_cons
         mbar_wait(drain_bar, 0, p.err, 16);
     } else if (warp >= 2) {
         // ------------------------------------------------------------ epilogue (both CTAs)
-        const int quad = warp & 3;
+        // TMEM lanes 32*quad .. 32*quad+31, columns coff .. coff + BN2/2 - 1 of the tile
+        const int quad = warp & 3, coff = ((warp - 2) >> 2) * (BN2 / 2);
         EpiTiles tiles;
         tiles.o = smem + S * Cfg::STAGE + (warp - 2) * EPI_OUT_BYTES;
-        tiles.x = smem + S * Cfg::STAGE + EPI_WARPS * EPI_OUT_BYTES + (warp - 2) * EPI_AUX_BYTES;
+        tiles.x = smem + S * Cfg::STAGE + EPI_WARPS2 * EPI_OUT_BYTES + (warp - 2) * EPI_AUX_BYTES;
         tiles.o_s = smem_u32(tiles.o);
         tiles.x_s = smem_u32(tiles.x);
         const uint32_t leader_tempty0 = map_rank(tempty_bar(0), 0), leader_tempty1 = map_rank(tempty_bar(1), 0);
@@ -667,7 +670,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc2_kernel(const __grid_cons
         auto tile_rows = [&](int tl, int& m_base, int& rows, int& n0) {
             m_base = (tl % num_m2) * 2 * BM + (int)rank * BM + quad * 32;
             rows = tl < ntiles ? max(0, min(32, mlim - m_base)) : 0;
-            n0 = (tl / num_m2) * BN2;
+            n0 = (tl / num_m2) * BN2 + coff;
         };
         float4 pre[8];
         {
@@ -686,8 +689,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc2_kernel(const __grid_cons
             int m_base, rows, n0, nm, nr, nn;
             tile_rows(tile, m_base, rows, n0);
             tile_rows(tile + npairs, nm, nr, nn);
-            epilogue_tile<BN2 / 32>(p, maps, tmem_base + ((uint32_t)(quad * 32) << 16) + a * BN2, m_base, rows, n0, nm,
-                                    nr, nn, tiles, lane, pre);
+            epilogue_tile<BN2 / 64>(p, maps, tmem_base + ((uint32_t)(quad * 32) << 16) + a * BN2 + coff, m_base, rows,
+                                    n0, nm, nr, nn, tiles, lane, pre);
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(a ? leader_tempty1 : leader_tempty0);
@@ -853,7 +856,7 @@ void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
     const int pairs = tiles < g_num_sms / 2 ? tiles : g_num_sms / 2;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
-    cfg.blockDim = dim3(NTHREADS, 1, 1);
+    cfg.blockDim = dim3(NTHREADS2, 1, 1);
     cfg.dynamicSmemBytes = Cfg::SMEM;
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
