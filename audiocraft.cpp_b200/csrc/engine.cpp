@@ -114,6 +114,11 @@ struct act_ctx {
     cudaStream_t side = nullptr;
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     bool side_pending = false;
+    bool in_side = false;  // kernels are being issued on the side stream
+    // stream-K workspace of the dense GEMMs (main stream only: launches sharing it must not overlap)
+    float* sk_part = nullptr;
+    int* sk_flag = nullptr;
+    bool use_sk = true;  // ACTRAIN_STREAMK=0 at context creation: whole tiles only
     std::string err;
     bool finalized = false;
     std::vector<void*> dallocs;
@@ -242,8 +247,15 @@ struct act_ctx {
         evnext = 0;
     }
 
-    void run_gemm(const GemmArgs& g, int cls = 0) {
-        const double fl = 2.0 * g.M * g.N * (double)(g.K1 + g.K2);
+    void run_gemm(const GemmArgs& g0, int cls = 0) {
+        const double fl = 2.0 * g0.M * g0.N * (double)(g0.K1 + g0.K2);
+        GemmArgs g = g0;
+        // stream-K only on the main stream and only while no side-stream work may run beside it:
+        // its pairs wait on their neighbours, which must all be resident to finish early
+        if (!in_side && use_sk && !side_pending) {
+            g.sk_part = sk_part;
+            g.sk_flag = sk_flag;
+        }
         if (use_tc && gemm_tc_supported(g)) timed(cls, fl, 0, [&] { gemm_tc_auto(g, kerr, stream); });
         else timed(cls, fl, 0, [&] { gemm(g, stream); });
     }
@@ -260,7 +272,9 @@ struct act_ctx {
         CK(cudaEventRecord(ev_fork, stream));
         CK(cudaStreamWaitEvent(side, ev_fork, 0));
         std::swap(stream, side);
+        in_side = true;
         fn();
+        in_side = false;
         std::swap(stream, side);
         side_pending = true;
     }
@@ -865,6 +879,14 @@ struct act_ctx {
         CK(cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming));
         CK(cudaEventCreateWithFlags(&ev_join, cudaEventDisableTiming));
         kerr = dalloc<int>(1);
+        {
+            int sms = 0;
+            CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+            sk_part = dalloc<float>(gemm_sk_part_floats(sms));
+            sk_flag = dalloc<int>(gemm_sk_flag_count(sms));
+        }
+        const char* skv = std::getenv("ACTRAIN_STREAMK");
+        use_sk = !(skv && std::string(skv) == "0");
         const char* gp = std::getenv("ACTRAIN_GEMM");
         use_tc = !(gp && std::string(gp) == "mma");
         D = md.dim; F = md.ff_dim; H = md.heads; L = md.layers;
@@ -1746,13 +1768,14 @@ int act_rank_gemm_bf16(int device, int kind, const void* A, const void* B, float
 int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path,
                   int reps, float* ms_per_call) {
     // Stand-alone check of the projection GEMM: C[M][N] (fp32) = A[M][K] . B(n,k), bf16 inputs,
-    // B given as [N][K] (b_mn_major = 0) or [K][N] (1).  path 0 auto, 1 mma.sync, 2 tcgen05.
-    void *dA = nullptr, *dB = nullptr, *dC = nullptr;
+    // B given as [N][K] (b_mn_major = 0) or [K][N] (1).  path 0 auto, 1 mma.sync, 2 tcgen05,
+    // 3 2-CTA (stream-K where it pays), 4 2-CTA 128-wide, 5 2-CTA whole tiles only.
+    void *dA = nullptr, *dB = nullptr, *dC = nullptr, *dsk = nullptr, *dflag = nullptr;
     int* derr = nullptr;
     cudaStream_t st = nullptr;
     auto cleanup = [&] {
         if (st) cudaStreamSynchronize(st);
-        cudaFree(dA); cudaFree(dB); cudaFree(dC); cudaFree(derr);
+        cudaFree(dA); cudaFree(dB); cudaFree(dC); cudaFree(derr); cudaFree(dsk); cudaFree(dflag);
         if (st) cudaStreamDestroy(st);
     };
     try {
@@ -1773,11 +1796,20 @@ int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int 
         g.mode = EPI_STORE_F32; g.out = dC; g.ldo = N;
         const bool tc = path >= 2 || (path == 0 && gemm_tc_supported(g));
         if (tc && !gemm_tc_supported(g)) throw Error(ACT_ERR_INVALID, "shape not supported by the tcgen05 path");
-        if ((path == 3 || path == 4) && !gemm_tc2_supported(g))
+        if (path >= 3 && !gemm_tc2_supported(g))
             throw Error(ACT_ERR_INVALID, "shape not supported by the 2-CTA path");
-        if (path < 0 || path > 4) throw Error(ACT_ERR_INVALID, "unknown GEMM path");
+        if (path < 0 || path > 5) throw Error(ACT_ERR_INVALID, "unknown GEMM path");
+        if (path == 0 || path == 3) {
+            int sms = 0;
+            CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+            CK(cudaMalloc(&dsk, sizeof(float) * gemm_sk_part_floats(sms)));
+            CK(cudaMalloc(&dflag, sizeof(int) * gemm_sk_flag_count(sms)));
+            CK(cudaMemsetAsync(dflag, 0, sizeof(int) * gemm_sk_flag_count(sms), st));
+            g.sk_part = static_cast<float*>(dsk);
+            g.sk_flag = static_cast<int*>(dflag);
+        }
         auto run = [&] {
-            if (path == 3) gemm_tc2(g, derr, st);
+            if (path == 3 || path == 5) gemm_tc2(g, derr, st);
             else if (path == 4) gemm_tc2_width(g, derr, st, 128);
             else if (path == 0 && tc) gemm_tc_auto(g, derr, st);
             else if (tc) gemm_tc(g, derr, st);

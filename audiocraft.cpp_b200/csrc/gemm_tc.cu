@@ -18,6 +18,7 @@
 // No cluster launch: every CTA issues its own TMA loads for its own tiles.
 #include <cuda.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <stdexcept>
 #include <string>
@@ -62,6 +63,10 @@ struct TcParams {
     int rope_T, rope_cols;
     int nvalid, mvalid;
     int* err;
+    // 2-CTA kernel, stream-K instantiation: fp32 partial pair tiles [pair][rank][warp][4096] and
+    // one ready counter per [pair][rank]
+    float* sk_part;
+    int* sk_flag;
 };
 
 struct TcMaps {
@@ -285,14 +290,27 @@ __device__ __forceinline__ void epilogue_warp32(const TcParams& p, const TcMaps&
 // All chunks of one accumulator tile (NCH x 32 columns from TMEM row address `trow`).  The
 // next chunk's inputs (this tile's, or chunk 0 of the warp's next tile) are fetched while the
 // current one is finished.
+// `part` (shared memory, may be null): an fp32 partial of the same accumulator fragment, added
+// before the epilogue; chunk c, float4 g of lane l at part[(c * 8 + g) * 32 + l].
 template <int NCH>
 __device__ __forceinline__ void epilogue_tile(const TcParams& p, const TcMaps& maps, uint32_t trow, int m_base,
                                               int rows, int n0, int next_m_base, int next_rows, int next_n0,
-                                              const EpiTiles& t, int lane, float4* pre) {
+                                              const EpiTiles& t, int lane, float4* pre,
+                                              const float4* part = nullptr) {
     const int kind = epi_input_kind(p.mode);
     for (int c = 0; c < NCH; ++c) {
         uint32_t r[32];
         tmem_ld32(trow + c * 32, r);
+        if (part) {
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+                const float4 q = part[(c * 8 + g) * 32 + lane];
+                r[4 * g] = __float_as_uint(__uint_as_float(r[4 * g]) + q.x);
+                r[4 * g + 1] = __float_as_uint(__uint_as_float(r[4 * g + 1]) + q.y);
+                r[4 * g + 2] = __float_as_uint(__uint_as_float(r[4 * g + 2]) + q.z);
+                r[4 * g + 3] = __float_as_uint(__uint_as_float(r[4 * g + 3]) + q.w);
+            }
+        }
         const int n = n0 + c * 32;
         if (rows > 0) tiles_free(lane);
         if (kind) {
@@ -538,7 +556,50 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
                  : "memory");
 }
 
-template <int BN2, bool B_MN>
+// Work of one CTA pair.  Whole tiles (sk = 0): tiles pair, pair + npairs, ...  Stream-K
+// (sk = 1): the pair takes units [pair * U / npairs, (pair + 1) * U / npairs) of the U = tiles x
+// k-blocks units, tile-major.  The host enables stream-K only when there are at least as many
+// tiles as pairs, so every range covers >= nk units: a tile is split at most once, between the
+// end of pair p's range (its first k-blocks, the pair's LAST item: SK_PART_IN) and the start
+// of pair p+1's (its last k-blocks, that pair's FIRST item: SK_PART_OUT).  Pair p+1 finishes
+// its part early and leaves the fp32 partial in slot p+1; pair p adds it in its epilogue.
+enum { SK_FULL = 0, SK_PART_OUT = 1, SK_PART_IN = 2 };
+
+struct PairWork {
+    int nk, ntiles, npairs, tile;
+    long u, end;
+    bool sk;
+    __device__ PairWork(int sk_, int nk_, int ntiles_, int pair, int npairs_)
+        : nk(nk_), ntiles(ntiles_), npairs(npairs_), tile(pair), u(0), end(0), sk(sk_ != 0) {
+        if (sk) {
+            const long units = (long)ntiles * nk;
+            u = units * pair / npairs;
+            end = units * (pair + 1) / npairs;
+        }
+    }
+    // next item: tile, k-block range [kb0, kb1), role; false when the pair is done
+    __device__ bool next(int& t, int& kb0, int& kb1, int& role) {
+        if (!sk) {
+            if (tile >= ntiles) return false;
+            t = tile; kb0 = 0; kb1 = nk; role = SK_FULL;
+            tile += npairs;
+            return true;
+        }
+        if (u >= end) return false;
+        t = (int)(u / nk);
+        kb0 = (int)(u - (long)t * nk);
+        kb1 = (int)min((long)nk, kb0 + (end - u));
+        role = kb0 > 0 ? SK_PART_OUT : (kb1 < nk ? SK_PART_IN : SK_FULL);
+        u += kb1 - kb0;
+        return true;
+    }
+};
+
+// stream-K partial of one epilogue warp: 32 rows x 128 columns, fp32, TMEM-fragment order
+constexpr int SK_WARP_FLOATS = 32 * 128;
+constexpr int SK_CTA_BYTES = EPI_WARPS2 * SK_WARP_FLOATS * 4;  // 128 KB: 4 stages of the 256-wide ring
+
+template <int BN2, bool B_MN, bool SK>
 __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_constant__ TcMaps maps, const TcParams p) {
     using Cfg = Tc2Cfg<BN2>;
     constexpr int BH2 = Cfg::BH;
@@ -553,7 +614,8 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
     auto tfull_bar = [&](int a) { return bars + 8 * (2 * S + a); };
     auto tempty_bar = [&](int a) { return bars + 8 * (2 * S + 2 + a); };
     const uint32_t drain_bar = bars + 8 * (2 * S + 4);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S * Cfg::STAGE + Cfg::EPI + 8 * (2 * S + 5));
+    const uint32_t part_bar = bars + 8 * (2 * S + 5);  // stream-K partial landed in the stages
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S * Cfg::STAGE + Cfg::EPI + 8 * (2 * S + 6));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_rank();
@@ -567,6 +629,7 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
             mbar_init(tempty_bar(a), 2 * EPI_WARPS2);  // leader: both CTAs' epilogue warps
         }
         mbar_init(drain_bar, 1);
+        mbar_init(part_bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
@@ -593,9 +656,11 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
         int s = 0;
         uint32_t ph = 0;
         bool ok = true;
-        for (int tile = pair; tile < ntiles && ok; tile += npairs) {
+        PairWork w(SK ? 1 : 0, nk, ntiles, pair, npairs);
+        int tile, kb0, kb1, role = SK_FULL;
+        while (ok && w.next(tile, kb0, kb1, role)) {
             const int mb = tile % num_m2, nb = tile / num_m2;
-            for (int kb = 0; kb < nk; ++kb) {
+            for (int kb = kb0; kb < kb1; ++kb) {
                 if (!mbar_wait(empty_bar(s), ph ^ 1, p.err, 11)) { ok = false; break; }
                 const bool seg2 = kb >= nk1;
                 const CUtensorMap* ma = seg2 ? &maps.a2 : &maps.a1;
@@ -615,6 +680,29 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
                 if (++s == S) { s = 0; ph ^= 1; }
             }
         }
+        if (SK && ok && role == SK_PART_IN) {
+            // The last item is the head of a split tile: once the next pair has published the
+            // tile's tail (its first item), stream this CTA's 128 KB of it into the next four
+            // stages of the ring as the mainloop releases them.
+            if (BN2 == 256) {
+                int* flag = p.sk_flag + (pair + 1) * 2 + (int)rank;
+                if (flag_wait(flag, EPI_WARPS2, p.err, 18)) {
+                    *flag = 0;  // consumed; the next launch starts from zero
+                    asm volatile("fence.proxy.async.global;" ::: "memory");
+                    mbar_expect_tx(part_bar, SK_CTA_BYTES);
+                    const unsigned char* src = reinterpret_cast<const unsigned char*>(
+                        p.sk_part + ((size_t)(pair + 1) * 2 + rank) * (EPI_WARPS2 * SK_WARP_FLOATS));
+                    for (int j = 0; j < SK_CTA_BYTES / Cfg::STAGE; ++j) {
+                        if (!mbar_wait(empty_bar(s), ph ^ 1, p.err, 11)) break;
+                        bulk_load(base + s * Cfg::STAGE, src + (size_t)j * Cfg::STAGE, Cfg::STAGE, part_bar);
+                        if (++s == S) { s = 0; ph ^= 1; }
+                    }
+                } else {
+                    mbar_arrive(part_bar);  // no data: let the epilogue go on (the error is recorded)
+                }
+                mbar_wait(part_bar, 0, p.err, 19);  // no copy still in flight when the CTA exits
+            }
+        }
     } else if (warp == 1 && lane == 0 && rank == 0) {
         // ------------------------------------------------------------ MMA issuer (leader)
         const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((B_MN ? 1u : 0u) << 16) |
@@ -627,13 +715,15 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
         int s = 0, u = 0;
         uint32_t ph = 0;
         bool ok = true;
-        for (int tile = pair; tile < ntiles && ok; tile += npairs, ++u) {
+        PairWork w(SK ? 1 : 0, nk, ntiles, pair, npairs);
+        int tile, kb0, kb1, role;
+        for (; ok && w.next(tile, kb0, kb1, role); ++u) {
             const int a = u & 1;
             ok = mbar_wait(tempty_bar(a), ((u >> 1) & 1) ^ 1, p.err, 12);
             if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t tacc = tmem_base + a * BN2;
-            for (int kb = 0; kb < nk; ++kb) {
+            for (int kb = kb0; kb < kb1; ++kb) {
                 if (!mbar_wait(full_bar(s), ph, p.err, 13)) { ok = false; break; }
                 const uint64_t soff = (uint64_t)((s * Cfg::STAGE) >> 4);
                 const uint64_t ad = a_desc0 + soff, bd = b_desc0 + soff;
@@ -641,10 +731,10 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
                 if (kv >= BKE) {
 #pragma unroll
                     for (int k16 = 0; k16 < BKE / 16; ++k16)
-                        mma_f16_pair(tacc, ad + A_STEP * k16, bd + B_STEP * k16, idesc, (kb | k16) ? 1u : 0u);
+                        mma_f16_pair(tacc, ad + A_STEP * k16, bd + B_STEP * k16, idesc, (kb > kb0 || k16) ? 1u : 0u);
                 } else {
                     for (int k16 = 0; k16 < (kv + 15) / 16; ++k16)
-                        mma_f16_pair(tacc, ad + A_STEP * k16, bd + B_STEP * k16, idesc, (kb | k16) ? 1u : 0u);
+                        mma_f16_pair(tacc, ad + A_STEP * k16, bd + B_STEP * k16, idesc, (kb > kb0 || k16) ? 1u : 0u);
                 }
                 mma_commit_pair(empty0 + 8 * s);
                 mma_commit_pair(empty1 + 8 * s);
@@ -659,10 +749,10 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
     } else if (warp >= 2) {
         // ------------------------------------------------------------ epilogue (both CTAs)
         // TMEM lanes 32*quad .. 32*quad+31, columns coff .. coff + BN2/2 - 1 of the tile
-        const int quad = warp & 3, coff = ((warp - 2) >> 2) * (BN2 / 2);
+        const int ew = warp - 2, quad = warp & 3, coff = (ew >> 2) * (BN2 / 2);
         EpiTiles tiles;
-        tiles.o = smem + S * Cfg::STAGE + (warp - 2) * EPI_OUT_BYTES;
-        tiles.x = smem + S * Cfg::STAGE + EPI_WARPS2 * EPI_OUT_BYTES + (warp - 2) * EPI_AUX_BYTES;
+        tiles.o = smem + S * Cfg::STAGE + ew * EPI_OUT_BYTES;
+        tiles.x = smem + S * Cfg::STAGE + EPI_WARPS2 * EPI_OUT_BYTES + ew * EPI_AUX_BYTES;
         tiles.o_s = smem_u32(tiles.o);
         tiles.x_s = smem_u32(tiles.x);
         const uint32_t leader_tempty0 = map_rank(tempty_bar(0), 0), leader_tempty1 = map_rank(tempty_bar(1), 0);
@@ -672,28 +762,70 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
             rows = tl < ntiles ? max(0, min(32, mlim - m_base)) : 0;
             n0 = (tl / num_m2) * BN2 + coff;
         };
+        PairWork w(SK ? 1 : 0, nk, ntiles, pair, npairs);
+        // the ring slot after this pair's last k-block: where a stream-K partial lands
+        int units = 0, first_epi = pair;
+        if (SK) {
+            first_epi = ntiles;
+            PairWork c = w;
+            int t, k0, k1, r;
+            while (c.next(t, k0, k1, r)) {
+                units += k1 - k0;
+                if (r != SK_PART_OUT && first_epi == ntiles) first_epi = t;
+            }
+        }
         float4 pre[8];
         {
             int mb0, r0, n00;
-            tile_rows(pair, mb0, r0, n00);
+            tile_rows(first_epi, mb0, r0, n00);
             fetch_input(p, epi_input_kind(p.mode), mb0, r0, n00, lane, pre);
         }
-        int u = 0;
-        for (int tile = pair; tile < ntiles; tile += npairs, ++u) {
+        int tile, kb0, kb1, role;
+        bool have = w.next(tile, kb0, kb1, role);
+        for (int u = 0; have; ++u) {
+            int ntile = ntiles, nkb0, nkb1, nrole;
+            const bool nhave = w.next(ntile, nkb0, nkb1, nrole);
+            if (!nhave) ntile = ntiles;
             const int a = u & 1;
             bool ok = true;
             if (lane == 0) ok = mbar_wait(tfull_bar(a), (u >> 1) & 1, p.err, 14);
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            int m_base, rows, n0, nm, nr, nn;
-            tile_rows(tile, m_base, rows, n0);
-            tile_rows(tile + npairs, nm, nr, nn);
-            epilogue_tile<BN2 / 64>(p, maps, tmem_base + ((uint32_t)(quad * 32) << 16) + a * BN2 + coff, m_base, rows,
-                                    n0, nm, nr, nn, tiles, lane, pre);
+            const uint32_t trow = tmem_base + ((uint32_t)(quad * 32) << 16) + a * BN2 + coff;
+            if (SK && role == SK_PART_OUT) {
+                // tail of a split tile: raw fp32 accumulators to slot `pair`, then count this warp in
+                float4* dst = reinterpret_cast<float4*>(
+                    p.sk_part + (((size_t)pair * 2 + rank) * EPI_WARPS2 + ew) * SK_WARP_FLOATS);
+                for (int c = 0; c < BN2 / 64; ++c) {
+                    uint32_t r[32];
+                    tmem_ld32(trow + c * 32, r);
+#pragma unroll
+                    for (int g = 0; g < 8; ++g)
+                        __stcg(dst + (c * 8 + g) * 32 + lane,
+                               make_float4(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1]),
+                                           __uint_as_float(r[4 * g + 2]), __uint_as_float(r[4 * g + 3])));
+                }
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) red_release_add(p.sk_flag + pair * 2 + (int)rank, 1);
+            } else {
+                const float4* part = nullptr;
+                if (SK && role == SK_PART_IN && BN2 == 256) {
+                    // head of a split tile: the producer streams the tail's partial into the ring
+                    mbar_wait(part_bar, 0, p.err, 20);
+                    part = reinterpret_cast<const float4*>(smem + ((units + (ew >> 1)) % S) * Cfg::STAGE +
+                                                           (ew & 1) * (SK_WARP_FLOATS * 4));
+                }
+                int m_base, rows, n0, nm, nr, nn;
+                tile_rows(tile, m_base, rows, n0);
+                tile_rows(ntile, nm, nr, nn);
+                epilogue_tile<BN2 / 64>(p, maps, trow, m_base, rows, n0, nm, nr, nn, tiles, lane, pre, part);
+            }
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(a ? leader_tempty1 : leader_tempty0);
+            tile = ntile; kb0 = nkb0; kb1 = nkb1; role = nrole; have = nhave;
         }
         if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
@@ -816,6 +948,19 @@ void launch_tc(const GemmArgs& a, int* err, cudaStream_t s) {
     cudaLaunchKernelEx(&cfg, kern, maps, p);
 }
 
+// Stream-K where it pays: 256-wide pair tiles, at least as many tiles as pairs (one split per
+// tile at most) and a workspace.  Its cost is the pair's share of k-blocks plus the partial
+// tile's round trip through L2 (a 256 KB write early, a read at the end, both while every SM
+// streams operands), measured at about 12 k-blocks of 256 x 256 x 64; whole tiles cost their
+// rounds.  So only long reductions with an idle last round gain (K = 3072, 4096 at N = 1024).
+bool sk_pays(int bn2, int tiles, int pairs, const GemmArgs& a) {
+    if (bn2 != 256 || !a.sk_part || !a.sk_flag || tiles < pairs || pairs < 2) return false;
+    const long nk = (a.K1 + BKE - 1) / BKE + (a.K2 + BKE - 1) / BKE;
+    const long rounds = (tiles + pairs - 1) / pairs;
+    const long share = (tiles * nk + pairs - 1) / pairs;
+    return share + 12 < 0.92 * rounds * nk;
+}
+
 template <int BN2, bool B_MN>
 void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
     using Cfg = Tc2Cfg<BN2>;
@@ -840,11 +985,15 @@ void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
     p.resid = a.resid; p.ldr = a.ldr; p.aux = a.aux; p.ldaux = a.ldaux; p.auxin = a.auxin; p.ldauxin = a.ldauxin;
     p.colscale2 = a.colscale2; p.bias = a.bias; p.nvalid = a.nvalid; p.mvalid = a.mvalid; p.err = err;
     p.rope = a.rope; p.rope_T = a.rope_T; p.rope_cols = a.rope_cols;
-    auto kern = gemm_tc2_kernel<BN2, B_MN>;
+    p.sk_part = a.sk_part; p.sk_flag = a.sk_flag;
+    auto whole = gemm_tc2_kernel<BN2, B_MN, false>;
+    auto split = gemm_tc2_kernel<BN2, B_MN, BN2 == 256>;
     static bool configured = false;
     if (!configured) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
-        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+        for (auto k : {whole, split}) {
+            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+            cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+        }
         configured = true;
     }
     if (!g_num_sms) {
@@ -854,6 +1003,7 @@ void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
     }
     const int tiles = ((a.M + 2 * BM - 1) / (2 * BM)) * (a.N / BN2);
     const int pairs = tiles < g_num_sms / 2 ? tiles : g_num_sms / 2;
+    const auto kern = sk_pays(BN2, tiles, pairs, a) ? split : whole;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
     cfg.blockDim = dim3(NTHREADS2, 1, 1);
@@ -900,6 +1050,9 @@ void gemm_tc2_width(const GemmArgs& a, int* err, cudaStream_t s, int width) {
     }
 }
 
+long gemm_sk_part_floats(int num_sms) { return (long)(num_sms / 2) * 2 * EPI_WARPS2 * SK_WARP_FLOATS; }
+int gemm_sk_flag_count(int num_sms) { return (num_sms / 2) * 2; }
+
 void gemm_tc2(const GemmArgs& a, int* err, cudaStream_t s) { gemm_tc2_width(a, err, s, a.N % 256 == 0 ? 256 : 128); }
 
 void gemm_tc_auto(const GemmArgs& a, int* err, cudaStream_t s) {
@@ -920,7 +1073,12 @@ void gemm_tc_auto(const GemmArgs& a, int* err, cudaStream_t s) {
     int choice = 0;
     if (gemm_tc2_supported(a)) {
         if (a.N % 256 == 0) {
-            const double c = rounds(m2 * (a.N / 256), pairs) * 256.0 * eff[1];
+            const long t2 = m2 * (a.N / 256);
+            // stream-K spreads the k-blocks evenly: cost by the mean share plus its fix-up
+            const long nk = (a.K1 + BKE - 1) / BKE + (a.K2 + BKE - 1) / BKE;
+            const double c = sk_pays(256, (int)t2, (int)std::min(t2, pairs), a)
+                                 ? ((double)t2 * nk / pairs + 12.0) / nk * 256.0 * eff[1]
+                                 : rounds(t2, pairs) * 256.0 * eff[1];
             if (c < best) { best = c; choice = 1; }
         }
         const double c = rounds(m2 * (a.N / 128), pairs) * 128.0 * eff[2];

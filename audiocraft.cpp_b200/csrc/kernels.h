@@ -61,7 +61,14 @@ struct GemmArgs {
     int rope_T = 1, rope_cols = 0;     //   ([rope_T][32] (cos, sin) table, 64-column heads; after aux)
     int nvalid = 1 << 30;              // columns >= nvalid are not written
     int mvalid = 1 << 30;              // rows >= mvalid are not written
+    // Stream-K workspace of the 2-CTA kernel (null: whole tiles only).  sk_part holds
+    // gemm_sk_part_floats(), sk_flag gemm_sk_flag_count() zero-initialised ints that every
+    // launch leaves at zero.  Launches sharing a workspace must not overlap on the device.
+    float* sk_part = nullptr;
+    int* sk_flag = nullptr;
 };
+long gemm_sk_part_floats(int num_sms);
+int gemm_sk_flag_count(int num_sms);
 
 void gemm(const GemmArgs& a, cudaStream_t s);                 // mma.sync path, any layout
 bool gemm_tc_supported(const GemmArgs& a);                     // shapes the tcgen05 path takes

@@ -66,6 +66,40 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
     return mbar_try(bar, parity) || mbar_wait_slow(bar, parity, err, code);
 }
 
+// Global flags between CTAs of one grid (all co-resident): release add by the producer side,
+// bounded acquire poll by the consumer side.
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void red_release_add(int* p, int v) {
+    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Wait until *flag >= target; false (and `code` recorded) if that does not happen in time.
+static __device__ __noinline__ bool flag_wait(const int* flag, int target, int* err, int code) {
+    const unsigned long long t0 = globaltimer();
+    while (ld_acquire_gpu(flag) < target) {
+        __nanosleep(256);
+        if (globaltimer() - t0 > WAIT_NS) {
+            atomicCAS(err, 0, code);
+            return false;
+        }
+        if (*(volatile int*)err) return false;
+    }
+    return true;
+}
+
+// Contiguous global -> shared copy by the bulk-copy engine (16-byte aligned, size % 16 == 0),
+// completing on an mbarrier of this CTA.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }

@@ -168,7 +168,9 @@ double act_step_flops(act_ctx* ctx, int n);
 /* stand-alone projection GEMM on host buffers (tests and the kernel sweep): C[M][N] fp32 =
  * A[M][K] . B(n,k) with bf16 A and B, B as [N][K] (b_mn_major 0) or [K][N] (1);
  * path 0 = automatic, 1 = mma.sync kernel, 2 = tcgen05 kernel, 3 = tcgen05 2-CTA (cta_group::2)
- * kernel, 4 = the 2-CTA kernel with 128-column pair tiles; when reps > 0 the GEMM is
+ * kernel (stream-K split of the tiles where whole tiles would leave the last round mostly
+ * idle), 4 = the 2-CTA kernel with 128-column pair tiles, 5 = the 2-CTA kernel on whole
+ * tiles only; when reps > 0 the GEMM is
  * re-run reps times back to back and *ms_per_call receives the mean device time */
 int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path,
                   int reps, float* ms_per_call);

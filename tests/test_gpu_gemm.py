@@ -16,13 +16,17 @@ def bits_to_f32(b):
     return (b.astype(np.uint32) << 16).view(np.float32)
 
 
-@pytest.mark.parametrize("path", [0, 1, 2, 3, 4], ids=["auto", "mma", "tcgen05", "tcgen05_pair", "tcgen05_pair128"])
+@pytest.mark.parametrize("path", [0, 1, 2, 3, 4, 5],
+                         ids=["auto", "mma", "tcgen05", "tcgen05_pair", "tcgen05_pair128", "tcgen05_pair_whole"])
 @pytest.mark.parametrize("b_mn", [False, True], ids=["NT", "NN"])
 @pytest.mark.parametrize("M,N,K", [(128, 128, 64), (300, 256, 128), (6000, 1024, 1024), (1000, 4096, 256),
-                                   (130, 512, 4096), (1000, 384, 256)])
+                                   (130, 512, 4096), (1000, 384, 256),
+                                   # stream-K on the 2-CTA path (more pair tiles than pairs, a mostly idle
+                                   # last round, long reductions): 76 tiles; 80 tiles with ragged rows
+                                   (4864, 1024, 2048), (5000, 1024, 2112)])
 def test_gemm_matches_numpy(path, b_mn, M, N, K):
     # path 3 takes 256-wide pair tiles when N % 256 == 0, else 128-wide ones (N = 384)
-    if path in (3, 4) and M <= 128:
+    if path in (3, 4, 5) and M <= 128:
         pytest.skip("the 2-CTA kernel needs M > 128")
     rng = np.random.default_rng(M + N + K)
     a = bf16_bits(rng.standard_normal((M, K)))

@@ -84,6 +84,26 @@ def test_graph_replay_matches_first_run():
         np.testing.assert_allclose(g, runs[0][1], rtol=1e-4, atol=1e-6 * np.abs(runs[0][1]).max())
 
 
+def test_mf_stream_k_matches_whole_tiles(monkeypatch):
+    """d1024 DiT, 8 x 750 frames: the 1024- and 4096-wide projections have more 256 x 256 pair
+    tiles than SM pairs with a mostly idle last round, so the GEMMs split them stream-K.  The
+    step must equal the same step on whole tiles up to fp32 summation order, and stay equal
+    over the eager, captured and replayed runs (the partial-tile flags reset every launch)."""
+    kw = dict(dim=1024, layers=2, heads=16, ff=4096, lat=128, cond=64, tdim=32, T=750, C=32, rank=16,
+              alpha=32.0, batch=8, seed=11)
+    monkeypatch.setenv("ACTRAIN_STREAMK", "0")
+    whole = MfCase(**kw)
+    monkeypatch.delenv("ACTRAIN_STREAMK")
+    split = MfCase(**kw)
+    inp = whole.inputs(modes=["cond", "padded", "null"] + ["cond"] * 5)
+    loss0 = whole.ctx.mf_step(*inp)
+    g0 = whole.ctx.get_grads()
+    for _ in range(3):
+        loss = split.ctx.mf_step(*inp)
+        _check(loss, loss0, split.ctx.get_grads(), g0, split.layout)
+        split.ctx.zero_grads()
+
+
 def test_gradients_accumulate_over_microbatches():
     case = MfCase(seed=7)
     a, b = case.inputs(n=2), case.inputs(n=1)
