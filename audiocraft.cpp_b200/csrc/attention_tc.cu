@@ -101,6 +101,25 @@ __device__ __forceinline__ float fast_ex2(float x) {
     return y;
 }
 
+// Packed fp32 pair arithmetic (sm_100: one instruction for two lanes' worth of FMA / ADD / MUL).
+__device__ __forceinline__ unsigned long long f2_bits(float2 v) { return *reinterpret_cast<unsigned long long*>(&v); }
+__device__ __forceinline__ float2 bits_f2(unsigned long long v) { return *reinterpret_cast<float2*>(&v); }
+__device__ __forceinline__ float2 fma_f2(float2 a, float2 b, float2 c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+    return bits_f2(d);
+}
+__device__ __forceinline__ float2 sub_f2(float2 a, float2 b) {
+    unsigned long long d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return bits_f2(d);
+}
+__device__ __forceinline__ float2 mul_f2(float2 a, float2 b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return bits_f2(d);
+}
+
 // byte offset of 16-byte unit u of row r in a 1024-aligned, 128-byte-swizzled tile
 __device__ __forceinline__ uint32_t at_sw128(int r, int u) { return r * 128 + ((u ^ (r & 7)) << 4); }
 
@@ -467,18 +486,24 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
         unsigned char* Pt = smem + AB_P_OFF;
         unsigned char* dSt = smem + AB_DS_OFF;
         bool ok = true;
+        // this thread's element of a block's lse (t < 64) or D (t >= 64), loaded one block ahead
+        // so that the global-load latency overlaps the current block's work
+        const int t = threadIdx.x - 64 - grp * 128, c = grp * 64 + (t & 63);
+        auto fetch_ld = [&](int u) {
+            const int qi = (qb_first + u) * AB_BQ + c;
+            const long off = ((long)b * a.H + h) * a.T + qi;
+            return (u < nq && qi < a.T) ? (t < 64 ? a.lse[off] : a.dvec[off]) : 0.f;
+        };
+        float next_ld = fetch_ld(0);
         for (int u = 0; u < nq; ++u) {
             const int q0 = (qb_first + u) * AB_BQ;
-            // this block's lse / D into shared memory (one element per thread)
             {
                 float* L = lsd + (u & 1) * 256;
-                const int t = threadIdx.x - 64 - grp * 128, c = grp * 64 + (t & 63), qi = q0 + c;
-                const long off = ((long)b * a.H + h) * a.T + qi;
-                if (t < 64) L[c] = qi < a.T ? a.lse[off] : 0.f;
-                else L[128 + c] = qi < a.T ? a.dvec[off] : 0.f;
+                L[t < 64 ? c : 128 + c] = t < 64 ? -next_ld : next_ld;  // -lse | D
                 if (grp == 0) asm volatile("bar.sync 1, 128;" ::: "memory");
                 else asm volatile("bar.sync 3, 128;" ::: "memory");
             }
+            next_ld = fetch_ld(u + 1);
             const float* L = lsd + (u & 1) * 256;
             // after a failed wait the loop keeps running (without work) so that every warp still
             // reaches each named barrier; waits after a failure return at once (error word set)
@@ -503,20 +528,38 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
                 int qlo = 0, qhi = min(32, a.T - qbase);
                 if (key >= kv_end) qhi = 0;
                 if (a.causal) qlo = max(0, key - qbase);
-                const float4* L4 = reinterpret_cast<const float4*>(L + qt * 32);         // lse
+                const float4* L4 = reinterpret_cast<const float4*>(L + qt * 32);         // -lse
                 const float4* D4 = reinterpret_cast<const float4*>(L + 128 + qt * 32);   // D
-                const bool full = qlo == 0 && qhi == 32;  // all but the edge blocks
+                if (qlo == 0 && qhi == 32) {  // all but the edge blocks: pairs of columns
+                    const float2 sl = make_float2(sl2, sl2);
 #pragma unroll
-                for (int c4 = 0; c4 < 8; ++c4) {
-                    const float4 l = L4[c4], dv = D4[c4];
-                    const float lv[4] = {l.x, l.y, l.z, l.w}, dd[4] = {dv.x, dv.y, dv.z, dv.w};
+                    for (int c4 = 0; c4 < 8; ++c4) {
+                        const float4 l = L4[c4], dv = D4[c4];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int c = 4 * c4 + e;
-                        float pv = fast_ex2(fmaf(sv[c], sl2, -lv[e]));
-                        if (!full && (c < qlo || c >= qhi)) pv = 0.f;
-                        sv[c] = pv;
-                        dp[c] = pv * (dp[c] - dd[e]);
+                        for (int e = 0; e < 2; ++e) {
+                            const int c = 4 * c4 + 2 * e;
+                            const float2 x = fma_f2(make_float2(sv[c], sv[c + 1]), sl,
+                                                    e ? make_float2(l.z, l.w) : make_float2(l.x, l.y));
+                            const float2 pv = make_float2(fast_ex2(x.x), fast_ex2(x.y));
+                            const float2 ds = mul_f2(pv, sub_f2(make_float2(dp[c], dp[c + 1]),
+                                                                e ? make_float2(dv.z, dv.w) : make_float2(dv.x, dv.y)));
+                            sv[c] = pv.x; sv[c + 1] = pv.y;
+                            dp[c] = ds.x; dp[c + 1] = ds.y;
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int c4 = 0; c4 < 8; ++c4) {
+                        const float4 l = L4[c4], dv = D4[c4];
+                        const float lv[4] = {l.x, l.y, l.z, l.w}, dd[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int c = 4 * c4 + e;
+                            float pv = fast_ex2(fmaf(sv[c], sl2, lv[e]));
+                            if (c < qlo || c >= qhi) pv = 0.f;
+                            sv[c] = pv;
+                            dp[c] = pv * (dp[c] - dd[e]);
+                        }
                     }
                 }
                 if (qt == 2 * grp && u > 0) {  // the previous block's MMAs have read P^T / dS^T
