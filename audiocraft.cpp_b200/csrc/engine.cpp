@@ -256,8 +256,15 @@ struct act_ctx {
             g.sk_part = sk_part;
             g.sk_flag = sk_flag;
         }
-        if (use_tc && gemm_tc_supported(g)) timed(cls, fl, 0, [&] { gemm_tc_auto(g, kerr, stream); });
-        else timed(cls, fl, 0, [&] { gemm(g, stream); });
+        if (use_tc && gemm_tc_supported(g)) {
+            timed(cls, fl, 0, [&] { gemm_tc_auto(g, kerr, stream); });
+        } else {
+            timed(cls, fl, 0, [&] { gemm(g, stream); });
+            if (g.out_bf)  // the generic path has no second output: convert afterwards
+                timed(2, 0, 0, [&] {
+                    residual_to_bf16(static_cast<float*>(g.out), nullptr, g.out_bf, nullptr, g.M, g.N, stream);
+                });
+        }
     }
 
     // Issue fn's kernels on the side stream, after everything the main stream has issued so far
@@ -497,16 +504,25 @@ struct act_ctx {
                 proj_fwd(y.p[5], y.f, rows, y.U[5], e);
                 timed(2, 0, 6.0 * rows * F, [&] { gelu_fwd(gelu_tab, y.z, y.gact, rows * F, 1, stream); });
             }
+            // the layer output also in bf16 where a skip projection reads it: as this layer's saved
+            // copy (a skip source) or as the next layer's x_prev operand
             GemmArgs o; o.mode = EPI_RESID_F32; o.out = y.xout; o.ldo = D; o.resid = y.xmid2; o.ldr = D;
+            o.out_bf = y.produces ? y.xsave_bf : (writes_prev_bf(l) ? xprev_bf : nullptr);
             if (y.p[6].dora) { o.aux = y.Yaux[6]; o.ldaux = D; }
             proj_fwd(y.p[6], y.gact, rows, y.U[6], o);
         }
-        if (y.produces) timed(2, 0, 0, [&] { residual_to_bf16(y.xout, nullptr, y.xsave_bf, nullptr, (int)rows, D, stream); });
     }
+
+    // block l's ff.2 epilogue leaves bf16(xout) in xprev_bf for the skip projection of block l+1
+    bool writes_prev_bf(int l) const { return !layers[l].produces && l + 1 < L && layers[l + 1].consumes; }
 
     // Backward of block l.  On entry dx/dxbf hold d(loss)/d(xout) (dxbf already scaled by
     // the DoRA factor of ff.2).  On exit dx holds d(loss)/d(xin) and dxbf is NOT prepared.
-    void block_bwd(int l, int n, const int* nvalid_dev, bool need_dx_in) {
+    // need_dx_in: the gradient of the block's input is needed (accumulated into dx by the last
+    // norm's backward, which also writes dxbf = bf16((dx + cvt_extra) * cvt_scale) when cvt is
+    // set: the operand of whatever consumes dx next, without a separate conversion pass)
+    void block_bwd(int l, int n, const int* nvalid_dev, bool need_dx_in, bool cvt = false,
+                   const float* cvt_extra = nullptr, const float* cvt_scale = nullptr) {
         Layer& y = layers[l];
         const long rows = (long)n * T, crows = (long)n * C;
         const bool dit = mf;
@@ -583,7 +599,10 @@ struct act_ctx {
             proj_bwd(y.p[0], dqkv, rows, y.h1, y.U[0], y.p[0].dora ? y.Yaux[0] : y.qkv, need_dx_in, e);
         }
         if (need_dx_in)
-            timed(2, 0, 0, [&] { layernorm_bwd(dtmp, y.xin, y.norm[0], y.mu[0], y.rs[0], dx, 1, nullptr, nullptr, nullptr, (int)rows, D, stream); });
+            timed(2, 0, 0, [&] {
+                layernorm_bwd(dtmp, y.xin, y.norm[0], y.mu[0], y.rs[0], dx, 1, cvt ? cvt_extra : nullptr,
+                              cvt ? dxbf : nullptr, cvt ? cvt_scale : nullptr, (int)rows, D, stream);
+            });
     }
 
     double attn_flops(int n, int keys, bool self) const {
@@ -594,10 +613,11 @@ struct act_ctx {
     }
 
     // dxbf := bf16((dx + dsaved[l]) * g_ff2(l))  -- entering block l's backward
+    const float* entry_extra(int l) { return layers[l].produces ? layers[l].dsaved : nullptr; }
+    const float* entry_scale(int l) { return layers[l].p[6].dora ? layers[l].p[6].g : nullptr; }
     void prepare_dxbf(int l, int n) {
-        Layer& y = layers[l];
         const long rows = (long)n * T;
-        timed(2, 0, 0, [&] { residual_to_bf16(dx, y.produces ? y.dsaved : nullptr, dxbf, y.p[6].dora ? y.p[6].g : nullptr, (int)rows, D, stream); });
+        timed(2, 0, 0, [&] { residual_to_bf16(dx, entry_extra(l), dxbf, entry_scale(l), (int)rows, D, stream); });
     }
 
     void mf_graph_body(int n) {
@@ -622,7 +642,8 @@ struct act_ctx {
         for (int l = 0; l < L; ++l) {
             Layer& y = layers[l];
             if (y.consumes) {
-                timed(2, 0, 0, [&] { residual_to_bf16(layers[l - 1].xout, nullptr, xprev_bf, nullptr, (int)rows, D, stream); });
+                if (!writes_prev_bf(l - 1))
+                    timed(2, 0, 0, [&] { residual_to_bf16(layers[l - 1].xout, nullptr, xprev_bf, nullptr, (int)rows, D, stream); });
                 GemmArgs k;
                 k.M = (int)rows; k.N = D; k.K1 = D; k.K2 = D;
                 k.A1 = xprev_bf; k.lda1 = D; k.A2 = layers[y.src].xsave_bf; k.lda2 = D;
@@ -651,16 +672,20 @@ struct act_ctx {
         timed(2, 0, 0, [&] {
             for (auto& y : layers)
                 if (y.produces) CK(cudaMemsetAsync(y.dsaved, 0, sizeof(float) * rows * D, stream));
-            layernorm_bwd(dtmp, last.xout, onw, muo, rso, dx, 0, nullptr, nullptr, nullptr, (int)rows, D, stream);
+            // also block L-1's entry operand dxbf (see block_bwd's cvt)
+            layernorm_bwd(dtmp, last.xout, onw, muo, rso, dx, 0, entry_extra(L - 1), dxbf, entry_scale(L - 1),
+                          (int)rows, D, stream);
         });
         const int first = ad.first_layer;
         for (int l = L - 1; l >= first; --l) {
             Layer& y = layers[l];
-            prepare_dxbf(l, n);
-            const bool need_dx = l > first;
-            block_bwd(l, n, d_nvalid, need_dx);
-            if (need_dx && y.consumes) {
-                timed(2, 0, 0, [&] { residual_to_bf16(dx, nullptr, dxbf, nullptr, (int)rows, D, stream); });
+            const bool need_dx = l > first, via_skip = need_dx && y.consumes;
+            // the block's last norm backward writes the next operand: bf16(dx) for the skip
+            // projection, else block l-1's entry operand
+            if (via_skip) block_bwd(l, n, d_nvalid, need_dx, true, nullptr, nullptr);
+            else if (need_dx) block_bwd(l, n, d_nvalid, need_dx, true, entry_extra(l - 1), entry_scale(l - 1));
+            else block_bwd(l, n, d_nvalid, need_dx);
+            if (via_skip) {
                 GemmArgs a;  // d x_prev = dx Wskip[:, :D]
                 a.M = (int)rows; a.N = D; a.K1 = D; a.A1 = dxbf; a.lda1 = D;
                 a.B1 = skip[y.proj]; a.ldb1 = 2 * D; a.b_kmajor = false; a.mode = EPI_STORE_F32; a.out = dx; a.ldo = D;
@@ -668,6 +693,7 @@ struct act_ctx {
                 GemmArgs b = a;  // d saved += dx Wskip[:, D:]
                 b.B1 = skip[y.proj] + D; b.mode = EPI_ACCUM_F32; b.out = layers[y.src].dsaved;
                 run_gemm(b, 0);
+                prepare_dxbf(l - 1, n);
             }
         }
         finish_adapters();
@@ -709,11 +735,14 @@ struct act_ctx {
                 dg.mode = EPI_ACCUM_F32; dg.out = dtmp + r0 * D; dg.ldo = D;
                 run_gemm(dg, 0);
             }
-        timed(2, 0, 0, [&] { layernorm_bwd(dtmp, last.xout, onw, muo, rso, dx, 0, nullptr, nullptr, nullptr, (int)rows, D, stream); });
+        timed(2, 0, 0, [&] {
+            layernorm_bwd(dtmp, last.xout, onw, muo, rso, dx, 0, entry_extra(L - 1), dxbf, entry_scale(L - 1),
+                          (int)rows, D, stream);
+        });
         const int first = ad.first_layer;
         for (int l = L - 1; l >= first; --l) {
-            prepare_dxbf(l, n);
-            block_bwd(l, n, nullptr, l > first);
+            if (l > first) block_bwd(l, n, nullptr, true, true, entry_extra(l - 1), entry_scale(l - 1));
+            else block_bwd(l, n, nullptr, false);
         }
         finish_adapters();
     }

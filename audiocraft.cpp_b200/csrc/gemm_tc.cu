@@ -54,6 +54,7 @@ struct TcParams {
     const float* resid;
     long ldr;
     bf16* aux;
+    bf16* out_bf;
     long ldaux;
     const bf16* auxin;
     long ldauxin;
@@ -72,6 +73,7 @@ struct TcParams {
 struct TcMaps {
     CUtensorMap a1, b1, a2, b2;
     CUtensorMap out, aux;  // epilogue stores: box 32 x 32, swizzle 128 B (fp32) / 64 B (bf16)
+    CUtensorMap out_bf;    // bf16 copy of an fp32 output
 };
 
 // Epilogue staging, per epilogue warp: a 32-row x 128-byte tile for the output chunk (32 fp32
@@ -241,6 +243,11 @@ __device__ __forceinline__ void epilogue_warp32(const TcParams& p, const TcMaps&
         if (p.mode != EPI_STORE_F32) add_row_f32(t.o, lane, v);  // residual / accumulator already staged in the tile
         put_row_f32(t.o, lane, v);
         tile_store(&maps.out, t.o_s, n, m_base, lane);
+        if (p.out_bf) {
+            if (p.aux) tiles_free(lane);  // the side tile is still being read by this chunk's aux store
+            put_row_b16(t.x, lane, v);
+            tile_store(&maps.out_bf, t.x_s, n, m_base, lane);
+        }
         return;
     }
     if (p.mode == EPI_BIAS_BF16) {
@@ -895,6 +902,8 @@ void make_epilogue_maps(TcMaps& maps, const GemmArgs& a) {
     make_store_map(&maps.out, a.out, f32, rows, a.N, a.ldo);
     if (a.aux) make_store_map(&maps.aux, a.aux, false, rows, a.N, a.ldaux);
     else maps.aux = maps.out;
+    if (a.out_bf && f32) make_store_map(&maps.out_bf, a.out_bf, false, rows, a.N, a.ldo);
+    else maps.out_bf = maps.out;
 }
 
 int g_num_sms = 0;
@@ -923,6 +932,7 @@ void launch_tc(const GemmArgs& a, int* err, cudaStream_t s) {
     p.resid = a.resid; p.ldr = a.ldr; p.aux = a.aux; p.ldaux = a.ldaux; p.auxin = a.auxin; p.ldauxin = a.ldauxin;
     p.colscale2 = a.colscale2; p.bias = a.bias; p.nvalid = a.nvalid; p.mvalid = a.mvalid; p.err = err;
     p.rope = a.rope; p.rope_T = a.rope_T; p.rope_cols = a.rope_cols;
+    p.out_bf = (a.mode == EPI_STORE_F32 || a.mode == EPI_ACCUM_F32 || a.mode == EPI_RESID_F32) ? a.out_bf : nullptr;
     auto kern = gemm_tc_kernel<BN, B_MN>;
     static bool configured = false;
     if (!configured) {
@@ -985,6 +995,7 @@ void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
     p.resid = a.resid; p.ldr = a.ldr; p.aux = a.aux; p.ldaux = a.ldaux; p.auxin = a.auxin; p.ldauxin = a.ldauxin;
     p.colscale2 = a.colscale2; p.bias = a.bias; p.nvalid = a.nvalid; p.mvalid = a.mvalid; p.err = err;
     p.rope = a.rope; p.rope_T = a.rope_T; p.rope_cols = a.rope_cols;
+    p.out_bf = (a.mode == EPI_STORE_F32 || a.mode == EPI_ACCUM_F32 || a.mode == EPI_RESID_F32) ? a.out_bf : nullptr;
     p.sk_part = a.sk_part; p.sk_flag = a.sk_flag;
     auto whole = gemm_tc2_kernel<BN2, B_MN, false>;
     auto split = gemm_tc2_kernel<BN2, B_MN, BN2 == 256>;
@@ -1034,7 +1045,7 @@ bool gemm_tc_supported(const GemmArgs& a) {
                          reinterpret_cast<uintptr_t>(a.auxin) | reinterpret_cast<uintptr_t>(a.resid) |
                          reinterpret_cast<uintptr_t>(a.colscale) | reinterpret_cast<uintptr_t>(a.A1) |
                          reinterpret_cast<uintptr_t>(a.B1) | reinterpret_cast<uintptr_t>(a.A2) |
-                         reinterpret_cast<uintptr_t>(a.B2);
+                         reinterpret_cast<uintptr_t>(a.B2) | reinterpret_cast<uintptr_t>(a.out_bf);
     return (al & 15) == 0;
 }
 

@@ -66,6 +66,8 @@ struct GemmArgs {
     // launch leaves at zero.  Launches sharing a workspace must not overlap on the device.
     float* sk_part = nullptr;
     int* sk_flag = nullptr;
+    // fp32 output modes (STORE / ACCUM / RESID): also store bf16(out), row stride ldo
+    bf16* out_bf = nullptr;
 };
 long gemm_sk_part_floats(int num_sms);
 int gemm_sk_flag_count(int num_sms);
