@@ -22,14 +22,16 @@
 // Backward (attn_bwd_tc): one CTA per 128 keys of one (clip, head), looping over blocks of 128
 // queries, with the scores recomputed in the transposed (key-major) frame:
 //   S^T = K Q^T, dP^T = V dO^T            (128 x 128 each, fp32 in TMEM)
-//   P^T = exp2(scale*log2e*S^T - lse), dS^T = P^T (dP^T - D)     (one key row per thread; bf16
-//                                         tiles in shared memory, queries contiguous)
+//   P^T = exp2(scale*log2e*S^T - lse), dS^T = P^T (dP^T - D)     (one key row per thread; P^T
+//                                         to TMEM, dS^T to shared memory, queries contiguous)
 //   dV += P^T dO, dK += dS^T Q             (fp32 accumulators stay in TMEM across the loop)
 //   dQ  = dS K  (dS read back from the dS^T tile as an MN-major operand), added into the fp32
 //         dQ accumulator with TMA bulk reduce-add tiles (out-of-range rows add exact zeros)
-// Warp roles: 0 TMA (K, V once; Q, dO per block into 2 stages), 1 MMA issue, 2..9 P / dS in two
+// Warp roles: 0 TMA (K, V once; Q, dO per block into 3 stages), 1 MMA issue, 2..9 P / dS in two
 // groups of query columns and the final dK / dV epilogue (RoPE undone on dK, DoRA column
-// factors), 10..13 the dQ epilogue.
+// factors), 10..13 the dQ epilogue.  P^T goes to TMEM as bf16 pairs and is the A operand of the
+// dV MMAs straight from there (released right after them); dS^T is double-buffered in shared
+// memory; Q / dO have three stages, so the next-but-one block's tiles load while this one runs.
 // Every mbarrier wait is bounded (globaltimer) and reports into the shared error word.
 #include <cuda.h>
 
@@ -94,6 +96,25 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* f) {
 }
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
+// D (+)= A B with A read from tensor memory (K-major: lane = row, two 16-bit K elements per
+// 32-bit column) and B from shared memory
+__device__ __forceinline__ void mma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
 
 __device__ __forceinline__ float fast_ex2(float x) {
     float y;
@@ -344,15 +365,16 @@ constexpr int AB_BQ = 128;  // queries per block
 constexpr int AB_T16 = 128 * 64 * 2;         // 16 KB: a 128 x 64 bf16 tile (128-byte rows)
 constexpr int AB_K_OFF = 0;
 constexpr int AB_V_OFF = AB_T16;
-constexpr int AB_QD_OFF = 2 * AB_T16;        // [2] stages of { Q, dO }
-constexpr int AB_P_OFF = 6 * AB_T16;         // P^T: [128 keys][128 queries] as two 64-query sub-tiles
-constexpr int AB_DS_OFF = 8 * AB_T16;        // dS^T, same layout
-constexpr int AB_DQ_OFF = 10 * AB_T16;       // dQ staging: two [128 queries][32 fp32] sub-tiles
-constexpr int AB_LSE_OFF = 12 * AB_T16;      // [2] x { lse[128], D[128] } fp32
+constexpr int AB_QD_STAGES = 3;
+constexpr int AB_QD_OFF = 2 * AB_T16;        // [3] stages of { Q, dO }
+constexpr int AB_DS_OFF = 8 * AB_T16;        // [2] buffers of dS^T: [128 keys][128 queries] as two 64-query sub-tiles
+constexpr int AB_DQ_OFF = 12 * AB_T16;       // dQ staging: one [128 queries][32 fp32] sub-tile
+constexpr int AB_LSE_OFF = 13 * AB_T16;      // [2] x { lse[128], D[128] } fp32
 constexpr int AB_BAR_OFF = AB_LSE_OFF + 2 * 256 * 4;
 constexpr int AB_SMEM = AB_BAR_OFF + 256 + 1024;
 constexpr int AB_THREADS = 14 * 32;
-constexpr uint32_t AB_TMEM_COLS = 512;  // S^T 0..127, dP^T 128..255, dV 256..319, dK 320..383, dQ 384..447
+// S^T 0..127, dP^T 128..255, dV 256..319, dK 320..383, dQ 384..447, P^T (bf16 pairs) 448..511
+constexpr uint32_t AB_TMEM_COLS = 512;
 
 struct AbMaps {
     CUtensorMap q, k, v, dout, dq;
@@ -365,11 +387,13 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
     const uint32_t base = (raw + 1023) & ~1023u;
     unsigned char* smem = smem_raw + (base - raw);
     const uint32_t bars = base + AB_BAR_OFF;
-    const uint32_t kv_full = bars, s_full = bars + 8, s_free = bars + 16, ds_full = bars + 24, ds_free = bars + 32,
+    // p_free: block u's dV MMAs have read P^T;  ds_free(d): the dK / dQ MMAs have read dS^T buffer d
+    const uint32_t kv_full = bars, s_full = bars + 8, s_free = bars + 16, ds_full = bars + 24, p_free = bars + 32,
                    dq_full = bars + 40, dq_free = bars + 48, acc_done = bars + 56;
     auto qd_full = [&](int st) { return bars + 64 + 8 * st; };
-    auto qd_empty = [&](int st) { return bars + 80 + 8 * st; };
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + AB_BAR_OFF + 96);
+    auto qd_empty = [&](int st) { return bars + 88 + 8 * st; };
+    auto ds_free = [&](int d) { return bars + 112 + 8 * d; };
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + AB_BAR_OFF + 128);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -385,11 +409,13 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
         mbar_init(s_full, 1);
         mbar_init(s_free, 8);   // one arrive per elementwise warp
         mbar_init(ds_full, 8);
-        mbar_init(ds_free, 1);
+        mbar_init(p_free, 1);
+        mbar_init(ds_free(0), 1);
+        mbar_init(ds_free(1), 1);
         mbar_init(dq_full, 1);
         mbar_init(dq_free, 4);
         mbar_init(acc_done, 1);
-        for (int st = 0; st < 2; ++st) {
+        for (int st = 0; st < AB_QD_STAGES; ++st) {
             mbar_init(qd_full(st), 1);
             mbar_init(qd_empty(st), 1);
         }
@@ -405,7 +431,8 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 320, tdQ = tmem + 384;
+    const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 320, tdQ = tmem + 384,
+                   tP = tmem + 448;
     pdl_wait();
     pdl_trigger();
 
@@ -416,8 +443,8 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
             tma_load_2d(base + AB_K_OFF, &maps.k, h * 64, b * a.Tk + k0, kv_full);
             tma_load_2d(base + AB_V_OFF, &maps.v, h * 64, b * a.Tk + k0, kv_full);
             for (int u = 0; u < nq; ++u) {
-                const int st = u & 1, q0 = (qb_first + u) * AB_BQ;
-                if (!mbar_wait(qd_empty(st), ((u >> 1) & 1) ^ 1, err, 41)) break;
+                const int st = u % AB_QD_STAGES, q0 = (qb_first + u) * AB_BQ;
+                if (!mbar_wait(qd_empty(st), ((u / AB_QD_STAGES) & 1) ^ 1, err, 41)) break;
                 const uint32_t dst = base + AB_QD_OFF + st * 2 * AB_T16;
                 mbar_expect_tx(qd_full(st), 2 * AB_T16);
                 tma_load_2d(dst, &maps.q, h * 64, b * a.T + q0, qd_full(st));
@@ -432,15 +459,13 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
                                   (8u << 24);  // 128x64, MN/MN
         const uint64_t dK_k = smem_desc(base + AB_K_OFF, 16, 1024), dV_k = smem_desc(base + AB_V_OFF, 16, 1024);
         const uint64_t dK_mn = smem_desc(base + AB_K_OFF, 8192, 1024);
-        const uint64_t dP_k = smem_desc(base + AB_P_OFF, 16, 1024), dS_k = smem_desc(base + AB_DS_OFF, 16, 1024);
-        const uint64_t dS_mn = smem_desc(base + AB_DS_OFF, 16384, 1024);
         bool ok = nq > 0 && mbar_wait(kv_full, 0, err, 42);
         // S^T / dP^T of block u (reduction over d).  Block u + 1's are issued as soon as the
         // elementwise warps have read block u's out of TMEM, ahead of block u's dV / dK / dQ, so
         // the tensor core computes them while the P / dS pass of block u still runs.
         auto issue_s = [&](int u) {
-            const uint32_t qs = base + AB_QD_OFF + (u & 1) * 2 * AB_T16;
-            if (!mbar_wait(qd_full(u & 1), (u >> 1) & 1, err, 43)) return false;
+            const uint32_t qs = base + AB_QD_OFF + (u % AB_QD_STAGES) * 2 * AB_T16;
+            if (!mbar_wait(qd_full(u % AB_QD_STAGES), (u / AB_QD_STAGES) & 1, err, 43)) return false;
             if (u > 0 && !mbar_wait(s_free, (u - 1) & 1, err, 44)) return false;
             const uint64_t dQ_k = smem_desc(qs, 16, 1024), dO_k = smem_desc(qs + AB_T16, 16, 1024);
 #pragma unroll
@@ -453,22 +478,29 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
         };
         if (ok) ok = issue_s(0);
         for (int u = 0; ok && u < nq; ++u) {
-            const int st = u & 1;
+            const int st = u % AB_QD_STAGES;
             const uint32_t qs = base + AB_QD_OFF + st * 2 * AB_T16;
             if (u + 1 < nq && !issue_s(u + 1)) { ok = false; break; }
             const uint64_t dQ_mn = smem_desc(qs, 8192, 1024), dO_mn = smem_desc(qs + AB_T16, 8192, 1024);
             if (!mbar_wait(ds_full, u & 1, err, 45)) { ok = false; break; }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");  // P^T stored by the pass
+            const uint32_t dsb = base + AB_DS_OFF + (u & 1) * 2 * AB_T16;  // this block's dS^T buffer
+            const uint64_t dS_k = smem_desc(dsb, 16, 1024), dS_mn = smem_desc(dsb, 16384, 1024);
+            // dV first, so that P^T is released a third of the way through the block's MMAs
 #pragma unroll
-            for (int k16 = 0; k16 < 8; ++k16) {  // dV += P^T dO ; dK += dS^T Q   (reduction over queries)
+            for (int k16 = 0; k16 < 8; ++k16)  // dV += P^T dO   (reduction over queries; P^T in TMEM)
+                mma_f16_ta(tdV, tP + 8 * k16, dO_mn + 128 * k16, ID_KV, (u > 0 || k16 > 0) ? 1u : 0u);
+            mma_commit(p_free);
+#pragma unroll
+            for (int k16 = 0; k16 < 8; ++k16) {  // dK += dS^T Q
                 const uint64_t ka = (uint64_t)((k16 >> 2) * (AB_T16 >> 4) + (k16 & 3) * 2);
-                mma_f16(tdV, dP_k + ka, dO_mn + 128 * k16, ID_KV, (u > 0 || k16 > 0) ? 1u : 0u);
                 mma_f16(tdK, dS_k + ka, dQ_mn + 128 * k16, ID_KV, (u > 0 || k16 > 0) ? 1u : 0u);
             }
             if (u > 0 && !mbar_wait(dq_free, (u - 1) & 1, err, 46)) { ok = false; break; }
 #pragma unroll
             for (int k16 = 0; k16 < 8; ++k16)  // dQ = dS K   (reduction over keys)
                 mma_f16(tdQ, dS_mn + 128 * k16, dK_mn + 128 * k16, ID_Q, k16 > 0 ? 1u : 0u);
-            mma_commit(ds_free);
+            mma_commit(ds_free(u & 1));
             mma_commit(qd_empty(st));
             mma_commit(dq_full);
         }
@@ -483,7 +515,6 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
         const float sl2 = a.scale * AT_LOG2E;
         float* lsd = reinterpret_cast<float*>(smem + AB_LSE_OFF);
-        unsigned char* Pt = smem + AB_P_OFF;
         unsigned char* dSt = smem + AB_DS_OFF;
         bool ok = true;
         // this thread's element of a block's lse (t < 64) or D (t >= 64), loaded one block ahead
@@ -562,23 +593,34 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
                         }
                     }
                 }
-                if (qt == 2 * grp && u > 0) {  // the previous block's MMAs have read P^T / dS^T
-                    if (lane == 0) ok = mbar_wait(ds_free, (u - 1) & 1, err, 48);
+                if (qt == 2 * grp && u > 0) {
+                    // P^T (TMEM): the previous block's dV MMAs have read it; dS^T buffer u & 1:
+                    // block u - 2's dK / dQ MMAs have read it
+                    if (lane == 0) {
+                        ok = mbar_wait(p_free, (u - 1) & 1, err, 48);
+                        if (ok && u > 1) ok = mbar_wait(ds_free(u & 1), ((u >> 1) - 1) & 1, err, 51);
+                    }
                     ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
                     if (!ok) break;
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                }
+                {  // P^T of this key row, query columns qt*32 .. qt*32+31, as bf16 pairs into TMEM
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) pk[j] = pack_bf16(sv[2 * j], sv[2 * j + 1]);
+                    tmem_st16(tP + lb + qt * 16, pk);
                 }
 #pragma unroll
                 for (int un = 0; un < 4; ++un) {
                     const uint32_t off = (qt >> 1) * AB_T16 + at_sw128(kr, (qt & 1) * 4 + un);
-                    *reinterpret_cast<uint4*>(Pt + off) =
-                        make_uint4(pack_bf16(sv[8 * un], sv[8 * un + 1]), pack_bf16(sv[8 * un + 2], sv[8 * un + 3]),
-                                   pack_bf16(sv[8 * un + 4], sv[8 * un + 5]), pack_bf16(sv[8 * un + 6], sv[8 * un + 7]));
-                    *reinterpret_cast<uint4*>(dSt + off) =
+                    *reinterpret_cast<uint4*>(dSt + (u & 1) * 2 * AB_T16 + off) =
                         make_uint4(pack_bf16(dp[8 * un], dp[8 * un + 1]), pack_bf16(dp[8 * un + 2], dp[8 * un + 3]),
                                    pack_bf16(dp[8 * un + 4], dp[8 * un + 5]), pack_bf16(dp[8 * un + 6], dp[8 * un + 7]));
                 }
             }
             if (!ok) continue;
+            tmem_wait_st();
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive(ds_full);
@@ -662,28 +704,28 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
 #pragma unroll
                 for (int e = 0; e < 64; ++e) d[e] = 0.f;
             }
-            // the previous reduce has finished reading the staging tiles
-            if (leader) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-            asm volatile("bar.sync 2, 128;" ::: "memory");
+            // one 32-column half at a time through the single staging tile
 #pragma unroll
-            for (int half = 0; half < 2; ++half)
+            for (int half = 0; half < 2; ++half) {
+                // the previous reduce has finished reading the staging tile
+                if (leader) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                asm volatile("bar.sync 2, 128;" ::: "memory");
 #pragma unroll
                 for (int un = 0; un < 8; ++un) {
                     const float* x = d + half * 32 + 4 * un;
-                    *reinterpret_cast<float4*>(stg + half * AB_T16 + at_sw128(qr, un)) =
+                    *reinterpret_cast<float4*>(stg + at_sw128(qr, un)) =
                         make_float4(x[0] * a.scale, x[1] * a.scale, x[2] * a.scale, x[3] * a.scale);
                 }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            asm volatile("bar.sync 2, 128;" ::: "memory");
-            if (leader) {
-#pragma unroll
-                for (int half = 0; half < 2; ++half)
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                asm volatile("bar.sync 2, 128;" ::: "memory");
+                if (leader) {
                     asm volatile(
                         "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%1, %2}], [%3];"
                         ::"l"(reinterpret_cast<uint64_t>(&maps.dq)), "r"(h * 64 + half * 32), "r"(b * a.T + q0),
-                          "r"(base + AB_DQ_OFF + half * AB_T16)
+                          "r"(base + AB_DQ_OFF)
                         : "memory");
-                asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                }
             }
         }
         if (leader) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
