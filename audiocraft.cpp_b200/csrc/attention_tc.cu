@@ -157,6 +157,11 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_fwd_tc_kernel(const __grid
     auto kv_empty = [&](int s) { return bars + 40 + 8 * AT_STAGES + 8 * s; };
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + AT_BAR_OFF + 40 + 16 * AT_STAGES);
 
+    if (threadIdx.x == 0) {
+        prefetch_tmap(&maps.q);
+        prefetch_tmap(&maps.k);
+        prefetch_tmap(&maps.v);
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int q0 = qb * AT_BQ;
@@ -395,6 +400,13 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
     auto ds_free = [&](int d) { return bars + 112 + 8 * d; };
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + AB_BAR_OFF + 128);
 
+    if (threadIdx.x == 0) {
+        prefetch_tmap(&maps.q);
+        prefetch_tmap(&maps.k);
+        prefetch_tmap(&maps.v);
+        prefetch_tmap(&maps.dout);
+        prefetch_tmap(&maps.dq);
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int k0 = kb * AB_BK;

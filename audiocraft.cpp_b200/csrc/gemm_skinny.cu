@@ -99,6 +99,10 @@ __global__ void __launch_bounds__(SK_THREADS, 2) skinny_kernel(const __grid_cons
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SK_STAGES * SK_STAGE + 8 * (2 * SK_STAGES + 1));
     float* part = reinterpret_cast<float*>(smem);  // STORE, split: [128][SK_PART_LD] partial tile (stages are free by then)
 
+    if (threadIdx.x == 0) {
+        prefetch_tmap(&maps.a);
+        prefetch_tmap(&maps.b);
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int mt = blockIdx.x, split = blockIdx.y;
     const int nk = (p.K + SK_BK - 1) / SK_BK;

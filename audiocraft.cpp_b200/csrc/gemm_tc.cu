@@ -347,6 +347,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(const __grid_const
     const uint32_t drain_bar = bars + 8 * (2 * S + 4);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S * Cfg::STAGE + EPI_SMEM + 8 * (2 * S + 5));
 
+    if (threadIdx.x == 0) {
+        prefetch_tmap(&maps.a1);
+        prefetch_tmap(&maps.b1);
+        prefetch_tmap(&maps.a2);
+        prefetch_tmap(&maps.b2);
+        prefetch_tmap(&maps.out);
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -624,6 +631,13 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
     const uint32_t part_bar = bars + 8 * (2 * S + 5);  // stream-K partial landed in the stages
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S * Cfg::STAGE + Cfg::EPI + 8 * (2 * S + 6));
 
+    if (threadIdx.x == 0) {
+        prefetch_tmap(&maps.a1);
+        prefetch_tmap(&maps.b1);
+        prefetch_tmap(&maps.a2);
+        prefetch_tmap(&maps.b2);
+        prefetch_tmap(&maps.out);
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_rank();
     if (threadIdx.x == 0) {
