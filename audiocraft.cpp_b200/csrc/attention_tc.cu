@@ -740,7 +740,7 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
                 }
             }
         }
-        if (leader) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        if (leader) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // staging read
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();

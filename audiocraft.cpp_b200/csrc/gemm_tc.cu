@@ -492,7 +492,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(const __grid_const
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty_bar(a));
         }
-        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // stores complete
+        // the staging tiles have been read; the stores themselves complete with the grid
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -848,7 +849,7 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
             if (lane == 0) mbar_arrive_remote(a ? leader_tempty1 : leader_tempty0);
             tile = ntile; kb0 = nkb0; kb1 = nkb1; role = nrole; have = nhave;
         }
-        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
