@@ -205,6 +205,15 @@ def test_mg_prefix_and_first_layer():
     _check(loss, ref_loss, case.ctx.get_grads(), ref_g, case.layout)
 
 
+def test_mg_cross_kv_without_adapter():
+    # no adapter on cross.kv: its projection runs as a plain GEMM and has no backward
+    case = MgCase(targets=0x77, layers=3, seed=24)
+    inp = case.inputs()
+    loss = case.ctx.mg_step(*inp)
+    ref_loss, ref_g = case.oracle(case.params, inp)
+    _check(loss, ref_loss, case.ctx.get_grads(), ref_g, case.layout)
+
+
 def test_invalid_inputs_are_rejected():
     case = MfCase(seed=12)
     clean, noise, hidden, t, unc, valid = case.inputs()
