@@ -167,9 +167,12 @@ __device__ __forceinline__ void get_row_b16(const unsigned char* t, int lane, fl
 // Epilogue inputs read per chunk: fp32 residual / accumulator rows (RESID, ACCUM) or bf16 GELU
 // pre-activations (GELU_BWD).  They are fetched one chunk ahead into registers as coalesced
 // 128-byte row segments, so their latency overlaps the previous chunk, then staged in the tile.
-__device__ __forceinline__ int epi_input_kind(int mode) {
-    return (mode == EPI_RESID_F32 || mode == EPI_ACCUM_F32) ? 1
-           : (mode == EPI_GELU_BWD || mode == EPI_GELU_BWD_D) ? 2 : 0;
+// Kind 3: the RoPE (cos, sin) pairs of a bf16-store chunk with rotary columns, loaded per lane
+// (its own row) from the position table, which does not stay in L1 beside the operand stages.
+__device__ __forceinline__ int epi_input_kind(const TcParams& p) {
+    return (p.mode == EPI_RESID_F32 || p.mode == EPI_ACCUM_F32) ? 1
+           : (p.mode == EPI_GELU_BWD || p.mode == EPI_GELU_BWD_D) ? 2
+           : p.rope ? 3 : 0;
 }
 
 // chunk rows m_base .. m_base+rows-1 (rows <= 0: nothing), columns n .. n+31
@@ -193,6 +196,13 @@ __device__ __forceinline__ void fetch_input(const TcParams& p, int kind, int m_b
             if (r < rows)
                 pre[it] = *reinterpret_cast<const float4*>(p.auxin + (long)(m_base + r) * p.ldauxin + n + 8 * u);
         }
+    } else if (kind == 3) {
+        // 16 (cos, sin) pairs of this lane's position for the chunk's columns within its head
+        if (rows > 0 && n < p.rope_cols) {
+            const float4* tt = reinterpret_cast<const float4*>(p.rope + (long)((m_base + lane) % p.rope_T) * 64 + n % 64);
+#pragma unroll
+            for (int it = 0; it < 8; ++it) pre[it] = tt[it];
+        }
     }
 }
 
@@ -205,6 +215,9 @@ __device__ __forceinline__ void stage_input(int kind, const float4* pre, const E
 #pragma unroll
         for (int it = 0; it < 4; ++it)
             *reinterpret_cast<float4*>(t.x + sw64(it * 8 + (lane >> 2), lane & 3)) = pre[it];
+    } else if (kind == 3) {  // the lane's own row of the output tile, read back by the same lane
+#pragma unroll
+        for (int it = 0; it < 8; ++it) *reinterpret_cast<float4*>(t.o + sw128(lane, it)) = pre[it];
     }
 }
 
@@ -213,7 +226,6 @@ __device__ __forceinline__ void stage_input(int kind, const float4* pre, const E
 // tiles `t` free.
 __device__ __forceinline__ void epilogue_warp32(const TcParams& p, const TcMaps& maps, int m_base, int rows, int n,
                                                 float* v, const EpiTiles& t, int lane) {
-    const int m = m_base + lane;
     if (p.alpha != 1.0f)
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] *= p.alpha;
@@ -230,14 +242,17 @@ __device__ __forceinline__ void epilogue_warp32(const TcParams& p, const TcMaps&
         tile_store(&maps.aux, t.x_s, n, m_base, lane);
     }
     if (p.rope && n < p.rope_cols) {  // 32 columns inside one 64-wide head: 16 rotary pairs
-        const float2* tt = reinterpret_cast<const float2*>(p.rope) + (long)(m % p.rope_T) * 32 + (n % 64) / 2;
+        // (cos, sin) pairs staged in this lane's row of the output tile (input kind 3)
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const float2 c = tt[j];
-            const float x0 = v[2 * j], x1 = v[2 * j + 1];
-            v[2 * j] = x0 * c.x - x1 * c.y;
-            v[2 * j + 1] = x0 * c.y + x1 * c.x;
+        for (int u = 0; u < 8; ++u) {
+            const float4 c = *reinterpret_cast<const float4*>(t.o + sw128(lane, u));
+            const float x0 = v[4 * u], x1 = v[4 * u + 1], x2 = v[4 * u + 2], x3 = v[4 * u + 3];
+            v[4 * u] = x0 * c.x - x1 * c.y;
+            v[4 * u + 1] = x0 * c.y + x1 * c.x;
+            v[4 * u + 2] = x2 * c.z - x3 * c.w;
+            v[4 * u + 3] = x2 * c.w + x3 * c.z;
         }
+        __syncwarp();  // every lane has its pairs before the output overwrites the tile
     }
     if (p.mode == EPI_STORE_F32 || p.mode == EPI_ACCUM_F32 || p.mode == EPI_RESID_F32) {
         if (p.mode != EPI_STORE_F32) add_row_f32(t.o, lane, v);  // residual / accumulator already staged in the tile
@@ -304,7 +319,7 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, const TcMaps& m
                                               int rows, int n0, int next_m_base, int next_rows, int next_n0,
                                               const EpiTiles& t, int lane, float4* pre,
                                               const float4* part = nullptr) {
-    const int kind = epi_input_kind(p.mode);
+    const int kind = epi_input_kind(p);
     for (int c = 0; c < NCH; ++c) {
         uint32_t r[32];
         tmem_ld32(trow + c * 32, r);
@@ -473,7 +488,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(const __grid_const
         {
             int mb0, r0, n00;
             tile_rows(blockIdx.x, mb0, r0, n00);
-            fetch_input(p, epi_input_kind(p.mode), mb0, r0, n00, lane, pre);
+            fetch_input(p, epi_input_kind(p), mb0, r0, n00, lane, pre);
         }
         int u = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++u) {
@@ -800,7 +815,7 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
         {
             int mb0, r0, n00;
             tile_rows(first_epi, mb0, r0, n00);
-            fetch_input(p, epi_input_kind(p.mode), mb0, r0, n00, lane, pre);
+            fetch_input(p, epi_input_kind(p), mb0, r0, n00, lane, pre);
         }
         int tile, kb0, kb1, role;
         bool have = w.next(tile, kb0, kb1, role);
