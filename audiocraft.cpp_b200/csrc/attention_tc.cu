@@ -130,6 +130,11 @@ __device__ __forceinline__ float2 fma_f2(float2 a, float2 b, float2 c) {
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
     return bits_f2(d);
 }
+__device__ __forceinline__ float2 add_f2(float2 a, float2 b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return bits_f2(d);
+}
 __device__ __forceinline__ float2 sub_f2(float2 a, float2 b) {
     unsigned long long d;
     asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
@@ -285,15 +290,20 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_fwd_tc_kernel(const __grid
             const float m_use = resc ? m_new : m_run;
             const float m_sub = m_use == -INFINITY ? 0.f : m_use;
             const float alpha = resc ? fast_ex2(m_run - m_sub) : 1.f;  // m_run = -inf: alpha = 0
-            float sm[8];
+            // exponentials and their sum on packed pairs (four independent partial sums)
+            float2 sm[4];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) sm[e] = 0.f;
+            for (int e = 0; e < 4; ++e) sm[e] = make_float2(0.f, 0.f);
+            const float2 sl = make_float2(sl2, sl2), nm = make_float2(-m_sub, -m_sub);
 #pragma unroll
-            for (int c = 0; c < AT_BK; ++c) {
-                s[c] = fast_ex2(fmaf(s[c], sl2, -m_sub));
-                sm[c & 7] += s[c];
+            for (int c = 0; c < AT_BK; c += 2) {
+                const float2 x = fma_f2(make_float2(s[c], s[c + 1]), sl, nm);
+                const float2 pv = make_float2(fast_ex2(x.x), fast_ex2(x.y));
+                s[c] = pv.x;
+                s[c + 1] = pv.y;
+                sm[(c >> 1) & 3] = add_f2(sm[(c >> 1) & 3], pv);
             }
-            const float ls = ((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7]));
+            const float ls = ((sm[0].x + sm[0].y) + (sm[1].x + sm[1].y)) + ((sm[2].x + sm[2].y) + (sm[3].x + sm[3].y));
             l_run = l_run * alpha + ls;
             m_run = m_use;
             // PV_{j-1} has finished: O may be rescaled and the P buffer rewritten
