@@ -18,14 +18,17 @@
 
 #include <algorithm>
 #include <chrono>
+#include <condition_variable>
 #include <cstdlib>
 #include <cmath>
 #include <cstring>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <random>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "kernels.h"
@@ -52,6 +55,83 @@ struct Error : std::runtime_error {
     } while (0)
 
 thread_local std::string g_error;
+
+// Host copies of a step's inputs into the pinned staging buffers, split over a few persistent
+// threads and the calling one: a single thread copying the ~7 MB of a cfg-2 batch took about
+// 1 ms per step, serial with the device work because the step API is synchronous.
+class CopyPool {
+  public:
+    struct Region {
+        void* dst;
+        const void* src;
+        size_t bytes;
+    };
+    explicit CopyPool(int workers) {
+        for (int i = 0; i < workers; ++i) th_.emplace_back([this, i] { run(i + 1); });
+    }
+    ~CopyPool() {
+        {
+            std::lock_guard<std::mutex> g(mu_);
+            stop_ = true;
+        }
+        cv_.notify_all();
+        for (auto& t : th_) t.join();
+    }
+    void copy(const std::vector<Region>& regions) {
+        size_t total = 0;
+        for (const auto& r : regions) total += r.bytes;
+        if (th_.empty() || total < (256u << 10)) {
+            for (const auto& r : regions) std::memcpy(r.dst, r.src, r.bytes);
+            return;
+        }
+        {
+            std::lock_guard<std::mutex> g(mu_);
+            job_ = &regions;
+            total_ = total;
+            remaining_ = (int)th_.size();
+            ++gen_;
+        }
+        cv_.notify_all();
+        share(0);
+        std::unique_lock<std::mutex> g(mu_);
+        done_.wait(g, [this] { return remaining_ == 0; });
+        job_ = nullptr;
+    }
+
+  private:
+    // participant p of P copies bytes [total * p / P, total * (p + 1) / P) of the regions laid end to end
+    void share(int p) {
+        const size_t P = th_.size() + 1, lo = total_ * p / P, hi = total_ * (p + 1) / P;
+        size_t at = 0;
+        for (const auto& r : *job_) {
+            const size_t a = std::max(lo, at), b = std::min(hi, at + r.bytes);
+            if (a < b) std::memcpy(static_cast<char*>(r.dst) + (a - at), static_cast<const char*>(r.src) + (a - at), b - a);
+            at += r.bytes;
+        }
+    }
+    void run(int p) {
+        uint64_t seen = 0;
+        for (;;) {
+            {
+                std::unique_lock<std::mutex> g(mu_);
+                cv_.wait(g, [&] { return stop_ || gen_ != seen; });
+                if (stop_) return;
+                seen = gen_;
+            }
+            share(p);
+            std::lock_guard<std::mutex> g(mu_);
+            if (--remaining_ == 0) done_.notify_one();
+        }
+    }
+    std::vector<std::thread> th_;
+    std::mutex mu_;
+    std::condition_variable cv_, done_;
+    const std::vector<Region>* job_ = nullptr;
+    size_t total_ = 0;
+    int remaining_ = 0;
+    uint64_t gen_ = 0;
+    bool stop_ = false;
+};
 
 }  // namespace
 
@@ -795,6 +875,35 @@ struct act_ctx {
     }
 
     // ---------------------------------------------------------------- staging
+    std::unique_ptr<CopyPool> copies;
+    CopyPool& copy_pool() {
+        if (!copies) {
+            const unsigned hc = std::thread::hardware_concurrency();
+            copies.reset(new CopyPool((int)std::min(7u, hc > 1 ? hc - 1 : 0u)));
+        }
+        return *copies;
+    }
+
+    // Caller arrays -> pinned staging -> device, in pieces of about 1.5 MB: each piece's copy to
+    // the device runs while the host copies the next one (the host copy and the host-to-device
+    // transfer of a cfg-2 batch each take about half a millisecond).
+    struct Upload {
+        void* dev;
+        void* pinned;
+        const void* src;
+        size_t bytes;
+    };
+    void upload(const std::vector<Upload>& ups) {
+        constexpr size_t PIECE = 3u << 19;
+        for (const auto& u : ups)
+            for (size_t off = 0; off < u.bytes; off += PIECE) {
+                const size_t len = std::min(PIECE, u.bytes - off);
+                copy_pool().copy({{static_cast<char*>(u.pinned) + off, static_cast<const char*>(u.src) + off, len}});
+                CK(cudaMemcpyAsync(static_cast<char*>(u.dev) + off, static_cast<char*>(u.pinned) + off, len,
+                                   cudaMemcpyHostToDevice, stream));
+            }
+    }
+
     void stage_mf(const act_mf_batch* b) {
         if (!mf) throw Error(ACT_ERR_INVALID, "not a MelodyFlow context");
         if (!b || b->n <= 0 || b->n > B || !b->clean || !b->noise || !b->hidden || !b->t)
@@ -820,12 +929,8 @@ struct act_ctx {
                 tf[half + k] = std::sin(arg);
             }
         }
-        std::memcpy(h_clean, b->clean, nx * 4);
-        std::memcpy(h_noise, b->noise, nx * 4);
-        std::memcpy(h_hidden, b->hidden, nh * 4);
-        CK(cudaMemcpyAsync(d_clean, h_clean, nx * 4, cudaMemcpyHostToDevice, stream));
-        CK(cudaMemcpyAsync(d_noise, h_noise, nx * 4, cudaMemcpyHostToDevice, stream));
-        CK(cudaMemcpyAsync(d_hidden, h_hidden, nh * 4, cudaMemcpyHostToDevice, stream));
+        upload({{d_clean, h_clean, b->clean, nx * 4}, {d_noise, h_noise, b->noise, nx * 4},
+                {d_hidden, h_hidden, b->hidden, nh * 4}});
         CK(cudaMemcpyAsync(d_t, h_t, n * 4, cudaMemcpyHostToDevice, stream));
         CK(cudaMemcpyAsync(d_tfeat, h_tfeat, (size_t)n * md.time_dim * 4, cudaMemcpyHostToDevice, stream));
         CK(cudaMemcpyAsync(d_nvalid, h_nvalid, n * 4, cudaMemcpyHostToDevice, stream));
@@ -855,10 +960,9 @@ struct act_ctx {
             }
         }
         (void)S;
-        std::memcpy(h_ctx, b->context, (size_t)n * C * D * 4);
         CK(cudaMemcpyAsync(d_ids, h_ids, (size_t)n * nq * T * 4, cudaMemcpyHostToDevice, stream));
         CK(cudaMemcpyAsync(d_tgt, h_tgt, (size_t)n * nq * sel * 4, cudaMemcpyHostToDevice, stream));
-        CK(cudaMemcpyAsync(d_ctx, h_ctx, (size_t)n * C * D * 4, cudaMemcpyHostToDevice, stream));
+        upload({{d_ctx, h_ctx, b->context, (size_t)n * C * D * 4}});
         staged_n = n;
     }
 
