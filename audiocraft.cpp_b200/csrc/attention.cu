@@ -560,7 +560,7 @@ void attn_dvec(const AttnArgs& a, cudaStream_t s) {
 }
 
 void attn_bwd(const AttnArgs& a, cudaStream_t s) {
-    if (!a.dvec_ready) attn_dvec(a, s);
+    attn_dvec(a, s);
     static bool configured = false;
     if (!configured) {
         set_smem(attn_bwd_kernel<true>, BWD_SMEM);

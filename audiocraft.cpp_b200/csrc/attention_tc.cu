@@ -833,7 +833,7 @@ bool attn_bwd_tc_supported(const AttnArgs& a) {
 
 void attn_bwd_tc(const AttnArgs& a, int* err, cudaStream_t s) {
     if (!attn_bwd_tc_supported(a)) throw std::runtime_error("attn_bwd_tc: unsupported arguments");
-    if (!a.dvec_ready) attn_dvec(a, s);
+    attn_dvec(a, s);
     AbMaps maps;
     tc_make_map(&maps.q, a.q, (long)a.clips * a.T, (long)a.H * 64, a.ldq, 64, AB_BQ);
     tc_make_map(&maps.dout, a.dout, (long)a.clips * a.T, (long)a.H * 64, a.lddo, 64, AB_BQ);

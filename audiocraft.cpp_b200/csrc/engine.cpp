@@ -344,14 +344,6 @@ struct act_ctx {
                 timed(2, 0, 0, [&] {
                     residual_to_bf16(static_cast<float*>(g.out), nullptr, g.out_bf, nullptr, g.M, g.N, stream);
                 });
-            if (g.dvec_out)  // nor the D vector
-                timed(1, 0, 0, [&] {
-                    AttnArgs d;
-                    d.T = g.dvec_T; d.H = g.dvec_H; d.clips = g.M / g.dvec_T;
-                    d.o = const_cast<bf16*>(g.dvec_o); d.ldo = g.dvec_ldo;
-                    d.dout = static_cast<const bf16*>(g.out); d.lddo = g.ldo; d.dvec = g.dvec_out;
-                    attn_dvec(d, stream);
-                });
         }
     }
 
@@ -624,9 +616,8 @@ struct act_ctx {
         }
         timed(2, 0, 0, [&] { layernorm_bwd(dtmp, y.xmid2, y.norm[4], y.mu[2], y.rs[2], dx, 1, nullptr, dxbf, y.p[4].dora ? y.p[4].g : nullptr, (int)rows, D, stream); });
         // ---- cross-attention
-        {  // dO of the cross-attention, and its D vector from the same epilogue
+        {
             GemmArgs e; e.mode = EPI_STORE_BF16; e.out = dob; e.ldo = D;
-            e.dvec_o = y.o2; e.dvec_ldo = D; e.dvec_out = dvec; e.dvec_T = T; e.dvec_H = H;
             proj_bwd(y.p[4], dxbf, rows, y.o2, y.U[4], y.Yaux[4], true, e);
         }
         AttnArgs ca;
@@ -634,7 +625,7 @@ struct act_ctx {
         ca.T = T; ca.Tk = C; ca.H = H; ca.clips = n; ca.nvalid = dit ? nvalid_dev : nullptr;
         ca.zero_key = dit ? md.add_zero_attn : 0; ca.scale = 1.0f / std::sqrt((float)md.head_dim);
         ca.o = y.o2; ca.ldo = D; ca.lse = y.lse2;
-        ca.dout = dob; ca.lddo = D; ca.dvec = dvec; ca.dvec_ready = 1; ca.dq_acc = dq_acc; ca.ldq_acc = D;
+        ca.dout = dob; ca.lddo = D; ca.dvec = dvec; ca.dq_acc = dq_acc; ca.ldq_acc = D;
         // dK / dV of the conditioning only feed an adapter on cross.kv (the conditioning itself
         // takes no gradient): without one they are not computed
         const bool need_dkv = y.p[3].adapted;
@@ -665,9 +656,8 @@ struct act_ctx {
         }
         timed(2, 0, 0, [&] { layernorm_bwd(dtmp, y.xmid, y.norm[2], y.mu[1], y.rs[1], dx, 1, nullptr, dxbf, y.p[1].dora ? y.p[1].g : nullptr, (int)rows, D, stream); });
         // ---- self-attention
-        {  // dO of the self-attention, and its D vector
+        {
             GemmArgs e; e.mode = EPI_STORE_BF16; e.out = dob; e.ldo = D;
-            e.dvec_o = y.o1; e.dvec_ldo = D; e.dvec_out = dvec; e.dvec_T = T; e.dvec_H = H;
             proj_bwd(y.p[1], dxbf, rows, y.o1, y.U[1], y.Yaux[1], true, e);
         }
         AttnArgs sa;
@@ -675,7 +665,7 @@ struct act_ctx {
         sa.T = T; sa.Tk = T; sa.H = H; sa.clips = n; sa.causal = dit ? 0 : 1; sa.zero_key = dit ? md.add_zero_attn : 0;
         sa.rope = dit ? rope : nullptr; sa.rope_load = 0; sa.scale = ca.scale;
         sa.o = y.o1; sa.ldo = D; sa.lse = y.lse1;
-        sa.dout = dob; sa.lddo = D; sa.dvec = dvec; sa.dvec_ready = 1; sa.dq_acc = dq_acc; sa.ldq_acc = D;
+        sa.dout = dob; sa.lddo = D; sa.dvec = dvec; sa.dq_acc = dq_acc; sa.ldq_acc = D;
         sa.dk = dqkv + D; sa.dv = dqkv + 2 * D; sa.lddk = sa.lddv = 3 * D;
         sa.kscale = y.p[0].dora ? y.p[0].g + D : nullptr; sa.vscale = y.p[0].dora ? y.p[0].g + 2 * D : nullptr;
         timed(1, 2 * attn_flops(n, T, true), 0, [&] {

@@ -55,10 +55,6 @@ struct TcParams {
     long ldr;
     bf16* aux;
     bf16* out_bf;
-    const bf16* dvec_o;
-    long dvec_ldo;
-    float* dvec_out;
-    int dvec_T, dvec_H;
     long ldaux;
     const bf16* auxin;
     long ldauxin;
@@ -173,12 +169,10 @@ __device__ __forceinline__ void get_row_b16(const unsigned char* t, int lane, fl
 // 128-byte row segments, so their latency overlaps the previous chunk, then staged in the tile.
 // Kind 3: the RoPE (cos, sin) pairs of a bf16-store chunk with rotary columns, loaded per lane
 // (its own row) from the position table, which does not stay in L1 beside the operand stages.
-// Kind 4: the attention output O of the lane's row and the chunk's 32 columns (64 bytes), for
-// the D vector of an attention-output gradient.
 __device__ __forceinline__ int epi_input_kind(const TcParams& p) {
     return (p.mode == EPI_RESID_F32 || p.mode == EPI_ACCUM_F32) ? 1
            : (p.mode == EPI_GELU_BWD || p.mode == EPI_GELU_BWD_D) ? 2
-           : p.rope ? 3 : p.dvec_out ? 4 : 0;
+           : p.rope ? 3 : 0;
 }
 
 // chunk rows m_base .. m_base+rows-1 (rows <= 0: nothing), columns n .. n+31
@@ -209,12 +203,6 @@ __device__ __forceinline__ void fetch_input(const TcParams& p, int kind, int m_b
 #pragma unroll
             for (int it = 0; it < 8; ++it) pre[it] = tt[it];
         }
-    } else if (kind == 4) {
-        if (lane < rows) {
-            const float4* oo = reinterpret_cast<const float4*>(p.dvec_o + (long)(m_base + lane) * p.dvec_ldo + n);
-#pragma unroll
-            for (int it = 0; it < 4; ++it) pre[it] = oo[it];
-        }
     }
 }
 
@@ -230,9 +218,6 @@ __device__ __forceinline__ void stage_input(int kind, const float4* pre, const E
     } else if (kind == 3) {  // the lane's own row of the output tile, read back by the same lane
 #pragma unroll
         for (int it = 0; it < 8; ++it) *reinterpret_cast<float4*>(t.o + sw128(lane, it)) = pre[it];
-    } else if (kind == 4) {  // the lane's own row of the side tile, read back by the same lane
-#pragma unroll
-        for (int it = 0; it < 4; ++it) *reinterpret_cast<float4*>(t.x + sw64(lane, it)) = pre[it];
     }
 }
 
@@ -335,7 +320,6 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, const TcMaps& m
                                               const EpiTiles& t, int lane, float4* pre,
                                               const float4* part = nullptr) {
     const int kind = epi_input_kind(p);
-    float dacc = 0.f;  // kind 4: this row's sum over the current head
     for (int c = 0; c < NCH; ++c) {
         uint32_t r[32];
         tmem_ld32(trow + c * 32, r);
@@ -357,29 +341,7 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, const TcMaps& m
             else fetch_input(p, kind, next_m_base, next_rows, next_n0, lane, pre);
             __syncwarp();
         }
-        if (rows > 0) {
-            epilogue_warp32(p, maps, m_base, rows, n, reinterpret_cast<float*>(r), t, lane);
-            if (kind == 4) {  // D: the stored (bf16-rounded) gradient times O, one head per two chunks
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const uint4 q = *reinterpret_cast<const uint4*>(t.x + sw64(lane, u));
-                    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float g0 = __bfloat162float(__float2bfloat16(__uint_as_float(r[8 * u + 2 * j])));
-                        const float g1 = __bfloat162float(__float2bfloat16(__uint_as_float(r[8 * u + 2 * j + 1])));
-                        dacc = fmaf(g0, __uint_as_float(w[j] << 16), dacc);
-                        dacc = fmaf(g1, __uint_as_float(w[j] & 0xffff0000u), dacc);
-                    }
-                }
-                if ((n & 63) == 32) {
-                    const int m = m_base + lane;
-                    if (lane < rows)
-                        p.dvec_out[((long)(m / p.dvec_T) * p.dvec_H + n / 64) * p.dvec_T + m % p.dvec_T] = dacc;
-                    dacc = 0.f;
-                }
-            }
-        }
+        if (rows > 0) epilogue_warp32(p, maps, m_base, rows, n, reinterpret_cast<float*>(r), t, lane);
     }
 }
 
@@ -1001,7 +963,6 @@ void launch_tc(const GemmArgs& a, int* err, cudaStream_t s) {
     p.colscale2 = a.colscale2; p.bias = a.bias; p.nvalid = a.nvalid; p.mvalid = a.mvalid; p.err = err;
     p.rope = a.rope; p.rope_T = a.rope_T; p.rope_cols = a.rope_cols;
     p.out_bf = (a.mode == EPI_STORE_F32 || a.mode == EPI_ACCUM_F32 || a.mode == EPI_RESID_F32) ? a.out_bf : nullptr;
-    p.dvec_o = a.dvec_o; p.dvec_ldo = a.dvec_ldo; p.dvec_out = a.dvec_out; p.dvec_T = a.dvec_T; p.dvec_H = a.dvec_H;
     auto kern = gemm_tc_kernel<BN, B_MN>;
     static bool configured = false;
     if (!configured) {
@@ -1065,7 +1026,6 @@ void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
     p.colscale2 = a.colscale2; p.bias = a.bias; p.nvalid = a.nvalid; p.mvalid = a.mvalid; p.err = err;
     p.rope = a.rope; p.rope_T = a.rope_T; p.rope_cols = a.rope_cols;
     p.out_bf = (a.mode == EPI_STORE_F32 || a.mode == EPI_ACCUM_F32 || a.mode == EPI_RESID_F32) ? a.out_bf : nullptr;
-    p.dvec_o = a.dvec_o; p.dvec_ldo = a.dvec_ldo; p.dvec_out = a.dvec_out; p.dvec_T = a.dvec_T; p.dvec_H = a.dvec_H;
     p.sk_part = a.sk_part; p.sk_flag = a.sk_flag;
     auto whole = gemm_tc2_kernel<BN2, B_MN, false>;
     auto split = gemm_tc2_kernel<BN2, B_MN, BN2 == 256>;
@@ -1111,9 +1071,6 @@ bool gemm_tc_supported(const GemmArgs& a) {
     if ((a.mode == EPI_GELU_BWD || a.mode == EPI_GELU_BWD_D) && a.aux)
         return false;  // its pre-activation input occupies the side tile
     if (a.ldo % 8 || (a.aux && a.ldaux % 8) || (a.auxin && a.ldauxin % 8) || (a.resid && a.ldr % 4)) return false;
-    if (a.dvec_out && (a.mode != EPI_STORE_BF16 || a.aux || a.rope || a.dvec_ldo % 8 || a.dvec_T <= 0 ||
-                       (reinterpret_cast<uintptr_t>(a.dvec_o) & 15)))
-        return false;  // the D vector rides on a plain bf16 store whose side tile is free
     const uintptr_t al = reinterpret_cast<uintptr_t>(a.out) | reinterpret_cast<uintptr_t>(a.aux) |
                          reinterpret_cast<uintptr_t>(a.auxin) | reinterpret_cast<uintptr_t>(a.resid) |
                          reinterpret_cast<uintptr_t>(a.colscale) | reinterpret_cast<uintptr_t>(a.A1) |

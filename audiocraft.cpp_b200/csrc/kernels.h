@@ -68,13 +68,6 @@ struct GemmArgs {
     int* sk_flag = nullptr;
     // fp32 output modes (STORE / ACCUM / RESID): also store bf16(out), row stride ldo
     bf16* out_bf = nullptr;
-    // EPI_STORE_BF16 producing an attention-output gradient dO (columns = heads of 64): also the
-    // attention backward's D vector, dvec_out[(b * dvec_H + h) * dvec_T + i] = sum over the head's
-    // columns of bf16(dO) * O for row b * dvec_T + i (O = dvec_o, row stride dvec_ldo)
-    const bf16* dvec_o = nullptr;
-    long dvec_ldo = 0;
-    float* dvec_out = nullptr;
-    int dvec_T = 0, dvec_H = 0;
 };
 long gemm_sk_part_floats(int num_sms);
 int gemm_sk_flag_count(int num_sms);
@@ -135,7 +128,6 @@ struct AttnArgs {
     const bf16* dout = nullptr;
     long lddo = 0;
     float* dvec = nullptr;        // [clips][H][T]  rowsum(dO * O)
-    int dvec_ready = 0;           // dvec already holds it (computed with dO): not recomputed
     float* dq_acc = nullptr;      // [clips*T][ldq_acc] fp32, rotated frame, zeroed by caller
     long ldq_acc = 0;
     bf16* dk = nullptr;
