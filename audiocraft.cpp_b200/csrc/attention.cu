@@ -298,7 +298,9 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
 
     const int qb0 = a.causal ? k0 / BWD_BQ : 0;
     const int nqb = (a.T + BWD_BQ - 1) / BWD_BQ;
-    const int qb_all = nk > 0 ? qb0 : nqb;
+    // without keys in range the CTA has nothing to add, except when it writes dQ directly: then
+    // its query blocks still run (every score masked, dQ exactly zero) so that their rows are written
+    const int qb_all = (nk > 0 || a.dq_bf) ? qb0 : nqb;
     // this CTA's share of the key block's query blocks
     const int qb_first = qb_all + (int)((long)(nqb - qb_all) * part / a.qsplit);
     const int qb_end = qb_all + (int)((long)(nqb - qb_all) * (part + 1) / a.qsplit);
@@ -434,7 +436,19 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
                 if (i >= a.T) continue;
                 float* dst = a.dq_acc + ((long)b * a.T + i) * a.ldq_acc + h * HD;
                 // with a single key block this CTA is the only contributor to these rows
-                if (a.Tk <= BKV) {
+                if (a.dq_bf) {
+                    bf16* db = a.dq_bf + ((long)b * a.T + i) * a.lddq_bf + h * HD;
+#pragma unroll
+                    for (int ni = 0; ni < 8; ++ni) {
+                        const int c = ni * 8 + 2 * q;
+                        float x0 = dq[ni][2 * hh] * a.scale, x1 = dq[ni][2 * hh + 1] * a.scale;
+                        if (a.dq_scale) {
+                            x0 *= a.dq_scale[h * HD + c];
+                            x1 *= a.dq_scale[h * HD + c + 1];
+                        }
+                        *reinterpret_cast<uint32_t*>(db + c) = pack_bf16(x0, x1);
+                    }
+                } else if (a.Tk <= BKV) {
 #pragma unroll
                     for (int ni = 0; ni < 8; ++ni)
                         *reinterpret_cast<float2*>(dst + ni * 8 + 2 * q) =
@@ -569,6 +583,8 @@ void attn_bwd(const AttnArgs& a, cudaStream_t s) {
     }
     if (a.qsplit < 1 || (a.qsplit > 1 && a.dk && (!a.dk_acc || !a.dv_acc)))
         throw std::runtime_error("attn_bwd: query split with dK / dV needs dk_acc / dv_acc");
+    if (a.dq_bf && (a.Tk > BKV || a.rope || a.lddq_bf % 2 || (reinterpret_cast<uintptr_t>(a.dq_bf) & 3)))
+        throw std::runtime_error("attn_bwd: direct bf16 dQ needs a single key block and no RoPE");
     dim3 grid((unsigned)(((a.Tk + BKV - 1) / BKV) * a.qsplit), a.H, a.clips);
     if (a.rope && a.rope_load) launch_pdl(attn_bwd_kernel<true>, grid, dim3(128), BWD_SMEM, s, a);
     else launch_pdl(attn_bwd_kernel<false>, grid, dim3(128), BWD_SMEM, s, a);

@@ -642,12 +642,20 @@ struct act_ctx {
                 ca.dv_acc = dkv_acc + crows * D;
             }
         }
+        // a single key block: each query row's dQ is final in one CTA and goes straight to dcq as
+        // bf16 (no fp32 accumulator to clear or convert)
+        const bool dq_direct = C <= 64;
+        if (dq_direct) {
+            ca.dq_bf = dcq;
+            ca.lddq_bf = D;
+            ca.dq_scale = y.p[2].dora ? y.p[2].g : nullptr;
+        }
         timed(1, 2 * attn_flops(n, C, false), 0, [&] {
-            CK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * D, stream));
+            if (!dq_direct) CK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * D, stream));
             if (split && need_dkv) CK(cudaMemsetAsync(dkv_acc, 0, sizeof(float) * crows * 2 * D, stream));
             attn_bwd(ca, stream);
             if (split && need_dkv) attn_dkv_finish(ca, stream);
-            attn_dq_finish(ca, dcq, D, y.p[2].dora ? y.p[2].g : nullptr, stream);
+            if (!dq_direct) attn_dq_finish(ca, dcq, D, y.p[2].dora ? y.p[2].g : nullptr, stream);
         });
         if (need_dkv) proj_bwd(y.p[3], dckv, crows, ctx_bf, y.U[3], y.ckv, false, GemmArgs());
         {

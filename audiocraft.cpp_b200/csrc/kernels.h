@@ -130,6 +130,12 @@ struct AttnArgs {
     float* dvec = nullptr;        // [clips][H][T]  rowsum(dO * O)
     float* dq_acc = nullptr;      // [clips*T][ldq_acc] fp32, rotated frame, zeroed by caller
     long ldq_acc = 0;
+    // mma.sync backward with a single key block (Tk <= 64, no RoPE): dQ is final inside one CTA,
+    // so it is written straight as bf16 (times the optional column factor dq_scale) to dq_bf;
+    // dq_acc is then not used and needs no zeroing
+    bf16* dq_bf = nullptr;
+    long lddq_bf = 0;
+    const float* dq_scale = nullptr;
     bf16* dk = nullptr;
     bf16* dv = nullptr;
     long lddk = 0, lddv = 0;
