@@ -136,6 +136,7 @@ __global__ void __launch_bounds__(FWD_WARPS * 32) attn_fwd_kernel(const AttnArgs
         const bf16* cK = sK + buf * BKV * LDS;
         const bf16* cV = sV + buf * BKV * LDS;
         const int k0 = kb * BKV;
+        const int nvk = kv_end - k0;  // keys of this block in range (>= 1): groups of 16 past them are skipped
         float s[8][4];
 #pragma unroll
         for (int i = 0; i < 8; ++i)
@@ -145,6 +146,7 @@ __global__ void __launch_bounds__(FWD_WARPS * 32) attn_fwd_kernel(const AttnArgs
         for (int kc = 0; kc < 4; ++kc)
 #pragma unroll
             for (int nj = 0; nj < 4; ++nj) {
+                if (nj * 16 >= nvk) continue;  // masked below
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4(b0, b1, b2, b3, cK + (nj * 16 + lr + 8 * (lsel >> 1)) * LDS + kc * 16 + 8 * (lsel & 1));
                 mma_bf16(s[2 * nj], qf[kc], b0, b1);
@@ -198,6 +200,7 @@ __global__ void __launch_bounds__(FWD_WARPS * 32) attn_fwd_kernel(const AttnArgs
         }
 #pragma unroll
         for (int kc = 0; kc < 4; ++kc) {
+            if (kc * 16 >= nvk) continue;  // these probabilities are zero
             uint32_t pa[4];
             pa[0] = pack_bf16(s[2 * kc][0], s[2 * kc][1]);
             pa[1] = pack_bf16(s[2 * kc][2], s[2 * kc][3]);
@@ -323,6 +326,13 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
     };
     if (qb_first < qb_end) load_q(qb_first, 0);
     cp_async_commit();
+    // a warp owns keys k0 + 16 warp .. +15; with none of them in range (few keys, e.g. the 32
+    // conditioning tokens in a 64-key block) its scores, dV / dK and dS^T rows are all zero: it
+    // skips that work and its dS^T rows are cleared once for the dQ product
+    const bool live = warp * 16 < nk;
+    if (!live)
+        for (int c = lane; c < 16 * (HD / 8); c += 32)
+            *reinterpret_cast<uint4*>(sdS + (warp * 16 + c / (HD / 8)) * LDS + (c % (HD / 8)) * 8) = make_uint4(0, 0, 0, 0);
 
     const float sl2 = a.scale * LOG2E;
     float dk[8][4], dv[8][4];
@@ -348,6 +358,7 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
         for (int i = 0; i < 8; ++i)
 #pragma unroll
             for (int e = 0; e < 4; ++e) s[i][e] = dp[i][e] = 0.f;
+        if (live) {
 #pragma unroll
         for (int kc = 0; kc < 4; ++kc) {
             uint32_t ka[4], va[4];
@@ -380,9 +391,11 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
                 s[ni][e] = p;
                 dp[ni][e] = p * (dp[ni][e] - cD[il]);
             }
+        }  // live
         // dV += P^T dO ; dK += dS^T Q  (A operands straight from the accumulators)
 #pragma unroll
         for (int kc = 0; kc < 4; ++kc) {
+            if (!live) break;
             uint32_t pa[4], sa[4];
             pa[0] = pack_bf16(s[2 * kc][0], s[2 * kc][1]);
             pa[1] = pack_bf16(s[2 * kc][2], s[2 * kc][3]);
