@@ -12,12 +12,12 @@
 //               masked)
 //   warp 1      MMA issuer (one thread): S = Q K^T (128 x 64, fp32, two TMEM buffers so the
 //               next block's scores are computed while this block's softmax runs), then
-//               O += P V (128 x 64, fp32 in TMEM) with P (bf16) from shared memory
+//               O += P V (128 x 64, fp32 in TMEM) with P (bf16 pairs) read from TMEM
 //   warps 2..5  softmax, one query row per thread: tcgen05.ld the row of S, online softmax in
 //               base 2 with a lazily updated running max (the max used for the exponentials is
 //               only raised when the block maximum exceeds it by more than 2^8, which bounds
 //               every probability by 256 and keeps O's rescaling off the common path), P to
-//               shared memory, O rescaled in TMEM when the max moved; finally O / l and the LSE.
+//               TMEM, O rescaled in TMEM when the max moved; finally O / l and the LSE.
 //
 // Backward (attn_bwd_tc): one CTA per 128 keys of one (clip, head), looping over blocks of 128
 // queries, with the scores recomputed in the transposed (key-major) frame:
@@ -57,11 +57,10 @@ constexpr int AT_STAGES = 4;
 constexpr int AT_Q_OFF = 0;
 constexpr int AT_K_OFF = AT_QTILE;                           // [AT_STAGES] stages of K
 constexpr int AT_V_OFF = AT_K_OFF + AT_STAGES * AT_KTILE;    // [AT_STAGES] stages of V
-constexpr int AT_P_OFF = AT_V_OFF + AT_STAGES * AT_KTILE;    // P: 128 queries x 64 keys
-constexpr int AT_BAR_OFF = AT_P_OFF + AT_QTILE;
+constexpr int AT_BAR_OFF = AT_V_OFF + AT_STAGES * AT_KTILE;
 constexpr int AT_SMEM = AT_BAR_OFF + 256 + 1024;
 constexpr int AT_THREADS = 6 * 32;
-constexpr uint32_t AT_TMEM_COLS = 256;       // S: columns 0..63 and 64..127, O: 128..191
+constexpr uint32_t AT_TMEM_COLS = 256;       // S: columns 0..63 and 64..127, O: 128..191, P (bf16 pairs): 192..223
 constexpr float AT_LOG2E = 1.4426950408889634f;
 constexpr float AT_RESCALE = 8.0f;           // lazy-max threshold (log2 units)
 
@@ -197,7 +196,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_fwd_tc_kernel(const __grid
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tS = tmem, tO = tmem + 2 * AT_BK;  // S buffer t at tS + t * AT_BK
+    const uint32_t tS = tmem, tO = tmem + 2 * AT_BK, tP = tmem + 3 * AT_BK;  // S buffer t at tS + t * AT_BK
     pdl_wait();
     pdl_trigger();
 
@@ -223,7 +222,6 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_fwd_tc_kernel(const __grid
         const uint64_t dq = smem_desc(base + AT_Q_OFF, 16, 1024);
         const uint64_t dk0 = smem_desc(base + AT_K_OFF, 16, 1024);
         const uint64_t dv0 = smem_desc(base + AT_V_OFF, 8192, 1024);
-        const uint64_t dp = smem_desc(base + AT_P_OFF, 16, 1024);
         bool ok = nkb > 0 && mbar_wait(q_full, 0, err, 32);
         auto issue_s = [&](int j) {  // S[j & 1] = Q K_j^T
             const int st = j % AT_STAGES;
@@ -242,10 +240,11 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_fwd_tc_kernel(const __grid
             // released by the softmax of block j - 1)
             if (j + 1 < nkb && !issue_s(j + 1)) { ok = false; break; }
             if (!mbar_wait(p_full, j & 1, err, 34)) { ok = false; break; }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");  // P stored by the softmax
             const uint64_t dv = dv0 + (uint64_t)(((j % AT_STAGES) * AT_KTILE) >> 4);
 #pragma unroll
-            for (int k16 = 0; k16 < AT_BK / 16; ++k16)  // P: K-major, +32 B; V: MN-major, +16 rows
-                mma_f16(tO, dp + (uint64_t)(k16 * 2), dv + (uint64_t)(k16 * 128), IDESC_PV, (j > 0 || k16 > 0) ? 1u : 0u);
+            for (int k16 = 0; k16 < AT_BK / 16; ++k16)  // P: TMEM, 8 columns per 16 keys; V: MN-major, +16 rows
+                mma_f16_ta(tO, tP + 8 * k16, dv + (uint64_t)(k16 * 128), IDESC_PV, (j > 0 || k16 > 0) ? 1u : 0u);
             mma_commit(o_done);
             mma_commit(kv_empty(j % AT_STAGES));
         }
@@ -259,7 +258,6 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_fwd_tc_kernel(const __grid
         float m_run = a.zero_key ? 0.f : -INFINITY;
         float l_run = a.zero_key ? 1.f : 0.f;
         bool ok = true;
-        unsigned char* P = smem + AT_P_OFF;
         for (int j = 0; j < nkb; ++j) {
             if (lane == 0) ok = mbar_wait(s_full(j & 1), (j >> 1) & 1, err, 36);
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -325,12 +323,13 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_fwd_tc_kernel(const __grid
                     tmem_wait_st();
                 }
             }
+            {  // P of this query row as bf16 pairs into TMEM, the A operand of O += P V
+                uint32_t pk[AT_BK / 2];
 #pragma unroll
-            for (int u = 0; u < AT_BK / 8; ++u)
-                *reinterpret_cast<uint4*>(P + at_sw128(r, u)) =
-                    make_uint4(pack_bf16(s[8 * u], s[8 * u + 1]), pack_bf16(s[8 * u + 2], s[8 * u + 3]),
-                               pack_bf16(s[8 * u + 4], s[8 * u + 5]), pack_bf16(s[8 * u + 6], s[8 * u + 7]));
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                for (int c2 = 0; c2 < AT_BK / 2; ++c2) pk[c2] = pack_bf16(s[2 * c2], s[2 * c2 + 1]);
+                tmem_st32(tP + lane_base, reinterpret_cast<const float*>(pk));
+                tmem_wait_st();
+            }
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full);
