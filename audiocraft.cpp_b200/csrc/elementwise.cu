@@ -81,7 +81,9 @@ __global__ void ln_bwd_kernel(const float* __restrict__ dy, const float* __restr
     constexpr int MAXV = NV;
     const int nv = NV;
     const float mu = mean[row], rs = rstd[row];
-    float4 gv[MAXV], xh[MAXV];
+    // every load of the row is issued before the reductions: dy, x, and the terms added to the
+    // result (the accumulated dx and the extra gradient), so that their latencies overlap
+    float4 gv[MAXV], xh[MAXV], ad[MAXV];
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int i = 0; i < MAXV; ++i)
@@ -90,6 +92,12 @@ __global__ void ln_bwd_kernel(const float* __restrict__ dy, const float* __restr
             const float4 d = *reinterpret_cast<const float4*>(dy + (long)row * D + j);
             const float4 xx = *reinterpret_cast<const float4*>(x + (long)row * D + j);
             const float4 ww = *reinterpret_cast<const float4*>(w + j);
+            ad[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (accumulate) ad[i] = *reinterpret_cast<const float4*>(dx + (long)row * D + j);
+            if (extra) {
+                const float4 e = *reinterpret_cast<const float4*>(extra + (long)row * D + j);
+                ad[i].x += e.x; ad[i].y += e.y; ad[i].z += e.z; ad[i].w += e.w;
+            }
             gv[i] = make_float4(d.x * ww.x, d.y * ww.y, d.z * ww.z, d.w * ww.w);
             xh[i] = make_float4((xx.x - mu) * rs, (xx.y - mu) * rs, (xx.z - mu) * rs, (xx.w - mu) * rs);
             s1 += gv[i].x + gv[i].y + gv[i].z + gv[i].w;
@@ -104,14 +112,7 @@ __global__ void ln_bwd_kernel(const float* __restrict__ dy, const float* __restr
             float4* dp = reinterpret_cast<float4*>(dx + (long)row * D + j);
             float4 r = make_float4(rs * (gv[i].x - s1 - xh[i].x * s2), rs * (gv[i].y - s1 - xh[i].y * s2),
                                    rs * (gv[i].z - s1 - xh[i].z * s2), rs * (gv[i].w - s1 - xh[i].w * s2));
-            if (accumulate) {
-                const float4 o = *dp;
-                r.x += o.x; r.y += o.y; r.z += o.z; r.w += o.w;
-            }
-            if (extra) {
-                const float4 e = *reinterpret_cast<const float4*>(extra + (long)row * D + j);
-                r.x += e.x; r.y += e.y; r.z += e.z; r.w += e.w;
-            }
+            r.x += ad[i].x; r.y += ad[i].y; r.z += ad[i].z; r.w += ad[i].w;
             *dp = r;
             if (dx_bf) {
                 float4 c = make_float4(1.f, 1.f, 1.f, 1.f);
