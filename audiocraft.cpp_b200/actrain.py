@@ -21,6 +21,9 @@ FAMILY_MELODYFLOW, FAMILY_MUSICGEN = 0, 1
 ADAPTER_LORA, ADAPTER_DORA_ROWS = 0, 1
 TYPE_F32, TYPE_F16, TYPE_Q8_0 = 0, 1, 8
 TARGETS = ("self.qkv", "self.out", "cross.q", "cross.kv", "cross.out", "ff.0", "ff.2")
+# kernel families counted by act_path_counts (ACT_PATH_*)
+PATHS = ("attn_fwd_tc", "attn_fwd_mma", "attn_bwd_tc", "attn_bwd_mma", "gemm_tc", "gemm_mma", "rank_tc",
+         "rank_mma")
 
 
 class ModelDesc(C.Structure):
@@ -101,6 +104,10 @@ SIGNATURES = {
     "act_gemm_bf16": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                 C.c_int, C.c_int, C.POINTER(C.c_float)]),
     "act_gelu_bf16": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int]),
+    "act_path_counts": (C.c_int, [C.c_void_p, C.POINTER(C.c_int64), C.c_int]),
+    "act_wait_probe": (C.c_int, [C.c_void_p, C.c_int64]),
+    "act_mg_staged": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t]),
+    "act_q8_0_dequant": (C.c_int, [C.c_int, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]),
     "act_rank_gemm_bf16": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                      C.c_int, C.c_int, C.c_float, C.c_int, C.c_int, C.POINTER(C.c_float)]),
 }
@@ -282,6 +289,23 @@ class Context:
     def graph_kernel_nodes(self, n: int) -> int:
         return int(self._L.act_graph_kernel_nodes(self.h, n))
 
+    def path_counts(self) -> dict:
+        """Launches issued so far per kernel family (act_path_counts)."""
+        buf = (C.c_int64 * len(PATHS))()
+        self._check(self._L.act_path_counts(self.h, buf, len(PATHS)))
+        return dict(zip(PATHS, list(buf)))
+
+    def wait_probe(self, limit_ns: int):
+        """act_wait_probe: a bounded device wait on a flag nothing sets; raises ActError."""
+        self._check(self._L.act_wait_probe(self.h, int(limit_ns)))
+
+    def mg_staged(self, n: int, n_q: int, steps: int, selected: int):
+        """Staged delayed ids [n][n_q][steps] and targets [n][n_q][selected] (act_mg_staged)."""
+        ids = np.zeros((n, n_q, steps), np.int32)
+        tgt = np.zeros((n, n_q, selected), np.int32)
+        self._check(self._L.act_mg_staged(self.h, ids.ctypes.data, ids.size, tgt.ctypes.data, tgt.size))
+        return ids, tgt
+
 
 def gemm_bf16(A_bits: np.ndarray, B_bits: np.ndarray, M: int, N: int, K: int, b_mn_major: bool, path: int = 0,
               device: int = 0, reps: int = 0):
@@ -307,6 +331,18 @@ def gelu_bf16(z_bits: np.ndarray, direct: bool, device: int = 0):
     if rc != ACT_OK:
         raise ActError(rc, lib().act_last_error(None).decode())
     return g, dg
+
+
+def q8_0_dequant(blocks: np.ndarray, device: int = 0):
+    """act_q8_0_dequant: (fp32 d*q, its bf16 bit patterns) of Q8_0 blocks ([nblocks][34] bytes)."""
+    b = np.ascontiguousarray(blocks, np.uint8).reshape(-1)
+    nb = b.size // 34
+    f = np.zeros(nb * 32, np.float32)
+    h = np.zeros(nb * 32, np.uint16)
+    rc = lib().act_q8_0_dequant(device, b.ctypes.data, nb, f.ctypes.data, h.ctypes.data)
+    if rc != ACT_OK:
+        raise ActError(rc, lib().act_last_error(None).decode())
+    return f, h
 
 
 RANK_ACC, RANK_ACC_T, RANK_STORE = 0, 1, 2

@@ -570,12 +570,11 @@ void set_smem(K kern, int bytes) {
 }  // namespace
 
 void attn_fwd(const AttnArgs& a, cudaStream_t s) {
-    static bool configured = false;
-    if (!configured) {
+    static DeviceOnce once;
+    once([] {
         set_smem(attn_fwd_kernel<true>, FWD_SMEM);
         set_smem(attn_fwd_kernel<false>, FWD_SMEM);
-        configured = true;
-    }
+    });
     dim3 grid((a.T + FWD_BQ - 1) / FWD_BQ, a.H, a.clips);
     if (a.rope && a.rope_load) launch_pdl(attn_fwd_kernel<true>, grid, dim3(FWD_WARPS * 32), FWD_SMEM, s, a);
     else launch_pdl(attn_fwd_kernel<false>, grid, dim3(FWD_WARPS * 32), FWD_SMEM, s, a);
@@ -588,12 +587,11 @@ void attn_dvec(const AttnArgs& a, cudaStream_t s) {
 
 void attn_bwd(const AttnArgs& a, cudaStream_t s) {
     attn_dvec(a, s);
-    static bool configured = false;
-    if (!configured) {
+    static DeviceOnce once;
+    once([] {
         set_smem(attn_bwd_kernel<true>, BWD_SMEM);
         set_smem(attn_bwd_kernel<false>, BWD_SMEM);
-        configured = true;
-    }
+    });
     if (a.qsplit < 1 || (a.qsplit > 1 && a.dk && (!a.dk_acc || !a.dv_acc)))
         throw std::runtime_error("attn_bwd: query split with dK / dV needs dk_acc / dv_acc");
     if (a.dq_bf && (a.Tk > BKV || a.rope || a.lddq_bf % 2 || (reinterpret_cast<uintptr_t>(a.dq_bf) & 3)))

@@ -31,18 +31,28 @@ int fail(int code, const std::string& msg) {
     return code;
 }
 
-}  // namespace
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
-extern "C" int act_attention_bwd_noalloc(const void* q, const void* k, const void* v, const void* o,
-                                         const float* lse, const void* dout, void* dq, void* dk, void* dv,
-                                         int clips, int T, int Tk, int H, const int32_t* nvalid, int causal,
-                                         int zero_key, const float* rope, void* stream) {
+int attention_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const float* lse,
+                          const void* dout, void* dq, void* dk, void* dv, int clips, int T, int Tk, int H,
+                          const int32_t* nvalid, int causal, int zero_key, const float* rope, void* stream) {
     if (!q || !k || !v || !o || !lse || !dout || !dq || !dk || !dv)
         return fail(ACT_ERR_INVALID, "act_attention_bwd_noalloc: null pointer");
     if (clips <= 0 || T <= 0 || Tk <= 0 || H <= 0)
         return fail(ACT_ERR_INVALID, "act_attention_bwd_noalloc: sizes must be positive");
     if (causal && Tk != T) return fail(ACT_ERR_INVALID, "act_attention_bwd_noalloc: causal attention needs Tk == T");
     if (rope && Tk > T) return fail(ACT_ERR_INVALID, "act_attention_bwd_noalloc: RoPE needs Tk <= T");
+    // The kernels move the bf16 tensors in 16-byte vectors, the RoPE table in (cos, sin) float
+    // pairs and lse / nvalid as 4-byte words: a misaligned pointer would fault on the device, so
+    // it is rejected here, before anything is queued.
+    for (const void* p : {q, k, v, o, dout, static_cast<const void*>(dq), static_cast<const void*>(dk),
+                          static_cast<const void*>(dv)})
+        if (!aligned(p, 16))
+            return fail(ACT_ERR_INVALID, "act_attention_bwd_noalloc: q, k, v, o, dout, dq, dk and dv must be "
+                                         "16-byte aligned");
+    if (!aligned(lse, 4) || (nvalid && !aligned(nvalid, 4)) || (rope && !aligned(rope, 8)))
+        return fail(ACT_ERR_INVALID, "act_attention_bwd_noalloc: lse and nvalid must be 4-byte aligned, rope "
+                                     "8-byte aligned");
     const long D = (long)H * 64;
     const long acc_floats = (long)clips * T * D;          // dQ accumulator
     const long dvec_floats = (long)clips * H * T;         // rowsum(dO * O)
@@ -60,6 +70,8 @@ extern "C" int act_attention_bwd_noalloc(const void* q, const void* k, const voi
     {
         // One-time set-up per device, with that device current: the address of this device's copy
         // of the array.  The host-side symbol is only a stand-in and must never reach a kernel.
+        // The address is kept for the life of the process, so the device must not be reset
+        // (cudaDeviceReset, or a reset of its primary context) after the first call.
         std::lock_guard<std::mutex> lock(g_scratch_mu);
         if (!g_scratch_ptr[dev]) {
             void* p = nullptr;
@@ -101,4 +113,25 @@ extern "C" int act_attention_bwd_noalloc(const void* q, const void* k, const voi
     e = cudaGetLastError();
     if (e != cudaSuccess) return fail(ACT_ERR_CUDA, std::string("attention backward launch: ") + cudaGetErrorString(e));
     return ACT_OK;
+}
+
+}  // namespace
+
+extern "C" int act_attention_bwd_noalloc(const void* q, const void* k, const void* v, const void* o,
+                                         const float* lse, const void* dout, void* dq, void* dk, void* dv,
+                                         int clips, int T, int Tk, int H, const int32_t* nvalid, int causal,
+                                         int zero_key, const float* rope, void* stream) {
+    // no C++ exception may cross the C ABI: an embedding host would terminate
+    try {
+        return attention_bwd_noalloc(q, k, v, o, lse, dout, dq, dk, dv, clips, T, Tk, H, nvalid, causal, zero_key,
+                                     rope, stream);
+    } catch (const std::exception& ex) {
+        try {
+            return fail(ACT_ERR_INVALID, std::string("act_attention_bwd_noalloc: ") + ex.what());
+        } catch (...) {
+            return ACT_ERR_INVALID;
+        }
+    } catch (...) {
+        return ACT_ERR_INVALID;
+    }
 }

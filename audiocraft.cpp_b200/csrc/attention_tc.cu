@@ -799,11 +799,8 @@ void attn_fwd_tc(const AttnArgs& a, int* err, cudaStream_t s) {
     tc_make_map(&maps.q, a.q, (long)a.clips * a.T, (long)a.H * AT_HD, a.ldq, AT_HD, AT_BQ);
     tc_make_map(&maps.k, a.k, (long)a.clips * a.Tk, (long)a.H * AT_HD, a.ldk, AT_HD, AT_BK);  // 64 x 64
     tc_make_map(&maps.v, a.v, (long)a.clips * a.Tk, (long)a.H * AT_HD, a.ldv, AT_HD, AT_BK);
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
-        configured = true;
-    }
+    static DeviceOnce once;
+    once([] { cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM); });
     {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((a.T + AT_BQ - 1) / AT_BQ, a.H, a.clips);
@@ -839,11 +836,8 @@ void attn_bwd_tc(const AttnArgs& a, int* err, cudaStream_t s) {
     tc_make_map(&maps.k, a.k, (long)a.clips * a.Tk, (long)a.H * 64, a.ldk, 64, AB_BK);
     tc_make_map(&maps.v, a.v, (long)a.clips * a.Tk, (long)a.H * 64, a.ldv, 64, AB_BK);
     make_f32_map(&maps.dq, a.dq_acc, (long)a.clips * a.T, (long)a.H * 64, a.ldq_acc);
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AB_SMEM);
-        configured = true;
-    }
+    static DeviceOnce once;
+    once([] { cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AB_SMEM); });
     {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((a.Tk + AB_BK - 1) / AB_BK, a.H, a.clips);

@@ -4,9 +4,51 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 typedef __nv_bfloat16 bf16;
 
 namespace act {
+
+// Kernel attributes set with cudaFuncSetAttribute belong to the device that is current at the
+// call, so a one-time set-up has to run once on every device that launches the kernel.
+// DeviceOnce runs its function at most once per device ordinal, from any number of host
+// threads; ordinals beyond 63 run it on every call.
+class DeviceOnce {
+  public:
+    template <class Fn>
+    void operator()(Fn&& fn) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) return;
+        if (dev < 0 || dev >= 64) {
+            fn();
+            return;
+        }
+        const uint64_t bit = 1ull << dev;
+        if (done_.load(std::memory_order_acquire) & bit) return;
+        std::lock_guard<std::mutex> g(mu_);
+        if (done_.load(std::memory_order_relaxed) & bit) return;
+        fn();
+        done_.fetch_or(bit, std::memory_order_release);
+    }
+
+  private:
+    std::atomic<uint64_t> done_{0};
+    std::mutex mu_;
+};
+
+// Multiprocessor count of the current device (cached per ordinal).
+inline int current_sm_count() {
+    static std::atomic<int> cache[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 1;
+    int n = (dev >= 0 && dev < 64) ? cache[dev].load(std::memory_order_relaxed) : 0;
+    if (n > 0) return n;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 1;
+    if (dev >= 0 && dev < 64) cache[dev].store(n, std::memory_order_relaxed);
+    return n;
+}
 
 // A&S 7.1.26 GELU and the derivative of that approximation (the reference trains through
 // the approximation, src/ac/lora.h:97-110, so its gradient is the one autodiff yields).

@@ -271,7 +271,10 @@ struct act_ctx {
 
     ncclComm_t comm = nullptr;
     int* kerr = nullptr;
+    int* probe_flag = nullptr;  // never set: act_wait_probe waits on it until its limit runs out
     bool use_tc = true;
+    // which kernel family each launch was issued to (ACT_PATH_*), counted as the step is issued
+    int64_t path_count[ACT_PATH_COUNT] = {};
 
     // ------------------------------------------------------------------------------------
     template <class Tp>
@@ -337,8 +340,10 @@ struct act_ctx {
             g.sk_flag = sk_flag;
         }
         if (use_tc && gemm_tc_supported(g)) {
+            ++path_count[ACT_PATH_GEMM_TC];
             timed(cls, fl, 0, [&] { gemm_tc_auto(g, kerr, stream); });
         } else {
+            ++path_count[ACT_PATH_GEMM_MMA];
             timed(cls, fl, 0, [&] { gemm(g, stream); });
             if (g.out_bf)  // the generic path has no second output: convert afterwards
                 timed(2, 0, 0, [&] {
@@ -376,16 +381,26 @@ struct act_ctx {
     // tcgen05 paths are disabled or the operands do not qualify
     void run_rank(const SkinnyArgs& k, const GemmArgs& fallback) {
         const double fl = 2.0 * k.M * k.nb * (double)k.K;
-        if (use_tc && skinny_supported(k)) timed(2, fl, 0, [&] { skinny_gemm(k, kerr, stream); });
-        else run_gemm(fallback, 2);
+        if (use_tc && skinny_supported(k)) {
+            ++path_count[ACT_PATH_RANK_TC];
+            timed(2, fl, 0, [&] { skinny_gemm(k, kerr, stream); });
+        } else {
+            ++path_count[ACT_PATH_RANK_MMA];
+            run_gemm(fallback, 2);
+        }
     }
 
     // kernels record a nonzero code here instead of hanging on a wait that cannot finish
+    // (the word is cleared when it is reported, so that the context stays usable afterwards)
     void check_kernel_error() {
         int e = 0;
         CK(cudaMemcpyAsync(&e, kerr, sizeof(int), cudaMemcpyDeviceToHost, stream));
         CK(cudaStreamSynchronize(stream));
-        if (e) throw Error(ACT_ERR_CUDA, "device kernel reported a timed-out wait (code " + std::to_string(e) + ")");
+        if (e) {
+            CK(cudaMemsetAsync(kerr, 0, sizeof(int), stream));
+            CK(cudaStreamSynchronize(stream));
+            throw Error(ACT_ERR_CUDA, "device kernel reported a timed-out wait (code " + std::to_string(e) + ")");
+        }
     }
 
     // split-K count for the token reductions: about two CTAs per SM, each with a long enough
@@ -543,8 +558,10 @@ struct act_ctx {
         sa.T = T; sa.Tk = T; sa.H = H; sa.clips = n; sa.causal = dit ? 0 : 1; sa.zero_key = dit ? md.add_zero_attn : 0;
         sa.rope = dit ? rope : nullptr; sa.rope_load = 0; sa.scale = 1.0f / std::sqrt((float)md.head_dim);
         sa.o = y.o1; sa.ldo = D; sa.lse = y.lse1;
+        const bool fwd_tc = use_tc && attn_fwd_tc_supported(sa);
+        ++path_count[fwd_tc ? ACT_PATH_ATTN_FWD_TC : ACT_PATH_ATTN_FWD_MMA];
         timed(1, attn_flops(n, T, true), 0, [&] {
-            if (use_tc && attn_fwd_tc_supported(sa)) attn_fwd_tc(sa, kerr, stream);
+            if (fwd_tc) attn_fwd_tc(sa, kerr, stream);
             else attn_fwd(sa, stream);
         });
         {
@@ -564,6 +581,7 @@ struct act_ctx {
         ca.T = T; ca.Tk = C; ca.H = H; ca.clips = n; ca.nvalid = dit ? nvalid_dev : nullptr;
         ca.zero_key = dit ? md.add_zero_attn : 0; ca.scale = sa.scale;
         ca.o = y.o2; ca.ldo = D; ca.lse = y.lse2;
+        ++path_count[ACT_PATH_ATTN_FWD_MMA];
         timed(1, attn_flops(n, C, false), 0, [&] { attn_fwd(ca, stream); });
         {
             GemmArgs e; e.mode = EPI_RESID_F32; e.out = y.xmid2; e.ldo = D; e.resid = y.xmid; e.ldr = D;
@@ -650,6 +668,7 @@ struct act_ctx {
             ca.lddq_bf = D;
             ca.dq_scale = y.p[2].dora ? y.p[2].g : nullptr;
         }
+        ++path_count[ACT_PATH_ATTN_BWD_MMA];
         timed(1, 2 * attn_flops(n, C, false), 0, [&] {
             if (!dq_direct) CK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * D, stream));
             if (split && need_dkv) CK(cudaMemsetAsync(dkv_acc, 0, sizeof(float) * crows * 2 * D, stream));
@@ -676,9 +695,11 @@ struct act_ctx {
         sa.dout = dob; sa.lddo = D; sa.dvec = dvec; sa.dq_acc = dq_acc; sa.ldq_acc = D;
         sa.dk = dqkv + D; sa.dv = dqkv + 2 * D; sa.lddk = sa.lddv = 3 * D;
         sa.kscale = y.p[0].dora ? y.p[0].g + D : nullptr; sa.vscale = y.p[0].dora ? y.p[0].g + 2 * D : nullptr;
+        const bool bwd_tc = use_tc && attn_bwd_tc_supported(sa);
+        ++path_count[bwd_tc ? ACT_PATH_ATTN_BWD_TC : ACT_PATH_ATTN_BWD_MMA];
         timed(1, 2 * attn_flops(n, T, true), 0, [&] {
             CK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * D, stream));
-            if (use_tc && attn_bwd_tc_supported(sa)) attn_bwd_tc(sa, kerr, stream);
+            if (bwd_tc) attn_bwd_tc(sa, kerr, stream);
             else attn_bwd(sa, stream);
             attn_dq_finish(sa, dqkv, 3 * D, y.p[0].dora ? y.p[0].g : nullptr, stream);
         });
@@ -1020,6 +1041,7 @@ struct act_ctx {
         CK(cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming));
         CK(cudaEventCreateWithFlags(&ev_join, cudaEventDisableTiming));
         kerr = dalloc<int>(1);
+        probe_flag = dalloc<int>(1);
         {
             int sms = 0;
             CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
@@ -2096,6 +2118,76 @@ int act_attention(int device, const void* q, const void* k, const void* v, const
             *ms_bwd = 0.f;
             if (bwd) CK(cudaEventElapsedTime(ms_bwd, ev[2], ev[3]));
         }
+        cleanup();
+        return ACT_OK;
+    } catch (const Error& e) {
+        g_error = e.what();
+        cleanup();
+        return e.code;
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        cleanup();
+        return ACT_ERR_INVALID;
+    }
+}
+
+int act_path_counts(act_ctx* ctx, int64_t* counts, int n) {
+    if (!ctx || !counts || n < 0) return ACT_ERR_INVALID;
+    for (int i = 0; i < n; ++i) counts[i] = i < ACT_PATH_COUNT ? ctx->path_count[i] : 0;
+    return ACT_OK;
+}
+
+int act_wait_probe(act_ctx* ctx, int64_t limit_ns) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] {
+        if (limit_ns <= 0 || limit_ns > 10000000000LL) throw Error(ACT_ERR_INVALID, "wait limit out of range");
+        wait_probe(ctx->probe_flag, limit_ns, ctx->kerr, ctx->stream);
+        CK(cudaGetLastError());
+        ctx->check_kernel_error();
+    });
+}
+
+int act_mg_staged(act_ctx* ctx, int32_t* ids, size_t n_ids, int32_t* targets, size_t n_targets) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] {
+        if (ctx->mf) throw Error(ACT_ERR_INVALID, "not a MusicGen context");
+        if (ctx->staged_n <= 0) throw Error(ACT_ERR_STATE, "no staged batch");
+        const size_t n = ctx->staged_n, nq = ctx->md.n_q, sel = ctx->ad.frames - ctx->ad.prefix_frames;
+        if (!ids || !targets || n_ids != n * nq * ctx->T || n_targets != n * nq * sel)
+            throw Error(ACT_ERR_INVALID, "staged buffer size mismatch");
+        CK(cudaMemcpyAsync(ids, ctx->d_ids, n_ids * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        CK(cudaMemcpyAsync(targets, ctx->d_tgt, n_targets * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        CK(cudaStreamSynchronize(ctx->stream));
+    });
+}
+
+int act_q8_0_dequant(int device, const void* blocks, int64_t nblocks, float* out_f32, uint16_t* out_bf16) {
+    void *db = nullptr, *df = nullptr, *dh = nullptr;
+    cudaStream_t st = nullptr;
+    auto cleanup = [&] {
+        if (st) cudaStreamSynchronize(st);
+        cudaFree(db); cudaFree(df); cudaFree(dh);
+        if (st) cudaStreamDestroy(st);
+    };
+    try {
+        if (!blocks || nblocks <= 0 || (!out_f32 && !out_bf16)) throw Error(ACT_ERR_INVALID, "invalid Q8_0 arguments");
+        CK(cudaSetDevice(device));
+        CK(cudaStreamCreate(&st));
+        const size_t n = (size_t)nblocks * 32;
+        CK(cudaMalloc(&db, (size_t)nblocks * 34));
+        CK(cudaMemcpyAsync(db, blocks, (size_t)nblocks * 34, cudaMemcpyHostToDevice, st));
+        if (out_f32) {
+            CK(cudaMalloc(&df, n * 4));
+            q8_0_to_f32(static_cast<const uint8_t*>(db), nblocks, static_cast<float*>(df), st);
+            CK(cudaMemcpyAsync(out_f32, df, n * 4, cudaMemcpyDeviceToHost, st));
+        }
+        if (out_bf16) {
+            CK(cudaMalloc(&dh, n * 2));
+            q8_0_to_bf16(static_cast<const uint8_t*>(db), nblocks, static_cast<bf16*>(dh), st);
+            CK(cudaMemcpyAsync(out_bf16, dh, n * 2, cudaMemcpyDeviceToHost, st));
+        }
+        CK(cudaGetLastError());
+        CK(cudaStreamSynchronize(st));
         cleanup();
         return ACT_OK;
     } catch (const Error& e) {

@@ -253,11 +253,8 @@ template <int BM, int BN, int WM_, int WN_, bool AK, bool BKM, int BK = 32, int 
 void launch(const GemmArgs& a, cudaStream_t s) {
     using S = Smem<BM, BN, AK, BKM, BK, STAGES>;
     auto kern = gemm_mma_kernel<BM, BN, WM_, WN_, AK, BKM, BK, STAGES>;
-    static bool configured = false;  // per instantiation; set before first launch / capture
-    if (!configured) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
-        configured = true;
-    }
+    static DeviceOnce once;  // per instantiation and device; before the first launch / capture
+    once([&] { cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES); });
     dim3 grid((a.N + BN - 1) / BN, (a.M + BM - 1) / BM, a.splitk);
     launch_pdl(kern, grid, dim3(WM_ * WN_ * 32), S::BYTES, s, a);
 }

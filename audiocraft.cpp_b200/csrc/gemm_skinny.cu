@@ -295,11 +295,8 @@ void skinny_gemm(const SkinnyArgs& a, int* err, cudaStream_t s) {
     p.M = a.M; p.K = a.K; p.nb = a.nb; p.a_mn = a.a_mn ? 1 : 0; p.b_mn = a.b_mn ? 1 : 0;
     p.kind = a.kind; p.alpha = a.alpha; p.out = a.out; p.ldo = a.ldo;
     p.splits = splits; p.err = err;
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM);
-        configured = true;
-    }
+    static DeviceOnce once;
+    once([] { cudaFuncSetAttribute(skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM); });
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(tiles, splits, 1);
     cfg.blockDim = dim3(SK_THREADS, 1, 1);

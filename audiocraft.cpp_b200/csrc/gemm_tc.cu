@@ -936,7 +936,6 @@ void make_epilogue_maps(TcMaps& maps, const GemmArgs& a) {
     else maps.out_bf = maps.out;
 }
 
-int g_num_sms = 0;
 
 template <int BN, bool B_MN>
 void launch_tc(const GemmArgs& a, int* err, cudaStream_t s) {
@@ -964,18 +963,11 @@ void launch_tc(const GemmArgs& a, int* err, cudaStream_t s) {
     p.rope = a.rope; p.rope_T = a.rope_T; p.rope_cols = a.rope_cols;
     p.out_bf = (a.mode == EPI_STORE_F32 || a.mode == EPI_ACCUM_F32 || a.mode == EPI_RESID_F32) ? a.out_bf : nullptr;
     auto kern = gemm_tc_kernel<BN, B_MN>;
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
-        configured = true;
-    }
-    if (!g_num_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    }
+    static DeviceOnce once;
+    once([&] { cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM); });
+    const int num_sms = current_sm_count();
     const int tiles = p.num_m * p.num_n;
-    const int grid = tiles < g_num_sms ? tiles : g_num_sms;
+    const int grid = tiles < num_sms ? tiles : num_sms;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
     cfg.blockDim = dim3(NTHREADS, 1, 1);
@@ -1029,21 +1021,16 @@ void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
     p.sk_part = a.sk_part; p.sk_flag = a.sk_flag;
     auto whole = gemm_tc2_kernel<BN2, B_MN, false>;
     auto split = gemm_tc2_kernel<BN2, B_MN, BN2 == 256>;
-    static bool configured = false;
-    if (!configured) {
+    static DeviceOnce once;
+    once([&] {
         for (auto k : {whole, split}) {
             cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
             cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
         }
-        configured = true;
-    }
-    if (!g_num_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    }
+    });
+    const int num_sms = current_sm_count();
     const int tiles = ((a.M + 2 * BM - 1) / (2 * BM)) * (a.N / BN2);
-    const int pairs = tiles < g_num_sms / 2 ? tiles : g_num_sms / 2;
+    const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
     const auto kern = sk_pays(BN2, tiles, pairs, a) ? split : whole;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
@@ -1097,20 +1084,16 @@ int gemm_sk_flag_count(int num_sms) { return (num_sms / 2) * 2; }
 void gemm_tc2(const GemmArgs& a, int* err, cudaStream_t s) { gemm_tc2_width(a, err, s, a.N % 256 == 0 ? 256 : 128); }
 
 void gemm_tc_auto(const GemmArgs& a, int* err, cudaStream_t s) {
-    if (!g_num_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    }
+    const int num_sms = current_sm_count();
     // Each SM computes 128-row tiles in every variant; the cost of a launch is its number of
     // rounds over the SMs times the tile width, scaled by per-column efficiencies measured on
     // the cfg-2 shapes (256-wide 2-CTA tiles fastest; 128-wide pair tiles 1.6x slower per
     // column, so they only win where they save whole rounds).
     static const double eff[3] = {1.05, 1.0, 1.62};  // 1-CTA 256 (or 128), 2-CTA 256, 2-CTA 128
     auto rounds = [&](long tiles, long slots) { return (tiles + slots - 1) / slots; };
-    const long m1 = (a.M + BM - 1) / BM, m2 = (a.M + 2 * BM - 1) / (2 * BM), pairs = g_num_sms / 2;
+    const long m1 = (a.M + BM - 1) / BM, m2 = (a.M + 2 * BM - 1) / (2 * BM), pairs = num_sms / 2;
     const int w1 = a.N % 256 == 0 ? 256 : 128;
-    double best = rounds(m1 * (a.N / w1), g_num_sms) * (double)w1 * eff[0];
+    double best = rounds(m1 * (a.N / w1), num_sms) * (double)w1 * eff[0];
     int choice = 0;
     if (gemm_tc2_supported(a)) {
         if (a.N % 256 == 0) {

@@ -222,6 +222,11 @@ void adamw(float* value, float* m, float* v, float* grad, const uint8_t* decay_m
            float inv_count, float clip, float lr, float beta1, float beta2, float eps, float decay,
            float bc1, float bc2, double* norm_partials, int* nonfinite, cudaStream_t s);
 
+// One bounded wait (the tcgen05 kernels' flag wait) on `flag` until it holds 1, giving up after
+// limit_ns nanoseconds with WAIT_PROBE_CODE recorded in *err (wait_probe.cu).
+constexpr int WAIT_PROBE_CODE = 99;
+void wait_probe(const int* flag, long long limit_ns, int* err, cudaStream_t s);
+
 // Q8_0 blocks -> bf16 (one-time weight binding) and fp32 (parity checks).
 void q8_0_to_bf16(const uint8_t* blocks, long nblocks, bf16* out, cudaStream_t s);
 void q8_0_to_f32(const uint8_t* blocks, long nblocks, float* out, cudaStream_t s);

@@ -78,12 +78,14 @@ __device__ __forceinline__ void red_release_add(int* p, int v) {
     asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Wait until *flag >= target; false (and `code` recorded) if that does not happen in time.
-static __device__ __noinline__ bool flag_wait(const int* flag, int target, int* err, int code) {
+// Wait until *flag >= target; false (and `code` recorded) if that does not happen within
+// limit_ns nanoseconds.
+static __device__ __noinline__ bool flag_wait(const int* flag, int target, int* err, int code,
+                                              unsigned long long limit_ns = WAIT_NS) {
     const unsigned long long t0 = globaltimer();
     while (ld_acquire_gpu(flag) < target) {
         __nanosleep(256);
-        if (globaltimer() - t0 > WAIT_NS) {
+        if (globaltimer() - t0 > limit_ns) {
             atomicCAS(err, 0, code);
             return false;
         }

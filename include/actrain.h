@@ -209,13 +209,43 @@ int act_attention(int device, const void* q, const void* k, const void* v, const
  * loads the library holds it until the process exits.  A problem needing more than
  * clips*T*H*64 + clips*H*T <= ACT_NOALLOC_ATTN_SCRATCH_FLOATS floats is rejected with
  * ACT_ERR_INVALID.  The first call on each device looks up that device's copy of the array
- * (cudaGetSymbolAddress); make that first call before any stream capture.  Every call uses
- * the same array and zeroes the accumulator it needs, so calls that overlap on the GPU (on
- * different streams, or from different threads) race: serialise them. */
+ * (cudaGetSymbolAddress); make that first call before any stream capture, and do not reset the
+ * device (cudaDeviceReset or a primary-context reset) afterwards: the looked-up address is kept
+ * for the life of the process.  Every call uses the same array and zeroes the accumulator it
+ * needs, so calls that overlap on the GPU (on different streams, or from different threads)
+ * race: serialise them.  q, k, v, o, dout, dq, dk and dv must be 16-byte aligned, rope 8-byte,
+ * lse and nvalid 4-byte; other pointers are rejected with ACT_ERR_INVALID before any work is
+ * queued. */
 #define ACT_NOALLOC_ATTN_SCRATCH_FLOATS (8L * 1024 * 1024)
 int act_attention_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const float* lse,
                               const void* dout, void* dq, void* dk, void* dv, int clips, int T, int Tk, int H,
                               const int32_t* nvalid, int causal, int zero_key, const float* rope, void* stream);
+/* Kernel family each launch of the steps issued so far went to, counted as the launches are
+ * issued (a captured graph counts once, when it is captured).  counts[i] for i < n receives the
+ * count of ACT_PATH_i. */
+#define ACT_PATH_ATTN_FWD_TC 0   /* tcgen05 self-attention forward (attention_tc.cu) */
+#define ACT_PATH_ATTN_FWD_MMA 1  /* mma.sync attention forward (attention.cu) */
+#define ACT_PATH_ATTN_BWD_TC 2   /* tcgen05 self-attention backward */
+#define ACT_PATH_ATTN_BWD_MMA 3  /* mma.sync attention backward */
+#define ACT_PATH_GEMM_TC 4       /* tcgen05 projection GEMM (gemm_tc.cu) */
+#define ACT_PATH_GEMM_MMA 5      /* mma.sync GEMM (gemm_mma.cu) */
+#define ACT_PATH_RANK_TC 6       /* tcgen05 rank-block product (gemm_skinny.cu) */
+#define ACT_PATH_RANK_MMA 7      /* rank-block product on the mma.sync GEMM */
+#define ACT_PATH_COUNT 8
+int act_path_counts(act_ctx* ctx, int64_t* counts, int n);
+/* Failure-path check of the device error word (no reference counterpart): one kernel runs the
+ * tcgen05 kernels' bounded flag wait on a flag that nothing sets, gives up after limit_ns
+ * (1 ns .. 10 s), records its code, and the call returns ACT_ERR_CUDA as a step would after a
+ * timed-out wait.  The word is cleared when reported: the context stays usable. */
+int act_wait_probe(act_ctx* ctx, int64_t limit_ns);
+/* MusicGen: read back the staged delayed inputs ([n][n_q][frames + n_q - 1], build_pattern_sequence
+ * of src/mg/pattern.h:64-76 without its last step) and the scored targets ([n][n_q][frames -
+ * prefix_frames], src/mg/train.h:195-205) of the last act_mg_stage / act_mg_step. */
+int act_mg_staged(act_ctx* ctx, int32_t* ids, size_t n_ids, int32_t* targets, size_t n_targets);
+/* Q8_0 blocks (34 bytes: fp16 d, int8 q[32]; tools/ac-quantize.cpp:161) dequantised on the
+ * device by the kernels act_bind_weight uses: out_f32 = d * q in fp32, out_bf16 = that value
+ * rounded to bf16 (the GEMM operand).  Either output may be NULL. */
+int act_q8_0_dequant(int device, const void* blocks, int64_t nblocks, float* out_f32, uint16_t* out_bf16);
 /* kernels in the captured step graph for microbatch size n (-1 before the graph exists) */
 int64_t act_graph_kernel_nodes(act_ctx* ctx, int n);
 

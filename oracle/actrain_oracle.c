@@ -58,13 +58,57 @@ typedef struct {
 /* ------------------------------------------------------------------------------------ */
 /* dense helpers                                                                         */
 
-#define MB_ 32
-#define NB_ 256
-#define KB_ 128
+/* Register-blocked fp32 matmul: a 4 x 24 micro-tile of C stays in 12 AVX2 registers across a
+ * k-chunk of KB_ while B is streamed from a packed panel.  Every element of C is summed over k
+ * in ascending order, chunk after chunk, whatever the thread count: results do not depend on
+ * the OpenMP schedule.  (The arithmetic is what the reference's CPU backend does for a mul_mat
+ * node; only the order of the additions is this file's own.) */
+#define MR_ 4
+#define NR_ 24
+#define MB_ 64
+#define NB_ 240
+#define KB_ 256
 
 static int imin(int a, int b) { return a < b ? a : b; }
 
-/* C[M][N] (=|+=) alpha * A[M][K] . B[K][N]; fixed k-ascending accumulation per element. */
+#if defined(__AVX2__) && defined(__FMA__)
+#include <immintrin.h>
+/* c[MR_][ldc] += a[MR_][lda] (k = 0..kc-1) . bp[kc][NR_] */
+static void ukern(int kc, const float* a, int lda, const float* bp, float* c, int ldc) {
+    __m256 c00 = _mm256_loadu_ps(c), c01 = _mm256_loadu_ps(c + 8), c02 = _mm256_loadu_ps(c + 16);
+    __m256 c10 = _mm256_loadu_ps(c + ldc), c11 = _mm256_loadu_ps(c + ldc + 8), c12 = _mm256_loadu_ps(c + ldc + 16);
+    __m256 c20 = _mm256_loadu_ps(c + 2 * ldc), c21 = _mm256_loadu_ps(c + 2 * ldc + 8),
+           c22 = _mm256_loadu_ps(c + 2 * ldc + 16);
+    __m256 c30 = _mm256_loadu_ps(c + 3 * ldc), c31 = _mm256_loadu_ps(c + 3 * ldc + 8),
+           c32 = _mm256_loadu_ps(c + 3 * ldc + 16);
+    for (int k = 0; k < kc; ++k) {
+        const __m256 b0 = _mm256_loadu_ps(bp + k * NR_), b1 = _mm256_loadu_ps(bp + k * NR_ + 8),
+                     b2 = _mm256_loadu_ps(bp + k * NR_ + 16);
+        __m256 av = _mm256_broadcast_ss(a + k);
+        c00 = _mm256_fmadd_ps(av, b0, c00); c01 = _mm256_fmadd_ps(av, b1, c01); c02 = _mm256_fmadd_ps(av, b2, c02);
+        av = _mm256_broadcast_ss(a + lda + k);
+        c10 = _mm256_fmadd_ps(av, b0, c10); c11 = _mm256_fmadd_ps(av, b1, c11); c12 = _mm256_fmadd_ps(av, b2, c12);
+        av = _mm256_broadcast_ss(a + 2 * lda + k);
+        c20 = _mm256_fmadd_ps(av, b0, c20); c21 = _mm256_fmadd_ps(av, b1, c21); c22 = _mm256_fmadd_ps(av, b2, c22);
+        av = _mm256_broadcast_ss(a + 3 * lda + k);
+        c30 = _mm256_fmadd_ps(av, b0, c30); c31 = _mm256_fmadd_ps(av, b1, c31); c32 = _mm256_fmadd_ps(av, b2, c32);
+    }
+    _mm256_storeu_ps(c, c00); _mm256_storeu_ps(c + 8, c01); _mm256_storeu_ps(c + 16, c02);
+    _mm256_storeu_ps(c + ldc, c10); _mm256_storeu_ps(c + ldc + 8, c11); _mm256_storeu_ps(c + ldc + 16, c12);
+    _mm256_storeu_ps(c + 2 * ldc, c20); _mm256_storeu_ps(c + 2 * ldc + 8, c21); _mm256_storeu_ps(c + 2 * ldc + 16, c22);
+    _mm256_storeu_ps(c + 3 * ldc, c30); _mm256_storeu_ps(c + 3 * ldc + 8, c31); _mm256_storeu_ps(c + 3 * ldc + 16, c32);
+}
+#else
+static void ukern(int kc, const float* a, int lda, const float* bp, float* c, int ldc) {
+    for (int i = 0; i < MR_; ++i)
+        for (int k = 0; k < kc; ++k) {
+            const float av = a[(size_t)i * lda + k];
+            for (int j = 0; j < NR_; ++j) c[(size_t)i * ldc + j] += av * bp[k * NR_ + j];
+        }
+}
+#endif
+
+/* C[M][N] (=|+=) alpha * A[M][K] . B[K][N]; k-ascending accumulation per element. */
 static void mm_nn(int M, int N, int K, const float* A, int lda, const float* B, int ldb,
                   float* C, int ldc, float alpha, int accumulate) {
     const int nib = (M + MB_ - 1) / MB_, njb = (N + NB_ - 1) / NB_;
@@ -72,19 +116,36 @@ static void mm_nn(int M, int N, int K, const float* A, int lda, const float* B, 
     for (int ib = 0; ib < nib; ++ib)
         for (int jb = 0; jb < njb; ++jb) {
             const int i0 = ib * MB_, i1 = imin(M, i0 + MB_), j0 = jb * NB_, j1 = imin(N, j0 + NB_);
-            const int nj = j1 - j0;
-            float acc[MB_][NB_];
-            for (int i = 0; i < i1 - i0; ++i) memset(acc[i], 0, sizeof(float) * nj);
+            const int nj = j1 - j0, npan = (nj + NR_ - 1) / NR_;
+            static __thread float acc[MB_ + MR_][NB_];
+            static __thread float bp[KB_ * NB_];
+            static __thread float ap[MR_][KB_];
+            for (int i = 0; i < i1 - i0; ++i) memset(acc[i], 0, sizeof(float) * NB_);
             for (int k0 = 0; k0 < K; k0 += KB_) {
-                const int k1 = imin(K, k0 + KB_);
-                for (int i = i0; i < i1; ++i) {
-                    float* ac = acc[i - i0];
-                    const float* a = A + (size_t)i * lda;
-                    for (int k = k0; k < k1; ++k) {
-                        const float av = a[k];
-                        const float* b = B + (size_t)k * ldb + j0;
-                        for (int j = 0; j < nj; ++j) ac[j] += av * b[j];
+                const int kc = imin(K, k0 + KB_) - k0;
+                /* pack B[k0 .. k0+kc)[j0 .. j1) as npan panels of [kc][NR_], zero padded */
+                for (int p = 0; p < npan; ++p) {
+                    float* dst = bp + (size_t)p * kc * NR_;
+                    const int jj = j0 + p * NR_, w = imin(NR_, j1 - jj);
+                    for (int k = 0; k < kc; ++k) {
+                        const float* src = B + (size_t)(k0 + k) * ldb + jj;
+                        int j = 0;
+                        for (; j < w; ++j) dst[k * NR_ + j] = src[j];
+                        for (; j < NR_; ++j) dst[k * NR_ + j] = 0.0f;
                     }
+                }
+                for (int i = i0; i < i1; i += MR_) {
+                    const int h = imin(MR_, i1 - i);
+                    const float* a = A + (size_t)i * lda + k0;
+                    int la = lda;
+                    if (h < MR_) { /* ragged last rows: pad a copy with zero rows */
+                        for (int r = 0; r < MR_; ++r)
+                            for (int k = 0; k < kc; ++k) ap[r][k] = r < h ? A[(size_t)(i + r) * lda + k0 + k] : 0.0f;
+                        a = &ap[0][0];
+                        la = KB_;
+                    }
+                    for (int p = 0; p < npan; ++p)
+                        ukern(kc, a, la, bp + (size_t)p * kc * NR_, &acc[i - i0][p * NR_], NB_);
                 }
             }
             for (int i = i0; i < i1; ++i) {

@@ -1,6 +1,9 @@
 """Generate the golden fixtures that pin the CPU oracle.
 
-Run from the repository root in the build container:  python tests/golden/gen_fixtures.py
+Run from the repository root:  python tests/golden/gen_fixtures.py [--reference DIR]
+
+DIR (or the environment variable AUDIOCRAFT_CPP_REFERENCE) is a checkout of the audiocraft.cpp
+tree; without it the delay-pattern goldens already committed are kept.
 
 Three sources, none of them the oracle itself:
   * an fp64 PyTorch restatement of the reference training graph, differentiated by torch
@@ -24,7 +27,7 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = "/root/reference"
+REF = os.environ.get("AUDIOCRAFT_CPP_REFERENCE", "")
 TARGETS = ("self.qkv", "self.out", "cross.q", "cross.kv", "cross.out", "ff.0", "ff.2")
 
 torch.set_default_dtype(torch.float64)
@@ -416,9 +419,9 @@ def q8_fixture():
 
 
 def pattern_fixture():
-    path = os.path.join(REF, "tests", "pattern_test.cpp")
+    path = os.path.join(REF, "tests", "pattern_test.cpp") if REF else ""
     out = os.path.join(HERE, "pattern_goldens.json")
-    if not os.path.exists(path):
+    if not path or not os.path.exists(path):
         print("pattern goldens: reference tree absent, keeping committed JSON")
         return
     text = open(path).read()
@@ -438,6 +441,9 @@ def pattern_fixture():
 
 
 def main():
+    global REF
+    if "--reference" in sys.argv:
+        REF = sys.argv[sys.argv.index("--reference") + 1]
     tiny = dict(dim=8, layers=4, heads=2, head_dim=4, ff_dim=16, latent_dim=4, cond_dim=6,
                 time_dim=8, n_skip=1, norm_eps=1e-5, add_zero_attn=True)
     small = dict(dim=16, layers=6, heads=2, head_dim=8, ff_dim=32, latent_dim=4, cond_dim=6,

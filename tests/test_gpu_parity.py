@@ -223,3 +223,67 @@ def test_invalid_inputs_are_rejected():
         case.ctx.mf_step(clean, noise, hidden, t, unc, np.array([99, -1, -1], np.int32))
     with pytest.raises(A.ActError):
         case.ctx.optimizer(lr=-1.0, step=1)
+
+
+# ---- the benchmarked configuration's shapes (BASELINE cfg 2 per layer: d1024, 16 heads, FFN 4096,
+# T = 750, 32 tokens, Q8_0 base, rank 16, alpha 32), two layers and two clips so that the oracle
+# finishes in seconds.  At T >= 128 the self-attention forward and backward run on the tcgen05
+# kernels inside the step; path_counts proves it.
+CFG2 = dict(dim=1024, layers=2, heads=16, ff=4096, lat=128, cond=768, tdim=256, T=750, C=32, rank=16,
+            alpha=32.0, wstd=0.02, wtype="q8_0", batch=2)
+
+
+def _assert_tc_attention(case, layers):
+    pc = case.ctx.path_counts()
+    assert pc["attn_fwd_tc"] == layers and pc["attn_bwd_tc"] == layers, pc
+    # every block projection (seven per layer, forward) at least runs on the tcgen05 GEMM
+    assert pc["gemm_tc"] >= 7 * layers, pc
+
+
+@pytest.mark.parametrize("dora,targets", [(False, 0x63), (False, 0x7F), (True, 0x7F)],
+                         ids=["lora-qkv-out-ffn", "lora-all", "dora-all"])
+def test_mf_cfg2_shapes_match_oracle(dora, targets):
+    case = MfCase(**CFG2, dora=dora, targets=targets, seed=50 + targets + dora)
+    inp = case.inputs(n=2, modes=["cond", "padded"])
+    loss = case.ctx.mf_step(*inp)
+    _assert_tc_attention(case, 2)
+    ref_loss, ref_g = case.oracle(case.params, inp)
+    _check(loss, ref_loss, case.ctx.get_grads(), ref_g, case.layout)
+
+
+@pytest.mark.parametrize("T", [200, 750])
+def test_mf_tcgen05_attention_in_step_with_dora(T):
+    # narrow model, long clips: the tcgen05 self-attention with the DoRA k / v / q column factors,
+    # the inverse RoPE of the dQ finish and the 3-D strided dQKV layout, against the oracle
+    case = MfCase(dim=128, layers=3, heads=2, ff=256, T=T, C=16, dora=True, batch=2, wtype="q8_0", seed=60 + T)
+    inp = case.inputs(n=2, modes=["cond", "null"])
+    loss = case.ctx.mf_step(*inp)
+    _assert_tc_attention(case, 3)
+    ref_loss, ref_g = case.oracle(case.params, inp)
+    _check(loss, ref_loss, case.ctx.get_grads(), ref_g, case.layout)
+
+
+def test_mf_cfg1_training_trajectory():
+    """BASELINE cfg 1: 24 blocks at d1024, one 250-frame clip, 16 tokens, F16 base, LoRA r16 / alpha
+    32 on q/k/v/o/ffn_in/ffn_out with the reference initialisation (B = 0), AdamW lr 1e-4 wd 0.01,
+    10 steps.  The per-step loss of the device trajectory stays within 1e-3 of the oracle's own
+    trajectory (oracle gradients, oracle AdamW)."""
+    case = MfCase(dim=1024, layers=24, heads=16, ff=4096, lat=128, cond=768, tdim=256, T=250, C=16, rank=16,
+                  alpha=32.0, wstd=0.02, wtype="f16", batch=1, targets=0x63, b_std=0.0, seed=0)
+    mask = np.zeros(case.params.size, np.uint8)
+    for name, off, shape in case.layout:
+        mask[off:off + int(np.prod(shape))] = 1
+    p = case.params.copy()
+    m, v = np.zeros_like(p), np.zeros_like(p)
+    for step in range(1, 11):
+        inp = case.inputs(n=1, modes=["cond"])
+        loss = case.ctx.mf_step(*inp)
+        ref_loss, ref_g = case.oracle(p, inp)
+        np.testing.assert_allclose(loss, ref_loss, rtol=LOSS_RTOL, err_msg=f"step {step}")
+        if step == 1:  # B = 0: only dB is nonzero, dA is exactly zero on both sides
+            g = case.ctx.get_grads()
+            cos, rel, _, _ = grad_metrics(g, ref_g, case.layout)
+            assert cos >= COS_MIN and rel <= GLOBAL_REL, (cos, rel)
+        assert case.ctx.optimizer(lr=1e-4, step=step, weight_decay=0.01, clip=1.0) == 0
+        O.lib().ora_adamw(p.size, p, m, v, ref_g.astype(np.float32), mask, 1, step, 1e-4, 0.9, 0.999, 1e-8,
+                          0.01, 1.0)

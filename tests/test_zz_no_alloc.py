@@ -88,3 +88,36 @@ def test_noalloc_rejects_problems_beyond_the_fixed_scratch():
         A.attention_bwd_noalloc(p, p, p, p, p, p, p, p, p, clips=64, T=3000, Tk=3000, H=24)
     assert err.value.code == A.ACT_ERR_INVALID
     assert "fixed maximum" in str(err.value)
+
+
+def test_noalloc_rejects_misaligned_pointers():
+    buf = torch.zeros(4096, dtype=torch.int16, device="cuda")  # never touched: rejected before launch
+    p = buf.data_ptr()
+    with pytest.raises(A.ActError) as err:
+        A.attention_bwd_noalloc(p + 2, p, p, p, p, p, p, p, p, clips=1, T=64, Tk=64, H=1)
+    assert err.value.code == A.ACT_ERR_INVALID
+    assert "aligned" in str(err.value)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs in one process")
+def test_noalloc_on_a_second_device_in_the_same_process():
+    # the scratch address and the kernels' shared-memory limits are set up per device
+    c = dict(clips=2, T=150, Tk=150, H=2)
+    rng = np.random.default_rng(7)
+    D = c["H"] * 64
+    q, k, v, do = (_bits(rng.standard_normal((c["clips"] * c["T"], D))) for _ in range(4))
+    tab = _rope(c["T"])
+    ref = A.attention(q, k, v, do, c["clips"], c["T"], c["Tk"], c["H"], None, False, True, tab, device=0)
+    for dev in (0, 1):
+        with torch.cuda.device(dev):
+            ins = [_dev(a) for a in (q, k, v, ref["o"], ref["lse"], do)]
+            rp = _dev(tab)
+            outs = [torch.zeros(a.shape, dtype=torch.int16, device="cuda") for a in (q, k, v)]
+            A.attention_bwd_noalloc(*[t.data_ptr() for t in ins], *[t.data_ptr() for t in outs], c["clips"], c["T"],
+                                    c["Tk"], c["H"], 0, False, True, rp.data_ptr(),
+                                    torch.cuda.current_stream().cuda_stream)
+            torch.cuda.synchronize()
+            for name, got in zip(("dq", "dk", "dv"), outs):
+                want = _f32(ref[name])
+                rel = np.linalg.norm(_f32(got.cpu().numpy()) - want) / np.linalg.norm(want)
+                assert rel <= REL_TOL, (dev, name, rel)
