@@ -101,14 +101,14 @@ SIGNATURES = {
                                 C.c_void_p, C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_float)]),
     "act_attention_bwd_noalloc": (C.c_int, [C.c_void_p] * 6 + [C.c_void_p] * 3 + [C.c_int] * 4 +
                                   [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
-    "act_gemm_bf16": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+    "act_gemm_f16": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                 C.c_int, C.c_int, C.POINTER(C.c_float)]),
-    "act_gelu_bf16": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int]),
+    "act_gelu_f16": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int]),
     "act_path_counts": (C.c_int, [C.c_void_p, C.POINTER(C.c_int64), C.c_int]),
     "act_wait_probe": (C.c_int, [C.c_void_p, C.c_int64]),
     "act_mg_staged": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t]),
     "act_q8_0_dequant": (C.c_int, [C.c_int, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]),
-    "act_rank_gemm_bf16": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
+    "act_rank_gemm_f16": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                      C.c_int, C.c_int, C.c_float, C.c_int, C.c_int, C.POINTER(C.c_float)]),
 }
 
@@ -307,34 +307,35 @@ class Context:
         return ids, tgt
 
 
-def gemm_bf16(A_bits: np.ndarray, B_bits: np.ndarray, M: int, N: int, K: int, b_mn_major: bool, path: int = 0,
+def gemm_f16(A_bits: np.ndarray, B_bits: np.ndarray, M: int, N: int, K: int, b_mn_major: bool, path: int = 0,
               device: int = 0, reps: int = 0):
-    """C = A . B(n,k) on the device; A_bits/B_bits are bf16 bit patterns (uint16).  With reps > 0
+    """C = A . B(n,k) on the device; A_bits/B_bits are f16 bit patterns (uint16).  With reps > 0
     returns (C, mean ms per call)."""
     C_ = np.zeros((M, N), np.float32)
     a = np.ascontiguousarray(A_bits, np.uint16)
     b = np.ascontiguousarray(B_bits, np.uint16)
     ms = C.c_float(0.0)
-    rc = lib().act_gemm_bf16(device, a.ctypes.data, b.ctypes.data, C_.ctypes.data, M, N, K, int(b_mn_major), path,
+    rc = lib().act_gemm_f16(device, a.ctypes.data, b.ctypes.data, C_.ctypes.data, M, N, K, int(b_mn_major), path,
                              reps, C.byref(ms))
     if rc != ACT_OK:
         raise ActError(rc, lib().act_last_error(None).decode())
     return (C_, ms.value) if reps > 0 else C_
 
 
-def gelu_bf16(z_bits: np.ndarray, direct: bool, device: int = 0):
-    """act_gelu_bf16: (gelu bits, gelu' bits) of bf16 inputs, by the A&S evaluation or the table."""
+def gelu_f16(z_bits: np.ndarray, direct: bool, device: int = 0):
+    """act_gelu_f16: (gelu bits, gelu' bits) of f16 inputs, element by element (direct) or by the
+    training step's vectorised pass."""
     z = np.ascontiguousarray(z_bits, np.uint16)
     g = np.zeros_like(z)
     dg = np.zeros_like(z)
-    rc = lib().act_gelu_bf16(device, z.ctypes.data, g.ctypes.data, dg.ctypes.data, z.size, int(direct))
+    rc = lib().act_gelu_f16(device, z.ctypes.data, g.ctypes.data, dg.ctypes.data, z.size, int(direct))
     if rc != ACT_OK:
         raise ActError(rc, lib().act_last_error(None).decode())
     return g, dg
 
 
 def q8_0_dequant(blocks: np.ndarray, device: int = 0):
-    """act_q8_0_dequant: (fp32 d*q, its bf16 bit patterns) of Q8_0 blocks ([nblocks][34] bytes)."""
+    """act_q8_0_dequant: (fp32 d*q, its f16 bit patterns) of Q8_0 blocks ([nblocks][34] bytes)."""
     b = np.ascontiguousarray(blocks, np.uint8).reshape(-1)
     nb = b.size // 34
     f = np.zeros(nb * 32, np.float32)
@@ -348,19 +349,19 @@ def q8_0_dequant(blocks: np.ndarray, device: int = 0):
 RANK_ACC, RANK_ACC_T, RANK_STORE = 0, 1, 2
 
 
-def rank_gemm_bf16(A_bits: np.ndarray, B_bits: np.ndarray, M: int, K: int, nb: int, a_mn: bool, b_mn: bool,
+def rank_gemm_f16(A_bits: np.ndarray, B_bits: np.ndarray, M: int, K: int, nb: int, a_mn: bool, b_mn: bool,
                    kind: int, alpha: float = 1.0, C_init: np.ndarray | None = None, splits: int = 0, device: int = 0,
                    reps: int = 0):
-    """Rank-block product C = alpha A(M x K) B(K x nb) (act_rank_gemm_bf16).  A_bits is [M][K]
+    """Rank-block product C = alpha A(M x K) B(K x nb) (act_rank_gemm_f16).  A_bits is [M][K]
     (a_mn False) or [K][M]; B_bits is [nb][K] (b_mn False) or [K][nb].  kind RANK_ACC returns
-    C_init + C ([M][nb]), RANK_ACC_T returns C_init + C^T ([nb][M]), RANK_STORE returns bf16(C).
+    C_init + C ([M][nb]), RANK_ACC_T returns C_init + C^T ([nb][M]), RANK_STORE returns f16(C).
     With reps > 0 returns (C, mean ms per call)."""
     shape = (nb, M) if kind == RANK_ACC_T else (M, nb)
     C_ = np.zeros(shape, np.float32) if C_init is None else np.ascontiguousarray(C_init, np.float32).copy()
     a = np.ascontiguousarray(A_bits, np.uint16)
     b = np.ascontiguousarray(B_bits, np.uint16)
     ms = C.c_float(0.0)
-    rc = lib().act_rank_gemm_bf16(device, kind, a.ctypes.data, b.ctypes.data, C_.ctypes.data, M, K, nb, int(a_mn),
+    rc = lib().act_rank_gemm_f16(device, kind, a.ctypes.data, b.ctypes.data, C_.ctypes.data, M, K, nb, int(a_mn),
                                   int(b_mn), float(alpha), splits, reps, C.byref(ms))
     if rc != ACT_OK:
         raise ActError(rc, lib().act_last_error(None).decode())
@@ -368,7 +369,7 @@ def rank_gemm_bf16(A_bits: np.ndarray, B_bits: np.ndarray, M: int, K: int, nb: i
 
 
 def attention(q, k, v, dout, clips, T, Tk, H, nvalid=None, causal=False, zero_key=False, rope=None, device=0):
-    """Kernel-level attention: bf16 bit-pattern inputs (uint16) -> dict of outputs and device times."""
+    """Kernel-level attention: f16 bit-pattern inputs (uint16) -> dict of outputs and device times."""
     D = H * 64
     o = np.zeros((clips * T, D), np.uint16)
     lse = np.zeros((clips, H, T), np.float32)

@@ -30,8 +30,8 @@ constexpr int BKV = 64;
 constexpr int LDS = HD + 8;
 constexpr float LOG2E = 1.4426950408889634f;
 
-// Synchronous staging of a [64 rows][64] bf16 tile, rotating pairs when rope != nullptr.
-__device__ __forceinline__ void stage_tile_sync(bf16* sm, const bf16* g, long ld, int nrows, int pos0,
+// Synchronous staging of a [64 rows][64] f16 tile, rotating pairs when rope != nullptr.
+__device__ __forceinline__ void stage_tile_sync(f16* sm, const f16* g, long ld, int nrows, int pos0,
                                                 const float* rope, int tid, int nthreads) {
     for (int c = tid; c < 64 * 8; c += nthreads) {
         const int r = c >> 3, ch = c & 7;
@@ -43,10 +43,10 @@ __device__ __forceinline__ void stage_tile_sync(bf16* sm, const bf16* g, long ld
                 uint32_t* w = reinterpret_cast<uint32_t*>(&v);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    __nv_bfloat162 b2 = *reinterpret_cast<__nv_bfloat162*>(&w[j]);
-                    const float x0 = __low2float(b2), x1 = __high2float(b2);
+                    const float2 xx = unpack_f16(w[j]);
+                    const float x0 = xx.x, x1 = xx.y;
                     const float2 t = cs[j];
-                    w[j] = pack_bf16(x0 * t.x - x1 * t.y, x0 * t.y + x1 * t.x);
+                    w[j] = pack_f16(x0 * t.x - x1 * t.y, x0 * t.y + x1 * t.x);
                 }
             }
         }
@@ -54,8 +54,8 @@ __device__ __forceinline__ void stage_tile_sync(bf16* sm, const bf16* g, long ld
     }
 }
 
-// Asynchronous staging of a [64 rows][64] bf16 tile (rows >= nrows zero-filled).
-__device__ __forceinline__ void stage_tile_async(bf16* sm, const bf16* g, long ld, int nrows, int tid, int nthreads) {
+// Asynchronous staging of a [64 rows][64] f16 tile (rows >= nrows zero-filled).
+__device__ __forceinline__ void stage_tile_async(f16* sm, const f16* g, long ld, int nrows, int tid, int nthreads) {
     for (int c = tid; c < 64 * 8; c += nthreads) {
         const int r = c >> 3, ch = c & 7;
         const bool ok = r < nrows;
@@ -64,7 +64,7 @@ __device__ __forceinline__ void stage_tile_async(bf16* sm, const bf16* g, long l
 }
 
 template <bool ROPE_LOAD>
-__device__ __forceinline__ void stage_tile(bf16* sm, const bf16* g, long ld, int nrows, int pos0, const float* rope,
+__device__ __forceinline__ void stage_tile(f16* sm, const f16* g, long ld, int nrows, int pos0, const float* rope,
                                            int tid, int nthreads) {
     if (ROPE_LOAD) stage_tile_sync(sm, g, ld, nrows, pos0, rope, tid, nthreads);
     else stage_tile_async(sm, g, ld, nrows, tid, nthreads);
@@ -82,9 +82,9 @@ __global__ void __launch_bounds__(FWD_WARPS * 32) attn_fwd_kernel(const AttnArgs
     pdl_wait();
     pdl_trigger();
     extern __shared__ __align__(16) unsigned char smraw[];
-    bf16* sQ = reinterpret_cast<bf16*>(smraw);
-    bf16* sK = sQ + FWD_BQ * LDS;  // [2][64][LDS]
-    bf16* sV = sK + 2 * BKV * LDS;  // [2][64][LDS]
+    f16* sQ = reinterpret_cast<f16*>(smraw);
+    f16* sK = sQ + FWD_BQ * LDS;  // [2][64][LDS]
+    f16* sV = sK + 2 * BKV * LDS;  // [2][64][LDS]
     constexpr int NT = FWD_WARPS * 32;
     const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(FWD_WARPS * 32) attn_fwd_kernel(const AttnArgs
     if (a.causal) kv_end = min(kv_end, q0 + FWD_BQ);
     const float* rope_load = ROPE_LOAD ? a.rope : nullptr;
 
-    const bf16* qg = a.q + ((long)b * a.T + q0) * a.ldq + h * HD;
+    const f16* qg = a.q + ((long)b * a.T + q0) * a.ldq + h * HD;
     stage_tile<ROPE_LOAD>(sQ, qg, a.ldq, nq, q0, rope_load, tid, NT);
     stage_tile<ROPE_LOAD>(sQ + 64 * LDS, qg + 64 * a.ldq, a.ldq, nq - 64, q0 + 64, rope_load, tid, NT);
     const int nkb = (kv_end + BKV - 1) / BKV;
@@ -133,8 +133,8 @@ __global__ void __launch_bounds__(FWD_WARPS * 32) attn_fwd_kernel(const AttnArgs
                 ldsm_x4(qf[kc][0], qf[kc][1], qf[kc][2], qf[kc][3],
                         sQ + (warp * 16 + lr + 8 * (lsel & 1)) * LDS + kc * 16 + 8 * (lsel >> 1));
         }
-        const bf16* cK = sK + buf * BKV * LDS;
-        const bf16* cV = sV + buf * BKV * LDS;
+        const f16* cK = sK + buf * BKV * LDS;
+        const f16* cV = sV + buf * BKV * LDS;
         const int k0 = kb * BKV;
         const int nvk = kv_end - k0;  // keys of this block in range (>= 1): groups of 16 past them are skipped
         float s[8][4];
@@ -149,8 +149,8 @@ __global__ void __launch_bounds__(FWD_WARPS * 32) attn_fwd_kernel(const AttnArgs
                 if (nj * 16 >= nvk) continue;  // masked below
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4(b0, b1, b2, b3, cK + (nj * 16 + lr + 8 * (lsel >> 1)) * LDS + kc * 16 + 8 * (lsel & 1));
-                mma_bf16(s[2 * nj], qf[kc], b0, b1);
-                mma_bf16(s[2 * nj + 1], qf[kc], b2, b3);
+                mma_sync_f16(s[2 * nj], qf[kc], b0, b1);
+                mma_sync_f16(s[2 * nj + 1], qf[kc], b2, b3);
             }
         float mx[2] = {-INFINITY, -INFINITY};
         const bool full = (k0 + BKV <= kv_end) && (!a.causal || k0 + BKV - 1 <= q0 + warp * 16);
@@ -202,16 +202,16 @@ __global__ void __launch_bounds__(FWD_WARPS * 32) attn_fwd_kernel(const AttnArgs
         for (int kc = 0; kc < 4; ++kc) {
             if (kc * 16 >= nvk) continue;  // these probabilities are zero
             uint32_t pa[4];
-            pa[0] = pack_bf16(s[2 * kc][0], s[2 * kc][1]);
-            pa[1] = pack_bf16(s[2 * kc][2], s[2 * kc][3]);
-            pa[2] = pack_bf16(s[2 * kc + 1][0], s[2 * kc + 1][1]);
-            pa[3] = pack_bf16(s[2 * kc + 1][2], s[2 * kc + 1][3]);
+            pa[0] = pack_f16(s[2 * kc][0], s[2 * kc][1]);
+            pa[1] = pack_f16(s[2 * kc][2], s[2 * kc][3]);
+            pa[2] = pack_f16(s[2 * kc + 1][0], s[2 * kc + 1][1]);
+            pa[3] = pack_f16(s[2 * kc + 1][2], s[2 * kc + 1][3]);
 #pragma unroll
             for (int nj = 0; nj < 4; ++nj) {
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4_t(b0, b1, b2, b3, cV + (kc * 16 + lr + 8 * (lsel & 1)) * LDS + nj * 16 + 8 * (lsel >> 1));
-                mma_bf16(o[2 * nj], pa, b0, b1);
-                mma_bf16(o[2 * nj + 1], pa, b2, b3);
+                mma_sync_f16(o[2 * nj], pa, b0, b1);
+                mma_sync_f16(o[2 * nj + 1], pa, b2, b3);
             }
         }
         __syncthreads();  // this buffer is refilled by the prefetch of iteration kb + 2
@@ -225,11 +225,11 @@ __global__ void __launch_bounds__(FWD_WARPS * 32) attn_fwd_kernel(const AttnArgs
         const int i = q0 + warp * 16 + g + 8 * hh;
         if (i >= a.T) continue;
         const float inv = lrow[hh] > 0.f ? 1.f / lrow[hh] : 0.f;
-        bf16* orow = a.o + ((long)b * a.T + i) * a.ldo + h * HD;
+        f16* orow = a.o + ((long)b * a.T + i) * a.ldo + h * HD;
 #pragma unroll
         for (int ni = 0; ni < 8; ++ni)
             *reinterpret_cast<uint32_t*>(orow + ni * 8 + 2 * q) =
-                pack_bf16(o[ni][2 * hh] * inv, o[ni][2 * hh + 1] * inv);
+                pack_f16(o[ni][2 * hh] * inv, o[ni][2 * hh + 1] * inv);
         if (q == 0) {
             const float mfin = mrow[hh] == -INFINITY ? 0.f : mrow[hh];
             a.lse[((long)b * a.H + h) * a.T + i] = mfin + log2f(lrow[hh]);
@@ -255,9 +255,8 @@ __global__ void attn_dvec_kernel(const AttnArgs a) {
         const uint32_t ow[4] = {oo.x, oo.y, oo.z, oo.w}, dw[4] = {dd.x, dd.y, dd.z, dd.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const __nv_bfloat162 o2 = *reinterpret_cast<const __nv_bfloat162*>(&ow[j]);
-            const __nv_bfloat162 d2 = *reinterpret_cast<const __nv_bfloat162*>(&dw[j]);
-            v += __low2float(o2) * __low2float(d2) + __high2float(o2) * __high2float(d2);
+            const float2 o2 = unpack_f16(ow[j]), d2 = unpack_f16(dw[j]);
+            v += o2.x * d2.x + o2.y * d2.y;
         }
     }
     v += __shfl_xor_sync(0xffffffffu, v, 1);
@@ -280,11 +279,11 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
     pdl_wait();
     pdl_trigger();
     extern __shared__ __align__(16) unsigned char smraw[];
-    bf16* sK = reinterpret_cast<bf16*>(smraw);
-    bf16* sV = sK + BKV * LDS;
-    bf16* sQ = sV + BKV * LDS;          // [2][64][LDS]
-    bf16* sdO = sQ + 2 * BWD_BQ * LDS;  // [2][64][LDS]
-    bf16* sdS = sdO + 2 * BWD_BQ * LDS; // [64 keys][LDS]  dS^T
+    f16* sK = reinterpret_cast<f16*>(smraw);
+    f16* sV = sK + BKV * LDS;
+    f16* sQ = sV + BKV * LDS;          // [2][64][LDS]
+    f16* sdO = sQ + 2 * BWD_BQ * LDS;  // [2][64][LDS]
+    f16* sdS = sdO + 2 * BWD_BQ * LDS; // [64 keys][LDS]  dS^T
     float* sL = reinterpret_cast<float*>(sdS + BKV * LDS);  // [2][64] lse
     float* sD = sL + 2 * BWD_BQ;                             // [2][64] rowsum(dO*O)
     const int kb = blockIdx.x / a.qsplit, part = blockIdx.x % a.qsplit, h = blockIdx.y, b = blockIdx.z;
@@ -303,7 +302,7 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
     const int nqb = (a.T + BWD_BQ - 1) / BWD_BQ;
     // without keys in range the CTA has nothing to add, except when it writes dQ directly: then
     // its query blocks still run (every score masked, dQ exactly zero) so that their rows are written
-    const int qb_all = (nk > 0 || a.dq_bf) ? qb0 : nqb;
+    const int qb_all = (nk > 0 || a.dq_h) ? qb0 : nqb;
     // this CTA's share of the key block's query blocks
     const int qb_first = qb_all + (int)((long)(nqb - qb_all) * part / a.qsplit);
     const int qb_end = qb_all + (int)((long)(nqb - qb_all) * (part + 1) / a.qsplit);
@@ -348,8 +347,8 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
         cp_async_wait<1>();
         __syncthreads();
         const int q0 = qb * BWD_BQ;
-        const bf16* cQ = sQ + buf * BWD_BQ * LDS;
-        const bf16* cdO = sdO + buf * BWD_BQ * LDS;
+        const f16* cQ = sQ + buf * BWD_BQ * LDS;
+        const f16* cdO = sdO + buf * BWD_BQ * LDS;
         const float* cL = sL + buf * BWD_BQ;
         const float* cD = sD + buf * BWD_BQ;
         // S^T = K Q^T and dP^T = V dO^T for this warp's 16 keys x 64 queries
@@ -368,11 +367,11 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
             for (int nj = 0; nj < 4; ++nj) {
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4(b0, b1, b2, b3, cQ + (nj * 16 + lr + 8 * (lsel >> 1)) * LDS + kc * 16 + 8 * (lsel & 1));
-                mma_bf16(s[2 * nj], ka, b0, b1);
-                mma_bf16(s[2 * nj + 1], ka, b2, b3);
+                mma_sync_f16(s[2 * nj], ka, b0, b1);
+                mma_sync_f16(s[2 * nj + 1], ka, b2, b3);
                 ldsm_x4(b0, b1, b2, b3, cdO + (nj * 16 + lr + 8 * (lsel >> 1)) * LDS + kc * 16 + 8 * (lsel & 1));
-                mma_bf16(dp[2 * nj], va, b0, b1);
-                mma_bf16(dp[2 * nj + 1], va, b2, b3);
+                mma_sync_f16(dp[2 * nj], va, b0, b1);
+                mma_sync_f16(dp[2 * nj + 1], va, b2, b3);
             }
         }
         const bool full = (q0 + BWD_BQ <= a.T) && (k0 + BKV <= kv_end) && (!a.causal || k0 + BKV - 1 <= q0);
@@ -397,23 +396,23 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
         for (int kc = 0; kc < 4; ++kc) {
             if (!live) break;
             uint32_t pa[4], sa[4];
-            pa[0] = pack_bf16(s[2 * kc][0], s[2 * kc][1]);
-            pa[1] = pack_bf16(s[2 * kc][2], s[2 * kc][3]);
-            pa[2] = pack_bf16(s[2 * kc + 1][0], s[2 * kc + 1][1]);
-            pa[3] = pack_bf16(s[2 * kc + 1][2], s[2 * kc + 1][3]);
-            sa[0] = pack_bf16(dp[2 * kc][0], dp[2 * kc][1]);
-            sa[1] = pack_bf16(dp[2 * kc][2], dp[2 * kc][3]);
-            sa[2] = pack_bf16(dp[2 * kc + 1][0], dp[2 * kc + 1][1]);
-            sa[3] = pack_bf16(dp[2 * kc + 1][2], dp[2 * kc + 1][3]);
+            pa[0] = pack_f16(s[2 * kc][0], s[2 * kc][1]);
+            pa[1] = pack_f16(s[2 * kc][2], s[2 * kc][3]);
+            pa[2] = pack_f16(s[2 * kc + 1][0], s[2 * kc + 1][1]);
+            pa[3] = pack_f16(s[2 * kc + 1][2], s[2 * kc + 1][3]);
+            sa[0] = pack_f16(dp[2 * kc][0], dp[2 * kc][1]);
+            sa[1] = pack_f16(dp[2 * kc][2], dp[2 * kc][3]);
+            sa[2] = pack_f16(dp[2 * kc + 1][0], dp[2 * kc + 1][1]);
+            sa[3] = pack_f16(dp[2 * kc + 1][2], dp[2 * kc + 1][3]);
 #pragma unroll
             for (int nj = 0; nj < 4; ++nj) {
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4_t(b0, b1, b2, b3, cdO + (kc * 16 + lr + 8 * (lsel & 1)) * LDS + nj * 16 + 8 * (lsel >> 1));
-                mma_bf16(dv[2 * nj], pa, b0, b1);
-                mma_bf16(dv[2 * nj + 1], pa, b2, b3);
+                mma_sync_f16(dv[2 * nj], pa, b0, b1);
+                mma_sync_f16(dv[2 * nj + 1], pa, b2, b3);
                 ldsm_x4_t(b0, b1, b2, b3, cQ + (kc * 16 + lr + 8 * (lsel & 1)) * LDS + nj * 16 + 8 * (lsel >> 1));
-                mma_bf16(dk[2 * nj], sa, b0, b1);
-                mma_bf16(dk[2 * nj + 1], sa, b2, b3);
+                mma_sync_f16(dk[2 * nj], sa, b0, b1);
+                mma_sync_f16(dk[2 * nj + 1], sa, b2, b3);
             }
             // dS^T rows of this warp to shared memory for dQ
 #pragma unroll
@@ -439,8 +438,8 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
                 for (int nj = 0; nj < 4; ++nj) {
                     uint32_t b0, b1, b2, b3;
                     ldsm_x4_t(b0, b1, b2, b3, sK + (kc * 16 + lr + 8 * (lsel & 1)) * LDS + nj * 16 + 8 * (lsel >> 1));
-                    mma_bf16(dq[2 * nj], da, b0, b1);
-                    mma_bf16(dq[2 * nj + 1], da, b2, b3);
+                    mma_sync_f16(dq[2 * nj], da, b0, b1);
+                    mma_sync_f16(dq[2 * nj + 1], da, b2, b3);
                 }
             }
 #pragma unroll
@@ -449,8 +448,8 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
                 if (i >= a.T) continue;
                 float* dst = a.dq_acc + ((long)b * a.T + i) * a.ldq_acc + h * HD;
                 // with a single key block this CTA is the only contributor to these rows
-                if (a.dq_bf) {
-                    bf16* db = a.dq_bf + ((long)b * a.T + i) * a.lddq_bf + h * HD;
+                if (a.dq_h) {
+                    f16* db = a.dq_h + ((long)b * a.T + i) * a.lddq_h + h * HD;
 #pragma unroll
                     for (int ni = 0; ni < 8; ++ni) {
                         const int c = ni * 8 + 2 * q;
@@ -459,7 +458,7 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
                             x0 *= a.dq_scale[h * HD + c];
                             x1 *= a.dq_scale[h * HD + c + 1];
                         }
-                        *reinterpret_cast<uint32_t*>(db + c) = pack_bf16(x0, x1);
+                        *reinterpret_cast<uint32_t*>(db + c) = pack_f16(x0, x1);
                     }
                 } else if (a.Tk <= BKV) {
 #pragma unroll
@@ -484,8 +483,8 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
         const int jl = warp * 16 + g + 8 * hh;
         const int j = k0 + jl;
         if (j >= a.Tk) continue;
-        bf16* dkr = a.dk + ((long)b * a.Tk + j) * a.lddk + h * HD;
-        bf16* dvr = a.dv + ((long)b * a.Tk + j) * a.lddv + h * HD;
+        f16* dkr = a.dk + ((long)b * a.Tk + j) * a.lddk + h * HD;
+        f16* dvr = a.dv + ((long)b * a.Tk + j) * a.lddv + h * HD;
 #pragma unroll
         for (int ni = 0; ni < 8; ++ni) {
             const int c = ni * 8 + 2 * q;
@@ -512,14 +511,14 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
                     atomicAdd(reinterpret_cast<float2*>(a.dv_acc + r), make_float2(v0, v1));
                 }
             } else {
-                *reinterpret_cast<uint32_t*>(dkr + c) = pack_bf16(x0, x1);
-                *reinterpret_cast<uint32_t*>(dvr + c) = pack_bf16(v0, v1);
+                *reinterpret_cast<uint32_t*>(dkr + c) = pack_f16(x0, x1);
+                *reinterpret_cast<uint32_t*>(dvr + c) = pack_f16(v0, v1);
             }
         }
     }
 }
 
-// dk / dv (bf16) from the fp32 accumulators of a query-split backward: 4 floats per thread
+// dk / dv (f16) from the fp32 accumulators of a query-split backward: 4 floats per thread
 __global__ void attn_dkv_finish_kernel(const AttnArgs a) {
     pdl_wait();
     pdl_trigger();
@@ -530,12 +529,12 @@ __global__ void attn_dkv_finish_kernel(const AttnArgs a) {
     const int c = (int)(idx % quads) * 4;
     const float4 k = *reinterpret_cast<const float4*>(a.dk_acc + row * a.H * HD + c);
     const float4 v = *reinterpret_cast<const float4*>(a.dv_acc + row * a.H * HD + c);
-    *reinterpret_cast<uint2*>(a.dk + row * a.lddk + c) = make_uint2(pack_bf16(k.x, k.y), pack_bf16(k.z, k.w));
-    *reinterpret_cast<uint2*>(a.dv + row * a.lddv + c) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
+    *reinterpret_cast<uint2*>(a.dk + row * a.lddk + c) = make_uint2(pack_f16(k.x, k.y), pack_f16(k.z, k.w));
+    *reinterpret_cast<uint2*>(a.dv + row * a.lddv + c) = make_uint2(pack_f16(v.x, v.y), pack_f16(v.z, v.w));
 }
 
-// dq (bf16) = unrotate(dq_acc) * qscale : 4 floats per thread
-__global__ void attn_dq_finish_kernel(const AttnArgs a, bf16* dq, long lddq, const float* qscale) {
+// dq (f16) = unrotate(dq_acc) * qscale : 4 floats per thread
+__global__ void attn_dq_finish_kernel(const AttnArgs a, f16* dq, long lddq, const float* qscale) {
     pdl_wait();
     pdl_trigger();
     const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -559,7 +558,7 @@ __global__ void attn_dq_finish_kernel(const AttnArgs a, bf16* dq, long lddq, con
     if (qscale)
 #pragma unroll
         for (int j = 0; j < 4; ++j) x[j] *= qscale[c + j];
-    *reinterpret_cast<uint2*>(dq + row * lddq + c) = make_uint2(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]));
+    *reinterpret_cast<uint2*>(dq + row * lddq + c) = make_uint2(pack_f16(x[0], x[1]), pack_f16(x[2], x[3]));
 }
 
 template <class K>
@@ -594,8 +593,8 @@ void attn_bwd(const AttnArgs& a, cudaStream_t s) {
     });
     if (a.qsplit < 1 || (a.qsplit > 1 && a.dk && (!a.dk_acc || !a.dv_acc)))
         throw std::runtime_error("attn_bwd: query split with dK / dV needs dk_acc / dv_acc");
-    if (a.dq_bf && (a.Tk > BKV || a.rope || a.lddq_bf % 2 || (reinterpret_cast<uintptr_t>(a.dq_bf) & 3)))
-        throw std::runtime_error("attn_bwd: direct bf16 dQ needs a single key block and no RoPE");
+    if (a.dq_h && (a.Tk > BKV || a.rope || a.lddq_h % 2 || (reinterpret_cast<uintptr_t>(a.dq_h) & 3)))
+        throw std::runtime_error("attn_bwd: direct f16 dQ needs a single key block and no RoPE");
     dim3 grid((unsigned)(((a.Tk + BKV - 1) / BKV) * a.qsplit), a.H, a.clips);
     if (a.rope && a.rope_load) launch_pdl(attn_bwd_kernel<true>, grid, dim3(128), BWD_SMEM, s, a);
     else launch_pdl(attn_bwd_kernel<false>, grid, dim3(128), BWD_SMEM, s, a);
@@ -606,7 +605,7 @@ void attn_dkv_finish(const AttnArgs& a, cudaStream_t s) {
     launch_pdl(attn_dkv_finish_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, a);
 }
 
-void attn_dq_finish(const AttnArgs& a, bf16* dq, long lddq, const float* qscale, cudaStream_t s) {
+void attn_dq_finish(const AttnArgs& a, f16* dq, long lddq, const float* qscale, cudaStream_t s) {
     const long n = (long)a.clips * a.T * a.H * HD / 4;
     launch_pdl(attn_dq_finish_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, a, dq, lddq, qscale);
 }

@@ -42,7 +42,7 @@ int attention_bwd_noalloc(const void* q, const void* k, const void* v, const voi
         return fail(ACT_ERR_INVALID, "act_attention_bwd_noalloc: sizes must be positive");
     if (causal && Tk != T) return fail(ACT_ERR_INVALID, "act_attention_bwd_noalloc: causal attention needs Tk == T");
     if (rope && Tk > T) return fail(ACT_ERR_INVALID, "act_attention_bwd_noalloc: RoPE needs Tk <= T");
-    // The kernels move the bf16 tensors in 16-byte vectors, the RoPE table in (cos, sin) float
+    // The kernels move the f16 tensors in 16-byte vectors, the RoPE table in (cos, sin) float
     // pairs and lse / nvalid as 4-byte words: a misaligned pointer would fault on the device, so
     // it is rejected here, before anything is queued.
     for (const void* p : {q, k, v, o, dout, static_cast<const void*>(dq), static_cast<const void*>(dk),
@@ -84,9 +84,9 @@ int attention_bwd_noalloc(const void* q, const void* k, const void* v, const voi
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     act::AttnArgs a;
-    a.q = static_cast<const bf16*>(q);
-    a.k = static_cast<const bf16*>(k);
-    a.v = static_cast<const bf16*>(v);
+    a.q = static_cast<const f16*>(q);
+    a.k = static_cast<const f16*>(k);
+    a.v = static_cast<const f16*>(v);
     a.ldq = a.ldk = a.ldv = D;
     a.T = T; a.Tk = Tk; a.H = H; a.clips = clips;
     a.nvalid = nvalid;
@@ -95,21 +95,21 @@ int attention_bwd_noalloc(const void* q, const void* k, const void* v, const voi
     a.rope = rope;
     a.rope_load = 1;
     a.scale = 0.125f;
-    a.o = const_cast<bf16*>(static_cast<const bf16*>(o));
+    a.o = const_cast<f16*>(static_cast<const f16*>(o));
     a.ldo = D;
     a.lse = const_cast<float*>(lse);
-    a.dout = static_cast<const bf16*>(dout);
+    a.dout = static_cast<const f16*>(dout);
     a.lddo = D;
     a.dq_acc = scratch;                 // accumulated with atomics: must start at zero every call
     a.ldq_acc = D;
     a.dvec = scratch + acc_floats;      // fully overwritten every call
-    a.dk = static_cast<bf16*>(dk);
-    a.dv = static_cast<bf16*>(dv);
+    a.dk = static_cast<f16*>(dk);
+    a.dv = static_cast<f16*>(dv);
     a.lddk = a.lddv = D;
     e = cudaMemsetAsync(a.dq_acc, 0, sizeof(float) * acc_floats, st);
     if (e != cudaSuccess) return fail(ACT_ERR_CUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
     act::attn_bwd(a, st);
-    act::attn_dq_finish(a, static_cast<bf16*>(dq), D, nullptr, st);
+    act::attn_dq_finish(a, static_cast<f16*>(dq), D, nullptr, st);
     e = cudaGetLastError();
     if (e != cudaSuccess) return fail(ACT_ERR_CUDA, std::string("attention backward launch: ") + cudaGetErrorString(e));
     return ACT_OK;

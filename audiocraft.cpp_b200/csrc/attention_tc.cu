@@ -12,7 +12,7 @@
 //               masked)
 //   warp 1      MMA issuer (one thread): S = Q K^T (128 x 64, fp32, two TMEM buffers so the
 //               next block's scores are computed while this block's softmax runs), then
-//               O += P V (128 x 64, fp32 in TMEM) with P (bf16 pairs) read from TMEM
+//               O += P V (128 x 64, fp32 in TMEM) with P (f16 pairs) read from TMEM
 //   warps 2..5  softmax, one query row per thread: tcgen05.ld the row of S, online softmax in
 //               base 2 with a lazily updated running max (the max used for the exponentials is
 //               only raised when the block maximum exceeds it by more than 2^8, which bounds
@@ -29,7 +29,7 @@
 //         dQ accumulator with TMA bulk reduce-add tiles (out-of-range rows add exact zeros)
 // Warp roles: 0 TMA (K, V once; Q, dO per block into 3 stages), 1 MMA issue, 2..9 P / dS in two
 // groups of query columns and the final dK / dV epilogue (RoPE undone on dK, DoRA column
-// factors), 10..13 the dQ epilogue.  P^T goes to TMEM as bf16 pairs and is the A operand of the
+// factors), 10..13 the dQ epilogue.  P^T goes to TMEM as f16 pairs and is the A operand of the
 // dV MMAs straight from there (released right after them); dS^T is double-buffered in shared
 // memory; Q / dO have three stages, so the next-but-one block's tiles load while this one runs.
 // Every mbarrier wait is bounded (globaltimer) and reports into the shared error word.
@@ -51,7 +51,7 @@ using namespace tc;
 constexpr int AT_BQ = 128;      // queries per CTA
 constexpr int AT_BK = 64;       // keys per block
 constexpr int AT_HD = 64;
-constexpr int AT_QTILE = AT_BQ * AT_HD * 2;  // 16 KB: 128 rows x 64 bf16 (128-byte rows)
+constexpr int AT_QTILE = AT_BQ * AT_HD * 2;  // 16 KB: 128 rows x 64 f16 (128-byte rows)
 constexpr int AT_KTILE = AT_BK * AT_HD * 2;  //  8 KB
 constexpr int AT_STAGES = 4;
 constexpr int AT_Q_OFF = 0;
@@ -60,7 +60,7 @@ constexpr int AT_V_OFF = AT_K_OFF + AT_STAGES * AT_KTILE;    // [AT_STAGES] stag
 constexpr int AT_BAR_OFF = AT_V_OFF + AT_STAGES * AT_KTILE;
 constexpr int AT_SMEM = AT_BAR_OFF + 256 + 1024;
 constexpr int AT_THREADS = 6 * 32;
-constexpr uint32_t AT_TMEM_COLS = 256;       // S: columns 0..63 and 64..127, O: 128..191, P (bf16 pairs): 192..223
+constexpr uint32_t AT_TMEM_COLS = 256;       // S: columns 0..63 and 64..127, O: 128..191, P (f16 pairs): 192..223
 constexpr float AT_LOG2E = 1.4426950408889634f;
 constexpr float AT_RESCALE = 8.0f;           // lazy-max threshold (log2 units)
 
@@ -215,9 +215,9 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_fwd_tc_kernel(const __grid
         }
     } else if (warp == 1 && lane == 0) {
         // ------------------------------------------------------------ MMA issuer
-        constexpr uint32_t IDESC_S = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(AT_BK >> 3) << 17) |
+        constexpr uint32_t IDESC_S = IDESC_F16_F32ACC | ((uint32_t)(AT_BK >> 3) << 17) |
                                      ((uint32_t)(AT_BQ >> 4) << 24);
-        constexpr uint32_t IDESC_PV = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) |
+        constexpr uint32_t IDESC_PV = IDESC_F16_F32ACC | (1u << 16) |
                                       ((uint32_t)(AT_HD >> 3) << 17) | ((uint32_t)(AT_BQ >> 4) << 24);
         const uint64_t dq = smem_desc(base + AT_Q_OFF, 16, 1024);
         const uint64_t dk0 = smem_desc(base + AT_K_OFF, 16, 1024);
@@ -323,10 +323,10 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_fwd_tc_kernel(const __grid
                     tmem_wait_st();
                 }
             }
-            {  // P of this query row as bf16 pairs into TMEM, the A operand of O += P V
+            {  // P of this query row as f16 pairs into TMEM, the A operand of O += P V
                 uint32_t pk[AT_BK / 2];
 #pragma unroll
-                for (int c2 = 0; c2 < AT_BK / 2; ++c2) pk[c2] = pack_bf16(s[2 * c2], s[2 * c2 + 1]);
+                for (int c2 = 0; c2 < AT_BK / 2; ++c2) pk[c2] = pack_f16(s[2 * c2], s[2 * c2 + 1]);
                 tmem_st32(tP + lane_base, reinterpret_cast<const float*>(pk));
                 tmem_wait_st();
             }
@@ -342,7 +342,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_fwd_tc_kernel(const __grid
         }
         if (have_o) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        bf16* orow = a.o + ((long)b * a.T + min(i, a.T - 1)) * a.ldo + h * AT_HD;
+        f16* orow = a.o + ((long)b * a.T + min(i, a.T - 1)) * a.ldo + h * AT_HD;
 #pragma unroll 1
         for (int c = 0; c < AT_HD / 32; ++c) {
             float o[32];
@@ -357,8 +357,8 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_fwd_tc_kernel(const __grid
 #pragma unroll
                 for (int u = 0; u < 4; ++u)
                     *reinterpret_cast<uint4*>(orow + c * 32 + 8 * u) = make_uint4(
-                        pack_bf16(o[8 * u] * inv, o[8 * u + 1] * inv), pack_bf16(o[8 * u + 2] * inv, o[8 * u + 3] * inv),
-                        pack_bf16(o[8 * u + 4] * inv, o[8 * u + 5] * inv), pack_bf16(o[8 * u + 6] * inv, o[8 * u + 7] * inv));
+                        pack_f16(o[8 * u] * inv, o[8 * u + 1] * inv), pack_f16(o[8 * u + 2] * inv, o[8 * u + 3] * inv),
+                        pack_f16(o[8 * u + 4] * inv, o[8 * u + 5] * inv), pack_f16(o[8 * u + 6] * inv, o[8 * u + 7] * inv));
         }
         if (i < a.T) {
             const float mfin = m_run == -INFINITY ? 0.f : m_run;
@@ -376,7 +376,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_fwd_tc_kernel(const __grid
 // backward
 constexpr int AB_BK = 128;  // keys per CTA
 constexpr int AB_BQ = 128;  // queries per block
-constexpr int AB_T16 = 128 * 64 * 2;         // 16 KB: a 128 x 64 bf16 tile (128-byte rows)
+constexpr int AB_T16 = 128 * 64 * 2;         // 16 KB: a 128 x 64 f16 tile (128-byte rows)
 constexpr int AB_K_OFF = 0;
 constexpr int AB_V_OFF = AB_T16;
 constexpr int AB_QD_STAGES = 3;
@@ -387,7 +387,7 @@ constexpr int AB_LSE_OFF = 13 * AB_T16;      // [2] x { lse[128], D[128] } fp32
 constexpr int AB_BAR_OFF = AB_LSE_OFF + 2 * 256 * 4;
 constexpr int AB_SMEM = AB_BAR_OFF + 256 + 1024;
 constexpr int AB_THREADS = 14 * 32;
-// S^T 0..127, dP^T 128..255, dV 256..319, dK 320..383, dQ 384..447, P^T (bf16 pairs) 448..511
+// S^T 0..127, dP^T 128..255, dV 256..319, dK 320..383, dQ 384..447, P^T (f16 pairs) 448..511
 constexpr uint32_t AB_TMEM_COLS = 512;
 
 struct AbMaps {
@@ -474,9 +474,9 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
         }
     } else if (warp == 1 && lane == 0) {
         // ------------------------------------------------------------ MMA issuer
-        constexpr uint32_t ID_S = (1u << 4) | (1u << 7) | (1u << 10) | (16u << 17) | (8u << 24);  // 128x128, K/K
-        constexpr uint32_t ID_KV = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | (8u << 17) | (8u << 24);  // 128x64, K/MN
-        constexpr uint32_t ID_Q = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) | (8u << 17) |
+        constexpr uint32_t ID_S = IDESC_F16_F32ACC | (16u << 17) | (8u << 24);  // 128x128, K/K
+        constexpr uint32_t ID_KV = IDESC_F16_F32ACC | (1u << 16) | (8u << 17) | (8u << 24);  // 128x64, K/MN
+        constexpr uint32_t ID_Q = IDESC_F16_F32ACC | (1u << 15) | (1u << 16) | (8u << 17) |
                                   (8u << 24);  // 128x64, MN/MN
         const uint64_t dK_k = smem_desc(base + AB_K_OFF, 16, 1024), dV_k = smem_desc(base + AB_V_OFF, 16, 1024);
         const uint64_t dK_mn = smem_desc(base + AB_K_OFF, 8192, 1024);
@@ -625,18 +625,18 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
                     if (!ok) break;
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 }
-                {  // P^T of this key row, query columns qt*32 .. qt*32+31, as bf16 pairs into TMEM
+                {  // P^T of this key row, query columns qt*32 .. qt*32+31, as f16 pairs into TMEM
                     uint32_t pk[16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) pk[j] = pack_bf16(sv[2 * j], sv[2 * j + 1]);
+                    for (int j = 0; j < 16; ++j) pk[j] = pack_f16(sv[2 * j], sv[2 * j + 1]);
                     tmem_st16(tP + lb + qt * 16, pk);
                 }
 #pragma unroll
                 for (int un = 0; un < 4; ++un) {
                     const uint32_t off = (qt >> 1) * AB_T16 + at_sw128(kr, (qt & 1) * 4 + un);
                     *reinterpret_cast<uint4*>(dSt + (u & 1) * 2 * AB_T16 + off) =
-                        make_uint4(pack_bf16(dp[8 * un], dp[8 * un + 1]), pack_bf16(dp[8 * un + 2], dp[8 * un + 3]),
-                                   pack_bf16(dp[8 * un + 4], dp[8 * un + 5]), pack_bf16(dp[8 * un + 6], dp[8 * un + 7]));
+                        make_uint4(pack_f16(dp[8 * un], dp[8 * un + 1]), pack_f16(dp[8 * un + 2], dp[8 * un + 3]),
+                                   pack_f16(dp[8 * un + 4], dp[8 * un + 5]), pack_f16(dp[8 * un + 6], dp[8 * un + 7]));
                 }
             }
             if (!ok) continue;
@@ -654,8 +654,8 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
         }
         if (have) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int krow = min(key, a.Tk - 1);
-        bf16* dkr = a.dk + ((long)b * a.Tk + krow) * a.lddk + h * 64;
-        bf16* dvr = a.dv + ((long)b * a.Tk + krow) * a.lddv + h * 64;
+        f16* dkr = a.dk + ((long)b * a.Tk + krow) * a.lddk + h * 64;
+        f16* dvr = a.dv + ((long)b * a.Tk + krow) * a.lddv + h * 64;
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
             float x[32];
@@ -689,12 +689,12 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
 #pragma unroll
                     for (int e = 0; e < 32; ++e) x[e] *= a.vscale[h * 64 + c * 32 + e];
                 }
-                bf16* dst = (grp == 0 ? dkr : dvr) + c * 32;
+                f16* dst = (grp == 0 ? dkr : dvr) + c * 32;
 #pragma unroll
                 for (int un = 0; un < 4; ++un)
                     *reinterpret_cast<uint4*>(dst + 8 * un) =
-                        make_uint4(pack_bf16(x[8 * un], x[8 * un + 1]), pack_bf16(x[8 * un + 2], x[8 * un + 3]),
-                                   pack_bf16(x[8 * un + 4], x[8 * un + 5]), pack_bf16(x[8 * un + 6], x[8 * un + 7]));
+                        make_uint4(pack_f16(x[8 * un], x[8 * un + 1]), pack_f16(x[8 * un + 2], x[8 * un + 3]),
+                                   pack_f16(x[8 * un + 4], x[8 * un + 5]), pack_f16(x[8 * un + 6], x[8 * un + 7]));
             }
         }
     } else if (warp >= 10) {

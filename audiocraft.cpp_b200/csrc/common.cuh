@@ -1,13 +1,13 @@
 // common.cuh -- shared device helpers for the adapter-training kernels (sm_100a).
 #pragma once
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include <atomic>
 #include <mutex>
 
-typedef __nv_bfloat16 bf16;
+typedef __half f16;
 
 namespace act {
 
@@ -53,7 +53,7 @@ inline int current_sm_count() {
 // A&S 7.1.26 GELU and the derivative of that approximation (the reference trains through
 // the approximation, src/ac/lora.h:97-110, so its gradient is the one autodiff yields).
 // The reciprocal and exponential use the fast hardware approximations (relative error ~1e-6):
-// every caller rounds the result to bf16 (relative step 2^-8), and these run once per element
+// every caller rounds the result to f16 (relative step 2^-8), and these run once per element
 // of the widest GEMM epilogues.
 __device__ __forceinline__ float gelu_as(float x) {
     const float z = x * 0.7071067811865475f, a = fabsf(z);
@@ -98,40 +98,6 @@ __device__ __forceinline__ void gelu_as_pair(float x, float& g, float& dg) {
     dg = half_cdf + x * 0.5f * derf * 0.7071067811865475f;
 }
 
-// GELU of a bf16 pre-activation by table.  z takes finitely many values: for |z| in
-// [2^-16, 16) the table holds bf16(gelu_as(z)) | bf16(gelu_as_grad(z)) << 16 for every bf16 z
-// (20 exponents x 128 mantissas x 2 signs), computed with gelu_as_pair; below 2^-16 both round
-// to z / 2 and 0.5 exactly, and from 16 up the A&S exponential underflows, giving z and 1 (or
-// -0 and -0 for negative z).  Results equal the direct evaluation bit for bit.
-constexpr int GELU_TAB_E0 = 111;  // biased exponent of 2^-16
-constexpr int GELU_TAB_NE = 20;
-constexpr int GELU_TAB_ENTRIES = 2 * GELU_TAB_NE * 128;
-
-__device__ __forceinline__ uint32_t gelu_tab_entry(int i) {
-    const uint32_t neg = i / (GELU_TAB_NE * 128), r = i % (GELU_TAB_NE * 128);
-    const uint32_t bits = (neg << 15) | ((GELU_TAB_E0 + (r >> 7)) << 7) | (r & 127);
-    float g, dg;
-    gelu_as_pair(__uint_as_float(bits << 16), g, dg);
-    const __nv_bfloat162 v = __floats2bfloat162_rn(g, dg);
-    return *reinterpret_cast<const uint32_t*>(&v);
-}
-
-// u: bf16 bits of z -> bf16 bits of gelu(z) | bf16 bits of gelu'(z) << 16
-__device__ __forceinline__ uint32_t gelu_tab_lookup(const uint32_t* tab, uint32_t u) {
-    const int e = (int)((u >> 7) & 0xFF);
-    const uint32_t neg = u >> 15;
-    const int idx = min(max(((e - GELU_TAB_E0) << 7) | (int)(u & 127), 0), GELU_TAB_NE * 128 - 1) +
-                    (int)neg * (GELU_TAB_NE * 128);
-    uint32_t t = tab[idx];
-    if (e < GELU_TAB_E0) {
-        const __nv_bfloat16 h = __float2bfloat16(__uint_as_float(u << 16) * 0.5f);
-        t = (uint32_t)(*reinterpret_cast<const unsigned short*>(&h)) | (0x3F00u << 16);
-    } else if (e >= GELU_TAB_E0 + GELU_TAB_NE) {
-        t = neg ? 0x80008000u : (u | (0x3F80u << 16));
-    }
-    return t;
-}
-
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -160,18 +126,24 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t& r0, uint32_t& r1, uint32_t& 
                  : "r"(smem_u32(p)));
 }
 
-// D += A(16x16, row) * B(16x8, col), bf16 inputs, fp32 accumulators.
-__device__ __forceinline__ void mma_bf16(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+// D += A(16x16, row) * B(16x8, col), f16 inputs, fp32 accumulators.
+__device__ __forceinline__ void mma_sync_f16(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
     asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+// two floats rounded to nearest-even f16, lo in the low half-word
+__device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// the two f16 halves of a word as floats
+__device__ __forceinline__ float2 unpack_f16(uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -16,7 +16,7 @@ namespace {
 template <int NV>
 __global__ void ln_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
                               const float* __restrict__ b, const float* __restrict__ add,
-                              int rows_per_clip, bf16* __restrict__ y, float* __restrict__ mean,
+                              int rows_per_clip, f16* __restrict__ y, float* __restrict__ mean,
                               float* __restrict__ rstd, int rows, int D, float eps) {
     pdl_wait();
     pdl_trigger();
@@ -62,7 +62,7 @@ __global__ void ln_fwd_kernel(const float* __restrict__ x, const float* __restri
                 const float4 aa = *reinterpret_cast<const float4*>(ad + j);
                 o0 += aa.x; o1 += aa.y; o2 += aa.z; o3 += aa.w;
             }
-            uint2 pk = make_uint2(pack_bf16(o0, o1), pack_bf16(o2, o3));
+            uint2 pk = make_uint2(pack_f16(o0, o1), pack_f16(o2, o3));
             *reinterpret_cast<uint2*>(y + (long)row * D + j) = pk;
         }
 }
@@ -71,7 +71,7 @@ template <int NV>
 __global__ void ln_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
                               const float* __restrict__ w, const float* __restrict__ mean,
                               const float* __restrict__ rstd, float* __restrict__ dx, int accumulate,
-                              const float* __restrict__ extra, bf16* __restrict__ dx_bf,
+                              const float* __restrict__ extra, f16* __restrict__ dx_h,
                               const float* __restrict__ colscale, int rows, int D) {
     pdl_wait();
     pdl_trigger();
@@ -114,17 +114,17 @@ __global__ void ln_bwd_kernel(const float* __restrict__ dy, const float* __restr
                                    rs * (gv[i].z - s1 - xh[i].z * s2), rs * (gv[i].w - s1 - xh[i].w * s2));
             r.x += ad[i].x; r.y += ad[i].y; r.z += ad[i].z; r.w += ad[i].w;
             *dp = r;
-            if (dx_bf) {
+            if (dx_h) {
                 float4 c = make_float4(1.f, 1.f, 1.f, 1.f);
                 if (colscale) c = *reinterpret_cast<const float4*>(colscale + j);
-                *reinterpret_cast<uint2*>(dx_bf + (long)row * D + j) =
-                    make_uint2(pack_bf16(r.x * c.x, r.y * c.y), pack_bf16(r.z * c.z, r.w * c.w));
+                *reinterpret_cast<uint2*>(dx_h + (long)row * D + j) =
+                    make_uint2(pack_f16(r.x * c.x, r.y * c.y), pack_f16(r.z * c.z, r.w * c.w));
             }
         }
 }
 
-__global__ void resid_bf16_kernel(float* __restrict__ x, const float* __restrict__ extra,
-                                  bf16* __restrict__ dst, const float* __restrict__ colscale, long n4, int D) {
+__global__ void resid_f16_kernel(float* __restrict__ x, const float* __restrict__ extra,
+                                  f16* __restrict__ dst, const float* __restrict__ colscale, long n4, int D) {
     pdl_wait();
     pdl_trigger();
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -137,19 +137,19 @@ __global__ void resid_bf16_kernel(float* __restrict__ x, const float* __restrict
     }
     float4 c = make_float4(1.f, 1.f, 1.f, 1.f);
     if (colscale) c = *reinterpret_cast<const float4*>(colscale + (i * 4) % D);
-    reinterpret_cast<uint2*>(dst)[i] = make_uint2(pack_bf16(v.x * c.x, v.y * c.y), pack_bf16(v.z * c.z, v.w * c.w));
+    reinterpret_cast<uint2*>(dst)[i] = make_uint2(pack_f16(v.x * c.x, v.y * c.y), pack_f16(v.z * c.z, v.w * c.w));
 }
 
-__global__ void f32_bf16_kernel(const float* __restrict__ x, bf16* __restrict__ y, long n) {
+__global__ void f32_f16_kernel(const float* __restrict__ x, f16* __restrict__ y, long n) {
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) y[i] = __float2bfloat16(x[i]);
+    if (i < n) y[i] = __float2half_rn(x[i]);
 }
 
 // ---------------------------------------------------------------------------------------
 // MelodyFlow inputs and loss, src/mf/train.h:154-159 and :107-108, src/mf/dit.h:172-173,208-216.
 __global__ void mf_inputs_kernel(const float* __restrict__ clean, const float* __restrict__ noise,
                                  const float* __restrict__ tv, int clips, int T, int lat,
-                                 bf16* __restrict__ x0, float* __restrict__ vstar) {
+                                 f16* __restrict__ x0, float* __restrict__ vstar) {
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     const long n = (long)clips * lat * T;
     if (i >= n) return;
@@ -158,19 +158,20 @@ __global__ void mf_inputs_kernel(const float* __restrict__ clean, const float* _
     const float t = tv[b];
     const float rescale = 1.0f / sqrtf(t * t + (1.0f - t) * (1.0f - t));
     const float cl = clean[i], nz = noise[i];
-    x0[((long)b * T + p) * lat + c] = __float2bfloat16(((1 - t) * nz + t * cl) * rescale);
+    x0[((long)b * T + p) * lat + c] = __float2half_rn(((1 - t) * nz + t * cl) * rescale);
     vstar[i] = cl - nz;
 }
 
-// MSE of the rescaled output against v* (flow target) and its seed gradient.  out / dout are
+// MSE of the rescaled output against v* (flow target) and its seed gradient, multiplied by the
+// backward's gradient scale gscale (a power of two; see kernels.h).  out / dout are
 // [clips][T][lat] (token-major), vstar [clips][lat][T]; block (b, j) takes a strided share of
 // clip b in out's order (coalesced out / dout) and leaves its partial sum in part[b][j].
 constexpr int LOSS_PARTS = 32;
 __global__ void mf_loss_part_kernel(const float* __restrict__ out, const float* __restrict__ vstar, int T,
-                                    int lat, float* __restrict__ part, bf16* __restrict__ dout) {
+                                    int lat, float* __restrict__ part, f16* __restrict__ dout, float gscale) {
     const int b = blockIdx.x, j = blockIdx.y;
     const long n = (long)T * lat;
-    const float inv = 1.0f / (float)n;
+    const float inv = 1.0f / (float)n, seed = 2.0f * sqrtf(2.0f) * inv * gscale;
     const float sq2 = sqrtf(2.0f);
     float acc = 0.f;
     for (long i = (long)j * blockDim.x + threadIdx.x; i < n; i += (long)LOSS_PARTS * blockDim.x) {
@@ -178,7 +179,7 @@ __global__ void mf_loss_part_kernel(const float* __restrict__ out, const float* 
         const long o = (long)b * n + i;
         const float d = out[o] * sq2 - vstar[(long)b * n + (long)c * T + p];
         acc += d * d;
-        dout[o] = __float2bfloat16(2.0f * d * inv * sq2);
+        dout[o] = __float2half_rn(d * seed);
     }
     __shared__ float red[32];
     acc = warp_sum(acc);
@@ -214,17 +215,17 @@ __global__ void linear_f32_kernel(const float* __restrict__ x, const float* __re
 
 // ---------------------------------------------------------------------------------------
 // DoRA-rows, src/ac/lora.h:62-79 (and the hand-derived backward of that factorisation).
-__global__ void dora_colsum_kernel(const bf16* __restrict__ a, long lda, const bf16* __restrict__ b,
+__global__ void dora_colsum_kernel(const f16* __restrict__ a, long lda, const f16* __restrict__ b,
                                    long ldb, int rows, int N, const float* __restrict__ g,
-                                   float* __restrict__ dg, int rows_per_block) {
+                                   float* __restrict__ dg, int rows_per_block, float inv_gscale) {
     const int n = blockIdx.x * blockDim.x + threadIdx.x;
     if (n >= N) return;
     const int r0 = blockIdx.y * rows_per_block, r1 = min(rows, r0 + rows_per_block);
     float acc = 0.f;
     for (int r = r0; r < r1; ++r)
-        acc += __bfloat162float(a[(long)r * lda + n]) * __bfloat162float(b[(long)r * ldb + n]);
+        acc += __half2float(a[(long)r * lda + n]) * __half2float(b[(long)r * ldb + n]);
     const float gg = g[n];
-    atomicAdd(dg + n, acc / (gg * gg));
+    atomicAdd(dg + n, acc * inv_gscale / (gg * gg));
 }
 
 __global__ void gram_kernel(const float* __restrict__ A, int r, int in, const float* __restrict__ wt,
@@ -272,7 +273,7 @@ __global__ void dora_tail_kernel(const float* __restrict__ dg, const float* __re
                                  const float* __restrict__ g, const float* __restrict__ B,
                                  const float* __restrict__ P, const float* __restrict__ Q, int r,
                                  int RP, int out, float s, float* __restrict__ gm, float* __restrict__ gB,
-                                 bf16* __restrict__ BD, float* __restrict__ dt3) {
+                                 f16* __restrict__ BD, float* __restrict__ dt3, float bd_scale) {
     const int o = blockIdx.x * blockDim.x + threadIdx.x;
     if (o >= out) return;
     const float sq = sqrtf(nsq[o]);
@@ -283,9 +284,9 @@ __global__ void dora_tail_kernel(const float* __restrict__ dg, const float* __re
     for (int j = 0; j < RP; ++j) {
         if (j < r) {
             gB[(long)o * r + j] += d2 * P[(long)o * RP + j] + 2.0f * d3 * Q[(long)o * r + j];
-            BD[(long)o * RP + j] = __float2bfloat16(d2 * B[(long)o * r + j]);
+            BD[(long)o * RP + j] = __float2half_rn(bd_scale * d2 * B[(long)o * r + j]);
         } else {
-            BD[(long)o * RP + j] = __float2bfloat16(0.f);
+            BD[(long)o * RP + j] = __float2half_rn(0.f);
         }
     }
 }
@@ -306,7 +307,7 @@ __global__ void refresh_kernel(const CopyJob* jobs) {
     const long n = (long)j.rows * j.cols;
     for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (long)gridDim.x * blockDim.x) {
         const int row = (int)(e / j.cols), col = (int)(e % j.cols);
-        j.dst[(long)row * j.ldd + col] = __float2bfloat16(j.src[e]);
+        j.dst[(long)row * j.ldd + col] = __float2half_rn(j.src[e]);
     }
 }
 
@@ -365,13 +366,14 @@ __global__ void adamw_kernel(float* __restrict__ value, float* __restrict__ m, f
 }
 
 // ---------------------------------------------------------------------------------------
-// Q8_0: 34-byte blocks {fp16 d; int8 q[32]}; w = d * q exactly in fp32.
-__global__ void q8_bf16_kernel(const uint8_t* __restrict__ blocks, long nblocks, bf16* __restrict__ out) {
+// Q8_0: 34-byte blocks {fp16 d; int8 q[32]}; w = d * q exactly in fp32 (then rounded to the
+// f16 GEMM operand).
+__global__ void q8_f16_kernel(const uint8_t* __restrict__ blocks, long nblocks, f16* __restrict__ out) {
     const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (e >= nblocks * 32) return;
     const uint8_t* blk = blocks + (e >> 5) * 34;
     const __half d = __ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8)));
-    out[e] = __float2bfloat16(__half2float(d) * (float)(int8_t)blk[2 + (e & 31)]);
+    out[e] = __float2half_rn(__half2float(d) * (float)(int8_t)blk[2 + (e & 31)]);
 }
 
 __global__ void q8_f32_kernel(const uint8_t* __restrict__ blocks, long nblocks, float* __restrict__ out) {
@@ -380,11 +382,6 @@ __global__ void q8_f32_kernel(const uint8_t* __restrict__ blocks, long nblocks, 
     const uint8_t* blk = blocks + (e >> 5) * 34;
     const __half d = __ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8)));
     out[e] = __half2float(d) * (float)(int8_t)blk[2 + (e & 31)];
-}
-
-__global__ void f16_bf16_kernel(const uint16_t* __restrict__ in, long n, bf16* __restrict__ out) {
-    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (e < n) out[e] = __float2bfloat16(__half2float(__ushort_as_half(in[e])));
 }
 
 // ---------------------------------------------------------------------------------------
@@ -408,11 +405,11 @@ __global__ void mg_embed_kernel(const int32_t* __restrict__ ids, int steps, int 
 // ggml_cross_entropy_loss over the selected rows, src/mg/train.h:131.
 __global__ void mg_ce_kernel(const float* __restrict__ logits, int card, const int32_t* __restrict__ targets,
                              int rows_per_seq, float inv_nsel, float* __restrict__ loss_acc,
-                             bf16* __restrict__ dlogits) {
+                             f16* __restrict__ dlogits, float gscale) {
     const int row = blockIdx.x;
     const int tgt = targets[row];
     const float* lg = logits + (long)row * card;
-    bf16* dl = dlogits + (long)row * card;
+    f16* dl = dlogits + (long)row * card;
     __shared__ float red[32];
     __shared__ float sh_max, sh_sum;
     float mx = -INFINITY;
@@ -443,61 +440,47 @@ __global__ void mg_ce_kernel(const float* __restrict__ logits, int card, const i
     __syncthreads();
     sm = sh_sum;
     if (tgt < 0) {
-        for (int j = threadIdx.x; j < card; j += blockDim.x) dl[j] = __float2bfloat16(0.f);
+        for (int j = threadIdx.x; j < card; j += blockDim.x) dl[j] = __float2half_rn(0.f);
         return;
     }
-    const float inv = 1.0f / sm;
+    const float inv = 1.0f / sm, seed = inv_nsel * gscale;
     for (int j = threadIdx.x; j < card; j += blockDim.x)
-        dl[j] = __float2bfloat16((expf(lg[j] - mx) * inv - (j == tgt ? 1.0f : 0.0f)) * inv_nsel);
+        dl[j] = __float2half_rn((expf(lg[j] - mx) * inv - (j == tgt ? 1.0f : 0.0f)) * seed);
     if (threadIdx.x == 0) atomicAdd(loss_acc + row / rows_per_seq, (mx + logf(sm) - lg[tgt]) * inv_nsel);
 }
 
-// the GELU table (built once per context)
-__global__ void gelu_table_kernel(uint32_t* tab) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < GELU_TAB_ENTRIES) tab[i] = gelu_tab_entry(i);
-}
-
-// gact = gelu(z); with store_grad, z is overwritten by gelu'(z).  8 bf16 per thread and step.
-__global__ void __launch_bounds__(256) gelu_fwd_kernel(const uint32_t* __restrict__ tab_g, bf16* __restrict__ z,
-                                                       bf16* __restrict__ gact, long n8, int store_grad) {
-    __shared__ __align__(16) uint32_t tab[GELU_TAB_ENTRIES];
+// gact = gelu(z); with store_grad, z is overwritten by gelu'(z).  8 f16 per thread and step;
+// the A&S evaluation of gelu_as_pair on each f16 pre-activation (the pass stays HBM-bound).
+__global__ void __launch_bounds__(256) gelu_fwd_kernel(f16* __restrict__ z, f16* __restrict__ gact, long n8,
+                                                       int store_grad) {
     pdl_wait();
     pdl_trigger();
-    for (int i = threadIdx.x; i < GELU_TAB_ENTRIES / 4; i += blockDim.x)
-        reinterpret_cast<uint4*>(tab)[i] = reinterpret_cast<const uint4*>(tab_g)[i];
-    __syncthreads();
     for (long c = (long)blockIdx.x * blockDim.x + threadIdx.x; c < n8; c += (long)gridDim.x * blockDim.x) {
         const uint4 zz = reinterpret_cast<const uint4*>(z)[c];
         const uint32_t w[4] = {zz.x, zz.y, zz.z, zz.w};
         uint32_t g[4], d[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const uint32_t lo = gelu_tab_lookup(tab, w[j] & 0xFFFFu), hi = gelu_tab_lookup(tab, w[j] >> 16);
-            g[j] = (lo & 0xFFFFu) | (hi << 16);
-            d[j] = (lo >> 16) | (hi & 0xFFFF0000u);
+            const float2 x = unpack_f16(w[j]);
+            float g0, d0, g1, d1;
+            gelu_as_pair(x.x, g0, d0);
+            gelu_as_pair(x.y, g1, d1);
+            g[j] = pack_f16(g0, g1);
+            d[j] = pack_f16(d0, d1);
         }
         reinterpret_cast<uint4*>(gact)[c] = make_uint4(g[0], g[1], g[2], g[3]);
         if (store_grad) reinterpret_cast<uint4*>(z)[c] = make_uint4(d[0], d[1], d[2], d[3]);
     }
 }
 
-// stand-alone check: gelu / gelu' of bf16 inputs, directly (A&S evaluation) or by table
-__global__ void gelu_check_kernel(const uint32_t* tab, const uint16_t* z, uint16_t* g, uint16_t* dg, long n,
-                                  int direct) {
+// stand-alone check: gelu / gelu' of f16 inputs through the training step's pass
+__global__ void gelu_check_kernel(const uint16_t* z, uint16_t* g, uint16_t* dg, long n) {
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    uint32_t t;
-    if (direct) {
-        float gv, dv;
-        gelu_as_pair(__uint_as_float((uint32_t)z[i] << 16), gv, dv);
-        const __nv_bfloat162 v = __floats2bfloat162_rn(gv, dv);
-        t = *reinterpret_cast<const uint32_t*>(&v);
-    } else {
-        t = gelu_tab_lookup(tab, z[i]);
-    }
-    g[i] = (uint16_t)(t & 0xFFFFu);
-    dg[i] = (uint16_t)(t >> 16);
+    float gv, dv;
+    gelu_as_pair(__half2float(__ushort_as_half(z[i])), gv, dv);
+    g[i] = __half_as_ushort(__float2half_rn(gv));
+    dg[i] = __half_as_ushort(__float2half_rn(dv));
 }
 
 inline unsigned blocks_for(long n, int t) { return (unsigned)((n + t - 1) / t); }
@@ -526,49 +509,45 @@ inline unsigned blocks_for(long n, int t) { return (unsigned)((n + t - 1) / t); 
     }
 
 void layernorm_fwd(const float* x, const float* w, const float* b, const float* add, int rows_per_clip,
-                   bf16* y, float* mean, float* rstd, int rows, int D, float eps, cudaStream_t s) {
+                   f16* y, float* mean, float* rstd, int rows, int D, float eps, cudaStream_t s) {
     LN_DISPATCH(ln_fwd_kernel, x, w, b, add, rows_per_clip, y, mean, rstd, rows, D, eps);
 }
 
 void layernorm_bwd(const float* dy, const float* x, const float* w, const float* mean, const float* rstd,
-                   float* dx, int accumulate, const float* extra, bf16* dx_bf, const float* colscale,
+                   float* dx, int accumulate, const float* extra, f16* dx_h, const float* colscale,
                    int rows, int D, cudaStream_t s) {
-    LN_DISPATCH(ln_bwd_kernel, dy, x, w, mean, rstd, dx, accumulate, extra, dx_bf, colscale, rows, D);
+    LN_DISPATCH(ln_bwd_kernel, dy, x, w, mean, rstd, dx, accumulate, extra, dx_h, colscale, rows, D);
 }
 
-void residual_to_bf16(float* x, const float* extra, bf16* dst, const float* colscale, int rows, int D,
+void residual_to_f16(float* x, const float* extra, f16* dst, const float* colscale, int rows, int D,
                       cudaStream_t s) {
     const long n4 = (long)rows * D / 4;
-    launch_pdl(resid_bf16_kernel, dim3(blocks_for(n4, 256)), dim3(256), 0, s, x, extra, dst, colscale, n4, D);
+    launch_pdl(resid_f16_kernel, dim3(blocks_for(n4, 256)), dim3(256), 0, s, x, extra, dst, colscale, n4, D);
 }
 
-void gelu_table_init(uint32_t* tab, cudaStream_t s) {
-    gelu_table_kernel<<<blocks_for(GELU_TAB_ENTRIES, 256), 256, 0, s>>>(tab);
+void gelu_check(const uint16_t* z, uint16_t* g, uint16_t* dg, long n, cudaStream_t s) {
+    gelu_check_kernel<<<blocks_for(n, 256), 256, 0, s>>>(z, g, dg, n);
 }
 
-void gelu_check(const uint32_t* tab, const uint16_t* z, uint16_t* g, uint16_t* dg, long n, int direct, cudaStream_t s) {
-    gelu_check_kernel<<<blocks_for(n, 256), 256, 0, s>>>(tab, z, g, dg, n, direct);
-}
-
-void gelu_fwd(const uint32_t* tab, bf16* z, bf16* gact, long n, int store_grad, cudaStream_t s) {
+void gelu_fwd(f16* z, f16* gact, long n, int store_grad, cudaStream_t s) {
     const long n8 = n / 8;
     long blocks = std::min<long>(blocks_for(n8, 256), 148L * 8);
-    launch_pdl(gelu_fwd_kernel, dim3((unsigned)blocks), dim3(256), 0, s, tab, z, gact, n8, store_grad);
+    launch_pdl(gelu_fwd_kernel, dim3((unsigned)blocks), dim3(256), 0, s, z, gact, n8, store_grad);
 }
 
-void f32_to_bf16(const float* x, bf16* y, long n, cudaStream_t s) {
-    f32_bf16_kernel<<<blocks_for(n, 256), 256, 0, s>>>(x, y, n);
+void f32_to_f16(const float* x, f16* y, long n, cudaStream_t s) {
+    f32_f16_kernel<<<blocks_for(n, 256), 256, 0, s>>>(x, y, n);
 }
 
-void mf_inputs(const float* clean, const float* noise, const float* t, int clips, int T, int lat, bf16* x0,
+void mf_inputs(const float* clean, const float* noise, const float* t, int clips, int T, int lat, f16* x0,
                float* vstar, cudaStream_t s) {
     const long n = (long)clips * lat * T;
     mf_inputs_kernel<<<blocks_for(n, 256), 256, 0, s>>>(clean, noise, t, clips, T, lat, x0, vstar);
 }
 
-void mf_loss(const float* out, const float* vstar, int clips, int T, int lat, float* loss, bf16* dout,
-             float* part, cudaStream_t s) {
-    mf_loss_part_kernel<<<dim3(clips, LOSS_PARTS), 256, 0, s>>>(out, vstar, T, lat, part, dout);
+void mf_loss(const float* out, const float* vstar, int clips, int T, int lat, float* loss, f16* dout,
+             float* part, float gscale, cudaStream_t s) {
+    mf_loss_part_kernel<<<dim3(clips, LOSS_PARTS), 256, 0, s>>>(out, vstar, T, lat, part, dout, gscale);
     mf_loss_sum_kernel<<<1, 32 * ((clips + 31) / 32), 0, s>>>(part, clips, 1.0f / ((float)T * lat), loss);
 }
 
@@ -576,11 +555,11 @@ void linear_f32(const float* x, const float* W, float* y, int rows, int N, int K
     linear_f32_kernel<<<blocks_for((long)rows * N, 8), 256, 0, s>>>(x, W, y, rows, N, K, act);
 }
 
-void dora_colsum(const bf16* a, long lda, const bf16* b, long ldb, int rows, int N, const float* colscale,
-                 float* dg, cudaStream_t s) {
+void dora_colsum(const f16* a, long lda, const f16* b, long ldb, int rows, int N, const float* colscale,
+                 float* dg, float inv_gscale, cudaStream_t s) {
     const int rpb = 256;
     dim3 grid(blocks_for(N, 256), blocks_for(rows, rpb));
-    dora_colsum_kernel<<<grid, 256, 0, s>>>(a, lda, b, ldb, rows, N, colscale, dg, rpb);
+    dora_colsum_kernel<<<grid, 256, 0, s>>>(a, lda, b, ldb, rows, N, colscale, dg, rpb, inv_gscale);
 }
 
 void dora_prepare(const float* A, const float* B, const float* m, const float* P, const float* base, int r,
@@ -592,16 +571,17 @@ void dora_prepare(const float* A, const float* B, const float* m, const float* P
 
 void dora_finish(const float* dg, const float* nsq, const float* g, const float* m, const float* B,
                  const float* P, const float* Q, const float* A, int r, int RP, int in, int out, float s,
-                 float* gm, float* gB, float* gA, bf16* BD, float* scratch, cudaStream_t st) {
+                 float* gm, float* gB, float* gA, f16* BD, float bd_scale, float* scratch, cudaStream_t st) {
     float* dt3 = scratch;           // [out]
     float* dG = scratch + out;      // [r][r]
-    dora_tail_kernel<<<blocks_for(out, 128), 128, 0, st>>>(dg, nsq, g, B, P, Q, r, RP, out, s, gm, gB, BD, dt3);
+    dora_tail_kernel<<<blocks_for(out, 128), 128, 0, st>>>(dg, nsq, g, B, P, Q, r, RP, out, s, gm, gB, BD, dt3,
+                                                           bd_scale);
     gram_kernel<<<r * r, 256, 0, st>>>(nullptr, r, out, dt3, B, r, dG);
     dora_ga_kernel<<<blocks_for((long)r * in, 256), 256, 0, st>>>(dG, A, r, in, gA);
     (void)m;
 }
 
-void refresh_bf16(const CopyJob* jobs_dev, int njobs, int max_elems, cudaStream_t s) {
+void refresh_f16(const CopyJob* jobs_dev, int njobs, int max_elems, cudaStream_t s) {
     if (njobs <= 0) return;
     dim3 grid(blocks_for(max_elems, 256) > 256 ? 256 : blocks_for(max_elems, 256), njobs);
     refresh_kernel<<<grid, 256, 0, s>>>(jobs_dev);
@@ -616,16 +596,12 @@ void adamw(float* value, float* m, float* v, float* grad, const uint8_t* decay_m
                                      decay, bc1, bc2, partials, nparts, nonfinite);
 }
 
-void q8_0_to_bf16(const uint8_t* blocks, long nblocks, bf16* out, cudaStream_t s) {
-    q8_bf16_kernel<<<blocks_for(nblocks * 32, 256), 256, 0, s>>>(blocks, nblocks, out);
+void q8_0_to_f16(const uint8_t* blocks, long nblocks, f16* out, cudaStream_t s) {
+    q8_f16_kernel<<<blocks_for(nblocks * 32, 256), 256, 0, s>>>(blocks, nblocks, out);
 }
 
 void q8_0_to_f32(const uint8_t* blocks, long nblocks, float* out, cudaStream_t s) {
     q8_f32_kernel<<<blocks_for(nblocks * 32, 256), 256, 0, s>>>(blocks, nblocks, out);
-}
-
-void f16_to_bf16(const uint16_t* in, long n, bf16* out, cudaStream_t s) {
-    f16_bf16_kernel<<<blocks_for(n, 256), 256, 0, s>>>(in, n, out);
 }
 
 void mg_embed(const int32_t* ids, int steps, int nq, const float* const* emb_dev, const float* pos, float* x,
@@ -635,8 +611,8 @@ void mg_embed(const int32_t* ids, int steps, int nq, const float* const* emb_dev
 }
 
 void mg_cross_entropy(const float* logits, int rows, int card, const int32_t* targets, int rows_per_seq,
-                      float inv_nsel, float* loss_acc, bf16* dlogits, cudaStream_t s) {
-    mg_ce_kernel<<<rows, 256, 0, s>>>(logits, card, targets, rows_per_seq, inv_nsel, loss_acc, dlogits);
+                      float inv_nsel, float* loss_acc, f16* dlogits, float gscale, cudaStream_t s) {
+    mg_ce_kernel<<<rows, 256, 0, s>>>(logits, card, targets, rows_per_seq, inv_nsel, loss_acc, dlogits, gscale);
 }
 
 }  // namespace act

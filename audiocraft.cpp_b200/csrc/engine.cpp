@@ -1,6 +1,6 @@
 // engine.cpp -- host side of libactrain.so: the C ABI of include/actrain.h.
 //
-// One act_ctx owns one device: the frozen base weights (bf16, dequantised once from
+// One act_ctx owns one device: the frozen base weights (f16, dequantised once from
 // F32/F16/Q8_0 at bind time), the fp32 adapter master parameters with their Adam moments and
 // gradient accumulator, the activation arena sized for (max_batch, frames, tokens), and one
 // CUDA graph per microbatch size that replays the whole forward + backward.
@@ -143,17 +143,17 @@ const char* const kTargets[7] = {"self.qkv", "self.out", "cross.q", "cross.kv", 
 
 struct Proj {
     int in = 0, out = 0;
-    bf16* W = nullptr;
+    f16* W = nullptr;
     bool bound = false;
     bool adapted = false, dora = false;
     int r = 0, RP = 0;
     float s = 0.f;
     int64_t offA = 0, offB = 0, offM = -1;
-    bf16* A_bf = nullptr;  // [RP][in], rows >= r zero
-    bf16* B_bf = nullptr;  // [out][RP], cols >= r zero
+    f16* A_h = nullptr;  // [RP][in], rows >= r zero
+    f16* B_h = nullptr;  // [out][RP], cols >= r zero
     float* base = nullptr; // DoRA: frozen ||W_o||^2 + in*1e-12 (double accumulated on the host)
     float *P = nullptr, *G = nullptr, *Q = nullptr, *nsq = nullptr, *g = nullptr, *dg = nullptr, *scr = nullptr;
-    bf16* BD = nullptr;
+    f16* BD = nullptr;
 };
 
 struct Layer {
@@ -163,12 +163,12 @@ struct Layer {
     int proj = 0, src = -1;
     float *xin = nullptr, *xmid = nullptr, *xmid2 = nullptr, *xout = nullptr;
     float *mu[3] = {}, *rs[3] = {};
-    bf16 *h1 = nullptr, *hc = nullptr, *f = nullptr, *qkv = nullptr, *o1 = nullptr, *cq = nullptr;
-    bf16 *ckv = nullptr, *o2 = nullptr, *z = nullptr, *gact = nullptr;
-    bf16* U[7] = {};
-    bf16* Yaux[7] = {};
+    f16 *h1 = nullptr, *hc = nullptr, *f = nullptr, *qkv = nullptr, *o1 = nullptr, *cq = nullptr;
+    f16 *ckv = nullptr, *o2 = nullptr, *z = nullptr, *gact = nullptr;
+    f16* U[7] = {};
+    f16* Yaux[7] = {};
     float *lse1 = nullptr, *lse2 = nullptr;
-    bf16* xsave_bf = nullptr;
+    f16* xsave_h = nullptr;
     float* dsaved = nullptr;
 };
 
@@ -209,16 +209,19 @@ struct act_ctx {
 
     std::vector<Layer> layers;
     // MelodyFlow globals
-    bf16 *in_proj = nullptr, *out_proj = nullptr, *cond_w = nullptr;
+    f16 *in_proj = nullptr, *out_proj = nullptr, *cond_w = nullptr;
     float *cond_b = nullptr, *te0 = nullptr, *te2 = nullptr, *onw = nullptr, *onb = nullptr;
-    std::vector<bf16*> skip;
+    std::vector<f16*> skip;
     std::vector<float> rope_ff;
     float* rope = nullptr;
-    uint32_t* gelu_tab = nullptr;  // bf16 GELU / GELU' table for the feed-forward activation
+    // backward gradient scale: a power of two near the loss's divisor (T * latent for the MSE,
+    // scored positions for the cross entropy); seeds are multiplied by it, adapter gradients by
+    // its inverse
+    float gscale = 1.f, inv_gscale = 1.f;
     // MusicGen globals
     std::vector<float*> emb;
     float** emb_dev = nullptr;
-    std::vector<bf16*> head;
+    std::vector<f16*> head;
     float* pos = nullptr;
     std::map<std::string, bool> bound;
 
@@ -243,15 +246,15 @@ struct act_ctx {
     int32_t *d_nvalid = nullptr, *d_ids = nullptr, *d_tgt = nullptr;
 
     // global activations / scratch
-    bf16 *x0 = nullptr, *hidden_bf = nullptr, *ctx_bf = nullptr, *xo = nullptr, *dout = nullptr, *xprev_bf = nullptr;
+    f16 *x0 = nullptr, *hidden_h = nullptr, *ctx_h = nullptr, *xo = nullptr, *dout = nullptr, *xprev_h = nullptr;
     float *vstar = nullptr, *te1 = nullptr, *te = nullptr, *x0f = nullptr, *muo = nullptr, *rso = nullptr,
           *outp = nullptr;
     float *dx = nullptr, *dtmp = nullptr, *dq_acc = nullptr, *dvec = nullptr;
     float* dkv_acc = nullptr;  // cross-attention dK | dV partial sums (fp32, [2][clips * C][D])
-    bf16 *dxbf = nullptr, *dz = nullptr, *dU = nullptr, *dob = nullptr, *dqkv = nullptr, *dcq = nullptr,
+    f16 *dxh = nullptr, *dz = nullptr, *dU = nullptr, *dob = nullptr, *dqkv = nullptr, *dcq = nullptr,
          *dckv = nullptr;
     float* logits = nullptr;
-    bf16* dlogits = nullptr;
+    f16* dlogits = nullptr;
 
     // execution
     std::map<int, cudaGraphExec_t> graphs;
@@ -345,9 +348,9 @@ struct act_ctx {
         } else {
             ++path_count[ACT_PATH_GEMM_MMA];
             timed(cls, fl, 0, [&] { gemm(g, stream); });
-            if (g.out_bf)  // the generic path has no second output: convert afterwards
+            if (g.out_h)  // the generic path has no second output: convert afterwards
                 timed(2, 0, 0, [&] {
-                    residual_to_bf16(static_cast<float*>(g.out), nullptr, g.out_bf, nullptr, g.M, g.N, stream);
+                    residual_to_f16(static_cast<float*>(g.out), nullptr, g.out_h, nullptr, g.M, g.N, stream);
                 });
         }
     }
@@ -413,62 +416,64 @@ struct act_ctx {
 
     // ---------------------------------------------------------------- projections
     // Y = (X W^T + s (X A^T) B^T) * g  with the epilogue given in `e` (mode/out/ldo/resid/aux).
-    void proj_fwd(Proj& p, const bf16* X, long rows, bf16* U, GemmArgs e) {
+    void proj_fwd(Proj& p, const f16* X, long rows, f16* U, GemmArgs e) {
         if (p.adapted) {
             GemmArgs u;
             u.M = (int)rows; u.N = p.RP; u.K1 = p.in;
-            u.A1 = X; u.lda1 = p.in; u.B1 = p.A_bf; u.ldb1 = p.in;
-            u.mode = EPI_STORE_BF16; u.alpha = p.s; u.out = U; u.ldo = p.RP;
+            u.A1 = X; u.lda1 = p.in; u.B1 = p.A_h; u.ldb1 = p.in;
+            u.mode = EPI_STORE_F16; u.alpha = p.s; u.out = U; u.ldo = p.RP;
             SkinnyArgs k;  // U = s X A^T
             k.M = (int)rows; k.K = p.in; k.nb = p.RP;
-            k.A = X; k.lda = p.in; k.B = p.A_bf; k.ldb = p.in;
+            k.A = X; k.lda = p.in; k.B = p.A_h; k.ldb = p.in;
             k.kind = SKINNY_STORE; k.alpha = p.s; k.out = U; k.ldo = p.RP;
             run_rank(k, u);
         }
         e.M = (int)rows; e.N = p.out; e.K1 = p.in;
         e.A1 = X; e.lda1 = p.in; e.B1 = p.W; e.ldb1 = p.in;
         if (p.adapted) {
-            e.K2 = p.RP; e.A2 = U; e.lda2 = p.RP; e.B2 = p.B_bf; e.ldb2 = p.RP;
+            e.K2 = p.RP; e.A2 = U; e.lda2 = p.RP; e.B2 = p.B_h; e.ldb2 = p.RP;
         }
         if (p.dora) e.colscale = p.g;
         run_gemm(e, 0);
     }
 
-    // Adapter gradients of one projection from dYl (= dY * g, bf16 [rows][out]) and, when
+    // Adapter gradients of one projection from dYl (= dY * g, f16 [rows][out]) and, when
     // `e` has an output, the input gradient dX = dYl W + dU A.
-    void proj_bwd(Proj& p, const bf16* dYl, long rows, const bf16* X, const bf16* U, const bf16* Y,
+    void proj_bwd(Proj& p, const f16* dYl, long rows, const f16* X, const f16* U, const f16* Y,
                   bool want_dx, GemmArgs e) {
-        if (p.dora) timed(2, 0, 4.0 * rows * p.out, [&] { dora_colsum(dYl, p.out, Y, p.out, (int)rows, p.out, p.g, p.dg, stream); });
+        if (p.dora)
+            timed(2, 0, 4.0 * rows * p.out,
+                  [&] { dora_colsum(dYl, p.out, Y, p.out, (int)rows, p.out, p.g, p.dg, inv_gscale, stream); });
         if (p.adapted) {
             GemmArgs u;
             u.M = (int)rows; u.N = p.RP; u.K1 = p.out;
-            u.A1 = dYl; u.lda1 = p.out; u.B1 = p.B_bf; u.ldb1 = p.RP; u.b_kmajor = false;
-            u.mode = EPI_STORE_BF16; u.alpha = p.s; u.out = dU; u.ldo = p.RP;
+            u.A1 = dYl; u.lda1 = p.out; u.B1 = p.B_h; u.ldb1 = p.RP; u.b_kmajor = false;
+            u.mode = EPI_STORE_F16; u.alpha = p.s; u.out = dU; u.ldo = p.RP;
             SkinnyArgs ku;  // dU = s dYl B
             ku.M = (int)rows; ku.K = p.out; ku.nb = p.RP;
-            ku.A = dYl; ku.lda = p.out; ku.B = p.B_bf; ku.ldb = p.RP; ku.b_mn = true;
+            ku.A = dYl; ku.lda = p.out; ku.B = p.B_h; ku.ldb = p.RP; ku.b_mn = true;
             ku.kind = SKINNY_STORE; ku.alpha = p.s; ku.out = dU; ku.ldo = p.RP;
             run_rank(ku, u);
             GemmArgs gb;
             gb.M = p.out; gb.N = p.RP; gb.K1 = (int)rows;
             gb.A1 = dYl; gb.lda1 = p.out; gb.a_kmajor = false;
             gb.B1 = U; gb.ldb1 = p.RP; gb.b_kmajor = false;
-            gb.mode = EPI_ATOMIC_F32; gb.out = grad + p.offB; gb.ldo = p.r; gb.nvalid = p.r;
+            gb.mode = EPI_ATOMIC_F32; gb.alpha = inv_gscale; gb.out = grad + p.offB; gb.ldo = p.r; gb.nvalid = p.r;
             gb.splitk = splitk_for((long)((p.out + 63) / 64), (rows + 63) / 64);
             SkinnyArgs kb;  // dB += dYl^T U   ([out][r])
             kb.M = p.out; kb.K = (int)rows; kb.nb = p.r;
             kb.A = dYl; kb.lda = p.out; kb.a_mn = true; kb.B = U; kb.ldb = p.RP; kb.b_mn = true;
-            kb.kind = SKINNY_ACC; kb.out = grad + p.offB; kb.ldo = p.r;
+            kb.kind = SKINNY_ACC; kb.alpha = inv_gscale; kb.out = grad + p.offB; kb.ldo = p.r;
             GemmArgs ga;
             ga.M = p.RP; ga.N = p.in; ga.K1 = (int)rows;
             ga.A1 = dU; ga.lda1 = p.RP; ga.a_kmajor = false;
             ga.B1 = X; ga.ldb1 = p.in; ga.b_kmajor = false;
-            ga.mode = EPI_ATOMIC_F32; ga.out = grad + p.offA; ga.ldo = p.in; ga.mvalid = p.r;
+            ga.mode = EPI_ATOMIC_F32; ga.alpha = inv_gscale; ga.out = grad + p.offA; ga.ldo = p.in; ga.mvalid = p.r;
             ga.splitk = splitk_for((long)((p.in + 127) / 128), (rows + 63) / 64);
             SkinnyArgs ka;  // dA += dU^T X   ([r][in], computed as its transpose)
             ka.M = p.in; ka.K = (int)rows; ka.nb = p.r;
             ka.A = X; ka.lda = p.in; ka.a_mn = true; ka.B = dU; ka.ldb = p.RP; ka.b_mn = true;
-            ka.kind = SKINNY_ACC_T; ka.out = grad + p.offA; ka.ldo = p.in;
+            ka.kind = SKINNY_ACC_T; ka.alpha = inv_gscale; ka.out = grad + p.offA; ka.ldo = p.in;
             // the adapter gradients only read dYl, U, X and dU: they overlap the input-gradient
             // GEMM below (which fills its last wave with idle SMs) and join before returning
             on_side([&] {
@@ -483,7 +488,7 @@ struct act_ctx {
         e.M = (int)rows; e.N = p.in; e.K1 = p.out;
         e.A1 = dYl; e.lda1 = p.out; e.B1 = p.W; e.ldb1 = p.in; e.b_kmajor = false;
         if (p.adapted) {
-            e.K2 = p.RP; e.A2 = dU; e.lda2 = p.RP; e.B2 = p.A_bf; e.ldb2 = p.in;
+            e.K2 = p.RP; e.A2 = dU; e.lda2 = p.RP; e.B2 = p.A_h; e.ldb2 = p.in;
         }
         run_gemm(e, 0);
         join_side();
@@ -491,13 +496,13 @@ struct act_ctx {
 
     // ---------------------------------------------------------------- the step
     void prepare_adapters() {
-        timed(2, 0, 0, [&] { refresh_bf16(jobs_dev, njobs, max_job, stream); });
+        timed(2, 0, 0, [&] { refresh_f16(jobs_dev, njobs, max_job, stream); });
         for (auto& lay : layers)
             for (auto& p : lay.p) {
                 if (!p.dora) continue;
                 GemmArgs a;
                 a.M = p.out; a.N = p.RP; a.K1 = p.in;
-                a.A1 = p.W; a.lda1 = p.in; a.B1 = p.A_bf; a.ldb1 = p.in;
+                a.A1 = p.W; a.lda1 = p.in; a.B1 = p.A_h; a.ldb1 = p.in;
                 a.mode = EPI_STORE_F32; a.out = p.P; a.ldo = p.RP;
                 run_gemm(a, 2);
                 timed(2, 0, 0, [&] {
@@ -514,19 +519,19 @@ struct act_ctx {
                 if (!p.dora) continue;
                 timed(2, 0, 0, [&] {
                     dora_finish(p.dg, p.nsq, p.g, value + p.offM, value + p.offB, p.P, p.Q, value + p.offA, p.r,
-                                p.RP, p.in, p.out, p.s, grad + p.offM, grad + p.offB, grad + p.offA, p.BD, p.scr,
-                                stream);
+                                p.RP, p.in, p.out, p.s, grad + p.offM, grad + p.offB, grad + p.offA, p.BD, gscale,
+                                p.scr, stream);
                 });
                 GemmArgs a;  // gA += BD^T W
                 a.M = p.RP; a.N = p.in; a.K1 = p.out;
                 a.A1 = p.BD; a.lda1 = p.RP; a.a_kmajor = false;
                 a.B1 = p.W; a.ldb1 = p.in; a.b_kmajor = false;
-                a.mode = EPI_ATOMIC_F32; a.out = grad + p.offA; a.ldo = p.in; a.mvalid = p.r;
+                a.mode = EPI_ATOMIC_F32; a.alpha = inv_gscale; a.out = grad + p.offA; a.ldo = p.in; a.mvalid = p.r;
                 a.splitk = splitk_for((p.in + 127) / 128, (p.out + 63) / 64);
                 SkinnyArgs k;  // the same as (W^T BD)^T over the out dimension
                 k.M = p.in; k.K = p.out; k.nb = p.r;
                 k.A = p.W; k.lda = p.in; k.a_mn = true; k.B = p.BD; k.ldb = p.RP; k.b_mn = true;
-                k.kind = SKINNY_ACC_T; k.out = grad + p.offA; k.ldo = p.in;
+                k.kind = SKINNY_ACC_T; k.alpha = inv_gscale; k.out = grad + p.offA; k.ldo = p.in;
                 run_rank(k, a);
             }
     }
@@ -540,15 +545,15 @@ struct act_ctx {
         // the cross-attention K/V projection reads only the conditioning: it runs on the side
         // stream, overlapping the self-attention half of the block
         on_side([&] {
-            GemmArgs k; k.mode = EPI_STORE_BF16; k.out = y.ckv; k.ldo = 2 * D;
-            proj_fwd(y.p[3], ctx_bf, crows, y.U[3], k);
+            GemmArgs k; k.mode = EPI_STORE_F16; k.out = y.ckv; k.ldo = 2 * D;
+            proj_fwd(y.p[3], ctx_h, crows, y.U[3], k);
         });
         // pre-norm self-attention
         timed(2, 0, 0, [&] { layernorm_fwd(y.xin, y.norm[0], y.norm[1], dit ? te : nullptr, T, y.h1, y.mu[0], y.rs[0], (int)rows, D, eps, stream); });
         {
             // q and k leave the projection already rotated (RoPE in the epilogue); DoRA keeps the
             // unrotated output for its row-norm gradient
-            GemmArgs e; e.mode = EPI_STORE_BF16; e.out = y.qkv; e.ldo = 3 * D;
+            GemmArgs e; e.mode = EPI_STORE_F16; e.out = y.qkv; e.ldo = 3 * D;
             if (dit) { e.rope = rope; e.rope_T = T; e.rope_cols = 2 * D; }
             if (y.p[0].dora) { e.aux = y.Yaux[0]; e.ldaux = 3 * D; }
             proj_fwd(y.p[0], y.h1, rows, y.U[0], e);
@@ -572,7 +577,7 @@ struct act_ctx {
         // cross-attention
         timed(2, 0, 0, [&] { layernorm_fwd(y.xmid, y.norm[2], y.norm[3], dit ? te : nullptr, T, y.hc, y.mu[1], y.rs[1], (int)rows, D, eps, stream); });
         {
-            GemmArgs e; e.mode = EPI_STORE_BF16; e.out = y.cq; e.ldo = D;
+            GemmArgs e; e.mode = EPI_STORE_F16; e.out = y.cq; e.ldo = D;
             proj_fwd(y.p[2], y.hc, rows, y.U[2], e);
         }
         join_side();
@@ -598,26 +603,26 @@ struct act_ctx {
                 GemmArgs e; e.mode = EPI_GELU; e.out = y.gact; e.ldo = F; e.aux = y.z; e.ldaux = F;
                 proj_fwd(y.p[5], y.f, rows, y.U[5], e);
             } else {
-                GemmArgs e; e.mode = EPI_STORE_BF16; e.out = y.z; e.ldo = F;
+                GemmArgs e; e.mode = EPI_STORE_F16; e.out = y.z; e.ldo = F;
                 proj_fwd(y.p[5], y.f, rows, y.U[5], e);
-                timed(2, 0, 6.0 * rows * F, [&] { gelu_fwd(gelu_tab, y.z, y.gact, rows * F, 1, stream); });
+                timed(2, 0, 6.0 * rows * F, [&] { gelu_fwd(y.z, y.gact, rows * F, 1, stream); });
             }
-            // the layer output also in bf16 where a skip projection reads it: as this layer's saved
+            // the layer output also in f16 where a skip projection reads it: as this layer's saved
             // copy (a skip source) or as the next layer's x_prev operand
             GemmArgs o; o.mode = EPI_RESID_F32; o.out = y.xout; o.ldo = D; o.resid = y.xmid2; o.ldr = D;
-            o.out_bf = y.produces ? y.xsave_bf : (writes_prev_bf(l) ? xprev_bf : nullptr);
+            o.out_h = y.produces ? y.xsave_h : (writes_prev_bf(l) ? xprev_h : nullptr);
             if (y.p[6].dora) { o.aux = y.Yaux[6]; o.ldaux = D; }
             proj_fwd(y.p[6], y.gact, rows, y.U[6], o);
         }
     }
 
-    // block l's ff.2 epilogue leaves bf16(xout) in xprev_bf for the skip projection of block l+1
+    // block l's ff.2 epilogue leaves f16(xout) in xprev_h for the skip projection of block l+1
     bool writes_prev_bf(int l) const { return !layers[l].produces && l + 1 < L && layers[l + 1].consumes; }
 
-    // Backward of block l.  On entry dx/dxbf hold d(loss)/d(xout) (dxbf already scaled by
-    // the DoRA factor of ff.2).  On exit dx holds d(loss)/d(xin) and dxbf is NOT prepared.
+    // Backward of block l.  On entry dx/dxh hold d(loss)/d(xout) (dxh already scaled by
+    // the DoRA factor of ff.2).  On exit dx holds d(loss)/d(xin) and dxh is NOT prepared.
     // need_dx_in: the gradient of the block's input is needed (accumulated into dx by the last
-    // norm's backward, which also writes dxbf = bf16((dx + cvt_extra) * cvt_scale) when cvt is
+    // norm's backward, which also writes dxh = f16((dx + cvt_extra) * cvt_scale) when cvt is
     // set: the operand of whatever consumes dx next, without a separate conversion pass)
     void block_bwd(int l, int n, const int* nvalid_dev, bool need_dx_in, bool cvt = false,
                    const float* cvt_extra = nullptr, const float* cvt_scale = nullptr) {
@@ -628,15 +633,15 @@ struct act_ctx {
         {
             GemmArgs e; e.mode = y.p[5].dora ? EPI_GELU_BWD : EPI_GELU_BWD_D; e.out = dz; e.ldo = F; e.auxin = y.z; e.ldauxin = F;
             e.colscale2 = y.p[5].dora ? y.p[5].g : nullptr;
-            proj_bwd(y.p[6], dxbf, rows, y.gact, y.U[6], y.Yaux[6], true, e);
+            proj_bwd(y.p[6], dxh, rows, y.gact, y.U[6], y.Yaux[6], true, e);
             GemmArgs d; d.mode = EPI_STORE_F32; d.out = dtmp; d.ldo = D;
             proj_bwd(y.p[5], dz, rows, y.f, y.U[5], y.z, true, d);
         }
-        timed(2, 0, 0, [&] { layernorm_bwd(dtmp, y.xmid2, y.norm[4], y.mu[2], y.rs[2], dx, 1, nullptr, dxbf, y.p[4].dora ? y.p[4].g : nullptr, (int)rows, D, stream); });
+        timed(2, 0, 0, [&] { layernorm_bwd(dtmp, y.xmid2, y.norm[4], y.mu[2], y.rs[2], dx, 1, nullptr, dxh, y.p[4].dora ? y.p[4].g : nullptr, (int)rows, D, stream); });
         // ---- cross-attention
         {
-            GemmArgs e; e.mode = EPI_STORE_BF16; e.out = dob; e.ldo = D;
-            proj_bwd(y.p[4], dxbf, rows, y.o2, y.U[4], y.Yaux[4], true, e);
+            GemmArgs e; e.mode = EPI_STORE_F16; e.out = dob; e.ldo = D;
+            proj_bwd(y.p[4], dxh, rows, y.o2, y.U[4], y.Yaux[4], true, e);
         }
         AttnArgs ca;
         ca.q = y.cq; ca.ldq = D; ca.k = y.ckv; ca.v = y.ckv + D; ca.ldk = ca.ldv = 2 * D;
@@ -661,11 +666,11 @@ struct act_ctx {
             }
         }
         // a single key block: each query row's dQ is final in one CTA and goes straight to dcq as
-        // bf16 (no fp32 accumulator to clear or convert)
+        // f16 (no fp32 accumulator to clear or convert)
         const bool dq_direct = C <= 64;
         if (dq_direct) {
-            ca.dq_bf = dcq;
-            ca.lddq_bf = D;
+            ca.dq_h = dcq;
+            ca.lddq_h = D;
             ca.dq_scale = y.p[2].dora ? y.p[2].g : nullptr;
         }
         ++path_count[ACT_PATH_ATTN_BWD_MMA];
@@ -676,16 +681,16 @@ struct act_ctx {
             if (split && need_dkv) attn_dkv_finish(ca, stream);
             if (!dq_direct) attn_dq_finish(ca, dcq, D, y.p[2].dora ? y.p[2].g : nullptr, stream);
         });
-        if (need_dkv) proj_bwd(y.p[3], dckv, crows, ctx_bf, y.U[3], y.ckv, false, GemmArgs());
+        if (need_dkv) proj_bwd(y.p[3], dckv, crows, ctx_h, y.U[3], y.ckv, false, GemmArgs());
         {
             GemmArgs e; e.mode = EPI_STORE_F32; e.out = dtmp; e.ldo = D;
             proj_bwd(y.p[2], dcq, rows, y.hc, y.U[2], y.cq, true, e);
         }
-        timed(2, 0, 0, [&] { layernorm_bwd(dtmp, y.xmid, y.norm[2], y.mu[1], y.rs[1], dx, 1, nullptr, dxbf, y.p[1].dora ? y.p[1].g : nullptr, (int)rows, D, stream); });
+        timed(2, 0, 0, [&] { layernorm_bwd(dtmp, y.xmid, y.norm[2], y.mu[1], y.rs[1], dx, 1, nullptr, dxh, y.p[1].dora ? y.p[1].g : nullptr, (int)rows, D, stream); });
         // ---- self-attention
         {
-            GemmArgs e; e.mode = EPI_STORE_BF16; e.out = dob; e.ldo = D;
-            proj_bwd(y.p[1], dxbf, rows, y.o1, y.U[1], y.Yaux[1], true, e);
+            GemmArgs e; e.mode = EPI_STORE_F16; e.out = dob; e.ldo = D;
+            proj_bwd(y.p[1], dxh, rows, y.o1, y.U[1], y.Yaux[1], true, e);
         }
         AttnArgs sa;
         sa.q = y.qkv; sa.k = y.qkv + D; sa.v = y.qkv + 2 * D; sa.ldq = sa.ldk = sa.ldv = 3 * D;
@@ -710,7 +715,7 @@ struct act_ctx {
         if (need_dx_in)
             timed(2, 0, 0, [&] {
                 layernorm_bwd(dtmp, y.xin, y.norm[0], y.mu[0], y.rs[0], dx, 1, cvt ? cvt_extra : nullptr,
-                              cvt ? dxbf : nullptr, cvt ? cvt_scale : nullptr, (int)rows, D, stream);
+                              cvt ? dxh : nullptr, cvt ? cvt_scale : nullptr, (int)rows, D, stream);
             });
     }
 
@@ -721,12 +726,12 @@ struct act_ctx {
         return f;
     }
 
-    // dxbf := bf16((dx + dsaved[l]) * g_ff2(l))  -- entering block l's backward
+    // dxh := f16((dx + dsaved[l]) * g_ff2(l))  -- entering block l's backward
     const float* entry_extra(int l) { return layers[l].produces ? layers[l].dsaved : nullptr; }
     const float* entry_scale(int l) { return layers[l].p[6].dora ? layers[l].p[6].g : nullptr; }
     void prepare_dxbf(int l, int n) {
         const long rows = (long)n * T;
-        timed(2, 0, 0, [&] { residual_to_bf16(dx, entry_extra(l), dxbf, entry_scale(l), (int)rows, D, stream); });
+        timed(2, 0, 0, [&] { residual_to_f16(dx, entry_extra(l), dxh, entry_scale(l), (int)rows, D, stream); });
     }
 
     void mf_graph_body(int n) {
@@ -736,12 +741,12 @@ struct act_ctx {
             mf_inputs(d_clean, d_noise, d_t, n, T, md.latent_dim, x0, vstar, stream);
             linear_f32(d_tfeat, te0, te1, n, D, md.time_dim, 1, stream);
             linear_f32(te1, te2, te, n, D, D, 0, stream);
-            f32_to_bf16(d_hidden, hidden_bf, crows * md.cond_dim, stream);
+            f32_to_f16(d_hidden, hidden_h, crows * md.cond_dim, stream);
         });
         {
             GemmArgs c;  // context = hidden cond_proj^T + bias
-            c.M = (int)crows; c.N = D; c.K1 = md.cond_dim; c.A1 = hidden_bf; c.lda1 = md.cond_dim;
-            c.B1 = cond_w; c.ldb1 = md.cond_dim; c.mode = EPI_BIAS_BF16; c.bias = cond_b; c.out = ctx_bf; c.ldo = D;
+            c.M = (int)crows; c.N = D; c.K1 = md.cond_dim; c.A1 = hidden_h; c.lda1 = md.cond_dim;
+            c.B1 = cond_w; c.ldb1 = md.cond_dim; c.mode = EPI_BIAS_F16; c.bias = cond_b; c.out = ctx_h; c.ldo = D;
             run_gemm(c, 0);
             GemmArgs x;  // in_proj
             x.M = (int)rows; x.N = D; x.K1 = md.latent_dim; x.A1 = x0; x.lda1 = md.latent_dim;
@@ -752,10 +757,10 @@ struct act_ctx {
             Layer& y = layers[l];
             if (y.consumes) {
                 if (!writes_prev_bf(l - 1))
-                    timed(2, 0, 0, [&] { residual_to_bf16(layers[l - 1].xout, nullptr, xprev_bf, nullptr, (int)rows, D, stream); });
+                    timed(2, 0, 0, [&] { residual_to_f16(layers[l - 1].xout, nullptr, xprev_h, nullptr, (int)rows, D, stream); });
                 GemmArgs k;
                 k.M = (int)rows; k.N = D; k.K1 = D; k.K2 = D;
-                k.A1 = xprev_bf; k.lda1 = D; k.A2 = layers[y.src].xsave_bf; k.lda2 = D;
+                k.A1 = xprev_h; k.lda1 = D; k.A2 = layers[y.src].xsave_h; k.lda2 = D;
                 k.B1 = skip[y.proj]; k.ldb1 = 2 * D; k.B2 = skip[y.proj] + D; k.ldb2 = 2 * D;
                 k.mode = EPI_STORE_F32; k.out = y.xin; k.ldo = D;
                 run_gemm(k, 0);
@@ -770,7 +775,7 @@ struct act_ctx {
             o.mode = EPI_STORE_F32; o.out = outp; o.ldo = md.latent_dim;
             run_gemm(o, 0);
         }
-        timed(2, 0, 0, [&] { mf_loss(outp, vstar, n, T, md.latent_dim, d_loss, dout, loss_part, stream); });
+        timed(2, 0, 0, [&] { mf_loss(outp, vstar, n, T, md.latent_dim, d_loss, dout, loss_part, gscale, stream); });
         // ---------------- backward
         {
             GemmArgs d;
@@ -781,22 +786,22 @@ struct act_ctx {
         timed(2, 0, 0, [&] {
             for (auto& y : layers)
                 if (y.produces) CK(cudaMemsetAsync(y.dsaved, 0, sizeof(float) * rows * D, stream));
-            // also block L-1's entry operand dxbf (see block_bwd's cvt)
-            layernorm_bwd(dtmp, last.xout, onw, muo, rso, dx, 0, entry_extra(L - 1), dxbf, entry_scale(L - 1),
+            // also block L-1's entry operand dxh (see block_bwd's cvt)
+            layernorm_bwd(dtmp, last.xout, onw, muo, rso, dx, 0, entry_extra(L - 1), dxh, entry_scale(L - 1),
                           (int)rows, D, stream);
         });
         const int first = ad.first_layer;
         for (int l = L - 1; l >= first; --l) {
             Layer& y = layers[l];
             const bool need_dx = l > first, via_skip = need_dx && y.consumes;
-            // the block's last norm backward writes the next operand: bf16(dx) for the skip
+            // the block's last norm backward writes the next operand: f16(dx) for the skip
             // projection, else block l-1's entry operand
             if (via_skip) block_bwd(l, n, d_nvalid, need_dx, true, nullptr, nullptr);
             else if (need_dx) block_bwd(l, n, d_nvalid, need_dx, true, entry_extra(l - 1), entry_scale(l - 1));
             else block_bwd(l, n, d_nvalid, need_dx);
             if (via_skip) {
                 GemmArgs a;  // d x_prev = dx Wskip[:, :D]
-                a.M = (int)rows; a.N = D; a.K1 = D; a.A1 = dxbf; a.lda1 = D;
+                a.M = (int)rows; a.N = D; a.K1 = D; a.A1 = dxh; a.lda1 = D;
                 a.B1 = skip[y.proj]; a.ldb1 = 2 * D; a.b_kmajor = false; a.mode = EPI_STORE_F32; a.out = dx; a.ldo = D;
                 run_gemm(a, 0);
                 GemmArgs b = a;  // d saved += dx Wskip[:, D:]
@@ -815,7 +820,7 @@ struct act_ctx {
         prepare_adapters();
         timed(2, 0, 0, [&] {
             mg_embed(d_ids, T, nq, emb_dev, pos, x0f, D, n, stream);
-            f32_to_bf16(d_ctx, ctx_bf, crows * D, stream);
+            f32_to_f16(d_ctx, ctx_h, crows * D, stream);
         });
         for (int l = 0; l < L; ++l) block_fwd(l, n, nullptr);
         Layer& last = layers[L - 1];
@@ -829,14 +834,14 @@ struct act_ctx {
             for (int q = 0; q < nq; ++q) {
                 const long r0 = (long)b * T + q + prefix;  // rows s = q + prefix .. q + frames - 1
                 float* lg = logits + ((long)(b * nq + q) * sel) * card;
-                bf16* dl = dlogits + ((long)(b * nq + q) * sel) * card;
+                f16* dl = dlogits + ((long)(b * nq + q) * sel) * card;
                 GemmArgs hgm;
                 hgm.M = sel; hgm.N = card; hgm.K1 = D; hgm.A1 = xo + r0 * D; hgm.lda1 = D;
                 hgm.B1 = head[q]; hgm.ldb1 = D; hgm.mode = EPI_STORE_F32; hgm.out = lg; hgm.ldo = card;
                 run_gemm(hgm, 0);
                 timed(2, 0, 0, [&] {
                     mg_cross_entropy(lg, sel, card, d_tgt + (long)(b * nq + q) * sel, sel * nq, inv_nsel,
-                                     d_loss + b, dl, stream);
+                                     d_loss + b, dl, gscale, stream);
                 });
                 GemmArgs dg;
                 dg.M = sel; dg.N = D; dg.K1 = card; dg.A1 = dl; dg.lda1 = card;
@@ -845,7 +850,7 @@ struct act_ctx {
                 run_gemm(dg, 0);
             }
         timed(2, 0, 0, [&] {
-            layernorm_bwd(dtmp, last.xout, onw, muo, rso, dx, 0, entry_extra(L - 1), dxbf, entry_scale(L - 1),
+            layernorm_bwd(dtmp, last.xout, onw, muo, rso, dx, 0, entry_extra(L - 1), dxh, entry_scale(L - 1),
                           (int)rows, D, stream);
         });
         const int first = ad.first_layer;
@@ -1056,6 +1061,13 @@ struct act_ctx {
         C = ad.tokens; B = ad.max_batch;
         T = mf ? ad.frames : ad.frames + md.n_q - 1;  // MusicGen: pattern steps - 1 (src/mg/train.h:74)
         RP = (ad.rank + 31) / 32 * 32;
+        {
+            // gradient scale: the power of two nearest the loss's divisor, so that the scaled
+            // seed gradient is O(1) (an exact power of two: unscaling adds no rounding)
+            const double divisor = mf ? (double)T * md.latent_dim : (double)md.n_q * (ad.frames - ad.prefix_frames);
+            gscale = std::ldexp(1.0f, (int)std::lround(std::log2(std::max(divisor, 1.0))));
+            inv_gscale = 1.0f / gscale;
+        }
         M = (long)B * T;
         MC = (long)B * C;
         layers.resize(L);
@@ -1090,7 +1102,7 @@ struct act_ctx {
         if (!cname || !host) throw Error(ACT_ERR_INVALID, "null weight");
         const std::string name = cname;
         long rows = 0, cols = 0;
-        enum { DST_BF16, DST_F32, DST_HOST } dst_kind = DST_BF16;
+        enum { DST_F16, DST_F32, DST_HOST } dst_kind = DST_F16;
         void** dst = nullptr;
         Proj* proj = nullptr;
         const std::string pre = mf ? "dit." : "lm.";
@@ -1165,7 +1177,7 @@ struct act_ctx {
         if (bound.count(name)) throw Error(ACT_ERR_INVALID, "weight bound twice: " + name);
         // host fp32 view (DoRA norms, fp32 destinations, rope factors)
         const bool dora_proj = proj && ad.type == ACT_ADAPTER_DORA_ROWS;
-        if (dst_kind != DST_BF16 || dora_proj) {
+        if (dst_kind != DST_F16 || dora_proj) {
             f32.resize(n);
             if (type == ACT_TYPE_F32) std::memcpy(f32.data(), host, n * 4);
             else if (type == ACT_TYPE_F16) {
@@ -1187,13 +1199,13 @@ struct act_ctx {
             CK(cudaStreamSynchronize(stream));
             *dst = d;
         } else {
-            bf16* d = dalloc<bf16>(n);
+            f16* d = dalloc<f16>(n);
             void* tmp = nullptr;
             CK(cudaMalloc(&tmp, need));
             CK(cudaMemcpyAsync(tmp, host, need, cudaMemcpyHostToDevice, stream));
-            if (type == ACT_TYPE_F32) f32_to_bf16(static_cast<float*>(tmp), d, n, stream);
-            else if (type == ACT_TYPE_F16) f16_to_bf16(static_cast<uint16_t*>(tmp), n, d, stream);
-            else q8_0_to_bf16(static_cast<uint8_t*>(tmp), n / 32, d, stream);
+            if (type == ACT_TYPE_F32) f32_to_f16(static_cast<float*>(tmp), d, n, stream);
+            else if (type == ACT_TYPE_F16) CK(cudaMemcpyAsync(d, tmp, need, cudaMemcpyDeviceToDevice, stream));
+            else q8_0_to_f16(static_cast<uint8_t*>(tmp), n / 32, d, stream);
             CK(cudaStreamSynchronize(stream));
             CK(cudaFree(tmp));
             *dst = d;
@@ -1332,10 +1344,10 @@ struct act_ctx {
         for (auto& lay : layers)
             for (auto& p : lay.p) {
                 if (!p.adapted) continue;
-                p.A_bf = dalloc<bf16>((size_t)RP * p.in);
-                p.B_bf = dalloc<bf16>((size_t)p.out * RP);
-                jobs.push_back({value + p.offA, p.A_bf, p.r, p.in, p.in});
-                jobs.push_back({value + p.offB, p.B_bf, p.out, p.r, RP});
+                p.A_h = dalloc<f16>((size_t)RP * p.in);
+                p.B_h = dalloc<f16>((size_t)p.out * RP);
+                jobs.push_back({value + p.offA, p.A_h, p.r, p.in, p.in});
+                jobs.push_back({value + p.offB, p.B_h, p.out, p.r, RP});
                 max_job = std::max(max_job, std::max(p.r * p.in, p.out * p.r));
                 if (p.dora) {
                     p.P = dalloc<float>((size_t)p.out * RP);
@@ -1345,15 +1357,13 @@ struct act_ctx {
                     p.g = dalloc<float>(p.out);
                     p.dg = dalloc<float>(p.out);
                     p.scr = dalloc<float>((size_t)p.out + p.r * p.r);
-                    p.BD = dalloc<bf16>((size_t)p.out * RP);
+                    p.BD = dalloc<f16>((size_t)p.out * RP);
                 }
             }
         njobs = (int)jobs.size();
         jobs_dev = dalloc<CopyJob>(std::max(njobs, 1));
         if (njobs) CK(cudaMemcpyAsync(jobs_dev, jobs.data(), sizeof(CopyJob) * njobs, cudaMemcpyHostToDevice, stream));
         // rope table (src/ac/transformer.h:55-61 with freq_base 1): theta = pos / ff[i]
-        gelu_tab = dalloc<uint32_t>(GELU_TABLE_WORDS);
-        gelu_table_init(gelu_tab, stream);
         if (mf) {
             if ((int)rope_ff.size() != md.head_dim / 2) throw Error(ACT_ERR_INVALID, "rope_freq_factors size mismatch");
             std::vector<float> tab((size_t)T * 64);
@@ -1400,53 +1410,53 @@ struct act_ctx {
                 y.mu[i] = dalloc<float>(Mr);
                 y.rs[i] = dalloc<float>(Mr);
             }
-            y.h1 = dalloc<bf16>(Mr * D);
-            y.hc = dalloc<bf16>(Mr * D);
-            y.f = dalloc<bf16>(Mr * D);
-            y.qkv = dalloc<bf16>(Mr * 3 * D);
-            y.o1 = dalloc<bf16>(Mr * D);
-            y.cq = dalloc<bf16>(Mr * D);
-            y.ckv = dalloc<bf16>(Cr * 2 * D);
-            y.o2 = dalloc<bf16>(Mr * D);
-            y.z = dalloc<bf16>(Mr * F);
-            y.gact = dalloc<bf16>(Mr * F);
+            y.h1 = dalloc<f16>(Mr * D);
+            y.hc = dalloc<f16>(Mr * D);
+            y.f = dalloc<f16>(Mr * D);
+            y.qkv = dalloc<f16>(Mr * 3 * D);
+            y.o1 = dalloc<f16>(Mr * D);
+            y.cq = dalloc<f16>(Mr * D);
+            y.ckv = dalloc<f16>(Cr * 2 * D);
+            y.o2 = dalloc<f16>(Mr * D);
+            y.z = dalloc<f16>(Mr * F);
+            y.gact = dalloc<f16>(Mr * F);
             y.lse1 = dalloc<float>((long)B * H * T);
             y.lse2 = dalloc<float>((long)B * H * T);
             for (int t = 0; t < 7; ++t) {
                 if (!y.p[t].adapted) continue;
-                y.U[t] = dalloc<bf16>((t == 3 ? Cr : Mr) * RP);
-                if (y.p[t].dora && (t == 0 || t == 1 || t == 4 || t == 6)) y.Yaux[t] = dalloc<bf16>(Mr * y.p[t].out);
+                y.U[t] = dalloc<f16>((t == 3 ? Cr : Mr) * RP);
+                if (y.p[t].dora && (t == 0 || t == 1 || t == 4 || t == 6)) y.Yaux[t] = dalloc<f16>(Mr * y.p[t].out);
             }
             if (y.produces) {
-                y.xsave_bf = dalloc<bf16>(Mr * D);
+                y.xsave_h = dalloc<f16>(Mr * D);
                 y.dsaved = dalloc<float>(Mr * D);
             }
         }
         if (!x0f) x0f = layers[0].xin;
         const int lat = mf ? md.latent_dim : 8;
-        x0 = dalloc<bf16>(Mr * lat);
+        x0 = dalloc<f16>(Mr * lat);
         vstar = dalloc<float>(Mr * lat);
         te1 = dalloc<float>((long)B * D);
         te = dalloc<float>((long)B * D);
-        if (mf) hidden_bf = dalloc<bf16>(Cr * md.cond_dim);
-        ctx_bf = dalloc<bf16>(Cr * D);
-        xo = dalloc<bf16>(Mr * D);
+        if (mf) hidden_h = dalloc<f16>(Cr * md.cond_dim);
+        ctx_h = dalloc<f16>(Cr * D);
+        xo = dalloc<f16>(Mr * D);
         muo = dalloc<float>(Mr);
         rso = dalloc<float>(Mr);
         outp = dalloc<float>(Mr * lat);
-        dout = dalloc<bf16>(Mr * lat);
-        xprev_bf = dalloc<bf16>(Mr * D);
+        dout = dalloc<f16>(Mr * lat);
+        xprev_h = dalloc<f16>(Mr * D);
         dx = dalloc<float>(Mr * D);
         dtmp = dalloc<float>(Mr * D);
         dq_acc = dalloc<float>(Mr * D);
         dvec = dalloc<float>((long)B * H * T);
-        dxbf = dalloc<bf16>(Mr * D);
-        dz = dalloc<bf16>(Mr * F);
-        dU = dalloc<bf16>(std::max(Mr, Cr) * RP);
-        dob = dalloc<bf16>(Mr * D);
-        dqkv = dalloc<bf16>(Mr * 3 * D);
-        dcq = dalloc<bf16>(Mr * D);
-        dckv = dalloc<bf16>(Cr * 2 * D);
+        dxh = dalloc<f16>(Mr * D);
+        dz = dalloc<f16>(Mr * F);
+        dU = dalloc<f16>(std::max(Mr, Cr) * RP);
+        dob = dalloc<f16>(Mr * D);
+        dqkv = dalloc<f16>(Mr * 3 * D);
+        dcq = dalloc<f16>(Mr * D);
+        dckv = dalloc<f16>(Cr * 2 * D);
         dkv_acc = dalloc<float>(Cr * 2 * D);
         d_loss = dalloc<float>(B);
         loss_part = dalloc<float>((long)B * 32);
@@ -1468,7 +1478,7 @@ struct act_ctx {
             d_tgt = dalloc<int32_t>((size_t)B * md.n_q * sel);
             d_ctx = dalloc<float>((size_t)Cr * D);
             logits = dalloc<float>((size_t)B * md.n_q * sel * md.card);
-            dlogits = dalloc<bf16>((size_t)B * md.n_q * sel * md.card);
+            dlogits = dalloc<f16>((size_t)B * md.n_q * sel * md.card);
         }
         CK(cudaStreamSynchronize(stream));
     }
@@ -1802,26 +1812,31 @@ int act_reset_kernel_stats(act_ctx* ctx) {
 
 double act_step_flops(act_ctx* ctx, int n) { return ctx && ctx->finalized ? ctx->step_flops(n) : -1.0; }
 
-int act_gelu_bf16(int device, const uint16_t* z, uint16_t* g, uint16_t* dg, int64_t n, int direct) {
-    void *dz = nullptr, *dgo = nullptr, *ddg = nullptr, *tab = nullptr;
+int act_gelu_f16(int device, const uint16_t* z, uint16_t* g, uint16_t* dg, int64_t n, int direct) {
+    void *dz = nullptr, *dgo = nullptr, *ddg = nullptr;
     cudaStream_t st = nullptr;
     auto cleanup = [&] {
         if (st) cudaStreamSynchronize(st);
-        cudaFree(dz); cudaFree(dgo); cudaFree(ddg); cudaFree(tab);
+        cudaFree(dz); cudaFree(dgo); cudaFree(ddg);
         if (st) cudaStreamDestroy(st);
     };
     try {
         if (!z || !g || !dg || n <= 0) throw Error(ACT_ERR_INVALID, "invalid GELU arguments");
         CK(cudaSetDevice(device));
         CK(cudaStreamCreate(&st));
-        CK(cudaMalloc(&dz, n * 2));
-        CK(cudaMalloc(&dgo, n * 2));
-        CK(cudaMalloc(&ddg, n * 2));
-        CK(cudaMalloc(&tab, GELU_TABLE_WORDS * 4));
-        gelu_table_init(static_cast<uint32_t*>(tab), st);
+        const int64_t n8 = (n + 7) / 8 * 8;  // the step's pass works on 8 values per thread
+        CK(cudaMalloc(&dz, n8 * 2));
+        CK(cudaMalloc(&dgo, n8 * 2));
+        CK(cudaMalloc(&ddg, n8 * 2));
+        CK(cudaMemsetAsync(dz, 0, n8 * 2, st));
         CK(cudaMemcpyAsync(dz, z, n * 2, cudaMemcpyHostToDevice, st));
-        gelu_check(static_cast<const uint32_t*>(tab), static_cast<const uint16_t*>(dz), static_cast<uint16_t*>(dgo),
-                   static_cast<uint16_t*>(ddg), n, direct, st);
+        if (direct) {
+            gelu_check(static_cast<const uint16_t*>(dz), static_cast<uint16_t*>(dgo), static_cast<uint16_t*>(ddg), n,
+                       st);
+        } else {  // the training step's pass: gelu into dgo, gelu' over the input in place
+            gelu_fwd(static_cast<f16*>(dz), static_cast<f16*>(dgo), n8, 1, st);
+            CK(cudaMemcpyAsync(ddg, dz, n8 * 2, cudaMemcpyDeviceToDevice, st));
+        }
         CK(cudaGetLastError());
         CK(cudaMemcpyAsync(g, dgo, n * 2, cudaMemcpyDeviceToHost, st));
         CK(cudaMemcpyAsync(dg, ddg, n * 2, cudaMemcpyDeviceToHost, st));
@@ -1839,7 +1854,7 @@ int act_gelu_bf16(int device, const uint16_t* z, uint16_t* g, uint16_t* dg, int6
     }
 }
 
-int act_rank_gemm_bf16(int device, int kind, const void* A, const void* B, float* C, int M, int K, int nb, int a_mn,
+int act_rank_gemm_f16(int device, int kind, const void* A, const void* B, float* C, int M, int K, int nb, int a_mn,
                        int b_mn, float alpha, int splits, int reps, float* ms_per_call) {
     void *dA = nullptr, *dB = nullptr, *dC = nullptr;
     int* derr = nullptr;
@@ -1864,8 +1879,8 @@ int act_rank_gemm_bf16(int device, int kind, const void* A, const void* B, float
         CK(cudaMemcpyAsync(dB, B, (size_t)nb * K * 2, cudaMemcpyHostToDevice, st));
         SkinnyArgs g;
         g.M = M; g.K = K; g.nb = nb;
-        g.A = static_cast<const bf16*>(dA); g.lda = a_mn ? M : K; g.a_mn = a_mn != 0;
-        g.B = static_cast<const bf16*>(dB); g.ldb = b_mn ? nb : K; g.b_mn = b_mn != 0;
+        g.A = static_cast<const f16*>(dA); g.lda = a_mn ? M : K; g.a_mn = a_mn != 0;
+        g.B = static_cast<const f16*>(dB); g.ldb = b_mn ? nb : K; g.b_mn = b_mn != 0;
         g.kind = kind; g.alpha = alpha; g.out = dC; g.ldo = kind == SKINNY_ACC_T ? M : nb;
         g.splits = splits;
         if (kind == SKINNY_STORE) {
@@ -1901,13 +1916,10 @@ int act_rank_gemm_bf16(int device, int kind, const void* A, const void* B, float
         }
         if (kind == SKINNY_STORE) {
             std::vector<uint16_t> hb(cn);
-            // the bf16 result occupies the first cn * 2 bytes of dC (row stride nb)
+            // the f16 result occupies the first cn * 2 bytes of dC (row stride nb)
             CK(cudaMemcpyAsync(hb.data(), dC, cn * 2, cudaMemcpyDeviceToHost, st));
             CK(cudaStreamSynchronize(st));
-            for (size_t i = 0; i < cn; ++i) {
-                const uint32_t w = (uint32_t)hb[i] << 16;
-                std::memcpy(&C[i], &w, 4);
-            }
+            for (size_t i = 0; i < cn; ++i) C[i] = act_ctx::half_to_float(hb[i]);
         } else {
             CK(cudaMemcpyAsync(C, dC, cn * 4, cudaMemcpyDeviceToHost, st));
         }
@@ -1928,9 +1940,9 @@ int act_rank_gemm_bf16(int device, int kind, const void* A, const void* B, float
     }
 }
 
-int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path,
+int act_gemm_f16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path,
                   int reps, float* ms_per_call) {
-    // Stand-alone check of the projection GEMM: C[M][N] (fp32) = A[M][K] . B(n,k), bf16 inputs,
+    // Stand-alone check of the projection GEMM: C[M][N] (fp32) = A[M][K] . B(n,k), f16 inputs,
     // B given as [N][K] (b_mn_major = 0) or [K][N] (1).  path 0 auto, 1 mma.sync, 2 tcgen05,
     // 3 2-CTA (stream-K where it pays), 4 2-CTA 128-wide, 5 2-CTA whole tiles only.
     void *dA = nullptr, *dB = nullptr, *dC = nullptr, *dsk = nullptr, *dflag = nullptr;
@@ -1954,8 +1966,8 @@ int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int 
         CK(cudaMemcpyAsync(dB, B, (size_t)N * K * 2, cudaMemcpyHostToDevice, st));
         GemmArgs g;
         g.M = M; g.N = N; g.K1 = K;
-        g.A1 = static_cast<const bf16*>(dA); g.lda1 = K;
-        g.B1 = static_cast<const bf16*>(dB); g.ldb1 = b_mn_major ? N : K; g.b_kmajor = !b_mn_major;
+        g.A1 = static_cast<const f16*>(dA); g.lda1 = K;
+        g.B1 = static_cast<const f16*>(dB); g.ldb1 = b_mn_major ? N : K; g.b_kmajor = !b_mn_major;
         g.mode = EPI_STORE_F32; g.out = dC; g.ldo = N;
         const bool tc = path >= 2 || (path == 0 && gemm_tc_supported(g));
         if (tc && !gemm_tc_supported(g)) throw Error(ACT_ERR_INVALID, "shape not supported by the tcgen05 path");
@@ -2053,9 +2065,9 @@ int act_attention(int device, const void* q, const void* k, const void* v, const
             return d;
         };
         AttnArgs a;
-        a.q = static_cast<const bf16*>(up(q, rq * D * 2));
-        a.k = static_cast<const bf16*>(up(k, rk * D * 2));
-        a.v = static_cast<const bf16*>(up(v, rk * D * 2));
+        a.q = static_cast<const f16*>(up(q, rq * D * 2));
+        a.k = static_cast<const f16*>(up(k, rk * D * 2));
+        a.v = static_cast<const f16*>(up(v, rk * D * 2));
         a.ldq = a.ldk = a.ldv = D;
         a.T = T; a.Tk = Tk; a.H = H; a.clips = clips;
         a.nvalid = nvalid ? static_cast<const int*>(up(nvalid, clips * 4)) : nullptr;
@@ -2064,7 +2076,7 @@ int act_attention(int device, const void* q, const void* k, const void* v, const
         a.rope_load = rope ? 1 : 0;  // unrotated inputs: rotate while staging
         if (rope && Tk > T) throw Error(ACT_ERR_INVALID, "RoPE needs Tk <= T");
         a.scale = 0.125f;
-        a.o = static_cast<bf16*>(up(nullptr, rq * D * 2));
+        a.o = static_cast<f16*>(up(nullptr, rq * D * 2));
         a.ldo = D;
         a.lse = static_cast<float*>(up(nullptr, rq * H * 4));
         int* derr = static_cast<int*>(up(nullptr, sizeof(int)));
@@ -2075,17 +2087,17 @@ int act_attention(int device, const void* q, const void* k, const void* v, const
         CK(cudaEventRecord(ev[1], st));
         CK(cudaGetLastError());
         const bool bwd = dout && dq && dk && dv;
-        bf16* ddq = nullptr;
+        f16* ddq = nullptr;
         if (bwd) {
-            a.dout = static_cast<const bf16*>(up(dout, rq * D * 2));
+            a.dout = static_cast<const f16*>(up(dout, rq * D * 2));
             a.lddo = D;
             a.dvec = static_cast<float*>(up(nullptr, rq * H * 4));
             a.dq_acc = static_cast<float*>(up(nullptr, rq * D * 4));
             a.ldq_acc = D;
-            a.dk = static_cast<bf16*>(up(nullptr, rk * D * 2));
-            a.dv = static_cast<bf16*>(up(nullptr, rk * D * 2));
+            a.dk = static_cast<f16*>(up(nullptr, rk * D * 2));
+            a.dv = static_cast<f16*>(up(nullptr, rk * D * 2));
             a.lddk = a.lddv = D;
-            ddq = static_cast<bf16*>(up(nullptr, rq * D * 2));
+            ddq = static_cast<f16*>(up(nullptr, rq * D * 2));
             CK(cudaEventRecord(ev[2], st));
             if (attn_bwd_tc_supported(a) && !std::getenv("ACTRAIN_ATTN_MMA")) {
                 attn_bwd_tc(a, derr, st);
@@ -2161,7 +2173,7 @@ int act_mg_staged(act_ctx* ctx, int32_t* ids, size_t n_ids, int32_t* targets, si
     });
 }
 
-int act_q8_0_dequant(int device, const void* blocks, int64_t nblocks, float* out_f32, uint16_t* out_bf16) {
+int act_q8_0_dequant(int device, const void* blocks, int64_t nblocks, float* out_f32, uint16_t* out_f16) {
     void *db = nullptr, *df = nullptr, *dh = nullptr;
     cudaStream_t st = nullptr;
     auto cleanup = [&] {
@@ -2170,7 +2182,7 @@ int act_q8_0_dequant(int device, const void* blocks, int64_t nblocks, float* out
         if (st) cudaStreamDestroy(st);
     };
     try {
-        if (!blocks || nblocks <= 0 || (!out_f32 && !out_bf16)) throw Error(ACT_ERR_INVALID, "invalid Q8_0 arguments");
+        if (!blocks || nblocks <= 0 || (!out_f32 && !out_f16)) throw Error(ACT_ERR_INVALID, "invalid Q8_0 arguments");
         CK(cudaSetDevice(device));
         CK(cudaStreamCreate(&st));
         const size_t n = (size_t)nblocks * 32;
@@ -2181,10 +2193,10 @@ int act_q8_0_dequant(int device, const void* blocks, int64_t nblocks, float* out
             q8_0_to_f32(static_cast<const uint8_t*>(db), nblocks, static_cast<float*>(df), st);
             CK(cudaMemcpyAsync(out_f32, df, n * 4, cudaMemcpyDeviceToHost, st));
         }
-        if (out_bf16) {
+        if (out_f16) {
             CK(cudaMalloc(&dh, n * 2));
-            q8_0_to_bf16(static_cast<const uint8_t*>(db), nblocks, static_cast<bf16*>(dh), st);
-            CK(cudaMemcpyAsync(out_bf16, dh, n * 2, cudaMemcpyDeviceToHost, st));
+            q8_0_to_f16(static_cast<const uint8_t*>(db), nblocks, static_cast<f16*>(dh), st);
+            CK(cudaMemcpyAsync(out_f16, dh, n * 2, cudaMemcpyDeviceToHost, st));
         }
         CK(cudaGetLastError());
         CK(cudaStreamSynchronize(st));

@@ -1,4 +1,4 @@
-// gemm_mma.cu -- generic bf16 GEMM on the warp-level tensor-core path (mma.sync m16n8k16).
+// gemm_mma.cu -- generic f16 GEMM on the warp-level tensor-core path (mma.sync m16n8k16).
 //
 // Covers every operand layout the training step needs (forward Y = X W^T, input gradient
 // dX = dY W, adapter gradients dB = dY^T U and dA = dU^T X), a second K segment for the
@@ -35,7 +35,7 @@ gemm_mma_kernel(const GemmArgs p) {
     static_assert(NI % 2 == 0, "warp tile N must be a multiple of 16");
     using S = Smem<BM, BN, AK, BKM, BK, STAGES>;
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    bf16* smem = reinterpret_cast<bf16*>(smem_raw);
+    f16* smem = reinterpret_cast<f16*>(smem_raw);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int wm = warp / WN_, wn = warp % WN_;
@@ -49,13 +49,13 @@ gemm_mma_kernel(const GemmArgs p) {
     auto load_tile = [&](int t, int stage) {
         const int kt = kbeg + t;
         const bool seg2 = kt >= kt1;
-        const bf16* A = seg2 ? p.A2 : p.A1;
-        const bf16* B = seg2 ? p.B2 : p.B1;
+        const f16* A = seg2 ? p.A2 : p.A1;
+        const f16* B = seg2 ? p.B2 : p.B1;
         const long lda = seg2 ? p.lda2 : p.lda1, ldb = seg2 ? p.ldb2 : p.ldb1;
         const int Kseg = seg2 ? p.K2 : p.K1;
         const int k0 = (seg2 ? kt - kt1 : kt) * BK;
-        bf16* sA = smem + stage * S::STAGE;
-        bf16* sB = sA + S::A_ELEMS;
+        f16* sA = smem + stage * S::STAGE;
+        f16* sB = sA + S::A_ELEMS;
         if (AK) {
             for (int c = tid; c < BM * (BK / 8); c += NT) {
                 const int r = c / (BK / 8), kc = (c % (BK / 8)) * 8;
@@ -108,8 +108,8 @@ gemm_mma_kernel(const GemmArgs p) {
         __syncthreads();
         if (t + STAGES - 1 < ntiles) load_tile(t + STAGES - 1, (t + STAGES - 1) % STAGES);
         cp_async_commit();
-        const bf16* sA = smem + (t % STAGES) * S::STAGE;
-        const bf16* sB = sA + S::A_ELEMS;
+        const f16* sA = smem + (t % STAGES) * S::STAGE;
+        const f16* sB = sA + S::A_ELEMS;
 #pragma unroll
         for (int kk = 0; kk < BK; kk += 16) {
             uint32_t af[MI][4];
@@ -117,10 +117,10 @@ gemm_mma_kernel(const GemmArgs p) {
             for (int mi = 0; mi < MI; ++mi) {
                 const int mb = wm * WTM + mi * 16;
                 if (AK) {
-                    const bf16* ptr = sA + (mb + lr + 8 * (lsel & 1)) * (BK + 8) + kk + 8 * (lsel >> 1);
+                    const f16* ptr = sA + (mb + lr + 8 * (lsel & 1)) * (BK + 8) + kk + 8 * (lsel >> 1);
                     ldsm_x4(af[mi][0], af[mi][1], af[mi][2], af[mi][3], ptr);
                 } else {
-                    const bf16* ptr = sA + (kk + lr + 8 * (lsel >> 1)) * (BM + 8) + mb + 8 * (lsel & 1);
+                    const f16* ptr = sA + (kk + lr + 8 * (lsel >> 1)) * (BM + 8) + mb + 8 * (lsel & 1);
                     ldsm_x4_t(af[mi][0], af[mi][1], af[mi][2], af[mi][3], ptr);
                 }
             }
@@ -129,16 +129,16 @@ gemm_mma_kernel(const GemmArgs p) {
                 const int nb = wn * WTN + nj * 16;
                 uint32_t b0, b1, b2, b3;
                 if (BKM) {
-                    const bf16* ptr = sB + (nb + lr + 8 * (lsel >> 1)) * (BK + 8) + kk + 8 * (lsel & 1);
+                    const f16* ptr = sB + (nb + lr + 8 * (lsel >> 1)) * (BK + 8) + kk + 8 * (lsel & 1);
                     ldsm_x4(b0, b1, b2, b3, ptr);
                 } else {
-                    const bf16* ptr = sB + (kk + lr + 8 * (lsel & 1)) * (BN + 8) + nb + 8 * (lsel >> 1);
+                    const f16* ptr = sB + (kk + lr + 8 * (lsel & 1)) * (BN + 8) + nb + 8 * (lsel >> 1);
                     ldsm_x4_t(b0, b1, b2, b3, ptr);
                 }
 #pragma unroll
                 for (int mi = 0; mi < MI; ++mi) {
-                    mma_bf16(acc[mi][2 * nj], af[mi], b0, b1);
-                    mma_bf16(acc[mi][2 * nj + 1], af[mi], b2, b3);
+                    mma_sync_f16(acc[mi][2 * nj], af[mi], b0, b1);
+                    mma_sync_f16(acc[mi][2 * nj + 1], af[mi], b2, b3);
                 }
             }
         }
@@ -163,9 +163,9 @@ gemm_mma_kernel(const GemmArgs p) {
                     if (two) v1 *= p.colscale[n + 1];
                 }
                 if (p.aux && p.mode != EPI_GELU) {
-                    bf16* a = p.aux + (long)m * p.ldaux + n;
-                    if (two) *reinterpret_cast<uint32_t*>(a) = pack_bf16(v0, v1);
-                    else a[0] = __float2bfloat16(v0);
+                    f16* a = p.aux + (long)m * p.ldaux + n;
+                    if (two) *reinterpret_cast<uint32_t*>(a) = pack_f16(v0, v1);
+                    else a[0] = __float2half_rn(v0);
                 }
                 if (p.rope && n < p.rope_cols) {  // n is even: (v0, v1) is one rotary pair
                     const float2 t = reinterpret_cast<const float2*>(p.rope)[(long)(m % p.rope_T) * 32 + (n % 64) / 2];
@@ -196,52 +196,52 @@ gemm_mma_kernel(const GemmArgs p) {
                         if (two) atomicAdd(o + 1, v1);
                         break;
                     }
-                    case EPI_STORE_BF16:
-                    case EPI_BIAS_BF16:
+                    case EPI_STORE_F16:
+                    case EPI_BIAS_F16:
                     case EPI_GELU:
                     case EPI_GELU_D:
                     case EPI_GELU_BWD:
                     case EPI_GELU_BWD_D: {
-                        if (p.mode == EPI_BIAS_BF16) {
+                        if (p.mode == EPI_BIAS_F16) {
                             v0 += p.bias[n];
                             if (two) v1 += p.bias[n + 1];
                         } else if (p.mode == EPI_GELU) {
-                            bf16* a = p.aux + (long)m * p.ldaux + n;
+                            f16* a = p.aux + (long)m * p.ldaux + n;
                             // the backward differentiates at the stored (rounded) value
-                            const bf16 z0 = __float2bfloat16(v0), z1 = __float2bfloat16(v1);
+                            const f16 z0 = __float2half_rn(v0), z1 = __float2half_rn(v1);
                             a[0] = z0;
                             if (two) a[1] = z1;
-                            v0 = gelu_as(__bfloat162float(z0));
-                            v1 = gelu_as(__bfloat162float(z1));
+                            v0 = gelu_as(__half2float(z0));
+                            v1 = gelu_as(__half2float(z1));
                         } else if (p.mode == EPI_GELU_D) {
-                            bf16* a = p.aux + (long)m * p.ldaux + n;
+                            f16* a = p.aux + (long)m * p.ldaux + n;
                             float g0, d0, g1, d1;
-                            gelu_as_pair(__bfloat162float(__float2bfloat16(v0)), g0, d0);
-                            gelu_as_pair(__bfloat162float(__float2bfloat16(v1)), g1, d1);
-                            a[0] = __float2bfloat16(d0);
-                            if (two) a[1] = __float2bfloat16(d1);
+                            gelu_as_pair(__half2float(__float2half_rn(v0)), g0, d0);
+                            gelu_as_pair(__half2float(__float2half_rn(v1)), g1, d1);
+                            a[0] = __float2half_rn(d0);
+                            if (two) a[1] = __float2half_rn(d1);
                             v0 = g0;
                             v1 = g1;
                         } else if (p.mode == EPI_GELU_BWD || p.mode == EPI_GELU_BWD_D) {
-                            const bf16* z = p.auxin + (long)m * p.ldauxin + n;
+                            const f16* z = p.auxin + (long)m * p.ldauxin + n;
                             if (p.mode == EPI_GELU_BWD) {
-                                v0 *= gelu_as_grad(__bfloat162float(z[0]));
-                                if (two) v1 *= gelu_as_grad(__bfloat162float(z[1]));
+                                v0 *= gelu_as_grad(__half2float(z[0]));
+                                if (two) v1 *= gelu_as_grad(__half2float(z[1]));
                             } else {
-                                v0 *= __bfloat162float(z[0]);
-                                if (two) v1 *= __bfloat162float(z[1]);
+                                v0 *= __half2float(z[0]);
+                                if (two) v1 *= __half2float(z[1]);
                             }
                             if (p.colscale2) {
                                 v0 *= p.colscale2[n];
                                 if (two) v1 *= p.colscale2[n + 1];
                             }
                         }
-                        bf16* o = static_cast<bf16*>(p.out) + (long)m * p.ldo + n;
+                        f16* o = static_cast<f16*>(p.out) + (long)m * p.ldo + n;
                         if (two && ((((long)m * p.ldo + n) & 1) == 0))
-                            *reinterpret_cast<uint32_t*>(o) = pack_bf16(v0, v1);
+                            *reinterpret_cast<uint32_t*>(o) = pack_f16(v0, v1);
                         else {
-                            o[0] = __float2bfloat16(v0);
-                            if (two) o[1] = __float2bfloat16(v1);
+                            o[0] = __float2half_rn(v0);
+                            if (two) o[1] = __float2half_rn(v1);
                         }
                         break;
                     }

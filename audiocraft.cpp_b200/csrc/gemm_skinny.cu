@@ -2,8 +2,8 @@
 //
 // Every adapted projection adds four products whose small side is the rank block (RP <= 64
 // columns) and whose large side is a whole activation / gradient matrix, read once:
-//   U  = s X A^T         rows x RP,  reduction over in     (A = X K-major,   B = A_bf K-major)
-//   dU = s dY B          rows x RP,  reduction over out    (A = dY K-major,  B = B_bf MN-major)
+//   U  = s X A^T         rows x RP,  reduction over in     (A = X K-major,   B = A_h K-major)
+//   dU = s dY B          rows x RP,  reduction over out    (A = dY K-major,  B = B_h MN-major)
 //   dB += dY^T U         out  x RP,  reduction over rows   (A = dY MN-major, B = U MN-major)
 //   dA += (dU^T X)       stored transposed [RP][in]; the tile is in x RP, reduction over rows
 // (src/ac/lora.h:34-95 and src/mf/train.h:150-190 for the products; the reference runs them as
@@ -14,7 +14,7 @@
 // tcgen05.mma 128 x 64 x 16 into TMEM, and four epilogue warps finish the tile:
 //   ACC      fp32 atomics into the gradient (row-major)
 //   ACC_T    fp32 atomics into the gradient, transposed (tile rows are the gradient's columns)
-//   STORE    bf16 result.  The split-K CTAs of a tile form one thread-block cluster; each
+//   STORE    f16 result.  The split-K CTAs of a tile form one thread-block cluster; each
 //            leaves its fp32 partial tile in its own shared memory and, after a cluster barrier,
 //            reduces its share of the rows over all partials through distributed shared memory
 //            (fixed summation order: deterministic), converts and stores.
@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(SK_THREADS, 2) skinny_kernel(const __grid_cons
             }
     } else if (warp == 1 && lane == 0) {
         // ------------------------------------------------------------ MMA issuer
-        const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)p.a_mn << 15) |
+        const uint32_t idesc = IDESC_F16_F32ACC | ((uint32_t)p.a_mn << 15) |
                                ((uint32_t)p.b_mn << 16) | ((uint32_t)(SK_BN >> 3) << 17) |
                                ((uint32_t)(SK_BM >> 4) << 24);
         const uint64_t a_desc0 = p.a_mn ? smem_desc(base, 8192, 1024) : smem_desc(base, 16, 1024);
@@ -214,11 +214,11 @@ __global__ void __launch_bounds__(SK_THREADS, 2) skinny_kernel(const __grid_cons
                 for (int j = 0; j < SK_BN; ++j)
                     if (j < p.nb) atomicAdd(o + (long)j * p.ldo, v[j]);  // lanes: consecutive rows
         } else if (p.splits == 1) {
-            bf16* o = static_cast<bf16*>(p.out) + (long)row * p.ldo;
+            f16* o = static_cast<f16*>(p.out) + (long)row * p.ldo;
             if (in)
 #pragma unroll
                 for (int j = 0; j < SK_BN; j += 2)
-                    if (j < p.nb) *reinterpret_cast<uint32_t*>(o + j) = pack_bf16(v[j], v[j + 1]);
+                    if (j < p.nb) *reinterpret_cast<uint32_t*>(o + j) = pack_f16(v[j], v[j + 1]);
         } else {
             float* pr = part + (quad * 32 + lane) * SK_PART_LD;
 #pragma unroll
@@ -245,8 +245,8 @@ __global__ void __launch_bounds__(SK_THREADS, 2) skinny_kernel(const __grid_cons
             }
             const int grow = mt * SK_BM + rl;
             if (grow < p.M)
-                *reinterpret_cast<uint2*>(static_cast<bf16*>(p.out) + (long)grow * p.ldo + 4 * c4) =
-                    make_uint2(pack_bf16(acc.x, acc.y), pack_bf16(acc.z, acc.w));
+                *reinterpret_cast<uint2*>(static_cast<f16*>(p.out) + (long)grow * p.ldo + 4 * c4) =
+                    make_uint2(pack_f16(acc.x, acc.y), pack_f16(acc.z, acc.w));
         }
         cluster_sync_all();  // peers keep their partials until every reader is done
     }

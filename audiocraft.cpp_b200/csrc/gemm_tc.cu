@@ -53,10 +53,10 @@ struct TcParams {
     long ldo;
     const float* resid;
     long ldr;
-    bf16* aux;
-    bf16* out_bf;
+    f16* aux;
+    f16* out_h;
     long ldaux;
-    const bf16* auxin;
+    const f16* auxin;
     long ldauxin;
     const float* colscale2;
     const float* bias;
@@ -72,12 +72,12 @@ struct TcParams {
 
 struct TcMaps {
     CUtensorMap a1, b1, a2, b2;
-    CUtensorMap out, aux;  // epilogue stores: box 32 x 32, swizzle 128 B (fp32) / 64 B (bf16)
-    CUtensorMap out_bf;    // bf16 copy of an fp32 output
+    CUtensorMap out, aux;  // epilogue stores: box 32 x 32, swizzle 128 B (fp32) / 64 B (f16)
+    CUtensorMap out_h;    // f16 copy of an fp32 output
 };
 
 // Epilogue staging, per epilogue warp: a 32-row x 128-byte tile for the output chunk (32 fp32
-// or 32 bf16 columns; 128-byte swizzle) and a 32 x 64-byte tile for bf16 side outputs/inputs
+// or 32 f16 columns; 128-byte swizzle) and a 32 x 64-byte tile for f16 side outputs/inputs
 // (64-byte swizzle).  Both leave shared memory through TMA bulk tensor stores.
 constexpr int EPI_OUT_BYTES = 32 * 128;
 constexpr int EPI_AUX_BYTES = 32 * 64;
@@ -107,7 +107,7 @@ __device__ __forceinline__ uint32_t sw64(int r, int u) { return r * 64 + ((u ^ (
 
 struct EpiTiles {
     unsigned char* o;  // output chunk tile (EPI_OUT_BYTES)
-    unsigned char* x;  // bf16 side tile (EPI_AUX_BYTES)
+    unsigned char* x;  // f16 side tile (EPI_AUX_BYTES)
     uint32_t o_s, x_s; // their shared-state-space addresses
 };
 
@@ -142,13 +142,13 @@ __device__ __forceinline__ void add_row_f32(const unsigned char* t, int lane, fl
     }
 }
 
-// 32 bf16 of this lane's row into a 64-byte-swizzled tile
+// 32 f16 of this lane's row into a 64-byte-swizzled tile
 __device__ __forceinline__ void put_row_b16(unsigned char* t, int lane, const float* v) {
 #pragma unroll
     for (int u = 0; u < 4; ++u)
         *reinterpret_cast<uint4*>(t + sw64(lane, u)) =
-            make_uint4(pack_bf16(v[8 * u], v[8 * u + 1]), pack_bf16(v[8 * u + 2], v[8 * u + 3]),
-                       pack_bf16(v[8 * u + 4], v[8 * u + 5]), pack_bf16(v[8 * u + 6], v[8 * u + 7]));
+            make_uint4(pack_f16(v[8 * u], v[8 * u + 1]), pack_f16(v[8 * u + 2], v[8 * u + 3]),
+                       pack_f16(v[8 * u + 4], v[8 * u + 5]), pack_f16(v[8 * u + 6], v[8 * u + 7]));
 }
 
 __device__ __forceinline__ void get_row_b16(const unsigned char* t, int lane, float* v) {
@@ -158,16 +158,17 @@ __device__ __forceinline__ void get_row_b16(const unsigned char* t, int lane, fl
         const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            v[8 * u + 2 * j] = __uint_as_float(w[j] << 16);
-            v[8 * u + 2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+            const float2 x = unpack_f16(w[j]);
+            v[8 * u + 2 * j] = x.x;
+            v[8 * u + 2 * j + 1] = x.y;
         }
     }
 }
 
-// Epilogue inputs read per chunk: fp32 residual / accumulator rows (RESID, ACCUM) or bf16 GELU
+// Epilogue inputs read per chunk: fp32 residual / accumulator rows (RESID, ACCUM) or f16 GELU
 // pre-activations (GELU_BWD).  They are fetched one chunk ahead into registers as coalesced
 // 128-byte row segments, so their latency overlaps the previous chunk, then staged in the tile.
-// Kind 3: the RoPE (cos, sin) pairs of a bf16-store chunk with rotary columns, loaded per lane
+// Kind 3: the RoPE (cos, sin) pairs of a f16-store chunk with rotary columns, loaded per lane
 // (its own row) from the position table, which does not stay in L1 beside the operand stages.
 __device__ __forceinline__ int epi_input_kind(const TcParams& p) {
     return (p.mode == EPI_RESID_F32 || p.mode == EPI_ACCUM_F32) ? 1
@@ -258,37 +259,37 @@ __device__ __forceinline__ void epilogue_warp32(const TcParams& p, const TcMaps&
         if (p.mode != EPI_STORE_F32) add_row_f32(t.o, lane, v);  // residual / accumulator already staged in the tile
         put_row_f32(t.o, lane, v);
         tile_store(&maps.out, t.o_s, n, m_base, lane);
-        if (p.out_bf) {
+        if (p.out_h) {
             if (p.aux) tiles_free(lane);  // the side tile is still being read by this chunk's aux store
             put_row_b16(t.x, lane, v);
-            tile_store(&maps.out_bf, t.x_s, n, m_base, lane);
+            tile_store(&maps.out_h, t.x_s, n, m_base, lane);
         }
         return;
     }
-    if (p.mode == EPI_BIAS_BF16) {
+    if (p.mode == EPI_BIAS_F16) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] += p.bias[n + i];
     } else if (p.mode == EPI_GELU) {
-        // the stored pre-activation is bf16; the activation and its backward use that value
+        // the stored pre-activation is f16; the activation and its backward use that value
         put_row_b16(t.x, lane, v);
         get_row_b16(t.x, lane, v);
         tile_store(&maps.aux, t.x_s, n, m_base, lane);
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = gelu_as(v[i]);
     } else if (p.mode == EPI_GELU_D) {
-        // gelu' of the bf16-rounded pre-activation goes to aux, gelu of it to the output
+        // gelu' of the f16-rounded pre-activation goes to aux, gelu of it to the output
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             float d8[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 float g;
-                gelu_as_pair(__bfloat162float(__float2bfloat16(v[8 * u + j])), g, d8[j]);
+                gelu_as_pair(__half2float(__float2half_rn(v[8 * u + j])), g, d8[j]);
                 v[8 * u + j] = g;
             }
             *reinterpret_cast<uint4*>(t.x + sw64(lane, u)) =
-                make_uint4(pack_bf16(d8[0], d8[1]), pack_bf16(d8[2], d8[3]), pack_bf16(d8[4], d8[5]),
-                           pack_bf16(d8[6], d8[7]));
+                make_uint4(pack_f16(d8[0], d8[1]), pack_f16(d8[2], d8[3]), pack_f16(d8[4], d8[5]),
+                           pack_f16(d8[6], d8[7]));
         }
         tile_store(&maps.aux, t.x_s, n, m_base, lane);
     } else if (p.mode == EPI_GELU_BWD || p.mode == EPI_GELU_BWD_D) {
@@ -431,7 +432,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(const __grid_const
             }
     } else if (warp == 1 && lane == 0) {
         // ------------------------------------------------------------ MMA issuer
-        const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((B_MN ? 1u : 0u) << 16) |
+        const uint32_t idesc = IDESC_F16_F32ACC | ((B_MN ? 1u : 0u) << 16) |
                                ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
         // Stage-0 descriptors; a stage offset or a k16 step is added to the 14-bit start-address
         // field (shared-memory addresses stay below 256 KB, so the field cannot carry over).
@@ -742,7 +743,7 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
         }
     } else if (warp == 1 && lane == 0 && rank == 0) {
         // ------------------------------------------------------------ MMA issuer (leader)
-        const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((B_MN ? 1u : 0u) << 16) |
+        const uint32_t idesc = IDESC_F16_F32ACC | ((B_MN ? 1u : 0u) << 16) |
                                ((uint32_t)(BN2 >> 3) << 17) | ((uint32_t)((2 * BM) >> 4) << 24);
         const uint64_t a_desc0 = smem_desc(base, 16, 1024);
         const uint64_t b_desc0 = B_MN ? smem_desc(base + Cfg::A_BYTES, 8192, 1024)
@@ -895,22 +896,22 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 2D bf16 row-major tensor [rows][cols] with row stride ld (elements); box {box_cols, box_rows}.
-void make_map(CUtensorMap* map, const bf16* ptr, long rows, long cols, long ld, int box_cols, int box_rows) {
+// 2D f16 row-major tensor [rows][cols] with row stride ld (elements); box {box_cols, box_rows}.
+void make_map(CUtensorMap* map, const f16* ptr, long rows, long cols, long ld, int box_cols, int box_rows) {
     if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * 2) % 16)
         throw std::runtime_error("gemm_tc: operand not 16-byte aligned");
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
     cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<bf16*>(ptr), dims, strides, box,
+    CUresult r = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<f16*>(ptr), dims, strides, box,
                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
 }
 
-// Epilogue store maps: the output as fp32 (box 32 x 32, 128-byte swizzle) or bf16 (box 32 x 32,
-// 64-byte swizzle) over rows min(M, mvalid); the bf16 side output (aux) the same way.
+// Epilogue store maps: the output as fp32 (box 32 x 32, 128-byte swizzle) or f16 (box 32 x 32,
+// 64-byte swizzle) over rows min(M, mvalid); the f16 side output (aux) the same way.
 void make_store_map(CUtensorMap* map, const void* ptr, bool f32, long rows, long cols, long ld) {
     const int esz = f32 ? 4 : 2;
     if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * esz) % 16)
@@ -919,7 +920,7 @@ void make_store_map(CUtensorMap* map, const void* ptr, bool f32, long rows, long
     cuuint64_t strides[1] = {(cuuint64_t)(ld * esz)};
     cuuint32_t box[2] = {32, 32};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = encode_fn()(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+    CUresult r = encode_fn()(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                              const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                              f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -932,8 +933,8 @@ void make_epilogue_maps(TcMaps& maps, const GemmArgs& a) {
     make_store_map(&maps.out, a.out, f32, rows, a.N, a.ldo);
     if (a.aux) make_store_map(&maps.aux, a.aux, false, rows, a.N, a.ldaux);
     else maps.aux = maps.out;
-    if (a.out_bf && f32) make_store_map(&maps.out_bf, a.out_bf, false, rows, a.N, a.ldo);
-    else maps.out_bf = maps.out;
+    if (a.out_h && f32) make_store_map(&maps.out_h, a.out_h, false, rows, a.N, a.ldo);
+    else maps.out_h = maps.out;
 }
 
 
@@ -961,7 +962,7 @@ void launch_tc(const GemmArgs& a, int* err, cudaStream_t s) {
     p.resid = a.resid; p.ldr = a.ldr; p.aux = a.aux; p.ldaux = a.ldaux; p.auxin = a.auxin; p.ldauxin = a.ldauxin;
     p.colscale2 = a.colscale2; p.bias = a.bias; p.nvalid = a.nvalid; p.mvalid = a.mvalid; p.err = err;
     p.rope = a.rope; p.rope_T = a.rope_T; p.rope_cols = a.rope_cols;
-    p.out_bf = (a.mode == EPI_STORE_F32 || a.mode == EPI_ACCUM_F32 || a.mode == EPI_RESID_F32) ? a.out_bf : nullptr;
+    p.out_h = (a.mode == EPI_STORE_F32 || a.mode == EPI_ACCUM_F32 || a.mode == EPI_RESID_F32) ? a.out_h : nullptr;
     auto kern = gemm_tc_kernel<BN, B_MN>;
     static DeviceOnce once;
     once([&] { cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM); });
@@ -1017,7 +1018,7 @@ void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
     p.resid = a.resid; p.ldr = a.ldr; p.aux = a.aux; p.ldaux = a.ldaux; p.auxin = a.auxin; p.ldauxin = a.ldauxin;
     p.colscale2 = a.colscale2; p.bias = a.bias; p.nvalid = a.nvalid; p.mvalid = a.mvalid; p.err = err;
     p.rope = a.rope; p.rope_T = a.rope_T; p.rope_cols = a.rope_cols;
-    p.out_bf = (a.mode == EPI_STORE_F32 || a.mode == EPI_ACCUM_F32 || a.mode == EPI_RESID_F32) ? a.out_bf : nullptr;
+    p.out_h = (a.mode == EPI_STORE_F32 || a.mode == EPI_ACCUM_F32 || a.mode == EPI_RESID_F32) ? a.out_h : nullptr;
     p.sk_part = a.sk_part; p.sk_flag = a.sk_flag;
     auto whole = gemm_tc2_kernel<BN2, B_MN, false>;
     auto split = gemm_tc2_kernel<BN2, B_MN, BN2 == 256>;
@@ -1062,7 +1063,7 @@ bool gemm_tc_supported(const GemmArgs& a) {
                          reinterpret_cast<uintptr_t>(a.auxin) | reinterpret_cast<uintptr_t>(a.resid) |
                          reinterpret_cast<uintptr_t>(a.colscale) | reinterpret_cast<uintptr_t>(a.A1) |
                          reinterpret_cast<uintptr_t>(a.B1) | reinterpret_cast<uintptr_t>(a.A2) |
-                         reinterpret_cast<uintptr_t>(a.B2) | reinterpret_cast<uintptr_t>(a.out_bf);
+                         reinterpret_cast<uintptr_t>(a.B2) | reinterpret_cast<uintptr_t>(a.out_h);
     return (al & 15) == 0;
 }
 
@@ -1131,7 +1132,7 @@ void gemm_tc(const GemmArgs& a, int* err, cudaStream_t s) {
     }
 }
 
-void tc_make_map(CUtensorMap* map, const bf16* ptr, long rows, long cols, long ld, int box_cols, int box_rows) {
+void tc_make_map(CUtensorMap* map, const f16* ptr, long rows, long cols, long ld, int box_cols, int box_rows) {
     make_map(map, ptr, rows, cols, ld, box_cols, box_rows);
 }
 

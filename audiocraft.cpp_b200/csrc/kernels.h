@@ -1,13 +1,13 @@
 // kernels.h -- launch interface between the host engine (engine.cpp) and the sm_100a kernels.
 // Every matrix is row-major; activations are token-major [rows][features].
 #pragma once
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include <string>
 
-typedef __nv_bfloat16 bf16;
+typedef __half f16;
 
 namespace act {
 
@@ -25,21 +25,21 @@ enum EpiMode : int {
     EPI_ACCUM_F32 = 1,   // out_f32 += alpha*acc
     EPI_ATOMIC_F32 = 2,  // atomicAdd(out_f32, alpha*acc)        (split-K reductions)
     EPI_RESID_F32 = 3,   // out_f32 = resid + alpha*acc
-    EPI_STORE_BF16 = 4,  // out_bf16 = alpha*acc
+    EPI_STORE_F16 = 4,  // out_bf16 = alpha*acc
     EPI_GELU = 5,        // aux_bf16 = acc ; out_bf16 = gelu(acc)
     EPI_GELU_BWD = 6,    // out_bf16 = acc * gelu'(auxin) * colscale2[n]
-    EPI_BIAS_BF16 = 7,   // out_bf16 = acc + bias[n]
-    EPI_GELU_D = 8,      // z = bf16(acc): aux_bf16 = gelu'(z) ; out_bf16 = gelu(z)   (z itself not kept)
+    EPI_BIAS_F16 = 7,   // out_bf16 = acc + bias[n]
+    EPI_GELU_D = 8,      // z = f16(acc): aux_bf16 = gelu'(z) ; out_bf16 = gelu(z)   (z itself not kept)
     EPI_GELU_BWD_D = 9,  // out_bf16 = acc * auxin(= gelu') * colscale2[n]
 };
 
 struct GemmArgs {
     int M = 0, N = 0, K1 = 0, K2 = 0;
-    const bf16* A1 = nullptr;
-    const bf16* A2 = nullptr;
+    const f16* A1 = nullptr;
+    const f16* A2 = nullptr;
     long lda1 = 0, lda2 = 0;
-    const bf16* B1 = nullptr;
-    const bf16* B2 = nullptr;
+    const f16* B1 = nullptr;
+    const f16* B2 = nullptr;
     long ldb1 = 0, ldb2 = 0;
     bool a_kmajor = true, b_kmajor = true;
     int splitk = 1;
@@ -51,12 +51,12 @@ struct GemmArgs {
     long ldo = 0;
     const float* resid = nullptr;      // EPI_RESID_F32
     long ldr = 0;
-    bf16* aux = nullptr;               // additionally store acc (after colscale) as bf16
+    f16* aux = nullptr;               // additionally store acc (after colscale) as f16
     long ldaux = 0;
-    const bf16* auxin = nullptr;       // EPI_GELU_BWD: pre-activation; EPI_GELU_BWD_D: gelu' of it
+    const f16* auxin = nullptr;       // EPI_GELU_BWD: pre-activation; EPI_GELU_BWD_D: gelu' of it
     long ldauxin = 0;
     const float* colscale2 = nullptr;  // EPI_GELU_BWD: DoRA factor of the producing projection
-    const float* bias = nullptr;       // EPI_BIAS_BF16
+    const float* bias = nullptr;       // EPI_BIAS_F16
     const float* rope = nullptr;       // rotate column pairs n < rope_cols by position m % rope_T
     int rope_T = 1, rope_cols = 0;     //   ([rope_T][32] (cos, sin) table, 64-column heads; after aux)
     int nvalid = 1 << 30;              // columns >= nvalid are not written
@@ -66,8 +66,8 @@ struct GemmArgs {
     // launch leaves at zero.  Launches sharing a workspace must not overlap on the device.
     float* sk_part = nullptr;
     int* sk_flag = nullptr;
-    // fp32 output modes (STORE / ACCUM / RESID): also store bf16(out), row stride ldo
-    bf16* out_bf = nullptr;
+    // fp32 output modes (STORE / ACCUM / RESID): also store f16(out), row stride ldo
+    f16* out_h = nullptr;
 };
 long gemm_sk_part_floats(int num_sms);
 int gemm_sk_flag_count(int num_sms);
@@ -80,19 +80,19 @@ void gemm_tc2(const GemmArgs& a, int* err, cudaStream_t s);     // 256 columns w
 void gemm_tc2_width(const GemmArgs& a, int* err, cudaStream_t s, int width);  // width 256 or 128
 // Rank-block products on tcgen05 (gemm_skinny.cu): C = alpha * A(M x K) B(K x nb), nb <= 64,
 // split over K across CTAs.  ACC / ACC_T add C (or C^T) into an fp32 gradient with atomics;
-// STORE writes bf16 C, reducing the split-K partials of a tile inside a thread-block cluster.
+// STORE writes f16 C, reducing the split-K partials of a tile inside a thread-block cluster.
 enum { SKINNY_ACC = 0, SKINNY_ACC_T = 1, SKINNY_STORE = 2 };
 struct SkinnyArgs {
     int M = 0, K = 0, nb = 0;
-    const bf16* A = nullptr;  // A(m, k): a_mn ? A[k * lda + m] : A[m * lda + k]
+    const f16* A = nullptr;  // A(m, k): a_mn ? A[k * lda + m] : A[m * lda + k]
     long lda = 0;
     bool a_mn = false;
-    const bf16* B = nullptr;  // B(k, n): b_mn ? B[k * ldb + n] : B[n * ldb + k]
+    const f16* B = nullptr;  // B(k, n): b_mn ? B[k * ldb + n] : B[n * ldb + k]
     long ldb = 0;
     bool b_mn = false;
     int kind = SKINNY_ACC;
     float alpha = 1.0f;
-    void* out = nullptr;      // ACC: out[m * ldo + n]; ACC_T: out[n * ldo + m]; STORE: bf16 out[m * ldo + n]
+    void* out = nullptr;      // ACC: out[m * ldo + n]; ACC_T: out[n * ldo + m]; STORE: f16 out[m * ldo + n]
     long ldo = 0;
     int splits = 0;           // 0: about two CTAs per SM (STORE: a power of two <= 8)
 };
@@ -106,9 +106,9 @@ void gemm_tc_auto(const GemmArgs& a, int* err, cudaStream_t s);
 // ---------------------------------------------------------------------------------------
 // attention over token-major q/k/v (head h at columns h*64 .. h*64+63), head_dim 64.
 struct AttnArgs {
-    const bf16* q = nullptr;
-    const bf16* k = nullptr;
-    const bf16* v = nullptr;
+    const f16* q = nullptr;
+    const f16* k = nullptr;
+    const f16* v = nullptr;
     long ldq = 0, ldk = 0, ldv = 0;
     int T = 0;           // queries per clip
     int Tk = 0;          // stored keys per clip
@@ -121,23 +121,23 @@ struct AttnArgs {
     int rope_load = 0;            // 1: q/k arrive unrotated (rotate while staging); 0: pre-rotated
                                   // (either way dq / dk come back unrotated)
     float scale = 0.125f;
-    bf16* o = nullptr;
+    f16* o = nullptr;
     long ldo = 0;
     float* lse = nullptr;         // [clips][H][T], log2 units
     // backward
-    const bf16* dout = nullptr;
+    const f16* dout = nullptr;
     long lddo = 0;
     float* dvec = nullptr;        // [clips][H][T]  rowsum(dO * O)
     float* dq_acc = nullptr;      // [clips*T][ldq_acc] fp32, rotated frame, zeroed by caller
     long ldq_acc = 0;
     // mma.sync backward with a single key block (Tk <= 64, no RoPE): dQ is final inside one CTA,
-    // so it is written straight as bf16 (times the optional column factor dq_scale) to dq_bf;
+    // so it is written straight as f16 (times the optional column factor dq_scale) to dq_h;
     // dq_acc is then not used and needs no zeroing
-    bf16* dq_bf = nullptr;
-    long lddq_bf = 0;
+    f16* dq_h = nullptr;
+    long lddq_h = 0;
     const float* dq_scale = nullptr;
-    bf16* dk = nullptr;
-    bf16* dv = nullptr;
+    f16* dk = nullptr;
+    f16* dv = nullptr;
     long lddk = 0, lddv = 0;
     const float* kscale = nullptr;  // DoRA factor applied to dk columns (nullable)
     const float* vscale = nullptr;  // DoRA factor applied to dv columns (nullable)
@@ -156,65 +156,70 @@ bool attn_fwd_tc_supported(const AttnArgs& a);
 void attn_fwd_tc(const AttnArgs& a, int* err, cudaStream_t s);
 void attn_bwd(const AttnArgs& a, cudaStream_t s);  // computes dvec itself
 void attn_dvec(const AttnArgs& a, cudaStream_t s);  // dvec = rowsum(dO * O)
-void attn_dkv_finish(const AttnArgs& a, cudaStream_t s);  // dk / dv (bf16) from dk_acc / dv_acc
+void attn_dkv_finish(const AttnArgs& a, cudaStream_t s);  // dk / dv (f16) from dk_acc / dv_acc
 // the same backward on tcgen05 (attention_tc.cu): pre-rotated q/k, Tk >= 128; computes dvec itself
 // and adds into dq_acc (zeroed by the caller) like attn_bwd
 bool attn_bwd_tc_supported(const AttnArgs& a);
 void attn_bwd_tc(const AttnArgs& a, int* err, cudaStream_t s);
-// dq (bf16) = unrotate(dq_acc) * qscale[col]
-void attn_dq_finish(const AttnArgs& a, bf16* dq, long lddq, const float* qscale, cudaStream_t s);
+// dq (f16) = unrotate(dq_acc) * qscale[col]
+void attn_dq_finish(const AttnArgs& a, f16* dq, long lddq, const float* qscale, cudaStream_t s);
 
 // ---------------------------------------------------------------------------------------
 // element-wise / row kernels
-// LayerNorm over rows of D (fp32 in), y = xhat*w + b (+ add[row / rows_per_clip]) -> bf16.
+// LayerNorm over rows of D (fp32 in), y = xhat*w + b (+ add[row / rows_per_clip]) -> f16.
 void layernorm_fwd(const float* x, const float* w, const float* b, const float* add, int rows_per_clip,
-                   bf16* y, float* mean, float* rstd, int rows, int D, float eps, cudaStream_t s);
-// dx (=|+=) LN'(dy) (+ extra); also dx_bf = bf16(dx * colscale).  dy fp32.
+                   f16* y, float* mean, float* rstd, int rows, int D, float eps, cudaStream_t s);
+// dx (=|+=) LN'(dy) (+ extra); also dx_h = f16(dx * colscale).  dy fp32.
 void layernorm_bwd(const float* dy, const float* x, const float* w, const float* mean,
-                   const float* rstd, float* dx, int accumulate, const float* extra, bf16* dx_bf,
+                   const float* rstd, float* dx, int accumulate, const float* extra, f16* dx_h,
                    const float* colscale, int rows, int D, cudaStream_t s);
-// dst_bf = bf16((x (+ extra)) * colscale); x updated with extra when given.
-void residual_to_bf16(float* x, const float* extra, bf16* dst, const float* colscale, int rows, int D,
+// dst_h = f16((x (+ extra)) * colscale); x updated with extra when given.
+void residual_to_f16(float* x, const float* extra, f16* dst, const float* colscale, int rows, int D,
                       cudaStream_t s);
-void f32_to_bf16(const float* x, bf16* y, long n, cudaStream_t s);
-// GELU by table (bit-identical to the A&S evaluation on bf16 inputs): tab holds
-// GELU_TAB_ENTRIES words filled by gelu_table_init; gact = gelu(z) and, with store_grad,
-// z <- gelu'(z) in place (n a multiple of 8)
-constexpr int GELU_TABLE_WORDS = 5120;
-void gelu_table_init(uint32_t* tab, cudaStream_t s);
-void gelu_fwd(const uint32_t* tab, bf16* z, bf16* gact, long n, int store_grad, cudaStream_t s);
-void gelu_check(const uint32_t* tab, const uint16_t* z, uint16_t* g, uint16_t* dg, long n, int direct, cudaStream_t s);
+void f32_to_f16(const float* x, f16* y, long n, cudaStream_t s);
+// GELU of the f16 pre-activation (A&S 7.1.26, gelu_as_pair): gact = gelu(z) and, with
+// store_grad, z <- gelu'(z) in place (n a multiple of 8)
+void gelu_fwd(f16* z, f16* gact, long n, int store_grad, cudaStream_t s);
+// the same evaluation on f16 bit patterns, element by element (stand-alone check)
+void gelu_check(const uint16_t* z, uint16_t* g, uint16_t* dg, long n, cudaStream_t s);
+
+// Gradient scale of the backward.  The seed gradient (the MSE's or the cross entropy's) is
+// multiplied by a power of two gscale so that the f16 backward operands sit well inside the
+// f16 range (d loss / d out is O(1 / (T * latent)) before scaling); every product that writes an
+// fp32 adapter gradient multiplies by 1 / gscale, which is exact.
 
 // MelodyFlow inputs: x0[m][c] = ((1-t)noise + t clean) * rescale(t), vstar = clean - noise.
 void mf_inputs(const float* clean, const float* noise, const float* t, int clips, int T, int lat,
-               bf16* x0, float* vstar, cudaStream_t s);
-// loss[b] = mean((sqrt2*out - vstar)^2) ; dout = d loss / d out (bf16, token-major)
+               f16* x0, float* vstar, cudaStream_t s);
+// loss[b] = mean((sqrt2*out - vstar)^2) ; dout = gscale * d loss / d out (f16, token-major)
 // part: clips * 32 floats of scratch (partial sums)
-void mf_loss(const float* out, const float* vstar, int clips, int T, int lat, float* loss, bf16* dout,
-             float* part, cudaStream_t s);
+void mf_loss(const float* out, const float* vstar, int clips, int T, int lat, float* loss, f16* dout,
+             float* part, float gscale, cudaStream_t s);
 // small fp32 linear for the timestep MLP: y[b][n] = act(sum_k x[b][k] W[n][k]); act 1 = SiLU
 void linear_f32(const float* x, const float* W, float* y, int rows, int N, int K, int act,
                 cudaStream_t s);
-// DoRA: dg[n] += sum_m a[m][n] * b[m][n] / colscale[n]^2  (a already includes colscale)
-void dora_colsum(const bf16* a, long lda, const bf16* b, long ldb, int rows, int N, const float* colscale,
-                 float* dg, cudaStream_t s);
+// DoRA: dg[n] += inv_gscale * sum_m a[m][n] * b[m][n] / colscale[n]^2  (a already includes
+// colscale and the gradient scale; dg is the unscaled gradient)
+void dora_colsum(const f16* a, long lda, const f16* b, long ldb, int rows, int N, const float* colscale,
+                 float* dg, float inv_gscale, cudaStream_t s);
 // DoRA per-step factors: G = A A^T, Q = B G, nsq = base + 2s<P,B> + s^2<B,Q>, g = m / sqrt(nsq)
 void dora_prepare(const float* A, const float* B, const float* m, const float* P, const float* base,
                   int r, int in, int out, float s, float* G, float* Q, float* nsq, float* g,
                   cudaStream_t st);
 // DoRA backward tail: gm += dg/sqrt(nsq); dt2 = 2s dnsq, dt3 = s^2 dnsq;
-// gB += dt2 P + 2 dt3 Q; BD = bf16(dt2 * B) [out][RP]; dG = B^T diag(dt3) B -> gA += 2 dG A
+// gB += dt2 P + 2 dt3 Q; BD = f16(bd_scale * dt2 * B) [out][RP] (the product gA += BD^T W that
+// consumes it multiplies by 1 / bd_scale); dG = B^T diag(dt3) B -> gA += 2 dG A
 void dora_finish(const float* dg, const float* nsq, const float* g, const float* m, const float* B,
                  const float* P, const float* Q, const float* A, int r, int RP, int in, int out, float s,
-                 float* gm, float* gB, float* gA, bf16* BD, float* scratch, cudaStream_t st);
+                 float* gm, float* gB, float* gA, f16* BD, float bd_scale, float* scratch, cudaStream_t st);
 
-// refresh bf16 working copies: dst[row*ldd + col] = src[row*cols + col] for row<rows, col<cols
+// refresh f16 working copies: dst[row*ldd + col] = src[row*cols + col] for row<rows, col<cols
 struct CopyJob {
     const float* src;
-    bf16* dst;
+    f16* dst;
     int rows, cols, ldd;
 };
-void refresh_bf16(const CopyJob* jobs_dev, int njobs, int max_elems, cudaStream_t s);
+void refresh_f16(const CopyJob* jobs_dev, int njobs, int max_elems, cudaStream_t s);
 
 // AdamW over the flat parameter buffer (TrainAccumulation::update semantics).
 // norm_partials: >= 1024 doubles of scratch.  nonfinite: int counter (accumulates).
@@ -227,17 +232,16 @@ void adamw(float* value, float* m, float* v, float* grad, const uint8_t* decay_m
 constexpr int WAIT_PROBE_CODE = 99;
 void wait_probe(const int* flag, long long limit_ns, int* err, cudaStream_t s);
 
-// Q8_0 blocks -> bf16 (one-time weight binding) and fp32 (parity checks).
-void q8_0_to_bf16(const uint8_t* blocks, long nblocks, bf16* out, cudaStream_t s);
+// Q8_0 blocks -> f16 (one-time weight binding) and fp32 (parity checks).
+void q8_0_to_f16(const uint8_t* blocks, long nblocks, f16* out, cudaStream_t s);
 void q8_0_to_f32(const uint8_t* blocks, long nblocks, float* out, cudaStream_t s);
-void f16_to_bf16(const uint16_t* in, long n, bf16* out, cudaStream_t s);
 
 // MusicGen: x[s][:] = sum_q emb_q[ids[q][s]] + pos[s]   (fp32 out)
 void mg_embed(const int32_t* ids, int steps, int nq, const float* const* emb_dev, const float* pos,
               float* x, int D, int seqs, cudaStream_t s);
 // Cross entropy over selected rows: logits fp32 [rows][card]; targets per row (-1: skip);
-// loss_acc[seq] += ce / nsel; dlogits bf16 = (softmax - onehot) / nsel.
+// loss_acc[seq] += ce / nsel; dlogits f16 = gscale * (softmax - onehot) / nsel.
 void mg_cross_entropy(const float* logits, int rows, int card, const int32_t* targets, int rows_per_seq,
-                      float inv_nsel, float* loss_acc, bf16* dlogits, cudaStream_t s);
+                      float inv_nsel, float* loss_acc, f16* dlogits, float gscale, cudaStream_t s);
 
 }  // namespace act

@@ -11,6 +11,11 @@ namespace tc {
 
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s per wait
 
+// Instruction-descriptor bits shared by every tcgen05.mma.kind::f16 here: fp32 accumulator
+// (bits 4-5 = 1) with f16 A and B operands (bits 7-9 and 10-12 = 0).  Majors, N >> 3 and
+// M >> 4 are or-ed in per call site.
+constexpr uint32_t IDESC_F16_F32ACC = 1u << 4;
+
 __device__ __forceinline__ unsigned long long globaltimer() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -163,8 +168,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
 
 
 // Host: cuTensorMapEncodeTiled through the driver entry point (no libcuda link dependency).
-// 2D bf16 row-major tensor [rows][cols] with row stride ld (elements); box {box_cols, box_rows},
+// 2D f16 row-major tensor [rows][cols] with row stride ld (elements); box {box_cols, box_rows},
 // 128-byte swizzle.
-void tc_make_map(CUtensorMap* map, const bf16* ptr, long rows, long cols, long ld, int box_cols, int box_rows);
+void tc_make_map(CUtensorMap* map, const f16* ptr, long rows, long cols, long ld, int box_cols, int box_rows);
 
 }  // namespace act

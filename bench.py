@@ -232,7 +232,7 @@ def run_sweep(kind, reps):
                         if path == 3 and N % 256:
                             continue
                         a, b = bits((M, K)), bits((K, N) if b_mn else (N, K))
-                        _, ms = A.gemm_bf16(a, b, M, N, K, b_mn, path, reps=reps)
+                        _, ms = A.gemm_f16(a, b, M, N, K, b_mn, path, reps=reps)
                         tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
                         print(json.dumps({"sweep": "gemm", "M": M, "N": N, "K": K,
                                           "layout": "NN (dX = dY W)" if b_mn else "NT (Y = X W^T)",
@@ -424,7 +424,7 @@ def main():
         "metric": metric,
         "value": value, "unit": line_unit,
         "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
         "config": config,
         "e2e": {"value": e2e_value, "unit": line_unit, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},

@@ -166,33 +166,34 @@ int act_reset_kernel_stats(act_ctx* ctx);
 /* algorithmic FLOPs of one step of n samples (2 per multiply-add) */
 double act_step_flops(act_ctx* ctx, int n);
 /* stand-alone projection GEMM on host buffers (tests and the kernel sweep): C[M][N] fp32 =
- * A[M][K] . B(n,k) with bf16 A and B, B as [N][K] (b_mn_major 0) or [K][N] (1);
+ * A[M][K] . B(n,k) with f16 A and B, B as [N][K] (b_mn_major 0) or [K][N] (1);
  * path 0 = automatic, 1 = mma.sync kernel, 2 = tcgen05 kernel, 3 = tcgen05 2-CTA (cta_group::2)
  * kernel (stream-K split of the tiles where whole tiles would leave the last round mostly
  * idle), 4 = the 2-CTA kernel with 128-column pair tiles, 5 = the 2-CTA kernel on whole
  * tiles only; when reps > 0 the GEMM is
  * re-run reps times back to back and *ms_per_call receives the mean device time */
-int act_gemm_bf16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path,
-                  int reps, float* ms_per_call);
+int act_gemm_f16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path,
+                 int reps, float* ms_per_call);
 /* stand-alone rank-block product (tests and the kernel sweep): C = alpha * A(M x K) B(K x nb),
- * nb <= 64, bf16 A stored [M][K] (a_mn 0) or [K][M] (1), bf16 B stored [nb][K] (b_mn 0) or
+ * nb <= 64, f16 A stored [M][K] (a_mn 0) or [K][M] (1), f16 B stored [nb][K] (b_mn 0) or
  * [K][nb] (1).  kind 0: C [M][nb] fp32 += result; kind 1: C [nb][M] fp32 += result transposed;
- * kind 2: C [M][nb] = the result rounded to bf16 (returned as fp32).  splits 0 = automatic.
+ * kind 2: C [M][nb] = the result rounded to f16 (returned as fp32).  splits 0 = automatic.
  * No reference counterpart: the reference evaluates these products as separate ggml mul_mat
  * nodes (src/ac/lora.h:34-95).  When reps > 0 the call is re-run reps times (kind 0/1 keep
  * accumulating) and *ms_per_call receives the mean device time. */
-/* stand-alone check of the feed-forward activation: g = bf16(gelu(z)), dg = bf16(gelu'(z)) for
- * bf16 z (A&S 7.1.26 GELU of src/ac/lora.h:97-110 and the derivative of that approximation),
- * evaluated directly (direct = 1) or by the lookup table the training step uses (0). */
-int act_gelu_bf16(int device, const uint16_t* z, uint16_t* g, uint16_t* dg, int64_t n, int direct);
-int act_rank_gemm_bf16(int device, int kind, const void* A, const void* B, float* C, int M, int K, int nb, int a_mn,
-                       int b_mn, float alpha, int splits, int reps, float* ms_per_call);
+/* stand-alone check of the feed-forward activation: g = f16(gelu(z)), dg = f16(gelu'(z)) for
+ * f16 z (A&S 7.1.26 GELU of src/ac/lora.h:97-110 and the derivative of that approximation),
+ * evaluated element by element (direct = 1) or by the vectorised pass the training step runs,
+ * which overwrites the pre-activation with gelu' (0); the two agree bit for bit. */
+int act_gelu_f16(int device, const uint16_t* z, uint16_t* g, uint16_t* dg, int64_t n, int direct);
+int act_rank_gemm_f16(int device, int kind, const void* A, const void* B, float* C, int M, int K, int nb, int a_mn,
+                      int b_mn, float alpha, int splits, int reps, float* ms_per_call);
 /* stand-alone attention forward + backward on host buffers (tests and the kernel sweep):
- * token-major bf16 q [clips*T][H*64], k/v [clips*Tk][H*64], dout like q; scale 1/8 (head_dim 64);
+ * token-major f16 q [clips*T][H*64], k/v [clips*Tk][H*64], dout like q; scale 1/8 (head_dim 64);
  * nvalid: per-clip valid key count or NULL; causal; zero_key = the prepended zero key of
- * src/ac/transformer.h:74-79; rope: [T][32] (cos, sin) pairs or NULL.  Outputs o (bf16),
+ * src/ac/transformer.h:74-79; rope: [T][32] (cos, sin) pairs or NULL.  Outputs o (f16),
  * lse (fp32 [clips][H][T], base-2 log-sum-exp of the scaled scores), and, when dout is given,
- * dq (bf16, like q), dk / dv (bf16, like k).  ms_fwd / ms_bwd (nullable) receive device times. */
+ * dq (f16, like q), dk / dv (f16, like k).  ms_fwd / ms_bwd (nullable) receive device times. */
 int act_attention(int device, const void* q, const void* k, const void* v, const void* dout, int clips, int T,
                   int Tk, int H, const int32_t* nvalid, int causal, int zero_key, const float* rope, void* o,
                   float* lse, void* dq, void* dk, void* dv, float* ms_fwd, float* ms_bwd);
@@ -243,9 +244,9 @@ int act_wait_probe(act_ctx* ctx, int64_t limit_ns);
  * prefix_frames], src/mg/train.h:195-205) of the last act_mg_stage / act_mg_step. */
 int act_mg_staged(act_ctx* ctx, int32_t* ids, size_t n_ids, int32_t* targets, size_t n_targets);
 /* Q8_0 blocks (34 bytes: fp16 d, int8 q[32]; tools/ac-quantize.cpp:161) dequantised on the
- * device by the kernels act_bind_weight uses: out_f32 = d * q in fp32, out_bf16 = that value
- * rounded to bf16 (the GEMM operand).  Either output may be NULL. */
-int act_q8_0_dequant(int device, const void* blocks, int64_t nblocks, float* out_f32, uint16_t* out_bf16);
+ * device by the kernels act_bind_weight uses: out_f32 = d * q in fp32, out_f16 = that value
+ * rounded to nearest-even f16 (the GEMM operand).  Either output may be NULL. */
+int act_q8_0_dequant(int device, const void* blocks, int64_t nblocks, float* out_f32, uint16_t* out_f16);
 /* kernels in the captured step graph for microbatch size n (-1 before the graph exists) */
 int64_t act_graph_kernel_nodes(act_ctx* ctx, int n);
 

@@ -1,21 +1,17 @@
 """Attention kernels (act_attention) vs an fp64 numpy restatement of src/ac/transformer.h:108-125
 (dense softmax with the optional zero key and additive masks) with the stored-frequency RoPE of
-src/ac/transformer.h:55-61.  Tolerance: relative L2 <= 1e-2 per output (bf16 operands)."""
+src/ac/transformer.h:55-61.  Tolerance: relative L2 <= 1e-2 per output (f16 operands)."""
 import numpy as np
 import pytest
 
 import actrain as A
+from f16util import bits_to_f32, f16_bits
 
 pytestmark = pytest.mark.gpu
 
 
-def bf16_bits(x):
-    u = np.ascontiguousarray(x, np.float32).view(np.uint32)
-    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
-
-
 def f32(b):
-    return (b.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    return bits_to_f32(b).astype(np.float64)
 
 
 def rope_table(T):
@@ -89,10 +85,10 @@ def test_attention_matches_reference(name):
     c = CASES[name]
     rng = np.random.default_rng(len(name))
     D = c["H"] * 64
-    q = bf16_bits(rng.standard_normal((c["clips"] * c["T"], D)))
-    k = bf16_bits(rng.standard_normal((c["clips"] * c["Tk"], D)))
-    v = bf16_bits(rng.standard_normal((c["clips"] * c["Tk"], D)))
-    do = bf16_bits(rng.standard_normal((c["clips"] * c["T"], D)))
+    q = f16_bits(rng.standard_normal((c["clips"] * c["T"], D)))
+    k = f16_bits(rng.standard_normal((c["clips"] * c["Tk"], D)))
+    v = f16_bits(rng.standard_normal((c["clips"] * c["Tk"], D)))
+    do = f16_bits(rng.standard_normal((c["clips"] * c["T"], D)))
     tab = rope_table(c["T"]) if c["rope"] else None
     out = A.attention(q, k, v, do, c["clips"], c["T"], c["Tk"], c["H"], c["nvalid"], c["causal"], c["zero_key"], tab)
     ro, rdq, rdk, rdv = reference(f32(q), f32(k), f32(v), f32(do), c["clips"], c["T"], c["Tk"], c["H"],

@@ -1,12 +1,10 @@
 """CUDA path vs the CPU oracle, through the C ABI (libactrain.so).
 
-Tolerances (bf16 GEMM operands, fp32 accumulation, against the fp32 oracle on the same
-dequantised weights):
-  loss        |rel| <= 1e-3                                     (BASELINE parity gate)
-  gradients   cosine >= 0.9999 and ||g - ref|| / ||ref|| <= 1e-2 over all adapter
-              gradients (BASELINE gates), and every single tensor's ||g - ref|| / ||ref||
-              <= 3e-2 (measured bf16 noise floor of these small models: 1-2e-2 at the
-              smallest-gradient tensors, half of it from rounding the weights to bf16).
+Tolerances (f16 GEMM operands, fp32 accumulation, against the fp32 oracle on the same
+dequantised weights), the BASELINE parity gates:
+  loss        |rel| <= 1e-3
+  gradients   cosine >= 0.9999 over all adapter gradients, and the relative error of every
+              adapter tensor, ||g - ref|| / ||ref||, <= 1e-2 (so also over all of them).
 """
 import numpy as np
 import pytest
@@ -20,7 +18,7 @@ pytestmark = pytest.mark.gpu
 LOSS_RTOL = 1e-3
 COS_MIN = 0.9999
 GLOBAL_REL = 1e-2
-TENSOR_REL = 3e-2
+TENSOR_REL = 1e-2
 
 
 def _check(loss, ref_loss, g, ref_g, layout):

@@ -1,7 +1,7 @@
 """Bit-exact pins of the library's own integer / format work on the device, and the failure path
 of a bounded device wait -- all through the C ABI.
 
-* Q8_0: the device dequantisation that act_bind_weight runs (fp32 d*q, then the bf16 GEMM
+* Q8_0: the device dequantisation that act_bind_weight runs (fp32 d*q, then the f16 GEMM
   operand) against gguf-py's Q8_0.dequantize_blocks goldens (tests/golden/q8_0.npz), bit for bit.
   Format: tools/ac-quantize.cpp:161,204 (34-byte blocks, fp16 d, int8 q[32]).
 * Delay pattern: the delayed ids and scored targets that act_mg_stage puts on the device against
@@ -25,17 +25,16 @@ pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 
-def _bf16_rne(x):
-    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
-    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+def _f16_rne(x):
+    return np.ascontiguousarray(x, np.float32).astype(np.float16).view(np.uint16)
 
 
 def test_q8_0_device_dequantisation_is_bit_exact():
     g = np.load(os.path.join(GOLDEN, "q8_0.npz"))
-    f32, bf = A.q8_0_dequant(g["q"])
+    f32, h = A.q8_0_dequant(g["q"])
     want = g["deq"].astype(np.float32).ravel()
     np.testing.assert_array_equal(f32.view(np.uint32), want.view(np.uint32))
-    np.testing.assert_array_equal(bf, _bf16_rne(want))
+    np.testing.assert_array_equal(h, _f16_rne(want))
 
 
 def _pattern_cases():

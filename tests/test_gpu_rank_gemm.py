@@ -1,28 +1,24 @@
 """Rank-block products (the LoRA U, dU, dB and dA GEMMs) on the tcgen05 skinny kernel vs numpy.
 
-bf16 inputs are exact in fp32 and the kernel accumulates in fp32, so the accumulate kinds match a
-float64 product to accumulation-order rounding; the bf16 kind matches it to one bf16 rounding.
+f16 inputs are exact in fp32 and the kernel accumulates in fp32, so the accumulate kinds match a
+float64 product to accumulation-order rounding; the f16 kind matches it to one f16 rounding.
 """
 import numpy as np
 import pytest
 
 import actrain as A
+from f16util import bits_to_f32, f16_bits
 
 pytestmark = pytest.mark.gpu
 
 
-def bf16_bits(x):
-    u = np.ascontiguousarray(x, np.float32).view(np.uint32)
-    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
-
-
 def bits_to_f64(b):
-    return (b.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    return bits_to_f32(b).astype(np.float64)
 
 
 def operands(rng, M, K, nb, a_mn, b_mn):
-    a = bf16_bits(rng.standard_normal((K, M) if a_mn else (M, K)))
-    b = bf16_bits(rng.standard_normal((K, nb) if b_mn else (nb, K)))
+    a = f16_bits(rng.standard_normal((K, M) if a_mn else (M, K)))
+    b = f16_bits(rng.standard_normal((K, nb) if b_mn else (nb, K)))
     af = bits_to_f64(a)
     bf = bits_to_f64(b)
     Am = af.T if a_mn else af          # [M][K]
@@ -53,10 +49,10 @@ def test_rank_gemm_matches_numpy(M, K, nb, a_mn, b_mn, kind, splits):
     init = None
     if kind != A.RANK_STORE:
         init = rng.standard_normal((nb, M) if kind == A.RANK_ACC_T else (M, nb)).astype(np.float32)
-    c = A.rank_gemm_bf16(a, b, M, K, nb, a_mn, b_mn, kind, alpha, C_init=init, splits=splits)
+    c = A.rank_gemm_f16(a, b, M, K, nb, a_mn, b_mn, kind, alpha, C_init=init, splits=splits)
     if kind == A.RANK_STORE:
-        # one bf16 rounding, plus fp32 accumulation-order error that grows like sqrt(K)
-        np.testing.assert_allclose(c, ref, rtol=2 ** -8, atol=3e-5 * np.sqrt(K))
+        # one f16 rounding, plus fp32 accumulation-order error that grows like sqrt(K)
+        np.testing.assert_allclose(c, ref, rtol=2 ** -11, atol=3e-5 * np.sqrt(K))
     else:
         want = init.astype(np.float64) + (ref.T if kind == A.RANK_ACC_T else ref)
         np.testing.assert_allclose(c, want, rtol=1e-5, atol=1e-5 * np.sqrt(K))
@@ -66,7 +62,7 @@ def test_rank_store_repeatable():
     # the cluster reduction sums the split-K partials in a fixed order: repeated calls agree bit for bit
     rng = np.random.default_rng(5)
     a, b, ref = operands(rng, 1000, 2048, 32, False, False)
-    first = A.rank_gemm_bf16(a, b, 1000, 2048, 32, False, False, A.RANK_STORE, 1.0, reps=3)[0]
-    again = A.rank_gemm_bf16(a, b, 1000, 2048, 32, False, False, A.RANK_STORE, 1.0)
+    first = A.rank_gemm_f16(a, b, 1000, 2048, 32, False, False, A.RANK_STORE, 1.0, reps=3)[0]
+    again = A.rank_gemm_f16(a, b, 1000, 2048, 32, False, False, A.RANK_STORE, 1.0)
     np.testing.assert_array_equal(first, again)
-    np.testing.assert_allclose(first, ref, rtol=2 ** -8, atol=3e-5 * np.sqrt(2048))
+    np.testing.assert_allclose(first, ref, rtol=2 ** -11, atol=3e-5 * np.sqrt(2048))

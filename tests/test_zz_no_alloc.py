@@ -12,19 +12,19 @@ import pytest
 import torch
 
 import actrain as A
+from f16util import bits_to_f32, f16_bits
 
 pytestmark = pytest.mark.gpu
 
-REL_TOL = 1e-2  # the attention tests' tolerance (relative L2, bf16 outputs)
+REL_TOL = 1e-2  # the attention tests' tolerance (relative L2, f16 outputs)
 
 
 def _bits(x):
-    u = np.ascontiguousarray(x, np.float32).view(np.uint32)
-    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    return f16_bits(x)
 
 
 def _f32(b):
-    return (np.ascontiguousarray(b).view(np.uint16).astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    return bits_to_f32(np.ascontiguousarray(b).view(np.uint16)).astype(np.float64)
 
 
 def _rope(T):
