@@ -158,9 +158,12 @@ static void mm_nn(int M, int N, int K, const float* A, int lda, const float* B, 
 
 static float* transpose(int R, int Cc, const float* X, int ldx) {
     float* T = (float*)malloc(sizeof(float) * (size_t)R * Cc);
-#pragma omp parallel for schedule(static) if ((long)R * Cc > 65536)
-    for (int r = 0; r < R; ++r)
-        for (int c = 0; c < Cc; ++c) T[(size_t)c * R + r] = X[(size_t)r * ldx + c];
+    /* 32 x 32 blocks: both sides stay in cache lines */
+#pragma omp parallel for collapse(2) schedule(static) if ((long)R * Cc > 65536)
+    for (int r0 = 0; r0 < R; r0 += 32)
+        for (int c0 = 0; c0 < Cc; c0 += 32)
+            for (int r = r0; r < imin(R, r0 + 32); ++r)
+                for (int c = c0; c < imin(Cc, c0 + 32); ++c) T[(size_t)c * R + r] = X[(size_t)r * ldx + c];
     return T;
 }
 
@@ -484,27 +487,43 @@ static void attn_bwd(const attn_shape* a, const float* q, int ldq, const float* 
                 P[(size_t)i * kend_all + j] = p;
                 dS[(size_t)i * kend_all + j] = ds;
             }
+            /* dq_i = scale * sum_j dS_ij k_j   (j ascending for every element) */
             float* dqi = dq + (size_t)i * lddq + h * hd;
-            for (int c = 0; c < hd; ++c) {
-                float acc = 0;
-                for (int j = 0; j < kend_all; ++j)
-                    acc += dS[(size_t)i * kend_all + j] * k[(size_t)j * ldk + h * hd + c];
-                dqi[c] = acc * a->scale;
+            float acc[256];
+            for (int c = 0; c < hd; ++c) acc[c] = 0;
+            for (int j = 0; j < kend_all; ++j) {
+                const float ds = dS[(size_t)i * kend_all + j];
+                const float* kj = k + (size_t)j * ldk + h * hd;
+                for (int c = 0; c < hd; ++c) acc[c] += ds * kj[c];
+            }
+            for (int c = 0; c < hd; ++c) dqi[c] = acc[c] * a->scale;
+        }
+        /* dk_j += scale * sum_i dS_ij q_i, dv_j += sum_i P_ij dO_i   (i ascending for every element) */
+        float* ak = (float*)calloc((size_t)kend_all * hd + 1, sizeof(float));
+        float* av = (float*)calloc((size_t)kend_all * hd + 1, sizeof(float));
+        for (int i = 0; i < T; ++i) {
+            const float* qi = q + (size_t)i * ldq + h * hd;
+            const float* doi = dout + (size_t)i * lddo + h * hd;
+            for (int j = 0; j < kend_all; ++j) {
+                const float ds = dS[(size_t)i * kend_all + j], p = P[(size_t)i * kend_all + j];
+                float* akj = ak + (size_t)j * hd;
+                float* avj = av + (size_t)j * hd;
+                for (int c = 0; c < hd; ++c) {
+                    akj[c] += ds * qi[c];
+                    avj[c] += p * doi[c];
+                }
             }
         }
         for (int j = 0; j < kend_all; ++j) {
             float* dkj = dk + (size_t)j * lddk + h * hd;
             float* dvj = dv + (size_t)j * lddv + h * hd;
             for (int c = 0; c < hd; ++c) {
-                float ak = 0, av = 0;
-                for (int i = 0; i < T; ++i) {
-                    ak += dS[(size_t)i * kend_all + j] * q[(size_t)i * ldq + h * hd + c];
-                    av += P[(size_t)i * kend_all + j] * dout[(size_t)i * lddo + h * hd + c];
-                }
-                dkj[c] += ak * a->scale;
-                dvj[c] += av;
+                dkj[c] += ak[(size_t)j * hd + c] * a->scale;
+                dvj[c] += av[(size_t)j * hd + c];
             }
         }
+        free(ak);
+        free(av);
         free(P);
         free(dS);
     }
