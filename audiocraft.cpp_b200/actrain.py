@@ -83,6 +83,8 @@ SIGNATURES = {
     "act_nccl_get_unique_id": (C.c_int, [C.c_void_p]),
     "act_nccl_init": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int]),
     "act_allreduce_grads": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
+    "act_set_grad_sync": (C.c_int, [C.c_void_p, C.c_int]),
+    "act_set_timeout": (C.c_int, [C.c_void_p, C.c_int64]),
     "act_optimizer": (C.c_int, [C.c_void_p, C.POINTER(Opt), C.POINTER(C.c_int)]),
     "act_last_error": (C.c_char_p, [C.c_void_p]),
     "act_destroy": (None, [C.c_void_p]),
@@ -267,6 +269,14 @@ class Context:
 
     def allreduce_grads(self, global_count: int):
         self._check(self._L.act_allreduce_grads(self.h, None, global_count))
+
+    def set_grad_sync(self, global_count: int):
+        """act_set_grad_sync: the next step all-reduces its gradients in-step (per-layer buckets)."""
+        self._check(self._L.act_set_grad_sync(self.h, global_count))
+
+    def set_timeout(self, ms: int):
+        """act_set_timeout: bound on NCCL initialisation and on host waits while a communicator lives."""
+        self._check(self._L.act_set_timeout(self.h, int(ms)))
 
     # ----------------------------------------------------------------- measurement
     def stream(self) -> int:

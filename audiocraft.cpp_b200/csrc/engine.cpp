@@ -32,6 +32,7 @@
 #include <vector>
 
 #include "kernels.h"
+#include "watchdog.h"
 
 using namespace act;
 
@@ -257,6 +258,7 @@ struct act_ctx {
     f16* dlogits = nullptr;
 
     // execution
+    // captured step graphs and eager-run counts, keyed by 2 * n + (1 if the step all-reduces)
     std::map<int, cudaGraphExec_t> graphs;
     std::map<int, int> eager_runs;
     std::map<int, int64_t> kernel_nodes;
@@ -273,6 +275,17 @@ struct act_ctx {
     size_t evnext = 0;
 
     ncclComm_t comm = nullptr;
+    // host waits on the device while a communicator is live, and NCCL initialisation, give up
+    // after this long (0: no limit): the communicator is then aborted and the call fails
+    int64_t timeout_ms = 0;
+    // in-step gradient all-reduce (act_set_grad_sync): per-layer buckets on their own stream,
+    // each started as soon as its layer's backward has been issued
+    cudaStream_t comm_stream = nullptr;
+    cudaEvent_t ev_comm_fork = nullptr, ev_comm_join = nullptr;
+    int grad_sync = 0;               // > 0: the next step all-reduces, then averages over this count
+    bool in_step_sync = false;       // the body being issued carries the all-reduce
+    bool comm_pending = false;
+    std::vector<std::pair<int64_t, int64_t>> layer_params;  // [first, end) of each layer's parameters
     int* kerr = nullptr;
     int* probe_flag = nullptr;  // never set: act_wait_probe waits on it until its limit runs out
     bool use_tc = true;
@@ -380,6 +393,34 @@ struct act_ctx {
         side_pending = false;
     }
 
+    // In-step all-reduce of the gradient range [first, end) on the communicator's stream, after
+    // everything the main stream has issued so far (that range's gradients are complete then)
+    // and concurrently with what it issues next.  No-op unless this step all-reduces.
+    void sync_bucket(int64_t first, int64_t end) {
+        if (!in_step_sync || end <= first) return;
+        CK(cudaEventRecord(ev_comm_fork, stream));
+        CK(cudaStreamWaitEvent(comm_stream, ev_comm_fork, 0));
+        nccl_call(ncclAllReduce(grad + first, grad + first, (size_t)(end - first), ncclFloat, ncclSum, comm,
+                                comm_stream),
+                  "gradient all-reduce");
+        comm_pending = true;
+    }
+    void join_comm() {
+        if (!comm_pending) return;
+        CK(cudaEventRecord(ev_comm_join, comm_stream));
+        CK(cudaStreamWaitEvent(stream, ev_comm_join, 0));
+        comm_pending = false;
+    }
+    // after layer l's backward: its adapters' gradients are final (LoRA; DoRA's row-norm terms
+    // are added for every layer after the whole backward, so DoRA all-reduces once at the end)
+    void sync_layer(int l) {
+        if (ad.type == ACT_ADAPTER_LORA) sync_bucket(layer_params[l].first, layer_params[l].second);
+    }
+    void sync_rest() {
+        if (ad.type != ACT_ADAPTER_LORA) sync_bucket(0, nparam);
+        join_comm();
+    }
+
     // rank-block products: the tcgen05 skinny kernel, or the generic GEMM `fallback` when the
     // tcgen05 paths are disabled or the operands do not qualify
     void run_rank(const SkinnyArgs& k, const GemmArgs& fallback) {
@@ -393,12 +434,80 @@ struct act_ctx {
         }
     }
 
+    // ---------------------------------------------------------------- bounded waits (NCCL)
+    // The communicator is gone (ncclCommAbort): graphs that carry its collectives are dropped.
+    void abort_comm() {
+        if (!comm) return;
+        ncclCommAbort(comm);
+        comm = nullptr;
+        for (auto it = graphs.begin(); it != graphs.end();) {
+            if (it->first & 1) {
+                cudaGraphExecDestroy(it->second);
+                it = graphs.erase(it);
+            } else {
+                ++it;
+            }
+        }
+    }
+    // Until the communicator's pending work (initialisation, an enqueue) is done: bounded by
+    // timeout_ms, failure or expiry aborts it.
+    void wait_nccl(const char* what) {
+        const WaitResult r = bounded_wait(
+            [&] {
+                ncclResult_t st = ncclSuccess;
+                if (ncclCommGetAsyncError(comm, &st) != ncclSuccess) return WaitState::Failed;
+                return st == ncclSuccess ? WaitState::Done : st == ncclInProgress ? WaitState::Pending : WaitState::Failed;
+            },
+            [&] { abort_comm(); }, timeout_ms, 100);
+        if (r != WaitResult::Done)
+            throw Error(ACT_ERR_NCCL, std::string("NCCL ") + what + (r == WaitResult::TimedOut ? " timed out" : " failed") +
+                                          ": communicator aborted");
+    }
+    void nccl_call(ncclResult_t r, const char* what) {
+        if (r == ncclInProgress) return wait_nccl(what);
+        if (r != ncclSuccess) {
+            abort_comm();
+            throw Error(ACT_ERR_NCCL, std::string("NCCL ") + what + ": " + ncclGetErrorString(r));
+        }
+    }
+    // Wait for the context's stream.  While a communicator is live, a collective whose peer died
+    // or stalled never finishes: poll the stream and NCCL's asynchronous error, within timeout_ms.
+    void sync_stream() {
+        if (!comm) {
+            CK(cudaStreamSynchronize(stream));
+            return;
+        }
+        cudaError_t cerr = cudaSuccess;
+        const WaitResult r = bounded_wait(
+            [&] {
+                const cudaError_t e = cudaStreamQuery(stream);
+                if (e == cudaSuccess) return WaitState::Done;
+                if (e != cudaErrorNotReady) {
+                    cerr = e;
+                    return WaitState::Done;
+                }
+                ncclResult_t st = ncclSuccess;
+                if (ncclCommGetAsyncError(comm, &st) != ncclSuccess || (st != ncclSuccess && st != ncclInProgress))
+                    return WaitState::Failed;
+                return WaitState::Pending;
+            },
+            [&] { abort_comm(); }, timeout_ms, 50);
+        if (cerr != cudaSuccess) throw Error(ACT_ERR_CUDA, std::string("stream: ") + cudaGetErrorString(cerr));
+        if (r != WaitResult::Done) {
+            // after the abort the collective returns and the stream drains
+            cudaStreamSynchronize(stream);
+            throw Error(ACT_ERR_NCCL, r == WaitResult::TimedOut
+                                          ? "timed out waiting for a collective (a peer rank stalled or died): communicator aborted"
+                                          : "NCCL reported an asynchronous error: communicator aborted");
+        }
+    }
+
     // kernels record a nonzero code here instead of hanging on a wait that cannot finish
     // (the word is cleared when it is reported, so that the context stays usable afterwards)
     void check_kernel_error() {
         int e = 0;
         CK(cudaMemcpyAsync(&e, kerr, sizeof(int), cudaMemcpyDeviceToHost, stream));
-        CK(cudaStreamSynchronize(stream));
+        sync_stream();
         if (e) {
             CK(cudaMemsetAsync(kerr, 0, sizeof(int), stream));
             CK(cudaStreamSynchronize(stream));
@@ -729,7 +838,7 @@ struct act_ctx {
     // dxh := f16((dx + dsaved[l]) * g_ff2(l))  -- entering block l's backward
     const float* entry_extra(int l) { return layers[l].produces ? layers[l].dsaved : nullptr; }
     const float* entry_scale(int l) { return layers[l].p[6].dora ? layers[l].p[6].g : nullptr; }
-    void prepare_dxbf(int l, int n) {
+    void prepare_dxh(int l, int n) {
         const long rows = (long)n * T;
         timed(2, 0, 0, [&] { residual_to_f16(dx, entry_extra(l), dxh, entry_scale(l), (int)rows, D, stream); });
     }
@@ -807,10 +916,12 @@ struct act_ctx {
                 GemmArgs b = a;  // d saved += dx Wskip[:, D:]
                 b.B1 = skip[y.proj] + D; b.mode = EPI_ACCUM_F32; b.out = layers[y.src].dsaved;
                 run_gemm(b, 0);
-                prepare_dxbf(l - 1, n);
+                prepare_dxh(l - 1, n);
             }
+            sync_layer(l);
         }
         finish_adapters();
+        sync_rest();
     }
 
     void mg_graph_body(int n) {
@@ -857,8 +968,10 @@ struct act_ctx {
         for (int l = L - 1; l >= first; --l) {
             if (l > first) block_bwd(l, n, nullptr, true, true, entry_extra(l - 1), entry_scale(l - 1));
             else block_bwd(l, n, nullptr, false);
+            sync_layer(l);
         }
         finish_adapters();
+        sync_rest();
     }
 
     void run_body(int n) {
@@ -873,9 +986,10 @@ struct act_ctx {
             collect_stats();
             return;
         }
-        auto it = graphs.find(n);
+        const int key = 2 * n + (in_step_sync ? 1 : 0);
+        auto it = graphs.find(key);
         if (it == graphs.end()) {
-            if (eager_runs[n]++ == 0) {  // first use of this size runs eagerly (sets kernel attributes)
+            if (eager_runs[key]++ == 0) {  // first use of this size runs eagerly (sets kernel attributes)
                 run_body(n);
                 CK(cudaGetLastError());
                 return;
@@ -899,11 +1013,11 @@ struct act_ctx {
                 CK(cudaGraphNodeGetType(nd, &ty));
                 kn += ty == cudaGraphNodeTypeKernel;
             }
-            kernel_nodes[n] = kn;
+            kernel_nodes[n] = kn;  // the step's graph (with the all-reduce's kernels when it carries them)
             cudaGraphExec_t exec;
             CK(cudaGraphInstantiate(&exec, graph, 0));
             CK(cudaGraphDestroy(graph));
-            it = graphs.emplace(n, exec).first;
+            it = graphs.emplace(key, exec).first;
         }
         CK(cudaGraphLaunch(it->second, stream));
     }
@@ -1004,8 +1118,20 @@ struct act_ctx {
         if (!finalized) throw Error(ACT_ERR_STATE, "act_finalize has not been called");
         if (staged_n <= 0) throw Error(ACT_ERR_STATE, "no staged batch");
         const int n = staged_n;
-        launch_step(n);
+        in_step_sync = grad_sync > 0;
+        if (in_step_sync && !comm) throw Error(ACT_ERR_STATE, "in-step gradient all-reduce needs a communicator");
+        try {
+            launch_step(n);
+        } catch (...) {
+            in_step_sync = false;
+            throw;
+        }
         accumulated += n;
+        if (in_step_sync) {  // the step's all-reduce replaced a separate act_allreduce_grads call
+            count_override = grad_sync;
+            grad_sync = 0;
+            in_step_sync = false;
+        }
         if (loss) {
             CK(cudaMemcpyAsync(h_loss, d_loss, n * 4, cudaMemcpyDeviceToHost, stream));
             check_kernel_error();
@@ -1045,6 +1171,9 @@ struct act_ctx {
         CK(cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking));
         CK(cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming));
         CK(cudaEventCreateWithFlags(&ev_join, cudaEventDisableTiming));
+        CK(cudaStreamCreateWithFlags(&comm_stream, cudaStreamNonBlocking));
+        CK(cudaEventCreateWithFlags(&ev_comm_fork, cudaEventDisableTiming));
+        CK(cudaEventCreateWithFlags(&ev_comm_join, cudaEventDisableTiming));
         kerr = dalloc<int>(1);
         probe_flag = dalloc<int>(1);
         {
@@ -1311,6 +1440,13 @@ struct act_ctx {
                 }
             }
         nparam = off;
+        layer_params.assign(L, {0, 0});
+        for (const auto& pi : ptable) {
+            const int l = std::atoi(pi.name.c_str() + pre.size());
+            auto& r = layer_params[l];
+            if (r.second == 0) r.first = pi.off;
+            r.second = pi.off + pi.rows * pi.cols;
+        }
         value = dalloc<float>(nparam);
         mom1 = dalloc<float>(nparam);
         mom2 = dalloc<float>(nparam);
@@ -1551,6 +1687,10 @@ struct act_ctx {
         for (void* p : dallocs) cudaFree(p);
         for (void* p : hallocs) cudaFreeHost(p);
         if (side) cudaStreamSynchronize(side);
+        if (comm_stream) cudaStreamSynchronize(comm_stream);
+        if (ev_comm_fork) cudaEventDestroy(ev_comm_fork);
+        if (ev_comm_join) cudaEventDestroy(ev_comm_join);
+        if (comm_stream) cudaStreamDestroy(comm_stream);
         if (ev_fork) cudaEventDestroy(ev_fork);
         if (ev_join) cudaEventDestroy(ev_join);
         if (side) cudaStreamDestroy(side);
@@ -1753,9 +1893,19 @@ int act_nccl_init(act_ctx* ctx, const void* id, int nranks, int rank) {
     if (!ctx || !id) return ACT_ERR_INVALID;
     return guarded(ctx, [&] {
         if (ctx->comm) throw Error(ACT_ERR_STATE, "communicator already initialised");
+        if (nranks <= 0 || rank < 0 || rank >= nranks) throw Error(ACT_ERR_INVALID, "invalid rank or rank count");
         ncclUniqueId u;
         std::memcpy(&u, id, sizeof(u));
-        NK(ncclCommInitRank(&ctx->comm, nranks, u, rank));
+        // non-blocking: a peer that never joins ends in ncclCommAbort after the context's timeout
+        ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+        cfg.blocking = 0;
+        const ncclResult_t r = ncclCommInitRankConfig(&ctx->comm, nranks, u, rank, &cfg);
+        if (r != ncclSuccess && r != ncclInProgress) {
+            if (ctx->comm) ncclCommAbort(ctx->comm);
+            ctx->comm = nullptr;
+            throw Error(ACT_ERR_NCCL, std::string("ncclCommInitRankConfig: ") + ncclGetErrorString(r));
+        }
+        ctx->wait_nccl("communicator initialisation");
     });
 }
 
@@ -1767,9 +1917,26 @@ int act_allreduce_grads(act_ctx* ctx, void* comm, int global_count) {
         if (!c) throw Error(ACT_ERR_STATE, "no NCCL communicator");
         if (global_count <= 0) throw Error(ACT_ERR_INVALID, "invalid global sample count");
         ctx->timed(2, 0, 8.0 * ctx->nparam, [&] {
-            NK(ncclAllReduce(ctx->grad, ctx->grad, ctx->nparam, ncclFloat, ncclSum, c, ctx->stream));
+            const ncclResult_t r = ncclAllReduce(ctx->grad, ctx->grad, ctx->nparam, ncclFloat, ncclSum, c, ctx->stream);
+            if (c == ctx->comm) ctx->nccl_call(r, "gradient all-reduce");
+            else if (r != ncclSuccess) throw Error(ACT_ERR_NCCL, std::string("ncclAllReduce: ") + ncclGetErrorString(r));
         });
         ctx->count_override = global_count;
+    });
+}
+
+int act_set_timeout(act_ctx* ctx, int64_t timeout_ms) {
+    if (!ctx || timeout_ms < 0) return ACT_ERR_INVALID;
+    ctx->timeout_ms = timeout_ms;
+    return ACT_OK;
+}
+
+int act_set_grad_sync(act_ctx* ctx, int global_count) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] {
+        if (global_count < 0) throw Error(ACT_ERR_INVALID, "invalid global sample count");
+        if (global_count > 0 && !ctx->comm) throw Error(ACT_ERR_STATE, "no NCCL communicator");
+        ctx->grad_sync = global_count;
     });
 }
 

@@ -324,15 +324,17 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
+    host = None
     if world > 1:
         from datetime import timedelta
+        import dp
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+        host = dp.host_group(120.0)  # host-side coordination (gloo), bounded
 
     ctx = build_context(A, c, args.workload, local)
     if world > 1:
-        uid = [A.Context.nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        ctx.nccl_init(uid[0], world, rank)
+        ctx.set_timeout(120_000)  # a stalled peer ends in an aborted communicator, not a hang
+        ctx.nccl_init(dp.share_nccl_id(host, rank, A.Context.nccl_unique_id), world, rank)
 
     rng = np.random.default_rng(1000 + rank)
     n = c["batch"]
@@ -357,12 +359,12 @@ def main():
     step_counter = [0]
 
     def one_step(e2e=False):
+        if world > 1:  # the step all-reduces its gradients itself, layer by layer, overlapping the backward
+            ctx.set_grad_sync(n * world)
         if e2e:
             e2e_step()
         else:
             ctx.run_staged(n, read_loss=False)
-        if world > 1:
-            ctx.allreduce_grads(n * world)
         step_counter[0] += 1
         ctx.optimizer(lr=1e-4, step=step_counter[0], weight_decay=0.01, clip=1.0)
 
@@ -384,6 +386,8 @@ def main():
     for _ in range(max(args.warmup, 3)):
         one_step()
     barrier()
+    if host is not None:  # every rank is alive and through its warm-up before anything is timed
+        dp.check_peers(host, 120.0, "the timed steps")
 
     # ---- value: device-timed, inputs resident in HBM
     clocks = Clocks(local)
@@ -417,7 +421,7 @@ def main():
         one_step()
     ctx.set_profiling(False)
     stats = [ctx.kernel_stats(i) for i in range(3)]
-    kernels_per_step = ctx.graph_kernel_nodes(n) + 2 + (1 if world > 1 else 0)
+    kernels_per_step = ctx.graph_kernel_nodes(n) + 2
     step_flops = ctx.step_flops(n)
 
     peaks = {}

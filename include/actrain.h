@@ -144,6 +144,18 @@ int act_nccl_init(act_ctx* ctx, const void* id_128_bytes, int nranks, int rank);
 /* sum gradients over ranks; nccl_comm NULL uses the context's own communicator.
  * global_count becomes the averaging count of the next act_optimizer. */
 int act_allreduce_grads(act_ctx* ctx, void* nccl_comm, int global_count);
+/* The next step (act_mf_step / act_mg_step / act_run_staged) all-reduces the gradients inside
+ * the step, over the context's communicator: each layer's gradients start their all-reduce as
+ * soon as that layer's backward has been issued (DoRA: once, after the whole backward), on a
+ * stream of their own that overlaps the remaining backward.  It takes the place of
+ * act_allreduce_grads after the last microbatch of an accumulation; global_count becomes the
+ * averaging count of the next act_optimizer.  0 cancels. */
+int act_set_grad_sync(act_ctx* ctx, int global_count);
+/* Bound, in milliseconds, on NCCL initialisation and on every host wait for the device while
+ * a communicator is live (0 = none, the default).  A rank that stalls or dies makes the others'
+ * next wait expire: their communicator is aborted (ncclCommAbort) and the call returns
+ * ACT_ERR_NCCL instead of blocking forever. */
+int act_set_timeout(act_ctx* ctx, int64_t timeout_ms);
 
 /* mean, clip, AdamW, zero gradients (TrainAccumulation::update).  *nonfinite receives the
  * number of nonfinite updated values; a nonzero count also returns ACT_ERR_NONFINITE. */
