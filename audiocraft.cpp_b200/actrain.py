@@ -105,6 +105,8 @@ SIGNATURES = {
                                   [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "act_gemm_f16": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                 C.c_int, C.c_int, C.POINTER(C.c_float)]),
+    "act_gemm_q8_0": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                 C.c_int, C.c_int, C.POINTER(C.c_float)]),
     "act_gelu_f16": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int]),
     "act_path_counts": (C.c_int, [C.c_void_p, C.POINTER(C.c_int64), C.c_int]),
     "act_wait_probe": (C.c_int, [C.c_void_p, C.c_int64]),
@@ -326,6 +328,21 @@ def gemm_f16(A_bits: np.ndarray, B_bits: np.ndarray, M: int, N: int, K: int, b_m
     b = np.ascontiguousarray(B_bits, np.uint16)
     ms = C.c_float(0.0)
     rc = lib().act_gemm_f16(device, a.ctypes.data, b.ctypes.data, C_.ctypes.data, M, N, K, int(b_mn_major), path,
+                             reps, C.byref(ms))
+    if rc != ACT_OK:
+        raise ActError(rc, lib().act_last_error(None).decode())
+    return (C_, ms.value) if reps > 0 else C_
+
+
+def gemm_q8_0(A_bits: np.ndarray, B_blocks: np.ndarray, M: int, N: int, K: int, b_mn_major: bool, path: int = 0,
+              device: int = 0, reps: int = 0):
+    """C = A . B(n,k) with B as the Q8_0 blocks of the weight ([N][K], or [K][N] when b_mn_major),
+    dequantised inside the GEMM.  With reps > 0 returns (C, mean ms per call)."""
+    C_ = np.zeros((M, N), np.float32)
+    a = np.ascontiguousarray(A_bits, np.uint16)
+    b = np.ascontiguousarray(B_blocks, np.uint8)
+    ms = C.c_float(0.0)
+    rc = lib().act_gemm_q8_0(device, a.ctypes.data, b.ctypes.data, C_.ctypes.data, M, N, K, int(b_mn_major), path,
                              reps, C.byref(ms))
     if rc != ACT_OK:
         raise ActError(rc, lib().act_last_error(None).decode())

@@ -376,6 +376,41 @@ __global__ void q8_f16_kernel(const uint8_t* __restrict__ blocks, long nblocks, 
     out[e] = __float2half_rn(__half2float(d) * (float)(int8_t)blk[2 + (e & 31)]);
 }
 
+// Q8_0 weight [rows][cols] split into its quants biased to unsigned ([rows][cols], q + 128) and
+// its scales transposed ([cols / 32][rows]); one block per thread.
+__global__ void q8_split_kernel(const uint8_t* __restrict__ blocks, int rows, int cols, uint8_t* __restrict__ q,
+                                f16* __restrict__ d) {
+    const long b = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int nb = cols / 32;
+    if (b >= (long)rows * nb) return;
+    const int r = (int)(b / nb), j = (int)(b % nb);
+    const uint8_t* blk = blocks + b * 34;
+    d[(long)j * rows + r] = __ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8)));
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        w[i] = (blk[2 + 4 * i] | (blk[3 + 4 * i] << 8) | (blk[4 + 4 * i] << 16) | ((uint32_t)blk[5 + 4 * i] << 24)) ^
+               0x80808080u;
+    uint4* dst = reinterpret_cast<uint4*>(q + (long)r * cols + j * 32);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+// A Q8_0 weight view as f16 (biased quants, transposed scales); 8 columns per thread.
+__global__ void q8_view_f16_kernel(const uint8_t* __restrict__ q, long ldq, const f16* __restrict__ d, long ldd,
+                                   int rows, int cols, f16* __restrict__ out, long ldo) {
+    const long e = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+    if (e >= (long)rows * cols) return;
+    const int r = (int)(e / cols), c = (int)(e % cols);
+    const float sc = __half2float(d[(long)(c / 32) * ldd + r]);
+    const uint8_t* qr = q + (long)r * ldq + c;
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        o[j] = pack_f16(sc * (float)((int)qr[2 * j] - 128), sc * (float)((int)qr[2 * j + 1] - 128));
+    *reinterpret_cast<uint4*>(out + (long)r * ldo + c) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 __global__ void q8_f32_kernel(const uint8_t* __restrict__ blocks, long nblocks, float* __restrict__ out) {
     const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (e >= nblocks * 32) return;
@@ -598,6 +633,17 @@ void adamw(float* value, float* m, float* v, float* grad, const uint8_t* decay_m
 
 void q8_0_to_f16(const uint8_t* blocks, long nblocks, f16* out, cudaStream_t s) {
     q8_f16_kernel<<<blocks_for(nblocks * 32, 256), 256, 0, s>>>(blocks, nblocks, out);
+}
+
+void q8_0_split(const uint8_t* blocks, int rows, int cols, uint8_t* q, f16* d, cudaStream_t s) {
+    const long n = (long)rows * (cols / 32);
+    q8_split_kernel<<<blocks_for(n, 256), 256, 0, s>>>(blocks, rows, cols, q, d);
+}
+
+void q8_view_to_f16(const uint8_t* q, long ldq, const f16* d, long ldd, int rows, int cols, f16* out, long ldo,
+                    cudaStream_t s) {
+    const long n8 = (long)rows * cols / 8;  // cols is a multiple of 32
+    q8_view_f16_kernel<<<blocks_for(n8, 256), 256, 0, s>>>(q, ldq, d, ldd, rows, cols, out, ldo);
 }
 
 void q8_0_to_f32(const uint8_t* blocks, long nblocks, float* out, cudaStream_t s) {

@@ -142,9 +142,20 @@ namespace {
 
 const char* const kTargets[7] = {"self.qkv", "self.out", "cross.q", "cross.kv", "cross.out", "ff.0", "ff.2"};
 
+// A frozen 2-D weight [rows = out][cols = in]: f16 (bound as F32 / F16), or a Q8_0 weight kept
+// as its blocks' two fields apart: quants biased to unsigned (q + 128) [rows][cols] and f16 block
+// scales transposed [cols / 32][rows].  Q8_0 weights are not expanded in HBM for the projection
+// GEMMs: the GEMM's converter warps multiply quants by scales in shared memory (gemm_tc.cu).
+struct Weight {
+    f16* h = nullptr;
+    uint8_t* q = nullptr;
+    f16* d = nullptr;
+    int rows = 0, cols = 0;
+};
+
 struct Proj {
     int in = 0, out = 0;
-    f16* W = nullptr;
+    Weight W;
     bool bound = false;
     bool adapted = false, dora = false;
     int r = 0, RP = 0;
@@ -210,9 +221,9 @@ struct act_ctx {
 
     std::vector<Layer> layers;
     // MelodyFlow globals
-    f16 *in_proj = nullptr, *out_proj = nullptr, *cond_w = nullptr;
+    Weight in_proj, out_proj, cond_w;
     float *cond_b = nullptr, *te0 = nullptr, *te2 = nullptr, *onw = nullptr, *onb = nullptr;
-    std::vector<f16*> skip;
+    std::vector<Weight> skip;
     std::vector<float> rope_ff;
     float* rope = nullptr;
     // backward gradient scale: a power of two near the loss's divisor (T * latent for the MSE,
@@ -222,7 +233,7 @@ struct act_ctx {
     // MusicGen globals
     std::vector<float*> emb;
     float** emb_dev = nullptr;
-    std::vector<f16*> head;
+    std::vector<Weight> head;
     float* pos = nullptr;
     std::map<std::string, bool> bound;
 
@@ -291,6 +302,10 @@ struct act_ctx {
     bool use_tc = true;
     // which kernel family each launch was issued to (ACT_PATH_*), counted as the step is issued
     int64_t path_count[ACT_PATH_COUNT] = {};
+    // f16 expansions of Q8_0 weights for the paths that read f16 weights (DoRA's weight products,
+    // shapes the fused GEMM does not take): two per stream, sized for the largest weight
+    f16* wscratch[2][2] = {};
+    long wscratch_elems = 0;
 
     // ------------------------------------------------------------------------------------
     template <class Tp>
@@ -346,6 +361,39 @@ struct act_ctx {
         evnext = 0;
     }
 
+    // B segment seg (1, 2) of g reads weight w from column c0: K-major (B(n, k) = w[n][c0 + k],
+    // the forward) or MN-major (B(n, k) = w[k][c0 + n], the input gradient)
+    static void set_b(GemmArgs& g, int seg, const Weight& w, bool kmajor, int c0 = 0) {
+        g.b_kmajor = kmajor;
+        const f16* h = w.h ? w.h + c0 : nullptr;
+        const uint8_t* q = w.q ? w.q + c0 : nullptr;
+        const f16* d = w.q ? w.d + (long)(c0 / 32) * w.rows : nullptr;
+        if (seg == 1) { g.B1 = h; g.B1q = q; g.B1d = d; g.ldb1 = w.cols; g.ldd1 = w.rows; }
+        else { g.B2 = h; g.B2q = q; g.B2d = d; g.ldb2 = w.cols; g.ldd2 = w.rows; }
+    }
+    // f16 view of a whole weight: itself, or its expansion into this stream's scratch slot
+    const f16* weight_h(const Weight& w, int slot = 0) {
+        if (w.h) return w.h;
+        f16* out = wscratch[in_side ? 1 : 0][slot];
+        timed(2, 0, 0, [&] { q8_view_to_f16(w.q, w.cols, w.d, w.rows, w.rows, w.cols, out, w.cols, stream); });
+        return out;
+    }
+    // A Q8_0 segment that the fused path cannot take: expand its view into scratch first
+    void expand_q8(GemmArgs& g) {
+        for (int seg = 1; seg <= 2; ++seg) {
+            const uint8_t* q = seg == 1 ? g.B1q : g.B2q;
+            if (!q || (seg == 2 && g.K2 <= 0)) continue;
+            const int K = seg == 1 ? g.K1 : g.K2;
+            const int rows = g.b_kmajor ? g.N : K, cols = g.b_kmajor ? K : g.N;
+            f16* out = wscratch[in_side ? 1 : 0][seg - 1];
+            const f16* d = seg == 1 ? g.B1d : g.B2d;
+            const long ldq = seg == 1 ? g.ldb1 : g.ldb2, ldd = seg == 1 ? g.ldd1 : g.ldd2;
+            timed(2, 0, 0, [&] { q8_view_to_f16(q, ldq, d, ldd, rows, cols, out, cols, stream); });
+            if (seg == 1) { g.B1 = out; g.B1q = nullptr; g.B1d = nullptr; g.ldb1 = cols; }
+            else { g.B2 = out; g.B2q = nullptr; g.B2d = nullptr; g.ldb2 = cols; }
+        }
+    }
+
     void run_gemm(const GemmArgs& g0, int cls = 0) {
         const double fl = 2.0 * g0.M * g0.N * (double)(g0.K1 + g0.K2);
         GemmArgs g = g0;
@@ -355,6 +403,7 @@ struct act_ctx {
             g.sk_part = sk_part;
             g.sk_flag = sk_flag;
         }
+        if ((g.B1q || g.B2q) && !(use_tc && gemm_tc_supported(g))) expand_q8(g);
         if (use_tc && gemm_tc_supported(g)) {
             ++path_count[ACT_PATH_GEMM_TC];
             timed(cls, fl, 0, [&] { gemm_tc_auto(g, kerr, stream); });
@@ -538,7 +587,7 @@ struct act_ctx {
             run_rank(k, u);
         }
         e.M = (int)rows; e.N = p.out; e.K1 = p.in;
-        e.A1 = X; e.lda1 = p.in; e.B1 = p.W; e.ldb1 = p.in;
+        e.A1 = X; e.lda1 = p.in; set_b(e, 1, p.W, true);
         if (p.adapted) {
             e.K2 = p.RP; e.A2 = U; e.lda2 = p.RP; e.B2 = p.B_h; e.ldb2 = p.RP;
         }
@@ -595,7 +644,7 @@ struct act_ctx {
             return;
         }
         e.M = (int)rows; e.N = p.in; e.K1 = p.out;
-        e.A1 = dYl; e.lda1 = p.out; e.B1 = p.W; e.ldb1 = p.in; e.b_kmajor = false;
+        e.A1 = dYl; e.lda1 = p.out; set_b(e, 1, p.W, false);
         if (p.adapted) {
             e.K2 = p.RP; e.A2 = dU; e.lda2 = p.RP; e.B2 = p.A_h; e.ldb2 = p.in;
         }
@@ -611,7 +660,7 @@ struct act_ctx {
                 if (!p.dora) continue;
                 GemmArgs a;
                 a.M = p.out; a.N = p.RP; a.K1 = p.in;
-                a.A1 = p.W; a.lda1 = p.in; a.B1 = p.A_h; a.ldb1 = p.in;
+                a.A1 = weight_h(p.W); a.lda1 = p.in; a.B1 = p.A_h; a.ldb1 = p.in;
                 a.mode = EPI_STORE_F32; a.out = p.P; a.ldo = p.RP;
                 run_gemm(a, 2);
                 timed(2, 0, 0, [&] {
@@ -634,12 +683,13 @@ struct act_ctx {
                 GemmArgs a;  // gA += BD^T W
                 a.M = p.RP; a.N = p.in; a.K1 = p.out;
                 a.A1 = p.BD; a.lda1 = p.RP; a.a_kmajor = false;
-                a.B1 = p.W; a.ldb1 = p.in; a.b_kmajor = false;
+                const f16* Wh = weight_h(p.W);
+                a.B1 = Wh; a.ldb1 = p.in; a.b_kmajor = false;
                 a.mode = EPI_ATOMIC_F32; a.alpha = inv_gscale; a.out = grad + p.offA; a.ldo = p.in; a.mvalid = p.r;
                 a.splitk = splitk_for((p.in + 127) / 128, (p.out + 63) / 64);
                 SkinnyArgs k;  // the same as (W^T BD)^T over the out dimension
                 k.M = p.in; k.K = p.out; k.nb = p.r;
-                k.A = p.W; k.lda = p.in; k.a_mn = true; k.B = p.BD; k.ldb = p.RP; k.b_mn = true;
+                k.A = Wh; k.lda = p.in; k.a_mn = true; k.B = p.BD; k.ldb = p.RP; k.b_mn = true;
                 k.kind = SKINNY_ACC_T; k.alpha = inv_gscale; k.out = grad + p.offA; k.ldo = p.in;
                 run_rank(k, a);
             }
@@ -855,11 +905,11 @@ struct act_ctx {
         {
             GemmArgs c;  // context = hidden cond_proj^T + bias
             c.M = (int)crows; c.N = D; c.K1 = md.cond_dim; c.A1 = hidden_h; c.lda1 = md.cond_dim;
-            c.B1 = cond_w; c.ldb1 = md.cond_dim; c.mode = EPI_BIAS_F16; c.bias = cond_b; c.out = ctx_h; c.ldo = D;
+            set_b(c, 1, cond_w, true); c.mode = EPI_BIAS_F16; c.bias = cond_b; c.out = ctx_h; c.ldo = D;
             run_gemm(c, 0);
             GemmArgs x;  // in_proj
             x.M = (int)rows; x.N = D; x.K1 = md.latent_dim; x.A1 = x0; x.lda1 = md.latent_dim;
-            x.B1 = in_proj; x.ldb1 = md.latent_dim; x.mode = EPI_STORE_F32; x.out = x0f; x.ldo = D;
+            set_b(x, 1, in_proj, true); x.mode = EPI_STORE_F32; x.out = x0f; x.ldo = D;
             run_gemm(x, 0);
         }
         for (int l = 0; l < L; ++l) {
@@ -870,7 +920,7 @@ struct act_ctx {
                 GemmArgs k;
                 k.M = (int)rows; k.N = D; k.K1 = D; k.K2 = D;
                 k.A1 = xprev_h; k.lda1 = D; k.A2 = layers[y.src].xsave_h; k.lda2 = D;
-                k.B1 = skip[y.proj]; k.ldb1 = 2 * D; k.B2 = skip[y.proj] + D; k.ldb2 = 2 * D;
+                set_b(k, 1, skip[y.proj], true); set_b(k, 2, skip[y.proj], true, D);
                 k.mode = EPI_STORE_F32; k.out = y.xin; k.ldo = D;
                 run_gemm(k, 0);
             }
@@ -880,7 +930,7 @@ struct act_ctx {
         timed(2, 0, 0, [&] { layernorm_fwd(last.xout, onw, onb, nullptr, T, xo, muo, rso, (int)rows, D, md.norm_eps, stream); });
         {
             GemmArgs o;
-            o.M = (int)rows; o.N = md.latent_dim; o.K1 = D; o.A1 = xo; o.lda1 = D; o.B1 = out_proj; o.ldb1 = D;
+            o.M = (int)rows; o.N = md.latent_dim; o.K1 = D; o.A1 = xo; o.lda1 = D; set_b(o, 1, out_proj, true);
             o.mode = EPI_STORE_F32; o.out = outp; o.ldo = md.latent_dim;
             run_gemm(o, 0);
         }
@@ -889,7 +939,7 @@ struct act_ctx {
         {
             GemmArgs d;
             d.M = (int)rows; d.N = D; d.K1 = md.latent_dim; d.A1 = dout; d.lda1 = md.latent_dim;
-            d.B1 = out_proj; d.ldb1 = D; d.b_kmajor = false; d.mode = EPI_STORE_F32; d.out = dtmp; d.ldo = D;
+            set_b(d, 1, out_proj, false); d.mode = EPI_STORE_F32; d.out = dtmp; d.ldo = D;
             run_gemm(d, 0);
         }
         timed(2, 0, 0, [&] {
@@ -911,10 +961,10 @@ struct act_ctx {
             if (via_skip) {
                 GemmArgs a;  // d x_prev = dx Wskip[:, :D]
                 a.M = (int)rows; a.N = D; a.K1 = D; a.A1 = dxh; a.lda1 = D;
-                a.B1 = skip[y.proj]; a.ldb1 = 2 * D; a.b_kmajor = false; a.mode = EPI_STORE_F32; a.out = dx; a.ldo = D;
+                set_b(a, 1, skip[y.proj], false); a.mode = EPI_STORE_F32; a.out = dx; a.ldo = D;
                 run_gemm(a, 0);
                 GemmArgs b = a;  // d saved += dx Wskip[:, D:]
-                b.B1 = skip[y.proj] + D; b.mode = EPI_ACCUM_F32; b.out = layers[y.src].dsaved;
+                set_b(b, 1, skip[y.proj], false, D); b.mode = EPI_ACCUM_F32; b.out = layers[y.src].dsaved;
                 run_gemm(b, 0);
                 prepare_dxh(l - 1, n);
             }
@@ -948,7 +998,7 @@ struct act_ctx {
                 f16* dl = dlogits + ((long)(b * nq + q) * sel) * card;
                 GemmArgs hgm;
                 hgm.M = sel; hgm.N = card; hgm.K1 = D; hgm.A1 = xo + r0 * D; hgm.lda1 = D;
-                hgm.B1 = head[q]; hgm.ldb1 = D; hgm.mode = EPI_STORE_F32; hgm.out = lg; hgm.ldo = card;
+                set_b(hgm, 1, head[q], true); hgm.mode = EPI_STORE_F32; hgm.out = lg; hgm.ldo = card;
                 run_gemm(hgm, 0);
                 timed(2, 0, 0, [&] {
                     mg_cross_entropy(lg, sel, card, d_tgt + (long)(b * nq + q) * sel, sel * nq, inv_nsel,
@@ -956,7 +1006,7 @@ struct act_ctx {
                 });
                 GemmArgs dg;
                 dg.M = sel; dg.N = D; dg.K1 = card; dg.A1 = dl; dg.lda1 = card;
-                dg.B1 = head[q]; dg.ldb1 = D; dg.b_kmajor = false;
+                set_b(dg, 1, head[q], false);
                 dg.mode = EPI_ACCUM_F32; dg.out = dtmp + r0 * D; dg.ldo = D;
                 run_gemm(dg, 0);
             }
@@ -1232,7 +1282,8 @@ struct act_ctx {
         const std::string name = cname;
         long rows = 0, cols = 0;
         enum { DST_F16, DST_F32, DST_HOST } dst_kind = DST_F16;
-        void** dst = nullptr;
+        void** dst = nullptr;    // fp32 destinations
+        Weight* wdst = nullptr;  // 2-D weights (f16 or Q8_0)
         Proj* proj = nullptr;
         const std::string pre = mf ? "dit." : "lm.";
         auto layer_of = [&](const std::string& rest, int& l, std::string& tail) {
@@ -1258,16 +1309,16 @@ struct act_ctx {
             for (int t = 0; t < 7; ++t)
                 if (tail == std::string(kTargets[t]) + ".weight") {
                     proj = &y.p[t];
-                    dst = (void**)&proj->W;
+                    wdst = &proj->W;
                     rows = proj->out;
                     cols = proj->in;
                 }
         } else if (mf) {
-            if (rest == "in_proj.weight") { dst = (void**)&in_proj; rows = D; cols = md.latent_dim; }
-            else if (rest == "out_proj.weight") { dst = (void**)&out_proj; rows = md.latent_dim; cols = D; }
+            if (rest == "in_proj.weight") { wdst = &in_proj; rows = D; cols = md.latent_dim; }
+            else if (rest == "out_proj.weight") { wdst = &out_proj; rows = md.latent_dim; cols = D; }
             else if (rest == "time_embed.0.weight") { dst = (void**)&te0; dst_kind = DST_F32; rows = D; cols = md.time_dim; }
             else if (rest == "time_embed.2.weight") { dst = (void**)&te2; dst_kind = DST_F32; rows = D; cols = D; }
-            else if (rest == "cond_proj.weight") { dst = (void**)&cond_w; rows = D; cols = md.cond_dim; }
+            else if (rest == "cond_proj.weight") { wdst = &cond_w; rows = D; cols = md.cond_dim; }
             else if (rest == "cond_proj.bias") { dst = (void**)&cond_b; dst_kind = DST_F32; rows = 1; cols = D; }
             else if (rest == "out_norm.weight") { dst = (void**)&onw; dst_kind = DST_F32; rows = 1; cols = D; }
             else if (rest == "out_norm.bias") { dst = (void**)&onb; dst_kind = DST_F32; rows = 1; cols = D; }
@@ -1276,7 +1327,7 @@ struct act_ctx {
                 const int i = std::atoi(rest.c_str() + 5);
                 if (i < 0 || i >= md.n_skip || rest != "skip." + std::to_string(i) + ".weight")
                     throw Error(ACT_ERR_INVALID, "unexpected tensor: " + name);
-                dst = (void**)&skip[i]; rows = D; cols = 2 * D;
+                wdst = &skip[i]; rows = D; cols = 2 * D;
             } else if (rest == "latent_mean" || rest == "latent_std" || rest == "time_embed.0.bias") {
                 return;  // cache normalisation: not used by the step
             }
@@ -1288,12 +1339,12 @@ struct act_ctx {
                 const int q = std::atoi(rest.c_str() + (isemb ? 4 : 5));
                 if (q < 0 || q >= md.n_q) throw Error(ACT_ERR_INVALID, "unexpected tensor: " + name);
                 if (isemb) { dst = (void**)&emb[q]; dst_kind = DST_F32; rows = md.card + 1; cols = D; }
-                else { dst = (void**)&head[q]; rows = md.card; cols = D; }
+                else { wdst = &head[q]; rows = md.card; cols = D; }
             } else if (rest.rfind("cond_proj", 0) == 0) {
                 return;  // the trainer consumes already projected conditioning
             }
         }
-        if (!dst && dst_kind != DST_HOST) throw Error(ACT_ERR_INVALID, "unexpected tensor: " + name);
+        if (!dst && !wdst && dst_kind != DST_HOST) throw Error(ACT_ERR_INVALID, "unexpected tensor: " + name);
         const long n = rows * cols;
         size_t need = 0;
         if (type == ACT_TYPE_F32) need = (size_t)n * 4;
@@ -1328,16 +1379,25 @@ struct act_ctx {
             CK(cudaStreamSynchronize(stream));
             *dst = d;
         } else {
-            f16* d = dalloc<f16>(n);
+            Weight w;
+            w.rows = (int)rows;
+            w.cols = (int)cols;
             void* tmp = nullptr;
             CK(cudaMalloc(&tmp, need));
             CK(cudaMemcpyAsync(tmp, host, need, cudaMemcpyHostToDevice, stream));
-            if (type == ACT_TYPE_F32) f32_to_f16(static_cast<float*>(tmp), d, n, stream);
-            else if (type == ACT_TYPE_F16) CK(cudaMemcpyAsync(d, tmp, need, cudaMemcpyDeviceToDevice, stream));
-            else q8_0_to_f16(static_cast<uint8_t*>(tmp), n / 32, d, stream);
+            if (type == ACT_TYPE_Q8_0) {  // quants and scales apart; no f16 copy of the weight
+                w.q = dalloc<uint8_t>(n);
+                w.d = dalloc<f16>(n / 32);
+                q8_0_split(static_cast<uint8_t*>(tmp), (int)rows, (int)cols, w.q, w.d, stream);
+                wscratch_elems = std::max<long>(wscratch_elems, n);
+            } else {
+                w.h = dalloc<f16>(n);
+                if (type == ACT_TYPE_F32) f32_to_f16(static_cast<float*>(tmp), w.h, n, stream);
+                else CK(cudaMemcpyAsync(w.h, tmp, need, cudaMemcpyDeviceToDevice, stream));
+            }
             CK(cudaStreamSynchronize(stream));
             CK(cudaFree(tmp));
-            *dst = d;
+            *wdst = w;
         }
         if (proj) {
             proj->bound = true;
@@ -1529,6 +1589,9 @@ struct act_ctx {
             CK(cudaStreamSynchronize(stream));
         }
         allocate_activations();
+        if (wscratch_elems > 0)
+            for (auto& slots : wscratch)
+                for (auto& w : slots) w = dalloc<f16>(wscratch_elems);
         finalized = true;
     }
 
@@ -1731,10 +1794,10 @@ int act_create(act_ctx** out, int device, const act_model_desc* model, const act
     auto* ctx = new act_ctx();
     try {
         ctx->setup(device, model, adapter);
-        if (ctx->mf) ctx->skip.assign(model->n_skip, nullptr);
+        if (ctx->mf) ctx->skip.assign(model->n_skip, Weight());
         else {
             ctx->emb.assign(model->n_q, nullptr);
-            ctx->head.assign(model->n_q, nullptr);
+            ctx->head.assign(model->n_q, Weight());
         }
     } catch (const Error& e) {
         g_error = e.what();
@@ -2107,34 +2170,51 @@ int act_rank_gemm_f16(int device, int kind, const void* A, const void* B, float*
     }
 }
 
-int act_gemm_f16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path,
-                  int reps, float* ms_per_call) {
-    // Stand-alone check of the projection GEMM: C[M][N] (fp32) = A[M][K] . B(n,k), f16 inputs,
-    // B given as [N][K] (b_mn_major = 0) or [K][N] (1).  path 0 auto, 1 mma.sync, 2 tcgen05,
-    // 3 2-CTA (stream-K where it pays), 4 2-CTA 128-wide, 5 2-CTA whole tiles only.
-    void *dA = nullptr, *dB = nullptr, *dC = nullptr, *dsk = nullptr, *dflag = nullptr;
+namespace {
+
+// Stand-alone projection GEMM on host buffers: C[M][N] (fp32) = A[M][K] . B(n,k) with f16 A and
+// B either f16 (B) or the Q8_0 blocks of the weight (Bq8: [N][K] or [K][N] as b_mn_major says).
+int gemm_entry(int device, const void* A, const void* B, const void* Bq8, void* C, int M, int N, int K,
+               int b_mn_major, int path, int reps, float* ms_per_call) {
+    void *dA = nullptr, *dB = nullptr, *dC = nullptr, *dsk = nullptr, *dflag = nullptr, *dq = nullptr, *dd = nullptr;
     int* derr = nullptr;
     cudaStream_t st = nullptr;
     auto cleanup = [&] {
         if (st) cudaStreamSynchronize(st);
         cudaFree(dA); cudaFree(dB); cudaFree(dC); cudaFree(derr); cudaFree(dsk); cudaFree(dflag);
+        cudaFree(dq); cudaFree(dd);
         if (st) cudaStreamDestroy(st);
     };
     try {
-        if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0) throw Error(ACT_ERR_INVALID, "invalid GEMM arguments");
+        if (!A || !(B || Bq8) || !C || M <= 0 || N <= 0 || K <= 0) throw Error(ACT_ERR_INVALID, "invalid GEMM arguments");
+        const int wrows = b_mn_major ? K : N, wcols = b_mn_major ? N : K;  // the weight [out][in]
+        if (Bq8 && (wcols % 32 || path == 1 || path == 2))
+            throw Error(ACT_ERR_INVALID, "Q8_0 weights take the 2-CTA paths (0, 3, 4, 5) with whole blocks");
         CK(cudaSetDevice(device));
         CK(cudaStreamCreate(&st));
         CK(cudaMalloc(&dA, (size_t)M * K * 2));
-        CK(cudaMalloc(&dB, (size_t)N * K * 2));
         CK(cudaMalloc(&dC, (size_t)M * N * 4));
         CK(cudaMalloc(&derr, sizeof(int)));
         CK(cudaMemsetAsync(derr, 0, sizeof(int), st));
         CK(cudaMemcpyAsync(dA, A, (size_t)M * K * 2, cudaMemcpyHostToDevice, st));
-        CK(cudaMemcpyAsync(dB, B, (size_t)N * K * 2, cudaMemcpyHostToDevice, st));
         GemmArgs g;
         g.M = M; g.N = N; g.K1 = K;
         g.A1 = static_cast<const f16*>(dA); g.lda1 = K;
-        g.B1 = static_cast<const f16*>(dB); g.ldb1 = b_mn_major ? N : K; g.b_kmajor = !b_mn_major;
+        g.b_kmajor = !b_mn_major;
+        if (Bq8) {
+            const size_t nb = (size_t)N * K / 32;
+            CK(cudaMalloc(&dB, nb * 34));
+            CK(cudaMalloc(&dq, (size_t)N * K));
+            CK(cudaMalloc(&dd, nb * 2));
+            CK(cudaMemcpyAsync(dB, Bq8, nb * 34, cudaMemcpyHostToDevice, st));
+            q8_0_split(static_cast<const uint8_t*>(dB), wrows, wcols, static_cast<uint8_t*>(dq), static_cast<f16*>(dd), st);
+            g.B1q = static_cast<const uint8_t*>(dq); g.ldb1 = wcols;
+            g.B1d = static_cast<const f16*>(dd); g.ldd1 = wrows;
+        } else {
+            CK(cudaMalloc(&dB, (size_t)N * K * 2));
+            CK(cudaMemcpyAsync(dB, B, (size_t)N * K * 2, cudaMemcpyHostToDevice, st));
+            g.B1 = static_cast<const f16*>(dB); g.ldb1 = wcols;
+        }
         g.mode = EPI_STORE_F32; g.out = dC; g.ldo = N;
         const bool tc = path >= 2 || (path == 0 && gemm_tc_supported(g));
         if (tc && !gemm_tc_supported(g)) throw Error(ACT_ERR_INVALID, "shape not supported by the tcgen05 path");
@@ -2199,6 +2279,20 @@ int act_gemm_f16(int device, const void* A, const void* B, void* C, int M, int N
         cleanup();
         return ACT_ERR_INVALID;
     }
+}
+
+}  // namespace
+
+int act_gemm_f16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path,
+                 int reps, float* ms_per_call) {
+    // path 0 auto, 1 mma.sync, 2 tcgen05, 3 2-CTA (stream-K where it pays), 4 2-CTA 128-wide,
+    // 5 2-CTA whole tiles only
+    return gemm_entry(device, A, B, nullptr, C, M, N, K, b_mn_major, path, reps, ms_per_call);
+}
+
+int act_gemm_q8_0(int device, const void* A, const void* Bq8, void* C, int M, int N, int K, int b_mn_major, int path,
+                  int reps, float* ms_per_call) {
+    return gemm_entry(device, A, nullptr, Bq8, C, M, N, K, b_mn_major, path, reps, ms_per_call);
 }
 
 int act_attention(int device, const void* q, const void* k, const void* v, const void* dout, int clips, int T,

@@ -68,10 +68,13 @@ struct TcParams {
     // one ready counter per [pair][rank]
     float* sk_part;
     int* sk_flag;
+    // 2-CTA kernel, Q8_0 instantiation: bit i set when K segment i + 1 reads Q8_0 weights
+    int q8mask;
 };
 
 struct TcMaps {
     CUtensorMap a1, b1, a2, b2;
+    CUtensorMap s1, s2;   // Q8_0 segments: block scales (b1 / b2 then map the quants)
     CUtensorMap out, aux;  // epilogue stores: box 32 x 32, swizzle 128 B (fp32) / 64 B (f16)
     CUtensorMap out_h;    // f16 copy of an fp32 output
 };
@@ -531,16 +534,31 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(const __grid_const
 // Each CTA drains its 128 accumulator rows with 8 epilogue warps (warps 2..9): two per TMEM
 // lane quarter, each taking half of the tile's columns.
 
-// BNP: output columns of a pair tile (256 or 128); each CTA stages BNP / 2 rows of B
-template <int BNP>
+// BNP: output columns of a pair tile (256 or 128); each CTA stages BNP / 2 rows of B.
+// Q8: B arrives as Q8_0 weights.  The quants (biased to unsigned, BH x 64 bytes per k-block) and
+// their f16 block scales (BH x 2 values) come by TMA into a ring of raw slots of their own, which
+// the converter warps keep filled RSLOTS k-blocks ahead (the weights do not wait for the MMA to
+// free a stage); once a stage is free the CW converter warps turn its raw slot into the f16
+// operand tile.  The conversion is redone for every row tile, about two instructions per weight
+// element, so it gets as many warps as the epilogue: the Q8_0 kernel drains TMEM with 4
+// epilogue warps (one per lane quarter, all columns) and converts with 4, in the same 320
+// threads, and keeps one operand stage fewer to make room for the raw ring.
+template <int BNP, bool Q8 = false>
 struct Tc2Cfg {
     static constexpr int BH = BNP / 2;
+    static constexpr int EW = Q8 ? 4 : EPI_WARPS2;  // epilogue warps
+    static constexpr int CW = Q8 ? 4 : 0;           // converter warps
     static constexpr int A_BYTES = BM * BKE * 2;
     static constexpr int B_BYTES = BH * BKE * 2;
     static constexpr int STAGE = A_BYTES + B_BYTES;
-    static constexpr int STAGES = BNP == 256 ? 5 : 7;
-    static constexpr int EPI = EPI_WARPS2 * (EPI_OUT_BYTES + EPI_AUX_BYTES);
-    static constexpr int SMEM = STAGES * STAGE + EPI + 1024 + 256;
+    static constexpr int STAGES = (BNP == 256 ? 5 : 7) - (Q8 ? 1 : 0);
+    static constexpr int EPI = EW * (EPI_OUT_BYTES + EPI_AUX_BYTES);
+    static constexpr int Q_BYTES = BH * BKE;         // quants of this CTA's half of B, one k-block
+    static constexpr int S_BYTES = 2 * BH * 2;       // their f16 scales (BH * 64 / 32)
+    static constexpr int RAW = Q8 ? (Q_BYTES + S_BYTES + 1023) / 1024 * 1024 : 0;
+    static constexpr int RSLOTS = Q8 ? 8 : 0;
+    static constexpr int SMEM = STAGES * STAGE + EPI + RSLOTS * RAW + 1024 + 256;
+    static constexpr int THREADS = (2 + EW + CW) * 32;
     static constexpr uint32_t TMEM_COLS = 2 * BNP;
 };
 
@@ -587,6 +605,77 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
                  : "memory");
 }
 
+// Eight Q8_0 quants (biased: q + 128, one byte each) times their block scale -> eight f16.  The
+// biased quant goes into the mantissa of the f16 1024 + (q + 128) (byte permute), 1152 is
+// subtracted (exact), and one f16 multiply rounds q * d to nearest-even: the same single rounding
+// of the exact product that the bind-time dequantisation applies (fp32 d * q, exact, to f16).
+__device__ __forceinline__ uint4 q8x8_to_f16(uint2 u, uint32_t dd) {
+    const uint32_t w[4] = {__byte_perm(u.x, 0x64646464u, 0x5140), __byte_perm(u.x, 0x64646464u, 0x5342),
+                           __byte_perm(u.y, 0x64646464u, 0x5140), __byte_perm(u.y, 0x64646464u, 0x5342)};
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+    const __half2 d2 = *reinterpret_cast<const __half2*>(&dd);
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half2 v = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&w[i]), bias), d2);
+        o[i] = *reinterpret_cast<const uint32_t*>(&v);
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// One k-block of Q8_0 B for this CTA into its f16 operand slot, by NT converter threads (ct).
+// K-major (forward, B(n, k) = W[n][k]): raw quants [BH][64] bytes, scales [2][BH] (k / 32, n);
+// the operand is rows of 128 bytes with the 128-byte swizzle TMA would have applied.
+// MN-major (input gradient, B(n, k) = W[k][n]): raw quants [64][BH] bytes, scales [BH / 32][64]
+// (n / 32, k); the operand is BH / 64 boxes of [64 k][64 n] with the same swizzle.  Lanes read
+// consecutive 8-byte pieces of a row (conflict-free) and write whole swizzled 128-byte rows.
+template <int BH, bool B_MN, int NT>
+__device__ __forceinline__ void convert_q8_stage(const unsigned char* smem, uint32_t rq_off, uint32_t sb_off, int ct) {
+    const unsigned char* rq = smem + rq_off;
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(rq + BH * BKE);
+    unsigned char* sb = const_cast<unsigned char*>(smem) + sb_off;
+    // Every load of the k-block is issued before the first store: the compiler cannot tell the
+    // raw slot from the operand tile, so interleaved loads and stores would each wait for the
+    // shared-memory latency (long while the tensor core streams its operands).
+    if (!B_MN) {
+        constexpr int RPP = NT / 8;  // rows per pass: 8 chunks of 8 k per row
+        constexpr int IT = BH / RPP;
+        uint2 q[IT];
+        uint32_t d[IT];
+        const int c = ct & 7;
+#pragma unroll
+        for (int it = 0; it < IT; ++it) {
+            const int row = it * RPP + (ct >> 3);
+            q[it] = *reinterpret_cast<const uint2*>(rq + row * BKE + c * 8);
+            d[it] = sc[(c >> 2) * BH + row];
+        }
+#pragma unroll
+        for (int it = 0; it < IT; ++it) {
+            const int row = it * RPP + (ct >> 3);
+            *reinterpret_cast<uint4*>(sb + sw128(row, c)) = q8x8_to_f16(q[it], d[it] | (d[it] << 16));
+        }
+    } else {
+        constexpr int CPR = BH / 8;    // 8-wide chunks of n per k-row
+        constexpr int RPP = NT / CPR;  // k-rows per pass
+        constexpr int IT = BKE / RPP;
+        uint2 q[IT];
+        uint32_t d[IT];
+        const int c = ct % CPR;
+#pragma unroll
+        for (int it = 0; it < IT; ++it) {
+            const int k = it * RPP + ct / CPR;
+            q[it] = *reinterpret_cast<const uint2*>(rq + k * BH + c * 8);
+            d[it] = sc[(c >> 2) * BKE + k];
+        }
+#pragma unroll
+        for (int it = 0; it < IT; ++it) {
+            const int k = it * RPP + ct / CPR;
+            *reinterpret_cast<uint4*>(sb + (c >> 3) * 8192 + sw128(k, c & 7)) =
+                q8x8_to_f16(q[it], d[it] | (d[it] << 16));
+        }
+    }
+}
+
 // Work of one CTA pair.  Whole tiles (sk = 0): tiles pair, pair + npairs, ...  Stream-K
 // (sk = 1): the pair takes units [pair * U / npairs, (pair + 1) * U / npairs) of the U = tiles x
 // k-blocks units, tile-major.  The host enables stream-K only when there are at least as many
@@ -630,23 +719,29 @@ struct PairWork {
 constexpr int SK_WARP_FLOATS = 32 * 128;
 constexpr int SK_CTA_BYTES = EPI_WARPS2 * SK_WARP_FLOATS * 4;  // 128 KB: 4 stages of the 256-wide ring
 
-template <int BN2, bool B_MN, bool SK>
-__global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_constant__ TcMaps maps, const TcParams p) {
-    using Cfg = Tc2Cfg<BN2>;
+template <int BN2, bool B_MN, bool SK, bool Q8>
+__global__ void __launch_bounds__(Tc2Cfg<BN2, Q8>::THREADS, 1)
+    gemm_tc2_kernel(const __grid_constant__ TcMaps maps, const TcParams p) {
+    using Cfg = Tc2Cfg<BN2, Q8>;
     constexpr int BH2 = Cfg::BH;
     constexpr int S = Cfg::STAGES;
+    constexpr int R = Cfg::RSLOTS;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023) & ~1023u;
     unsigned char* smem = smem_raw + (base - raw);
-    const uint32_t bars = base + S * Cfg::STAGE + Cfg::EPI;
+    const uint32_t raw_off = S * Cfg::STAGE + Cfg::EPI;  // Q8: the raw ring
+    const uint32_t bars = base + raw_off + R * Cfg::RAW;
     auto full_bar = [&](int s) { return bars + 8 * s; };
     auto empty_bar = [&](int s) { return bars + 8 * (S + s); };
     auto tfull_bar = [&](int a) { return bars + 8 * (2 * S + a); };
     auto tempty_bar = [&](int a) { return bars + 8 * (2 * S + 2 + a); };
     const uint32_t drain_bar = bars + 8 * (2 * S + 4);
     const uint32_t part_bar = bars + 8 * (2 * S + 5);  // stream-K partial landed in the stages
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S * Cfg::STAGE + Cfg::EPI + 8 * (2 * S + 6));
+    auto raw_bar = [&](int r) { return bars + 8 * (2 * S + 6 + r); };  // Q8: raw slot r landed (this CTA)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + raw_off + R * Cfg::RAW + 8 * (2 * S + 6 + R));
+    // Q8: 16 bytes that the peer CTA's converters copy to the leader to count into full_bar
+    constexpr uint32_t SIG_OFF = (8 * (2 * S + 6 + R) + 4 + 15) / 16 * 16;
 
     if (threadIdx.x == 0) {
         prefetch_tmap(&maps.a1);
@@ -654,17 +749,24 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
         prefetch_tmap(&maps.a2);
         prefetch_tmap(&maps.b2);
         prefetch_tmap(&maps.out);
+        if (Q8) {
+            prefetch_tmap(&maps.s1);
+            prefetch_tmap(&maps.s2);
+        }
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_rank();
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(full_bar(s), 1);   // leader: one arrive_expect_tx for both CTAs' bytes
+            // leader: one arrive_expect_tx for both CTAs' bytes (Q8: plus the leader's converters'
+            // arrival; the peer's converters count in through the 16 bytes they copy here)
+            mbar_init(full_bar(s), Q8 ? 2 : 1);
             mbar_init(empty_bar(s), 1);  // each CTA: one commit from the leader
         }
+        for (int r = 0; r < R; ++r) mbar_init(raw_bar(r), 1);
         for (int a = 0; a < 2; ++a) {
             mbar_init(tfull_bar(a), 1);
-            mbar_init(tempty_bar(a), 2 * EPI_WARPS2);  // leader: both CTAs' epilogue warps
+            mbar_init(tempty_bar(a), 2 * Cfg::EW);  // leader: both CTAs' epilogue warps
         }
         mbar_init(drain_bar, 1);
         mbar_init(part_bar, 1);
@@ -696,6 +798,38 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
         bool ok = true;
         PairWork w(SK ? 1 : 0, nk, ntiles, pair, npairs);
         int tile, kb0, kb1, role = SK_FULL;
+        // Q8: the raw ring.  Conv k-block i (the i-th Q8_0 k-block of the schedule) uses slot
+        // i % R.  Waiting for stage s's release proves that the k-block S stages back has been
+        // converted, so its slot is free: with each Q8_0 k-block this thread issues the quants of
+        // the one R - S conv k-blocks ahead (the first R - S before the loop).
+        PairWork ahead(SK ? 1 : 0, nk, ntiles, pair, npairs);
+        int a_tile = 0, a_kb = 0, a_kb1 = 0, a_role, raw_issued = 0;
+        auto issue_raw = [&]() {
+            for (;;) {
+                while (a_kb >= a_kb1)
+                    if (!ahead.next(a_tile, a_kb, a_kb1, a_role)) return;
+                const int k = a_kb++;
+                if (!((p.q8mask >> (k >= nk1 ? 1 : 0)) & 1)) continue;
+                const bool seg2 = k >= nk1;
+                const int k0 = (seg2 ? k - nk1 : k) * BKE;
+                const int n0 = (a_tile / num_m2) * BN2 + (int)rank * BH2;
+                const CUtensorMap* mq = seg2 ? &maps.b2 : &maps.b1;
+                const CUtensorMap* msc = seg2 ? &maps.s2 : &maps.s1;
+                const int slot = raw_issued++ % R;
+                const uint32_t rq = base + raw_off + slot * Cfg::RAW, rsc = rq + Cfg::Q_BYTES;
+                mbar_expect_tx(raw_bar(slot), Cfg::Q_BYTES + Cfg::S_BYTES);
+                if (B_MN) {
+                    tma_load_2d(rq, mq, n0, k0, raw_bar(slot));
+                    tma_load_2d(rsc, msc, k0, n0 / 32, raw_bar(slot));
+                } else {
+                    tma_load_2d(rq, mq, k0, n0, raw_bar(slot));
+                    tma_load_2d(rsc, msc, n0, k0 / 32, raw_bar(slot));
+                }
+                return;
+            }
+        };
+        if (Q8)
+            for (int i = 0; i < R - S; ++i) issue_raw();
         while (ok && w.next(tile, kb0, kb1, role)) {
             const int mb = tile % num_m2, nb = tile / num_m2;
             for (int kb = kb0; kb < kb1; ++kb) {
@@ -706,9 +840,17 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
                 const int k0 = (seg2 ? kb - nk1 : kb) * BKE;
                 const uint32_t sa = base + s * Cfg::STAGE, sb = sa + Cfg::A_BYTES;
                 const uint32_t lbar = map_rank(full_bar(s), 0);
-                if (rank == 0) mbar_expect_tx(full_bar(s), 2 * Cfg::STAGE);
-                tma_load_2d_pair(sa, ma, k0, mb * 2 * BM + rank * BM, lbar);
                 const int n0 = nb * BN2 + rank * BH2;
+                if (Q8 && ((p.q8mask >> (seg2 ? 1 : 0)) & 1)) {
+                    // A only: B's quants come through the raw ring, for the converters
+                    if (rank == 0) mbar_expect_tx(full_bar(s), 2 * Cfg::A_BYTES + 16);
+                    tma_load_2d_pair(sa, ma, k0, mb * 2 * BM + rank * BM, lbar);
+                    issue_raw();
+                    if (++s == S) { s = 0; ph ^= 1; }
+                    continue;
+                }
+                if (rank == 0) mbar_expect_tx(full_bar(s), 2 * Cfg::STAGE + (Q8 ? 16 : 0));
+                tma_load_2d_pair(sa, ma, k0, mb * 2 * BM + rank * BM, lbar);
                 if (B_MN) {
 #pragma unroll
                     for (int j = 0; j < BH2 / 64; ++j) tma_load_2d_pair(sb + j * 8192, mbm, n0 + 64 * j, k0, lbar);
@@ -718,6 +860,12 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
                 if (++s == S) { s = 0; ph ^= 1; }
             }
         }
+        // no quants may still be landing when the CTA leaves (after a failed wait, the converters
+        // stop early): the latest load of each slot is waited for, bounded and regardless of the
+        // error word; on the normal path those phases completed long ago
+        if (Q8)
+            for (int i = raw_issued - 1; i >= 0 && i >= raw_issued - R; --i)
+                mbar_wait_drain(raw_bar(i % R), (uint32_t)((i / R) & 1));
         if (SK && ok && role == SK_PART_IN) {
             // The last item is the head of a split tile: once the next pair has published the
             // tile's tail (its first item), stream this CTA's 128 KB of it into the next four
@@ -784,13 +932,72 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
         }
         mma_commit_pair(map_rank(drain_bar, 0));
         mbar_wait(drain_bar, 0, p.err, 16);
+    } else if (Q8 && warp >= 2 + Cfg::EW) {
+        // ------------------------------------------------------------ Q8_0 converters (both CTAs)
+        // Same k-block schedule as the producer.  Per k-block: wait until the stage is free, wait
+        // for its raw slot (Q8_0 segments), write the f16 operand tile, make it visible to the
+        // tensor core (async proxy), and count this CTA into the leader's full barrier: a local
+        // arrival in the leader, a 16-byte DSMEM copy with complete_tx from the peer (an
+        // asynchronous signal: the converters go on while it travels).  The producer keeps the
+        // raw ring filled ahead of them.
+        constexpr int CT = (Cfg::CW ? Cfg::CW : 1) * 32;  // converter threads (the non-Q8 kernel has none)
+        const int ct = threadIdx.x - (2 + Cfg::EW) * 32;
+        const uint32_t leader_full0 = map_rank(full_bar(0), 0);
+        const uint32_t sig_local = bars + SIG_OFF, sig_leader = map_rank(bars + SIG_OFF, 0);
+        int s = 0, r = 0;
+        uint32_t ph = 0, rph = 0;  // operand-ring parity, raw-ring parity
+        PairWork w(SK ? 1 : 0, nk, ntiles, pair, npairs);
+        int tile, kb0, kb1, role;
+        bool ok = true;
+        while (ok && w.next(tile, kb0, kb1, role)) {
+            for (int kb = kb0; kb < kb1; ++kb) {
+                const bool conv = (p.q8mask >> (kb >= nk1 ? 1 : 0)) & 1;
+                bool got = mbar_wait(empty_bar(s), ph ^ 1, p.err, 22);
+                if (conv && got) {
+                    got = mbar_wait(raw_bar(r), rph, p.err, 21);
+                    if (got) {
+                        convert_q8_stage<BH2, B_MN, CT>(smem, raw_off + r * Cfg::RAW,
+                                                                  s * Cfg::STAGE + Cfg::A_BYTES, ct);
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    }
+                }
+                // all converter threads agree (and have written the tile) before the signal; on a
+                // failed wait they leave together (the MMA then gives up on its own bounded wait)
+                uint32_t all;
+                asm volatile(
+                    "{\n\t.reg .pred p, q;\n\t"
+                    "setp.ne.u32 p, %1, 0;\n\t"
+                    "bar.red.and.pred q, 1, %2, p;\n\t"
+                    "selp.u32 %0, 1, 0, q;\n\t}"
+                    : "=r"(all)
+                    : "r"(got ? 1u : 0u), "n"(CT)
+                    : "memory");
+                if (!all) {
+                    ok = false;
+                    break;
+                }
+                if (ct == 0) {
+                    if (rank == 0) {
+                        mbar_arrive(full_bar(s));
+                    } else {
+                        asm volatile(
+                            "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], 16, [%2];"
+                            ::"r"(sig_leader), "r"(sig_local), "r"(leader_full0 + 8 * s)
+                            : "memory");
+                    }
+                }
+                if (conv && ++r == R) { r = 0; rph ^= 1; }
+                if (++s == S) { s = 0; ph ^= 1; }
+            }
+        }
     } else if (warp >= 2) {
         // ------------------------------------------------------------ epilogue (both CTAs)
-        // TMEM lanes 32*quad .. 32*quad+31, columns coff .. coff + BN2/2 - 1 of the tile
-        const int ew = warp - 2, quad = warp & 3, coff = (ew >> 2) * (BN2 / 2);
+        // TMEM lanes 32*quad .. 32*quad+31, columns coff .. coff + WCOLS - 1 of the tile
+        constexpr int WCOLS = BN2 / (Cfg::EW / 4);  // columns per epilogue warp
+        const int ew = warp - 2, quad = warp & 3, coff = (ew >> 2) * WCOLS;
         EpiTiles tiles;
         tiles.o = smem + S * Cfg::STAGE + ew * EPI_OUT_BYTES;
-        tiles.x = smem + S * Cfg::STAGE + EPI_WARPS2 * EPI_OUT_BYTES + ew * EPI_AUX_BYTES;
+        tiles.x = smem + S * Cfg::STAGE + Cfg::EW * EPI_OUT_BYTES + ew * EPI_AUX_BYTES;
         tiles.o_s = smem_u32(tiles.o);
         tiles.x_s = smem_u32(tiles.x);
         const uint32_t leader_tempty0 = map_rank(tempty_bar(0), 0), leader_tempty1 = map_rank(tempty_bar(1), 0);
@@ -835,7 +1042,7 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
                 // tail of a split tile: raw fp32 accumulators to slot `pair`, then count this warp in
                 float4* dst = reinterpret_cast<float4*>(
                     p.sk_part + (((size_t)pair * 2 + rank) * EPI_WARPS2 + ew) * SK_WARP_FLOATS);
-                for (int c = 0; c < BN2 / 64; ++c) {
+                for (int c = 0; c < WCOLS / 32; ++c) {
                     uint32_t r[32];
                     tmem_ld32(trow + c * 32, r);
 #pragma unroll
@@ -858,7 +1065,7 @@ __global__ void __launch_bounds__(NTHREADS2, 1) gemm_tc2_kernel(const __grid_con
                 int m_base, rows, n0, nm, nr, nn;
                 tile_rows(tile, m_base, rows, n0);
                 tile_rows(ntile, nm, nr, nn);
-                epilogue_tile<BN2 / 64>(p, maps, trow, m_base, rows, n0, nm, nr, nn, tiles, lane, pre, part);
+                epilogue_tile<WCOLS / 32>(p, maps, trow, m_base, rows, n0, nm, nr, nn, tiles, lane, pre, part);
             }
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
@@ -908,6 +1115,43 @@ void make_map(CUtensorMap* map, const f16* ptr, long rows, long cols, long ld, i
                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+}
+
+// Raw (unswizzled) maps of a Q8_0 weight view: quants [rows][cols] (row stride ld bytes) and f16
+// scales [rows][cols] (row stride ld elements).
+void make_map_raw(CUtensorMap* map, const void* ptr, bool f16v, long rows, long cols, long ld, int box_cols,
+                  int box_rows) {
+    const int esz = f16v ? 2 : 1;
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * esz) % 16 || (box_cols * esz) % 16)
+        throw std::runtime_error("gemm_tc: Q8_0 operand not 16-byte aligned");
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * esz};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(map, f16v ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                             const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled (Q8_0) failed: " + std::to_string((int)r));
+}
+
+// B segment maps: f16 (128-byte swizzle, straight into the operand tile) or Q8_0 (quants and
+// scales into the raw ring).  K-major B is [N][K], MN-major [K][N]; bh = B rows per CTA.
+void make_b_maps(CUtensorMap* bmap, CUtensorMap* smap, const f16* B, const uint8_t* Bq, const f16* Bd, long ldb,
+                 long ldd, int K, int N, bool mn, int bh) {
+    if (!Bq) {
+        if (mn) make_map(bmap, B, K, N, ldb, 64, BKE);
+        else make_map(bmap, B, N, K, ldb, BKE, bh);
+        *smap = *bmap;
+        return;
+    }
+    if (mn) {
+        make_map_raw(bmap, Bq, false, K, N, ldb, bh, BKE);          // bh quants (n) x 64 rows (k)
+        make_map_raw(smap, Bd, true, N / 32, K, ldd, BKE, bh / 32);  // 64 scales (k) x bh / 32 rows
+    } else {
+        make_map_raw(bmap, Bq, false, N, K, ldb, BKE, bh);          // 64 quants (k) x bh rows (n)
+        make_map_raw(smap, Bd, true, K / 32, N, ldd, bh, 2);         // bh scales (n) x 2 rows (k / 32)
+    }
 }
 
 // Epilogue store maps: the output as fp32 (box 32 x 32, 128-byte swizzle) or f16 (box 32 x 32,
@@ -994,21 +1238,20 @@ bool sk_pays(int bn2, int tiles, int pairs, const GemmArgs& a) {
     return share + 12 < 0.92 * rounds * nk;
 }
 
-template <int BN2, bool B_MN>
+template <int BN2, bool B_MN, bool Q8>
 void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
-    using Cfg = Tc2Cfg<BN2>;
+    using Cfg = Tc2Cfg<BN2, Q8>;
     constexpr int BH2 = Cfg::BH;
     TcMaps maps;
     make_map(&maps.a1, a.A1, a.M, a.K1, a.lda1, BKE, BM);
-    if (B_MN) make_map(&maps.b1, a.B1, a.K1, a.N, a.ldb1, 64, BKE);
-    else make_map(&maps.b1, a.B1, a.N, a.K1, a.ldb1, BKE, BH2);
+    make_b_maps(&maps.b1, &maps.s1, a.B1, a.B1q, a.B1d, a.ldb1, a.ldd1, a.K1, a.N, B_MN, BH2);
     if (a.K2 > 0) {
         make_map(&maps.a2, a.A2, a.M, a.K2, a.lda2, BKE, BM);
-        if (B_MN) make_map(&maps.b2, a.B2, a.K2, a.N, a.ldb2, 64, BKE);
-        else make_map(&maps.b2, a.B2, a.N, a.K2, a.ldb2, BKE, BH2);
+        make_b_maps(&maps.b2, &maps.s2, a.B2, a.B2q, a.B2d, a.ldb2, a.ldd2, a.K2, a.N, B_MN, BH2);
     } else {
         maps.a2 = maps.a1;
         maps.b2 = maps.b1;
+        maps.s2 = maps.s1;
     }
     make_epilogue_maps(maps, a);
     TcParams p;
@@ -1020,8 +1263,10 @@ void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
     p.rope = a.rope; p.rope_T = a.rope_T; p.rope_cols = a.rope_cols;
     p.out_h = (a.mode == EPI_STORE_F32 || a.mode == EPI_ACCUM_F32 || a.mode == EPI_RESID_F32) ? a.out_h : nullptr;
     p.sk_part = a.sk_part; p.sk_flag = a.sk_flag;
-    auto whole = gemm_tc2_kernel<BN2, B_MN, false>;
-    auto split = gemm_tc2_kernel<BN2, B_MN, BN2 == 256>;
+    p.q8mask = (a.B1q ? 1 : 0) | (a.K2 > 0 && a.B2q ? 2 : 0);
+    // no stream-K with Q8_0 weights: its partial-tile layout assumes 8 epilogue warps
+    auto whole = gemm_tc2_kernel<BN2, B_MN, false, Q8>;
+    auto split = gemm_tc2_kernel<BN2, B_MN, BN2 == 256 && !Q8, Q8>;
     static DeviceOnce once;
     once([&] {
         for (auto k : {whole, split}) {
@@ -1032,10 +1277,10 @@ void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
     const int num_sms = current_sm_count();
     const int tiles = ((a.M + 2 * BM - 1) / (2 * BM)) * (a.N / BN2);
     const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
-    const auto kern = sk_pays(BN2, tiles, pairs, a) ? split : whole;
+    const auto kern = !Q8 && sk_pays(BN2, tiles, pairs, a) ? split : whole;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
-    cfg.blockDim = dim3(NTHREADS2, 1, 1);
+    cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
     cfg.dynamicSmemBytes = Cfg::SMEM;
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
@@ -1051,10 +1296,22 @@ void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
 
 }  // namespace
 
+namespace {
+bool q8_args(const GemmArgs& a) { return a.B1q || (a.K2 > 0 && a.B2q); }
+bool q8_segment_ok(const uint8_t* q, const f16* d, long ldq, long ldd, int K) {
+    const uintptr_t al = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(d);
+    return d && (al & 15) == 0 && ldq % 16 == 0 && (ldd * 2) % 16 == 0 && K % BKE == 0;
+}
+}  // namespace
+
 bool gemm_tc_supported(const GemmArgs& a) {
     if (!a.a_kmajor) return false;
     if (a.M < BM || a.N % 128 || a.K1 % BKE || a.K1 <= 0 || a.splitk != 1) return false;
-    if (a.K2 && (a.K2 % 8 || !a.A2 || !a.B2)) return false;
+    if (a.K2 && (a.K2 % 8 || !a.A2 || !(a.B2 || a.B2q))) return false;
+    // Q8_0 weights: the 2-CTA kernel only (it has the converter warps)
+    if (q8_args(a) && (a.M <= BM || (a.B1q && !q8_segment_ok(a.B1q, a.B1d, a.ldb1, a.ldd1, a.K1)) ||
+                       (a.K2 > 0 && a.B2q && !q8_segment_ok(a.B2q, a.B2d, a.ldb2, a.ldd2, a.K2))))
+        return false;
     if (a.mode == EPI_ATOMIC_F32 || a.nvalid < a.N || a.mvalid < a.M) return false;
     if ((a.mode == EPI_GELU_BWD || a.mode == EPI_GELU_BWD_D) && a.aux)
         return false;  // its pre-activation input occupies the side tile
@@ -1070,12 +1327,13 @@ bool gemm_tc_supported(const GemmArgs& a) {
 bool gemm_tc2_supported(const GemmArgs& a) { return gemm_tc_supported(a) && a.M > BM; }
 
 void gemm_tc2_width(const GemmArgs& a, int* err, cudaStream_t s, int width) {
+    const bool q8 = q8_args(a);
     if (width == 256) {
-        if (a.b_kmajor) launch_tc2<256, false>(a, err, s);
-        else launch_tc2<256, true>(a, err, s);
+        if (a.b_kmajor) q8 ? launch_tc2<256, false, true>(a, err, s) : launch_tc2<256, false, false>(a, err, s);
+        else q8 ? launch_tc2<256, true, true>(a, err, s) : launch_tc2<256, true, false>(a, err, s);
     } else {
-        if (a.b_kmajor) launch_tc2<128, false>(a, err, s);
-        else launch_tc2<128, true>(a, err, s);
+        if (a.b_kmajor) q8 ? launch_tc2<128, false, true>(a, err, s) : launch_tc2<128, false, false>(a, err, s);
+        else q8 ? launch_tc2<128, true, true>(a, err, s) : launch_tc2<128, true, false>(a, err, s);
     }
 }
 
@@ -1094,14 +1352,14 @@ void gemm_tc_auto(const GemmArgs& a, int* err, cudaStream_t s) {
     auto rounds = [&](long tiles, long slots) { return (tiles + slots - 1) / slots; };
     const long m1 = (a.M + BM - 1) / BM, m2 = (a.M + 2 * BM - 1) / (2 * BM), pairs = num_sms / 2;
     const int w1 = a.N % 256 == 0 ? 256 : 128;
-    double best = rounds(m1 * (a.N / w1), num_sms) * (double)w1 * eff[0];
+    double best = q8_args(a) ? 1e30 : rounds(m1 * (a.N / w1), num_sms) * (double)w1 * eff[0];
     int choice = 0;
     if (gemm_tc2_supported(a)) {
         if (a.N % 256 == 0) {
             const long t2 = m2 * (a.N / 256);
             // stream-K spreads the k-blocks evenly: cost by the mean share plus its fix-up
             const long nk = (a.K1 + BKE - 1) / BKE + (a.K2 + BKE - 1) / BKE;
-            const double c = sk_pays(256, (int)t2, (int)std::min(t2, pairs), a)
+            const double c = !q8_args(a) && sk_pays(256, (int)t2, (int)std::min(t2, pairs), a)
                                  ? ((double)t2 * nk / pairs + 12.0) / nk * 256.0 * eff[1]
                                  : rounds(t2, pairs) * 256.0 * eff[1];
             if (c < best) { best = c; choice = 1; }
@@ -1114,6 +1372,7 @@ void gemm_tc_auto(const GemmArgs& a, int* err, cudaStream_t s) {
 }
 
 void gemm_tc(const GemmArgs& a, int* err, cudaStream_t s) {
+    if (q8_args(a)) throw std::runtime_error("gemm_tc: Q8_0 weights need the 2-CTA kernel");
     const long tiles256 = (long)((a.M + BM - 1) / BM) * (a.N / 256);
     static const int force_bn = [] {
         const char* e = std::getenv("ACTRAIN_TC_BN");  // tuning experiments only

@@ -68,6 +68,18 @@ struct GemmArgs {
     int* sk_flag = nullptr;
     // fp32 output modes (STORE / ACCUM / RESID): also store f16(out), row stride ldo
     f16* out_h = nullptr;
+    // Q8_0 weights in place of B1 / B2 (tcgen05 2-CTA path; the B pointer of that segment stays
+    // null): Bq the quants biased to unsigned (q + 128), laid out exactly as B would be ([N][K]
+    // K-major or [K][N] MN-major, row stride ldb), Bd the f16 block scales of those quants,
+    // transposed: one row per 32 quant columns, [cols / 32][rows] with row stride ldd (a weight
+    // [out][in] keeps its scales as [in / 32][out]).  Each quant is multiplied by its scale on
+    // the way into the MMA.
+    const uint8_t* B1q = nullptr;
+    const f16* B1d = nullptr;
+    long ldd1 = 0;
+    const uint8_t* B2q = nullptr;
+    const f16* B2d = nullptr;
+    long ldd2 = 0;
 };
 long gemm_sk_part_floats(int num_sms);
 int gemm_sk_flag_count(int num_sms);
@@ -100,8 +112,15 @@ bool skinny_supported(const SkinnyArgs& a);
 void skinny_gemm(const SkinnyArgs& a, int* err, cudaStream_t s);
 
 // tcgen05 path with the tile shape chosen per problem: 2-CTA 256 x 256 tiles unless they need
-// more waves over the SMs than 1-CTA 128 x 256 tiles
+// more waves over the SMs than 1-CTA 128 x 256 tiles (Q8_0 segments: 2-CTA only)
 void gemm_tc_auto(const GemmArgs& a, int* err, cudaStream_t s);
+// Q8_0 blocks of a [rows][cols] weight (rows of cols / 32 blocks of 34 bytes: fp16 d, int8
+// q[32]) -> quants biased to unsigned, q + 128, [rows][cols] and f16 scales [cols / 32][rows]
+void q8_0_split(const uint8_t* blocks, int rows, int cols, uint8_t* q, f16* d, cudaStream_t s);
+// Q8_0 weight view -> f16: out[r][c] = (q[r * ldq + c] - 128) * d[(c / 32) * ldd + r], rounded to
+// f16 (the values the fused path feeds the MMA), for the paths that take f16 weights
+void q8_view_to_f16(const uint8_t* q, long ldq, const f16* d, long ldd, int rows, int cols, f16* out, long ldo,
+                    cudaStream_t s);
 
 // ---------------------------------------------------------------------------------------
 // attention over token-major q/k/v (head h at columns h*64 .. h*64+63), head_dim 64.

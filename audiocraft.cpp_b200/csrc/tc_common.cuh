@@ -71,6 +71,15 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
     return mbar_try(bar, parity) || mbar_wait_slow(bar, parity, err, code);
 }
 
+// Wait for copies this thread issued to land before its CTA exits, after another wait failed:
+// bounded (limit_ns) but not cut short by the error word, which is already set by then.
+static __device__ __noinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity,
+                                                    unsigned long long limit_ns = 100000000ull) {
+    const unsigned long long t0 = globaltimer();
+    while (!mbar_try_sleep(bar, parity, 20000u))
+        if (globaltimer() - t0 > limit_ns) return;
+}
+
 // Global flags between CTAs of one grid (all co-resident): release add by the producer side,
 // bounded acquire poll by the consumer side.
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {

@@ -249,11 +249,19 @@ def run_sweep(kind, reps):
                         if path == 3 and N % 256:
                             continue
                         a, b = bits((M, K)), bits((K, N) if b_mn else (N, K))
-                        _, ms = A.gemm_f16(a, b, M, N, K, b_mn, path, reps=reps)
+                        q8 = os.environ.get("SWEEP_Q8") == "1"
+                        if q8:  # the same shape with the weight as Q8_0 blocks, dequantised in the GEMM
+                            if path not in (0, 3, 5):
+                                continue
+                            wq = q8_0(0.02 * rng.standard_normal((K, N) if b_mn else (N, K)).astype(np.float32))
+                            _, ms = A.gemm_q8_0(a, wq, M, N, K, b_mn, path, reps=reps)
+                        else:
+                            _, ms = A.gemm_f16(a, b, M, N, K, b_mn, path, reps=reps)
                         tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
                         print(json.dumps({"sweep": "gemm", "M": M, "N": N, "K": K,
                                           "layout": "NN (dX = dY W)" if b_mn else "NT (Y = X W^T)",
-                                          "kernel": {1: "mma.sync", 2: "tcgen05", 3: "tcgen05_pair"}[path], "ms": ms,
+                                          "kernel": {1: "mma.sync", 2: "tcgen05", 3: "tcgen05_pair"}[path],
+                                          "weights": "q8_0" if q8 else "f16", "ms": ms,
                                           "tflops": tf, "frac_of_peak": tf / peak}), flush=True)
     else:
         for H in (16, 24):

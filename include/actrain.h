@@ -186,6 +186,13 @@ double act_step_flops(act_ctx* ctx, int n);
  * re-run reps times back to back and *ms_per_call receives the mean device time */
 int act_gemm_f16(int device, const void* A, const void* B, void* C, int M, int N, int K, int b_mn_major, int path,
                  int reps, float* ms_per_call);
+/* The same with B given as the Q8_0 blocks (34 bytes each, tools/ac-quantize.cpp:161) of the
+ * weight [N][K] (b_mn_major 0) or [K][N] (1), kept quantised on the device: the 2-CTA kernel's
+ * converter warps dequantise each k-block in shared memory (paths 0, 3, 4, 5).  The MMA sees the
+ * values act_q8_0_dequant gives, so C equals act_gemm_f16 on that dequantised B bit for bit when
+ * both run the same tile schedule (paths 4 and 5). */
+int act_gemm_q8_0(int device, const void* A, const void* Bq8, void* C, int M, int N, int K, int b_mn_major, int path,
+                  int reps, float* ms_per_call);
 /* stand-alone rank-block product (tests and the kernel sweep): C = alpha * A(M x K) B(K x nb),
  * nb <= 64, f16 A stored [M][K] (a_mn 0) or [K][M] (1), f16 B stored [nb][K] (b_mn 0) or
  * [K][nb] (1).  kind 0: C [M][nb] fp32 += result; kind 1: C [nb][M] fp32 += result transposed;
