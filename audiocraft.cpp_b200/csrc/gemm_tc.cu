@@ -716,8 +716,10 @@ struct PairWork {
 };
 
 // stream-K partial of one epilogue warp: 32 rows x 128 columns, fp32, TMEM-fragment order
-constexpr int SK_WARP_FLOATS = 32 * 128;
-constexpr int SK_CTA_BYTES = EPI_WARPS2 * SK_WARP_FLOATS * 4;  // 128 KB: 4 stages of the 256-wide ring
+// A stream-K partial is one CTA's 128 x 256 fp32 accumulator (128 KB: 4 stages of the 256-wide
+// ring), stored epilogue-warp-major: each warp's 32 rows x its columns, chunk by chunk.
+constexpr int SK_CTA_FLOATS = 128 * 256;
+constexpr int SK_CTA_BYTES = SK_CTA_FLOATS * 4;
 
 template <int BN2, bool B_MN, bool SK, bool Q8>
 __global__ void __launch_bounds__(Tc2Cfg<BN2, Q8>::THREADS, 1)
@@ -726,6 +728,7 @@ __global__ void __launch_bounds__(Tc2Cfg<BN2, Q8>::THREADS, 1)
     constexpr int BH2 = Cfg::BH;
     constexpr int S = Cfg::STAGES;
     constexpr int R = Cfg::RSLOTS;
+    static_assert(!SK || S * Cfg::STAGE >= SK_CTA_BYTES, "a stream-K partial must fit in the operand ring");
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023) & ~1023u;
@@ -872,12 +875,12 @@ __global__ void __launch_bounds__(Tc2Cfg<BN2, Q8>::THREADS, 1)
             // stages of the ring as the mainloop releases them.
             if (BN2 == 256) {
                 int* flag = p.sk_flag + (pair + 1) * 2 + (int)rank;
-                if (flag_wait(flag, EPI_WARPS2, p.err, 18)) {
+                if (flag_wait(flag, Cfg::EW, p.err, 18)) {
                     *flag = 0;  // consumed; the next launch starts from zero
                     asm volatile("fence.proxy.async.global;" ::: "memory");
                     mbar_expect_tx(part_bar, SK_CTA_BYTES);
                     const unsigned char* src = reinterpret_cast<const unsigned char*>(
-                        p.sk_part + ((size_t)(pair + 1) * 2 + rank) * (EPI_WARPS2 * SK_WARP_FLOATS));
+                        p.sk_part + ((size_t)(pair + 1) * 2 + rank) * SK_CTA_FLOATS);
                     for (int j = 0; j < SK_CTA_BYTES / Cfg::STAGE; ++j) {
                         if (!mbar_wait(empty_bar(s), ph ^ 1, p.err, 11)) break;
                         bulk_load(base + s * Cfg::STAGE, src + (size_t)j * Cfg::STAGE, Cfg::STAGE, part_bar);
@@ -940,50 +943,57 @@ __global__ void __launch_bounds__(Tc2Cfg<BN2, Q8>::THREADS, 1)
         // arrival in the leader, a 16-byte DSMEM copy with complete_tx from the peer (an
         // asynchronous signal: the converters go on while it travels).  The producer keeps the
         // raw ring filled ahead of them.
-        constexpr int CT = (Cfg::CW ? Cfg::CW : 1) * 32;  // converter threads (the non-Q8 kernel has none)
+        // Two groups of converter warps take alternate k-blocks, so one group's shared-memory
+        // latency, fence and barrier overlap the other's conversion.
+        constexpr int CT = (Cfg::CW ? Cfg::CW : 2) * 32;  // converter threads (the non-Q8 kernel has none)
+        constexpr int GT = CT / 2;                          // threads per group
         const int ct = threadIdx.x - (2 + Cfg::EW) * 32;
+        const int grp = ct / GT, gct = ct % GT;
         const uint32_t leader_full0 = map_rank(full_bar(0), 0);
         const uint32_t sig_local = bars + SIG_OFF, sig_leader = map_rank(bars + SIG_OFF, 0);
-        int s = 0, r = 0;
+        int s = 0, r = 0, seq = 0;
         uint32_t ph = 0, rph = 0;  // operand-ring parity, raw-ring parity
         PairWork w(SK ? 1 : 0, nk, ntiles, pair, npairs);
         int tile, kb0, kb1, role;
         bool ok = true;
         while (ok && w.next(tile, kb0, kb1, role)) {
-            for (int kb = kb0; kb < kb1; ++kb) {
+            for (int kb = kb0; kb < kb1; ++kb, ++seq) {
                 const bool conv = (p.q8mask >> (kb >= nk1 ? 1 : 0)) & 1;
-                bool got = mbar_wait(empty_bar(s), ph ^ 1, p.err, 22);
-                if (conv && got) {
-                    got = mbar_wait(raw_bar(r), rph, p.err, 21);
-                    if (got) {
-                        convert_q8_stage<BH2, B_MN, CT>(smem, raw_off + r * Cfg::RAW,
-                                                                  s * Cfg::STAGE + Cfg::A_BYTES, ct);
-                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                if ((seq & 1) == grp) {
+                    bool got = mbar_wait(empty_bar(s), ph ^ 1, p.err, 22);
+                    if (conv && got) {
+                        got = mbar_wait(raw_bar(r), rph, p.err, 21);
+                        if (got) {
+                            convert_q8_stage<BH2, B_MN, GT>(smem, raw_off + r * Cfg::RAW,
+                                                            s * Cfg::STAGE + Cfg::A_BYTES, gct);
+                            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        }
                     }
-                }
-                // all converter threads agree (and have written the tile) before the signal; on a
-                // failed wait they leave together (the MMA then gives up on its own bounded wait)
-                uint32_t all;
-                asm volatile(
-                    "{\n\t.reg .pred p, q;\n\t"
-                    "setp.ne.u32 p, %1, 0;\n\t"
-                    "bar.red.and.pred q, 1, %2, p;\n\t"
-                    "selp.u32 %0, 1, 0, q;\n\t}"
-                    : "=r"(all)
-                    : "r"(got ? 1u : 0u), "n"(CT)
-                    : "memory");
-                if (!all) {
-                    ok = false;
-                    break;
-                }
-                if (ct == 0) {
-                    if (rank == 0) {
-                        mbar_arrive(full_bar(s));
-                    } else {
-                        asm volatile(
-                            "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], 16, [%2];"
-                            ::"r"(sig_leader), "r"(sig_local), "r"(leader_full0 + 8 * s)
-                            : "memory");
+                    // the group's threads agree (and have written the tile) before the signal; on
+                    // a failed wait they leave together (the MMA then gives up on its own bounded
+                    // wait, and the other group on its own)
+                    uint32_t all;
+                    asm volatile(
+                        "{\n\t.reg .pred p, q;\n\t"
+                        "setp.ne.u32 p, %1, 0;\n\t"
+                        "bar.red.and.pred q, %2, %3, p;\n\t"
+                        "selp.u32 %0, 1, 0, q;\n\t}"
+                        : "=r"(all)
+                        : "r"(got ? 1u : 0u), "r"(1 + grp), "n"(GT)
+                        : "memory");
+                    if (!all) {
+                        ok = false;
+                        break;
+                    }
+                    if (gct == 0) {
+                        if (rank == 0) {
+                            mbar_arrive(full_bar(s));
+                        } else {
+                            asm volatile(
+                                "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], 16, [%2];"
+                                ::"r"(sig_leader), "r"(sig_local), "r"(leader_full0 + 8 * s)
+                                : "memory");
+                        }
                     }
                 }
                 if (conv && ++r == R) { r = 0; rph ^= 1; }
@@ -994,6 +1004,7 @@ __global__ void __launch_bounds__(Tc2Cfg<BN2, Q8>::THREADS, 1)
         // ------------------------------------------------------------ epilogue (both CTAs)
         // TMEM lanes 32*quad .. 32*quad+31, columns coff .. coff + WCOLS - 1 of the tile
         constexpr int WCOLS = BN2 / (Cfg::EW / 4);  // columns per epilogue warp
+        constexpr int WARP_FLOATS = 32 * WCOLS;     // its share of a stream-K partial
         const int ew = warp - 2, quad = warp & 3, coff = (ew >> 2) * WCOLS;
         EpiTiles tiles;
         tiles.o = smem + S * Cfg::STAGE + ew * EPI_OUT_BYTES;
@@ -1040,8 +1051,8 @@ __global__ void __launch_bounds__(Tc2Cfg<BN2, Q8>::THREADS, 1)
             const uint32_t trow = tmem_base + ((uint32_t)(quad * 32) << 16) + a * BN2 + coff;
             if (SK && role == SK_PART_OUT) {
                 // tail of a split tile: raw fp32 accumulators to slot `pair`, then count this warp in
-                float4* dst = reinterpret_cast<float4*>(
-                    p.sk_part + (((size_t)pair * 2 + rank) * EPI_WARPS2 + ew) * SK_WARP_FLOATS);
+                float4* dst = reinterpret_cast<float4*>(p.sk_part + ((size_t)pair * 2 + rank) * SK_CTA_FLOATS +
+                                                        (size_t)ew * WARP_FLOATS);
                 for (int c = 0; c < WCOLS / 32; ++c) {
                     uint32_t r[32];
                     tmem_ld32(trow + c * 32, r);
@@ -1059,8 +1070,9 @@ __global__ void __launch_bounds__(Tc2Cfg<BN2, Q8>::THREADS, 1)
                 if (SK && role == SK_PART_IN && BN2 == 256) {
                     // head of a split tile: the producer streams the tail's partial into the ring
                     mbar_wait(part_bar, 0, p.err, 20);
-                    part = reinterpret_cast<const float4*>(smem + ((units + (ew >> 1)) % S) * Cfg::STAGE +
-                                                           (ew & 1) * (SK_WARP_FLOATS * 4));
+                    const int at = ew * WARP_FLOATS * 4;  // this warp's bytes in the streamed partial
+                    part = reinterpret_cast<const float4*>(smem + ((units + at / Cfg::STAGE) % S) * Cfg::STAGE +
+                                                           at % Cfg::STAGE);
                 }
                 int m_base, rows, n0, nm, nr, nn;
                 tile_rows(tile, m_base, rows, n0);
@@ -1264,9 +1276,8 @@ void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
     p.out_h = (a.mode == EPI_STORE_F32 || a.mode == EPI_ACCUM_F32 || a.mode == EPI_RESID_F32) ? a.out_h : nullptr;
     p.sk_part = a.sk_part; p.sk_flag = a.sk_flag;
     p.q8mask = (a.B1q ? 1 : 0) | (a.K2 > 0 && a.B2q ? 2 : 0);
-    // no stream-K with Q8_0 weights: its partial-tile layout assumes 8 epilogue warps
     auto whole = gemm_tc2_kernel<BN2, B_MN, false, Q8>;
-    auto split = gemm_tc2_kernel<BN2, B_MN, BN2 == 256 && !Q8, Q8>;
+    auto split = gemm_tc2_kernel<BN2, B_MN, BN2 == 256, Q8>;
     static DeviceOnce once;
     once([&] {
         for (auto k : {whole, split}) {
@@ -1277,7 +1288,7 @@ void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
     const int num_sms = current_sm_count();
     const int tiles = ((a.M + 2 * BM - 1) / (2 * BM)) * (a.N / BN2);
     const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
-    const auto kern = !Q8 && sk_pays(BN2, tiles, pairs, a) ? split : whole;
+    const auto kern = sk_pays(BN2, tiles, pairs, a) ? split : whole;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
     cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
@@ -1337,7 +1348,7 @@ void gemm_tc2_width(const GemmArgs& a, int* err, cudaStream_t s, int width) {
     }
 }
 
-long gemm_sk_part_floats(int num_sms) { return (long)(num_sms / 2) * 2 * EPI_WARPS2 * SK_WARP_FLOATS; }
+long gemm_sk_part_floats(int num_sms) { return (long)(num_sms / 2) * 2 * SK_CTA_FLOATS; }
 int gemm_sk_flag_count(int num_sms) { return (num_sms / 2) * 2; }
 
 void gemm_tc2(const GemmArgs& a, int* err, cudaStream_t s) { gemm_tc2_width(a, err, s, a.N % 256 == 0 ? 256 : 128); }
@@ -1359,7 +1370,7 @@ void gemm_tc_auto(const GemmArgs& a, int* err, cudaStream_t s) {
             const long t2 = m2 * (a.N / 256);
             // stream-K spreads the k-blocks evenly: cost by the mean share plus its fix-up
             const long nk = (a.K1 + BKE - 1) / BKE + (a.K2 + BKE - 1) / BKE;
-            const double c = !q8_args(a) && sk_pays(256, (int)t2, (int)std::min(t2, pairs), a)
+            const double c = sk_pays(256, (int)t2, (int)std::min(t2, pairs), a)
                                  ? ((double)t2 * nk / pairs + 12.0) / nk * 256.0 * eff[1]
                                  : rounds(t2, pairs) * 256.0 * eff[1];
             if (c < best) { best = c; choice = 1; }

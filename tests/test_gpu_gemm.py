@@ -33,12 +33,14 @@ def test_gemm_matches_numpy(path, b_mn, M, N, K):
 @pytest.mark.parametrize("path", [0, 3, 4, 5], ids=["auto", "pair", "pair128", "pair_whole"])
 @pytest.mark.parametrize("b_mn", [False, True], ids=["NT", "NN"])
 @pytest.mark.parametrize("M,N,K", [(300, 256, 128), (6000, 1024, 1024), (1000, 4096, 256), (4864, 1024, 2048),
-                                   (1000, 384, 256)])
+                                   (5000, 1024, 2112), (6000, 1024, 4096), (1000, 384, 256)])
 def test_q8_0_gemm_equals_f16_gemm_on_the_dequantised_weight(path, b_mn, M, N, K):
     """Q8_0 weights stay quantised on the device; the converter warps' f16 operand is exactly the
     bind-time dequantisation (tools/ac-quantize.cpp:161 blocks, fp32 d * q rounded to f16), so the
-    product is bit-identical to the f16 GEMM on that dequantised weight with the same tile schedule,
-    and matches the fp64 product of the dequantised operands on every 2-CTA path."""
+    product is bit-identical to the f16 GEMM on that dequantised weight with the same tile schedule
+    (stream-K splits included: 4864 x 1024 x 2048, 5000 x 1024 x 2112 and 6000 x 1024 x 4096 split
+    tiles on the 256-wide pair path), and matches the fp64 product of the dequantised operands on
+    every 2-CTA path."""
     from cases import q8_0_bytes
     if path == 3 and N % 256:
         pytest.skip("256-wide pair tiles need N % 256 == 0")
@@ -49,7 +51,7 @@ def test_q8_0_gemm_equals_f16_gemm_on_the_dequantised_weight(path, b_mn, M, N, K
     blocks = q8_0_bytes(w)
     _, wh = A.q8_0_dequant(blocks)
     c8 = A.gemm_q8_0(a, blocks, M, N, K, b_mn, path)
-    if path in (4, 5):  # the same tile schedule on f16 weights (paths 0 / 3 may split f16 tiles stream-K)
+    if path in (3, 4, 5):  # the same tile schedule on f16 weights (auto may pick the 1-CTA kernel for f16)
         c16 = A.gemm_f16(a, wh.reshape(wshape), M, N, K, b_mn, path)
         np.testing.assert_array_equal(c8, c16)
     wf = bits_to_f32(wh).reshape(wshape).astype(np.float64)
