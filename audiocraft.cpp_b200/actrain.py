@@ -44,7 +44,7 @@ class AdapterDesc(C.Structure):
 class MfBatch(C.Structure):
     _fields_ = [("n", C.c_int), ("clean", C.c_void_p), ("noise", C.c_void_p),
                 ("hidden", C.c_void_p), ("t", C.c_void_p), ("unconditional", C.c_void_p),
-                ("valid_tokens", C.c_void_p)]
+                ("valid_tokens", C.c_void_p), ("pivot", C.c_void_p), ("edit_start", C.c_void_p)]
 
 
 class MgBatch(C.Structure):
@@ -206,16 +206,20 @@ class Context:
         self._check(self._L.act_zero_grads(self.h))
 
     # ----------------------------------------------------------------- steps
-    def _mf_batch(self, clean, noise, hidden, t, unconditional=None, valid_tokens=None):
-        arrs = [np.ascontiguousarray(clean, np.float32), np.ascontiguousarray(noise, np.float32),
-                np.ascontiguousarray(hidden, np.float32), np.ascontiguousarray(t, np.float32),
+    def _mf_batch(self, clean, noise, hidden, t, unconditional=None, valid_tokens=None, pivot=None,
+                  edit_start=None):
+        f32 = lambda a: None if a is None else np.ascontiguousarray(a, np.float32)
+        arrs = [f32(clean), f32(noise), f32(hidden), f32(t),
                 None if unconditional is None else np.ascontiguousarray(unconditional, np.int32),
-                None if valid_tokens is None else np.ascontiguousarray(valid_tokens, np.int32)]
+                None if valid_tokens is None else np.ascontiguousarray(valid_tokens, np.int32),
+                f32(pivot), f32(edit_start)]
         self._keep = arrs
         return MfBatch(arrs[0].shape[0], *[_ptr(a) for a in arrs])
 
-    def mf_step(self, clean, noise, hidden, t, unconditional=None, valid_tokens=None):
-        b = self._mf_batch(clean, noise, hidden, t, unconditional, valid_tokens)
+    def mf_step(self, clean, noise, hidden, t, unconditional=None, valid_tokens=None, pivot=None,
+                edit_start=None):
+        """One microbatch; with pivot/edit_start the edit-bridge objective (noise unused)."""
+        b = self._mf_batch(clean, noise, hidden, t, unconditional, valid_tokens, pivot, edit_start)
         loss = np.zeros(b.n, np.float32)
         self._check(self._L.act_mf_step(self.h, C.byref(b), loss.ctypes.data))
         return loss

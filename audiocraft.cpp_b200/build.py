@@ -69,7 +69,36 @@ def build(jobs: int = 8, verbose: bool = False) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n" + r.stderr + r.stdout)
+    build_trainers()
     return LIB
+
+
+TRAINER = os.path.join(HERE, "trainer")
+BIN = os.path.join(HERE, "bin")
+CXX = os.environ.get("CXX", "g++")
+
+
+def build_trainers() -> list:
+    """The mf-train / mg-train front ends: host C++ over libactrain.so (found next to bin/)."""
+    os.makedirs(BIN, exist_ok=True)
+    common = [os.path.join(TRAINER, f) for f in ("gguf_file.cpp", "train_host.cpp")]
+    headers = [os.path.join(TRAINER, f) for f in os.listdir(TRAINER) if f.endswith(".h")]
+    headers.append(os.path.join(ROOT, "include", "actrain.h"))
+    out = []
+    for main, exe in (("mf_train.cpp", "mf-train"), ("mg_train.cpp", "mg-train")):
+        src = os.path.join(TRAINER, main)
+        if not os.path.exists(src):
+            continue
+        dst = os.path.join(BIN, exe)
+        inputs = [src, LIB] + common + headers
+        if not os.path.exists(dst) or os.path.getmtime(dst) < max(os.path.getmtime(f) for f in inputs):
+            cmd = [CXX, "-std=c++17", "-O2", "-Wall", "-I" + TRAINER, "-I" + os.path.join(ROOT, "include"), src] + \
+                  common + ["-o", dst, "-L" + HERE, "-lactrain", "-Wl,-rpath,$ORIGIN/.."]
+            r = subprocess.run(cmd, capture_output=True, text=True)
+            if r.returncode != 0:
+                raise RuntimeError(exe + " build failed:\n" + r.stderr + r.stdout)
+        out.append(dst)
+    return out
 
 
 if __name__ == "__main__":

@@ -147,9 +147,12 @@ __global__ void f32_f16_kernel(const float* __restrict__ x, f16* __restrict__ y,
 
 // ---------------------------------------------------------------------------------------
 // MelodyFlow inputs and loss, src/mf/train.h:154-159 and :107-108, src/mf/dit.h:172-173,208-216.
+// An edit-bridge sample (start >= 0) replaces its noise with the t = 0 endpoint of the straight
+// pivot -> clean bridge, (pivot - start*clean) / (1 - start) (src/mf/train.h:196-203), in the
+// reference's float operations, each rounded once (no contraction into an FMA).
 __global__ void mf_inputs_kernel(const float* __restrict__ clean, const float* __restrict__ noise,
-                                 const float* __restrict__ tv, int clips, int T, int lat,
-                                 f16* __restrict__ x0, float* __restrict__ vstar) {
+                                 const float* __restrict__ tv, const float* __restrict__ start, int clips,
+                                 int T, int lat, f16* __restrict__ x0, float* __restrict__ vstar) {
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     const long n = (long)clips * lat * T;
     if (i >= n) return;
@@ -157,7 +160,9 @@ __global__ void mf_inputs_kernel(const float* __restrict__ clean, const float* _
     const int c = (int)((i / T) % lat), p = (int)(i % T);
     const float t = tv[b];
     const float rescale = 1.0f / sqrtf(t * t + (1.0f - t) * (1.0f - t));
-    const float cl = clean[i], nz = noise[i];
+    const float cl = clean[i], st = start[b];
+    float nz = noise[i];
+    if (st >= 0.0f) nz = __fdiv_rn(__fsub_rn(nz, __fmul_rn(st, cl)), __fsub_rn(1.0f, st));
     x0[((long)b * T + p) * lat + c] = __float2half_rn(((1 - t) * nz + t * cl) * rescale);
     vstar[i] = cl - nz;
 }
@@ -574,10 +579,10 @@ void f32_to_f16(const float* x, f16* y, long n, cudaStream_t s) {
     f32_f16_kernel<<<blocks_for(n, 256), 256, 0, s>>>(x, y, n);
 }
 
-void mf_inputs(const float* clean, const float* noise, const float* t, int clips, int T, int lat, f16* x0,
-               float* vstar, cudaStream_t s) {
+void mf_inputs(const float* clean, const float* noise, const float* t, const float* start, int clips, int T,
+               int lat, f16* x0, float* vstar, cudaStream_t s) {
     const long n = (long)clips * lat * T;
-    mf_inputs_kernel<<<blocks_for(n, 256), 256, 0, s>>>(clean, noise, t, clips, T, lat, x0, vstar);
+    mf_inputs_kernel<<<blocks_for(n, 256), 256, 0, s>>>(clean, noise, t, start, clips, T, lat, x0, vstar);
 }
 
 void mf_loss(const float* out, const float* vstar, int clips, int T, int lat, float* loss, f16* dout,

@@ -250,10 +250,10 @@ struct act_ctx {
 
     // staging (host pinned + device)
     float *h_clean = nullptr, *h_noise = nullptr, *h_hidden = nullptr, *h_t = nullptr, *h_tfeat = nullptr,
-          *h_loss = nullptr, *h_ctx = nullptr;
+          *h_loss = nullptr, *h_ctx = nullptr, *h_start = nullptr;
     int32_t *h_nvalid = nullptr, *h_ids = nullptr, *h_tgt = nullptr;
     float *d_clean = nullptr, *d_noise = nullptr, *d_hidden = nullptr, *d_t = nullptr, *d_tfeat = nullptr,
-          *d_loss = nullptr, *d_ctx = nullptr;
+          *d_loss = nullptr, *d_ctx = nullptr, *d_start = nullptr;  // d_start: edit-bridge start, -1 = none
     float* loss_part = nullptr;  // per-clip partial sums of the MSE ([max_batch][32])
     int32_t *d_nvalid = nullptr, *d_ids = nullptr, *d_tgt = nullptr;
 
@@ -897,7 +897,7 @@ struct act_ctx {
         const long rows = (long)n * T, crows = (long)n * C;
         prepare_adapters();
         timed(2, 0, 0, [&] {
-            mf_inputs(d_clean, d_noise, d_t, n, T, md.latent_dim, x0, vstar, stream);
+            mf_inputs(d_clean, d_noise, d_t, d_start, n, T, md.latent_dim, x0, vstar, stream);
             linear_f32(d_tfeat, te0, te1, n, D, md.time_dim, 1, stream);
             linear_f32(te1, te2, te, n, D, D, 0, stream);
             f32_to_f16(d_hidden, hidden_h, crows * md.cond_dim, stream);
@@ -1104,13 +1104,19 @@ struct act_ctx {
 
     void stage_mf(const act_mf_batch* b) {
         if (!mf) throw Error(ACT_ERR_INVALID, "not a MelodyFlow context");
-        if (!b || b->n <= 0 || b->n > B || !b->clean || !b->noise || !b->hidden || !b->t)
+        const bool bridge = b && b->pivot;
+        if (!b || b->n <= 0 || b->n > B || !b->clean || !(bridge ? b->edit_start : b->noise) || !b->hidden || !b->t)
             throw Error(ACT_ERR_INVALID, "invalid training sample");
         const int n = b->n, lat = md.latent_dim;
         const size_t nx = (size_t)n * lat * T, nh = (size_t)n * C * md.cond_dim;
         for (int i = 0; i < n; ++i) {
             const float t = b->t[i];
             if (!std::isfinite(t) || t < 0 || t > 1) throw Error(ACT_ERR_INVALID, "invalid training sample");
+            // src/mf/train.h:193-195
+            const float start = bridge ? b->edit_start[i] : -1.0f;
+            if (bridge && (!std::isfinite(start) || start < 0 || start >= 1 || t < start))
+                throw Error(ACT_ERR_INVALID, "invalid edit bridge");
+            h_start[i] = start;
             const int v = b->valid_tokens ? b->valid_tokens[i] : -1;
             if (v > C) throw Error(ACT_ERR_INVALID, "invalid valid token count");
             const bool uncond = b->unconditional && b->unconditional[i];
@@ -1127,9 +1133,11 @@ struct act_ctx {
                 tf[half + k] = std::sin(arg);
             }
         }
-        upload({{d_clean, h_clean, b->clean, nx * 4}, {d_noise, h_noise, b->noise, nx * 4},
+        // the bridge's pivot takes the noise buffer: the input kernel turns it into the endpoint
+        upload({{d_clean, h_clean, b->clean, nx * 4}, {d_noise, h_noise, bridge ? b->pivot : b->noise, nx * 4},
                 {d_hidden, h_hidden, b->hidden, nh * 4}});
         CK(cudaMemcpyAsync(d_t, h_t, n * 4, cudaMemcpyHostToDevice, stream));
+        CK(cudaMemcpyAsync(d_start, h_start, n * 4, cudaMemcpyHostToDevice, stream));
         CK(cudaMemcpyAsync(d_tfeat, h_tfeat, (size_t)n * md.time_dim * 4, cudaMemcpyHostToDevice, stream));
         CK(cudaMemcpyAsync(d_nvalid, h_nvalid, n * 4, cudaMemcpyHostToDevice, stream));
         staged_n = n;
@@ -1665,9 +1673,11 @@ struct act_ctx {
             h_clean = halloc<float>(nx); h_noise = halloc<float>(nx);
             h_hidden = halloc<float>((size_t)Cr * md.cond_dim);
             h_t = halloc<float>(B); h_tfeat = halloc<float>((size_t)B * md.time_dim); h_nvalid = halloc<int32_t>(B);
+            h_start = halloc<float>(B);
             d_clean = dalloc<float>(nx); d_noise = dalloc<float>(nx);
             d_hidden = dalloc<float>((size_t)Cr * md.cond_dim);
             d_t = dalloc<float>(B); d_tfeat = dalloc<float>((size_t)B * md.time_dim); d_nvalid = dalloc<int32_t>(B);
+            d_start = dalloc<float>(B);
         } else {
             const int sel = ad.frames - ad.prefix_frames;
             h_ids = halloc<int32_t>((size_t)B * md.n_q * T);

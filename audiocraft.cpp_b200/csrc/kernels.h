@@ -208,8 +208,9 @@ void gelu_check(const uint16_t* z, uint16_t* g, uint16_t* dg, long n, cudaStream
 // fp32 adapter gradient multiplies by 1 / gscale, which is exact.
 
 // MelodyFlow inputs: x0[m][c] = ((1-t)noise + t clean) * rescale(t), vstar = clean - noise.
-void mf_inputs(const float* clean, const float* noise, const float* t, int clips, int T, int lat,
-               f16* x0, float* vstar, cudaStream_t s);
+// start[b] >= 0: noise holds the edit-bridge pivot and becomes (pivot - start*clean) / (1 - start)
+void mf_inputs(const float* clean, const float* noise, const float* t, const float* start, int clips, int T,
+               int lat, f16* x0, float* vstar, cudaStream_t s);
 // loss[b] = mean((sqrt2*out - vstar)^2) ; dout = gscale * d loss / d out (f16, token-major)
 // part: clips * 32 floats of scratch (partial sums)
 void mf_loss(const float* out, const float* vstar, int clips, int T, int lat, float* loss, f16* dout,

@@ -95,6 +95,13 @@ typedef struct {
     const float* t;            /* [n] flow time in [0, 1] */
     const int32_t* unconditional; /* [n] or NULL: 1 masks every text token */
     const int32_t* valid_tokens;  /* [n] or NULL: tokens >= valid are masked; -1 = all */
+    /* Edit-bridge objective (MfTrainGraph::compute_bridge, src/mf/train.h:190-204), or NULL for
+     * flow matching.  The straight bridge x_t = (1-u) pivot + u clean, u = (t-start)/(1-start),
+     * is trained through its equivalent t = 0 endpoint (pivot - start*clean) / (1 - start), which
+     * the device forms in place of noise (noise may then be NULL).  Needs 0 <= start < 1 and
+     * start <= t <= 1 for every sample. */
+    const float* pivot;           /* [n][latent_dim][frames] */
+    const float* edit_start;      /* [n] */
 } act_mf_batch;
 
 /* One MusicGen microbatch (MgTrainGraph::compute, src/mg/train.h:178-227). */
