@@ -504,12 +504,10 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
                 v0 *= a.vscale[h * HD + c];
                 v1 *= a.vscale[h * HD + c + 1];
             }
-            if (a.dk_acc) {  // partial over this CTA's query blocks
-                if (qb_first < qb_end) {
-                    const long r = ((long)b * a.Tk + j) * a.H * HD + h * HD + c;
-                    atomicAdd(reinterpret_cast<float2*>(a.dk_acc + r), make_float2(x0, x1));
-                    atomicAdd(reinterpret_cast<float2*>(a.dv_acc + r), make_float2(v0, v1));
-                }
+            if (a.dk_acc) {  // partial over this CTA's query blocks, in its own slice (zero if it had none)
+                const long r = ((long)part * a.clips * a.Tk + (long)b * a.Tk + j) * a.H * HD + h * HD + c;
+                *reinterpret_cast<float2*>(a.dk_acc + r) = make_float2(x0, x1);
+                *reinterpret_cast<float2*>(a.dv_acc + r) = make_float2(v0, v1);
             } else {
                 *reinterpret_cast<uint32_t*>(dkr + c) = pack_f16(x0, x1);
                 *reinterpret_cast<uint32_t*>(dvr + c) = pack_f16(v0, v1);
@@ -518,17 +516,25 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnArgs a) {
     }
 }
 
-// dk / dv (f16) from the fp32 accumulators of a query-split backward: 4 floats per thread
+// dk / dv (f16) from the fp32 partials of a query-split backward, added in split order (the
+// same sum whichever CTA finished first): 4 floats per thread
 __global__ void attn_dkv_finish_kernel(const AttnArgs a) {
     pdl_wait();
     pdl_trigger();
     const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
     const int quads = a.H * HD / 4;
-    if (idx >= (long)a.clips * a.Tk * quads) return;
+    const long rows = (long)a.clips * a.Tk;
+    if (idx >= rows * quads) return;
     const long row = idx / quads;
     const int c = (int)(idx % quads) * 4;
-    const float4 k = *reinterpret_cast<const float4*>(a.dk_acc + row * a.H * HD + c);
-    const float4 v = *reinterpret_cast<const float4*>(a.dv_acc + row * a.H * HD + c);
+    float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
+    for (int q = 0; q < a.qsplit; ++q) {
+        const long at = ((long)q * rows + row) * a.H * HD + c;
+        const float4 kq = *reinterpret_cast<const float4*>(a.dk_acc + at);
+        const float4 vq = *reinterpret_cast<const float4*>(a.dv_acc + at);
+        k.x += kq.x; k.y += kq.y; k.z += kq.z; k.w += kq.w;
+        v.x += vq.x; v.y += vq.y; v.z += vq.z; v.w += vq.w;
+    }
     *reinterpret_cast<uint2*>(a.dk + row * a.lddk + c) = make_uint2(pack_f16(k.x, k.y), pack_f16(k.z, k.w));
     *reinterpret_cast<uint2*>(a.dv + row * a.lddv + c) = make_uint2(pack_f16(v.x, v.y), pack_f16(v.z, v.w));
 }

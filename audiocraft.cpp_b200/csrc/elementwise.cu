@@ -220,17 +220,28 @@ __global__ void linear_f32_kernel(const float* __restrict__ x, const float* __re
 
 // ---------------------------------------------------------------------------------------
 // DoRA-rows, src/ac/lora.h:62-79 (and the hand-derived backward of that factorisation).
+// Column sums of a * b over the rows in DORA_COLSUM_PARTS row blocks: each block leaves its partial
+// in part[block][n]; the second kernel adds them in block order (no atomics, so the sum does not
+// depend on the order in which blocks finish).
 __global__ void dora_colsum_kernel(const f16* __restrict__ a, long lda, const f16* __restrict__ b,
-                                   long ldb, int rows, int N, const float* __restrict__ g,
-                                   float* __restrict__ dg, int rows_per_block, float inv_gscale) {
+                                   long ldb, int rows, int N, float* __restrict__ part, int rows_per_block) {
     const int n = blockIdx.x * blockDim.x + threadIdx.x;
     if (n >= N) return;
     const int r0 = blockIdx.y * rows_per_block, r1 = min(rows, r0 + rows_per_block);
     float acc = 0.f;
     for (int r = r0; r < r1; ++r)
         acc += __half2float(a[(long)r * lda + n]) * __half2float(b[(long)r * ldb + n]);
+    part[(long)blockIdx.y * N + n] = acc;
+}
+
+__global__ void dora_colsum_add_kernel(const float* __restrict__ part, int parts, int N,
+                                       const float* __restrict__ g, float* __restrict__ dg, float inv_gscale) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    float acc = 0.f;
+    for (int j = 0; j < parts; ++j) acc += part[(long)j * N + n];
     const float gg = g[n];
-    atomicAdd(dg + n, acc * inv_gscale / (gg * gg));
+    dg[n] += acc * inv_gscale / (gg * gg);
 }
 
 __global__ void gram_kernel(const float* __restrict__ A, int r, int in, const float* __restrict__ wt,
@@ -443,9 +454,9 @@ __global__ void mg_embed_kernel(const int32_t* __restrict__ ids, int steps, int 
 }
 
 // ggml_cross_entropy_loss over the selected rows, src/mg/train.h:131.
+// Each row leaves its loss term in rowloss[row]; mg_loss_add_kernel sums them in row order.
 __global__ void mg_ce_kernel(const float* __restrict__ logits, int card, const int32_t* __restrict__ targets,
-                             int rows_per_seq, float inv_nsel, float* __restrict__ loss_acc,
-                             f16* __restrict__ dlogits, float gscale) {
+                             float inv_nsel, float* __restrict__ rowloss, f16* __restrict__ dlogits, float gscale) {
     const int row = blockIdx.x;
     const int tgt = targets[row];
     const float* lg = logits + (long)row * card;
@@ -481,12 +492,32 @@ __global__ void mg_ce_kernel(const float* __restrict__ logits, int card, const i
     sm = sh_sum;
     if (tgt < 0) {
         for (int j = threadIdx.x; j < card; j += blockDim.x) dl[j] = __float2half_rn(0.f);
+        if (threadIdx.x == 0) rowloss[row] = 0.f;
         return;
     }
     const float inv = 1.0f / sm, seed = inv_nsel * gscale;
     for (int j = threadIdx.x; j < card; j += blockDim.x)
         dl[j] = __float2half_rn((expf(lg[j] - mx) * inv - (j == tgt ? 1.0f : 0.0f)) * seed);
-    if (threadIdx.x == 0) atomicAdd(loss_acc + row / rows_per_seq, (mx + logf(sm) - lg[tgt]) * inv_nsel);
+    if (threadIdx.x == 0) rowloss[row] = (mx + logf(sm) - lg[tgt]) * inv_nsel;
+}
+
+// loss_acc[seq] += the row terms of seq in a fixed order (one block per sequence): the printed
+// loss does not depend on the order in which rows finished
+__global__ void mg_loss_add_kernel(const float* __restrict__ rowloss, int rows, int rows_per_seq,
+                                   float* __restrict__ loss_acc) {
+    const int seq = blockIdx.x;
+    const int r0 = seq * rows_per_seq, r1 = min(rows, r0 + rows_per_seq);
+    float v = 0.f;
+    for (int r = r0 + (int)threadIdx.x; r < r1; r += blockDim.x) v += rowloss[r];
+    __shared__ float red[32];
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float w = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+        w = warp_sum(w);
+        if (threadIdx.x == 0) loss_acc[seq] += w;
+    }
 }
 
 // gact = gelu(z); with store_grad, z is overwritten by gelu'(z).  8 f16 per thread and step;
@@ -596,10 +627,12 @@ void linear_f32(const float* x, const float* W, float* y, int rows, int N, int K
 }
 
 void dora_colsum(const f16* a, long lda, const f16* b, long ldb, int rows, int N, const float* colscale,
-                 float* dg, float inv_gscale, cudaStream_t s) {
-    const int rpb = 256;
-    dim3 grid(blocks_for(N, 256), blocks_for(rows, rpb));
-    dora_colsum_kernel<<<grid, 256, 0, s>>>(a, lda, b, ldb, rows, N, colscale, dg, rpb, inv_gscale);
+                 float* dg, float* part, float inv_gscale, cudaStream_t s) {
+    const int rpb = (rows + DORA_COLSUM_PARTS - 1) / DORA_COLSUM_PARTS;
+    const int parts = (rows + rpb - 1) / rpb;
+    dim3 grid(blocks_for(N, 256), parts);
+    dora_colsum_kernel<<<grid, 256, 0, s>>>(a, lda, b, ldb, rows, N, part, rpb);
+    dora_colsum_add_kernel<<<blocks_for(N, 256), 256, 0, s>>>(part, parts, N, colscale, dg, inv_gscale);
 }
 
 void dora_prepare(const float* A, const float* B, const float* m, const float* P, const float* base, int r,
@@ -662,8 +695,9 @@ void mg_embed(const int32_t* ids, int steps, int nq, const float* const* emb_dev
 }
 
 void mg_cross_entropy(const float* logits, int rows, int card, const int32_t* targets, int rows_per_seq,
-                      float inv_nsel, float* loss_acc, f16* dlogits, float gscale, cudaStream_t s) {
-    mg_ce_kernel<<<rows, 256, 0, s>>>(logits, card, targets, rows_per_seq, inv_nsel, loss_acc, dlogits, gscale);
+                      float inv_nsel, float* loss_acc, float* rowloss, f16* dlogits, float gscale, cudaStream_t s) {
+    mg_ce_kernel<<<rows, 256, 0, s>>>(logits, card, targets, inv_nsel, rowloss, dlogits, gscale);
+    mg_loss_add_kernel<<<(rows + rows_per_seq - 1) / rows_per_seq, 256, 0, s>>>(rowloss, rows, rows_per_seq, loss_acc);
 }
 
 }  // namespace act

@@ -164,7 +164,8 @@ struct Proj {
     f16* A_h = nullptr;  // [RP][in], rows >= r zero
     f16* B_h = nullptr;  // [out][RP], cols >= r zero
     float* base = nullptr; // DoRA: frozen ||W_o||^2 + in*1e-12 (double accumulated on the host)
-    float *P = nullptr, *G = nullptr, *Q = nullptr, *nsq = nullptr, *g = nullptr, *dg = nullptr, *scr = nullptr;
+    float *P = nullptr, *G = nullptr, *Q = nullptr, *nsq = nullptr, *g = nullptr, *dg = nullptr, *scr = nullptr,
+          *colpart = nullptr;
     f16* BD = nullptr;
 };
 
@@ -256,13 +257,15 @@ struct act_ctx {
           *d_loss = nullptr, *d_ctx = nullptr, *d_start = nullptr;  // d_start: edit-bridge start, -1 = none
     float* loss_part = nullptr;  // per-clip partial sums of the MSE ([max_batch][32])
     int32_t *d_nvalid = nullptr, *d_ids = nullptr, *d_tgt = nullptr;
+    float* mg_rowloss = nullptr;  // per-row cross-entropy terms of one (sample, codebook)
 
     // global activations / scratch
     f16 *x0 = nullptr, *hidden_h = nullptr, *ctx_h = nullptr, *xo = nullptr, *dout = nullptr, *xprev_h = nullptr;
     float *vstar = nullptr, *te1 = nullptr, *te = nullptr, *x0f = nullptr, *muo = nullptr, *rso = nullptr,
           *outp = nullptr;
     float *dx = nullptr, *dtmp = nullptr, *dq_acc = nullptr, *dvec = nullptr;
-    float* dkv_acc = nullptr;  // cross-attention dK | dV partial sums (fp32, [2][clips * C][D])
+    float* dkv_acc = nullptr;  // cross-attention dK | dV partials (fp32, [2][qsplit][clips * C][D])
+    int cross_qsplit = 1;
     f16 *dxh = nullptr, *dz = nullptr, *dU = nullptr, *dob = nullptr, *dqkv = nullptr, *dcq = nullptr,
          *dckv = nullptr;
     float* logits = nullptr;
@@ -601,7 +604,7 @@ struct act_ctx {
                   bool want_dx, GemmArgs e) {
         if (p.dora)
             timed(2, 0, 4.0 * rows * p.out,
-                  [&] { dora_colsum(dYl, p.out, Y, p.out, (int)rows, p.out, p.g, p.dg, inv_gscale, stream); });
+                  [&] { dora_colsum(dYl, p.out, Y, p.out, (int)rows, p.out, p.g, p.dg, p.colpart, inv_gscale, stream); });
         if (p.adapted) {
             GemmArgs u;
             u.M = (int)rows; u.N = p.RP; u.K1 = p.out;
@@ -818,10 +821,10 @@ struct act_ctx {
         // few keys: split every (head, clip)'s query blocks over CTAs, dK / dV through fp32 partials
         const bool split = C <= 64;
         if (split) {
-            ca.qsplit = ((T + 63) / 64 + 1) / 2;  // two query blocks per CTA
+            ca.qsplit = cross_qsplit;
             if (need_dkv) {
                 ca.dk_acc = dkv_acc;
-                ca.dv_acc = dkv_acc + crows * D;
+                ca.dv_acc = dkv_acc + (long)cross_qsplit * crows * D;
             }
         }
         // a single key block: each query row's dQ is final in one CTA and goes straight to dcq as
@@ -835,7 +838,6 @@ struct act_ctx {
         ++path_count[ACT_PATH_ATTN_BWD_MMA];
         timed(1, 2 * attn_flops(n, C, false), 0, [&] {
             if (!dq_direct) CK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * D, stream));
-            if (split && need_dkv) CK(cudaMemsetAsync(dkv_acc, 0, sizeof(float) * crows * 2 * D, stream));
             attn_bwd(ca, stream);
             if (split && need_dkv) attn_dkv_finish(ca, stream);
             if (!dq_direct) attn_dq_finish(ca, dcq, D, y.p[2].dora ? y.p[2].g : nullptr, stream);
@@ -1002,7 +1004,7 @@ struct act_ctx {
                 run_gemm(hgm, 0);
                 timed(2, 0, 0, [&] {
                     mg_cross_entropy(lg, sel, card, d_tgt + (long)(b * nq + q) * sel, sel * nq, inv_nsel,
-                                     d_loss + b, dl, gscale, stream);
+                                     d_loss + b, mg_rowloss, dl, gscale, stream);
                 });
                 GemmArgs dg;
                 dg.M = sel; dg.N = D; dg.K1 = card; dg.A1 = dl; dg.lda1 = card;
@@ -1561,6 +1563,7 @@ struct act_ctx {
                     p.g = dalloc<float>(p.out);
                     p.dg = dalloc<float>(p.out);
                     p.scr = dalloc<float>((size_t)p.out + p.r * p.r);
+                    p.colpart = dalloc<float>((size_t)DORA_COLSUM_PARTS * p.out);
                     p.BD = dalloc<f16>((size_t)p.out * RP);
                 }
             }
@@ -1664,7 +1667,8 @@ struct act_ctx {
         dqkv = dalloc<f16>(Mr * 3 * D);
         dcq = dalloc<f16>(Mr * D);
         dckv = dalloc<f16>(Cr * 2 * D);
-        dkv_acc = dalloc<float>(Cr * 2 * D);
+        cross_qsplit = ((T + 63) / 64 + 1) / 2;  // two query blocks per CTA
+        dkv_acc = dalloc<float>((size_t)cross_qsplit * Cr * 2 * D);
         d_loss = dalloc<float>(B);
         loss_part = dalloc<float>((long)B * 32);
         h_loss = halloc<float>(B);
@@ -1685,6 +1689,7 @@ struct act_ctx {
             h_ctx = halloc<float>((size_t)Cr * D);
             d_ids = dalloc<int32_t>((size_t)B * md.n_q * T);
             d_tgt = dalloc<int32_t>((size_t)B * md.n_q * sel);
+            mg_rowloss = dalloc<float>((size_t)std::max(sel, 1));
             d_ctx = dalloc<float>((size_t)Cr * D);
             logits = dalloc<float>((size_t)B * md.n_q * sel * md.card);
             dlogits = dalloc<f16>((size_t)B * md.n_q * sel * md.card);
@@ -2374,8 +2379,8 @@ int act_attention(int device, const void* q, const void* k, const void* v, const
                 attn_bwd_tc(a, derr, st);
             } else if (Tk <= 64) {  // few keys: query-split backward, as the training step runs it
                 a.qsplit = (T + 63) / 64;
-                a.dk_acc = static_cast<float*>(up(nullptr, rk * D * 4));
-                a.dv_acc = static_cast<float*>(up(nullptr, rk * D * 4));
+                a.dk_acc = static_cast<float*>(up(nullptr, (size_t)a.qsplit * rk * D * 4));
+                a.dv_acc = static_cast<float*>(up(nullptr, (size_t)a.qsplit * rk * D * 4));
                 attn_bwd(a, st);
                 attn_dkv_finish(a, st);
             } else {

@@ -12,12 +12,15 @@
 // (split-K), so a few hundred CTAs keep enough bytes in flight; TMA stages 128 x 64 and 64 x 64
 // boxes (128-byte swizzle, out-of-range rows and columns read as zero), one thread issues
 // tcgen05.mma 128 x 64 x 16 into TMEM, and four epilogue warps finish the tile:
-//   ACC      fp32 atomics into the gradient (row-major)
-//   ACC_T    fp32 atomics into the gradient, transposed (tile rows are the gradient's columns)
-//   STORE    f16 result.  The split-K CTAs of a tile form one thread-block cluster; each
-//            leaves its fp32 partial tile in its own shared memory and, after a cluster barrier,
-//            reduces its share of the rows over all partials through distributed shared memory
-//            (fixed summation order: deterministic), converts and stores.
+//   ACC      fp32, added into the gradient (row-major)
+//   ACC_T    fp32, added into the gradient, transposed (tile rows are the gradient's columns)
+//   STORE    f16 result.
+// The split-K CTAs of a tile form one thread-block cluster; each leaves its fp32 partial tile in
+// its own shared memory and, after a cluster barrier, reduces its share of the rows over all
+// partials through distributed shared memory in split order, then converts and stores (STORE) or
+// adds the sum into the gradient with one read-modify-write (ACC kinds: the cluster owns those
+// entries in this launch).  No atomics: the result does not depend on the order in which CTAs
+// finish, so a step (and a resumed run) is bit-for-bit reproducible.
 // Every mbarrier wait is bounded (the shared error word records the site).
 #include <cuda.h>
 
@@ -97,7 +100,7 @@ __global__ void __launch_bounds__(SK_THREADS, 2) skinny_kernel(const __grid_cons
     auto empty_bar = [&](int s) { return bars + 8 * (SK_STAGES + s); };
     const uint32_t tfull = bars + 8 * (2 * SK_STAGES);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SK_STAGES * SK_STAGE + 8 * (2 * SK_STAGES + 1));
-    float* part = reinterpret_cast<float*>(smem);  // STORE, split: [128][SK_PART_LD] partial tile (stages are free by then)
+    float* part = reinterpret_cast<float*>(smem);  // split: [128][SK_PART_LD] partial tile (stages are free by then)
 
     if (threadIdx.x == 0) {
         prefetch_tmap(&maps.a);
@@ -193,26 +196,18 @@ __global__ void __launch_bounds__(SK_THREADS, 2) skinny_kernel(const __grid_cons
             for (int i = 0; i < 32; ++i) v[c * 32 + i] = any ? __uint_as_float(r[i]) * p.alpha : 0.f;
         }
         const bool in = row < p.M;
-        if (p.kind == SKINNY_ACC) {
+        if (p.splits == 1 && p.kind == SKINNY_ACC) {
             float* o = static_cast<float*>(p.out) + (long)row * p.ldo;
-            if (in && any) {
-                if ((p.ldo & 3) == 0 && (p.nb & 3) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0) {
+            if (in && any)
 #pragma unroll
-                    for (int j = 0; j < SK_BN; j += 4)
-                        if (j < p.nb)
-                            atomicAdd(reinterpret_cast<float4*>(o + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
-                } else {
-#pragma unroll
-                    for (int j = 0; j < SK_BN; ++j)
-                        if (j < p.nb) atomicAdd(o + j, v[j]);
-                }
-            }
-        } else if (p.kind == SKINNY_ACC_T) {
+                for (int j = 0; j < SK_BN; ++j)
+                    if (j < p.nb) o[j] += v[j];
+        } else if (p.splits == 1 && p.kind == SKINNY_ACC_T) {
             float* o = static_cast<float*>(p.out) + row;
             if (in && any)
 #pragma unroll
                 for (int j = 0; j < SK_BN; ++j)
-                    if (j < p.nb) atomicAdd(o + (long)j * p.ldo, v[j]);  // lanes: consecutive rows
+                    if (j < p.nb) o[(long)j * p.ldo] += v[j];  // lanes: consecutive rows
         } else if (p.splits == 1) {
             f16* o = static_cast<f16*>(p.out) + (long)row * p.ldo;
             if (in)
@@ -229,24 +224,35 @@ __global__ void __launch_bounds__(SK_THREADS, 2) skinny_kernel(const __grid_cons
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (p.kind == SKINNY_STORE && p.splits > 1) {
+    if (p.splits > 1) {
         // every thread of every CTA of the cluster passes both barriers (no early exit above)
         cluster_sync_all();
         const int S = p.splits, rank = (int)cluster_ctarank();
-        const int rows_per = SK_BM / S, r0 = rank * rows_per, c4n = p.nb / 4;
+        const int rows_per = SK_BM / S, r0 = rank * rows_per, c4n = (p.nb + 3) / 4;
         const uint32_t part_s = smem_u32(part);
+        // items run along the rows first for ACC_T (its rows are the gradient's columns)
+        const bool trans = p.kind == SKINNY_ACC_T;
         for (int item = threadIdx.x; item < rows_per * c4n; item += SK_THREADS) {
-            const int rl = r0 + item / c4n, c4 = item % c4n;
+            const int rl = r0 + (trans ? item % rows_per : item / c4n), c4 = trans ? item / rows_per : item % c4n;
             const uint32_t off = part_s + (uint32_t)(rl * SK_PART_LD + 4 * c4) * 4;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int q = 0; q < S; ++q) {
+            for (int q = 0; q < S; ++q) {  // split order: the same sum whoever finished first
                 const float4 t = ld_dsmem_f4(map_cta(off, (uint32_t)q));
                 acc.x += t.x; acc.y += t.y; acc.z += t.z; acc.w += t.w;
             }
             const int grow = mt * SK_BM + rl;
-            if (grow < p.M)
+            if (grow >= p.M) continue;
+            const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+            if (p.kind == SKINNY_STORE) {
                 *reinterpret_cast<uint2*>(static_cast<f16*>(p.out) + (long)grow * p.ldo + 4 * c4) =
                     make_uint2(pack_f16(acc.x, acc.y), pack_f16(acc.z, acc.w));
+            } else if (p.kind == SKINNY_ACC) {
+                float* o = static_cast<float*>(p.out) + (long)grow * p.ldo + 4 * c4;
+                for (int j = 0; j < 4 && 4 * c4 + j < p.nb; ++j) o[j] += a4[j];
+            } else {
+                float* o = static_cast<float*>(p.out) + grow + (long)(4 * c4) * p.ldo;
+                for (int j = 0; j < 4 && 4 * c4 + j < p.nb; ++j) o[(long)j * p.ldo] += a4[j];
+            }
         }
         cluster_sync_all();  // peers keep their partials until every reader is done
     }
@@ -286,7 +292,7 @@ void skinny_gemm(const SkinnyArgs& a, int* err, cudaStream_t s) {
     int splits = a.splits > 0 ? a.splits : (2 * g_sms + tiles - 1) / tiles;  // about two CTAs per SM
     if (splits > nk) splits = nk;
     if (splits < 1) splits = 1;
-    if (a.kind == SKINNY_STORE) {  // the split CTAs form one cluster: a power of two up to 8
+    {  // the split CTAs form one cluster: a power of two up to 8
         int c = 1;
         while (c * 2 <= splits && c * 2 <= 8) c *= 2;
         splits = c;
@@ -305,7 +311,7 @@ void skinny_gemm(const SkinnyArgs& a, int* err, cudaStream_t s) {
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = a.kind == SKINNY_STORE ? splits : 1;
+    attr[0].val.clusterDim.y = splits;
     attr[0].val.clusterDim.z = 1;
     pdl_attr(attr[1]);
     cfg.attrs = attr;

@@ -160,10 +160,10 @@ struct AttnArgs {
     long lddk = 0, lddv = 0;
     const float* kscale = nullptr;  // DoRA factor applied to dk columns (nullable)
     const float* vscale = nullptr;  // DoRA factor applied to dv columns (nullable)
-    // mma.sync backward only: split each key block's query blocks over qsplit CTAs; the partial
-    // dK / dV then go by fp32 atomics into dk_acc / dv_acc ([clips*Tk][H*64], zeroed by the
-    // caller) and attn_dkv_finish writes dk / dv.  For few keys (cross-attention) this spreads the
-    // query loop over the GPU instead of one CTA per (key block, head, clip).
+    // mma.sync backward only: split each key block's query blocks over qsplit CTAs; each leaves
+    // its partial dK / dV in its own slice of dk_acc / dv_acc ([qsplit][clips*Tk][H*64]) and
+    // attn_dkv_finish adds the slices in order and writes dk / dv.  For few keys (cross-attention)
+    // this spreads the query loop over the GPU instead of one CTA per (key block, head, clip).
     int qsplit = 1;
     float* dk_acc = nullptr;
     float* dv_acc = nullptr;
@@ -220,8 +220,9 @@ void linear_f32(const float* x, const float* W, float* y, int rows, int N, int K
                 cudaStream_t s);
 // DoRA: dg[n] += inv_gscale * sum_m a[m][n] * b[m][n] / colscale[n]^2  (a already includes
 // colscale and the gradient scale; dg is the unscaled gradient)
+constexpr int DORA_COLSUM_PARTS = 8;  // row blocks of dora_colsum; part holds DORA_COLSUM_PARTS * N floats
 void dora_colsum(const f16* a, long lda, const f16* b, long ldb, int rows, int N, const float* colscale,
-                 float* dg, float inv_gscale, cudaStream_t s);
+                 float* dg, float* part, float inv_gscale, cudaStream_t s);
 // DoRA per-step factors: G = A A^T, Q = B G, nsq = base + 2s<P,B> + s^2<B,Q>, g = m / sqrt(nsq)
 void dora_prepare(const float* A, const float* B, const float* m, const float* P, const float* base,
                   int r, int in, int out, float s, float* G, float* Q, float* nsq, float* g,
@@ -260,8 +261,9 @@ void q8_0_to_f32(const uint8_t* blocks, long nblocks, float* out, cudaStream_t s
 void mg_embed(const int32_t* ids, int steps, int nq, const float* const* emb_dev, const float* pos,
               float* x, int D, int seqs, cudaStream_t s);
 // Cross entropy over selected rows: logits fp32 [rows][card]; targets per row (-1: skip);
-// loss_acc[seq] += ce / nsel; dlogits f16 = gscale * (softmax - onehot) / nsel.
+// loss_acc[seq] += ce / nsel (row terms through rowloss, [rows], added in row order);
+// dlogits f16 = gscale * (softmax - onehot) / nsel.
 void mg_cross_entropy(const float* logits, int rows, int card, const int32_t* targets, int rows_per_seq,
-                      float inv_nsel, float* loss_acc, f16* dlogits, float gscale, cudaStream_t s);
+                      float inv_nsel, float* loss_acc, float* rowloss, f16* dlogits, float gscale, cudaStream_t s);
 
 }  // namespace act
