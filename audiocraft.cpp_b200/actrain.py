@@ -112,6 +112,8 @@ SIGNATURES = {
     "act_wait_probe": (C.c_int, [C.c_void_p, C.c_int64]),
     "act_mg_staged": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t]),
     "act_q8_0_dequant": (C.c_int, [C.c_int, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]),
+    "act_lora_linear": (C.c_int, [C.c_int, C.c_void_p, C.c_int64, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
+                                  C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_void_p, C.c_float, C.c_void_p]),
     "act_rank_gemm_f16": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                      C.c_int, C.c_int, C.c_float, C.c_int, C.c_int, C.POINTER(C.c_float)]),
 }
@@ -375,6 +377,25 @@ def q8_0_dequant(blocks: np.ndarray, device: int = 0):
     if rc != ACT_OK:
         raise ActError(rc, lib().act_last_error(None).decode())
     return f, h
+
+
+def lora_linear(x: np.ndarray, w: np.ndarray, w_type: int, out: int, A=None, B=None, alpha: float = 1.0,
+                magnitude=None, strength: float = 1.0, device: int = 0) -> np.ndarray:
+    """act_lora_linear: y = W x with a LoRA / DoRA-rows adapter applied (inference, src/ac/lora.h:50-83).
+    x [rows][in] fp32; w the weight's raw data (fp32 values, f16 bit patterns or Q8_0 blocks)."""
+    xa = np.ascontiguousarray(x, np.float32)
+    rows, n_in = xa.shape
+    wa = np.ascontiguousarray(w)
+    keep = [xa, wa]
+    ptr = lambda a: None if a is None else keep.append(np.ascontiguousarray(a, np.float32)) or keep[-1].ctypes.data
+    pa, pb, pm = ptr(A), ptr(B), ptr(magnitude)
+    rank = 0 if A is None else np.asarray(A).shape[0]
+    y = np.zeros((rows, out), np.float32)
+    rc = lib().act_lora_linear(device, xa.ctypes.data, rows, n_in, out, w_type, wa.ctypes.data, wa.nbytes, pa, pb, rank,
+                               alpha, pm, strength, y.ctypes.data)
+    if rc != ACT_OK:
+        raise ActError(rc, lib().act_last_error(None).decode())
+    return y
 
 
 RANK_ACC, RANK_ACC_T, RANK_STORE = 0, 1, 2

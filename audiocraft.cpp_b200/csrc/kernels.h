@@ -13,6 +13,11 @@ namespace act {
 
 // message returned by act_last_error(NULL) (defined with the C ABI in engine.cpp)
 void set_last_error(const std::string& msg);
+// inference lora_linear on host buffers (act_lora_linear); throws std::invalid_argument for bad
+// arguments, std::runtime_error for CUDA failures
+void lora_linear(int device, const float* x, int64_t rows, int in, int out, int w_type, const void* w,
+                 size_t w_bytes, const float* A, const float* B, int rank, float alpha, const float* magnitude,
+                 float strength, float* y);
 
 // ---------------------------------------------------------------------------------------
 // GEMM:  C[m][n] = epilogue( sum_k A(m,k) B(n,k) ),  K = K1 (+ K2 second segment).

@@ -64,14 +64,6 @@ struct Sample {
     float edit_start = 0;
 };
 
-std::vector<std::filesystem::path> gguf_files(const std::string& directory) {
-    std::vector<std::filesystem::path> paths;
-    for (const auto& entry : std::filesystem::directory_iterator(directory))
-        if (entry.is_regular_file() && entry.path().extension() == ".gguf") paths.push_back(entry.path());
-    std::sort(paths.begin(), paths.end());
-    return paths;
-}
-
 // read_samples (tools/mf-train.cpp:17-95)
 std::vector<Sample> read_samples(const std::string& directory, const GgufReader& model, const act_model_desc& c,
                                  int frames, int& max_tokens, const std::string& objective, float t_min) {
@@ -79,8 +71,9 @@ std::vector<Sample> read_samples(const std::string& directory, const GgufReader&
     auto normalization_std = model.read_f32("dit.latent_std");
     for (auto& v : normalization_std) v += 1e-5f;
     std::vector<Sample> out;
-    for (const auto& path : gguf_files(directory)) {
-        GgufReader cache(path.string());
+    for (const auto& file : actf::gguf_files(directory)) {
+        const std::filesystem::path path(file);
+        GgufReader cache(file);
         const bool bridge = objective == "edit-bridge";
         if (cache.string("general.architecture") != (bridge ? "ac-melodyflow-edit-cache" : "ac-melodyflow-train-cache") ||
             cache.u32("ac.cache.version") != 1)
@@ -156,14 +149,6 @@ void usage() {
                     "  --device gpu|gpu:N  CUDA device (default gpu = device 0; this build has no CPU path)\n"
                     "  --max-batch N     samples per device microbatch (default min(accumulation, 8))\n"
                     "Exact resume via .state sidecars.\n");
-}
-
-int parse_device(const std::string& d) {
-    if (d == "gpu" || d == "cuda") return 0;
-    for (const char* pre : {"gpu:", "cuda:"})
-        if (d.rfind(pre, 0) == 0) return std::stoi(d.substr(std::string(pre).size()));
-    if (d == "cpu") throw std::runtime_error("this trainer runs the step on a CUDA device; use --device gpu");
-    throw std::runtime_error("unknown device: " + d);
 }
 
 // One drawn training / probe window, ready for the device.
@@ -243,25 +228,6 @@ private:
     std::vector<float> losses_;
 };
 
-// MfTrainGraph::save (src/mf/train.h:229-255)
-void save_adapter(act_ctx* ctx, const std::string& path, int rank, float alpha, const std::string& type,
-                  const std::string& objective, const std::string& density, const std::string& base_name) {
-    if (std::filesystem::exists(path)) throw std::runtime_error("refusing to overwrite adapter: " + path);
-    const auto params = actf::read_params(ctx, false);
-    actf::GgufWriter g;
-    g.add_string("general.architecture", "ac-melodyflow-lora");
-    g.add_u32("ac.lora.version", 1);
-    g.add_u32("ac.lora.rank", (uint32_t)rank);
-    g.add_f32("ac.lora.alpha", alpha);
-    g.add_string("ac.lora.type", type);
-    g.add_string("ac.lora.training_activation", "erf-approx-as-7.1.26");
-    if (!objective.empty()) g.add_string("ac.lora.training_objective", objective);
-    if (!density.empty()) g.add_string("ac.lora.training_time_density", density);
-    if (!base_name.empty()) g.add_string("ac.lora.base_name", base_name);
-    for (const auto& p : params) g.add_f32_tensor(p.name, {p.cols, p.rows}, p.value.data());
-    g.write(path);
-}
-
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -331,7 +297,7 @@ int main(int argc, char** argv) {
         if (std::filesystem::exists(out_path)) throw std::runtime_error("output already exists: " + out_path);
         const actf::MfTimeSampler time_sampler(t_sampling, t_mean, t_std);
         if (alpha == -1) alpha = (float)rank;
-        const int device_index = parse_device(device);
+        const int device_index = actf::parse_device(device);
         GgufReader model(dit_path);
         const DitShape shape = dit_config(model);
         const act_model_desc& config = shape.desc;
@@ -432,8 +398,9 @@ int main(int argc, char** argv) {
                                                       t_std, t_min, adapter_type, first_layer);
         for (const auto& dir : {cache_path, validation_path})
             if (!dir.empty())
-                for (const auto& p : gguf_files(dir))
-                    state_signature += "|" + p.filename().string() + ":" + actf::train_file_identity(p.string());
+                for (const auto& p : actf::gguf_files(dir))
+                    state_signature +=
+                        "|" + std::filesystem::path(p).filename().string() + ":" + actf::train_file_identity(p);
         int completed = 0;
         size_t seen = 0;
         if (!controls.resume.empty()) {
@@ -447,8 +414,19 @@ int main(int argc, char** argv) {
             auto params = actf::read_params(ctx, true);
             actf::train_state(path + ".state", false, state_signature, params, completed, seen, rng, order);
         };
+        // MfTrainGraph::save (src/mf/train.h:229-255)
         auto save = [&](const std::string& path) {
-            save_adapter(ctx, path, rank, alpha, adapter_type, objective, t_sampling, shape.name);
+            actf::save_adapter(ctx, path, [&](actf::GgufWriter& g) {
+                g.add_string("general.architecture", "ac-melodyflow-lora");
+                g.add_u32("ac.lora.version", 1);
+                g.add_u32("ac.lora.rank", (uint32_t)rank);
+                g.add_f32("ac.lora.alpha", alpha);
+                g.add_string("ac.lora.type", adapter_type);
+                g.add_string("ac.lora.training_activation", "erf-approx-as-7.1.26");
+                g.add_string("ac.lora.training_objective", objective);
+                g.add_string("ac.lora.training_time_density", t_sampling);
+                if (!shape.name.empty()) g.add_string("ac.lora.base_name", shape.name);
+            });
         };
         const auto start = std::chrono::steady_clock::now();
         for (int step = completed + 1; step <= steps; ++step) {

@@ -9,6 +9,7 @@
 #include <fstream>
 #include <iomanip>
 #include <limits>
+#include <map>
 #include <set>
 #include <sstream>
 
@@ -16,6 +17,99 @@ namespace actf {
 
 void check(act_ctx* ctx, int rc, const char* what) {
     if (rc != ACT_OK) throw std::runtime_error(std::string(what) + ": " + act_last_error(ctx));
+}
+
+std::vector<std::string> gguf_files(const std::string& directory) {
+    std::vector<std::string> paths;
+    for (const auto& entry : std::filesystem::directory_iterator(directory))
+        if (entry.is_regular_file() && entry.path().extension() == ".gguf") paths.push_back(entry.path().string());
+    std::sort(paths.begin(), paths.end());
+    return paths;
+}
+
+int parse_device(const std::string& d) {
+    if (d == "gpu" || d == "cuda") return 0;
+    for (const std::string pre : {"gpu:", "cuda:"})
+        if (d.rfind(pre, 0) == 0) return std::stoi(d.substr(pre.size()));
+    if (d == "cpu") throw std::runtime_error("this trainer runs the step on a CUDA device; use --device gpu");
+    throw std::runtime_error("unknown device: " + d);
+}
+
+void save_adapter(act_ctx* ctx, const std::string& path, const std::function<void(GgufWriter&)>& meta) {
+    if (std::filesystem::exists(path)) throw std::runtime_error("refusing to overwrite adapter: " + path);
+    const auto params = read_params(ctx, false);
+    GgufWriter g;
+    meta(g);
+    for (const auto& p : params) g.add_f32_tensor(p.name, {p.cols, p.rows}, p.value.data());
+    g.write(path);
+}
+
+std::vector<LoadedLora> load_lora(const GgufReader& base, const GgufReader& adapter, float strength,
+                                  const std::string& family) {
+    const std::string want = family == "dit" ? "ac-melodyflow-lora" : "ac-musicgen-lora";
+    if (adapter.string("general.architecture") != want)
+        throw GgufError(family == "dit" ? "not a MelodyFlow adapter" : "not a MusicGen adapter");
+    if (adapter.u32("ac.lora.version") != 1) throw GgufError("unsupported adapter");
+    const int rank = (int)adapter.u32("ac.lora.rank");
+    const float alpha = adapter.f32("ac.lora.alpha");
+    const std::string type = adapter.has("ac.lora.type") ? adapter.string("ac.lora.type") : "lora";
+    if (type != "lora" && type != "dora-rows") throw GgufError("unsupported adapter type: " + type);
+    const bool dora = type == "dora-rows";
+    if (rank <= 0 || !std::isfinite(alpha) || alpha <= 0 || !std::isfinite(strength))
+        throw GgufError("invalid adapter rank, alpha or strength");
+    auto ends_with = [](const std::string& x, const std::string& tail) {
+        return x.size() > tail.size() && x.compare(x.size() - tail.size(), tail.size(), tail) == 0;
+    };
+    std::map<std::string, LoadedLora> out;
+    for (const auto& t : adapter.tensors()) {
+        if (!ends_with(t.name, ".lora_A")) continue;
+        const std::string stem = t.name.substr(0, t.name.size() - 7);
+        const GgufTensor& B = adapter.get(stem + ".lora_B");
+        const GgufTensor& W = base.get(stem);
+        const bool w2d = W.ne[1] > 1 && W.ne[2] == 1 && W.ne[3] == 1;
+        if (t.type != GT_F32 || B.type != GT_F32 || !w2d || t.ne[0] != W.ne[0] || t.ne[1] != rank ||
+            B.ne[0] != rank || B.ne[1] != W.ne[1] || t.ne[2] != 1 || t.ne[3] != 1 || B.ne[2] != 1 || B.ne[3] != 1)
+            throw GgufError("adapter shape mismatch: " + stem);
+        LoadedLora p;
+        p.stem = stem;
+        p.A = &t;
+        p.B = &B;
+        p.scale = (dora ? 1 : strength) * alpha / rank;
+        if (dora) {
+            const GgufTensor& m = adapter.get(stem + ".magnitude");
+            if (m.type != GT_F32 || m.ne[0] != W.ne[1] || m.ne[1] != 1 || m.ne[2] != 1 || m.ne[3] != 1)
+                throw GgufError("DoRA magnitude shape mismatch: " + stem);
+            if (W.type != GT_F32 && W.type != GT_F16 && W.type != GT_Q8_0)
+                throw GgufError("DoRA rows requires F16/F32/Q8_0 matrix weights");
+            p.magnitude = &m;
+            p.strength = strength;
+        }
+        out[stem] = p;
+    }
+    if (out.empty() || adapter.tensors().size() != (dora ? 3 : 2) * out.size())
+        throw GgufError("empty or incomplete adapter");
+    for (const auto& e : out)
+        for (const GgufTensor* t : {e.second.A, e.second.B, e.second.magnitude}) {
+            if (!t) continue;
+            const float* v = reinterpret_cast<const float*>(t->data);
+            for (int64_t i = 0; i < t->nelements(); ++i)
+                if (!std::isfinite(v[i])) throw GgufError("nonfinite adapter tensor");
+        }
+    if (adapter.has("ac.lora.base_name") && adapter.string("ac.lora.base_name") != base.string("general.name"))
+        throw GgufError("adapter base model name does not match");
+    static const char* kSuffixes[] = {".self.qkv.weight", ".self.out.weight", ".cross.q.weight", ".cross.kv.weight",
+                                      ".cross.out.weight", ".ff.0.weight", ".ff.2.weight"};
+    std::vector<LoadedLora> result;
+    for (const auto& e : out) {
+        bool supported = false;
+        for (const char* suffix : kSuffixes)
+            supported |= e.first.rfind(family + ".", 0) == 0 && ends_with(e.first, suffix);
+        if (!supported)
+            throw GgufError(std::string(family == "dit" ? "unsupported MelodyFlow" : "unsupported MusicGen") +
+                            " adapter target: " + e.first);
+        result.push_back(e.second);
+    }
+    return result;
 }
 
 // ------------------------------------------------------------------ controls and schedule

@@ -4,12 +4,14 @@
 // src/ac/prompt_pool.h); the device work goes through the act_* C ABI.
 #pragma once
 #include <cstdint>
+#include <functional>
 #include <random>
 #include <stdexcept>
 #include <string>
 #include <vector>
 
 #include "actrain.h"
+#include "gguf_file.h"
 
 namespace actf {
 
@@ -81,6 +83,32 @@ void write_prompt_pool(const std::string& path, const std::string& adapter, cons
 
 // The ABI's status as an exception (the CLIs report it and return 1).
 void check(act_ctx* ctx, int rc, const char* what);
+
+// The *.gguf files of a directory, sorted by path (the reference's cache order).
+std::vector<std::string> gguf_files(const std::string& directory);
+// "gpu" / "cuda" (device 0) or "gpu:N" / "cuda:N"; "cpu" is refused: the step runs on a GPU.
+int parse_device(const std::string& device);
+// An adapter file: `meta` sets the keys, then every parameter tensor follows as F32 in the
+// reference's order and shape (MfTrainGraph::save / MgTrainGraph::save); an existing file is kept.
+void save_adapter(act_ctx* ctx, const std::string& path, const std::function<void(GgufWriter&)>& meta);
+
+// One adapted projection of a validated adapter file (LoraProjection, src/ac/lora.h:38-47).
+struct LoadedLora {
+    std::string stem;  // the base weight's name, e.g. dit.3.self.qkv.weight
+    const GgufTensor* A = nullptr;          // [rank][in]
+    const GgufTensor* B = nullptr;          // [out][rank]
+    const GgufTensor* magnitude = nullptr;  // [out] (DoRA rows) or null
+    float scale = 1.0f;                     // (DoRA ? 1 : strength) * alpha / rank
+    float strength = 1.0f;
+};
+
+// load_mf_lora / load_mg_lora (src/ac/lora.h:113-210): checks an adapter file against its base
+// model -- architecture and version, rank / alpha / type, every tensor's shape against the base
+// weight, completeness, finite values, the base model's name, the supported targets of the family
+// ("dit" for MelodyFlow, "lm" for MusicGen) -- and returns its projections in name order.
+// Unlike the reference, DoRA rows may sit on a Q8_0 base (this library trains them).
+std::vector<LoadedLora> load_lora(const GgufReader& base, const GgufReader& adapter, float strength,
+                                  const std::string& family);
 
 template <class Next>
 bool TrainControls::parse(const std::string& a, Next next) {

@@ -276,6 +276,22 @@ int act_q8_0_dequant(int device, const void* blocks, int64_t nblocks, float* out
 /* kernels in the captured step graph for microbatch size n (-1 before the graph exists) */
 int64_t act_graph_kernel_nodes(act_ctx* ctx, int n);
 
+/* ---- adapter consumption (inference) ---- */
+/* lora_linear (src/ac/lora.h:50-83) on host buffers: y [rows][out] (fp32) = W x with the adapter
+ * applied as load_lora (src/ac/lora.h:113-170) configures it.  x [rows][in] fp32; W [out][in] of
+ * ggml type ACT_TYPE_F32 / F16 / Q8_0 (w_bytes its size); A [rank][in], B [out][rank] fp32, or A
+ * NULL for the bare projection; magnitude [out] (DoRA rows) or NULL (LoRA).
+ *   LoRA: y = W x + (strength * alpha / rank) B A x
+ *   DoRA: y' = (W x + s B A x) * m / sqrt(||W_o||^2 + in*1e-12 + 2s<W_o,(BA)_o> + s^2||(BA)_o||^2),
+ *         s = alpha / rank; y = W x + strength (y' - W x)
+ * W x runs on the tensor cores (f16 operands: x and F32 weights rounded to f16, Q8_0 dequantised
+ * inside the GEMM for more than 128 rows), the rank-sized products in fp32.  in and out must be
+ * multiples of 8 (32 for Q8_0), rank <= 64.  Failures: ACT_ERR_INVALID / ACT_ERR_CUDA, message
+ * from act_last_error(NULL). */
+int act_lora_linear(int device, const float* x, int64_t rows, int in, int out, int w_type, const void* w,
+                    size_t w_bytes, const float* A, const float* B, int rank, float alpha, const float* magnitude,
+                    float strength, float* y);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

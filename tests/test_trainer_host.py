@@ -154,6 +154,16 @@ int main(int argc, char** argv) {
         std::printf("path %s\n", prompt_pool_path("/a/b/c.step-2.gguf").c_str());
         return 0;
     }
+    if (mode == "lora") {
+        GgufReader base(argv[2]), adapter(argv[3]);
+        try {
+            const auto m = load_lora(base, adapter, std::stof(argv[5]), argv[4]);
+            std::printf("ok %zu %a %d\n", m.size(), m[0].scale, (int)(m[0].magnitude != nullptr));
+        } catch (const std::exception& e) {
+            std::printf("error %s\n", e.what());
+        }
+        return 0;
+    }
     if (mode == "rate") {
         for (const char* sched : {"constant", "inverse"})
             for (int warm : {0, 3, 50}) {
@@ -341,3 +351,90 @@ def test_cli_usage_without_required_paths():
         pytest.skip("mf-train is not built")
     r = subprocess.run([exe, "--steps", "3"], capture_output=True, text=True, timeout=60)
     assert r.returncode == 2 and "usage: mf-train" in r.stderr
+
+
+def _lora_files(tmp_path, kind="lora", **bad):
+    """A tiny DiT base and an adapter for two projections, with one defect from `bad`."""
+    gguf = pytest.importorskip("gguf")
+    rng = np.random.default_rng(0)
+    base = {"dit.0.self.qkv.weight": rng.standard_normal((24, 8)).astype(np.float32),
+            "dit.1.ff.0.weight": rng.standard_normal((16, 8)).astype(np.float32)}
+    w = gguf.GGUFWriter(str(tmp_path / "base.gguf"), "audiocraft")
+    w.add_string("general.name", "tiny")
+    for k, v in base.items():
+        w.add_tensor(k, v)
+    w.write_header_to_file(); w.write_kv_data_to_file(); w.write_tensors_to_file(); w.close()
+    r = 2
+    t = {}
+    for stem, W in base.items():
+        t[stem + ".lora_A"] = rng.standard_normal((r, W.shape[1])).astype(np.float32)
+        t[stem + ".lora_B"] = rng.standard_normal((W.shape[0], r)).astype(np.float32)
+        if kind == "dora-rows":
+            t[stem + ".magnitude"] = np.abs(rng.standard_normal(W.shape[0])).astype(np.float32)
+    if bad.get("shape"):
+        t["dit.1.ff.0.weight.lora_B"] = np.zeros((15, r), np.float32)
+    if bad.get("missing"):
+        del t["dit.1.ff.0.weight.lora_B"]
+    if bad.get("extra"):
+        t["dit.1.ff.0.weight.extra"] = np.zeros(3, np.float32)
+    if bad.get("nan"):
+        t["dit.0.self.qkv.weight.lora_A"][0, 0] = np.nan
+    if bad.get("target"):
+        base_name = "dit.0.self.qkv.weight"
+        t = {k.replace(base_name, "dit.0.norm1.weight"): v for k, v in t.items()}
+    arch = bad.get("arch", "ac-melodyflow-lora")
+    w = gguf.GGUFWriter(str(tmp_path / "a.gguf"), arch)
+    w.add_uint32("ac.lora.version", 1)
+    w.add_uint32("ac.lora.rank", r)
+    w.add_float32("ac.lora.alpha", 4.0)
+    w.add_string("ac.lora.type", kind)
+    w.add_string("ac.lora.base_name", bad.get("base_name", "tiny"))
+    for k, v in t.items():
+        w.add_tensor(k, v)
+    w.write_header_to_file(); w.write_kv_data_to_file(); w.write_tensors_to_file(); w.close()
+    return tmp_path / "base.gguf", tmp_path / "a.gguf"
+
+
+@pytest.mark.parametrize("kind", ["lora", "dora-rows"])
+def test_adapter_loader_accepts_a_trained_adapter(harness, tmp_path, kind):
+    base, ad = _lora_files(tmp_path, kind)
+    out = harness("lora", base, ad, "dit", "0.5").split()
+    assert out[0] == "ok" and out[1] == "2" and out[3] == ("1" if kind == "dora-rows" else "0")
+    # load_lora: LoRA folds the strength into the scale, DoRA keeps it apart (src/ac/lora.h:141)
+    assert _f(out[2]) == np.float32(np.float32(0.5 if kind == "lora" else 1.0) * np.float32(4.0) / np.float32(2))
+
+
+@pytest.mark.parametrize("defect,message", [
+    ({"shape": True}, "adapter shape mismatch: dit.1.ff.0.weight"),
+    ({"missing": True}, "missing tensor dit.1.ff.0.weight.lora_B"),
+    ({"extra": True}, "empty or incomplete adapter"),
+    ({"nan": True}, "nonfinite adapter tensor"),
+    ({"base_name": "other"}, "adapter base model name does not match"),
+    ({"arch": "ac-musicgen-lora"}, "not a MelodyFlow adapter"),
+], ids=["shape", "missing", "extra", "nan", "base_name", "arch"])
+def test_adapter_loader_rejects_what_the_reference_rejects(harness, tmp_path, defect, message):
+    base, ad = _lora_files(tmp_path, **defect)
+    out = harness("lora", base, ad, "dit", "1")
+    assert out.startswith("error ") and message in out, out
+
+
+def test_adapter_loader_rejects_unsupported_targets(harness, tmp_path):
+    gguf = pytest.importorskip("gguf")
+    base, ad = _lora_files(tmp_path, target=True)
+    out = harness("lora", base, ad, "dit", "1")
+    assert out.startswith("error ")  # the base has no dit.0.norm1.weight, or the target is refused
+
+
+MG_BAD = [["--accumulation-steps", "0"], ["--lr-schedule", "bogus"], ["--cfg-dropout", "nan"], ["--lr", "inf"],
+          ["--steps", "0"], ["--device", "cpu"], ["--bogus-flag"]]
+
+
+@pytest.mark.parametrize("extra", MG_BAD, ids=[" ".join(e) for e in MG_BAD])
+def test_mg_cli_rejects_bad_settings_before_any_device_work(extra, tmp_path):
+    exe = os.path.join(PKG, "bin", "mg-train")
+    if not os.path.exists(exe):
+        pytest.skip("mg-train is not built")
+    out = tmp_path / "bad.gguf"
+    r = subprocess.run([exe, "--lm", str(tmp_path / "missing.gguf"), "--cache", str(tmp_path), "--out", str(out)] + extra,
+                       capture_output=True, text=True, timeout=60)
+    assert r.returncode == 1 and "error:" in r.stderr and not out.exists(), r.stderr
