@@ -218,6 +218,8 @@ struct act_ctx {
     std::vector<void*> hallocs;
 
     int D = 0, F = 0, H = 0, L = 0, T = 0, C = 0, B = 0, RP = 0;
+    int Ctok = 0;                 // the caller's conditioning tokens; C is that rounded up to 8
+    int32_t* d_mgvalid = nullptr;  // MusicGen: Ctok per clip (masks the padding rows past Ctok)
     long M = 0, MC = 0;  // activation rows, context rows (capacity)
 
     std::vector<Layer> layers;
@@ -745,7 +747,7 @@ struct act_ctx {
         join_side();
         AttnArgs ca;
         ca.q = y.cq; ca.ldq = D; ca.k = y.ckv; ca.v = y.ckv + D; ca.ldk = ca.ldv = 2 * D;
-        ca.T = T; ca.Tk = C; ca.H = H; ca.clips = n; ca.nvalid = dit ? nvalid_dev : nullptr;
+        ca.T = T; ca.Tk = C; ca.H = H; ca.clips = n; ca.nvalid = dit ? nvalid_dev : (C != Ctok ? d_mgvalid : nullptr);
         ca.zero_key = dit ? md.add_zero_attn : 0; ca.scale = sa.scale;
         ca.o = y.o2; ca.ldo = D; ca.lse = y.lse2;
         ++path_count[ACT_PATH_ATTN_FWD_MMA];
@@ -807,7 +809,7 @@ struct act_ctx {
         }
         AttnArgs ca;
         ca.q = y.cq; ca.ldq = D; ca.k = y.ckv; ca.v = y.ckv + D; ca.ldk = ca.ldv = 2 * D;
-        ca.T = T; ca.Tk = C; ca.H = H; ca.clips = n; ca.nvalid = dit ? nvalid_dev : nullptr;
+        ca.T = T; ca.Tk = C; ca.H = H; ca.clips = n; ca.nvalid = dit ? nvalid_dev : (C != Ctok ? d_mgvalid : nullptr);
         ca.zero_key = dit ? md.add_zero_attn : 0; ca.scale = 1.0f / std::sqrt((float)md.head_dim);
         ca.o = y.o2; ca.ldo = D; ca.lse = y.lse2;
         ca.dout = dob; ca.lddo = D; ca.dvec = dvec; ca.dq_acc = dq_acc; ca.ldq_acc = D;
@@ -1104,13 +1106,28 @@ struct act_ctx {
             }
     }
 
+    // n clips of `rows` host rows each into the device's `padded`-row layout (zero rows after)
+    void upload_rows(void* dev, void* pinned, const void* src, int n, int rows, int padded, size_t row_bytes) {
+        if (rows == padded) {
+            upload({{dev, pinned, src, (size_t)n * rows * row_bytes}});
+            return;
+        }
+        char* p = static_cast<char*>(pinned);
+        for (int i = 0; i < n; ++i) {
+            std::memcpy(p + (size_t)i * padded * row_bytes, static_cast<const char*>(src) + (size_t)i * rows * row_bytes,
+                        (size_t)rows * row_bytes);
+            std::memset(p + ((size_t)i * padded + rows) * row_bytes, 0, (size_t)(padded - rows) * row_bytes);
+        }
+        CK(cudaMemcpyAsync(dev, pinned, (size_t)n * padded * row_bytes, cudaMemcpyHostToDevice, stream));
+    }
+
     void stage_mf(const act_mf_batch* b) {
         if (!mf) throw Error(ACT_ERR_INVALID, "not a MelodyFlow context");
         const bool bridge = b && b->pivot;
         if (!b || b->n <= 0 || b->n > B || !b->clean || !(bridge ? b->edit_start : b->noise) || !b->hidden || !b->t)
             throw Error(ACT_ERR_INVALID, "invalid training sample");
         const int n = b->n, lat = md.latent_dim;
-        const size_t nx = (size_t)n * lat * T, nh = (size_t)n * C * md.cond_dim;
+        const size_t nx = (size_t)n * lat * T;
         for (int i = 0; i < n; ++i) {
             const float t = b->t[i];
             if (!std::isfinite(t) || t < 0 || t > 1) throw Error(ACT_ERR_INVALID, "invalid training sample");
@@ -1120,9 +1137,9 @@ struct act_ctx {
                 throw Error(ACT_ERR_INVALID, "invalid edit bridge");
             h_start[i] = start;
             const int v = b->valid_tokens ? b->valid_tokens[i] : -1;
-            if (v > C) throw Error(ACT_ERR_INVALID, "invalid valid token count");
+            if (v > Ctok) throw Error(ACT_ERR_INVALID, "invalid valid token count");
             const bool uncond = b->unconditional && b->unconditional[i];
-            h_nvalid[i] = uncond ? 0 : (v >= 0 ? v : C);
+            h_nvalid[i] = uncond ? 0 : (v >= 0 ? v : Ctok);
             h_t[i] = t;
             // timestep features on the host, float arithmetic as src/ac/transformer.h:144-154
             const int half = md.time_dim / 2;
@@ -1136,8 +1153,8 @@ struct act_ctx {
             }
         }
         // the bridge's pivot takes the noise buffer: the input kernel turns it into the endpoint
-        upload({{d_clean, h_clean, b->clean, nx * 4}, {d_noise, h_noise, bridge ? b->pivot : b->noise, nx * 4},
-                {d_hidden, h_hidden, b->hidden, nh * 4}});
+        upload({{d_clean, h_clean, b->clean, nx * 4}, {d_noise, h_noise, bridge ? b->pivot : b->noise, nx * 4}});
+        upload_rows(d_hidden, h_hidden, b->hidden, n, Ctok, C, (size_t)md.cond_dim * 4);
         CK(cudaMemcpyAsync(d_t, h_t, n * 4, cudaMemcpyHostToDevice, stream));
         CK(cudaMemcpyAsync(d_start, h_start, n * 4, cudaMemcpyHostToDevice, stream));
         CK(cudaMemcpyAsync(d_tfeat, h_tfeat, (size_t)n * md.time_dim * 4, cudaMemcpyHostToDevice, stream));
@@ -1153,7 +1170,7 @@ struct act_ctx {
         const int S = 1 + frames + (nq - 1);  // src/mg/pattern.h:55
         for (size_t i = 0; i < (size_t)n * nq * frames; ++i)
             if (b->codes[i] < 0 || b->codes[i] >= md.card) throw Error(ACT_ERR_INVALID, "invalid codec token");
-        for (size_t i = 0; i < (size_t)n * C * D; ++i)
+        for (size_t i = 0; i < (size_t)n * Ctok * D; ++i)
             if (!std::isfinite(b->context[i])) throw Error(ACT_ERR_INVALID, "nonfinite condition");
         for (int s = 0; s < n; ++s) {
             const int32_t* codes = b->codes + (size_t)s * nq * frames;
@@ -1170,7 +1187,7 @@ struct act_ctx {
         (void)S;
         CK(cudaMemcpyAsync(d_ids, h_ids, (size_t)n * nq * T * 4, cudaMemcpyHostToDevice, stream));
         CK(cudaMemcpyAsync(d_tgt, h_tgt, (size_t)n * nq * sel * 4, cudaMemcpyHostToDevice, stream));
-        upload({{d_ctx, h_ctx, b->context, (size_t)n * C * D * 4}});
+        upload_rows(d_ctx, h_ctx, b->context, n, Ctok, C, (size_t)D * 4);
         staged_n = n;
     }
 
@@ -1225,7 +1242,6 @@ struct act_ctx {
             throw Error(ACT_ERR_INVALID, "invalid MusicGen training configuration");
         if (mf && (md.latent_dim % 8 || md.cond_dim % 8 || md.time_dim % 2))
             throw Error(ACT_ERR_INVALID, "latent_dim and cond_dim must be multiples of 8");
-        if (ad.tokens % 8) throw Error(ACT_ERR_INVALID, "tokens must be a multiple of 8 (pad the conditioning)");
         CK(cudaSetDevice(device));
         CK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
         CK(cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking));
@@ -1247,7 +1263,11 @@ struct act_ctx {
         const char* gp = std::getenv("ACTRAIN_GEMM");
         use_tc = !(gp && std::string(gp) == "mma");
         D = md.dim; F = md.ff_dim; H = md.heads; L = md.layers;
-        C = ad.tokens; B = ad.max_batch;
+        // the conditioning is padded to a multiple of 8 rows on the device; the rows past the
+        // caller's tokens are masked in cross-attention (MelodyFlow already masks past
+        // valid_tokens; MusicGen attends to all of the caller's rows, zero padding included, as
+        // src/mg/train.h:181-186 does, and to none of ours)
+        Ctok = ad.tokens; C = (Ctok + 7) / 8 * 8; B = ad.max_batch;
         T = mf ? ad.frames : ad.frames + md.n_q - 1;  // MusicGen: pattern steps - 1 (src/mg/train.h:74)
         RP = (ad.rank + 31) / 32 * 32;
         {
@@ -1691,6 +1711,11 @@ struct act_ctx {
             d_tgt = dalloc<int32_t>((size_t)B * md.n_q * sel);
             mg_rowloss = dalloc<float>((size_t)std::max(sel, 1));
             d_ctx = dalloc<float>((size_t)Cr * D);
+            if (C != Ctok) {
+                d_mgvalid = dalloc<int32_t>(B);
+                std::vector<int32_t> v((size_t)B, Ctok);
+                CK(cudaMemcpy(d_mgvalid, v.data(), (size_t)B * 4, cudaMemcpyHostToDevice));
+            }
             logits = dalloc<float>((size_t)B * md.n_q * sel * md.card);
             dlogits = dalloc<f16>((size_t)B * md.n_q * sel * md.card);
         }

@@ -203,6 +203,23 @@ def test_mg_prefix_and_first_layer():
     _check(loss, ref_loss, case.ctx.get_grads(), ref_g, case.layout)
 
 
+@pytest.mark.parametrize("tokens", [5, 13])
+def test_conditioning_not_a_multiple_of_eight(tokens):
+    """Any token count: the device pads the conditioning to a multiple of 8 and masks the padding.
+    MusicGen attends to every caller row (the reference pads with zeros and does not mask them,
+    src/mg/train.h:181-186); MelodyFlow masks past valid_tokens as before."""
+    mg = MgCase(C=tokens, dora=True, seed=40 + tokens)
+    inp = mg.inputs()
+    loss = mg.ctx.mg_step(*inp)
+    ref_loss, ref_g = mg.oracle(mg.params, inp)
+    _check(loss, ref_loss, mg.ctx.get_grads(), ref_g, mg.layout)
+    mf = MfCase(C=tokens, seed=50 + tokens)
+    inp = mf.inputs()
+    loss = mf.ctx.mf_step(*inp)
+    ref_loss, ref_g = mf.oracle(mf.params, inp)
+    _check(loss, ref_loss, mf.ctx.get_grads(), ref_g, mf.layout)
+
+
 def test_mg_cross_kv_without_adapter():
     # no adapter on cross.kv: its projection runs as a plain GEMM and has no backward
     case = MgCase(targets=0x77, layers=3, seed=24)
