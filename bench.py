@@ -263,6 +263,8 @@ def run_sweep(kind, reps):
                                           "kernel": {1: "mma.sync", 2: "tcgen05", 3: "tcgen05_pair"}[path],
                                           "weights": "q8_0" if q8 else "f16", "ms": ms,
                                           "tflops": tf, "frac_of_peak": tf / peak}), flush=True)
+    elif kind == "record":
+        run_sweep_record(A, reps, peak)
     else:
         for H in (16, 24):
             for T in (750, 1500, 3000):
@@ -278,6 +280,79 @@ def run_sweep(kind, reps):
                                       "zero_key": not causal, "ms_fwd": out["ms_fwd"], "ms_bwd": out["ms_bwd"],
                                       "tflops_fwd": f_fwd / (out["ms_fwd"] / 1e3) / 1e12,
                                       "tflops_bwd": f_bwd / (out["ms_bwd"] / 1e3) / 1e12}), flush=True)
+
+
+def run_sweep_record(A, reps, peak):
+    """The kernel sweep of BASELINE cfg 5 as one record: the cfg-2 / cfg-4 projection shapes with
+    f16 and Q8_0 weights beside cuBLAS (torch.matmul, f16 in / f16 out, fp32 accumulation) timed in
+    the same process; the four LoRA rank products at ranks 8..64; self-attention at 750 / 1500 /
+    3000 frames.  Every GEMM result is checked against cuBLAS's."""
+    import torch
+    rng = np.random.default_rng(0)
+    bits = lambda shape: (rng.integers(0x3C00, 0x3F80, size=shape, dtype=np.uint16) ^
+                          (rng.integers(0, 2, size=shape, dtype=np.uint16) << 15))
+    dev = torch.device("cuda", 0)
+
+    def cublas_ms(a16, b16, b_mn):
+        x = torch.from_numpy(a16.view(np.float16)).to(dev)
+        w = torch.from_numpy(b16.view(np.float16)).to(dev)
+        f = (lambda: torch.matmul(x, w)) if b_mn else (lambda: torch.matmul(x, w.t()))
+        for _ in range(3):
+            y = f()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            f()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps, y.float().cpu().numpy()
+
+    shapes = [(6000, 1024, 1024), (6000, 3072, 1024), (6000, 4096, 1024), (6000, 1024, 4096),
+              (6012, 1536, 1536), (6012, 4608, 1536), (6012, 6144, 1536), (6012, 1536, 6144)]
+    for M, N, K in shapes:
+        for b_mn in (False, True):
+            wshape = (K, N) if b_mn else (N, K)
+            a = bits((M, K))
+            w32 = (0.02 * rng.standard_normal(wshape)).astype(np.float32)
+            blocks = q8_0(w32)
+            _, wh = A.q8_0_dequant(blocks)
+            wh = wh.reshape(wshape)
+            c16, ms16 = A.gemm_f16(a, wh, M, N, K, b_mn, 0, reps=reps)
+            c8, ms8 = A.gemm_q8_0(a, blocks, M, N, K, b_mn, 0, reps=reps)
+            msc, cref = cublas_ms(a, wh, b_mn)
+            fl = 2.0 * M * N * K
+            scale = np.abs(cref).max()
+            print(json.dumps({"sweep": "gemm", "M": M, "N": N, "K": K,
+                              "layout": "NN (dX = dY W)" if b_mn else "NT (Y = X W^T)",
+                              "ms_f16": ms16, "ms_q8_0": ms8, "ms_cublas": msc,
+                              "tflops_f16": fl / ms16 / 1e9, "tflops_q8_0": fl / ms8 / 1e9, "tflops_cublas": fl / msc / 1e9,
+                              "frac_of_peak_f16": fl / ms16 / 1e9 / peak, "frac_of_peak_q8_0": fl / ms8 / 1e9 / peak,
+                              "max_rel_diff_vs_cublas": float(max(np.abs(c16 - cref).max(), np.abs(c8 - cref).max()) / scale),
+                              "q8_0_equals_f16": bool(np.array_equal(c8, c16))}), flush=True)
+    for K in (1024, 4096):
+        for r in (8, 16, 32, 64):
+            nb = (r + 31) // 32 * 32
+            for kind, name, a_mn, b_mn, M, KK in ((2, "U = s X A^T", 0, 0, 6000, K), (2, "dU = s dY B", 0, 1, 6000, K),
+                                                  (0, "dB += dY^T U", 1, 1, K, 6000), (1, "dA += dU^T X", 1, 1, K, 6000)):
+                aa = bits((KK, M) if a_mn else (M, KK))
+                bb = bits((KK, nb) if b_mn else (nb, KK))
+                _, ms = A.rank_gemm_f16(aa, bb, M, KK, nb, bool(a_mn), bool(b_mn), kind, 1.0, reps=reps)
+                byts = 2.0 * M * KK + 2.0 * KK * nb
+                print(json.dumps({"sweep": "rank", "product": name, "rank": r, "M": M, "K": KK, "nb": nb, "ms": ms,
+                                  "gbs": byts / ms / 1e6}), flush=True)
+    for H in (16,):
+        for T in (750, 1500, 3000):
+            clips = max(1, 6000 // T)
+            D = H * 64
+            q, k, v, do = (bits((clips * T, D)) for _ in range(4))
+            A.attention(q, k, v, do, clips, T, T, H, None, False, True, None)
+            out = A.attention(q, k, v, do, clips, T, T, H, None, False, True, None)
+            keys = T * (T + 1)
+            print(json.dumps({"sweep": "attention", "heads": H, "seq": T, "clips": clips, "zero_key": True,
+                              "ms_fwd": out["ms_fwd"], "ms_bwd": out["ms_bwd"],
+                              "tflops_fwd": 4.0 * clips * keys * D / (out["ms_fwd"] / 1e3) / 1e12,
+                              "tflops_bwd": 8.0 * clips * keys * D / (out["ms_bwd"] / 1e3) / 1e12}), flush=True)
 
 
 def build_context(A, c, workload, device, seed=0):
@@ -312,7 +387,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override depth (profiling captures only)")
     ap.add_argument("--batch", type=int, default=0, help="override clips per rank (profiling captures only)")
-    ap.add_argument("--sweep", choices=["gemm", "attention"], help="kernel-level sweep instead of the step")
+    ap.add_argument("--sweep", choices=["gemm", "attention", "record"], help="kernel-level sweep instead of the step")
     args = ap.parse_args()
     if args.sweep:
         return run_sweep(args.sweep, max(args.steps, 3))
