@@ -44,7 +44,8 @@ class AdapterDesc(C.Structure):
 class MfBatch(C.Structure):
     _fields_ = [("n", C.c_int), ("clean", C.c_void_p), ("noise", C.c_void_p),
                 ("hidden", C.c_void_p), ("t", C.c_void_p), ("unconditional", C.c_void_p),
-                ("valid_tokens", C.c_void_p), ("pivot", C.c_void_p), ("edit_start", C.c_void_p)]
+                ("valid_tokens", C.c_void_p), ("pivot", C.c_void_p), ("edit_start", C.c_void_p),
+                ("stddev", C.c_void_p), ("sample_seed", C.c_uint64), ("window0", C.c_uint64)]
 
 
 class MgBatch(C.Structure):
@@ -112,6 +113,8 @@ SIGNATURES = {
     "act_wait_probe": (C.c_int, [C.c_void_p, C.c_int64]),
     "act_mg_staged": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t]),
     "act_q8_0_dequant": (C.c_int, [C.c_int, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]),
+    "act_set_deterministic": (C.c_int, [C.c_void_p, C.c_int]),
+    "act_mf_staged": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]),
     "act_lora_linear": (C.c_int, [C.c_int, C.c_void_p, C.c_int64, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
                                   C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_void_p, C.c_float, C.c_void_p]),
     "act_rank_gemm_f16": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
@@ -209,19 +212,21 @@ class Context:
 
     # ----------------------------------------------------------------- steps
     def _mf_batch(self, clean, noise, hidden, t, unconditional=None, valid_tokens=None, pivot=None,
-                  edit_start=None):
+                  edit_start=None, stddev=None, sample_seed=0, window0=0):
         f32 = lambda a: None if a is None else np.ascontiguousarray(a, np.float32)
         arrs = [f32(clean), f32(noise), f32(hidden), f32(t),
                 None if unconditional is None else np.ascontiguousarray(unconditional, np.int32),
                 None if valid_tokens is None else np.ascontiguousarray(valid_tokens, np.int32),
-                f32(pivot), f32(edit_start)]
+                f32(pivot), f32(edit_start), f32(stddev)]
         self._keep = arrs
-        return MfBatch(arrs[0].shape[0], *[_ptr(a) for a in arrs])
+        return MfBatch(arrs[0].shape[0], *[_ptr(a) for a in arrs], sample_seed, window0)
 
     def mf_step(self, clean, noise, hidden, t, unconditional=None, valid_tokens=None, pivot=None,
-                edit_start=None):
-        """One microbatch; with pivot/edit_start the edit-bridge objective (noise unused)."""
-        b = self._mf_batch(clean, noise, hidden, t, unconditional, valid_tokens, pivot, edit_start)
+                edit_start=None, stddev=None, sample_seed=0, window0=0):
+        """One microbatch; with pivot/edit_start the edit-bridge objective (noise unused); with stddev
+        the device draws clean = clean + stddev * z and the noise itself (noise unused)."""
+        b = self._mf_batch(clean, noise, hidden, t, unconditional, valid_tokens, pivot, edit_start, stddev,
+                           sample_seed, window0)
         loss = np.zeros(b.n, np.float32)
         self._check(self._L.act_mf_step(self.h, C.byref(b), loss.ctypes.data))
         return loss
@@ -230,6 +235,17 @@ class Context:
         b = self._mf_batch(clean, noise, hidden, t, unconditional, valid_tokens)
         self._check(self._L.act_mf_stage(self.h, C.byref(b)))
         return b.n
+
+    def set_deterministic(self, on: bool = True):
+        """act_set_deterministic: bit-for-bit reproducible steps (ordered dQ adds)."""
+        self._check(self._L.act_set_deterministic(self.h, int(on)))
+
+    def mf_staged(self, n, lat, T):
+        """The clean / noise windows the device holds for the last MelodyFlow batch."""
+        c = np.zeros((n, lat, T), np.float32)
+        z = np.zeros((n, lat, T), np.float32)
+        self._check(self._L.act_mf_staged(self.h, c.ctypes.data, z.ctypes.data, c.size))
+        return c, z
 
     def mg_step(self, codes, context):
         arrs = [np.ascontiguousarray(codes, np.int32), np.ascontiguousarray(context, np.float32)]

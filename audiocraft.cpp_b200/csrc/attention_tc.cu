@@ -725,6 +725,12 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
 #pragma unroll
                 for (int e = 0; e < 64; ++e) d[e] = 0.f;
             }
+            // ordered adds: this key block's turn comes after the earlier key blocks that add to
+            // this query block (key blocks 0 .. kb contribute, in that order); bounded wait
+            int* turn = a.dq_turn ? a.dq_turn + ((long)b * a.H + h) * nqb_all + (qb_first + u) : nullptr;
+            // (a wait that gives up has recorded its code: the step fails; the add still goes, so
+            // the later key blocks are not held up)
+            if (turn && leader) (void)flag_wait(turn, kb, err, 52);
             // one 32-column half at a time through the single staging tile
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
@@ -747,6 +753,12 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
                         : "memory");
                     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                 }
+            }
+            if (turn && leader) {
+                // this block's adds are performed before the next key block may add
+                asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+                asm volatile("fence.proxy.async.global;" ::: "memory");
+                red_release_add(turn, 1);
             }
         }
         if (leader) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // staging read

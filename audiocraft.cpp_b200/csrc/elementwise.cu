@@ -5,6 +5,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "philox.cuh"
 
 namespace act {
 
@@ -165,6 +166,40 @@ __global__ void mf_inputs_kernel(const float* __restrict__ clean, const float* _
     if (st >= 0.0f) nz = __fdiv_rn(__fsub_rn(nz, __fmul_rn(st, cl)), __fsub_rn(1.0f, st));
     x0[((long)b * T + p) * lat + c] = __float2half_rn(((1 - t) * nz + t * cl) * rescale);
     vstar[i] = cl - nz;
+}
+
+// On-device posterior sampling: clean = mean + stddev * z and noise = z' with z, z' ~ N(0,1) by
+// Box-Muller from one Philox4x32-10 call per two elements, keyed by `seed` and counted by
+// (element pair, window): the draw of an element depends only on the seed, its window number and
+// its index.  clean holds the mean and noise the stddev on entry (both [clips][lat * T]).
+__global__ void mf_sample_kernel(float* __restrict__ clean, float* __restrict__ noise, int clips, long per_clip,
+                                 uint64_t seed, uint64_t window0) {
+    const long pairs = (per_clip + 1) / 2;
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long)clips * pairs) return;
+    const int b = (int)(i / pairs);
+    const long p = i % pairs;
+    const uint64_t w = window0 + (uint64_t)b;
+    const Philox4 r = philox4x32_10((uint32_t)p, (uint32_t)w, (uint32_t)(w >> 32), 0x4D46u, (uint32_t)seed,
+                                    (uint32_t)(seed >> 32));
+    float z[4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const float rad = sqrtf(-2.0f * logf(philox_open01(r.v[2 * h])));
+        float sn, cs;
+        sincospif(2.0f * philox_01(r.v[2 * h + 1]), &sn, &cs);
+        z[2 * h] = rad * cs;
+        z[2 * h + 1] = rad * sn;
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const long e = 2 * p + h;
+        if (e >= per_clip) break;
+        const long at = (long)b * per_clip + e;
+        const float m = clean[at], sd = noise[at];
+        clean[at] = m + sd * z[2 * h];
+        noise[at] = z[2 * h + 1];
+    }
 }
 
 // MSE of the rescaled output against v* (flow target) and its seed gradient, multiplied by the
@@ -608,6 +643,11 @@ void gelu_fwd(f16* z, f16* gact, long n, int store_grad, cudaStream_t s) {
 
 void f32_to_f16(const float* x, f16* y, long n, cudaStream_t s) {
     f32_f16_kernel<<<blocks_for(n, 256), 256, 0, s>>>(x, y, n);
+}
+
+void mf_sample(float* clean, float* noise, int clips, long per_clip, uint64_t seed, uint64_t window0, cudaStream_t s) {
+    const long n = (long)clips * ((per_clip + 1) / 2);
+    mf_sample_kernel<<<blocks_for(n, 256), 256, 0, s>>>(clean, noise, clips, per_clip, seed, window0);
 }
 
 void mf_inputs(const float* clean, const float* noise, const float* t, const float* start, int clips, int T,

@@ -266,6 +266,8 @@ struct act_ctx {
     float *vstar = nullptr, *te1 = nullptr, *te = nullptr, *x0f = nullptr, *muo = nullptr, *rso = nullptr,
           *outp = nullptr;
     float *dx = nullptr, *dtmp = nullptr, *dq_acc = nullptr, *dvec = nullptr;
+    int* dq_turn = nullptr;  // self-attention backward: ordered dQ adds ([B][H][ceil(T/128)])
+    bool deterministic = false;  // act_set_deterministic: ordered dQ adds in the tcgen05 backward
     float* dkv_acc = nullptr;  // cross-attention dK | dV partials (fp32, [2][qsplit][clips * C][D])
     int cross_qsplit = 1;
     f16 *dxh = nullptr, *dz = nullptr, *dU = nullptr, *dob = nullptr, *dqkv = nullptr, *dcq = nullptr,
@@ -861,12 +863,14 @@ struct act_ctx {
         sa.rope = dit ? rope : nullptr; sa.rope_load = 0; sa.scale = ca.scale;
         sa.o = y.o1; sa.ldo = D; sa.lse = y.lse1;
         sa.dout = dob; sa.lddo = D; sa.dvec = dvec; sa.dq_acc = dq_acc; sa.ldq_acc = D;
+        sa.dq_turn = deterministic ? dq_turn : nullptr;
         sa.dk = dqkv + D; sa.dv = dqkv + 2 * D; sa.lddk = sa.lddv = 3 * D;
         sa.kscale = y.p[0].dora ? y.p[0].g + D : nullptr; sa.vscale = y.p[0].dora ? y.p[0].g + 2 * D : nullptr;
         const bool bwd_tc = use_tc && attn_bwd_tc_supported(sa);
         ++path_count[bwd_tc ? ACT_PATH_ATTN_BWD_TC : ACT_PATH_ATTN_BWD_MMA];
         timed(1, 2 * attn_flops(n, T, true), 0, [&] {
             CK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * D, stream));
+            if (bwd_tc && sa.dq_turn) CK(cudaMemsetAsync(dq_turn, 0, sizeof(int) * n * H * ((T + 127) / 128), stream));
             if (bwd_tc) attn_bwd_tc(sa, kerr, stream);
             else attn_bwd(sa, stream);
             attn_dq_finish(sa, dqkv, 3 * D, y.p[0].dora ? y.p[0].g : nullptr, stream);
@@ -1123,8 +1127,9 @@ struct act_ctx {
 
     void stage_mf(const act_mf_batch* b) {
         if (!mf) throw Error(ACT_ERR_INVALID, "not a MelodyFlow context");
-        const bool bridge = b && b->pivot;
-        if (!b || b->n <= 0 || b->n > B || !b->clean || !(bridge ? b->edit_start : b->noise) || !b->hidden || !b->t)
+        const bool bridge = b && b->pivot, sampled = b && b->stddev;
+        if (!b || b->n <= 0 || b->n > B || !b->clean || (bridge && !b->edit_start) || (!bridge && !sampled && !b->noise) ||
+            (bridge && sampled) || !b->hidden || !b->t)
             throw Error(ACT_ERR_INVALID, "invalid training sample");
         const int n = b->n, lat = md.latent_dim;
         const size_t nx = (size_t)n * lat * T;
@@ -1153,7 +1158,10 @@ struct act_ctx {
             }
         }
         // the bridge's pivot takes the noise buffer: the input kernel turns it into the endpoint
-        upload({{d_clean, h_clean, b->clean, nx * 4}, {d_noise, h_noise, bridge ? b->pivot : b->noise, nx * 4}});
+        // on-device sampling: mean and stddev go up in place of clean and noise, then are drawn from
+        upload({{d_clean, h_clean, b->clean, nx * 4},
+                {d_noise, h_noise, bridge ? b->pivot : sampled ? b->stddev : b->noise, nx * 4}});
+        if (sampled) mf_sample(d_clean, d_noise, n, (long)lat * T, b->sample_seed, b->window0, stream);
         upload_rows(d_hidden, h_hidden, b->hidden, n, Ctok, C, (size_t)md.cond_dim * 4);
         CK(cudaMemcpyAsync(d_t, h_t, n * 4, cudaMemcpyHostToDevice, stream));
         CK(cudaMemcpyAsync(d_start, h_start, n * 4, cudaMemcpyHostToDevice, stream));
@@ -1679,6 +1687,7 @@ struct act_ctx {
         dx = dalloc<float>(Mr * D);
         dtmp = dalloc<float>(Mr * D);
         dq_acc = dalloc<float>(Mr * D);
+        dq_turn = dalloc<int>((size_t)B * H * ((T + 127) / 128));
         dvec = dalloc<float>((long)B * H * T);
         dxh = dalloc<f16>(Mr * D);
         dz = dalloc<f16>(Mr * F);
@@ -2032,6 +2041,18 @@ int act_set_timeout(act_ctx* ctx, int64_t timeout_ms) {
     if (!ctx || timeout_ms < 0) return ACT_ERR_INVALID;
     ctx->timeout_ms = timeout_ms;
     return ACT_OK;
+}
+
+int act_set_deterministic(act_ctx* ctx, int enable) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] {
+        const bool on = enable != 0;
+        if (on == ctx->deterministic) return;
+        CK(cudaStreamSynchronize(ctx->stream));
+        for (auto& g : ctx->graphs) cudaGraphExecDestroy(g.second);  // captured with the other order
+        ctx->graphs.clear();
+        ctx->deterministic = on;
+    });
 }
 
 int act_set_grad_sync(act_ctx* ctx, int global_count) {
@@ -2470,6 +2491,19 @@ int act_mg_staged(act_ctx* ctx, int32_t* ids, size_t n_ids, int32_t* targets, si
             throw Error(ACT_ERR_INVALID, "staged buffer size mismatch");
         CK(cudaMemcpyAsync(ids, ctx->d_ids, n_ids * 4, cudaMemcpyDeviceToHost, ctx->stream));
         CK(cudaMemcpyAsync(targets, ctx->d_tgt, n_targets * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        CK(cudaStreamSynchronize(ctx->stream));
+    });
+}
+
+int act_mf_staged(act_ctx* ctx, float* clean, float* noise, size_t n_values) {
+    if (!ctx) return ACT_ERR_INVALID;
+    return guarded(ctx, [&] {
+        if (!ctx->mf) throw Error(ACT_ERR_INVALID, "not a MelodyFlow context");
+        if (ctx->staged_n <= 0) throw Error(ACT_ERR_STATE, "no staged batch");
+        const size_t nx = (size_t)ctx->staged_n * ctx->md.latent_dim * ctx->T;
+        if (n_values < nx) throw Error(ACT_ERR_INVALID, "buffers too small");
+        if (clean) CK(cudaMemcpyAsync(clean, ctx->d_clean, nx * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        if (noise) CK(cudaMemcpyAsync(noise, ctx->d_noise, nx * 4, cudaMemcpyDeviceToHost, ctx->stream));
         CK(cudaStreamSynchronize(ctx->stream));
     });
 }

@@ -154,6 +154,10 @@ struct AttnArgs {
     float* dvec = nullptr;        // [clips][H][T]  rowsum(dO * O)
     float* dq_acc = nullptr;      // [clips*T][ldq_acc] fp32, rotated frame, zeroed by caller
     long ldq_acc = 0;
+    // tcgen05 backward: per (clip, head, 128-query block) turn counters, zeroed by the caller
+    // ([clips][H][ceil(T/128)]); when given, the key blocks add their dQ tiles into dq_acc in
+    // key-block order (each waits for its predecessors' adds), so the sum is reproducible
+    int* dq_turn = nullptr;
     // mma.sync backward with a single key block (Tk <= 64, no RoPE): dQ is final inside one CTA,
     // so it is written straight as f16 (times the optional column factor dq_scale) to dq_h;
     // dq_acc is then not used and needs no zeroing
@@ -213,6 +217,9 @@ void gelu_check(const uint16_t* z, uint16_t* g, uint16_t* dg, long n, cudaStream
 // fp32 adapter gradient multiplies by 1 / gscale, which is exact.
 
 // MelodyFlow inputs: x0[m][c] = ((1-t)noise + t clean) * rescale(t), vstar = clean - noise.
+// On-device posterior draws: clean (holding the mean) += stddev (held in noise) * N(0,1), noise =
+// N(0,1), from Philox4x32-10 keyed by seed, counted by (element pair, window0 + clip)
+void mf_sample(float* clean, float* noise, int clips, long per_clip, uint64_t seed, uint64_t window0, cudaStream_t s);
 // start[b] >= 0: noise holds the edit-bridge pivot and becomes (pivot - start*clean) / (1 - start)
 void mf_inputs(const float* clean, const float* noise, const float* t, const float* start, int clips, int T,
                int lat, f16* x0, float* vstar, cudaStream_t s);

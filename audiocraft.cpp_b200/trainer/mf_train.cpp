@@ -148,24 +148,31 @@ void usage() {
                     "  --checkpoint-every N  save and evaluate every N steps (default 0)\n"
                     "  --device gpu|gpu:N  CUDA device (default gpu = device 0; this build has no CPU path)\n"
                     "  --max-batch N     samples per device microbatch (default min(accumulation, 8))\n"
+                    "  --device-sampling draw the posterior and noise on the GPU (Philox, per seed and window)\n"
                     "Exact resume via .state sidecars.\n");
 }
 
-// One drawn training / probe window, ready for the device.
+// One drawn training / probe window, ready for the device.  With on-device sampling, clean and
+// noise hold the window's posterior mean and stddev, and `window` numbers its device draws.
 struct Draw {
     std::vector<float> clean, noise;
     const Sample* sample;
     float t;
     bool uncond;
+    uint64_t window = 0;
 };
 
 // Device microbatches of drawn windows: submitted in draw order, losses returned in that order.
 class Batcher {
 public:
-    Batcher(act_ctx* ctx, const act_model_desc& m, int frames, int tokens, int max_batch, bool bridge)
-        : ctx_(ctx), m_(m), frames_(frames), tokens_(tokens), max_(max_batch), bridge_(bridge) {}
+    Batcher(act_ctx* ctx, const act_model_desc& m, int frames, int tokens, int max_batch, bool bridge,
+            bool device_sampling, uint64_t seed)
+        : ctx_(ctx), m_(m), frames_(frames), tokens_(tokens), max_(max_batch), bridge_(bridge),
+          device_(device_sampling), seed_(seed) {}
 
     void add(Draw d) {
+        // one device batch numbers its windows consecutively
+        if (device_ && !pending_.empty() && d.window != pending_.back().window + 1) flush();
         pending_.push_back(std::move(d));
         if ((int)pending_.size() == max_) flush();
     }
@@ -211,6 +218,12 @@ private:
         b.valid_tokens = valid.data();
         b.pivot = bridge_ ? pivot.data() : nullptr;
         b.edit_start = bridge_ ? start.data() : nullptr;
+        if (device_) {
+            b.noise = nullptr;
+            b.stddev = noise.data();
+            b.sample_seed = seed_;
+            b.window0 = pending_[0].window;
+        }
         std::vector<float> loss(n);
         actf::check(ctx_, act_mf_step(ctx_, &b, loss.data()), "training step");
         for (float l : loss) {
@@ -223,7 +236,8 @@ private:
     act_ctx* ctx_;
     act_model_desc m_;
     int frames_, tokens_, max_;
-    bool bridge_;
+    bool bridge_, device_;
+    uint64_t seed_;
     std::vector<Draw> pending_;
     std::vector<float> losses_;
 };
@@ -245,6 +259,7 @@ int main(int argc, char** argv) {
         std::string objective = "flow-matching";
         std::string adapter_type = "lora";
         float t_min = -1;
+        bool device_sampling = false;
         for (int i = 1; i < argc; ++i) {
             std::string a = argv[i];
             auto next = [&]() -> std::string {
@@ -276,6 +291,7 @@ int main(int argc, char** argv) {
             else if (a == "--eval-draws") eval_draws = std::stoi(next());
             else if (a == "--checkpoint-every") checkpoint_every = std::stoi(next());
             else if (a == "--max-batch") max_batch = std::stoi(next());
+            else if (a == "--device-sampling") device_sampling = true;
             else if (a == "--help" || a == "-h") {
                 usage();
                 fprintf(stderr, "%s", actf::TrainControls::help());
@@ -294,6 +310,8 @@ int main(int argc, char** argv) {
             throw std::runtime_error("invalid training settings");
         if (adapter_type != "lora" && adapter_type != "dora-rows")
             throw std::runtime_error("invalid training dimensions or adapter configuration");
+        if (device_sampling && objective == "edit-bridge")
+            throw std::runtime_error("--device-sampling draws a posterior; edit-bridge caches have fixed targets");
         if (std::filesystem::exists(out_path)) throw std::runtime_error("output already exists: " + out_path);
         const actf::MfTimeSampler time_sampler(t_sampling, t_mean, t_std);
         if (alpha == -1) alpha = (float)rank;
@@ -341,16 +359,19 @@ int main(int argc, char** argv) {
             if (t.name.rfind("dit.", 0) == 0)
                 actf::check(ctx, act_bind_weight(ctx, t.name.c_str(), (int)t.type, t.data, t.bytes), "act_bind_weight");
         actf::check(ctx, act_finalize(ctx), "act_finalize");
+        // exact resume and checkpoint invariance need bit-for-bit reproducible steps
+        actf::check(ctx, act_set_deterministic(ctx, 1), "act_set_deterministic");
         fprintf(stderr, "[train] adapter type: %s\n", adapter_type.c_str());
         const bool bridge = objective == "edit-bridge";
-        Batcher batcher(ctx, config, frames, max_tokens, max_batch, bridge);
+        Batcher batcher(ctx, config, frames, max_tokens, max_batch, bridge, device_sampling, seed);
 
         std::mt19937 rng(seed);
         std::uniform_real_distribution<float> uniform(0, 1);
         std::vector<size_t> order(samples.size());
         for (size_t i = 0; i < order.size(); ++i) order[i] = i;
         // compute_sample's draws (tools/mf-train.cpp:250-270)
-        auto draw_sample = [&](const Sample& s, std::mt19937& random, bool drop, float fixed_t, bool training) {
+        auto draw_sample = [&](const Sample& s, std::mt19937& random, bool drop, float fixed_t, bool training,
+                               uint64_t window) {
             std::normal_distribution<float> gaussian;
             const int crop = training && controls.random_crop
                                  ? std::uniform_int_distribution<int>(0, s.frames - frames)(random)
@@ -358,8 +379,14 @@ int main(int argc, char** argv) {
             Draw d;
             d.clean.resize((size_t)frames * config.latent_dim);
             d.noise.resize(d.clean.size());
+            d.window = window;
             for (size_t i = 0; i < d.clean.size(); ++i) {
                 const size_t at = (i / frames) * s.frames + crop + i % frames;
+                if (device_sampling) {  // the device draws clean = mean + stddev * z and the noise
+                    d.clean[i] = s.mean[at];
+                    d.noise[i] = s.stddev[at];
+                    continue;
+                }
                 d.clean[i] = s.mean[at] + s.stddev[at] * gaussian(random);
                 d.noise[i] = gaussian(random);
             }
@@ -376,9 +403,10 @@ int main(int argc, char** argv) {
             const auto& probes = validation.empty() ? samples : validation;
             const size_t count = eval_samples == 0 ? probes.size() : std::min<size_t>((size_t)eval_samples, probes.size());
             for (size_t i = 0; i < count; ++i)
-                for (int draw = 0; draw < eval_draws; ++draw)
+                for (int draw = 0; draw < eval_draws; ++draw)  // probe windows number from 2^63 up
                     batcher.add(draw_sample(probes[i], eval_rng, controls.eval_null,
-                                            eval_draws > 1 ? ((float)draw + 0.5f) / eval_draws : -1.0f, false));
+                                            eval_draws > 1 ? ((float)draw + 0.5f) / eval_draws : -1.0f, false,
+                                            (1ull << 63) + i * eval_draws + draw));
             for (float l : batcher.take()) loss += l;
             // probes leave no gradient behind
             actf::check(ctx, act_zero_grads(ctx), "act_zero_grads");
@@ -396,6 +424,7 @@ int main(int argc, char** argv) {
         std::string state_signature = controls.signature(lr) + actf::train_file_identity(dit_path) +
                                       actf::train_key(frames, rank, alpha, dropout, seed, objective, t_sampling, t_mean,
                                                       t_std, t_min, adapter_type, first_layer);
+        if (device_sampling) state_signature += "|device-sampling";
         for (const auto& dir : {cache_path, validation_path})
             if (!dir.empty())
                 for (const auto& p : actf::gguf_files(dir))
@@ -435,7 +464,7 @@ int main(int argc, char** argv) {
                 if (index == 0) std::shuffle(order.begin(), order.end(), rng);
                 const auto& sample = samples[order[index]];
                 const bool drop = uniform(rng) < dropout;
-                batcher.add(draw_sample(sample, rng, drop, -1.f, true));
+                batcher.add(draw_sample(sample, rng, drop, -1.f, true, seen));
                 ++seen;
             }
             double loss = 0;

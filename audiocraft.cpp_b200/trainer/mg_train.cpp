@@ -259,6 +259,8 @@ int main(int argc, char** argv) {
             if (t.name.rfind("lm.", 0) == 0)
                 actf::check(ctx, act_bind_weight(ctx, t.name.c_str(), (int)t.type, t.data, t.bytes), "act_bind_weight");
         actf::check(ctx, act_finalize(ctx), "act_finalize");
+        // exact resume and checkpoint invariance need bit-for-bit reproducible steps
+        actf::check(ctx, act_set_deterministic(ctx, 1), "act_set_deterministic");
         if (!evaluate_adapter.empty()) {
             // the adapter must adapt exactly this configuration (load_mg_lora, src/ac/lora.h:178-210)
             GgufReader adapter(evaluate_adapter);

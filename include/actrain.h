@@ -102,6 +102,15 @@ typedef struct {
      * start <= t <= 1 for every sample. */
     const float* pivot;           /* [n][latent_dim][frames] */
     const float* edit_start;      /* [n] */
+    /* On-device sampling (the reference draws these on the host, tools/mf-train.cpp:250-262):
+     * when stddev is given, `clean` holds the posterior mean and the device draws clean = mean +
+     * stddev * z and noise = z' (z, z' ~ N(0,1), Box-Muller from Philox4x32-10 keyed by
+     * sample_seed, counted by window number window0 + i and element), and `noise` is ignored.
+     * Reproducible per (seed, window, element), not the reference's host random stream.  Not
+     * with pivot. */
+    const float* stddev;          /* [n][latent_dim][frames] or NULL */
+    uint64_t sample_seed;
+    uint64_t window0;
 } act_mf_batch;
 
 /* One MusicGen microbatch (MgTrainGraph::compute, src/mg/train.h:178-227). */
@@ -158,6 +167,13 @@ int act_allreduce_grads(act_ctx* ctx, void* nccl_comm, int global_count);
  * act_allreduce_grads after the last microbatch of an accumulation; global_count becomes the
  * averaging count of the next act_optimizer.  0 cancels. */
 int act_set_grad_sync(act_ctx* ctx, int global_count);
+/* Bit-for-bit reproducible steps (1) or the default (0).  Every reduction of the step is
+ * order-independent except the self-attention backward's dQ, whose key blocks add their tiles
+ * into one fp32 accumulator as they finish; with 1 they add in key-block order (each waits for
+ * its predecessors, bounded), which makes the whole step a pure function of its inputs at the
+ * cost of about 1.5 ms per cfg-2 step (5%).  The trainer front ends turn it on: exact resume and
+ * checkpoints that leave training unchanged depend on it. */
+int act_set_deterministic(act_ctx* ctx, int enable);
 /* Bound, in milliseconds, on NCCL initialisation and on every host wait for the device while
  * a communicator is live (0 = none, the default).  A rank that stalls or dies makes the others'
  * next wait expire: their communicator is aborted (ncclCommAbort) and the call returns
@@ -269,6 +285,9 @@ int act_wait_probe(act_ctx* ctx, int64_t limit_ns);
  * of src/mg/pattern.h:64-76 without its last step) and the scored targets ([n][n_q][frames -
  * prefix_frames], src/mg/train.h:195-205) of the last act_mg_stage / act_mg_step. */
 int act_mg_staged(act_ctx* ctx, int32_t* ids, size_t n_ids, int32_t* targets, size_t n_targets);
+/* MelodyFlow: read back the clean / noise windows of the last act_mf_stage / act_mf_step as the
+ * device holds them ([n][latent_dim][frames] each; after on-device sampling, the drawn values). */
+int act_mf_staged(act_ctx* ctx, float* clean, float* noise, size_t n_values);
 /* Q8_0 blocks (34 bytes: fp16 d, int8 q[32]; tools/ac-quantize.cpp:161) dequantised on the
  * device by the kernels act_bind_weight uses: out_f32 = d * q in fp32, out_f16 = that value
  * rounded to nearest-even f16 (the GEMM operand).  Either output may be NULL. */

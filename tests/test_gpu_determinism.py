@@ -1,5 +1,5 @@
-"""The step is bit-for-bit reproducible: the same microbatch gives the same losses and gradients
-on every run.  The reference's CPU graph is deterministic and mf-train / mg-train rely on it
+"""With act_set_deterministic the step is bit-for-bit reproducible: the same microbatch gives the
+same losses and gradients on every run.  The reference's CPU graph is deterministic and mf-train / mg-train rely on it
 (exact resume from a .state file, checkpoints that leave the trained weights unchanged:
 src/ac/train_controls.h:122-196, tools/mf-train.cpp:300-346), so no reduction on the device may
 depend on the order in which CTAs finish.  The shapes make every split reduction run with several
@@ -21,9 +21,11 @@ def _twice(step, get):
     return out
 
 
-@pytest.mark.parametrize("dora", [False, True], ids=["lora", "dora"])
-def test_mf_step_is_reproducible(dora):
-    case = MfCase(dim=256, heads=4, ff=512, T=200, C=24, rank=8, alpha=16.0, dora=dora, batch=3, seed=31)
+@pytest.mark.parametrize("dora,T", [(False, 200), (True, 200), (False, 640)], ids=["lora", "dora", "lora-T640"])
+def test_mf_step_is_reproducible(dora, T):
+    # T = 640: five 128-key blocks add into every query block's dQ (the ordered adds)
+    case = MfCase(dim=256, heads=4, ff=512, T=T, C=24, rank=8, alpha=16.0, dora=dora, batch=3, seed=31)
+    case.ctx.set_deterministic(True)
     inp = case.inputs()
 
     def step():
@@ -37,7 +39,8 @@ def test_mf_step_is_reproducible(dora):
 
 
 def test_mg_step_is_reproducible():
-    case = MgCase(dim=256, heads=4, ff=512, frames=150, card=128, dora=True, batch=2, seed=32)
+    case = MgCase(dim=256, heads=4, ff=512, frames=600, card=128, dora=True, batch=2, seed=32)
+    case.ctx.set_deterministic(True)
     inp = case.inputs()
 
     def step():

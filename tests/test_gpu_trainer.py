@@ -189,3 +189,25 @@ def test_bridge_endpoint_on_the_device_matches_the_host_formula():
     with pytest.raises(A.ActError):  # t below the bridge start
         case.ctx.mf_step(clean, None, hidden, np.zeros(3, np.float32) + 0.1, unc, valid, pivot=pivot,
                          edit_start=np.full(3, 0.5, np.float32))
+
+
+def test_device_sampling_is_resumable_and_checkpoint_invariant(world):
+    """--device-sampling: the posterior and noise are drawn on the GPU per (seed, window), so a
+    resumed run and a checkpointed run still write what the uninterrupted one writes."""
+    root, _ = world
+    ds = common(root) + ["--device-sampling", "--accumulation-steps", 2, "--random-crop", "--frames", 40]
+    full = run(root, *ds, "--out", root / "ds.gguf", "--checkpoint-every", 2)
+    assert full.returncode == 0, full.stderr
+    resumed = run(root, *ds, "--out", root / "ds-resumed.gguf", "--resume", root / "ds.step-2.gguf.state")
+    assert resumed.returncode == 0, resumed.stderr
+    assert (root / "ds.gguf").read_bytes() == (root / "ds-resumed.gguf").read_bytes()
+    host = run(root, *[a for a in ds if a != "--device-sampling"], "--out", root / "ds-host.gguf")
+    assert host.returncode == 0, host.stderr
+    assert (root / "ds.gguf").read_bytes() != (root / "ds-host.gguf").read_bytes()
+    # the state records the sampling mode: a host-sampling resume of it is refused
+    mixed = run(root, *[a for a in ds if a != "--device-sampling"], "--out", root / "ds-mixed.gguf", "--resume",
+                root / "ds.step-2.gguf.state")
+    assert mixed.returncode != 0 and not (root / "ds-mixed.gguf").exists()
+    bridge = run(root, *common(root, "bridge_train", "bridge_validation"), "--objective", "edit-bridge",
+                 "--device-sampling", "--out", root / "ds-bridge.gguf")
+    assert bridge.returncode != 0 and not (root / "ds-bridge.gguf").exists()
