@@ -2,6 +2,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <stdexcept>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -255,18 +256,44 @@ __global__ void linear_f32_kernel(const float* __restrict__ x, const float* __re
 
 // ---------------------------------------------------------------------------------------
 // DoRA-rows, src/ac/lora.h:62-79 (and the hand-derived backward of that factorisation).
-// Column sums of a * b over the rows in DORA_COLSUM_PARTS row blocks: each block leaves its partial
-// in part[block][n]; the second kernel adds them in block order (no atomics, so the sum does not
-// depend on the order in which blocks finish).
-__global__ void dora_colsum_kernel(const f16* __restrict__ a, long lda, const f16* __restrict__ b,
-                                   long ldb, int rows, int N, float* __restrict__ part, int rows_per_block) {
-    const int n = blockIdx.x * blockDim.x + threadIdx.x;
-    if (n >= N) return;
+// Column sums of a * b over the rows in DORA_COLSUM_PARTS row blocks.  A block takes 256 columns
+// (8 per lane, 16-byte loads) and one row block, its 8 warps taking every 8th row; the warps'
+// sums meet in shared memory and are added in warp order, and the block leaves its partial in
+// part[row block][n]; the second kernel adds the row blocks in order (no atomics, so the sum does
+// not depend on the order in which blocks finish).
+__global__ void __launch_bounds__(256) dora_colsum_kernel(const f16* __restrict__ a, long lda,
+                                                          const f16* __restrict__ b, long ldb, int rows, int N,
+                                                          float* __restrict__ part, int rows_per_block) {
+    __shared__ float red[8][256];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c0 = blockIdx.x * 256 + lane * 8;
     const int r0 = blockIdx.y * rows_per_block, r1 = min(rows, r0 + rows_per_block);
-    float acc = 0.f;
-    for (int r = r0; r < r1; ++r)
-        acc += __half2float(a[(long)r * lda + n]) * __half2float(b[(long)r * ldb + n]);
-    part[(long)blockIdx.y * N + n] = acc;
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    if (c0 < N) {
+        for (int r = r0 + warp; r < r1; r += 8) {
+            const uint4 x = *reinterpret_cast<const uint4*>(a + (long)r * lda + c0);
+            const uint4 y = *reinterpret_cast<const uint4*>(b + (long)r * ldb + c0);
+            const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 u = unpack_f16(xs[e]), v = unpack_f16(ys[e]);
+                acc[2 * e] += u.x * v.x;
+                acc[2 * e + 1] += u.y * v.y;
+            }
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) red[warp][lane * 8 + e] = acc[e];
+    __syncthreads();
+    const int n = blockIdx.x * 256 + threadIdx.x;
+    if (n < N) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) v += red[w][threadIdx.x];
+        part[(long)blockIdx.y * N + n] = v;
+    }
 }
 
 __global__ void dora_colsum_add_kernel(const float* __restrict__ part, int parts, int N,
@@ -301,23 +328,31 @@ __global__ void gram_kernel(const float* __restrict__ A, int r, int in, const fl
     }
 }
 
+// One warp per output row: Q[o] = B[o] G, nsq = ||W_o||^2 + in*1e-12 + 2s<W_o,(BA)_o> + s^2 B[o]·Q[o]
+// (P[o] = (W A^T)[o] gives <W_o,(BA)_o> = P[o]·B[o]), g = m / sqrt(nsq); lanes take the rank
+// columns, then a fixed-order warp sum.
 __global__ void dora_rows_kernel(const float* __restrict__ B, const float* __restrict__ m,
                                  const float* __restrict__ P, const float* __restrict__ base,
                                  const float* __restrict__ G, int r, int RP, int out, float s,
                                  float* __restrict__ Q, float* __restrict__ nsq, float* __restrict__ g) {
-    const int o = blockIdx.x * blockDim.x + threadIdx.x;
+    const int o = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
     if (o >= out) return;
+    const float* b = B + (long)o * r;
     float t2 = 0.f, t3 = 0.f;
-    for (int j = 0; j < r; ++j) {
+    for (int j = lane; j < r; j += 32) {
         float qv = 0.f;
-        for (int k = 0; k < r; ++k) qv += B[(long)o * r + k] * G[k * r + j];
+        for (int k = 0; k < r; ++k) qv += b[k] * G[k * r + j];
         Q[(long)o * r + j] = qv;
-        t2 += P[(long)o * RP + j] * B[(long)o * r + j];
-        t3 += B[(long)o * r + j] * qv;
+        t2 += P[(long)o * RP + j] * b[j];
+        t3 += b[j] * qv;
     }
-    const float n = base[o] + 2.0f * s * t2 + s * s * t3;
-    nsq[o] = n;
-    g[o] = m[o] / sqrtf(n);
+    t2 = warp_sum(t2);
+    t3 = warp_sum(t3);
+    if (lane == 0) {
+        const float n = base[o] + 2.0f * s * t2 + s * s * t3;
+        nsq[o] = n;
+        g[o] = m[o] / sqrtf(n);
+    }
 }
 
 __global__ void dora_tail_kernel(const float* __restrict__ dg, const float* __restrict__ nsq,
@@ -668,6 +703,7 @@ void linear_f32(const float* x, const float* W, float* y, int rows, int N, int K
 
 void dora_colsum(const f16* a, long lda, const f16* b, long ldb, int rows, int N, const float* colscale,
                  float* dg, float* part, float inv_gscale, cudaStream_t s) {
+    if (N % 8 || lda % 8 || ldb % 8) throw std::runtime_error("dora_colsum: rows must be whole 16-byte pieces");
     const int rpb = (rows + DORA_COLSUM_PARTS - 1) / DORA_COLSUM_PARTS;
     const int parts = (rows + rpb - 1) / rpb;
     dim3 grid(blocks_for(N, 256), parts);
@@ -679,7 +715,7 @@ void dora_prepare(const float* A, const float* B, const float* m, const float* P
                   int in, int out, float s, float* G, float* Q, float* nsq, float* g, cudaStream_t st) {
     gram_kernel<<<r * r, 256, 0, st>>>(A, r, in, nullptr, nullptr, 0, G);
     const int RP = (r + 31) / 32 * 32;
-    dora_rows_kernel<<<blocks_for(out, 128), 128, 0, st>>>(B, m, P, base, G, r, RP, out, s, Q, nsq, g);
+    dora_rows_kernel<<<blocks_for(out, 8), 256, 0, st>>>(B, m, P, base, G, r, RP, out, s, Q, nsq, g);
 }
 
 void dora_finish(const float* dg, const float* nsq, const float* g, const float* m, const float* B,

@@ -665,11 +665,18 @@ struct act_ctx {
         for (auto& lay : layers)
             for (auto& p : lay.p) {
                 if (!p.dora) continue;
+                // P = W A^T [out][RP]: a rank-block product (the weight read once, f16 operands)
+                const f16* Wh = weight_h(p.W);
                 GemmArgs a;
                 a.M = p.out; a.N = p.RP; a.K1 = p.in;
-                a.A1 = weight_h(p.W); a.lda1 = p.in; a.B1 = p.A_h; a.ldb1 = p.in;
+                a.A1 = Wh; a.lda1 = p.in; a.B1 = p.A_h; a.ldb1 = p.in;
                 a.mode = EPI_STORE_F32; a.out = p.P; a.ldo = p.RP;
-                run_gemm(a, 2);
+                SkinnyArgs k;
+                k.M = p.out; k.K = p.in; k.nb = p.RP;
+                k.A = Wh; k.lda = p.in; k.B = p.A_h; k.ldb = p.in;
+                k.kind = SKINNY_ACC; k.alpha = 1.0f; k.out = p.P; k.ldo = p.RP;
+                if (use_tc && skinny_supported(k)) CK(cudaMemsetAsync(p.P, 0, sizeof(float) * p.out * p.RP, stream));
+                run_rank(k, a);
                 timed(2, 0, 0, [&] {
                     dora_prepare(value + p.offA, value + p.offB, value + p.offM, p.P, p.base, p.r, p.in, p.out, p.s,
                                  p.G, p.Q, p.nsq, p.g, stream);

@@ -232,7 +232,7 @@ void linear_f32(const float* x, const float* W, float* y, int rows, int N, int K
                 cudaStream_t s);
 // DoRA: dg[n] += inv_gscale * sum_m a[m][n] * b[m][n] / colscale[n]^2  (a already includes
 // colscale and the gradient scale; dg is the unscaled gradient)
-constexpr int DORA_COLSUM_PARTS = 8;  // row blocks of dora_colsum; part holds DORA_COLSUM_PARTS * N floats
+constexpr int DORA_COLSUM_PARTS = 16;  // row blocks of dora_colsum; part holds DORA_COLSUM_PARTS * N floats
 void dora_colsum(const f16* a, long lda, const f16* b, long ldb, int rows, int N, const float* colscale,
                  float* dg, float* part, float inv_gscale, cudaStream_t s);
 // DoRA per-step factors: G = A A^T, Q = B G, nsq = base + 2s<P,B> + s^2<B,Q>, g = m / sqrt(nsq)
