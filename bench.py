@@ -1,7 +1,7 @@
 """Benchmark of the adapter training step (BASELINE.json metric: DiT LoRA train steps/s on
 8 x 30 s clips).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload mf|mg]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload mf|mf-cfg1|mg]
 
 N > 1 is launched by torchrun (one process per GPU).  Per-GPU work is fixed (8 clips of 750
 frames per rank, weak scaling) and `value` is the whole-job rate in units of 8-clip steps:
@@ -27,6 +27,8 @@ sys.path.insert(0, os.path.join(ROOT, "audiocraft.cpp_b200"))
 # LoRA (alpha 32) on self.qkv, self.out, ff.0, ff.2.
 MF = dict(dim=1024, layers=24, heads=16, ff=4096, lat=128, cond=768, tdim=256, T=750, C=32, batch=8,
           rank=16, alpha=32.0, targets=0x63)
+# BASELINE cfg 1: the same model with an F16 base, one 250-frame clip and 16 tokens per step.
+MF1 = dict(MF, T=250, C=16, batch=1, weights="f16")
 # BASELINE cfg 4 (per GPU): MusicGen-medium d1536 x48, 24 heads, FFN 6144, 4 codebooks of 2048,
 # 1500 frames, 32 tokens, DoRA-rows rank 16 on all seven projections, 4 sequences per GPU.
 MG = dict(dim=1536, layers=48, heads=24, ff=6144, n_q=4, card=2048, frames=1500, C=32, batch=4,
@@ -154,6 +156,8 @@ def cpu_sample(c):
     (seconds, clips per step, description)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
+    if "frames" in c:
+        return cpu_sample_lm(c, O)
     L = c["layers"]
     key = (c["dim"], L, c["ff"], c["T"])
     if key not in _CPU_MODEL:  # weights and adapters once per process (1.6 GB of fp32 at cfg 2)
@@ -178,15 +182,57 @@ def cpu_sample(c):
     return dt, c["batch"], desc
 
 
+MG_SAMPLE_LAYERS = 12
+
+
+def cpu_sample_lm(c, O):
+    """The MusicGen step's bounded sample: one sequence (all frames, full width) through
+    MG_SAMPLE_LAYERS of the model's identical transformer layers, forward + backward, with the
+    embeddings, output norm and the four codebook heads.  The layers cost the same, so the full
+    step is clips x layers / MG_SAMPLE_LAYERS x this (which counts the embeddings and heads a few
+    times over: an overestimate of the CPU step of about 2%)."""
+    Ls = min(MG_SAMPLE_LAYERS, c["layers"])
+    key = ("lm", c["dim"], Ls, c["ff"], c["frames"])
+    if key not in _CPU_MODEL:
+        D = c["dim"]
+        cfg = O.LmCfg(D, Ls, c["heads"], D // c["heads"], c["ff"], c["n_q"], c["card"], c["card"], D // 2 - 1,
+                      10000.0, 1e-5)
+        rng = np.random.default_rng(0)
+        W = 0.02 * rng.standard_normal(sum(r * k for r, k in O.lm_tensor_shapes(cfg)), dtype=np.float32)
+        ad = O.Adapter(c["rank"], c["alpha"], 1, 0, c["targets"])
+        p = (0.02 * rng.standard_normal(O.lib().ora_adapter_numel(D, c["ff"], Ls, ad))).astype(np.float32)
+        args = (rng.integers(0, c["card"], (1, c["n_q"], c["frames"])).astype(np.int32),
+                rng.standard_normal((1, c["C"], D)).astype(np.float32))
+        _CPU_MODEL[key] = (cfg, W, ad, p, args)
+    cfg, W, ad, p, args = _CPU_MODEL[key]
+    t0 = time.perf_counter()
+    O.lm_step(cfg, W, ad, p, *args)
+    dt = time.perf_counter() - t0
+    scale = c["batch"] * c["layers"] / Ls
+    desc = (f"oracle C restatement (reference binary unbuildable: ggml absent), 1 sequence x {Ls} of "
+            f"{c['layers']} layers at d{c['dim']} {c['frames']} frames, DoRA rows, fwd+bwd; a step is "
+            f"{c['batch']} sequences x {c['layers']} layers, value scaled by sample_scale = {scale:g}")
+    return dt, scale, desc
+
+
 def line_header(args, c, n, world):
     """metric, unit and config shared by both arms (the driver compares their values)."""
-    mf = args.workload == "mf"
-    unit = "steps/s (8x30s-clip steps, summed over ranks)" if mf else "steps/s (4-seq steps, summed over ranks)"
-    metric = "DiT LoRA train steps/s (8x30s clips)" if mf else "MusicGen DoRA train steps/s (4x30s seqs per GPU)"
-    config = {"workload": ("mf-cfg2: DiT d1024 L24 H16 F4096 Q8_0 base, 8x750 frames/rank, 32 tokens, "
-                           "LoRA r16 a32 on qkv/out/ff.0/ff.2 (6,291,456 params), AdamW")
-              if mf else
-              "mg-cfg4: LM d1536 L48 H24 F6144 Q8_0 base, 4x1500 frames/rank, DoRA-rows r16 on 7 projections",
+    mf = args.workload.startswith("mf")
+    if args.workload == "mf-cfg1":
+        unit = "steps/s (1x10s-clip steps, summed over ranks)"
+        metric = "DiT LoRA train steps/s (1x10s clip, F16 base)"
+        work = ("mf-cfg1: DiT d1024 L24 H16 F4096 F16 base, 1x250 frames/rank, 16 tokens, "
+                "LoRA r16 a32 on qkv/out/ff.0/ff.2, AdamW")
+    elif mf:
+        unit = "steps/s (8x30s-clip steps, summed over ranks)"
+        metric = "DiT LoRA train steps/s (8x30s clips)"
+        work = ("mf-cfg2: DiT d1024 L24 H16 F4096 Q8_0 base, 8x750 frames/rank, 32 tokens, "
+                "LoRA r16 a32 on qkv/out/ff.0/ff.2 (6,291,456 params), AdamW")
+    else:
+        unit = "steps/s (4-seq steps, summed over ranks)"
+        metric = "MusicGen DoRA train steps/s (4x30s seqs per GPU)"
+        work = "mg-cfg4: LM d1536 L48 H24 F6144 Q8_0 base, 4x1500 frames/rank, DoRA-rows r16 on 7 projections"
+    config = {"workload": work,
               "global_batch": n * world, "seq_len": c.get("T", c.get("frames")),
               "layers": c["layers"], "clips_per_rank": n,
               "parallelism": f"dp{world}",
@@ -212,7 +258,7 @@ def run_reference(args, c):
     sample_s = float(np.mean(times))
     value = 1.0 / (sample_s * scale)
     metric, unit, config = line_header(args, c, c["batch"], max(args.gpus, 1))
-    config = dict(config, sample="1 clip per timed step (full depth), value scaled by sample_scale")
+    config = dict(config, sample=desc)
     line = {"metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": sample_s * 1e3, "sample_scale": scale,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -357,7 +403,7 @@ def run_sweep_record(A, reps, peak):
 
 def build_context(A, c, workload, device, seed=0):
     rng = np.random.default_rng(seed)
-    if workload == "mf":
+    if workload.startswith("mf"):
         md = A.mf_model(c["dim"], c["layers"], c["heads"], c["ff"], c["lat"], c["cond"], c["tdim"])
         ad = A.AdapterDesc(A.ADAPTER_LORA, c["rank"], c["alpha"], 0, c["targets"], 1234, c["batch"], c["T"], c["C"], 0)
         tensors = dit_tensors(c)
@@ -369,7 +415,9 @@ def build_context(A, c, workload, device, seed=0):
     ctx = A.Context(md, ad, device)
     for name, shape in tensors:
         w, kind = synth_weight(rng, name, shape)
-        if kind == "q8_0":
+        if kind == "q8_0" and c.get("weights") == "f16":
+            ctx.bind(name, w.astype(np.float16).view(np.uint16), A.TYPE_F16)
+        elif kind == "q8_0":
             ctx.bind(name, q8_0(w), A.TYPE_Q8_0)
         else:
             ctx.bind(name, w, A.TYPE_F32)
@@ -383,7 +431,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="mf", choices=["mf", "mg"])
+    ap.add_argument("--workload", default="mf", choices=["mf", "mf-cfg1", "mg"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override depth (profiling captures only)")
     ap.add_argument("--batch", type=int, default=0, help="override clips per rank (profiling captures only)")
@@ -391,7 +439,7 @@ def main():
     args = ap.parse_args()
     if args.sweep:
         return run_sweep(args.sweep, max(args.steps, 3))
-    c = dict(MF if args.workload == "mf" else MG)
+    c = dict({"mf": MF, "mf-cfg1": MF1, "mg": MG}[args.workload])
     if args.layers:
         c["layers"] = args.layers
     if args.batch:
@@ -421,7 +469,7 @@ def main():
 
     rng = np.random.default_rng(1000 + rank)
     n = c["batch"]
-    if args.workload == "mf":
+    if args.workload.startswith("mf"):
         batch = (rng.standard_normal((n, c["lat"], c["T"]), dtype=np.float32),
                  rng.standard_normal((n, c["lat"], c["T"]), dtype=np.float32),
                  rng.standard_normal((n, c["C"], c["cond"]), dtype=np.float32),
@@ -519,7 +567,9 @@ def main():
     traffic = None
     try:
         prof = json.load(open(os.path.join(ROOT, "profiles", "gemm_traffic.json")))
-        traffic = prof.get("bytes_per_launch")
+        # the capture covers one workload's shapes; another workload's launches move other bytes
+        if prof.get("bench_workload") == args.workload:
+            traffic = prof.get("bytes_per_launch")
     except (OSError, ValueError):
         pass
 
@@ -544,7 +594,7 @@ def main():
     }
     if clk:
         line["clocks"] = clk
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "mf":
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         dt, scale, desc = cpu_sample(c)
         line["cpu_baseline"] = {"value": 1.0 / (dt * scale), "unit": line_unit, "cores": os.cpu_count(),
                                 "kind": "port", "sample": desc, "sample_seconds": dt, "sample_scale": scale}

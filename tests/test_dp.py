@@ -69,7 +69,7 @@ def test_sample_sharded_gradients_equal_full_batch_accumulation():
     import oracle as O
     from fixtures import GOLDEN, load
     world, port = 2, _free_port()
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()  # no fork of a process that may hold a CUDA context
     out = mgr.dict()
     mp.spawn(_cpu_rank, args=(world, port, out), nprocs=world, join=True)
     z, c, ad = load(os.path.join(GOLDEN, "dit_small_dora.npz"))
@@ -137,7 +137,7 @@ def _gpu_rank(rank, world, port, out, mode, dora):
                          ids=["allreduce-after", "in-step-lora", "in-step-dora"])
 def test_nccl_allreduce_matches_single_device(mode, dora):
     world, port = 2, _free_port()
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()  # no fork of a process that may hold a CUDA context
     out = mgr.dict()
     mp.spawn(_gpu_rank, args=(world, port, out, mode, dora), nprocs=world, join=True)
     g0, v0, ref, g20 = out[0]
