@@ -23,7 +23,7 @@ TYPE_F32, TYPE_F16, TYPE_Q8_0 = 0, 1, 8
 TARGETS = ("self.qkv", "self.out", "cross.q", "cross.kv", "cross.out", "ff.0", "ff.2")
 # kernel families counted by act_path_counts (ACT_PATH_*)
 PATHS = ("attn_fwd_tc", "attn_fwd_mma", "attn_bwd_tc", "attn_bwd_mma", "gemm_tc", "gemm_mma", "rank_tc",
-         "rank_mma")
+         "rank_mma", "xattn_fwd_tc", "xattn_bwd_tc")
 
 
 class ModelDesc(C.Structure):

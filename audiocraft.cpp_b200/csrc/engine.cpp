@@ -759,8 +759,12 @@ struct act_ctx {
         ca.T = T; ca.Tk = C; ca.H = H; ca.clips = n; ca.nvalid = dit ? nvalid_dev : (C != Ctok ? d_mgvalid : nullptr);
         ca.zero_key = dit ? md.add_zero_attn : 0; ca.scale = sa.scale;
         ca.o = y.o2; ca.ldo = D; ca.lse = y.lse2;
-        ++path_count[ACT_PATH_ATTN_FWD_MMA];
-        timed(1, attn_flops(n, C, false), 0, [&] { attn_fwd(ca, stream); });
+        const bool xfwd_tc = use_tc && xattn_tc_supported(ca);
+        ++path_count[xfwd_tc ? ACT_PATH_XATTN_FWD_TC : ACT_PATH_ATTN_FWD_MMA];
+        timed(1, attn_flops(n, C, false), 0, [&] {
+            if (xfwd_tc) xattn_fwd_tc(ca, kerr, stream);
+            else attn_fwd(ca, stream);
+        });
         {
             GemmArgs e; e.mode = EPI_RESID_F32; e.out = y.xmid2; e.ldo = D; e.resid = y.xmid; e.ldr = D;
             if (y.p[4].dora) { e.aux = y.Yaux[4]; e.ldaux = D; }
@@ -846,8 +850,14 @@ struct act_ctx {
             ca.lddq_h = D;
             ca.dq_scale = y.p[2].dora ? y.p[2].g : nullptr;
         }
-        ++path_count[ACT_PATH_ATTN_BWD_MMA];
+        // at most 64 keys: the query-major tcgen05 backward (softmax recomputed, no dvec pass)
+        const bool xbwd_tc = use_tc && dq_direct && xattn_bwd_tc_supported(ca);
+        ++path_count[xbwd_tc ? ACT_PATH_XATTN_BWD_TC : ACT_PATH_ATTN_BWD_MMA];
         timed(1, 2 * attn_flops(n, C, false), 0, [&] {
+            if (xbwd_tc) {
+                xattn_bwd_tc(ca, kerr, stream);  // adds the dK / dV slices itself
+                return;
+            }
             if (!dq_direct) CK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * D, stream));
             attn_bwd(ca, stream);
             if (split && need_dkv) attn_dkv_finish(ca, stream);
@@ -2409,9 +2419,12 @@ int act_attention(int device, const void* q, const void* k, const void* v, const
         a.ldo = D;
         a.lse = static_cast<float*>(up(nullptr, rq * H * 4));
         int* derr = static_cast<int*>(up(nullptr, sizeof(int)));
-        const bool tc_fwd = attn_fwd_tc_supported(a) && !std::getenv("ACTRAIN_ATTN_MMA");
+        const bool mma_only = std::getenv("ACTRAIN_ATTN_MMA") != nullptr;
+        const bool x_tc = xattn_tc_supported(a) && !mma_only;  // at most 64 keys, as cross-attention runs
+        const bool tc_fwd = !x_tc && attn_fwd_tc_supported(a) && !mma_only;
         CK(cudaEventRecord(ev[0], st));
-        if (tc_fwd) attn_fwd_tc(a, derr, st);
+        if (x_tc) xattn_fwd_tc(a, derr, st);
+        else if (tc_fwd) attn_fwd_tc(a, derr, st);
         else attn_fwd(a, st);
         CK(cudaEventRecord(ev[1], st));
         CK(cudaGetLastError());
@@ -2427,8 +2440,17 @@ int act_attention(int device, const void* q, const void* k, const void* v, const
             a.dv = static_cast<f16*>(up(nullptr, rk * D * 2));
             a.lddk = a.lddv = D;
             ddq = static_cast<f16*>(up(nullptr, rq * D * 2));
+            if (x_tc) {  // dQ straight to f16, dK / dV through one fp32 slice per 128 queries
+                a.dq_h = ddq;
+                a.lddq_h = D;
+                a.qsplit = (T + 127) / 128;
+                a.dk_acc = static_cast<float*>(up(nullptr, (size_t)a.qsplit * rk * D * 4));
+                a.dv_acc = static_cast<float*>(up(nullptr, (size_t)a.qsplit * rk * D * 4));
+            }
             CK(cudaEventRecord(ev[2], st));
-            if (attn_bwd_tc_supported(a) && !std::getenv("ACTRAIN_ATTN_MMA")) {
+            if (x_tc) {
+                xattn_bwd_tc(a, derr, st);
+            } else if (attn_bwd_tc_supported(a) && !mma_only) {
                 attn_bwd_tc(a, derr, st);
             } else if (Tk <= 64) {  // few keys: query-split backward, as the training step runs it
                 a.qsplit = (T + 63) / 64;
@@ -2439,7 +2461,7 @@ int act_attention(int device, const void* q, const void* k, const void* v, const
             } else {
                 attn_bwd(a, st);
             }
-            attn_dq_finish(a, ddq, D, nullptr, st);
+            if (!x_tc) attn_dq_finish(a, ddq, D, nullptr, st);
             CK(cudaEventRecord(ev[3], st));
             CK(cudaGetLastError());
         }

@@ -1406,4 +1406,18 @@ void tc_make_map(CUtensorMap* map, const f16* ptr, long rows, long cols, long ld
     make_map(map, ptr, rows, cols, ld, box_cols, box_rows);
 }
 
+void tc_make_map3(CUtensorMap* map, const f16* ptr, long clips, long rows, long cols, long ld, int box_cols,
+                  int box_rows) {
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * 2) % 16)
+        throw std::runtime_error("tc_make_map3: operand not 16-byte aligned");
+    cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)clips};
+    cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)(rows * ld * 2)};
+    cuuint32_t box[3] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<f16*>(ptr), dims, strides, box,
+                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled (3-D) failed: " + std::to_string((int)r));
+}
+
 }  // namespace act

@@ -189,6 +189,14 @@ void attn_dkv_finish(const AttnArgs& a, cudaStream_t s);  // dk / dv (f16) from 
 // and adds into dq_acc (zeroed by the caller) like attn_bwd
 bool attn_bwd_tc_supported(const AttnArgs& a);
 void attn_bwd_tc(const AttnArgs& a, int* err, cudaStream_t s);
+// cross-attention over at most 64 keys per clip on tcgen05 (xattn_tc.cu): no RoPE, not causal,
+// query-major.  The forward writes o and lse; the backward recomputes the softmax (no lse / dvec),
+// writes dq_h (f16, times dq_scale) and, with dk_acc / dv_acc given, one fp32 dK / dV slice per
+// 128-query block (qsplit must equal ceil(T / 128)) added into dk / dv by attn_dkv_finish.
+bool xattn_tc_supported(const AttnArgs& a);
+bool xattn_bwd_tc_supported(const AttnArgs& a);
+void xattn_fwd_tc(const AttnArgs& a, int* err, cudaStream_t s);
+void xattn_bwd_tc(const AttnArgs& a, int* err, cudaStream_t s);
 // dq (f16) = unrotate(dq_acc) * qscale[col]
 void attn_dq_finish(const AttnArgs& a, f16* dq, long lddq, const float* qscale, cudaStream_t s);
 

@@ -180,5 +180,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
 // 2D f16 row-major tensor [rows][cols] with row stride ld (elements); box {box_cols, box_rows},
 // 128-byte swizzle.
 void tc_make_map(CUtensorMap* map, const f16* ptr, long rows, long cols, long ld, int box_cols, int box_rows);
+// 3-D f16 tensor [clips][rows][cols] (row stride ld elements, clip stride rows * ld): a box
+// {box_cols, box_rows, 1} never crosses into the next clip (rows past `rows` read as zero).
+void tc_make_map3(CUtensorMap* map, const f16* ptr, long clips, long rows, long cols, long ld, int box_cols,
+                  int box_rows);
 
 }  // namespace act

@@ -274,7 +274,9 @@ int act_attention_bwd_noalloc(const void* q, const void* k, const void* v, const
 #define ACT_PATH_GEMM_MMA 5      /* mma.sync GEMM (gemm_mma.cu) */
 #define ACT_PATH_RANK_TC 6       /* tcgen05 rank-block product (gemm_skinny.cu) */
 #define ACT_PATH_RANK_MMA 7      /* rank-block product on the mma.sync GEMM */
-#define ACT_PATH_COUNT 8
+#define ACT_PATH_XATTN_FWD_TC 8  /* tcgen05 cross-attention forward, <= 64 keys (xattn_tc.cu) */
+#define ACT_PATH_XATTN_BWD_TC 9  /* tcgen05 cross-attention backward, <= 64 keys */
+#define ACT_PATH_COUNT 10
 int act_path_counts(act_ctx* ctx, int64_t* counts, int n);
 /* Failure-path check of the device error word (no reference counterpart): one kernel runs the
  * tcgen05 kernels' bounded flag wait on a flag that nothing sets, gives up after limit_ns

@@ -77,6 +77,12 @@ CASES = {
     # pre-rotated inputs at the benchmark's clip length: the tcgen05 forward
     "self_zero_key_750": dict(clips=2, T=750, Tk=750, H=2, nvalid=None, causal=False, zero_key=True, rope=False),
     "causal_333": dict(clips=1, T=333, Tk=333, H=2, nvalid=None, causal=True, zero_key=False, rope=False),
+    # at most 64 keys: the query-major tcgen05 cross-attention (xattn_tc.cu), with a partial last
+    # query block, per-clip valid counts, with and without the zero key
+    "cross_750": dict(clips=2, T=750, Tk=32, H=3, nvalid=[32, 20], causal=False, zero_key=True, rope=False),
+    "cross_no_zero_key": dict(clips=3, T=200, Tk=40, H=2, nvalid=[40, 13, 1], causal=False, zero_key=False,
+                              rope=False),
+    "cross_64_keys": dict(clips=2, T=129, Tk=64, H=2, nvalid=None, causal=False, zero_key=True, rope=False),
 }
 
 
@@ -100,3 +106,28 @@ def test_attention_matches_reference(name):
             assert np.count_nonzero(got) == 0, key
             continue
         assert np.linalg.norm(got - ref) / scale < 1e-2, (key, np.linalg.norm(got - ref) / scale)
+
+
+@pytest.mark.parametrize("name", ["cross_masked", "cross_750", "cross_no_zero_key"])
+def test_cross_attention_tc_matches_mma_path(name, monkeypatch):
+    # the tcgen05 cross-attention against the mma.sync kernels on the same inputs (ACTRAIN_ATTN_MMA
+    # routes act_attention to the latter): both restate the same softmax, so they agree to f16
+    # rounding, and the log-sum-exp the forward leaves for other callers is the same
+    c = CASES[name]
+    rng = np.random.default_rng(7 + len(name))
+    D = c["H"] * 64
+    q = f16_bits(rng.standard_normal((c["clips"] * c["T"], D)))
+    k = f16_bits(rng.standard_normal((c["clips"] * c["Tk"], D)))
+    v = f16_bits(rng.standard_normal((c["clips"] * c["Tk"], D)))
+    do = f16_bits(rng.standard_normal((c["clips"] * c["T"], D)))
+    args = (q, k, v, do, c["clips"], c["T"], c["Tk"], c["H"], c["nvalid"], False, c["zero_key"], None)
+    tc = A.attention(*args)
+    monkeypatch.setenv("ACTRAIN_ATTN_MMA", "1")
+    mma = A.attention(*args)
+    for key in ("o", "dq", "dk", "dv"):
+        a, b = f32(tc[key]), f32(mma[key])
+        scale = np.linalg.norm(b)
+        assert (np.linalg.norm(a - b) / scale if scale else np.abs(a).max()) < 5e-3, key
+    fin = np.isfinite(mma["lse"])
+    np.testing.assert_array_equal(fin, np.isfinite(tc["lse"]))
+    np.testing.assert_allclose(tc["lse"][fin], mma["lse"][fin], rtol=0, atol=1e-4)

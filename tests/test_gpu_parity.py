@@ -251,6 +251,8 @@ CFG2 = dict(dim=1024, layers=2, heads=16, ff=4096, lat=128, cond=768, tdim=256, 
 def _assert_tc_attention(case, layers):
     pc = case.ctx.path_counts()
     assert pc["attn_fwd_tc"] == layers and pc["attn_bwd_tc"] == layers, pc
+    # cross-attention over the conditioning tokens (at most 64): the tcgen05 query-major kernels
+    assert pc["xattn_fwd_tc"] == layers and pc["xattn_bwd_tc"] == layers, pc
     # every block projection (seven per layer, forward) at least runs on the tcgen05 GEMM
     assert pc["gemm_tc"] >= 7 * layers, pc
 
