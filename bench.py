@@ -312,6 +312,21 @@ def run_sweep(kind, reps):
     elif kind == "record":
         run_sweep_record(A, reps, peak)
     else:
+        # cross-attention over the 32 conditioning tokens first (the tcgen05 query-major kernels of
+        # xattn_tc.cu), then self-attention
+        for H in (16, 24):
+            for T in (750, 1500):
+                clips = max(1, 6000 // T)
+                D = H * 64
+                q, do = bits((clips * T, D)), bits((clips * T, D))
+                k, v = bits((clips * 32, D)), bits((clips * 32, D))
+                A.attention(q, k, v, do, clips, T, 32, H, [32] * clips, False, True, None)  # warm
+                out = A.attention(q, k, v, do, clips, T, 32, H, [32] * clips, False, True, None)
+                byts_f, byts_b = 4.0 * clips * T * D, 6.0 * clips * T * D  # Q in + O out; Q, dO in + dQ out
+                print(json.dumps({"sweep": "cross_attention", "heads": H, "seq": T, "keys": 32, "clips": clips,
+                                  "ms_fwd": out["ms_fwd"], "ms_bwd": out["ms_bwd"],
+                                  "gbs_fwd": byts_f / (out["ms_fwd"] / 1e3) / 1e9,
+                                  "gbs_bwd": byts_b / (out["ms_bwd"] / 1e3) / 1e9}), flush=True)
         for H in (16, 24):
             for T in (750, 1500, 3000):
                 for causal in (False, True):
