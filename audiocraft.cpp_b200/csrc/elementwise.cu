@@ -704,7 +704,12 @@ void linear_f32(const float* x, const float* W, float* y, int rows, int N, int K
 void dora_colsum(const f16* a, long lda, const f16* b, long ldb, int rows, int N, const float* colscale,
                  float* dg, float* part, float inv_gscale, cudaStream_t s) {
     if (N % 8 || lda % 8 || ldb % 8) throw std::runtime_error("dora_colsum: rows must be whole 16-byte pieces");
-    const int rpb = (rows + DORA_COLSUM_PARTS - 1) / DORA_COLSUM_PARTS;
+    // about four blocks per SM in all (the loads of a block are few and serial), each block at
+    // least 64 rows: a fixed split for a given shape and device
+    const int col_blocks = blocks_for(N, 256);
+    const int want = std::max(1, (4 * current_sm_count() + col_blocks - 1) / col_blocks);
+    const int nparts = std::min(std::min(want, DORA_COLSUM_PARTS), std::max(1, rows / 64));
+    const int rpb = (rows + nparts - 1) / nparts;
     const int parts = (rows + rpb - 1) / rpb;
     dim3 grid(blocks_for(N, 256), parts);
     dora_colsum_kernel<<<grid, 256, 0, s>>>(a, lda, b, ldb, rows, N, part, rpb);

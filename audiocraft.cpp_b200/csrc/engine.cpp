@@ -378,13 +378,6 @@ struct act_ctx {
         if (seg == 1) { g.B1 = h; g.B1q = q; g.B1d = d; g.ldb1 = w.cols; g.ldd1 = w.rows; }
         else { g.B2 = h; g.B2q = q; g.B2d = d; g.ldb2 = w.cols; g.ldd2 = w.rows; }
     }
-    // f16 view of a whole weight: itself, or its expansion into this stream's scratch slot
-    const f16* weight_h(const Weight& w, int slot = 0) {
-        if (w.h) return w.h;
-        f16* out = wscratch[in_side ? 1 : 0][slot];
-        timed(2, 0, 0, [&] { q8_view_to_f16(w.q, w.cols, w.d, w.rows, w.rows, w.cols, out, w.cols, stream); });
-        return out;
-    }
     // A Q8_0 segment that the fused path cannot take: expand its view into scratch first
     void expand_q8(GemmArgs& g) {
         for (int seg = 1; seg <= 2; ++seg) {
@@ -410,7 +403,19 @@ struct act_ctx {
             g.sk_part = sk_part;
             g.sk_flag = sk_flag;
         }
-        if ((g.B1q || g.B2q) && !(use_tc && gemm_tc_supported(g))) expand_q8(g);
+        // A few rows (a rank block, the conditioning of a small batch) run on one whole tile of
+        // the tcgen05 kernel: its maps read the rows past them as zero and clip the rows written
+        if (use_tc && g.M <= 128 && g.arows == 0) {
+            GemmArgs t = g;
+            t.arows = g.M;
+            t.mvalid = std::min(g.mvalid, g.M);
+            t.M = (g.B1q || (g.K2 > 0 && g.B2q)) ? 256 : 128;
+            if (gemm_tc_supported(t)) g = t;
+        }
+        if ((g.B1q || g.B2q) && !(use_tc && gemm_tc_supported(g))) {
+            expand_q8(g);
+            g.a2_from_prev = false;  // the expansion now runs between A2's producer and the GEMM
+        }
         if (use_tc && gemm_tc_supported(g)) {
             ++path_count[ACT_PATH_GEMM_TC];
             timed(cls, fl, 0, [&] { gemm_tc_auto(g, kerr, stream); });
@@ -467,15 +472,10 @@ struct act_ctx {
         CK(cudaStreamWaitEvent(stream, ev_comm_join, 0));
         comm_pending = false;
     }
-    // after layer l's backward: its adapters' gradients are final (LoRA; DoRA's row-norm terms
-    // are added for every layer after the whole backward, so DoRA all-reduces once at the end)
-    void sync_layer(int l) {
-        if (ad.type == ACT_ADAPTER_LORA) sync_bucket(layer_params[l].first, layer_params[l].second);
-    }
-    void sync_rest() {
-        if (ad.type != ACT_ADAPTER_LORA) sync_bucket(0, nparam);
-        join_comm();
-    }
+    // after layer l's backward and its DoRA terms (finish_layer): its adapters' gradients are
+    // final.  Layers the backward does not reach keep zero gradients on every rank.
+    void sync_layer(int l) { sync_bucket(layer_params[l].first, layer_params[l].second); }
+    void sync_rest() { join_comm(); }
 
     // rank-block products: the tcgen05 skinny kernel, or the generic GEMM `fallback` when the
     // tcgen05 paths are disabled or the operands do not qualify
@@ -597,6 +597,7 @@ struct act_ctx {
         e.A1 = X; e.lda1 = p.in; set_b(e, 1, p.W, true);
         if (p.adapted) {
             e.K2 = p.RP; e.A2 = U; e.lda2 = p.RP; e.B2 = p.B_h; e.ldb2 = p.RP;
+            e.a2_from_prev = true;  // U was written by the launch just above
         }
         if (p.dora) e.colscale = p.g;
         run_gemm(e, 0);
@@ -654,29 +655,60 @@ struct act_ctx {
         e.A1 = dYl; e.lda1 = p.out; set_b(e, 1, p.W, false);
         if (p.adapted) {
             e.K2 = p.RP; e.A2 = dU; e.lda2 = p.RP; e.B2 = p.A_h; e.ldb2 = p.in;
+            e.a2_from_prev = true;  // dU: the last launch on this stream (dB / dA went to the side)
         }
         run_gemm(e, 0);
         join_side();
     }
 
     // ---------------------------------------------------------------- the step
+    // The large operand of a rank-block product that is a whole frozen weight W [out][in]
+    // (A(m, k) = W[m][k], or W[k][m] with mn): its f16 values, or its Q8_0 quants and scales,
+    // which the kernel dequantises on the way into the MMA
+    static void set_rank_weight(SkinnyArgs& k, const Weight& w, bool mn) {
+        k.a_mn = mn;
+        k.lda = w.cols;
+        if (w.q) { k.Aq = w.q; k.Ad = w.d; k.ldad = w.rows; }
+        else k.A = w.h;
+    }
+    // The same product on the generic GEMM (tcgen05 paths off, or operands the rank-block kernel
+    // does not take): the weight's f16 view, expanded into this stream's scratch if quantised
+    void run_rank_weight(const SkinnyArgs& k, const Weight& w, GemmArgs fallback, bool a_is_w) {
+        if (use_tc && skinny_supported(k)) {
+            ++path_count[ACT_PATH_RANK_TC];
+            timed(2, 2.0 * k.M * k.nb * (double)k.K, 0, [&] { skinny_gemm(k, kerr, stream); });
+            return;
+        }
+        const f16* Wh = w.h;
+        if (!Wh) {
+            f16* out = wscratch[in_side ? 1 : 0][0];
+            timed(2, 0, 0, [&] { q8_view_to_f16(w.q, w.cols, w.d, w.rows, w.rows, w.cols, out, w.cols, stream); });
+            Wh = out;
+        }
+        if (a_is_w) fallback.A1 = Wh;
+        else fallback.B1 = Wh;
+        ++path_count[ACT_PATH_RANK_MMA];
+        run_gemm(fallback, 2);
+    }
+
     void prepare_adapters() {
         timed(2, 0, 0, [&] { refresh_f16(jobs_dev, njobs, max_job, stream); });
         for (auto& lay : layers)
             for (auto& p : lay.p) {
                 if (!p.dora) continue;
-                // P = W A^T [out][RP]: a rank-block product (the weight read once, f16 operands)
-                const f16* Wh = weight_h(p.W);
-                GemmArgs a;
-                a.M = p.out; a.N = p.RP; a.K1 = p.in;
-                a.A1 = Wh; a.lda1 = p.in; a.B1 = p.A_h; a.ldb1 = p.in;
-                a.mode = EPI_STORE_F32; a.out = p.P; a.ldo = p.RP;
+                // P = W A^T [out][RP]: a rank-block product reading the frozen weight once (kept
+                // quantised: the kernel's converter warps dequantise it)
                 SkinnyArgs k;
                 k.M = p.out; k.K = p.in; k.nb = p.RP;
-                k.A = Wh; k.lda = p.in; k.B = p.A_h; k.ldb = p.in;
+                set_rank_weight(k, p.W, false);
+                k.B = p.A_h; k.ldb = p.in;
                 k.kind = SKINNY_ACC; k.alpha = 1.0f; k.out = p.P; k.ldo = p.RP;
+                GemmArgs a;
+                a.M = p.out; a.N = p.RP; a.K1 = p.in;
+                a.lda1 = p.in; a.B1 = p.A_h; a.ldb1 = p.in;
+                a.mode = EPI_STORE_F32; a.out = p.P; a.ldo = p.RP;
                 if (use_tc && skinny_supported(k)) CK(cudaMemsetAsync(p.P, 0, sizeof(float) * p.out * p.RP, stream));
-                run_rank(k, a);
+                run_rank_weight(k, p.W, a, true);
                 timed(2, 0, 0, [&] {
                     dora_prepare(value + p.offA, value + p.offB, value + p.offM, p.P, p.base, p.r, p.in, p.out, p.s,
                                  p.G, p.Q, p.nsq, p.g, stream);
@@ -685,28 +717,29 @@ struct act_ctx {
             }
     }
 
-    void finish_adapters() {
-        for (auto& lay : layers)
-            for (auto& p : lay.p) {
-                if (!p.dora) continue;
-                timed(2, 0, 0, [&] {
-                    dora_finish(p.dg, p.nsq, p.g, value + p.offM, value + p.offB, p.P, p.Q, value + p.offA, p.r,
-                                p.RP, p.in, p.out, p.s, grad + p.offM, grad + p.offB, grad + p.offA, p.BD, gscale,
-                                p.scr, stream);
-                });
-                GemmArgs a;  // gA += BD^T W
-                a.M = p.RP; a.N = p.in; a.K1 = p.out;
-                a.A1 = p.BD; a.lda1 = p.RP; a.a_kmajor = false;
-                const f16* Wh = weight_h(p.W);
-                a.B1 = Wh; a.ldb1 = p.in; a.b_kmajor = false;
-                a.mode = EPI_ATOMIC_F32; a.alpha = inv_gscale; a.out = grad + p.offA; a.ldo = p.in; a.mvalid = p.r;
-                a.splitk = splitk_for((p.in + 127) / 128, (p.out + 63) / 64);
-                SkinnyArgs k;  // the same as (W^T BD)^T over the out dimension
-                k.M = p.in; k.K = p.out; k.nb = p.r;
-                k.A = Wh; k.lda = p.in; k.a_mn = true; k.B = p.BD; k.ldb = p.RP; k.b_mn = true;
-                k.kind = SKINNY_ACC_T; k.alpha = inv_gscale; k.out = grad + p.offA; k.ldo = p.in;
-                run_rank(k, a);
-            }
+    // DoRA terms of layer l's adapter gradients, once its backward has been issued (its column
+    // sums dg are complete then: only its own projections add into them)
+    void finish_layer(int l) {
+        for (auto& p : layers[l].p) {
+            if (!p.dora) continue;
+            timed(2, 0, 0, [&] {
+                dora_finish(p.dg, p.nsq, p.g, value + p.offM, value + p.offB, p.P, p.Q, value + p.offA, p.r,
+                            p.RP, p.in, p.out, p.s, grad + p.offM, grad + p.offB, grad + p.offA, p.BD, gscale,
+                            p.scr, stream);
+            });
+            SkinnyArgs k;  // gA += BD^T W, as (W^T BD)^T over the out dimension
+            k.M = p.in; k.K = p.out; k.nb = p.r;
+            set_rank_weight(k, p.W, true);
+            k.B = p.BD; k.ldb = p.RP; k.b_mn = true;
+            k.kind = SKINNY_ACC_T; k.alpha = inv_gscale; k.out = grad + p.offA; k.ldo = p.in;
+            GemmArgs a;
+            a.M = p.RP; a.N = p.in; a.K1 = p.out;
+            a.A1 = p.BD; a.lda1 = p.RP; a.a_kmajor = false;
+            a.ldb1 = p.in; a.b_kmajor = false;
+            a.mode = EPI_ATOMIC_F32; a.alpha = inv_gscale; a.out = grad + p.offA; a.ldo = p.in; a.mvalid = p.r;
+            a.splitk = splitk_for((p.in + 127) / 128, (p.out + 63) / 64);
+            run_rank_weight(k, p.W, a, false);
+        }
     }
 
     // One transformer block forward.  te: per-clip timestep embedding (MelodyFlow) or null.
@@ -993,9 +1026,9 @@ struct act_ctx {
                 run_gemm(b, 0);
                 prepare_dxh(l - 1, n);
             }
+            finish_layer(l);
             sync_layer(l);
         }
-        finish_adapters();
         sync_rest();
     }
 
@@ -1043,9 +1076,9 @@ struct act_ctx {
         for (int l = L - 1; l >= first; --l) {
             if (l > first) block_bwd(l, n, nullptr, true, true, entry_extra(l - 1), entry_scale(l - 1));
             else block_bwd(l, n, nullptr, false);
+            finish_layer(l);
             sync_layer(l);
         }
-        finish_adapters();
         sync_rest();
     }
 

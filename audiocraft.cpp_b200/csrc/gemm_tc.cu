@@ -70,6 +70,9 @@ struct TcParams {
     int* sk_flag;
     // 2-CTA kernel, Q8_0 instantiation: bit i set when K segment i + 1 reads Q8_0 weights
     int q8mask;
+    // 2-CTA kernel: A2 is the previous kernel's output; only the producer waits for that kernel,
+    // right before its first A2 load (everything else the CTA reads is older)
+    int late_wait;
 };
 
 struct TcMaps {
@@ -605,77 +608,6 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
                  : "memory");
 }
 
-// Eight Q8_0 quants (biased: q + 128, one byte each) times their block scale -> eight f16.  The
-// biased quant goes into the mantissa of the f16 1024 + (q + 128) (byte permute), 1152 is
-// subtracted (exact), and one f16 multiply rounds q * d to nearest-even: the same single rounding
-// of the exact product that the bind-time dequantisation applies (fp32 d * q, exact, to f16).
-__device__ __forceinline__ uint4 q8x8_to_f16(uint2 u, uint32_t dd) {
-    const uint32_t w[4] = {__byte_perm(u.x, 0x64646464u, 0x5140), __byte_perm(u.x, 0x64646464u, 0x5342),
-                           __byte_perm(u.y, 0x64646464u, 0x5140), __byte_perm(u.y, 0x64646464u, 0x5342)};
-    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
-    const __half2 d2 = *reinterpret_cast<const __half2*>(&dd);
-    uint32_t o[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const __half2 v = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&w[i]), bias), d2);
-        o[i] = *reinterpret_cast<const uint32_t*>(&v);
-    }
-    return make_uint4(o[0], o[1], o[2], o[3]);
-}
-
-// One k-block of Q8_0 B for this CTA into its f16 operand slot, by NT converter threads (ct).
-// K-major (forward, B(n, k) = W[n][k]): raw quants [BH][64] bytes, scales [2][BH] (k / 32, n);
-// the operand is rows of 128 bytes with the 128-byte swizzle TMA would have applied.
-// MN-major (input gradient, B(n, k) = W[k][n]): raw quants [64][BH] bytes, scales [BH / 32][64]
-// (n / 32, k); the operand is BH / 64 boxes of [64 k][64 n] with the same swizzle.  Lanes read
-// consecutive 8-byte pieces of a row (conflict-free) and write whole swizzled 128-byte rows.
-template <int BH, bool B_MN, int NT>
-__device__ __forceinline__ void convert_q8_stage(const unsigned char* smem, uint32_t rq_off, uint32_t sb_off, int ct) {
-    const unsigned char* rq = smem + rq_off;
-    const uint16_t* sc = reinterpret_cast<const uint16_t*>(rq + BH * BKE);
-    unsigned char* sb = const_cast<unsigned char*>(smem) + sb_off;
-    // Every load of the k-block is issued before the first store: the compiler cannot tell the
-    // raw slot from the operand tile, so interleaved loads and stores would each wait for the
-    // shared-memory latency (long while the tensor core streams its operands).
-    if (!B_MN) {
-        constexpr int RPP = NT / 8;  // rows per pass: 8 chunks of 8 k per row
-        constexpr int IT = BH / RPP;
-        uint2 q[IT];
-        uint32_t d[IT];
-        const int c = ct & 7;
-#pragma unroll
-        for (int it = 0; it < IT; ++it) {
-            const int row = it * RPP + (ct >> 3);
-            q[it] = *reinterpret_cast<const uint2*>(rq + row * BKE + c * 8);
-            d[it] = sc[(c >> 2) * BH + row];
-        }
-#pragma unroll
-        for (int it = 0; it < IT; ++it) {
-            const int row = it * RPP + (ct >> 3);
-            *reinterpret_cast<uint4*>(sb + sw128(row, c)) = q8x8_to_f16(q[it], d[it] | (d[it] << 16));
-        }
-    } else {
-        constexpr int CPR = BH / 8;    // 8-wide chunks of n per k-row
-        constexpr int RPP = NT / CPR;  // k-rows per pass
-        constexpr int IT = BKE / RPP;
-        uint2 q[IT];
-        uint32_t d[IT];
-        const int c = ct % CPR;
-#pragma unroll
-        for (int it = 0; it < IT; ++it) {
-            const int k = it * RPP + ct / CPR;
-            q[it] = *reinterpret_cast<const uint2*>(rq + k * BH + c * 8);
-            d[it] = sc[(c >> 2) * BKE + k];
-        }
-#pragma unroll
-        for (int it = 0; it < IT; ++it) {
-            const int k = it * RPP + ct / CPR;
-            *reinterpret_cast<uint4*>(sb + (c >> 3) * 8192 + sw128(k, c & 7)) =
-                q8x8_to_f16(q[it], d[it] | (d[it] << 16));
-        }
-    }
-}
-
 // Work of one CTA pair.  Whole tiles (sk = 0): tiles pair, pair + npairs, ...  Stream-K
 // (sk = 1): the pair takes units [pair * U / npairs, (pair + 1) * U / npairs) of the U = tiles x
 // k-blocks units, tile-major.  The host enables stream-K only when there are at least as many
@@ -786,7 +718,11 @@ __global__ void __launch_bounds__(Tc2Cfg<BN2, Q8>::THREADS, 1)
     cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem_base = *tmem_slot;
-    pdl_wait();
+    // late_wait: the previous kernel writes only A2, and it started after everything older had
+    // completed (every kernel here waits before it triggers), so the CTA may stream A1 / B1 and
+    // read its epilogue inputs now; the producer waits for the previous kernel before its first
+    // A2 load, and every global write of the CTA follows that load through the MMA pipeline
+    if (!p.late_wait) pdl_wait();
     pdl_trigger();
 
     const int nk1 = (p.K1 + BKE - 1) / BKE, nk2 = (p.K2 + BKE - 1) / BKE, nk = nk1 + nk2;
@@ -833,11 +769,16 @@ __global__ void __launch_bounds__(Tc2Cfg<BN2, Q8>::THREADS, 1)
         };
         if (Q8)
             for (int i = 0; i < R - S; ++i) issue_raw();
+        bool waited = !p.late_wait;
         while (ok && w.next(tile, kb0, kb1, role)) {
             const int mb = tile % num_m2, nb = tile / num_m2;
             for (int kb = kb0; kb < kb1; ++kb) {
                 if (!mbar_wait(empty_bar(s), ph ^ 1, p.err, 11)) { ok = false; break; }
                 const bool seg2 = kb >= nk1;
+                if (seg2 && !waited) {
+                    pdl_wait();  // A2 is the previous kernel's output
+                    waited = true;
+                }
                 const CUtensorMap* ma = seg2 ? &maps.a2 : &maps.a1;
                 const CUtensorMap* mbm = seg2 ? &maps.b2 : &maps.b1;
                 const int k0 = (seg2 ? kb - nk1 : kb) * BKE;
@@ -1183,6 +1124,9 @@ void make_store_map(CUtensorMap* map, const void* ptr, bool f32, long rows, long
     if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled (store) failed: " + std::to_string((int)r));
 }
 
+// rows of A in memory: the maps end there and TMA reads the rows past them as zero
+long a_rows(const GemmArgs& a) { return a.arows > 0 && a.arows < a.M ? a.arows : a.M; }
+
 void make_epilogue_maps(TcMaps& maps, const GemmArgs& a) {
     const long rows = a.M < a.mvalid ? a.M : a.mvalid;
     const bool f32 = a.mode == EPI_STORE_F32 || a.mode == EPI_ACCUM_F32 || a.mode == EPI_RESID_F32;
@@ -1199,11 +1143,11 @@ void launch_tc(const GemmArgs& a, int* err, cudaStream_t s) {
     using Cfg = TcCfg<BN>;
     TcMaps maps;
     // A: [M][K] K-major; box 64 (k) x 128 (m)
-    make_map(&maps.a1, a.A1, a.M, a.K1, a.lda1, BKE, BM);
+    make_map(&maps.a1, a.A1, a_rows(a), a.K1, a.lda1, BKE, BM);
     if (B_MN) make_map(&maps.b1, a.B1, a.K1, a.N, a.ldb1, 64, BKE);   // [K][N]: box 64 (n) x 64 (k)
     else make_map(&maps.b1, a.B1, a.N, a.K1, a.ldb1, BKE, BN);        // [N][K]: box 64 (k) x BN (n)
     if (a.K2 > 0) {
-        make_map(&maps.a2, a.A2, a.M, a.K2, a.lda2, BKE, BM);
+        make_map(&maps.a2, a.A2, a_rows(a), a.K2, a.lda2, BKE, BM);
         if (B_MN) make_map(&maps.b2, a.B2, a.K2, a.N, a.ldb2, 64, BKE);
         else make_map(&maps.b2, a.B2, a.N, a.K2, a.ldb2, BKE, BN);
     } else {
@@ -1214,6 +1158,7 @@ void launch_tc(const GemmArgs& a, int* err, cudaStream_t s) {
     TcParams p;
     p.M = a.M; p.N = a.N; p.K1 = a.K1; p.K2 = a.K2;
     p.num_m = (a.M + BM - 1) / BM; p.num_n = a.N / BN;
+    p.q8mask = 0; p.late_wait = 0; p.sk_part = nullptr; p.sk_flag = nullptr;
     p.mode = a.mode; p.alpha = a.alpha; p.colscale = a.colscale; p.out = a.out; p.ldo = a.ldo;
     p.resid = a.resid; p.ldr = a.ldr; p.aux = a.aux; p.ldaux = a.ldaux; p.auxin = a.auxin; p.ldauxin = a.ldauxin;
     p.colscale2 = a.colscale2; p.bias = a.bias; p.nvalid = a.nvalid; p.mvalid = a.mvalid; p.err = err;
@@ -1255,10 +1200,10 @@ void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
     using Cfg = Tc2Cfg<BN2, Q8>;
     constexpr int BH2 = Cfg::BH;
     TcMaps maps;
-    make_map(&maps.a1, a.A1, a.M, a.K1, a.lda1, BKE, BM);
+    make_map(&maps.a1, a.A1, a_rows(a), a.K1, a.lda1, BKE, BM);
     make_b_maps(&maps.b1, &maps.s1, a.B1, a.B1q, a.B1d, a.ldb1, a.ldd1, a.K1, a.N, B_MN, BH2);
     if (a.K2 > 0) {
-        make_map(&maps.a2, a.A2, a.M, a.K2, a.lda2, BKE, BM);
+        make_map(&maps.a2, a.A2, a_rows(a), a.K2, a.lda2, BKE, BM);
         make_b_maps(&maps.b2, &maps.s2, a.B2, a.B2q, a.B2d, a.ldb2, a.ldd2, a.K2, a.N, B_MN, BH2);
     } else {
         maps.a2 = maps.a1;
@@ -1276,6 +1221,7 @@ void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
     p.out_h = (a.mode == EPI_STORE_F32 || a.mode == EPI_ACCUM_F32 || a.mode == EPI_RESID_F32) ? a.out_h : nullptr;
     p.sk_part = a.sk_part; p.sk_flag = a.sk_flag;
     p.q8mask = (a.B1q ? 1 : 0) | (a.K2 > 0 && a.B2q ? 2 : 0);
+    p.late_wait = a.a2_from_prev && a.K2 > 0 ? 1 : 0;
     auto whole = gemm_tc2_kernel<BN2, B_MN, false, Q8>;
     auto split = gemm_tc2_kernel<BN2, B_MN, BN2 == 256, Q8>;
     static DeviceOnce once;
@@ -1323,7 +1269,8 @@ bool gemm_tc_supported(const GemmArgs& a) {
     if (q8_args(a) && (a.M <= BM || (a.B1q && !q8_segment_ok(a.B1q, a.B1d, a.ldb1, a.ldd1, a.K1)) ||
                        (a.K2 > 0 && a.B2q && !q8_segment_ok(a.B2q, a.B2d, a.ldb2, a.ldd2, a.K2))))
         return false;
-    if (a.mode == EPI_ATOMIC_F32 || a.nvalid < a.N || a.mvalid < a.M) return false;
+    // rows past mvalid are clipped by the store maps and skipped by the epilogue's inputs
+    if (a.mode == EPI_ATOMIC_F32 || a.nvalid < a.N || a.mvalid <= 0) return false;
     if ((a.mode == EPI_GELU_BWD || a.mode == EPI_GELU_BWD_D) && a.aux)
         return false;  // its pre-activation input occupies the side tile
     if (a.ldo % 8 || (a.aux && a.ldaux % 8) || (a.auxin && a.ldauxin % 8) || (a.resid && a.ldr % 4)) return false;
@@ -1404,6 +1351,11 @@ void gemm_tc(const GemmArgs& a, int* err, cudaStream_t s) {
 
 void tc_make_map(CUtensorMap* map, const f16* ptr, long rows, long cols, long ld, int box_cols, int box_rows) {
     make_map(map, ptr, rows, cols, ld, box_cols, box_rows);
+}
+
+void tc_make_map_raw(CUtensorMap* map, const void* ptr, bool f16v, long rows, long cols, long ld, int box_cols,
+                     int box_rows) {
+    make_map_raw(map, ptr, f16v, rows, cols, ld, box_cols, box_rows);
 }
 
 void tc_make_map3(CUtensorMap* map, const f16* ptr, long clips, long rows, long cols, long ld, int box_cols,

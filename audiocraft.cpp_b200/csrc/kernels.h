@@ -85,6 +85,15 @@ struct GemmArgs {
     const uint8_t* B2q = nullptr;
     const f16* B2d = nullptr;
     long ldd2 = 0;
+    // tcgen05 paths: rows of A1 / A2 present in memory (0: M).  The tensor maps end there, so
+    // rows arows .. M-1 read as zero; with mvalid <= arows nothing past them is written.  Lets
+    // a product with a few rows (a rank block) run on a whole tile.
+    int arows = 0;
+    // 2-CTA kernel: A2 (the rank block) is written by the kernel launched immediately before
+    // this one on the same stream, and A1, B1, B2 and every epilogue input by kernels before
+    // that.  The GEMM then starts streaming its first K segment while its predecessor still
+    // runs, and waits for the predecessor's completion only before its first A2 load.
+    bool a2_from_prev = false;
 };
 long gemm_sk_part_floats(int num_sms);
 int gemm_sk_flag_count(int num_sms);
@@ -112,6 +121,12 @@ struct SkinnyArgs {
     void* out = nullptr;      // ACC: out[m * ldo + n]; ACC_T: out[n * ldo + m]; STORE: f16 out[m * ldo + n]
     long ldo = 0;
     int splits = 0;           // 0: about two CTAs per SM (STORE: a power of two <= 8)
+    // A as a Q8_0 weight in place of A (A stays null): Aq the quants biased to unsigned (q + 128),
+    // laid out as A would be (row stride lda bytes), Ad their f16 block scales, one row per 32
+    // quant columns ([cols / 32][rows], row stride ldad), dequantised on the way into the MMA
+    const uint8_t* Aq = nullptr;
+    const f16* Ad = nullptr;
+    long ldad = 0;
 };
 bool skinny_supported(const SkinnyArgs& a);
 void skinny_gemm(const SkinnyArgs& a, int* err, cudaStream_t s);
@@ -240,7 +255,10 @@ void linear_f32(const float* x, const float* W, float* y, int rows, int N, int K
                 cudaStream_t s);
 // DoRA: dg[n] += inv_gscale * sum_m a[m][n] * b[m][n] / colscale[n]^2  (a already includes
 // colscale and the gradient scale; dg is the unscaled gradient)
-constexpr int DORA_COLSUM_PARTS = 16;  // row blocks of dora_colsum; part holds DORA_COLSUM_PARTS * N floats
+// dora_colsum splits the rows into at most DORA_COLSUM_PARTS blocks (enough to fill the GPU for
+// the column count; fixed for a shape, so the ordered sum of the parts is reproducible); part
+// holds DORA_COLSUM_PARTS * N floats
+constexpr int DORA_COLSUM_PARTS = 64;
 void dora_colsum(const f16* a, long lda, const f16* b, long ldb, int rows, int N, const float* colscale,
                  float* dg, float* part, float inv_gscale, cudaStream_t s);
 // DoRA per-step factors: G = A A^T, Q = B G, nsq = base + 2s<P,B> + s^2<B,Q>, g = m / sqrt(nsq)

@@ -173,6 +173,87 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// ---------------------------------------------------------------------------------------
+// Q8_0 weights dequantised in shared memory on their way into an MMA operand (the 2-CTA GEMM's
+// B and the rank-block kernel's A): a raw slot holds one k-block of biased quants (q + 128) and
+// their f16 block scales as TMA brought them; converter threads write the f16 operand tile in
+// the 128-byte-swizzled layout a TMA load of the f16 values would have produced.
+constexpr int Q8_BK = 64;  // k per block of the operand ring
+
+// byte offset of 16-byte unit u of row r in a 128-byte-swizzled tile (1024-byte aligned)
+__device__ __forceinline__ uint32_t q8_sw128(int r, int u) { return r * 128 + ((u ^ (r & 7)) << 4); }
+
+// Eight Q8_0 quants (biased: q + 128, one byte each) times their block scale -> eight f16.  The
+// biased quant goes into the mantissa of the f16 1024 + (q + 128) (byte permute), 1152 is
+// subtracted (exact), and one f16 multiply rounds q * d to nearest-even: the same single rounding
+// of the exact product that the bind-time dequantisation applies (fp32 d * q, exact, to f16).
+__device__ __forceinline__ uint4 q8x8_to_f16(uint2 u, uint32_t dd) {
+    const uint32_t w[4] = {__byte_perm(u.x, 0x64646464u, 0x5140), __byte_perm(u.x, 0x64646464u, 0x5342),
+                           __byte_perm(u.y, 0x64646464u, 0x5140), __byte_perm(u.y, 0x64646464u, 0x5342)};
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+    const __half2 d2 = *reinterpret_cast<const __half2*>(&dd);
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half2 v = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&w[i]), bias), d2);
+        o[i] = *reinterpret_cast<const uint32_t*>(&v);
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// One k-block of Q8_0 B for this CTA into its f16 operand slot, by NT converter threads (ct).
+// K-major (forward, B(n, k) = W[n][k]): raw quants [BH][64] bytes, scales [2][BH] (k / 32, n);
+// the operand is rows of 128 bytes with the 128-byte swizzle TMA would have applied.
+// MN-major (input gradient, B(n, k) = W[k][n]): raw quants [64][BH] bytes, scales [BH / 32][64]
+// (n / 32, k); the operand is BH / 64 boxes of [64 k][64 n] with the same swizzle.  Lanes read
+// consecutive 8-byte pieces of a row (conflict-free) and write whole swizzled 128-byte rows.
+template <int BH, bool B_MN, int NT>
+__device__ __forceinline__ void convert_q8_stage(const unsigned char* smem, uint32_t rq_off, uint32_t sb_off, int ct) {
+    const unsigned char* rq = smem + rq_off;
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(rq + BH * Q8_BK);
+    unsigned char* sb = const_cast<unsigned char*>(smem) + sb_off;
+    // Every load of the k-block is issued before the first store: the compiler cannot tell the
+    // raw slot from the operand tile, so interleaved loads and stores would each wait for the
+    // shared-memory latency (long while the tensor core streams its operands).
+    if (!B_MN) {
+        constexpr int RPP = NT / 8;  // rows per pass: 8 chunks of 8 k per row
+        constexpr int IT = BH / RPP;
+        uint2 q[IT];
+        uint32_t d[IT];
+        const int c = ct & 7;
+#pragma unroll
+        for (int it = 0; it < IT; ++it) {
+            const int row = it * RPP + (ct >> 3);
+            q[it] = *reinterpret_cast<const uint2*>(rq + row * Q8_BK + c * 8);
+            d[it] = sc[(c >> 2) * BH + row];
+        }
+#pragma unroll
+        for (int it = 0; it < IT; ++it) {
+            const int row = it * RPP + (ct >> 3);
+            *reinterpret_cast<uint4*>(sb + q8_sw128(row, c)) = q8x8_to_f16(q[it], d[it] | (d[it] << 16));
+        }
+    } else {
+        constexpr int CPR = BH / 8;    // 8-wide chunks of n per k-row
+        constexpr int RPP = NT / CPR;  // k-rows per pass
+        constexpr int IT = Q8_BK / RPP;
+        uint2 q[IT];
+        uint32_t d[IT];
+        const int c = ct % CPR;
+#pragma unroll
+        for (int it = 0; it < IT; ++it) {
+            const int k = it * RPP + ct / CPR;
+            q[it] = *reinterpret_cast<const uint2*>(rq + k * BH + c * 8);
+            d[it] = sc[(c >> 2) * Q8_BK + k];
+        }
+#pragma unroll
+        for (int it = 0; it < IT; ++it) {
+            const int k = it * RPP + ct / CPR;
+            *reinterpret_cast<uint4*>(sb + (c >> 3) * 8192 + q8_sw128(k, c & 7)) =
+                q8x8_to_f16(q[it], d[it] | (d[it] << 16));
+        }
+    }
+}
+
 }  // namespace tc
 
 
@@ -180,6 +261,10 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
 // 2D f16 row-major tensor [rows][cols] with row stride ld (elements); box {box_cols, box_rows},
 // 128-byte swizzle.
 void tc_make_map(CUtensorMap* map, const f16* ptr, long rows, long cols, long ld, int box_cols, int box_rows);
+// Unswizzled map of raw bytes (f16v = 0: uint8 Q8_0 quants) or f16 values (f16v = 1: their block
+// scales), [rows][cols] with row stride ld elements, box {box_cols, box_rows}.
+void tc_make_map_raw(CUtensorMap* map, const void* ptr, bool f16v, long rows, long cols, long ld, int box_cols,
+                     int box_rows);
 // 3-D f16 tensor [clips][rows][cols] (row stride ld elements, clip stride rows * ld): a box
 // {box_cols, box_rows, 1} never crosses into the next clip (rows past `rows` read as zero).
 void tc_make_map3(CUtensorMap* map, const f16* ptr, long clips, long rows, long cols, long ld, int box_cols,
