@@ -301,90 +301,114 @@ __global__ void dora_colsum_add_kernel(const float* __restrict__ part, int parts
     const int n = blockIdx.x * blockDim.x + threadIdx.x;
     if (n >= N) return;
     float acc = 0.f;
-    for (int j = 0; j < parts; ++j) acc += part[(long)j * N + n];
+#pragma unroll 8
+    for (int j = 0; j < parts; ++j) acc += part[(long)j * N + n];  // loads issued ahead, added in order
     const float gg = g[n];
     dg[n] += acc * inv_gscale / (gg * gg);
 }
 
-__global__ void gram_kernel(const float* __restrict__ A, int r, int in, const float* __restrict__ wt,
-                            const float* __restrict__ B, int ldb, float* __restrict__ G) {
-    // G[j][k] = sum_i X[j][i] X[k][i] (A mode, wt == nullptr, X = A [r][in])
-    //        or sum_o wt[o] B[o][j] B[o][k]   (B mode: X^T diag(wt) X with X = B [in=out][r])
-    const int e = blockIdx.x;  // one entry per block
-    const int j = e / r, k = e % r;
-    float acc = 0.f;
-    if (!wt)
-        for (int i = threadIdx.x; i < in; i += blockDim.x) acc += A[(long)j * in + i] * A[(long)k * in + i];
-    else
-        for (int o = threadIdx.x; o < in; o += blockDim.x) acc += wt[o] * B[(long)o * ldb + j] * B[(long)o * ldb + k];
-    __shared__ float red[32];
+// The per-step factors and the backward tail are batched: one launch covers a list of
+// projections (blockIdx.y), so the whole model's factors, or one layer's tails, cost one launch
+// per stage instead of one per projection.  Blocks past a projection's own size exit.
+
+// sum of one value per thread over a block of 256 threads, in a fixed order; thread 0 has it
+__device__ __forceinline__ float block_sum256(float acc) {
+    __shared__ float red[8];
     acc = warp_sum(acc);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
     __syncthreads();
+    float v = 0.f;
     if (threadIdx.x < 32) {
-        float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+        v = threadIdx.x < 8 ? red[threadIdx.x] : 0.f;
         v = warp_sum(v);
-        if (threadIdx.x == 0) G[e] = v;
     }
+    return v;
+}
+
+// G = A A^T [r][r], one block per entry
+__global__ void __launch_bounds__(256) dora_gram_a_kernel(const DoraJob* __restrict__ jobs) {
+    const DoraJob J = jobs[blockIdx.y];
+    if ((int)blockIdx.x >= J.r * J.r) return;
+    const int j = blockIdx.x / J.r, k = blockIdx.x % J.r;
+    float acc = 0.f;
+    for (int i = threadIdx.x; i < J.in; i += 256) acc += J.A[(long)j * J.in + i] * J.A[(long)k * J.in + i];
+    acc = block_sum256(acc);
+    if (threadIdx.x == 0) J.G[blockIdx.x] = acc;
 }
 
 // One warp per output row: Q[o] = B[o] G, nsq = ||W_o||^2 + in*1e-12 + 2s<W_o,(BA)_o> + s^2 B[o]·Q[o]
 // (P[o] = (W A^T)[o] gives <W_o,(BA)_o> = P[o]·B[o]), g = m / sqrt(nsq); lanes take the rank
-// columns, then a fixed-order warp sum.
-__global__ void dora_rows_kernel(const float* __restrict__ B, const float* __restrict__ m,
-                                 const float* __restrict__ P, const float* __restrict__ base,
-                                 const float* __restrict__ G, int r, int RP, int out, float s,
-                                 float* __restrict__ Q, float* __restrict__ nsq, float* __restrict__ g) {
-    const int o = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
-    if (o >= out) return;
-    const float* b = B + (long)o * r;
+// columns, then a fixed-order warp sum.  The row's column-sum accumulator dg starts at zero.
+__global__ void __launch_bounds__(256) dora_rows_kernel(const DoraJob* __restrict__ jobs) {
+    const DoraJob J = jobs[blockIdx.y];
+    const int o = blockIdx.x * 8 + threadIdx.x / 32, lane = threadIdx.x & 31;
+    if (o >= J.out) return;
+    const int r = J.r;
+    const float* b = J.B + (long)o * r;
     float t2 = 0.f, t3 = 0.f;
     for (int j = lane; j < r; j += 32) {
         float qv = 0.f;
-        for (int k = 0; k < r; ++k) qv += b[k] * G[k * r + j];
-        Q[(long)o * r + j] = qv;
-        t2 += P[(long)o * RP + j] * b[j];
+        for (int k = 0; k < r; ++k) qv += b[k] * J.G[k * r + j];
+        J.Q[(long)o * r + j] = qv;
+        t2 += J.P[(long)o * J.RP + j] * b[j];
         t3 += b[j] * qv;
     }
     t2 = warp_sum(t2);
     t3 = warp_sum(t3);
     if (lane == 0) {
-        const float n = base[o] + 2.0f * s * t2 + s * s * t3;
-        nsq[o] = n;
-        g[o] = m[o] / sqrtf(n);
+        const float n = J.base[o] + 2.0f * J.s * t2 + J.s * J.s * t3;
+        J.nsq[o] = n;
+        J.g[o] = J.m[o] / sqrtf(n);
+        J.dg[o] = 0.f;
     }
 }
 
-__global__ void dora_tail_kernel(const float* __restrict__ dg, const float* __restrict__ nsq,
-                                 const float* __restrict__ g, const float* __restrict__ B,
-                                 const float* __restrict__ P, const float* __restrict__ Q, int r,
-                                 int RP, int out, float s, float* __restrict__ gm, float* __restrict__ gB,
-                                 f16* __restrict__ BD, float* __restrict__ dt3, float bd_scale) {
-    const int o = blockIdx.x * blockDim.x + threadIdx.x;
-    if (o >= out) return;
-    const float sq = sqrtf(nsq[o]);
-    gm[o] += dg[o] / sq;
-    const float dn = -0.5f * dg[o] * g[o] / nsq[o];
-    const float d2 = 2.0f * s * dn, d3 = s * s * dn;
-    dt3[o] = d3;
-    for (int j = 0; j < RP; ++j) {
-        if (j < r) {
-            gB[(long)o * r + j] += d2 * P[(long)o * RP + j] + 2.0f * d3 * Q[(long)o * r + j];
-            BD[(long)o * RP + j] = __float2half_rn(bd_scale * d2 * B[(long)o * r + j]);
+// One warp per output row: gm += dg / sqrt(nsq); dt2 = 2s dnsq, dt3 = s^2 dnsq (kept in scr);
+// gB[o] += dt2 P[o] + 2 dt3 Q[o] and BD[o] = f16(bd_scale dt2 B[o]) (zero past r), lanes along
+// the rank columns so every row's loads and stores are contiguous.
+__global__ void __launch_bounds__(256) dora_tail_kernel(const DoraJob* __restrict__ jobs, float bd_scale) {
+    const DoraJob J = jobs[blockIdx.y];
+    const int o = blockIdx.x * 8 + threadIdx.x / 32, lane = threadIdx.x & 31;
+    if (o >= J.out) return;
+    const float dg = J.dg[o], nsq = J.nsq[o];
+    const float sq = sqrtf(nsq);
+    const float dn = -0.5f * dg * J.g[o] / nsq;
+    const float d2 = 2.0f * J.s * dn, d3 = J.s * J.s * dn;
+    if (lane == 0) {
+        J.gm[o] += dg / sq;
+        J.scr[o] = d3;
+    }
+    for (int j = lane; j < J.RP; j += 32) {
+        if (j < J.r) {
+            J.gB[(long)o * J.r + j] += d2 * J.P[(long)o * J.RP + j] + 2.0f * d3 * J.Q[(long)o * J.r + j];
+            J.BD[(long)o * J.RP + j] = __float2half_rn(bd_scale * d2 * J.B[(long)o * J.r + j]);
         } else {
-            BD[(long)o * RP + j] = __float2half_rn(0.f);
+            J.BD[(long)o * J.RP + j] = __float2half_rn(0.f);
         }
     }
 }
 
-__global__ void dora_ga_kernel(const float* __restrict__ dG, const float* __restrict__ A, int r, int in,
-                               float* __restrict__ gA) {
-    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (e >= (long)r * in) return;
-    const int j = (int)(e / in), i = (int)(e % in);
+// dG = B^T diag(dt3) B [r][r] into scr + out, one block per entry
+__global__ void __launch_bounds__(256) dora_gram_b_kernel(const DoraJob* __restrict__ jobs) {
+    const DoraJob J = jobs[blockIdx.y];
+    if ((int)blockIdx.x >= J.r * J.r) return;
+    const int r = J.r, j = blockIdx.x / r, k = blockIdx.x % r;
     float acc = 0.f;
-    for (int k = 0; k < r; ++k) acc += dG[j * r + k] * A[(long)k * in + i];
-    gA[e] += 2.0f * acc;
+    for (int o = threadIdx.x; o < J.out; o += 256) acc += J.scr[o] * J.B[(long)o * r + j] * J.B[(long)o * r + k];
+    acc = block_sum256(acc);
+    if (threadIdx.x == 0) J.scr[J.out + blockIdx.x] = acc;
+}
+
+// gA [r][in] += 2 dG A
+__global__ void __launch_bounds__(256) dora_ga_kernel(const DoraJob* __restrict__ jobs) {
+    const DoraJob J = jobs[blockIdx.y];
+    const long e = (long)blockIdx.x * 256 + threadIdx.x;
+    if (e >= (long)J.r * J.in) return;
+    const int r = J.r, j = (int)(e / J.in), i = (int)(e % J.in);
+    const float* dG = J.scr + J.out;
+    float acc = 0.f;
+    for (int k = 0; k < r; ++k) acc += dG[j * r + k] * J.A[(long)k * J.in + i];
+    J.gA[e] += 2.0f * acc;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -716,23 +740,17 @@ void dora_colsum(const f16* a, long lda, const f16* b, long ldb, int rows, int N
     dora_colsum_add_kernel<<<blocks_for(N, 256), 256, 0, s>>>(part, parts, N, colscale, dg, inv_gscale);
 }
 
-void dora_prepare(const float* A, const float* B, const float* m, const float* P, const float* base, int r,
-                  int in, int out, float s, float* G, float* Q, float* nsq, float* g, cudaStream_t st) {
-    gram_kernel<<<r * r, 256, 0, st>>>(A, r, in, nullptr, nullptr, 0, G);
-    const int RP = (r + 31) / 32 * 32;
-    dora_rows_kernel<<<blocks_for(out, 8), 256, 0, st>>>(B, m, P, base, G, r, RP, out, s, Q, nsq, g);
+void dora_factors(const DoraJob* jobs, int n, int r, int max_out, cudaStream_t st) {
+    if (n <= 0) return;
+    dora_gram_a_kernel<<<dim3(r * r, n), 256, 0, st>>>(jobs);
+    dora_rows_kernel<<<dim3(blocks_for(max_out, 8), n), 256, 0, st>>>(jobs);
 }
 
-void dora_finish(const float* dg, const float* nsq, const float* g, const float* m, const float* B,
-                 const float* P, const float* Q, const float* A, int r, int RP, int in, int out, float s,
-                 float* gm, float* gB, float* gA, f16* BD, float bd_scale, float* scratch, cudaStream_t st) {
-    float* dt3 = scratch;           // [out]
-    float* dG = scratch + out;      // [r][r]
-    dora_tail_kernel<<<blocks_for(out, 128), 128, 0, st>>>(dg, nsq, g, B, P, Q, r, RP, out, s, gm, gB, BD, dt3,
-                                                           bd_scale);
-    gram_kernel<<<r * r, 256, 0, st>>>(nullptr, r, out, dt3, B, r, dG);
-    dora_ga_kernel<<<blocks_for((long)r * in, 256), 256, 0, st>>>(dG, A, r, in, gA);
-    (void)m;
+void dora_tail(const DoraJob* jobs, int n, int r, int max_out, int max_in, float bd_scale, cudaStream_t st) {
+    if (n <= 0) return;
+    dora_tail_kernel<<<dim3(blocks_for(max_out, 8), n), 256, 0, st>>>(jobs, bd_scale);
+    dora_gram_b_kernel<<<dim3(r * r, n), 256, 0, st>>>(jobs);
+    dora_ga_kernel<<<dim3(blocks_for((long)r * max_in, 256), n), 256, 0, st>>>(jobs);
 }
 
 void refresh_f16(const CopyJob* jobs_dev, int njobs, int max_elems, cudaStream_t s) {

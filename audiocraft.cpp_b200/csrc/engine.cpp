@@ -313,6 +313,14 @@ struct act_ctx {
     // shapes the fused GEMM does not take): two per stream, sized for the largest weight
     f16* wscratch[2][2] = {};
     long wscratch_elems = 0;
+    // DoRA projections in layer order (device table for the batched factor / tail kernels) and
+    // each layer's span of it
+    struct DoraSpan {
+        int first = 0, n = 0, max_out = 0, max_in = 0;
+    };
+    DoraJob* dora_jobs_dev = nullptr;
+    int dora_n = 0, dora_max_out = 0;
+    std::vector<DoraSpan> dora_layer;
 
     // ------------------------------------------------------------------------------------
     template <class Tp>
@@ -709,24 +717,22 @@ struct act_ctx {
                 a.mode = EPI_STORE_F32; a.out = p.P; a.ldo = p.RP;
                 if (use_tc && skinny_supported(k)) CK(cudaMemsetAsync(p.P, 0, sizeof(float) * p.out * p.RP, stream));
                 run_rank_weight(k, p.W, a, true);
-                timed(2, 0, 0, [&] {
-                    dora_prepare(value + p.offA, value + p.offB, value + p.offM, p.P, p.base, p.r, p.in, p.out, p.s,
-                                 p.G, p.Q, p.nsq, p.g, stream);
-                    CK(cudaMemsetAsync(p.dg, 0, sizeof(float) * p.out, stream));
-                });
             }
+        // the row factors of every DoRA projection in one pass per stage
+        if (dora_n)
+            timed(2, 0, 0, [&] { dora_factors(dora_jobs_dev, dora_n, ad.rank, dora_max_out, stream); });
     }
 
     // DoRA terms of layer l's adapter gradients, once its backward has been issued (its column
     // sums dg are complete then: only its own projections add into them)
     void finish_layer(int l) {
+        const DoraSpan& sp = dora_layer[l];
+        if (sp.n)
+            timed(2, 0, 0, [&] {
+                dora_tail(dora_jobs_dev + sp.first, sp.n, ad.rank, sp.max_out, sp.max_in, gscale, stream);
+            });
         for (auto& p : layers[l].p) {
             if (!p.dora) continue;
-            timed(2, 0, 0, [&] {
-                dora_finish(p.dg, p.nsq, p.g, value + p.offM, value + p.offB, p.P, p.Q, value + p.offA, p.r,
-                            p.RP, p.in, p.out, p.s, grad + p.offM, grad + p.offB, grad + p.offA, p.BD, gscale,
-                            p.scr, stream);
-            });
             SkinnyArgs k;  // gA += BD^T W, as (W^T BD)^T over the out dimension
             k.M = p.in; k.K = p.out; k.nb = p.r;
             set_rank_weight(k, p.W, true);
@@ -1645,6 +1651,33 @@ struct act_ctx {
                     p.BD = dalloc<f16>((size_t)p.out * RP);
                 }
             }
+        {
+            std::vector<DoraJob> dj;
+            dora_layer.assign(layers.size(), DoraSpan());
+            for (size_t l = 0; l < layers.size(); ++l) {
+                DoraSpan& sp = dora_layer[l];
+                sp.first = (int)dj.size();
+                for (auto& p : layers[l].p) {
+                    if (!p.dora) continue;
+                    DoraJob j;
+                    j.A = value + p.offA; j.B = value + p.offB; j.m = value + p.offM;
+                    j.P = p.P; j.base = p.base; j.G = p.G; j.Q = p.Q; j.nsq = p.nsq; j.g = p.g; j.dg = p.dg;
+                    j.scr = p.scr; j.gm = grad + p.offM; j.gB = grad + p.offB; j.gA = grad + p.offA; j.BD = p.BD;
+                    j.r = p.r; j.RP = p.RP; j.in = p.in; j.out = p.out; j.s = p.s;
+                    dj.push_back(j);
+                    sp.max_out = std::max(sp.max_out, p.out);
+                    sp.max_in = std::max(sp.max_in, p.in);
+                }
+                sp.n = (int)dj.size() - sp.first;
+                dora_max_out = std::max(dora_max_out, sp.max_out);
+            }
+            dora_n = (int)dj.size();
+            if (dora_n) {
+                dora_jobs_dev = dalloc<DoraJob>(dora_n);
+                CK(cudaMemcpyAsync(dora_jobs_dev, dj.data(), sizeof(DoraJob) * dora_n, cudaMemcpyHostToDevice, stream));
+                CK(cudaStreamSynchronize(stream));
+            }
+        }
         njobs = (int)jobs.size();
         jobs_dev = dalloc<CopyJob>(std::max(njobs, 1));
         if (njobs) CK(cudaMemcpyAsync(jobs_dev, jobs.data(), sizeof(CopyJob) * njobs, cudaMemcpyHostToDevice, stream));

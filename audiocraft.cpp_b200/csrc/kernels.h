@@ -261,16 +261,27 @@ void linear_f32(const float* x, const float* W, float* y, int rows, int N, int K
 constexpr int DORA_COLSUM_PARTS = 64;
 void dora_colsum(const f16* a, long lda, const f16* b, long ldb, int rows, int N, const float* colscale,
                  float* dg, float* part, float inv_gscale, cudaStream_t s);
-// DoRA per-step factors: G = A A^T, Q = B G, nsq = base + 2s<P,B> + s^2<B,Q>, g = m / sqrt(nsq)
-void dora_prepare(const float* A, const float* B, const float* m, const float* P, const float* base,
-                  int r, int in, int out, float s, float* G, float* Q, float* nsq, float* g,
-                  cudaStream_t st);
-// DoRA backward tail: gm += dg/sqrt(nsq); dt2 = 2s dnsq, dt3 = s^2 dnsq;
-// gB += dt2 P + 2 dt3 Q; BD = f16(bd_scale * dt2 * B) [out][RP] (the product gA += BD^T W that
-// consumes it multiplies by 1 / bd_scale); dG = B^T diag(dt3) B -> gA += 2 dG A
-void dora_finish(const float* dg, const float* nsq, const float* g, const float* m, const float* B,
-                 const float* P, const float* Q, const float* A, int r, int RP, int in, int out, float s,
-                 float* gm, float* gB, float* gA, f16* BD, float bd_scale, float* scratch, cudaStream_t st);
+// DoRA-rows of one projection, for the batched kernels below (src/ac/lora.h:62-79 and the
+// hand-derived backward of that factorisation)
+struct DoraJob {
+    const float *A, *B, *m;   // adapter values: lora_A [r][in], lora_B [out][r], magnitude [out]
+    const float* P;           // W A^T [out][RP]
+    const float* base;        // ||W_o||^2 + in * 1e-12
+    float *G, *Q, *nsq, *g;   // per-step factors: A A^T [r][r], B G [out][r], row norms^2, m / row norm
+    float* dg;                // d loss / d g [out], accumulated by dora_colsum
+    float* scr;               // [out + r * r]: dt3, then dG
+    float *gm, *gB, *gA;      // gradients of magnitude, lora_B, lora_A
+    f16* BD;                  // [out][RP]: f16(bd_scale * dt2 * B), the rank block of gA += BD^T W
+    int r, RP, in, out;
+    float s;
+};
+// Per-step factors of n projections (jobs in device memory): G = A A^T, Q = B G,
+// nsq = base + 2s<P,B> + s^2<B,Q>, g = m / sqrt(nsq); dg = 0.  P must be computed first.
+void dora_factors(const DoraJob* jobs, int n, int r, int max_out, cudaStream_t st);
+// Backward tail of n projections once their dg is complete: gm += dg/sqrt(nsq);
+// dt2 = 2s dnsq, dt3 = s^2 dnsq; gB += dt2 P + 2 dt3 Q; BD = f16(bd_scale * dt2 * B) (the product
+// gA += BD^T W that consumes it multiplies by 1 / bd_scale); dG = B^T diag(dt3) B; gA += 2 dG A
+void dora_tail(const DoraJob* jobs, int n, int r, int max_out, int max_in, float bd_scale, cudaStream_t st);
 
 // refresh f16 working copies: dst[row*ldd + col] = src[row*cols + col] for row<rows, col<cols
 struct CopyJob {
