@@ -407,6 +407,7 @@ struct act_ctx {
         GemmArgs g = g0;
         // stream-K only on the main stream and only while no side-stream work may run beside it:
         // its pairs wait on their neighbours, which must all be resident to finish early
+        // (measured: allowing it beside the rank products costs 0.55 ms per cfg-2 step)
         if (!in_side && use_sk && !side_pending) {
             g.sk_part = sk_part;
             g.sk_flag = sk_flag;

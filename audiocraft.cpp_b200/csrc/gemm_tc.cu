@@ -1234,7 +1234,11 @@ void launch_tc2(const GemmArgs& a, int* err, cudaStream_t s) {
     const int num_sms = current_sm_count();
     const int tiles = ((a.M + 2 * BM - 1) / (2 * BM)) * (a.N / BN2);
     const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
-    const auto kern = sk_pays(BN2, tiles, pairs, a) ? split : whole;
+    const bool use_split = sk_pays(BN2, tiles, pairs, a);
+    const auto kern = use_split ? split : whole;
+    // stream-K: a pair whose range holds only the head of a tile (no A2 k-blocks) would store
+    // outputs without having waited, so the early start is for whole tiles only
+    if (use_split) p.late_wait = 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
     cfg.blockDim = dim3(Cfg::THREADS, 1, 1);

@@ -92,7 +92,8 @@ struct GemmArgs {
     // 2-CTA kernel: A2 (the rank block) is written by the kernel launched immediately before
     // this one on the same stream, and A1, B1, B2 and every epilogue input by kernels before
     // that.  The GEMM then starts streaming its first K segment while its predecessor still
-    // runs, and waits for the predecessor's completion only before its first A2 load.
+    // runs, and waits for the predecessor's completion only before its first A2 load (whole-
+    // tile schedules; a stream-K launch waits at its start).
     bool a2_from_prev = false;
 };
 long gemm_sk_part_floats(int num_sms);
