@@ -119,6 +119,8 @@ SIGNATURES = {
                                   C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_void_p, C.c_float, C.c_void_p]),
     "act_rank_gemm_f16": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                      C.c_int, C.c_int, C.c_float, C.c_int, C.c_int, C.POINTER(C.c_float)]),
+    "act_rank_gemm_q8_0": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                      C.c_int, C.c_int, C.c_float, C.c_int, C.c_int, C.POINTER(C.c_float)]),
 }
 
 
@@ -435,6 +437,23 @@ def rank_gemm_f16(A_bits: np.ndarray, B_bits: np.ndarray, M: int, K: int, nb: in
         raise ActError(rc, lib().act_last_error(None).decode())
     return (C_, ms.value) if reps > 0 else C_
 
+
+
+def rank_gemm_q8_0(W_blocks: np.ndarray, B_bits: np.ndarray, M: int, K: int, nb: int, a_mn: bool, b_mn: bool,
+                   kind: int, alpha: float = 1.0, C_init: np.ndarray | None = None, splits: int = 0, device: int = 0,
+                   reps: int = 0):
+    """act_rank_gemm_q8_0: rank_gemm_f16 with A read from a weight given as its Q8_0 blocks
+    ([M][K] when a_mn is False, [K][M] when True), kept quantised on the device."""
+    shape = (nb, M) if kind == RANK_ACC_T else (M, nb)
+    C_ = np.zeros(shape, np.float32) if C_init is None else np.ascontiguousarray(C_init, np.float32).copy()
+    w = np.ascontiguousarray(W_blocks, np.uint8)
+    b = np.ascontiguousarray(B_bits, np.uint16)
+    ms = C.c_float(0.0)
+    rc = lib().act_rank_gemm_q8_0(device, kind, w.ctypes.data, b.ctypes.data, C_.ctypes.data, M, K, nb, int(a_mn),
+                                   int(b_mn), float(alpha), splits, reps, C.byref(ms))
+    if rc != ACT_OK:
+        raise ActError(rc, lib().act_last_error(None).decode())
+    return (C_, ms.value) if reps > 0 else C_
 
 def attention(q, k, v, dout, clips, T, Tk, H, nvalid=None, causal=False, zero_key=False, rope=None, device=0):
     """Kernel-level attention: f16 bit-pattern inputs (uint16) -> dict of outputs and device times."""

@@ -2229,32 +2229,54 @@ int act_gelu_f16(int device, const uint16_t* z, uint16_t* g, uint16_t* dg, int64
     }
 }
 
-int act_rank_gemm_f16(int device, int kind, const void* A, const void* B, float* C, int M, int K, int nb, int a_mn,
-                       int b_mn, float alpha, int splits, int reps, float* ms_per_call) {
-    void *dA = nullptr, *dB = nullptr, *dC = nullptr;
+// The rank-block kernel on host buffers: A as f16 bits, or (Aq8 non-null) as the Q8_0 blocks of
+// the weight it is read from ([M][K] when a_mn is 0, [K][M] when 1), kept quantised on the device.
+static int rank_gemm_host(int device, int kind, const void* A, const void* Aq8, const void* B, float* C, int M, int K,
+                          int nb, int a_mn, int b_mn, float alpha, int splits, int reps, float* ms_per_call) {
+    void *dA = nullptr, *dB = nullptr, *dC = nullptr, *dQ = nullptr, *dD = nullptr;
     int* derr = nullptr;
     cudaStream_t st = nullptr;
     auto cleanup = [&] {
         if (st) cudaStreamSynchronize(st);
-        cudaFree(dA); cudaFree(dB); cudaFree(dC); cudaFree(derr);
+        cudaFree(dA); cudaFree(dB); cudaFree(dC); cudaFree(derr); cudaFree(dQ); cudaFree(dD);
         if (st) cudaStreamDestroy(st);
     };
     try {
-        if (!A || !B || !C || M <= 0 || K <= 0 || nb <= 0 || kind < 0 || kind > 2)
+        if ((!A && !Aq8) || !B || !C || M <= 0 || K <= 0 || nb <= 0 || kind < 0 || kind > 2)
             throw Error(ACT_ERR_INVALID, "invalid rank-GEMM arguments");
+        const int wrows = a_mn ? K : M, wcols = a_mn ? M : K;  // the stored matrix A is read from
+        if (Aq8 && wcols % 32) throw Error(ACT_ERR_INVALID, "Q8_0 rows must be whole 32-blocks");
         CK(cudaSetDevice(device));
         CK(cudaStreamCreate(&st));
         const size_t cn = (size_t)M * nb;
-        CK(cudaMalloc(&dA, (size_t)M * K * 2));
+        if (Aq8) {
+            const size_t nblk = (size_t)wrows * wcols / 32;
+            CK(cudaMalloc(&dA, nblk * 34));
+            CK(cudaMalloc(&dQ, (size_t)wrows * wcols));
+            CK(cudaMalloc(&dD, nblk * 2));
+        } else {
+            CK(cudaMalloc(&dA, (size_t)M * K * 2));
+        }
         CK(cudaMalloc(&dB, (size_t)nb * K * 2));
         CK(cudaMalloc(&dC, cn * 4));
         CK(cudaMalloc(&derr, sizeof(int)));
         CK(cudaMemsetAsync(derr, 0, sizeof(int), st));
-        CK(cudaMemcpyAsync(dA, A, (size_t)M * K * 2, cudaMemcpyHostToDevice, st));
+        if (Aq8) {
+            CK(cudaMemcpyAsync(dA, Aq8, (size_t)wrows * wcols / 32 * 34, cudaMemcpyHostToDevice, st));
+            q8_0_split(static_cast<const uint8_t*>(dA), wrows, wcols, static_cast<uint8_t*>(dQ),
+                       static_cast<f16*>(dD), st);
+        } else {
+            CK(cudaMemcpyAsync(dA, A, (size_t)M * K * 2, cudaMemcpyHostToDevice, st));
+        }
         CK(cudaMemcpyAsync(dB, B, (size_t)nb * K * 2, cudaMemcpyHostToDevice, st));
         SkinnyArgs g;
         g.M = M; g.K = K; g.nb = nb;
-        g.A = static_cast<const f16*>(dA); g.lda = a_mn ? M : K; g.a_mn = a_mn != 0;
+        g.lda = a_mn ? M : K; g.a_mn = a_mn != 0;
+        if (Aq8) {
+            g.Aq = static_cast<const uint8_t*>(dQ); g.Ad = static_cast<const f16*>(dD); g.ldad = wrows;
+        } else {
+            g.A = static_cast<const f16*>(dA);
+        }
         g.B = static_cast<const f16*>(dB); g.ldb = b_mn ? nb : K; g.b_mn = b_mn != 0;
         g.kind = kind; g.alpha = alpha; g.out = dC; g.ldo = kind == SKINNY_ACC_T ? M : nb;
         g.splits = splits;
@@ -2313,6 +2335,17 @@ int act_rank_gemm_f16(int device, int kind, const void* A, const void* B, float*
         cleanup();
         return ACT_ERR_CUDA;
     }
+}
+
+int act_rank_gemm_f16(int device, int kind, const void* A, const void* B, float* C, int M, int K, int nb, int a_mn,
+                      int b_mn, float alpha, int splits, int reps, float* ms_per_call) {
+    return rank_gemm_host(device, kind, A, nullptr, B, C, M, K, nb, a_mn, b_mn, alpha, splits, reps, ms_per_call);
+}
+
+int act_rank_gemm_q8_0(int device, int kind, const void* Aq8, const void* B, float* C, int M, int K, int nb, int a_mn,
+                       int b_mn, float alpha, int splits, int reps, float* ms_per_call) {
+    if (!Aq8) return ACT_ERR_INVALID;
+    return rank_gemm_host(device, kind, nullptr, Aq8, B, C, M, K, nb, a_mn, b_mn, alpha, splits, reps, ms_per_call);
 }
 
 namespace {

@@ -230,6 +230,13 @@ int act_gemm_q8_0(int device, const void* A, const void* Bq8, void* C, int M, in
 int act_gelu_f16(int device, const uint16_t* z, uint16_t* g, uint16_t* dg, int64_t n, int direct);
 int act_rank_gemm_f16(int device, int kind, const void* A, const void* B, float* C, int M, int K, int nb, int a_mn,
                       int b_mn, float alpha, int splits, int reps, float* ms_per_call);
+/* The same product with A read from a frozen weight given as its Q8_0 blocks (34 bytes each,
+ * tools/ac-quantize.cpp:161): the weight is [M][K] (a_mn 0) or [K][M] (1) and stays quantised on
+ * the device; the kernel's converter warps dequantise each k-block on its way into the MMA (the
+ * DoRA products P = W A^T and BD^T W of the training step, src/ac/lora.h:62-79).  With the same
+ * splits, C equals act_rank_gemm_f16 on the act_q8_0_dequant f16 values bit for bit. */
+int act_rank_gemm_q8_0(int device, int kind, const void* Aq8, const void* B, float* C, int M, int K, int nb, int a_mn,
+                       int b_mn, float alpha, int splits, int reps, float* ms_per_call);
 /* stand-alone attention forward + backward on host buffers (tests and the kernel sweep):
  * token-major f16 q [clips*T][H*64], k/v [clips*Tk][H*64], dout like q; scale 1/8 (head_dim 64);
  * nvalid: per-clip valid key count or NULL; causal; zero_key = the prepended zero key of

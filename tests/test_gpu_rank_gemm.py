@@ -66,3 +66,32 @@ def test_rank_store_repeatable():
     again = A.rank_gemm_f16(a, b, 1000, 2048, 32, False, False, A.RANK_STORE, 1.0)
     np.testing.assert_array_equal(first, again)
     np.testing.assert_allclose(first, ref, rtol=2 ** -11, atol=3e-5 * np.sqrt(2048))
+
+
+@pytest.mark.parametrize("kind,a_mn,b_mn", [(A.RANK_ACC, False, False), (A.RANK_ACC_T, True, True)],
+                         ids=["P=W_At(K-major W)", "BDt_W(MN-major W)"])
+@pytest.mark.parametrize("M,K,nb,splits", [(384, 1536, 32, 4), (4608, 1536, 32, 8), (1536, 6144, 16, 8),
+                                           (224, 320, 16, 2)])
+def test_q8_0_rank_product_equals_f16_on_the_dequantised_weight(kind, a_mn, b_mn, M, K, nb, splits):
+    """The DoRA products read the frozen Q8_0 weight through the rank-block kernel's converter
+    warps (P = W A^T with W K-major; BD^T W as (W^T BD)^T with W MN-major).  Their f16 operand is
+    exactly the bind-time dequantisation (fp32 d * q rounded to f16), so with the same split the
+    result is bit-identical to the f16 kernel on that weight, and it matches the fp64 product."""
+    from cases import q8_0_bytes
+    rng = np.random.default_rng(M + 5 * K + nb)
+    wshape = (K, M) if a_mn else (M, K)
+    w = (0.02 * rng.standard_normal(wshape) * np.exp(rng.standard_normal((wshape[0], 1)))).astype(np.float32)
+    blocks = q8_0_bytes(w)
+    _, wh = A.q8_0_dequant(blocks)
+    b = f16_bits(rng.standard_normal((K, nb) if b_mn else (nb, K)))
+    c0 = rng.standard_normal((nb, M) if kind == A.RANK_ACC_T else (M, nb)).astype(np.float32)
+    c8 = A.rank_gemm_q8_0(blocks, b, M, K, nb, a_mn, b_mn, kind, alpha=0.5, C_init=c0, splits=splits)
+    c16 = A.rank_gemm_f16(wh.reshape(wshape), b, M, K, nb, a_mn, b_mn, kind, alpha=0.5, C_init=c0, splits=splits)
+    np.testing.assert_array_equal(c8, c16)
+    wf = bits_to_f32(wh).reshape(wshape).astype(np.float64)
+    am = wf.T if a_mn else wf                                    # A(m, k) [M][K]
+    bk = bits_to_f32(b).astype(np.float64)
+    bm = bk if b_mn else bk.T                                    # B(k, n) [K][nb]
+    ref = 0.5 * (am @ bm)
+    ref = c0 + (ref.T if kind == A.RANK_ACC_T else ref)
+    assert np.abs(c8 - ref).max() / np.abs(ref).max() < 1e-5
