@@ -256,15 +256,19 @@ __global__ void linear_f32_kernel(const float* __restrict__ x, const float* __re
 
 // ---------------------------------------------------------------------------------------
 // DoRA-rows, src/ac/lora.h:62-79 (and the hand-derived backward of that factorisation).
-// Column sums of a * b over the rows in DORA_COLSUM_PARTS row blocks.  A block takes 256 columns
-// (8 per lane, 16-byte loads) and one row block, its 8 warps taking every 8th row; the warps'
-// sums meet in shared memory and are added in warp order, and the block leaves its partial in
-// part[row block][n]; the second kernel adds the row blocks in order (no atomics, so the sum does
-// not depend on the order in which blocks finish).
+// Column sums of a * b over the rows in at most DORA_COLSUM_PARTS row blocks.  A block takes 256
+// columns (8 per lane, 16-byte loads) and one row block, its 8 warps taking every 8th row; the
+// warps' sums meet in shared memory and are added in warp order, and the block leaves its
+// partial in part[row block][n].  The last block of a column block to finish (a counter per
+// column block, reset by that block) adds the row blocks' partials in row-block order, so the
+// sum does not depend on the order in which blocks finish, and applies the DoRA factor.
 __global__ void __launch_bounds__(256) dora_colsum_kernel(const f16* __restrict__ a, long lda,
                                                           const f16* __restrict__ b, long ldb, int rows, int N,
-                                                          float* __restrict__ part, int rows_per_block) {
+                                                          float* __restrict__ part, int rows_per_block,
+                                                          int* __restrict__ count, const float* __restrict__ g,
+                                                          float* __restrict__ dg, float inv_gscale) {
     __shared__ float red[8][256];
+    __shared__ int last;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int c0 = blockIdx.x * 256 + lane * 8;
     const int r0 = blockIdx.y * rows_per_block, r1 = min(rows, r0 + rows_per_block);
@@ -294,17 +298,20 @@ __global__ void __launch_bounds__(256) dora_colsum_kernel(const f16* __restrict_
         for (int w = 0; w < 8; ++w) v += red[w][threadIdx.x];
         part[(long)blockIdx.y * N + n] = v;
     }
-}
-
-__global__ void dora_colsum_add_kernel(const float* __restrict__ part, int parts, int N,
-                                       const float* __restrict__ g, float* __restrict__ dg, float inv_gscale) {
-    const int n = blockIdx.x * blockDim.x + threadIdx.x;
-    if (n >= N) return;
-    float acc = 0.f;
+    __threadfence();  // this block's partial is visible before it is counted
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(count + blockIdx.x, 1) == (int)gridDim.y - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (n < N) {
+        float t = 0.f;
 #pragma unroll 8
-    for (int j = 0; j < parts; ++j) acc += part[(long)j * N + n];  // loads issued ahead, added in order
-    const float gg = g[n];
-    dg[n] += acc * inv_gscale / (gg * gg);
+        for (int j = 0; j < (int)gridDim.y; ++j) t += __ldcg(part + (long)j * N + n);  // row-block order
+        const float gg = g[n];
+        dg[n] += t * inv_gscale / (gg * gg);
+    }
+    if (threadIdx.x == 0) count[blockIdx.x] = 0;  // ready for the next launch
 }
 
 // The per-step factors and the backward tail are batched: one launch covers a list of
@@ -726,7 +733,7 @@ void linear_f32(const float* x, const float* W, float* y, int rows, int N, int K
 }
 
 void dora_colsum(const f16* a, long lda, const f16* b, long ldb, int rows, int N, const float* colscale,
-                 float* dg, float* part, float inv_gscale, cudaStream_t s) {
+                 float* dg, float* part, int* count, float inv_gscale, cudaStream_t s) {
     if (N % 8 || lda % 8 || ldb % 8) throw std::runtime_error("dora_colsum: rows must be whole 16-byte pieces");
     // about four blocks per SM in all (the loads of a block are few and serial), each block at
     // least 64 rows: a fixed split for a given shape and device
@@ -735,9 +742,8 @@ void dora_colsum(const f16* a, long lda, const f16* b, long ldb, int rows, int N
     const int nparts = std::min(std::min(want, DORA_COLSUM_PARTS), std::max(1, rows / 64));
     const int rpb = (rows + nparts - 1) / nparts;
     const int parts = (rows + rpb - 1) / rpb;
-    dim3 grid(blocks_for(N, 256), parts);
-    dora_colsum_kernel<<<grid, 256, 0, s>>>(a, lda, b, ldb, rows, N, part, rpb);
-    dora_colsum_add_kernel<<<blocks_for(N, 256), 256, 0, s>>>(part, parts, N, colscale, dg, inv_gscale);
+    dim3 grid(col_blocks, parts);
+    dora_colsum_kernel<<<grid, 256, 0, s>>>(a, lda, b, ldb, rows, N, part, rpb, count, colscale, dg, inv_gscale);
 }
 
 void dora_factors(const DoraJob* jobs, int n, int r, int max_out, cudaStream_t st) {

@@ -166,6 +166,7 @@ struct Proj {
     float* base = nullptr; // DoRA: frozen ||W_o||^2 + in*1e-12 (double accumulated on the host)
     float *P = nullptr, *G = nullptr, *Q = nullptr, *nsq = nullptr, *g = nullptr, *dg = nullptr, *scr = nullptr,
           *colpart = nullptr;
+    int* colcnt = nullptr;  // dora_colsum's per-column-block counters (left at zero)
     f16* BD = nullptr;
 };
 
@@ -618,7 +619,7 @@ struct act_ctx {
                   bool want_dx, GemmArgs e) {
         if (p.dora)
             timed(2, 0, 4.0 * rows * p.out,
-                  [&] { dora_colsum(dYl, p.out, Y, p.out, (int)rows, p.out, p.g, p.dg, p.colpart, inv_gscale, stream); });
+                  [&] { dora_colsum(dYl, p.out, Y, p.out, (int)rows, p.out, p.g, p.dg, p.colpart, p.colcnt, inv_gscale, stream); });
         if (p.adapted) {
             GemmArgs u;
             u.M = (int)rows; u.N = p.RP; u.K1 = p.out;
@@ -1649,6 +1650,7 @@ struct act_ctx {
                     p.dg = dalloc<float>(p.out);
                     p.scr = dalloc<float>((size_t)p.out + p.r * p.r);
                     p.colpart = dalloc<float>((size_t)DORA_COLSUM_PARTS * p.out);
+                    p.colcnt = dalloc<int>((size_t)(p.out + 255) / 256);
                     p.BD = dalloc<f16>((size_t)p.out * RP);
                 }
             }

@@ -258,10 +258,10 @@ void linear_f32(const float* x, const float* W, float* y, int rows, int N, int K
 // colscale and the gradient scale; dg is the unscaled gradient)
 // dora_colsum splits the rows into at most DORA_COLSUM_PARTS blocks (enough to fill the GPU for
 // the column count; fixed for a shape, so the ordered sum of the parts is reproducible); part
-// holds DORA_COLSUM_PARTS * N floats
+// holds DORA_COLSUM_PARTS * N floats; count holds ceil(N / 256) zero ints (left at zero)
 constexpr int DORA_COLSUM_PARTS = 64;
 void dora_colsum(const f16* a, long lda, const f16* b, long ldb, int rows, int N, const float* colscale,
-                 float* dg, float* part, float inv_gscale, cudaStream_t s);
+                 float* dg, float* part, int* count, float inv_gscale, cudaStream_t s);
 // DoRA-rows of one projection, for the batched kernels below (src/ac/lora.h:62-79 and the
 // hand-derived backward of that factorisation)
 struct DoraJob {
