@@ -271,6 +271,7 @@ struct act_ctx {
     bool deterministic = false;  // act_set_deterministic: ordered dQ adds in the tcgen05 backward
     float* dkv_acc = nullptr;  // cross-attention dK | dV partials (fp32, [2][qsplit][clips * C][D])
     int cross_qsplit = 1;
+    f16* dU_cond = nullptr;  // dU of cross.kv, whose gradients run on the side stream
     f16 *dxh = nullptr, *dz = nullptr, *dU = nullptr, *dob = nullptr, *dqkv = nullptr, *dcq = nullptr,
          *dckv = nullptr;
     float* logits = nullptr;
@@ -615,8 +616,11 @@ struct act_ctx {
 
     // Adapter gradients of one projection from dYl (= dY * g, f16 [rows][out]) and, when
     // `e` has an output, the input gradient dX = dYl W + dU A.
+    // inline_grads: dB / dA run on the current stream and nothing is joined (the caller has put
+    // the whole call on the side stream); dUb: the dU scratch (default: the main one)
     void proj_bwd(Proj& p, const f16* dYl, long rows, const f16* X, const f16* U, const f16* Y,
-                  bool want_dx, GemmArgs e) {
+                  bool want_dx, GemmArgs e, f16* dUb = nullptr, bool inline_grads = false) {
+        f16* const dUs = dUb ? dUb : dU;
         if (p.dora)
             timed(2, 0, 4.0 * rows * p.out,
                   [&] { dora_colsum(dYl, p.out, Y, p.out, (int)rows, p.out, p.g, p.dg, p.colpart, p.colcnt, inv_gscale, stream); });
@@ -624,11 +628,11 @@ struct act_ctx {
             GemmArgs u;
             u.M = (int)rows; u.N = p.RP; u.K1 = p.out;
             u.A1 = dYl; u.lda1 = p.out; u.B1 = p.B_h; u.ldb1 = p.RP; u.b_kmajor = false;
-            u.mode = EPI_STORE_F16; u.alpha = p.s; u.out = dU; u.ldo = p.RP;
+            u.mode = EPI_STORE_F16; u.alpha = p.s; u.out = dUs; u.ldo = p.RP;
             SkinnyArgs ku;  // dU = s dYl B
             ku.M = (int)rows; ku.K = p.out; ku.nb = p.RP;
             ku.A = dYl; ku.lda = p.out; ku.B = p.B_h; ku.ldb = p.RP; ku.b_mn = true;
-            ku.kind = SKINNY_STORE; ku.alpha = p.s; ku.out = dU; ku.ldo = p.RP;
+            ku.kind = SKINNY_STORE; ku.alpha = p.s; ku.out = dUs; ku.ldo = p.RP;
             run_rank(ku, u);
             GemmArgs gb;
             gb.M = p.out; gb.N = p.RP; gb.K1 = (int)rows;
@@ -642,29 +646,34 @@ struct act_ctx {
             kb.kind = SKINNY_ACC; kb.alpha = inv_gscale; kb.out = grad + p.offB; kb.ldo = p.r;
             GemmArgs ga;
             ga.M = p.RP; ga.N = p.in; ga.K1 = (int)rows;
-            ga.A1 = dU; ga.lda1 = p.RP; ga.a_kmajor = false;
+            ga.A1 = dUs; ga.lda1 = p.RP; ga.a_kmajor = false;
             ga.B1 = X; ga.ldb1 = p.in; ga.b_kmajor = false;
             ga.mode = EPI_ATOMIC_F32; ga.alpha = inv_gscale; ga.out = grad + p.offA; ga.ldo = p.in; ga.mvalid = p.r;
             ga.splitk = splitk_for((long)((p.in + 127) / 128), (rows + 63) / 64);
             SkinnyArgs ka;  // dA += dU^T X   ([r][in], computed as its transpose)
             ka.M = p.in; ka.K = (int)rows; ka.nb = p.r;
-            ka.A = X; ka.lda = p.in; ka.a_mn = true; ka.B = dU; ka.ldb = p.RP; ka.b_mn = true;
+            ka.A = X; ka.lda = p.in; ka.a_mn = true; ka.B = dUs; ka.ldb = p.RP; ka.b_mn = true;
             ka.kind = SKINNY_ACC_T; ka.alpha = inv_gscale; ka.out = grad + p.offA; ka.ldo = p.in;
             // the adapter gradients only read dYl, U, X and dU: they overlap the input-gradient
             // GEMM below (which fills its last wave with idle SMs) and join before returning
-            on_side([&] {
+            if (inline_grads) {
                 run_rank(kb, gb);
                 run_rank(ka, ga);
-            });
+            } else {
+                on_side([&] {
+                    run_rank(kb, gb);
+                    run_rank(ka, ga);
+                });
+            }
         }
         if (!want_dx) {
-            join_side();
+            if (!inline_grads) join_side();
             return;
         }
         e.M = (int)rows; e.N = p.in; e.K1 = p.out;
         e.A1 = dYl; e.lda1 = p.out; set_b(e, 1, p.W, false);
         if (p.adapted) {
-            e.K2 = p.RP; e.A2 = dU; e.lda2 = p.RP; e.B2 = p.A_h; e.ldb2 = p.in;
+            e.K2 = p.RP; e.A2 = dUs; e.lda2 = p.RP; e.B2 = p.A_h; e.ldb2 = p.in;
             e.a2_from_prev = true;  // dU: the last launch on this stream (dB / dA went to the side)
         }
         run_gemm(e, 0);
@@ -904,7 +913,11 @@ struct act_ctx {
             if (split && need_dkv) attn_dkv_finish(ca, stream);
             if (!dq_direct) attn_dq_finish(ca, dcq, D, y.p[2].dora ? y.p[2].g : nullptr, stream);
         });
-        if (need_dkv) proj_bwd(y.p[3], dckv, crows, ctx_h, y.U[3], y.ckv, false, GemmArgs());
+        // cross.kv's adapter gradients (the conditioning needs no input gradient) go to the side
+        // stream with their own dU scratch: they overlap cross.q's backward, and the join after
+        // its input-gradient GEMM collects them before anything reads them
+        if (need_dkv)
+            on_side([&] { proj_bwd(y.p[3], dckv, crows, ctx_h, y.U[3], y.ckv, false, GemmArgs(), dU_cond, true); });
         {
             GemmArgs e; e.mode = EPI_STORE_F32; e.out = dtmp; e.ldo = D;
             proj_bwd(y.p[2], dcq, rows, y.hc, y.U[2], y.cq, true, e);
@@ -1778,6 +1791,7 @@ struct act_ctx {
         dxh = dalloc<f16>(Mr * D);
         dz = dalloc<f16>(Mr * F);
         dU = dalloc<f16>(std::max(Mr, Cr) * RP);
+        dU_cond = dalloc<f16>(Cr * RP);
         dob = dalloc<f16>(Mr * D);
         dqkv = dalloc<f16>(Mr * 3 * D);
         dcq = dalloc<f16>(Mr * D);
