@@ -556,12 +556,15 @@ __global__ void mg_embed_kernel(const int32_t* __restrict__ ids, int steps, int 
 
 // ggml_cross_entropy_loss over the selected rows, src/mg/train.h:131.
 // Each row leaves its loss term in rowloss[row]; mg_loss_add_kernel sums them in row order.
-__global__ void mg_ce_kernel(const float* __restrict__ logits, int card, const int32_t* __restrict__ targets,
-                             float inv_nsel, float* __restrict__ rowloss, f16* __restrict__ dlogits, float gscale) {
-    const int row = blockIdx.x;
-    const int tgt = targets[row];
-    const float* lg = logits + (long)row * card;
-    f16* dl = dlogits + (long)row * card;
+__global__ void mg_ce_kernel(const float* __restrict__ logits, int sel, int T, int row0, int card,
+                             const int32_t* __restrict__ targets, long tgt_stride, float inv_nsel,
+                             float* __restrict__ rowloss, f16* __restrict__ dlogits, float gscale) {
+    const int row = blockIdx.x;  // scored row of the codebook, sample-major
+    const int b = row / sel, st = row % sel;
+    const int tgt = targets[(long)b * tgt_stride + st];
+    const long lrow = (long)b * T + row0 + st;
+    const float* lg = logits + lrow * card;
+    f16* dl = dlogits + lrow * card;
     __shared__ float red[32];
     __shared__ float sh_max, sh_sum;
     float mx = -INFINITY;
@@ -799,10 +802,13 @@ void mg_embed(const int32_t* ids, int steps, int nq, const float* const* emb_dev
     mg_embed_kernel<<<blocks_for(n, 256), 256, 0, s>>>(ids, steps, nq, emb_dev, pos, x, D, seqs);
 }
 
-void mg_cross_entropy(const float* logits, int rows, int card, const int32_t* targets, int rows_per_seq,
-                      float inv_nsel, float* loss_acc, float* rowloss, f16* dlogits, float gscale, cudaStream_t s) {
-    mg_ce_kernel<<<rows, 256, 0, s>>>(logits, card, targets, inv_nsel, rowloss, dlogits, gscale);
-    mg_loss_add_kernel<<<(rows + rows_per_seq - 1) / rows_per_seq, 256, 0, s>>>(rowloss, rows, rows_per_seq, loss_acc);
+void mg_cross_entropy(const float* logits, int n, int sel, int T, int row0, int card, const int32_t* targets,
+                      long tgt_stride, float inv_nsel, float* loss_acc, float* rowloss, f16* dlogits, float gscale,
+                      cudaStream_t s) {
+    if (n <= 0 || sel <= 0) return;
+    mg_ce_kernel<<<n * sel, 256, 0, s>>>(logits, sel, T, row0, card, targets, tgt_stride, inv_nsel, rowloss, dlogits,
+                                         gscale);
+    mg_loss_add_kernel<<<n, 256, 0, s>>>(rowloss, n * sel, sel, loss_acc);
 }
 
 }  // namespace act

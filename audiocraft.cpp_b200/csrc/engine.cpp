@@ -260,7 +260,7 @@ struct act_ctx {
           *d_loss = nullptr, *d_ctx = nullptr, *d_start = nullptr;  // d_start: edit-bridge start, -1 = none
     float* loss_part = nullptr;  // per-clip partial sums of the MSE ([max_batch][32])
     int32_t *d_nvalid = nullptr, *d_ids = nullptr, *d_tgt = nullptr;
-    float* mg_rowloss = nullptr;  // per-row cross-entropy terms of one (sample, codebook)
+    float* mg_rowloss = nullptr;  // per-row cross-entropy terms of one codebook ([B][scored rows])
 
     // global activations / scratch
     f16 *x0 = nullptr, *hidden_h = nullptr, *ctx_h = nullptr, *xo = nullptr, *dout = nullptr, *xprev_h = nullptr;
@@ -1069,26 +1069,30 @@ struct act_ctx {
             CK(cudaMemsetAsync(d_loss, 0, sizeof(float) * n, stream));
             CK(cudaMemsetAsync(dtmp, 0, sizeof(float) * rows * D, stream));
         });
+        // The head per codebook over every row of every sample (src/mg/train.h:131-140 scores
+        // rows q + prefix .. q + frames - 1 of each sequence for codebook q): one logits GEMM,
+        // one cross-entropy over the scored rows, one input-gradient GEMM.  Codebook q's
+        // [B][T][card] block sits at a fixed place (maximum batch), so a row of dlogits is scored
+        // or not whatever the microbatch: the unscored rows stay zero from allocation and add
+        // nothing to the input gradient.
         const float inv_nsel = 1.0f / (float)(nq * sel);
-        for (int b = 0; b < n; ++b)
-            for (int q = 0; q < nq; ++q) {
-                const long r0 = (long)b * T + q + prefix;  // rows s = q + prefix .. q + frames - 1
-                float* lg = logits + ((long)(b * nq + q) * sel) * card;
-                f16* dl = dlogits + ((long)(b * nq + q) * sel) * card;
-                GemmArgs hgm;
-                hgm.M = sel; hgm.N = card; hgm.K1 = D; hgm.A1 = xo + r0 * D; hgm.lda1 = D;
-                set_b(hgm, 1, head[q], true); hgm.mode = EPI_STORE_F32; hgm.out = lg; hgm.ldo = card;
-                run_gemm(hgm, 0);
-                timed(2, 0, 0, [&] {
-                    mg_cross_entropy(lg, sel, card, d_tgt + (long)(b * nq + q) * sel, sel * nq, inv_nsel,
-                                     d_loss + b, mg_rowloss, dl, gscale, stream);
-                });
-                GemmArgs dg;
-                dg.M = sel; dg.N = D; dg.K1 = card; dg.A1 = dl; dg.lda1 = card;
-                set_b(dg, 1, head[q], false);
-                dg.mode = EPI_ACCUM_F32; dg.out = dtmp + r0 * D; dg.ldo = D;
-                run_gemm(dg, 0);
-            }
+        for (int q = 0; q < nq; ++q) {
+            float* lg = logits + (long)q * B * T * card;
+            f16* dl = dlogits + (long)q * B * T * card;
+            GemmArgs hgm;
+            hgm.M = (int)rows; hgm.N = card; hgm.K1 = D; hgm.A1 = xo; hgm.lda1 = D;
+            set_b(hgm, 1, head[q], true); hgm.mode = EPI_STORE_F32; hgm.out = lg; hgm.ldo = card;
+            run_gemm(hgm, 0);
+            timed(2, 0, 0, [&] {
+                mg_cross_entropy(lg, n, sel, T, q + prefix, card, d_tgt + (long)q * sel, (long)nq * sel, inv_nsel,
+                                 d_loss, mg_rowloss, dl, gscale, stream);
+            });
+            GemmArgs dg;
+            dg.M = (int)rows; dg.N = D; dg.K1 = card; dg.A1 = dl; dg.lda1 = card;
+            set_b(dg, 1, head[q], false);
+            dg.mode = EPI_ACCUM_F32; dg.out = dtmp; dg.ldo = D;
+            run_gemm(dg, 0);
+        }
         timed(2, 0, 0, [&] {
             layernorm_bwd(dtmp, last.xout, onw, muo, rso, dx, 0, entry_extra(L - 1), dxh, entry_scale(L - 1),
                           (int)rows, D, stream);
@@ -1818,15 +1822,15 @@ struct act_ctx {
             h_ctx = halloc<float>((size_t)Cr * D);
             d_ids = dalloc<int32_t>((size_t)B * md.n_q * T);
             d_tgt = dalloc<int32_t>((size_t)B * md.n_q * sel);
-            mg_rowloss = dalloc<float>((size_t)std::max(sel, 1));
+            mg_rowloss = dalloc<float>((size_t)B * std::max(sel, 1));
             d_ctx = dalloc<float>((size_t)Cr * D);
             if (C != Ctok) {
                 d_mgvalid = dalloc<int32_t>(B);
                 std::vector<int32_t> v((size_t)B, Ctok);
                 CK(cudaMemcpy(d_mgvalid, v.data(), (size_t)B * 4, cudaMemcpyHostToDevice));
             }
-            logits = dalloc<float>((size_t)B * md.n_q * sel * md.card);
-            dlogits = dalloc<f16>((size_t)B * md.n_q * sel * md.card);
+            logits = dalloc<float>((size_t)B * md.n_q * T * md.card);   // [n_q][B][T][card]
+            dlogits = dalloc<f16>((size_t)B * md.n_q * T * md.card);
         }
         CK(cudaStreamSynchronize(stream));
     }

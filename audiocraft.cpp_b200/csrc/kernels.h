@@ -310,10 +310,14 @@ void q8_0_to_f32(const uint8_t* blocks, long nblocks, float* out, cudaStream_t s
 // MusicGen: x[s][:] = sum_q emb_q[ids[q][s]] + pos[s]   (fp32 out)
 void mg_embed(const int32_t* ids, int steps, int nq, const float* const* emb_dev, const float* pos,
               float* x, int D, int seqs, cudaStream_t s);
-// Cross entropy over selected rows: logits fp32 [rows][card]; targets per row (-1: skip);
-// loss_acc[seq] += ce / nsel (row terms through rowloss, [rows], added in row order);
-// dlogits f16 = gscale * (softmax - onehot) / nsel.
-void mg_cross_entropy(const float* logits, int rows, int card, const int32_t* targets, int rows_per_seq,
-                      float inv_nsel, float* loss_acc, float* rowloss, f16* dlogits, float gscale, cudaStream_t s);
+// Cross entropy of one codebook over every sample's scored rows: row r of n * sel is sample
+// b = r / sel, step s = r % sel, whose logits (fp32) / dlogits (f16) row is b * T + row0 + s of a
+// [n * T][card] matrix and whose target is targets[b * tgt_stride + s] (-1: skip);
+// loss_acc[b] += ce / nsel (row terms through rowloss [n * sel], added per sample in row order);
+// dlogits = gscale * (softmax - onehot) / nsel.  Rows of dlogits outside the scored ones are not
+// written.
+void mg_cross_entropy(const float* logits, int n, int sel, int T, int row0, int card, const int32_t* targets,
+                      long tgt_stride, float inv_nsel, float* loss_acc, float* rowloss, f16* dlogits, float gscale,
+                      cudaStream_t s);
 
 }  // namespace act
