@@ -344,10 +344,11 @@ def run_sweep(kind, reps):
 
 
 def run_sweep_record(A, reps, peak):
-    """The kernel sweep of BASELINE cfg 5 as one record: the cfg-2 / cfg-4 projection shapes with
-    f16 and Q8_0 weights beside cuBLAS (torch.matmul, f16 in / f16 out, fp32 accumulation) timed in
-    the same process; the four LoRA rank products at ranks 8..64; self-attention at 750 / 1500 /
-    3000 frames.  Every GEMM result is checked against cuBLAS's."""
+    """The kernel sweep of BASELINE cfg 5 as one record: the cfg-2 / cfg-4 projection shapes and
+    2k-64k token rows at the cfg-2 widths with f16 and Q8_0 weights beside cuBLAS (torch.matmul,
+    f16 in / f16 out, fp32 accumulation) timed in the same process; the four LoRA rank products at
+    ranks 8..64 and the DoRA weight products on a Q8_0 weight; self-attention at 750 / 1500 / 3000
+    frames, 16 and 24 heads, causal and not.  Every GEMM result is checked against cuBLAS's."""
     import torch
     rng = np.random.default_rng(0)
     bits = lambda shape: (rng.integers(0x3C00, 0x3F80, size=shape, dtype=np.uint16) ^
@@ -369,28 +370,36 @@ def run_sweep_record(A, reps, peak):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / reps, y.float().cpu().numpy()
 
+    def gemm_line(M, N, K, b_mn, part):
+        wshape = (K, N) if b_mn else (N, K)
+        a = bits((M, K))
+        w32 = (0.02 * rng.standard_normal(wshape)).astype(np.float32)
+        blocks = q8_0(w32)
+        _, wh = A.q8_0_dequant(blocks)
+        wh = wh.reshape(wshape)
+        c16, ms16 = A.gemm_f16(a, wh, M, N, K, b_mn, 0, reps=reps)
+        c8, ms8 = A.gemm_q8_0(a, blocks, M, N, K, b_mn, 0, reps=reps)
+        msc, cref = cublas_ms(a, wh, b_mn)
+        fl = 2.0 * M * N * K
+        scale = np.abs(cref).max()
+        print(json.dumps({"sweep": "gemm", "part": part, "M": M, "N": N, "K": K,
+                          "layout": "NN (dX = dY W)" if b_mn else "NT (Y = X W^T)",
+                          "ms_f16": ms16, "ms_q8_0": ms8, "ms_cublas": msc,
+                          "tflops_f16": fl / ms16 / 1e9, "tflops_q8_0": fl / ms8 / 1e9, "tflops_cublas": fl / msc / 1e9,
+                          "frac_of_peak_f16": fl / ms16 / 1e9 / peak, "frac_of_peak_q8_0": fl / ms8 / 1e9 / peak,
+                          "max_rel_diff_vs_cublas": float(max(np.abs(c16 - cref).max(), np.abs(c8 - cref).max()) / scale),
+                          "q8_0_equals_f16": bool(np.array_equal(c8, c16))}), flush=True)
+
+    # the projection shapes of the benchmarked steps (cfg 2: 8 x 750 rows, cfg 4: 4 x 1 503 rows)
     shapes = [(6000, 1024, 1024), (6000, 3072, 1024), (6000, 4096, 1024), (6000, 1024, 4096),
               (6012, 1536, 1536), (6012, 4608, 1536), (6012, 6144, 1536), (6012, 1536, 6144)]
     for M, N, K in shapes:
         for b_mn in (False, True):
-            wshape = (K, N) if b_mn else (N, K)
-            a = bits((M, K))
-            w32 = (0.02 * rng.standard_normal(wshape)).astype(np.float32)
-            blocks = q8_0(w32)
-            _, wh = A.q8_0_dequant(blocks)
-            wh = wh.reshape(wshape)
-            c16, ms16 = A.gemm_f16(a, wh, M, N, K, b_mn, 0, reps=reps)
-            c8, ms8 = A.gemm_q8_0(a, blocks, M, N, K, b_mn, 0, reps=reps)
-            msc, cref = cublas_ms(a, wh, b_mn)
-            fl = 2.0 * M * N * K
-            scale = np.abs(cref).max()
-            print(json.dumps({"sweep": "gemm", "M": M, "N": N, "K": K,
-                              "layout": "NN (dX = dY W)" if b_mn else "NT (Y = X W^T)",
-                              "ms_f16": ms16, "ms_q8_0": ms8, "ms_cublas": msc,
-                              "tflops_f16": fl / ms16 / 1e9, "tflops_q8_0": fl / ms8 / 1e9, "tflops_cublas": fl / msc / 1e9,
-                              "frac_of_peak_f16": fl / ms16 / 1e9 / peak, "frac_of_peak_q8_0": fl / ms8 / 1e9 / peak,
-                              "max_rel_diff_vs_cublas": float(max(np.abs(c16 - cref).max(), np.abs(c8 - cref).max()) / scale),
-                              "q8_0_equals_f16": bool(np.array_equal(c8, c16))}), flush=True)
+            gemm_line(M, N, K, b_mn, "step shapes")
+    # cfg 5's token counts at the cfg-2 projection widths (forward layout)
+    for M in (2048, 8192, 32768, 65536):
+        for N, K in ((1024, 1024), (4096, 1024), (1024, 4096)):
+            gemm_line(M, N, K, False, "token sweep")
     for K in (1024, 4096):
         for r in (8, 16, 32, 64):
             nb = (r + 31) // 32 * 32
@@ -402,18 +411,30 @@ def run_sweep_record(A, reps, peak):
                 byts = 2.0 * M * KK + 2.0 * KK * nb
                 print(json.dumps({"sweep": "rank", "product": name, "rank": r, "M": M, "K": KK, "nb": nb, "ms": ms,
                                   "gbs": byts / ms / 1e6}), flush=True)
-    for H in (16,):
+    # the DoRA weight products on a Q8_0 weight (P = W A^T, K-major; BD^T W, MN-major), cfg-4 widths
+    for M, K in ((4608, 1536), (1536, 1536), (6144, 1536), (1536, 6144)):
+        for kind, name, a_mn, b_mn in ((0, "P = W A^T", 0, 0), (1, "BD^T W", 1, 1)):
+            mm, kk = (M, K) if not a_mn else (K, M)  # BD^T W reduces over the weight's rows
+            wshape = (kk, mm) if a_mn else (mm, kk)
+            blocks = q8_0((0.02 * rng.standard_normal(wshape)).astype(np.float32))
+            bb = bits((kk, 32) if b_mn else (32, kk))
+            _, ms = A.rank_gemm_q8_0(blocks, bb, mm, kk, 32, bool(a_mn), bool(b_mn), kind, 1.0, reps=reps)
+            byts = 1.0625 * mm * kk + 2.0 * kk * 32 + 8.0 * mm * 32
+            print(json.dumps({"sweep": "rank_q8_0", "product": name, "M": mm, "K": kk, "nb": 32, "ms": ms,
+                              "gbs": byts / ms / 1e6}), flush=True)
+    for H in (16, 24):
         for T in (750, 1500, 3000):
-            clips = max(1, 6000 // T)
-            D = H * 64
-            q, k, v, do = (bits((clips * T, D)) for _ in range(4))
-            A.attention(q, k, v, do, clips, T, T, H, None, False, True, None)
-            out = A.attention(q, k, v, do, clips, T, T, H, None, False, True, None)
-            keys = T * (T + 1)
-            print(json.dumps({"sweep": "attention", "heads": H, "seq": T, "clips": clips, "zero_key": True,
-                              "ms_fwd": out["ms_fwd"], "ms_bwd": out["ms_bwd"],
-                              "tflops_fwd": 4.0 * clips * keys * D / (out["ms_fwd"] / 1e3) / 1e12,
-                              "tflops_bwd": 8.0 * clips * keys * D / (out["ms_bwd"] / 1e3) / 1e12}), flush=True)
+            for causal in (False, True):
+                clips = max(1, 6000 // T)
+                D = H * 64
+                q, k, v, do = (bits((clips * T, D)) for _ in range(4))
+                A.attention(q, k, v, do, clips, T, T, H, None, causal, not causal, None)
+                out = A.attention(q, k, v, do, clips, T, T, H, None, causal, not causal, None)
+                keys = T * (T + 1) / 2 if causal else T * (T + 1)
+                print(json.dumps({"sweep": "attention", "heads": H, "seq": T, "clips": clips, "causal": causal,
+                                  "zero_key": not causal, "ms_fwd": out["ms_fwd"], "ms_bwd": out["ms_bwd"],
+                                  "tflops_fwd": 4.0 * clips * keys * D / (out["ms_fwd"] / 1e3) / 1e12,
+                                  "tflops_bwd": 8.0 * clips * keys * D / (out["ms_bwd"] / 1e3) / 1e12}), flush=True)
 
 
 def build_context(A, c, workload, device, seed=0):
