@@ -167,7 +167,15 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_fwd_tc_kernel(const __grid
         prefetch_tmap(&maps.v);
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    if (a.causal) {
+        // causal: query block qb visits qb + 1 key blocks.  The heaviest go first over every
+        // (clip, head), so the last wave holds the lightest CTAs.
+        const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z), per = gridDim.y * gridDim.z;
+        qb = gridDim.x - 1 - lin / per;
+        h = (lin % per) % gridDim.y;
+        b = (lin % per) / gridDim.y;
+    }
     const int q0 = qb * AT_BQ;
     int kv_end = a.Tk;
     if (a.nvalid) kv_end = min(kv_end, a.nvalid[b]);
@@ -417,7 +425,16 @@ __global__ void __launch_bounds__(AB_THREADS, 1) attn_bwd_tc_kernel(const __grid
         prefetch_tmap(&maps.dq);
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int kb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    int kb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    if (a.causal) {
+        // causal: key block kb visits the query blocks from kb on.  The heaviest (low kb) go
+        // first over every (clip, head), so the last wave holds the lightest CTAs; key blocks
+        // still start in ascending order, which the ordered dQ adds rely on.
+        const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z), per = gridDim.y * gridDim.z;
+        kb = lin / per;
+        h = (lin % per) % gridDim.y;
+        b = (lin % per) / gridDim.y;
+    }
     const int k0 = kb * AB_BK;
     int kv_end = a.Tk;
     if (a.nvalid) kv_end = min(kv_end, a.nvalid[b]);
