@@ -323,6 +323,14 @@ struct act_ctx {
     DoraJob* dora_jobs_dev = nullptr;
     int dora_n = 0, dora_max_out = 0;
     std::vector<DoraSpan> dora_layer;
+    // The DoRA weight products and row factors depend only on the adapters and the frozen
+    // weights: they run on a stream of their own, a layer ahead of the forward, which waits per
+    // layer (ev_dora[l]) only for its own factors
+    cudaStream_t dora_stream = nullptr;
+    cudaEvent_t ev_dora_fork = nullptr;
+    std::vector<cudaEvent_t> ev_dora;
+    bool dora_async_ok = false;  // every P product takes the rank-block kernel (no scratch expansion)
+    bool dora_async = false;     // the step being issued runs them on dora_stream
 
     // ------------------------------------------------------------------------------------
     template <class Tp>
@@ -485,8 +493,14 @@ struct act_ctx {
     }
     // after layer l's backward and its DoRA terms (finish_layer): its adapters' gradients are
     // final.  Layers the backward does not reach keep zero gradients on every rank.
-    void sync_layer(int l) { sync_bucket(layer_params[l].first, layer_params[l].second); }
-    void sync_rest() { join_comm(); }
+    void sync_layer(int l) {
+        if (in_step_sync) join_side();  // the layer's gA products (finish_layer) are part of it
+        sync_bucket(layer_params[l].first, layer_params[l].second);
+    }
+    void sync_rest() {
+        join_side();
+        join_comm();
+    }
 
     // rank-block products: the tcgen05 skinny kernel, or the generic GEMM `fallback` when the
     // tcgen05 paths are disabled or the operands do not qualify
@@ -710,25 +724,42 @@ struct act_ctx {
         run_gemm(fallback, 2);
     }
 
+    // P = W A^T [out][RP]: a rank-block product reading the frozen weight once (kept quantised:
+    // the kernel's converter warps dequantise it)
+    void dora_p_product(Proj& p) {
+        SkinnyArgs k;
+        k.M = p.out; k.K = p.in; k.nb = p.RP;
+        set_rank_weight(k, p.W, false);
+        k.B = p.A_h; k.ldb = p.in;
+        k.kind = SKINNY_ACC; k.alpha = 1.0f; k.out = p.P; k.ldo = p.RP;
+        GemmArgs a;
+        a.M = p.out; a.N = p.RP; a.K1 = p.in;
+        a.lda1 = p.in; a.B1 = p.A_h; a.ldb1 = p.in;
+        a.mode = EPI_STORE_F32; a.out = p.P; a.ldo = p.RP;
+        if (use_tc && skinny_supported(k)) CK(cudaMemsetAsync(p.P, 0, sizeof(float) * p.out * p.RP, stream));
+        run_rank_weight(k, p.W, a, true);
+    }
+
     void prepare_adapters() {
         timed(2, 0, 0, [&] { refresh_f16(jobs_dev, njobs, max_job, stream); });
-        for (auto& lay : layers)
-            for (auto& p : lay.p) {
-                if (!p.dora) continue;
-                // P = W A^T [out][RP]: a rank-block product reading the frozen weight once (kept
-                // quantised: the kernel's converter warps dequantise it)
-                SkinnyArgs k;
-                k.M = p.out; k.K = p.in; k.nb = p.RP;
-                set_rank_weight(k, p.W, false);
-                k.B = p.A_h; k.ldb = p.in;
-                k.kind = SKINNY_ACC; k.alpha = 1.0f; k.out = p.P; k.ldo = p.RP;
-                GemmArgs a;
-                a.M = p.out; a.N = p.RP; a.K1 = p.in;
-                a.lda1 = p.in; a.B1 = p.A_h; a.ldb1 = p.in;
-                a.mode = EPI_STORE_F32; a.out = p.P; a.ldo = p.RP;
-                if (use_tc && skinny_supported(k)) CK(cudaMemsetAsync(p.P, 0, sizeof(float) * p.out * p.RP, stream));
-                run_rank_weight(k, p.W, a, true);
+        dora_async = dora_n > 0 && dora_async_ok && use_tc && !profiling;
+        if (dora_async) {
+            CK(cudaEventRecord(ev_dora_fork, stream));
+            CK(cudaStreamWaitEvent(dora_stream, ev_dora_fork, 0));
+            std::swap(stream, dora_stream);
+            for (size_t l = 0; l < layers.size(); ++l) {
+                for (auto& p : layers[l].p)
+                    if (p.dora) dora_p_product(p);
+                const DoraSpan& sp = dora_layer[l];
+                if (sp.n) dora_factors(dora_jobs_dev + sp.first, sp.n, ad.rank, sp.max_out, stream);
+                CK(cudaEventRecord(ev_dora[l], stream));
             }
+            std::swap(stream, dora_stream);
+            return;
+        }
+        for (auto& lay : layers)
+            for (auto& p : lay.p)
+                if (p.dora) dora_p_product(p);
         // the row factors of every DoRA projection in one pass per stage
         if (dora_n)
             timed(2, 0, 0, [&] { dora_factors(dora_jobs_dev, dora_n, ad.rank, dora_max_out, stream); });
@@ -738,30 +769,36 @@ struct act_ctx {
     // sums dg are complete then: only its own projections add into them)
     void finish_layer(int l) {
         const DoraSpan& sp = dora_layer[l];
-        if (sp.n)
-            timed(2, 0, 0, [&] {
-                dora_tail(dora_jobs_dev + sp.first, sp.n, ad.rank, sp.max_out, sp.max_in, gscale, stream);
-            });
-        for (auto& p : layers[l].p) {
-            if (!p.dora) continue;
-            SkinnyArgs k;  // gA += BD^T W, as (W^T BD)^T over the out dimension
-            k.M = p.in; k.K = p.out; k.nb = p.r;
-            set_rank_weight(k, p.W, true);
-            k.B = p.BD; k.ldb = p.RP; k.b_mn = true;
-            k.kind = SKINNY_ACC_T; k.alpha = inv_gscale; k.out = grad + p.offA; k.ldo = p.in;
-            GemmArgs a;
-            a.M = p.RP; a.N = p.in; a.K1 = p.out;
-            a.A1 = p.BD; a.lda1 = p.RP; a.a_kmajor = false;
-            a.ldb1 = p.in; a.b_kmajor = false;
-            a.mode = EPI_ATOMIC_F32; a.alpha = inv_gscale; a.out = grad + p.offA; a.ldo = p.in; a.mvalid = p.r;
-            a.splitk = splitk_for((p.in + 127) / 128, (p.out + 63) / 64);
-            run_rank_weight(k, p.W, a, false);
-        }
+        if (!sp.n) return;
+        timed(2, 0, 0, [&] {
+            dora_tail(dora_jobs_dev + sp.first, sp.n, ad.rank, sp.max_out, sp.max_in, gscale, stream);
+        });
+        // gA += BD^T W, as (W^T BD)^T over the out dimension: only adds into gA, so it runs on
+        // the side stream beside the next layer's backward (joined before the all-reduce of this
+        // layer and at the end of the step)
+        on_side([&] {
+            for (auto& p : layers[l].p) {
+                if (!p.dora) continue;
+                SkinnyArgs k;
+                k.M = p.in; k.K = p.out; k.nb = p.r;
+                set_rank_weight(k, p.W, true);
+                k.B = p.BD; k.ldb = p.RP; k.b_mn = true;
+                k.kind = SKINNY_ACC_T; k.alpha = inv_gscale; k.out = grad + p.offA; k.ldo = p.in;
+                GemmArgs a;
+                a.M = p.RP; a.N = p.in; a.K1 = p.out;
+                a.A1 = p.BD; a.lda1 = p.RP; a.a_kmajor = false;
+                a.ldb1 = p.in; a.b_kmajor = false;
+                a.mode = EPI_ATOMIC_F32; a.alpha = inv_gscale; a.out = grad + p.offA; a.ldo = p.in; a.mvalid = p.r;
+                a.splitk = splitk_for((p.in + 127) / 128, (p.out + 63) / 64);
+                run_rank_weight(k, p.W, a, false);
+            }
+        });
     }
 
     // One transformer block forward.  te: per-clip timestep embedding (MelodyFlow) or null.
     void block_fwd(int l, int n, const int* nvalid_dev) {
         Layer& y = layers[l];
+        if (dora_async) CK(cudaStreamWaitEvent(stream, ev_dora[l], 0));  // this layer's DoRA factors
         const long rows = (long)n * T, crows = (long)n * C;
         const float eps = md.norm_eps;
         const bool dit = mf;
@@ -1693,6 +1730,20 @@ struct act_ctx {
             }
             dora_n = (int)dj.size();
             if (dora_n) {
+                CK(cudaStreamCreateWithFlags(&dora_stream, cudaStreamNonBlocking));
+                CK(cudaEventCreateWithFlags(&ev_dora_fork, cudaEventDisableTiming));
+                ev_dora.assign(layers.size(), nullptr);
+                for (auto& e : ev_dora) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+                dora_async_ok = true;
+                for (auto& lay : layers)
+                    for (auto& p : lay.p) {
+                        if (!p.dora) continue;
+                        SkinnyArgs k;
+                        k.M = p.out; k.K = p.in; k.nb = p.RP;
+                        set_rank_weight(k, p.W, false);
+                        k.B = p.A_h; k.ldb = p.in; k.kind = SKINNY_ACC; k.out = p.P; k.ldo = p.RP;
+                        if (!skinny_supported(k)) dora_async_ok = false;
+                    }
                 dora_jobs_dev = dalloc<DoraJob>(dora_n);
                 CK(cudaMemcpyAsync(dora_jobs_dev, dj.data(), sizeof(DoraJob) * dora_n, cudaMemcpyHostToDevice, stream));
                 CK(cudaStreamSynchronize(stream));
@@ -1903,6 +1954,7 @@ struct act_ctx {
         for (void* p : dallocs) cudaFree(p);
         for (void* p : hallocs) cudaFreeHost(p);
         if (side) cudaStreamSynchronize(side);
+        if (dora_stream) cudaStreamSynchronize(dora_stream);
         if (comm_stream) cudaStreamSynchronize(comm_stream);
         if (ev_comm_fork) cudaEventDestroy(ev_comm_fork);
         if (ev_comm_join) cudaEventDestroy(ev_comm_join);
@@ -1910,6 +1962,9 @@ struct act_ctx {
         if (ev_fork) cudaEventDestroy(ev_fork);
         if (ev_join) cudaEventDestroy(ev_join);
         if (side) cudaStreamDestroy(side);
+        for (auto e : ev_dora) if (e) cudaEventDestroy(e);
+        if (ev_dora_fork) cudaEventDestroy(ev_dora_fork);
+        if (dora_stream) cudaStreamDestroy(dora_stream);
         if (stream) cudaStreamDestroy(stream);
     }
 };
