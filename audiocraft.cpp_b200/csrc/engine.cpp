@@ -311,8 +311,9 @@ struct act_ctx {
     bool use_tc = true;
     // which kernel family each launch was issued to (ACT_PATH_*), counted as the step is issued
     int64_t path_count[ACT_PATH_COUNT] = {};
-    // f16 expansions of Q8_0 weights for the paths that read f16 weights (DoRA's weight products,
-    // shapes the fused GEMM does not take): two per stream, sized for the largest weight
+    // f16 expansions of Q8_0 weights, only for the generic paths (tcgen05 kernels switched off, or
+    // operands neither the fused GEMM nor the rank-block kernel takes; the benchmarked steps use
+    // none): two per stream, sized for the largest weight
     f16* wscratch[2][2] = {};
     long wscratch_elems = 0;
     // DoRA projections in layer order (device table for the batched factor / tail kernels) and
